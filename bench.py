@@ -1,0 +1,537 @@
+#!/usr/bin/env python3
+"""Benchmark of the fused quad dequant-GEMV on 1..8 B200s.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Workload: the quad-pack single-layer sweep -- four correlated synthetic models
+(base N(0,0.02) + delta N(0,0.002), 0.1% entries x20, FP16), packed into
+``.quadpack`` v2 streams (plug cap 5%), Linear shapes in x out = 2048x2048,
+2048x11008, 11008x2048, 2048x256, batch 1.  One step = one fused kernel launch
+per shape (4 outputs per pass over the codes, plug table merged in-kernel).
+R = 4 replica streams rotate step to step, so each step reads ~200 MB of
+codes that were last touched 3 steps (~600 MB) earlier: inputs exceed the
+126 MB L2 and no flush is needed.
+
+Metric: packed-stream GB/s = algorithmic bytes / device time, where the
+bytes of one Linear are 4*N*K (codes) + 12*P (plug index + values) +
+2*M*K (activations) + 8*M*N (four FP16 outputs).
+
+With N > 1 GPUs (launched by torch.distributed.run) each Linear is
+row-sharded (column-parallel): rank r owns output rows [r*N/P, (r+1)*N/P),
+which are a contiguous slice of the file-layout stream, and the four FP16
+outputs are all-gathered over NCCL after every Linear.  Total work is fixed
+(strong scaling); time is the max over ranks of CUDA-event time.
+
+``--impl reference`` times the reference's own CPU path (the oracle's
+restatement of ``unpack_quad`` -- float64 decode, plug merge, scale -- then a
+host matmul) on a bounded row sample of the same shapes, all host threads.
+"""
+from __future__ import annotations
+
+import argparse
+import concurrent.futures as cf
+import ctypes
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+SHAPES = [(2048, 2048), (2048, 11008), (11008, 2048), (2048, 256)]  # (in K, out N)
+METRIC = "fused quad dequant-GEMV GB/s (% HBM peak); 4-model decode tok/s @1-8 GPU"
+UNIT = "GB/s"
+WORKLOAD = "quad-pack single-layer sweep (BASELINE configs[1]): Linear in x out 2048x2048, 2048x11008, " \
+           "11008x2048, 2048x256, batch 1, 4 correlated models, .quadpack plug cap 5%"
+HBM_FALLBACK = 6650.0
+
+
+def measured_peak():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        try:
+            return float(json.loads(p.read_text())["hbm_gbs"]), "measured"
+        except Exception:
+            pass
+    return HBM_FALLBACK, "fallback"
+
+
+def layer_bytes(N, K, P, M):
+    return 4 * N * K + 12 * P + 2 * M * K + 8 * M * N
+
+
+# ------------------------------------------------------------ clocks ----
+class ClockSampler:
+    """nvidia-smi samples during the timed region (SM clock, throttle reasons)."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.lines = []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except Exception:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        time.sleep(0.25)
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.lines:
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for name, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ------------------------------------------------------------ workload ----
+def synth_models(torch, n, seed, device):
+    """Four correlated FP16 models of length n (BASELINE distribution)."""
+    g = torch.Generator(device=device)
+    g.manual_seed(seed)
+    base = torch.randn(n, generator=g, device=device, dtype=torch.float32) * 0.02
+    out = []
+    for _ in range(4):
+        w = base + torch.randn(n, generator=g, device=device, dtype=torch.float32) * 0.002
+        k = max(1, n // 1000)
+        idx = torch.randint(0, n, (k,), generator=g, device=device)
+        w[idx] *= 20
+        out.append(w.half())
+    del base
+    return out
+
+
+def build_streams(torch, replicas, device, shapes=SHAPES):
+    from polar_pack_b200.quadpack import DevicePackedStream, pack_quad_device
+    n = sum(N * K for K, N in shapes)
+    streams = []
+    for r in range(replicas):
+        models = synth_models(torch, n, 1000 + r, device)
+        p = pack_quad_device(models, plug_cap=0.05, seed=42, windows=16, window=1_000_000)
+        del models
+        streams.append(DevicePackedStream(p))
+        torch.cuda.empty_cache()
+    return streams
+
+
+def layer_slices(stream, shapes, rank, world):
+    """Row shard [rank*N/world, (rank+1)*N/world) of every Linear of a stream."""
+    res, off = [], 0
+    for K, N in shapes:
+        n0, n1 = N * rank // world, N * (rank + 1) // world
+        res.append(stream.linear(off + n0 * K, n1 - n0, K))
+        off += N * K
+    return res
+
+
+# ------------------------------------------------------------ our arm ----
+def run_ours(args):
+    import torch
+    import torch.distributed as dist
+    from polar_pack_b200 import _lib
+    from polar_pack_b200.quadpack import quad_linear, quad_linear_workspace_bytes
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=120))
+
+    M = args.batch
+    streams = build_streams(torch, args.replicas, dev)
+    sets = [layer_slices(s, SHAPES, rank, world) for s in streams]
+    for s in streams:
+        s.check_plug_index()
+    full_sets = [layer_slices(s, SHAPES, 0, 1) for s in streams] if world > 1 else sets
+
+    lib = _lib.load()
+    stream = torch.cuda.current_stream(dev)
+    sh = stream.cuda_stream
+    g = torch.Generator(device=dev)
+    g.manual_seed(7)
+    xs = [torch.randn(M, K, generator=g, device=dev).half() for K, _ in SHAPES]
+    ws_bytes = max(quad_linear_workspace_bytes(M, l.N, l.K) for st in sets for l in st)
+    ws = torch.zeros(max(ws_bytes, 256), dtype=torch.uint8, device=dev)
+
+    # pre-built C-ABI argument tuples: no Python allocation inside the timed loop
+    calls = []
+    for st in sets:
+        row = []
+        for l, x in zip(st, xs):
+            obuf = torch.empty((4, M, l.N), dtype=torch.float16, device=dev)
+            outs = [obuf[k] for k in range(4)]
+            pk = l.pack
+            args_c = (x.data_ptr(), x.stride(0), x.stride(1), l.codes.data_ptr(), l.K,
+                      _lib.ptr(l.plug_vals), _lib.ptr(l.plug_mask), _lib.ptr(l.plug_base),
+                      _lib.ptrs(pk.luts, 7), _lib.floats4(pk.scales), _lib.ptrs(outs, 4),
+                      outs[0].stride(0), outs[0].stride(1), M, l.N, l.K, ws.data_ptr(), ws.numel(), sh)
+            gbuf = None
+            if world > 1:
+                gbuf = (obuf, torch.empty((world, 4, M, l.N), dtype=torch.float16, device=dev))
+            row.append((args_c, outs, gbuf, l))
+        calls.append(row)
+
+    def launch(args_c):
+        rc = lib.pp_quad_linear(*args_c)
+        if rc:
+            _lib.check(rc)
+
+    def step(i, evs=None):
+        for j, (args_c, outs, gbuf, l) in enumerate(calls[i % len(calls)]):
+            if evs is not None:
+                evs[j][0].record(stream)
+            launch(args_c)
+            if evs is not None:
+                evs[j][1].record(stream)
+            if gbuf is not None:
+                # the 4 models' row shards, gathered over ranks
+                dist.all_gather_into_tensor(gbuf[1], gbuf[0])
+
+    per_step_bytes = sum(layer_bytes(l.N, l.K, l.p_hi - l.p_lo, M) for l in full_sets[0])
+    avg_bytes = statistics.mean(sum(layer_bytes(l.N, l.K, l.p_hi - l.p_lo, M) for l in fs) for fs in full_sets)
+
+    # correctness gate before timing: one shard output vs the public API path
+    ref = quad_linear(xs[0], sets[0][0])
+    launch(calls[0][0][0])
+    torch.cuda.synchronize(dev)
+    for k in range(4):
+        if not torch.equal(ref[k], calls[0][0][1][k]):
+            raise RuntimeError("pre-built launch disagrees with the public API")
+
+    for i in range(args.warmup):
+        step(i)
+    torch.cuda.synchronize(dev)
+    if world > 1:
+        dist.barrier()
+
+    K_steps = args.steps
+    launches_per_step = len(SHAPES)
+    evs = [[[torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)]
+            for _ in SHAPES] for _ in range(K_steps)]
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    clocks = ClockSampler(local)
+    clocks.start()
+    time.sleep(0.3)
+    torch.cuda.synchronize(dev)
+    if world > 1:
+        dist.barrier()
+    t0.record(stream)
+    for i in range(K_steps):
+        step(args.warmup + i, evs[i])
+    t1.record(stream)
+    torch.cuda.synchronize(dev)
+    if world > 1:
+        dist.barrier()
+    clk = clocks.stop()
+    ms = t0.elapsed_time(t1)
+    kernel_ms = sum(e[0].elapsed_time(e[1]) for step_evs in evs for e in step_evs)
+    kernel_bytes = 0
+    for i in range(K_steps):
+        for l in sets[(args.warmup + i) % len(sets)]:
+            kernel_bytes += layer_bytes(l.N, l.K, l.p_hi - l.p_lo, M)
+    if world > 1:
+        t = torch.tensor([ms], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    total_bytes = avg_bytes * K_steps
+    value = total_bytes / (ms * 1e-3) / 1e9
+    per_shape = {}
+    for j, (K, N) in enumerate(SHAPES):
+        tj = sum(evs[i][j][0].elapsed_time(evs[i][j][1]) for i in range(K_steps)) / K_steps
+        bj = statistics.mean(layer_bytes(st[j].N, st[j].K, st[j].p_hi - st[j].p_lo, M) for st in sets)
+        per_shape[f"{K}x{N}"] = {"us": round(tj * 1e3, 2), "GB/s": round(bj / (tj * 1e-3) / 1e9, 1)}
+
+    # e2e through the public API with host buffers (pinned), 1 GPU view of rank's work
+    e2e = run_e2e(torch, dist, sets, xs, dev, args, world, M)
+
+    peak, peak_kind = measured_peak()
+    achieved = kernel_bytes / (kernel_ms * 1e-3) / 1e9
+    traffic = load_traffic()
+    res = {
+        "metric": METRIC, "value": round(value, 1), "unit": UNIT, "n_gpus": world, "steps": K_steps,
+        "warmup": args.warmup, "ms_per_step": round(ms / K_steps, 4), "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "u32 codes -> fp16 weights, fp32 accumulate",
+        "data": "synthetic (seeded random-init correlated weights; no checkpoints available)",
+        "config": {"workload": WORKLOAD, "batch": M, "replica_streams": args.replicas,
+                   "bytes_per_step": int(per_step_bytes), "l2": "inputs per step ~200 MB > 126 MB L2, "
+                   "4 rotating replica streams (no flush)",
+                   "parallelism": f"row-sharded x{world} + NCCL all-gather" if world > 1 else "single GPU",
+                   "per_shape": per_shape},
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                     "frac": round(achieved / peak, 4), "peak_source": f"{peak_kind} hbm_gbs",
+                     "kernel": "quad_gemv_kernel<NK,NB=1,PLUG>",
+                     "traffic": traffic},
+        "e2e": e2e,
+        "gpu_launches": launches_per_step * K_steps,
+        "clocks": clk,
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        res["cpu_baseline"] = cpu_baseline(streams[0], M, budget_s=args.cpu_seconds)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(res))
+
+
+def run_e2e(torch, dist, sets, xs, dev, args, world, M):
+    """Same metric through the public API: pinned H2D of each step's inputs,
+    the Linear calls, D2H of the four outputs, all inside the timed region."""
+    from polar_pack_b200.quadpack import quad_linear
+    stream = torch.cuda.current_stream(dev)
+    hx = [x.cpu().pin_memory() for x in xs]
+    h2d = sum(x.numel() * 2 for x in hx)
+    d2h = 0
+    host_out = []
+    for l in sets[0]:
+        host_out.append([torch.empty((M, l.N), dtype=torch.float16).pin_memory() for _ in range(4)])
+        d2h += 4 * M * l.N * 2
+    dx = [torch.empty_like(x) for x in xs]
+
+    def step(i):
+        st = sets[i % len(sets)]
+        for j, l in enumerate(st):
+            dx[j].copy_(hx[j], non_blocking=True)
+            ys = quad_linear(dx[j], l)
+            for k in range(4):
+                host_out[j][k].copy_(ys[k], non_blocking=True)
+
+    for i in range(args.warmup):
+        step(i)
+    torch.cuda.synchronize(dev)
+    if world > 1:
+        dist.barrier()
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0.record(stream)
+    for i in range(args.steps):
+        step(args.warmup + i)
+    t1.record(stream)
+    torch.cuda.synchronize(dev)
+    ms = t0.elapsed_time(t1)
+    if world > 1:
+        t = torch.tensor([ms], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    total = 0
+    for i in range(args.steps):
+        for l in sets[(args.warmup + i) % len(sets)]:
+            total += layer_bytes(l.N, l.K, l.p_hi - l.p_lo, M)
+    total *= world  # every rank streams its shard
+    return {"value": round(total / (ms * 1e-3) / 1e9, 1), "unit": UNIT, "h2d_bytes_per_step": int(h2d),
+            "d2h_bytes_per_step": int(d2h), "api": "polar_pack_b200.quadpack.quad_linear"}
+
+
+def load_traffic():
+    p = ROOT / "profiles" / "quad_linear_traffic.json"
+    if not p.exists():
+        return None
+    try:
+        return json.loads(p.read_text()).get("dram_bytes_per_launch_2048x11008")
+    except Exception:
+        return None
+
+
+# ------------------------------------------------------ CPU reference ----
+def _ref_cpu_rows(ctx, K, N, off, rows, M, x):
+    """Reference CPU path on `rows` output rows of one Linear: unpack then matmul."""
+    import torch
+    from oracle.formats import unpack_quad_range
+    codes, pos, vals, scales, r_max, pool, nthreads = ctx
+    start, stop = off, off + rows * K
+    bounds = np.linspace(start, stop, nthreads + 1).astype(np.int64)
+    parts = list(pool.map(lambda ab: unpack_quad_range(codes, pos, vals, scales, r_max, int(ab[0]), int(ab[1])),
+                          zip(bounds[:-1], bounds[1:])))
+    ws = [np.concatenate([p[k] for p in parts]).reshape(rows, K) for k in range(4)]
+    xt = torch.from_numpy(x.astype(np.float32))
+    return [xt @ torch.from_numpy(w).T for w in ws]
+
+
+def cpu_context(stream_host, nthreads):
+    codes, pos, vals, scales, r_max = stream_host
+    pool = cf.ThreadPoolExecutor(max_workers=nthreads)
+    return (codes, pos, vals, scales, r_max, pool, nthreads)
+
+
+def host_stream(stream_dev):
+    return (stream_dev.codes.cpu().numpy(), stream_dev._pos_host, stream_dev.plug_vals.cpu().numpy(),
+            list(stream_dev.scales), stream_dev.header.r_max)
+
+
+def sample_shapes(fraction):
+    """(K, rows) per sweep shape: the leading `fraction` of the output rows."""
+    return [(K, max(1, int(round(N * fraction)))) for K, N in SHAPES]
+
+
+def timed_ref_sample(ctx, M, layers, rng):
+    """One reference step over `layers` [(K, rows, offset)]; returns (bytes, seconds)."""
+    nbytes, t = 0, 0.0
+    pos = ctx[1]
+    for K, rows, off in layers:
+        x = rng.normal(0, 1, size=(M, K)).astype(np.float16)
+        s = time.perf_counter()
+        _ref_cpu_rows(ctx, K, rows, off, rows, M, x)
+        t += time.perf_counter() - s
+        P = int(np.searchsorted(pos, off + rows * K) - np.searchsorted(pos, off))
+        nbytes += layer_bytes(rows, K, P, M)
+    return nbytes, t
+
+
+def stream_layers(shapes_rows, full_shapes=None):
+    """[(K, rows, offset)] for rows taken from the start of each Linear."""
+    res, off = [], 0
+    for i, (K, rows) in enumerate(shapes_rows):
+        res.append((K, rows, off))
+        off += (full_shapes[i][1] if full_shapes else rows) * K
+    return res
+
+
+def cpu_baseline(stream_dev, M, budget_s=15.0):
+    import torch
+    nthreads = os.cpu_count() or 1
+    torch.set_num_threads(nthreads)
+    ctx = cpu_context(host_stream(stream_dev), nthreads)
+    rng = np.random.default_rng(0)
+    fraction = 1 / 32
+    layers = stream_layers(sample_shapes(fraction), SHAPES)
+    total_b, total_t, steps = 0, 0.0, 0
+    while total_t < budget_s and steps < 64:
+        b, t = timed_ref_sample(ctx, M, layers, rng)
+        total_b += b
+        total_t += t
+        steps += 1
+    ctx[5].shutdown()
+    return {"value": round(total_b / total_t / 1e9, 4), "unit": UNIT, "cores": nthreads, "kind": "port",
+            "sample": f"{steps} passes over 1/32 of the output rows of each sweep shape: oracle unpack_quad "
+                      f"restatement (float64 decode + plug merge + scale, {nthreads} threads) then fp32 "
+                      f"torch.matmul on the host", "cpu": cpu_name()}
+
+
+def cpu_name():
+    try:
+        for line in open("/proc/cpuinfo"):
+            if line.startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except Exception:
+        pass
+    return "unknown"
+
+
+def run_reference(args):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    import torch
+    from polar_pack_b200.quadpack import pack_quad_device
+    nthreads = os.cpu_count() or 1
+    torch.set_num_threads(nthreads)
+    # the sampled rows of every sweep shape, synthesised and packed on the CPU
+    # (same distribution and packer as our arm's streams)
+    fraction = args.ref_fraction
+    shapes_rows = sample_shapes(fraction)
+    n = sum(K * rows for K, rows in shapes_rows)
+    models = synth_models_cpu(torch, n, 1000)
+    p = pack_quad_device(models, plug_cap=0.05, seed=42, windows=4, window=min(1_000_000, n // 2))
+    pos = p["plug_pos"].numpy().astype(np.int64)
+    stream_host = (p["codes"].numpy(), pos, p["plug_vals"].numpy(), list(p["scales"]), p["r_max"])
+    ctx = cpu_context(stream_host, nthreads)
+    layers = stream_layers(shapes_rows)
+    rng = np.random.default_rng(0)
+    for _ in range(args.warmup):
+        timed_ref_sample(ctx, args.batch, layers, rng)
+    tb, tt = 0, 0.0
+    for _ in range(args.steps):
+        b, t = timed_ref_sample(ctx, args.batch, layers, rng)
+        tb += b
+        tt += t
+    ctx[5].shutdown()
+    v = tb / tt / 1e9
+    res = {"impl": "reference", "metric": METRIC, "value": round(v, 4), "unit": UNIT, "n_gpus": world,
+           "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(tt / args.steps * 1e3, 2),
+           "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+           "dtype": "float64 decode, fp32 matmul (host)", "data": "synthetic",
+           "config": {"workload": WORKLOAD, "batch": args.batch, "sample": f"{fraction:.4f} of output rows"},
+           "cpu_baseline": {"value": round(v, 4), "unit": UNIT, "cores": nthreads, "kind": "port",
+                            "sample": f"rows [0, {fraction:.4f} N) of each sweep shape per step: oracle "
+                                      "unpack_quad restatement + torch.matmul, "
+                                      f"{nthreads} threads", "cpu": cpu_name()},
+           "e2e": {"value": round(v, 4), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+           "gpu_launches": 0}
+    print(json.dumps(res))
+
+
+def synth_models_cpu(torch, n, seed):
+    g = torch.Generator()
+    g.manual_seed(seed)
+    base = torch.randn(n, generator=g) * 0.02
+    out = []
+    for _ in range(4):
+        w = base + torch.randn(n, generator=g) * 0.002
+        idx = torch.randint(0, n, (max(1, n // 1000),), generator=g)
+        w[idx] *= 20
+        out.append(w.half())
+    return out
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--batch", type=int, default=1)
+    ap.add_argument("--replicas", type=int, default=4)
+    ap.add_argument("--cpu-seconds", type=float, default=15.0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--ref-fraction", type=float, default=1 / 32)
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,172 @@
+/*
+ * polar_pack_b200 -- C ABI of the B200 (sm_100a) fused dequant-matmul path
+ * for polar_pack's packed multi-model weight streams.
+ *
+ * Conventions
+ *  - Every pointer argument named a tensor is DEVICE memory owned by the
+ *    caller; the library allocates nothing per call.  Scalars and the
+ *    `scales` arrays are host values.
+ *  - FP16 data is passed as `void*` (IEEE binary16, little endian).
+ *  - Strides are in ELEMENTS, like torch's Tensor.stride().
+ *  - `stream` is a cudaStream_t (NULL = legacy default stream).  Every call
+ *    only enqueues work on that stream and returns; nothing synchronises.
+ *  - Return value: PP_OK (0) or an error code; pp_last_error() gives a
+ *    message for the calling thread.  Shape and argument errors are
+ *    detected on the host before anything is enqueued.  No function traps
+ *    or asserts on the device.
+ *  - Workspace: entry points that split the reduction over K across warps
+ *    and thread blocks need scratch memory of the size that the matching
+ *    *_workspace_bytes() function returns.  It must be zero-filled ONCE
+ *    when it is allocated; every call leaves it zero-filled again.  Two
+ *    calls that may run concurrently must not share a workspace.
+ */
+#ifndef POLAR_PACK_B200_H
+#define POLAR_PACK_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define PP_API __attribute__((visibility("default")))
+#else
+#define PP_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define PP_VERSION 1
+
+#define PP_OK 0
+#define PP_ERR_INVALID 1     /* bad shape, stride, alignment or argument */
+#define PP_ERR_WORKSPACE 2   /* workspace missing or too small */
+#define PP_ERR_CUDA 3        /* CUDA runtime / launch error */
+
+/* Message describing the last error returned on this thread. */
+PP_API const char* pp_last_error(void);
+
+/* Version of this ABI (PP_VERSION). */
+PP_API int pp_version(void);
+
+/* Number of SMs of `device` (what the work partition is sized for). */
+PP_API int pp_device_sm_count(int device);
+
+/* ------------------------------------------------------------------ quad --
+ * Kernel-layout fused dequant GEMM, the drop-in for `quad_bitpacked`
+ * (reference quad_kernels.py:146-159) and its Triton kernel
+ * `quad_bitpacked_kernel` (quad_kernels.py:68-143):
+ *
+ *   W_k = FP16 decode of codes[k][n] through the seven FP16[256] tables
+ *         luts = {norm, cos1, sin1, cos2, sin2, cos3, sin3}
+ *   out_k[m][n] = fp16( scales[k] * sum_k' a[m][k'] * W_k[k'][n] )   (FP32 acc)
+ *
+ * a: (M, K) FP16, element strides (lda_m, lda_k).
+ * codes: (K, N) uint32, element strides (ldc_k, ldc_n).  Either dimension may
+ *   be the contiguous one; other layouts run on a slower generic kernel.
+ * out[4]: four (M, N) FP16 outputs sharing strides (ldo_m, ldo_n).
+ * scales: 4 host floats (the per-model RMS `s_k`).
+ * Any M >= 0, N >= 0, K >= 0 (K == 0 writes zeros, as the reference does).
+ */
+PP_API int pp_quad_gemm_workspace_bytes(int64_t M, int64_t N, int64_t K, int64_t ldc_k, int64_t ldc_n,
+                                 size_t* bytes);
+
+PP_API int pp_quad_gemm(const void* a, int64_t lda_m, int64_t lda_k,
+                 const uint32_t* codes, int64_t ldc_k, int64_t ldc_n,
+                 const void* const luts[7], const float scales[4],
+                 void* const out[4], int64_t ldo_m, int64_t ldo_n,
+                 int64_t M, int64_t N, int64_t K,
+                 void* workspace, size_t workspace_bytes, void* stream);
+
+/* File-layout fused Linear with plug-table patching, the per-Linear decode of
+ * a `.quadpack` stream (reference quaternion_packer.py:141-214: codes of one
+ * nn.Linear are (out=N, in=K) row-major at a flat stream offset; plug entries
+ * replace the decoded normalised 4-tuple, quaternion_packer.py:187-193):
+ *
+ *   y_k[m][n] = fp16( scales[k] * sum_i x[m][i] * Wp_k[n][i] )
+ *   Wp_k[n][i] = plug value if (n*K + i) is plugged, else the FP16 decode.
+ *
+ * x: (M, K) FP16 with strides (ldx_m, ldx_k).  codes: row n at codes + n*ldw.
+ * plug_vals: (P, 4) FP16 plug values of this Linear, in stream order.
+ * plug_mask / plug_base: per (row, 64-wide column window) bitmask of
+ *   plugged columns and index of the window's first plug in plug_vals, as
+ *   built by pp_quad_plug_index().  All three may be NULL when P == 0.
+ * out[4]: (M, N) FP16 with strides (ldo_m, ldo_n).
+ */
+PP_API int pp_quad_linear_workspace_bytes(int64_t M, int64_t N, int64_t K, size_t* bytes);
+
+PP_API int pp_quad_linear(const void* x, int64_t ldx_m, int64_t ldx_k,
+                   const uint32_t* codes, int64_t ldw,
+                   const void* plug_vals, const uint64_t* plug_mask, const uint32_t* plug_base,
+                   const void* const luts[7], const float scales[4],
+                   void* const out[4], int64_t ldo_m, int64_t ldo_n,
+                   int64_t M, int64_t N, int64_t K,
+                   void* workspace, size_t workspace_bytes, void* stream);
+
+/* Builds plug_mask (uint64, N * ceil(K/64)) and plug_base (uint32, same
+ * count) for one Linear from the slice [p_lo, p_hi) of a `.quadpack` plug
+ * index table (uint32 global positions, ascending; reference
+ * quaternion_packer.py:97-116).  `base_lo32` is the low 32 bits of the
+ * Linear's flat stream offset: position - base (mod 2^32) is the
+ * position inside the Linear, so tables whose uint32 positions wrapped
+ * past 2^32 still index correctly.  Entries outside the Linear are skipped
+ * and counted into *bad_count (device int, may be NULL).  Both outputs are
+ * overwritten completely.
+ */
+PP_API int pp_quad_plug_index(const uint32_t* plug_idx, int64_t p_lo, int64_t p_hi, uint32_t base_lo32,
+                       int64_t N, int64_t K, uint64_t* plug_mask, uint32_t* plug_base,
+                       int* bad_count, void* stream);
+
+/* FP16 decode of a (R, C) code matrix into four (R, C) FP16 matrices,
+ * bit-exact with the reference kernel's chain (quad_kernels.py:103-121).
+ * scales == NULL keeps the normalised weights; otherwise each is multiplied
+ * by scales[k] in FP32 and rounded to FP16 once.
+ */
+PP_API int pp_quad_decode(const uint32_t* codes, int64_t ldc_r, int64_t ldc_c, int64_t R, int64_t C,
+                   const void* const luts[7], const float* scales,
+                   void* const out[4], int64_t ldo_r, int64_t ldo_c, void* stream);
+
+/* Restore n flat positions of a `.quadpack` stream on the GPU: FP16 decode
+ * (as pp_quad_decode) with plug entries [p_lo, p_hi) of the file's plug
+ * table substituted (positions relative to `base_lo32`, as above), then
+ * optional per-model scale.  Counterpart of unpack_quad
+ * (quaternion_packer.py:170-196) on the FP16 tables.
+ */
+PP_API int pp_quad_unpack(const uint32_t* codes, int64_t n, const uint32_t* plug_idx, const void* plug_vals,
+                   int64_t p_lo, int64_t p_hi, uint32_t base_lo32,
+                   const void* const luts[7], const float* scales,
+                   void* const out[4], void* stream);
+
+/* ------------------------------------------------------------------ dual --
+ * Kernel-layout fused dequant GEMM, the drop-in for `polar_dual_bitpacked`
+ * (reference polar_kernels.py:98-115, kernel 30-95):
+ *   u = packed + 32768, amp = (u >> 10) & 63, ph = u & 1023
+ *   A = fp32(amp_lut[amp]) * fp32(bmax[(k*N + n) / group_size])
+ *   B1 = fp16(A * fp32(cos_lut[ph])), B2 = fp16(A * fp32(sin_lut[ph]))
+ *   out_j[m][n] = fp16( sum_k a[m][k] * B_j[k][n] )                  (FP32 acc)
+ * packed: (K, N) int16 with strides (ldp_k, ldp_n); the group index always
+ * uses the logical row-major position k*N + n, as the reference does.
+ */
+PP_API int pp_dual_gemm_workspace_bytes(int64_t M, int64_t N, int64_t K, int64_t ldp_k, int64_t ldp_n,
+                                 size_t* bytes);
+
+PP_API int pp_dual_gemm(const void* a, int64_t lda_m, int64_t lda_k,
+                 const int16_t* packed, int64_t ldp_k, int64_t ldp_n,
+                 const void* bmax, int64_t group_size,
+                 const void* amp_lut, const void* cos_lut, const void* sin_lut,
+                 void* out1, void* out2, int64_t ldo_m, int64_t ldo_n,
+                 int64_t M, int64_t N, int64_t K,
+                 void* workspace, size_t workspace_bytes, void* stream);
+
+/* FP16 decode of a (K, N) int16 matrix into two FP16 matrices, bit-exact with
+ * the reference kernel (polar_kernels.py:64-79). */
+PP_API int pp_dual_decode(const int16_t* packed, int64_t ldp_k, int64_t ldp_n, int64_t K, int64_t N,
+                   const void* bmax, int64_t group_size,
+                   const void* amp_lut, const void* cos_lut, const void* sin_lut,
+                   void* out1, void* out2, int64_t ldo_k, int64_t ldo_n, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* POLAR_PACK_B200_H */

@@ -1,0 +1,160 @@
+"""ctypes binding of the in-tree CUDA library ``libpolarpack_b200.so``.
+
+The library exposes a plain C ABI (``include/polar_pack_b200.h``); this
+module declares the argument types, loads it once, and turns non-zero status
+codes into Python exceptions.  There is no fallback: if the shared object is
+missing or fails to load, every call raises ``RuntimeError``.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import threading
+from pathlib import Path
+
+import torch
+
+PKG = Path(__file__).resolve().parent
+LIB_PATH = PKG / "libpolarpack_b200.so"
+
+PP_OK, PP_ERR_INVALID, PP_ERR_WORKSPACE, PP_ERR_CUDA = 0, 1, 2, 3
+
+_c_void_p = ctypes.c_void_p
+_i64 = ctypes.c_int64
+_u32 = ctypes.c_uint32
+_size_t = ctypes.c_size_t
+_int = ctypes.c_int
+_PTR7 = _c_void_p * 7
+_PTR4 = _c_void_p * 4
+_F4 = ctypes.c_float * 4
+
+_SIGNATURES = {
+    "pp_last_error": ([], ctypes.c_char_p),
+    "pp_version": ([], _int),
+    "pp_device_sm_count": ([_int], _int),
+    "pp_quad_gemm_workspace_bytes": ([_i64, _i64, _i64, _i64, _i64, ctypes.POINTER(_size_t)], _int),
+    "pp_quad_gemm": ([_c_void_p, _i64, _i64, _c_void_p, _i64, _i64, _PTR7, _F4, _PTR4, _i64, _i64,
+                      _i64, _i64, _i64, _c_void_p, _size_t, _c_void_p], _int),
+    "pp_quad_linear_workspace_bytes": ([_i64, _i64, _i64, ctypes.POINTER(_size_t)], _int),
+    "pp_quad_linear": ([_c_void_p, _i64, _i64, _c_void_p, _i64, _c_void_p, _c_void_p, _c_void_p,
+                        _PTR7, _F4, _PTR4, _i64, _i64, _i64, _i64, _i64, _c_void_p, _size_t,
+                        _c_void_p], _int),
+    "pp_quad_plug_index": ([_c_void_p, _i64, _i64, _u32, _i64, _i64, _c_void_p, _c_void_p,
+                            _c_void_p, _c_void_p], _int),
+    "pp_quad_decode": ([_c_void_p, _i64, _i64, _i64, _i64, _PTR7, _c_void_p, _PTR4, _i64, _i64,
+                        _c_void_p], _int),
+    "pp_quad_unpack": ([_c_void_p, _i64, _c_void_p, _c_void_p, _i64, _i64, _u32, _PTR7, _c_void_p,
+                        _PTR4, _c_void_p], _int),
+    "pp_dual_gemm_workspace_bytes": ([_i64, _i64, _i64, _i64, _i64, ctypes.POINTER(_size_t)], _int),
+    "pp_dual_gemm": ([_c_void_p, _i64, _i64, _c_void_p, _i64, _i64, _c_void_p, _i64, _c_void_p,
+                      _c_void_p, _c_void_p, _c_void_p, _c_void_p, _i64, _i64, _i64, _i64, _i64,
+                      _c_void_p, _size_t, _c_void_p], _int),
+    "pp_dual_decode": ([_c_void_p, _i64, _i64, _i64, _i64, _c_void_p, _i64, _c_void_p, _c_void_p,
+                        _c_void_p, _c_void_p, _c_void_p, _i64, _i64, _c_void_p], _int),
+}
+
+_lock = threading.Lock()
+_lib = None
+
+
+def exported_symbols() -> list[str]:
+    """Every entry point the header declares (and this module binds)."""
+    return list(_SIGNATURES)
+
+
+def load() -> ctypes.CDLL:
+    """Load the shared library (once) and declare every signature."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    with _lock:
+        if _lib is not None:
+            return _lib
+        path = Path(os.environ.get("POLAR_PACK_B200_LIB", LIB_PATH))
+        if not path.exists():
+            raise RuntimeError(
+                f"CUDA library {path} is missing: build it with "
+                "`python -m polar_pack_b200.build` (there is no CPU fallback)")
+        lib = ctypes.CDLL(str(path))
+        for name, (args, res) in _SIGNATURES.items():
+            fn = getattr(lib, name)
+            fn.argtypes = args
+            fn.restype = res
+        _lib = lib
+    return _lib
+
+
+class PolarPackError(RuntimeError):
+    """A C-ABI call returned an error status."""
+
+    def __init__(self, code: int, msg: str):
+        super().__init__(f"[polar_pack_b200 error {code}] {msg}")
+        self.code = code
+
+
+def check(rc: int) -> None:
+    if rc != PP_OK:
+        msg = load().pp_last_error().decode(errors="replace")
+        if rc == PP_ERR_INVALID:
+            raise ValueError(msg)
+        raise PolarPackError(rc, msg)
+
+
+def call(name: str, *args) -> None:
+    check(getattr(load(), name)(*args))
+
+
+def ptr(t) -> int | None:
+    if t is None:
+        return None
+    return t.data_ptr()
+
+
+def ptrs(ts, n) -> ctypes.Array:
+    arr = (_c_void_p * n)()
+    for i, t in enumerate(ts):
+        arr[i] = t.data_ptr()
+    return arr
+
+
+def floats4(vals) -> ctypes.Array:
+    return _F4(*[float(v) for v in vals])
+
+
+def stream_handle(device: torch.device) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def require_cuda(*tensors) -> torch.device:
+    """All tensors on one CUDA device; the path has no CPU implementation."""
+    dev = None
+    for t in tensors:
+        if t is None:
+            continue
+        if not t.is_cuda:
+            raise RuntimeError("polar_pack_b200 kernels run on CUDA tensors only (no CPU fallback)")
+        if dev is None:
+            dev = t.device
+        elif t.device != dev:
+            raise ValueError(f"tensors on different devices: {dev} and {t.device}")
+    return dev
+
+
+# ------------------------------------------------------------- workspace --
+_ws: dict = {}
+
+
+def workspace(device: torch.device, nbytes: int) -> torch.Tensor:
+    """Zero-filled scratch for split-K reductions, one per (device, stream).
+
+    Kernels leave their counters at zero, so the buffer is reused as is by
+    later calls on the same stream; it only grows.
+    """
+    stream = torch.cuda.current_stream(device)
+    key = (device.index, stream.cuda_stream)
+    buf = _ws.get(key)
+    if buf is None or buf.numel() < nbytes:
+        size = max(nbytes, 1 << 20)
+        buf = torch.zeros(size, dtype=torch.uint8, device=device)
+        _ws[key] = buf
+    return buf

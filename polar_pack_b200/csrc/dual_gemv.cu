@@ -1,0 +1,523 @@
+// Dual-pack (2 models, 16-bit polar codes) fused dequant GEMV/GEMM, sm_100a.
+//
+// Kernel layout (K, N) int16, N contiguous.  A work unit is 16 k x 64
+// features: lane (g, c) loads 8 codes (128 bits) of features 8g..8g+7 for
+// rows 2c, 2c+1, 2c+8, 2c+9.  Per code: two conflict-free shared-memory
+// table reads (FP32 amplitude level, half2 (cos, sin)), one FP32 product
+// with the group scale and two with cos / sin -- the reference's rounding
+// points -- then one cvt packs two FP32 weights into an FP16 pair that is
+// directly an mma fragment register.  One m16n8k16 per feature column
+// carries both models (rows 0-7 model 1, rows 8-15 model 2).
+//
+// The split of K over warps / CTAs and the deterministic workspace
+// reduction are the same as in the quad kernel.
+#include "pp_common.cuh"
+#include "pp_host.h"
+
+namespace pp {
+
+int zero_f16(void* p, int64_t R, int64_t C, int64_t ldr, int64_t ldc, cudaStream_t s);
+
+__host__ __device__ constexpr int dual_warps(int nb) { return nb == 1 ? 12 : 8; }
+
+struct DualParams {
+  const __half* x;
+  int64_t ldx_m, ldx_k;
+  const int16_t* codes;
+  int64_t ldc;  // stride between rows k
+  const __half* bmax;
+  int gs;
+  const __half *amp_lut, *cos_lut, *sin_lut;
+  __half* out[2];
+  int64_t ldo_m, ldo_n;
+  int M, N, K;
+  int64_t units;
+  int upt;
+  int active_warps;
+  int* counters;
+  float* slots;
+  int xvec;
+};
+
+__device__ __forceinline__ int64_t dual_warp_of_unit(int64_t x, int64_t U, int64_t GW) {
+  int64_t w = ((x + 1) * GW + U - 1) / U - 1;
+  return w < GW - 1 ? w : GW - 1;
+}
+
+template <int NB>
+struct DualWarp {
+  static constexpr int kTileW = 64;
+  static constexpr int kNBat = 8 * NB;
+  static constexpr int kSlot = 2 * kNBat * kTileW;
+
+  const DualParams& p;
+  const uint8_t* lut;
+  int lane, g, c;
+  uint32_t laneoff;
+  float acc[8][NB][4];
+
+  __device__ __forceinline__ DualWarp(const DualParams& p_, const uint8_t* lut_, int lane_)
+      : p(p_), lut(lut_), lane(lane_), g(lane_ >> 2), c(lane_ & 3), laneoff((uint32_t)lane_ * 4u) {
+    zero();
+  }
+
+  __device__ __forceinline__ void zero() {
+#pragma unroll
+    for (int t = 0; t < 8; ++t)
+#pragma unroll
+      for (int nb = 0; nb < NB; ++nb)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) acc[t][nb][j] = 0.f;
+  }
+
+  __device__ __forceinline__ void load(uint4 (&buf)[4], float (&sc)[4], int64_t u) const {
+    const int64_t tile = u / p.upt;
+    const int kc = (int)(u - tile * p.upt);
+    const int64_t f = tile * 64 + 8 * g;
+#pragma unroll
+    for (int r = 0; r < 4; ++r) {
+      const int k = kc * 16 + 2 * c + (r & 1) + 8 * (r >> 1);
+      if (f < p.N && k < p.K) {
+        buf[r] = ldg_stream(p.codes + (int64_t)k * p.ldc + f);
+        sc[r] = __half2float(__ushort_as_half(ldg_u16(p.bmax + ((int64_t)k * p.N + f) / p.gs)));
+      } else {
+        buf[r] = make_uint4(0, 0, 0, 0);
+        sc[r] = 0.f;
+      }
+    }
+  }
+
+  __device__ __forceinline__ uint32_t xpair(int bat, int k) const {
+    if (bat >= p.M) return 0u;
+    const __half* row = p.x + (int64_t)bat * p.ldx_m;
+    if (p.xvec && k + 1 < p.K) return ldg_u32(row + k);
+    uint32_t lo = 0, hi = 0;
+    if (k < p.K) lo = ldg_u16(row + (int64_t)k * p.ldx_k);
+    if (k + 1 < p.K) hi = ldg_u16(row + (int64_t)(k + 1) * p.ldx_k);
+    return lo | (hi << 16);
+  }
+
+  // (B1, B2) of the low and high code of word w, FP32, reference rounding
+  __device__ __forceinline__ void decode2(uint32_t w, float s, float& b1l, float& b2l, float& b1h,
+                                          float& b2h) const {
+    const uint32_t al = ((w >> 3) & 0x1F80u) | laneoff;
+    const uint32_t ah = ((w >> 19) & 0x1F80u) | laneoff;
+    const uint32_t pl = ((w << 7) & 0x1FF80u) | laneoff;
+    const uint32_t ph = ((w >> 9) & 0x1FF80u) | laneoff;
+    const float ampl = __fmul_rn(*reinterpret_cast<const float*>(lut + al), s);
+    const float amph = __fmul_rn(*reinterpret_cast<const float*>(lut + ah), s);
+    const __half2 csl = u2h(*reinterpret_cast<const uint32_t*>(lut + kDualAmpBytes + pl));
+    const __half2 csh = u2h(*reinterpret_cast<const uint32_t*>(lut + kDualAmpBytes + ph));
+    b1l = __fmul_rn(ampl, __low2float(csl));
+    b2l = __fmul_rn(ampl, __high2float(csl));
+    b1h = __fmul_rn(amph, __low2float(csh));
+    b2h = __fmul_rn(amph, __high2float(csh));
+  }
+
+  __device__ __forceinline__ void compute(const uint4 (&buf)[4], const float (&sc)[4], int64_t u) {
+    const int64_t tile = u / p.upt;
+    const int kc = (int)(u - tile * p.upt);
+    const int kbase = kc * 16;
+    uint32_t b0[NB], b1[NB];
+#pragma unroll
+    for (int nb = 0; nb < NB; ++nb) {
+      b0[nb] = xpair(nb * 8 + g, kbase + 2 * c);
+      b1[nb] = xpair(nb * 8 + g, kbase + 2 * c + 8);
+    }
+    // rows beyond K: scale 0 gives +-0 weights, activations are 0 there too
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      float w1l[4], w2l[4], w1h[4], w2h[4];
+#pragma unroll
+      for (int r = 0; r < 4; ++r) {
+        const uint32_t w = j == 0 ? buf[r].x : j == 1 ? buf[r].y : j == 2 ? buf[r].z : buf[r].w;
+        decode2(w, sc[r], w1l[r], w2l[r], w1h[r], w2h[r]);
+      }
+      // feature t = 2j (low codes) and t = 2j + 1 (high codes)
+      const uint32_t al0 = h2u(__floats2half2_rn(w1l[0], w1l[1]));
+      const uint32_t al1 = h2u(__floats2half2_rn(w2l[0], w2l[1]));
+      const uint32_t al2 = h2u(__floats2half2_rn(w1l[2], w1l[3]));
+      const uint32_t al3 = h2u(__floats2half2_rn(w2l[2], w2l[3]));
+      const uint32_t ah0 = h2u(__floats2half2_rn(w1h[0], w1h[1]));
+      const uint32_t ah1 = h2u(__floats2half2_rn(w2h[0], w2h[1]));
+      const uint32_t ah2 = h2u(__floats2half2_rn(w1h[2], w1h[3]));
+      const uint32_t ah3 = h2u(__floats2half2_rn(w2h[2], w2h[3]));
+#pragma unroll
+      for (int nb = 0; nb < NB; ++nb) {
+        mma_16816(acc[2 * j][nb], al0, al1, al2, al3, b0[nb], b1[nb]);
+        mma_16816(acc[2 * j + 1][nb], ah0, ah1, ah2, ah3, b0[nb], b1[nb]);
+      }
+    }
+  }
+
+  // Fragment register j: model (j >> 1), batch 8nb + 2c + (j & 1), feature 8g + t.
+  __device__ __forceinline__ void store_direct(int64_t tile) const {
+#pragma unroll
+    for (int t = 0; t < 8; ++t) {
+      const int64_t f = tile * 64 + 8 * g + t;
+      if (f >= p.N) continue;
+#pragma unroll
+      for (int nb = 0; nb < NB; ++nb)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const int bat = nb * 8 + 2 * c + (j & 1);
+          if (bat < p.M)
+            p.out[j >> 1][(int64_t)bat * p.ldo_m + f * p.ldo_n] = __float2half_rn(acc[t][nb][j]);
+        }
+    }
+  }
+
+  __device__ __forceinline__ void store_partial(float* slot) const {
+#pragma unroll
+    for (int t = 0; t < 8; ++t)
+#pragma unroll
+      for (int nb = 0; nb < NB; ++nb)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const int bat = nb * 8 + 2 * c + (j & 1);
+          __stcg(slot + ((j >> 1) * kNBat + bat) * kTileW + 8 * g + t, acc[t][nb][j]);
+        }
+  }
+
+  __device__ __forceinline__ void finalize(int64_t tile, int64_t w_first, int64_t w_last) const {
+    const int64_t U = p.units, GW = p.active_warps;
+    const int64_t tile_u0 = tile * p.upt;
+    for (int e = lane; e < kSlot; e += 32) {
+      const int model = e / (kNBat * kTileW);
+      const int bat = (e / kTileW) % kNBat;
+      const int64_t f = tile * kTileW + e % kTileW;
+      float sum = 0.f;
+      for (int64_t w = w_first; w <= w_last; ++w) {
+        const int which = (U * w / GW >= tile_u0) ? 0 : 1;
+        sum += __ldcg(p.slots + (w * 2 + which) * kSlot + e);
+      }
+      if (bat < p.M && f < p.N) p.out[model][(int64_t)bat * p.ldo_m + f * p.ldo_n] = __float2half_rn(sum);
+    }
+  }
+};
+
+template <int NB>
+__global__ void __launch_bounds__(dual_warps(NB) * 32, 1) dual_gemv_kernel(const DualParams p) {
+  constexpr int kWarps = dual_warps(NB);
+  extern __shared__ __align__(1024) uint8_t smem[];
+  build_dual_lut(smem, p.amp_lut, p.cos_lut, p.sin_lut);
+  __syncthreads();
+
+  const int lane = threadIdx.x & 31;
+  const int64_t gw = (int64_t)blockIdx.x * kWarps + (threadIdx.x >> 5);
+  if (gw >= p.active_warps) return;
+  const int64_t U = p.units, GW = p.active_warps;
+  const int64_t u_begin = U * gw / GW, u_end = U * (gw + 1) / GW;
+  const int upt = p.upt;
+
+  DualWarp<NB> wk(p, smem, lane);
+  int64_t pending[2];
+  int npend = 0;
+  const int64_t first_tile = u_begin / upt;
+
+  auto finish_unit = [&](int64_t u) {
+    const int64_t tile = u / upt;
+    const int64_t tile_u0 = tile * upt;
+    if (u - tile_u0 == upt - 1 || u == u_end - 1) {
+      const bool whole = (u_begin <= tile_u0) && (u - tile_u0 == upt - 1);
+      if (whole) {
+        wk.store_direct(tile);
+      } else {
+        const int which = tile == first_tile ? 0 : 1;
+        wk.store_partial(p.slots + (gw * 2 + which) * DualWarp<NB>::kSlot);
+        if (npend < 2) pending[npend++] = tile;
+      }
+      wk.zero();
+    }
+  };
+
+  uint4 bufA[4], bufB[4];
+  float scA[4], scB[4];
+  wk.load(bufA, scA, u_begin);
+  int64_t u = u_begin;
+  while (true) {
+    if (u + 1 < u_end) wk.load(bufB, scB, u + 1);
+    wk.compute(bufA, scA, u);
+    finish_unit(u);
+    if (++u >= u_end) break;
+    if (u + 1 < u_end) wk.load(bufA, scA, u + 1);
+    wk.compute(bufB, scB, u);
+    finish_unit(u);
+    if (++u >= u_end) break;
+  }
+
+  if (npend == 0) return;
+  __threadfence();
+  __syncwarp();
+  for (int i = 0; i < npend; ++i) {
+    const int64_t tile = pending[i];
+    const int64_t w_first = dual_warp_of_unit(tile * upt, U, GW);
+    const int64_t w_last = dual_warp_of_unit(tile * upt + upt - 1, U, GW);
+    int old = 0;
+    if (lane == 0) old = atomicAdd(p.counters + tile, 1);
+    old = __shfl_sync(0xffffffffu, old, 0);
+    if (old == (int)(w_last - w_first)) {
+      __threadfence();
+      wk.finalize(tile, w_first, w_last);
+      __syncwarp();
+      if (lane == 0) p.counters[tile] = 0;
+    }
+  }
+}
+
+// ------------------------------------------------ generic and decode ----
+struct DualGenericParams {
+  const __half* x;
+  int64_t ldx_m, ldx_k;
+  const int16_t* codes;
+  int64_t ldc_k, ldc_n;
+  const __half* bmax;
+  int64_t gs;
+  const __half *amp_lut, *cos_lut, *sin_lut;
+  __half* out[2];
+  int64_t ldo_m, ldo_n;  // for decode: (ldo_k, ldo_n)
+  int64_t M, N, K;
+};
+
+__device__ __forceinline__ void dual_decode_one(const DualGenericParams& p, int64_t k, int64_t n, float& b1,
+                                                float& b2) {
+  const int32_t u = (int32_t)p.codes[k * p.ldc_k + n * p.ldc_n] + 32768;
+  const int aq = (u >> 10) & 63, ph = u & 1023;
+  const float amp = __fmul_rn(__half2float(p.amp_lut[aq]), __half2float(p.bmax[(k * p.N + n) / p.gs]));
+  b1 = __fmul_rn(amp, __half2float(p.cos_lut[ph]));
+  b2 = __fmul_rn(amp, __half2float(p.sin_lut[ph]));
+}
+
+__global__ void dual_generic_kernel(const DualGenericParams p) {
+  const int64_t n = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  const int64_t m = blockIdx.y;
+  if (n >= p.N || m >= p.M) return;
+  float a1 = 0.f, a2 = 0.f;
+  for (int64_t k = 0; k < p.K; ++k) {
+    float b1, b2;
+    dual_decode_one(p, k, n, b1, b2);
+    const float xv = __half2float(p.x[m * p.ldx_m + k * p.ldx_k]);
+    a1 = fmaf(xv, __half2float(__float2half_rn(b1)), a1);
+    a2 = fmaf(xv, __half2float(__float2half_rn(b2)), a2);
+  }
+  p.out[0][m * p.ldo_m + n * p.ldo_n] = __float2half_rn(a1);
+  p.out[1][m * p.ldo_m + n * p.ldo_n] = __float2half_rn(a2);
+}
+
+__global__ void dual_decode_kernel(const DualGenericParams p) {
+  const int64_t total = p.K * p.N;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t k = i / p.N, n = i - k * p.N;
+    float b1, b2;
+    dual_decode_one(p, k, n, b1, b2);
+    p.out[0][k * p.ldo_m + n * p.ldo_n] = __float2half_rn(b1);
+    p.out[1][k * p.ldo_m + n * p.ldo_n] = __float2half_rn(b2);
+  }
+}
+
+namespace {
+
+struct DualPlan {
+  int nb = 1;
+  int64_t tiles = 0, upt = 0, units = 0;
+  int grid = 0, active_warps = 0;
+  size_t counters_bytes = 0, slots_bytes = 0;
+  size_t total() const { return counters_bytes + slots_bytes; }
+};
+
+DualPlan dual_plan(int64_t Mc, int64_t N, int64_t K, int sms) {
+  DualPlan pl;
+  pl.nb = Mc > 8 ? 2 : 1;
+  pl.tiles = cdiv(N, 64);
+  pl.upt = cdiv(K, 16);
+  pl.units = pl.tiles * pl.upt;
+  if (pl.units == 0) return pl;
+  const int warps = dual_warps(pl.nb);
+  const int64_t want = cdiv(pl.units, warps);
+  pl.grid = (int)(want < sms ? want : sms);
+  const int64_t gw = (int64_t)pl.grid * warps;
+  pl.active_warps = (int)(gw < pl.units ? gw : pl.units);
+  pl.counters_bytes = align_up((size_t)pl.tiles * sizeof(int), 256);
+  pl.slots_bytes = (size_t)pl.active_warps * 2 * (2 * 8 * pl.nb * 64) * sizeof(float);
+  return pl;
+}
+
+bool g_dual_attr[2][64];
+
+template <int NB>
+int launch_dual(const DualParams& prm, int grid, cudaStream_t s) {
+  auto kern = dual_gemv_kernel<NB>;
+  int rc = ensure_smem_attr(kern, (int)kDualLutBytes, g_dual_attr[NB - 1]);
+  if (rc) return rc;
+  kern<<<grid, dual_warps(NB) * 32, kDualLutBytes, s>>>(prm);
+  return check_launch("dual_gemv_kernel");
+}
+
+bool dual_vector_ok(const int16_t* codes, int64_t ldp_k, int64_t ldp_n, int64_t N, int64_t gs) {
+  return aligned(codes, 16) && ldp_n == 1 && ldp_k % 8 == 0 && ldp_k >= N && N % 8 == 0 && gs % 8 == 0;
+}
+
+}  // namespace
+
+static int dual_run(const void* a, int64_t lda_m, int64_t lda_k, const int16_t* packed, int64_t ldp_k,
+                    int64_t ldp_n, const void* bmax, int64_t gs, const void* amp_lut, const void* cos_lut,
+                    const void* sin_lut, void* out1, void* out2, int64_t ldo_m, int64_t ldo_n, int64_t M,
+                    int64_t N, int64_t K, void* ws, size_t ws_bytes, cudaStream_t s) {
+  if (M < 0 || N < 0 || K < 0 || gs <= 0) {
+    set_error("invalid shape or group size");
+    return PP_ERR_INVALID;
+  }
+  if (N > INT32_MAX || K > INT32_MAX) {
+    set_error("N and K must fit in 32 bits");
+    return PP_ERR_INVALID;
+  }
+  if (M == 0 || N == 0) return PP_OK;
+  if (!out1 || !out2) {
+    set_error("outputs must not be NULL");
+    return PP_ERR_INVALID;
+  }
+  int rc;
+  if (K == 0) {
+    if ((rc = zero_f16(out1, M, N, ldo_m, ldo_n, s))) return rc;
+    return zero_f16(out2, M, N, ldo_m, ldo_n, s);
+  }
+  if (!a || !packed || !bmax || !amp_lut || !cos_lut || !sin_lut) {
+    set_error("a NULL tensor argument");
+    return PP_ERR_INVALID;
+  }
+  if (!dual_vector_ok(packed, ldp_k, ldp_n, N, gs)) {
+    DualGenericParams g{};
+    g.x = reinterpret_cast<const __half*>(a);
+    g.ldx_m = lda_m;
+    g.ldx_k = lda_k;
+    g.codes = packed;
+    g.ldc_k = ldp_k;
+    g.ldc_n = ldp_n;
+    g.bmax = reinterpret_cast<const __half*>(bmax);
+    g.gs = gs;
+    g.amp_lut = reinterpret_cast<const __half*>(amp_lut);
+    g.cos_lut = reinterpret_cast<const __half*>(cos_lut);
+    g.sin_lut = reinterpret_cast<const __half*>(sin_lut);
+    g.out[0] = reinterpret_cast<__half*>(out1);
+    g.out[1] = reinterpret_cast<__half*>(out2);
+    g.ldo_m = ldo_m;
+    g.ldo_n = ldo_n;
+    g.N = N;
+    g.K = K;
+    for (int64_t m0 = 0; m0 < M; m0 += 65535) {
+      DualGenericParams gg = g;
+      gg.x += m0 * lda_m;
+      gg.out[0] += m0 * ldo_m;
+      gg.out[1] += m0 * ldo_m;
+      gg.M = (M - m0) < 65535 ? (M - m0) : 65535;
+      dim3 grid((unsigned)cdiv(N, 128), (unsigned)gg.M);
+      dual_generic_kernel<<<grid, 128, 0, s>>>(gg);
+      if ((rc = check_launch("dual_generic_kernel"))) return rc;
+    }
+    return PP_OK;
+  }
+  const int sms = device_sm_count(current_device());
+  if (sms <= 0) {
+    set_error("cannot query the SM count of the current device");
+    return PP_ERR_CUDA;
+  }
+  const size_t need = dual_plan(M < 16 ? M : 16, N, K, sms).total();
+  if (ws_bytes < need || (need && !ws) || !aligned(ws, 256)) {
+    set_error("workspace of %zu bytes (256-byte aligned, zero-filled) required, got %zu", need, ws_bytes);
+    return PP_ERR_WORKSPACE;
+  }
+  DualParams prm{};
+  prm.ldx_m = lda_m;
+  prm.ldx_k = lda_k;
+  prm.codes = packed;
+  prm.ldc = ldp_k;
+  prm.bmax = reinterpret_cast<const __half*>(bmax);
+  prm.gs = (int)gs;
+  prm.amp_lut = reinterpret_cast<const __half*>(amp_lut);
+  prm.cos_lut = reinterpret_cast<const __half*>(cos_lut);
+  prm.sin_lut = reinterpret_cast<const __half*>(sin_lut);
+  prm.ldo_m = ldo_m;
+  prm.ldo_n = ldo_n;
+  prm.N = (int)N;
+  prm.K = (int)K;
+  for (int64_t m0 = 0; m0 < M; m0 += 16) {
+    const int64_t Mc = (M - m0) < 16 ? (M - m0) : 16;
+    DualPlan pl = dual_plan(Mc, N, K, sms);
+    prm.x = reinterpret_cast<const __half*>(a) + m0 * lda_m;
+    prm.out[0] = reinterpret_cast<__half*>(out1) + m0 * ldo_m;
+    prm.out[1] = reinterpret_cast<__half*>(out2) + m0 * ldo_m;
+    prm.M = (int)Mc;
+    prm.xvec = (lda_k == 1 && aligned(prm.x, 4) && (lda_m * 2) % 4 == 0) ? 1 : 0;
+    prm.units = pl.units;
+    prm.upt = (int)pl.upt;
+    prm.active_warps = pl.active_warps;
+    prm.counters = reinterpret_cast<int*>(ws);
+    prm.slots = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(ws) + pl.counters_bytes);
+    rc = pl.nb == 1 ? launch_dual<1>(prm, pl.grid, s) : launch_dual<2>(prm, pl.grid, s);
+    if (rc) return rc;
+  }
+  return PP_OK;
+}
+
+}  // namespace pp
+
+extern "C" {
+
+int pp_dual_gemm_workspace_bytes(int64_t M, int64_t N, int64_t K, int64_t ldp_k, int64_t ldp_n,
+                                 size_t* bytes) {
+  (void)ldp_k;
+  (void)ldp_n;
+  if (!bytes || M < 0 || N < 0 || K < 0) {
+    pp::set_error("invalid arguments");
+    return PP_ERR_INVALID;
+  }
+  const int sms = pp::device_sm_count(pp::current_device());
+  const int64_t Mc = M < 16 ? M : 16;
+  *bytes = Mc > 0 ? pp::dual_plan(Mc, N, K, sms > 0 ? sms : 148).total() : 0;
+  return PP_OK;
+}
+
+int pp_dual_gemm(const void* a, int64_t lda_m, int64_t lda_k, const int16_t* packed, int64_t ldp_k,
+                 int64_t ldp_n, const void* bmax, int64_t group_size, const void* amp_lut, const void* cos_lut,
+                 const void* sin_lut, void* out1, void* out2, int64_t ldo_m, int64_t ldo_n, int64_t M,
+                 int64_t N, int64_t K, void* workspace, size_t workspace_bytes, void* stream) {
+  return pp::dual_run(a, lda_m, lda_k, packed, ldp_k, ldp_n, bmax, group_size, amp_lut, cos_lut, sin_lut,
+                      out1, out2, ldo_m, ldo_n, M, N, K, workspace, workspace_bytes,
+                      reinterpret_cast<cudaStream_t>(stream));
+}
+
+int pp_dual_decode(const int16_t* packed, int64_t ldp_k, int64_t ldp_n, int64_t K, int64_t N,
+                   const void* bmax, int64_t group_size, const void* amp_lut, const void* cos_lut,
+                   const void* sin_lut, void* out1, void* out2, int64_t ldo_k, int64_t ldo_n, void* stream) {
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  if (K < 0 || N < 0 || group_size <= 0) {
+    pp::set_error("invalid arguments to dual decode");
+    return PP_ERR_INVALID;
+  }
+  if (K == 0 || N == 0) return PP_OK;
+  if (!packed || !bmax || !amp_lut || !cos_lut || !sin_lut || !out1 || !out2) {
+    pp::set_error("a NULL tensor argument");
+    return PP_ERR_INVALID;
+  }
+  pp::DualGenericParams g{};
+  g.codes = packed;
+  g.ldc_k = ldp_k;
+  g.ldc_n = ldp_n;
+  g.bmax = reinterpret_cast<const __half*>(bmax);
+  g.gs = group_size;
+  g.amp_lut = reinterpret_cast<const __half*>(amp_lut);
+  g.cos_lut = reinterpret_cast<const __half*>(cos_lut);
+  g.sin_lut = reinterpret_cast<const __half*>(sin_lut);
+  g.out[0] = reinterpret_cast<__half*>(out1);
+  g.out[1] = reinterpret_cast<__half*>(out2);
+  g.ldo_m = ldo_k;
+  g.ldo_n = ldo_n;
+  g.N = N;
+  g.K = K;
+  const int64_t blocks = pp::cdiv(K * N, 256);
+  pp::dual_decode_kernel<<<(int)(blocks < 8192 ? blocks : 8192), 256, 0, s>>>(g);
+  return pp::check_launch("dual_decode_kernel");
+}
+
+}  // extern "C"

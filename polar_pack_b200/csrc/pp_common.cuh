@@ -1,0 +1,139 @@
+// Shared device helpers for the polar_pack B200 kernels (sm_100a).
+//
+// Lookup tables live in shared memory, replicated once per warp lane so
+// that a warp-wide gather with 32 random indices is one conflict-free
+// shared-memory wavefront: lane l always reads bank l.  A table entry is
+// a 256-byte row; copy l of entry i sits at byte  i*256 + slot*128 + 4*l.
+// That makes the gather address for code byte b equal to
+// __byte_perm(code, 4*lane, 0x76b4) -- one PRMT per table read.
+#pragma once
+
+#include <cuda_fp16.h>
+#include <stdint.h>
+
+namespace pp {
+
+constexpr int kWarpSize = 32;
+
+// ----------------------------------------------------------------- PTX --
+__device__ __forceinline__ uint32_t h2u(__half2 h) { return *reinterpret_cast<uint32_t*>(&h); }
+__device__ __forceinline__ __half2 u2h(uint32_t u) { return *reinterpret_cast<__half2*>(&u); }
+
+// Streaming 128-bit load of packed codes: read once, keep out of L1.
+__device__ __forceinline__ uint4 ldg_stream(const void* p) {
+  uint4 v;
+  asm volatile("ld.global.nc.L1::no_allocate.L2::256B.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "l"(p));
+  return v;
+}
+
+// Activation / table loads: small, reused by many warps -> cache in L1.
+__device__ __forceinline__ uint2 ldg_u2(const void* p) {
+  return __ldg(reinterpret_cast<const uint2*>(p));
+}
+__device__ __forceinline__ uint32_t ldg_u32(const void* p) {
+  return __ldg(reinterpret_cast<const unsigned int*>(p));
+}
+__device__ __forceinline__ uint16_t ldg_u16(const void* p) {
+  return __ldg(reinterpret_cast<const unsigned short*>(p));
+}
+
+// D += A(16x16, row) * B(16x8, col), FP16 inputs, FP32 accumulate.
+__device__ __forceinline__ void mma_16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2,
+                                          uint32_t a3, uint32_t b0, uint32_t b1) {
+  asm("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 "
+      "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+__device__ __forceinline__ uint32_t lo_pair(uint32_t x, uint32_t y) { return __byte_perm(x, y, 0x5410); }
+__device__ __forceinline__ uint32_t hi_pair(uint32_t x, uint32_t y) { return __byte_perm(x, y, 0x7632); }
+
+// ------------------------------------------------------ quad LUT region --
+// Four tables of half2 words: T0 = (norm, norm), T1 = (cos1, sin1),
+// T2 = (cos2, sin2), T3 = (cos3, sin3).  Table t is at region (t>>1)
+// (64 KiB each) and slot (t&1).
+constexpr uint32_t kQuadLutBytes = 2u * 65536u;
+
+__device__ __forceinline__ uint32_t lut_off(int table) {
+  return (uint32_t)(table >> 1) * 65536u + (uint32_t)(table & 1) * 128u;
+}
+
+// Fill the replicated quad tables from the seven FP16[256] tables.
+// Called by every thread of the CTA; caller syncs afterwards.
+__device__ __forceinline__ void build_quad_lut(uint8_t* smem, const __half* const* luts) {
+  const uint16_t* norm = reinterpret_cast<const uint16_t*>(luts[0]);
+  // 4 tables x 256 entries x 8 uint4 stores (32 lane copies of 4 bytes)
+  for (int idx = threadIdx.x; idx < 4 * 256 * 8; idx += blockDim.x) {
+    const int t = idx >> 11, e = (idx >> 3) & 255, part = idx & 7;
+    uint32_t v;
+    if (t == 0) {
+      const uint32_t r = ldg_u16(norm + e);
+      v = r | (r << 16);
+    } else {
+      const uint16_t* c = reinterpret_cast<const uint16_t*>(luts[2 * t - 1]);
+      const uint16_t* s = reinterpret_cast<const uint16_t*>(luts[2 * t]);
+      v = (uint32_t)ldg_u16(c + e) | ((uint32_t)ldg_u16(s + e) << 16);
+    }
+    *reinterpret_cast<uint4*>(smem + lut_off(t) + (uint32_t)e * 256u + (uint32_t)part * 16u) =
+        make_uint4(v, v, v, v);
+  }
+}
+
+// Decoded tuple as three half2 words:
+//   p1 = (w1, rs), p2 = (w2, rss), p3 = (w3, w4)
+// following the FP16 product chain of the reference kernel: every product
+// rounds to FP16 (round to nearest even) exactly once.
+struct QuadDec {
+  uint32_t p1, p2, p3;
+};
+
+__device__ __forceinline__ QuadDec decode_quad(uint32_t code, const uint8_t* lut, uint32_t laneoff) {
+  const uint32_t o0 = __byte_perm(code, laneoff, 0x7634);  // norm index (byte 3)
+  const uint32_t o1 = __byte_perm(code, laneoff, 0x7624);  // t1 index   (byte 2)
+  const uint32_t o2 = __byte_perm(code, laneoff, 0x7614);  // t2 index   (byte 1)
+  const uint32_t o3 = __byte_perm(code, laneoff, 0x7604);  // t3 index   (byte 0)
+  const uint32_t rr = *reinterpret_cast<const uint32_t*>(lut + o0);
+  const uint32_t cs1 = *reinterpret_cast<const uint32_t*>(lut + 128u + o1);
+  const uint32_t cs2 = *reinterpret_cast<const uint32_t*>(lut + 65536u + o2);
+  const uint32_t cs3 = *reinterpret_cast<const uint32_t*>(lut + 65536u + 128u + o3);
+  const __half2 p1 = __hmul2_rn(u2h(rr), u2h(cs1));                // (r*c1, r*s1)
+  const __half2 p2 = __hmul2_rn(__high2half2(p1), u2h(cs2));       // (rs*c2, rs*s2)
+  const __half2 p3 = __hmul2_rn(__high2half2(p2), u2h(cs3));       // (rss*c3, rss*s3)
+  return QuadDec{h2u(p1), h2u(p2), h2u(p3)};
+}
+
+// ------------------------------------------------------ dual LUT region --
+// Amplitude table: 64 FP32 entries, indexed by the raw code bits 15..10
+// (the +32768 bias of the stored int16 flips bit 15, folded into the
+// table order).  Phase table: 1024 half2 (cos, sin) entries.  Entry
+// stride 128 bytes (32 lanes x 4 bytes) in both.
+constexpr uint32_t kDualAmpBytes = 64u * 128u;
+constexpr uint32_t kDualPhaseBytes = 1024u * 128u;
+constexpr uint32_t kDualLutBytes = kDualAmpBytes + kDualPhaseBytes;
+
+__device__ __forceinline__ void build_dual_lut(uint8_t* smem, const __half* amp_lut, const __half* cos_lut,
+                                               const __half* sin_lut) {
+  const uint16_t* a = reinterpret_cast<const uint16_t*>(amp_lut);
+  const uint16_t* c = reinterpret_cast<const uint16_t*>(cos_lut);
+  const uint16_t* s = reinterpret_cast<const uint16_t*>(sin_lut);
+  for (int idx = threadIdx.x; idx < (64 + 1024) * 8; idx += blockDim.x) {
+    const int e = idx >> 3, part = idx & 7;
+    uint32_t v;
+    uint32_t off;
+    if (e < 64) {
+      // stored bits b = ((u >> 10) & 63) ^ 32 where u = p + 32768
+      const float f = __half2float(__ushort_as_half(ldg_u16(a + (e ^ 32))));
+      v = __float_as_uint(f);
+      off = (uint32_t)e * 128u;
+    } else {
+      const int ph = e - 64;
+      v = (uint32_t)ldg_u16(c + ph) | ((uint32_t)ldg_u16(s + ph) << 16);
+      off = kDualAmpBytes + (uint32_t)ph * 128u;
+    }
+    *reinterpret_cast<uint4*>(smem + off + (uint32_t)part * 16u) = make_uint4(v, v, v, v);
+  }
+}
+
+}  // namespace pp

@@ -1,0 +1,240 @@
+// Quad-pack decode-only kernels: FP16 weight restore and plug-table indexing.
+//
+//  * quad_decode_kernel  -- (R, C) codes -> four (R, C) FP16 matrices with the
+//    same replicated shared-memory tables and FP16 chain as the GEMV.
+//  * quad_plug_scatter   -- overwrite plugged positions with the plug table's
+//    FP16 4-tuples (optionally scaled), the in-memory merge of
+//    quaternion_packer.py:187-193.
+//  * quad_plug_index     -- per (row, 64-column window) bitmask of plugged
+//    columns and the index of the window's first plug, the form the fused
+//    Linear kernel reads.
+#include "pp_common.cuh"
+#include "pp_host.h"
+
+namespace pp {
+
+struct QuadDecodeParams {
+  const uint32_t* codes;
+  int64_t ldc_r, ldc_c, R, C;
+  const __half* luts[7];
+  float scale[4];
+  int scaled;
+  __half* out[4];
+  int64_t ldo_r, ldo_c;
+};
+
+__global__ void __launch_bounds__(512, 1) quad_decode_kernel(const QuadDecodeParams p) {
+  extern __shared__ __align__(1024) uint8_t smem[];
+  build_quad_lut(smem, p.luts);
+  __syncthreads();
+  const uint32_t laneoff = (threadIdx.x & 31) * 4u;
+  const int64_t total = p.R * p.C;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t r = i / p.C, c = i - r * p.C;
+    const uint32_t code = __ldg(p.codes + r * p.ldc_r + c * p.ldc_c);
+    const QuadDec d = decode_quad(code, smem, laneoff);
+    __half w[4] = {__low2half(u2h(d.p1)), __low2half(u2h(d.p2)), __low2half(u2h(d.p3)),
+                   __high2half(u2h(d.p3))};
+    const int64_t o = r * p.ldo_r + c * p.ldo_c;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      __half v = w[k];
+      if (p.scaled) v = __float2half_rn(__half2float(v) * p.scale[k]);
+      p.out[k][o] = v;
+    }
+  }
+}
+
+struct QuadScatterParams {
+  const uint32_t* plug_idx;
+  const uint2* plug_vals;
+  int64_t p_lo, p_hi, n;
+  uint32_t base;
+  float scale[4];
+  int scaled;
+  __half* out[4];
+};
+
+__global__ void quad_plug_scatter(const QuadScatterParams p) {
+  for (int64_t j = p.p_lo + blockIdx.x * (int64_t)blockDim.x + threadIdx.x; j < p.p_hi;
+       j += (int64_t)gridDim.x * blockDim.x) {
+    const uint32_t loc = __ldg(p.plug_idx + j) - p.base;
+    if ((int64_t)loc >= p.n) continue;
+    const uint2 v = __ldg(p.plug_vals + j);
+    const uint16_t h[4] = {(uint16_t)(v.x & 0xFFFF), (uint16_t)(v.x >> 16), (uint16_t)(v.y & 0xFFFF),
+                           (uint16_t)(v.y >> 16)};
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      __half x = __ushort_as_half(h[k]);
+      if (p.scaled) x = __float2half_rn(__half2float(x) * p.scale[k]);
+      p.out[k][loc] = x;
+    }
+  }
+}
+
+__global__ void fill_zero_u32(uint32_t* p, int64_t n) {
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
+    p[i] = 0u;
+}
+
+struct PlugIndexParams {
+  const uint32_t* plug_idx;
+  int64_t p_lo, p_hi;
+  uint32_t base;
+  int64_t N, K, W;
+  unsigned long long* mask;
+  uint32_t* first;
+  int* bad;
+};
+
+__global__ void quad_plug_index_kernel(const PlugIndexParams p) {
+  const uint64_t span = (uint64_t)p.N * (uint64_t)p.K;
+  for (int64_t j = p.p_lo + blockIdx.x * (int64_t)blockDim.x + threadIdx.x; j < p.p_hi;
+       j += (int64_t)gridDim.x * blockDim.x) {
+    const uint32_t loc = __ldg(p.plug_idx + j) - p.base;
+    bool ok = (uint64_t)loc < span;
+    bool head = true;
+    if (ok && j > p.p_lo) {
+      const uint32_t prev = __ldg(p.plug_idx + j - 1) - p.base;
+      if ((uint64_t)prev < span) {
+        if (prev >= loc) ok = false;  // positions must strictly increase
+        head = (prev / (uint64_t)p.K != loc / (uint64_t)p.K) ||
+               ((prev % (uint64_t)p.K) >> 6) != ((loc % (uint64_t)p.K) >> 6);
+      }
+    }
+    if (!ok) {
+      if (p.bad) atomicAdd(p.bad, 1);
+      continue;
+    }
+    const uint64_t n = loc / (uint64_t)p.K, k = loc % (uint64_t)p.K;
+    const int64_t w = (int64_t)n * p.W + (int64_t)(k >> 6);
+    atomicOr(p.mask + w, 1ull << (k & 63));
+    if (head) p.first[w] = (uint32_t)(j - p.p_lo);
+  }
+}
+
+namespace {
+bool g_decode_attr[64];
+
+int grid_for(int64_t n, int threads) {
+  const int64_t b = cdiv(n, threads);
+  return (int)(b < 65535 ? (b > 0 ? b : 1) : 65535);
+}
+}  // namespace
+
+static int quad_decode_impl(const uint32_t* codes, int64_t ldc_r, int64_t ldc_c, int64_t R, int64_t C,
+                            const void* const luts[7], const float* scales, void* const out[4],
+                            int64_t ldo_r, int64_t ldo_c, cudaStream_t s) {
+  if (R < 0 || C < 0 || !luts || !out) {
+    set_error("invalid arguments to quad decode");
+    return PP_ERR_INVALID;
+  }
+  if (R == 0 || C == 0) return PP_OK;
+  if (!codes) {
+    set_error("codes is NULL");
+    return PP_ERR_INVALID;
+  }
+  QuadDecodeParams prm{};
+  prm.codes = codes;
+  prm.ldc_r = ldc_r;
+  prm.ldc_c = ldc_c;
+  prm.R = R;
+  prm.C = C;
+  for (int i = 0; i < 7; ++i) {
+    if (!luts[i]) {
+      set_error("luts[%d] is NULL", i);
+      return PP_ERR_INVALID;
+    }
+    prm.luts[i] = reinterpret_cast<const __half*>(luts[i]);
+  }
+  for (int i = 0; i < 4; ++i) {
+    if (!out[i]) {
+      set_error("out[%d] is NULL", i);
+      return PP_ERR_INVALID;
+    }
+    prm.out[i] = reinterpret_cast<__half*>(out[i]);
+    prm.scale[i] = scales ? scales[i] : 1.f;
+  }
+  prm.scaled = scales ? 1 : 0;
+  prm.ldo_r = ldo_r;
+  prm.ldo_c = ldo_c;
+  int rc = ensure_smem_attr(quad_decode_kernel, (int)kQuadLutBytes, g_decode_attr);
+  if (rc) return rc;
+  const int sms = device_sm_count(current_device());
+  const int64_t want = cdiv(R * C, 512);
+  const int grid = (int)(want < sms ? want : sms);
+  quad_decode_kernel<<<grid > 0 ? grid : 1, 512, kQuadLutBytes, s>>>(prm);
+  return check_launch("quad_decode_kernel");
+}
+
+}  // namespace pp
+
+extern "C" {
+
+int pp_quad_decode(const uint32_t* codes, int64_t ldc_r, int64_t ldc_c, int64_t R, int64_t C,
+                   const void* const luts[7], const float* scales, void* const out[4], int64_t ldo_r,
+                   int64_t ldo_c, void* stream) {
+  return pp::quad_decode_impl(codes, ldc_r, ldc_c, R, C, luts, scales, out, ldo_r, ldo_c,
+                              reinterpret_cast<cudaStream_t>(stream));
+}
+
+int pp_quad_unpack(const uint32_t* codes, int64_t n, const uint32_t* plug_idx, const void* plug_vals,
+                   int64_t p_lo, int64_t p_hi, uint32_t base_lo32, const void* const luts[7],
+                   const float* scales, void* const out[4], void* stream) {
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  if (n < 0 || p_lo < 0 || p_hi < p_lo) {
+    pp::set_error("invalid arguments to quad unpack");
+    return PP_ERR_INVALID;
+  }
+  int rc = pp::quad_decode_impl(codes, 0, 1, 1, n, luts, scales, out, 0, 1, s);
+  if (rc) return rc;
+  if (p_hi == p_lo || n == 0) return PP_OK;
+  if (!plug_idx || !plug_vals || !pp::aligned(plug_vals, 8)) {
+    pp::set_error("plug_idx / plug_vals missing or plug_vals not 8-byte aligned");
+    return PP_ERR_INVALID;
+  }
+  pp::QuadScatterParams sp{};
+  sp.plug_idx = plug_idx;
+  sp.plug_vals = reinterpret_cast<const uint2*>(plug_vals);
+  sp.p_lo = p_lo;
+  sp.p_hi = p_hi;
+  sp.n = n;
+  sp.base = base_lo32;
+  for (int i = 0; i < 4; ++i) {
+    sp.out[i] = reinterpret_cast<__half*>(out[i]);
+    sp.scale[i] = scales ? scales[i] : 1.f;
+  }
+  sp.scaled = scales ? 1 : 0;
+  pp::quad_plug_scatter<<<pp::grid_for(p_hi - p_lo, 256), 256, 0, s>>>(sp);
+  return pp::check_launch("quad_plug_scatter");
+}
+
+int pp_quad_plug_index(const uint32_t* plug_idx, int64_t p_lo, int64_t p_hi, uint32_t base_lo32, int64_t N,
+                       int64_t K, uint64_t* plug_mask, uint32_t* plug_base, int* bad_count, void* stream) {
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  if (N < 0 || K <= 0 || p_lo < 0 || p_hi < p_lo || !plug_mask || !plug_base) {
+    pp::set_error("invalid arguments to quad plug index");
+    return PP_ERR_INVALID;
+  }
+  const int64_t W = pp::cdiv(K, 64);
+  const int64_t words = N * W;
+  if (words == 0) return PP_OK;
+  pp::fill_zero_u32<<<pp::grid_for(2 * words, 256), 256, 0, s>>>(reinterpret_cast<uint32_t*>(plug_mask),
+                                                                  2 * words);
+  int rc = pp::check_launch("fill_zero_u32");
+  if (rc) return rc;
+  pp::fill_zero_u32<<<pp::grid_for(words, 256), 256, 0, s>>>(plug_base, words);
+  if ((rc = pp::check_launch("fill_zero_u32"))) return rc;
+  if (p_hi == p_lo) return PP_OK;
+  if (!plug_idx) {
+    pp::set_error("plug_idx is NULL");
+    return PP_ERR_INVALID;
+  }
+  pp::PlugIndexParams prm{plug_idx, p_lo, p_hi, base_lo32, N, K, W,
+                          reinterpret_cast<unsigned long long*>(plug_mask), plug_base, bad_count};
+  pp::quad_plug_index_kernel<<<pp::grid_for(p_hi - p_lo, 256), 256, 0, s>>>(prm);
+  return pp::check_launch("quad_plug_index_kernel");
+}
+
+}  // extern "C"

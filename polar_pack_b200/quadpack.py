@@ -1,0 +1,356 @@
+"""``.quadpack`` v2 streams on the GPU: reader, device upload, fused Linear.
+
+Format (reference quaternion_packer.py:13-19, 93-132, 155-157)::
+
+    header '<4sBBQBBBBfQ4ff4Q' (82 B): magic 'QUAD', version 2, n_models 4,
+        n_min, bits (8, 8, 8, 8), mu, plug_n, rms s_0..s_3, r_max, tails_0..3
+    codes     uint32[n_min]        word = nq<<24 | q1<<16 | q2<<8 | q3
+    plug_idx  uint32[plug_n]       ascending flat positions
+    plug_vals fp16[plug_n, 4]      RMS-normalised exact 4-tuples
+    tail_k    fp16[tails_k]        raw weights of model k beyond n_min
+
+Each ``nn.Linear`` of the packed models is an ``(out, in)`` row-major slice
+of the flat stream, in the layer-map order of ``collect_weights``
+(polar_main.py:25-51).  A :class:`QuadPackDevice` keeps codes and plug
+values resident in HBM; :meth:`QuadPackDevice.linear` returns a
+:class:`QuadLinearSlice` whose forward is one fused kernel launch
+(``pp_quad_linear``) producing the four models' outputs.
+"""
+from __future__ import annotations
+
+import ctypes
+import struct
+from dataclasses import dataclass, field
+from pathlib import Path
+
+import numpy as np
+import torch
+
+from . import _lib
+from .quad_kernels import quad_luts
+
+MAGIC = b"QUAD"
+VERSION = 2
+N_MODELS = 4
+MU = 255.0
+HEADER_FMT = "<4sBBQBBBBfQ4ff4Q"
+HEADER_SIZE = struct.calcsize(HEADER_FMT)
+
+
+@dataclass
+class QuadHeader:
+    n: int
+    plug_n: int
+    scales: list
+    r_max: float
+    tails: list
+    mu: float = MU
+    bits: tuple = (8, 8, 8, 8)
+
+    @classmethod
+    def parse(cls, buf) -> "QuadHeader":
+        if len(buf) < HEADER_SIZE:
+            raise ValueError("truncated .quadpack header")
+        h = struct.unpack(HEADER_FMT, bytes(buf[:HEADER_SIZE]))
+        magic, ver, nm, n, nb, b1, b2, b3, mu, plug_n = h[:10]
+        if magic != MAGIC or ver != VERSION:
+            raise ValueError(f"not a .quadpack v{VERSION} stream (magic={magic!r}, version={ver})")
+        if nm != N_MODELS or (nb, b1, b2, b3) != (8, 8, 8, 8):
+            raise ValueError("only 4-model 8+8+8+8-bit .quadpack streams are defined")
+        return cls(n=n, plug_n=plug_n, scales=list(h[10:14]), r_max=h[14], tails=list(h[15:19]),
+                   mu=mu, bits=(nb, b1, b2, b3))
+
+    def offsets(self) -> dict:
+        codes = HEADER_SIZE
+        plug_idx = codes + 4 * self.n
+        plug_vals = plug_idx + 4 * self.plug_n
+        tails = plug_vals + 8 * self.plug_n
+        return dict(codes=codes, plug_idx=plug_idx, plug_vals=plug_vals, tails=tails,
+                    end=tails + 2 * sum(self.tails))
+
+
+def unwrap_u32_positions(idx_u32: np.ndarray) -> np.ndarray:
+    """True int64 positions of an ascending plug index stored as uint32.
+
+    The reference writes positions as uint32 (quaternion_packer.py:107);
+    streams longer than 2^32 tuples wrap.  The true sequence is strictly
+    increasing, so every decrease marks one more wrap.
+    """
+    x = idx_u32.astype(np.int64)
+    if x.size < 2:
+        return x
+    wraps = np.concatenate([[0], np.cumsum(np.diff(x) < 0)])
+    return x + (wraps.astype(np.int64) << 32)
+
+
+class QuadPackFile:
+    """Host view of a ``.quadpack`` stream (file path, bytes or numpy buffer)."""
+
+    def __init__(self, src):
+        if isinstance(src, (str, Path)):
+            self.buf = np.memmap(str(src), dtype=np.uint8, mode="r")
+        else:
+            self.buf = np.frombuffer(src, dtype=np.uint8) if isinstance(src, (bytes, bytearray)) else src
+        self.header = QuadHeader.parse(self.buf[:HEADER_SIZE])
+        off = self.header.offsets()
+        if self.buf.size < off["end"]:
+            raise ValueError(f"truncated .quadpack stream: {self.buf.size} bytes, header needs {off['end']}")
+        h = self.header
+        self.codes = self.buf[off["codes"]:off["plug_idx"]].view(np.uint32)
+        self.plug_idx = self.buf[off["plug_idx"]:off["plug_vals"]].view(np.uint32)
+        self.plug_vals = self.buf[off["plug_vals"]:off["tails"]].view(np.float16).reshape(-1, 4)
+        self.tails = []
+        o = off["tails"]
+        for t in h.tails:
+            self.tails.append(self.buf[o:o + 2 * t].view(np.float16))
+            o += 2 * t
+        self.plug_pos = unwrap_u32_positions(np.asarray(self.plug_idx))
+        if self.plug_pos.size and (np.any(np.diff(self.plug_pos) <= 0) or self.plug_pos[-1] >= h.n):
+            raise ValueError("plug index is not strictly increasing inside [0, n)")
+
+    def plug_range(self, start: int, stop: int) -> tuple[int, int]:
+        """Slice ``[lo, hi)`` of the plug table covering flat positions ``[start, stop)``."""
+        return (int(np.searchsorted(self.plug_pos, start)), int(np.searchsorted(self.plug_pos, stop)))
+
+
+@dataclass
+class QuadLinearSlice:
+    """One packed ``nn.Linear`` (out=N, in=K) of a device-resident stream."""
+    pack: "QuadPackDevice"
+    offset: int
+    N: int
+    K: int
+    p_lo: int
+    p_hi: int
+    codes: torch.Tensor
+    plug_vals: torch.Tensor | None
+    plug_mask: torch.Tensor | None
+    plug_base: torch.Tensor | None
+    _ws: dict = field(default_factory=dict)
+
+    @property
+    def nbytes_stream(self) -> int:
+        """Algorithmic bytes of one pass: codes + plug entries (index + values)."""
+        return 4 * self.N * self.K + 12 * (self.p_hi - self.p_lo)
+
+    def __call__(self, x: torch.Tensor, out=None) -> list[torch.Tensor]:
+        return quad_linear(x, self, out=out)
+
+
+class QuadPackDevice:
+    """Codes, plug table and FP16 tables of a ``.quadpack`` stream resident on a GPU."""
+
+    def __init__(self, f: QuadPackFile, device):
+        self.file = f
+        self.header = f.header
+        self.device = torch.device(device)
+        h = f.header
+        self.codes = torch.from_numpy(np.asarray(f.codes)).to(self.device)
+        self.plug_idx = torch.from_numpy(np.asarray(f.plug_idx).view(np.int32)).to(self.device)
+        self.plug_vals = torch.from_numpy(np.ascontiguousarray(f.plug_vals)).to(self.device)
+        self.luts = [t.to(self.device) for t in quad_luts(h.r_max, MU)]
+        self.scales = [float(s) for s in h.scales]
+        self._bad = torch.zeros(1, dtype=torch.int32, device=self.device)
+
+    def _plug_range(self, start: int, stop: int) -> tuple[int, int]:
+        return self.file.plug_range(start, stop)
+
+    def linear(self, offset: int, N: int, K: int) -> QuadLinearSlice:
+        """The Linear whose ``(N, K)`` weights start at flat position ``offset``."""
+        n = self.header.n
+        if offset < 0 or offset + N * K > n:
+            raise ValueError(f"Linear [{offset}, {offset + N * K}) is outside the coded range [0, {n})")
+        p_lo, p_hi = self._plug_range(offset, offset + N * K)
+        codes = self.codes[offset:offset + N * K].view(N, K)
+        pv = pm = pb = None
+        if p_hi > p_lo:
+            W = -(-K // 64)
+            pm = torch.empty((N, W), dtype=torch.int64, device=self.device)
+            pb = torch.empty((N, W), dtype=torch.int32, device=self.device)
+            _lib.call("pp_quad_plug_index", self.plug_idx.data_ptr(), p_lo, p_hi,
+                      ctypes.c_uint32(offset & 0xFFFFFFFF), N, K, pm.data_ptr(), pb.data_ptr(),
+                      self._bad.data_ptr(), _lib.stream_handle(self.device))
+            pv = self.plug_vals[p_lo:p_hi]
+        return QuadLinearSlice(self, offset, N, K, p_lo, p_hi, codes, pv, pm, pb)
+
+    def check_plug_index(self) -> None:
+        """Raise if any plug entry fell outside its Linear (syncs the device)."""
+        bad = int(self._bad.item())
+        if bad:
+            raise ValueError(f"{bad} plug entries outside their Linear or out of order")
+
+    def unpack(self, start: int = 0, stop: int | None = None, scaled: bool = True) -> list[torch.Tensor]:
+        """GPU restore of flat positions ``[start, stop)`` into 4 FP16 vectors.
+
+        FP16 table decode with plug substitution (quaternion_packer.py:170-196
+        on the FP16 tables), optionally ``* s_k`` (one FP32 product, one FP16
+        rounding).
+        """
+        stop = self.header.n if stop is None else stop
+        n = stop - start
+        outs = [torch.empty(n, dtype=torch.float16, device=self.device) for _ in range(4)]
+        p_lo, p_hi = self._plug_range(start, stop)
+        sc = _lib.floats4(self.scales) if scaled else None
+        _lib.call("pp_quad_unpack", self.codes[start:].data_ptr() if n else self.codes.data_ptr(), n,
+                  self.plug_idx.data_ptr(), self.plug_vals.data_ptr(), p_lo, p_hi,
+                  ctypes.c_uint32(start & 0xFFFFFFFF), _lib.ptrs(self.luts, 7),
+                  ctypes.cast(sc, ctypes.c_void_p) if sc is not None else None,
+                  _lib.ptrs(outs, 4), _lib.stream_handle(self.device))
+        return outs
+
+
+def quad_linear_workspace_bytes(M: int, N: int, K: int) -> int:
+    nbytes = _lib._size_t()
+    _lib.check(_lib.load().pp_quad_linear_workspace_bytes(M, N, K, ctypes.byref(nbytes)))
+    return nbytes.value
+
+
+def quad_linear(x: torch.Tensor, layer: QuadLinearSlice, out=None) -> list[torch.Tensor]:
+    """``[y_k]``, ``y_k = fp16(s_k * x @ Wp_k^T)`` for one packed Linear.
+
+    ``x`` is FP16 ``(M, K)`` (any strides).  ``Wp_k`` is the FP16 decode with
+    plug values substituted; one kernel launch streams the codes once.
+    """
+    if x.dim() != 2 or x.shape[1] != layer.K:
+        raise ValueError(f"x must be (M, {layer.K}), got {tuple(x.shape)}")
+    if x.dtype != torch.float16:
+        raise ValueError("x must be fp16")
+    dev = _lib.require_cuda(x, layer.codes)
+    M = x.shape[0]
+    if out is None:
+        out = [torch.empty((M, layer.N), dtype=torch.float16, device=dev) for _ in range(4)]
+    nb = quad_linear_workspace_bytes(M, layer.N, layer.K)
+    ws = _lib.workspace(dev, nb) if nb else None
+    pk = layer.pack
+    _lib.call("pp_quad_linear", x.data_ptr(), x.stride(0), x.stride(1), layer.codes.data_ptr(), layer.K,
+              _lib.ptr(layer.plug_vals), _lib.ptr(layer.plug_mask), _lib.ptr(layer.plug_base),
+              _lib.ptrs(pk.luts, 7), _lib.floats4(pk.scales), _lib.ptrs(out, 4),
+              out[0].stride(0), out[0].stride(1), M, layer.N, layer.K,
+              _lib.ptr(ws), ws.numel() if ws is not None else 0, _lib.stream_handle(dev))
+    return out
+
+
+def layer_offsets(layer_map: list[dict]) -> list[tuple[str, int, tuple[int, int]]]:
+    """``(name, flat offset, (out, in))`` per entry of a ``collect_weights`` layer map.
+
+    The offset is the running sum of ``numel`` in map order, as
+    ``replace_model_weights`` walks it (polar_packer.py:296-316).
+    """
+    res, off = [], 0
+    for e in layer_map:
+        shape = tuple(int(s) for s in e["shape"])
+        res.append((e["name"], off, shape))
+        off += int(e["numel"])
+    return res
+
+
+# ------------------------------------------------------------ GPU packer --
+def _quantize_chunk_torch(wc, r_max: float, with_err: bool):
+    """Codes (and relative decode error) of one chunk; quaternion_packer.py:30-49.
+
+    Codes come from float32 math on the normalised weights; the error uses
+    float64 like the reference's ``thr_collect`` branch.
+    """
+    import math
+    w1, w2, w3, w4 = wc
+    r = torch.sqrt(w1 * w1 + w2 * w2 + w3 * w3 + w4 * w4)
+    t1 = torch.atan2(torch.sqrt(w2 * w2 + w3 * w3 + w4 * w4), w1)
+    t2 = torch.atan2(torch.sqrt(w3 * w3 + w4 * w4), w2)
+    t3 = torch.remainder(torch.atan2(w4, w3), 2 * math.pi)
+    log_mu = math.log1p(MU)
+    nq = torch.round(torch.log1p(MU * r / r_max) / log_mu * 255).clamp(0, 255).to(torch.int64)
+    q1 = torch.round(t1 / math.pi * 255).clamp(0, 255).to(torch.int64)
+    q2 = torch.round(t2 / math.pi * 255).clamp(0, 255).to(torch.int64)
+    q3 = torch.round(t3 / (2 * math.pi) * 255).clamp(0, 255).to(torch.int64)
+    codes = ((nq << 24) | (q1 << 16) | (q2 << 8) | q3).to(torch.uint32)
+    if not with_err:
+        return codes, None
+    rr = (torch.exp(nq.double() / 255 * log_mu) - 1) * r_max / MU
+    a1, a2, a3 = q1.double() / 255 * math.pi, q2.double() / 255 * math.pi, q3.double() / 255 * 2 * math.pi
+    s1, s2 = torch.sin(a1), torch.sin(a2)
+    rw = (rr * torch.cos(a1), rr * s1 * torch.cos(a2), rr * s1 * s2 * torch.cos(a3), rr * s1 * s2 * torch.sin(a3))
+    err = torch.sqrt(sum((wc[k].double() - rw[k]) ** 2 for k in range(4))) / torch.clamp(r.double(), min=1e-12)
+    return codes, err
+
+
+def pack_quad_device(models, plug_cap: float = 0.05, seed: int = 42, windows: int = 100,
+                     window: int = 1_000_000, chunk: int = 1 << 24) -> dict:
+    """Pack four 1-D weight tensors into ``.quadpack`` v2 sections on their device.
+
+    Restates pack_quad (quaternion_packer.py:52-138): pass A float64 RMS on
+    the common length, pass B ``r_max * 1.001`` and the ``(1 - plug_cap)``
+    percentile of the decode error over ``windows`` random windows drawn with
+    numpy's ``default_rng(seed)``, pass C codes and plug entries (ascending
+    positions, FP16 normalised 4-tuples), then raw FP16 tails.  Returns a
+    dict of device tensors plus header fields; :func:`to_bytes` serialises
+    it.  Transcendentals run on the GPU, so a code can differ from the numpy
+    writer's by one step where a value sits on a rounding boundary.
+    """
+    dev = models[0].device
+    lengths = [int(m.numel()) for m in models]
+    n = min(lengths)
+    tails = [L - n for L in lengths]
+    s = [float(torch.sqrt((m[:n].double() ** 2).sum() / n)) for m in models]
+    r_max = 0.0
+    for i in range(0, n, chunk):
+        wc = [m[i:min(i + chunk, n)].float() / sk for m, sk in zip(models, s)]
+        r_max = max(r_max, float(torch.sqrt(sum(x * x for x in wc)).max()))
+    r_max *= 1.001
+    window = min(window, max(1, n - 1))
+    rng = np.random.default_rng(seed)
+    starts = rng.integers(0, max(1, n - window), windows)
+    errs = []
+    for st in starts:
+        wc = [m[st:st + window].float() / sk for m, sk in zip(models, s)]
+        errs.append(_quantize_chunk_torch(wc, r_max, True)[1].cpu().numpy())
+    thr = float(np.percentile(np.concatenate(errs), (1 - plug_cap) * 100))
+    codes = torch.empty(n, dtype=torch.uint32, device=dev)
+    pidx, pval = [], []
+    for i in range(0, n, chunk):
+        wc = [m[i:min(i + chunk, n)].float() / sk for m, sk in zip(models, s)]
+        c, err = _quantize_chunk_torch(wc, r_max, True)
+        codes[i:i + c.numel()] = c
+        mask = err > thr
+        idx = torch.nonzero(mask).flatten()
+        if idx.numel():
+            pidx.append(idx + i)
+            pval.append(torch.stack([w[idx] for w in wc], dim=1).half())
+    plug_idx = torch.cat(pidx) if pidx else torch.zeros(0, dtype=torch.int64, device=dev)
+    plug_vals = torch.cat(pval) if pval else torch.zeros((0, 4), dtype=torch.float16, device=dev)
+    tail_t = [m[n:].half() for m in models]
+    return dict(n=n, scales=s, r_max=r_max, tails=tails, codes=codes, plug_pos=plug_idx,
+                plug_vals=plug_vals, tail_vals=tail_t, threshold=thr)
+
+
+def to_bytes(p: dict) -> bytes:
+    """Serialise :func:`pack_quad_device` output as a ``.quadpack`` v2 stream."""
+    hdr = struct.pack(HEADER_FMT, MAGIC, VERSION, N_MODELS, p["n"], 8, 8, 8, 8, MU,
+                      int(p["plug_pos"].numel()), *p["scales"], p["r_max"], *p["tails"])
+    parts = [hdr, p["codes"].cpu().numpy().tobytes(),
+             (p["plug_pos"].cpu().numpy() & 0xFFFFFFFF).astype(np.uint32).tobytes(),
+             p["plug_vals"].cpu().numpy().tobytes()]
+    parts += [t.cpu().numpy().tobytes() for t in p["tail_vals"] if t.numel()]
+    return b"".join(parts)
+
+
+class DevicePackedStream(QuadPackDevice):
+    """A :class:`QuadPackDevice` built from :func:`pack_quad_device` output
+    without a host round trip (used for synthetic full-size streams)."""
+
+    def __init__(self, p: dict):
+        self.file = None
+        self.device = p["codes"].device
+        self.header = QuadHeader(n=p["n"], plug_n=int(p["plug_pos"].numel()), scales=list(p["scales"]),
+                                 r_max=p["r_max"], tails=list(p["tails"]))
+        self.codes = p["codes"]
+        pos = p["plug_pos"].to(torch.int64)
+        self._pos_host = pos.cpu().numpy()
+        self.plug_idx = (pos & 0xFFFFFFFF).to(torch.int64).to(torch.int32) if pos.numel() else \
+            torch.zeros(0, dtype=torch.int32, device=self.device)
+        self.plug_vals = p["plug_vals"].contiguous()
+        self.luts = [t.to(self.device) for t in quad_luts(p["r_max"], MU)]
+        self.scales = [float(x) for x in p["scales"]]
+        self._bad = torch.zeros(1, dtype=torch.int32, device=self.device)
+
+    def _plug_range(self, start: int, stop: int) -> tuple[int, int]:
+        return (int(np.searchsorted(self._pos_host, start)), int(np.searchsorted(self._pos_host, stop)))
