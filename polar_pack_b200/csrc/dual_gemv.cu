@@ -9,9 +9,9 @@
 // directly an mma fragment register.  One m16n8k16 per feature column
 // carries both models (rows 0-7 model 1, rows 8-15 model 2).
 //
-// The split of K over warps / CTAs and the deterministic workspace
-// reduction are the same as in the quad kernel.
+// Work partition and the deterministic split-K reduction: pp_engine.cuh.
 #include "pp_common.cuh"
+#include "pp_engine.cuh"
 #include "pp_host.h"
 
 namespace pp {
@@ -31,35 +31,36 @@ struct DualParams {
   __half* out[2];
   int64_t ldo_m, ldo_n;
   int M, N, K;
-  int64_t units;
-  int upt;
-  int active_warps;
-  int* counters;
-  float* slots;
+  Partition part;
   int xvec;
 };
 
-__device__ __forceinline__ int64_t dual_warp_of_unit(int64_t x, int64_t U, int64_t GW) {
-  int64_t w = ((x + 1) * GW + U - 1) / U - 1;
-  return w < GW - 1 ? w : GW - 1;
-}
+struct DualBuf {
+  uint4 q[4];
+  float sc[4];
+};
 
 template <int NB>
-struct DualWarp {
+struct DualOp {
+  static constexpr int kWarps = dual_warps(NB);
   static constexpr int kTileW = 64;
+  static constexpr int kNOut = 2;
   static constexpr int kNBat = 8 * NB;
-  static constexpr int kSlot = 2 * kNBat * kTileW;
+  static constexpr int kSlot = kNOut * kNBat * kTileW;
+  using Buf = DualBuf;
 
   const DualParams& p;
   const uint8_t* lut;
-  int lane, g, c;
+  int g, c;
   uint32_t laneoff;
   float acc[8][NB][4];
 
-  __device__ __forceinline__ DualWarp(const DualParams& p_, const uint8_t* lut_, int lane_)
-      : p(p_), lut(lut_), lane(lane_), g(lane_ >> 2), c(lane_ & 3), laneoff((uint32_t)lane_ * 4u) {
-    zero();
-  }
+  __device__ __forceinline__ DualOp(const DualParams& p_, const uint8_t* lut_)
+      : p(p_), lut(lut_), g((threadIdx.x & 31) >> 2), c(threadIdx.x & 3),
+        laneoff((threadIdx.x & 31) * 4u) {}
+
+  __device__ __forceinline__ int M() const { return p.M; }
+  __device__ __forceinline__ int64_t N() const { return p.N; }
 
   __device__ __forceinline__ void zero() {
 #pragma unroll
@@ -70,19 +71,17 @@ struct DualWarp {
         for (int j = 0; j < 4; ++j) acc[t][nb][j] = 0.f;
   }
 
-  __device__ __forceinline__ void load(uint4 (&buf)[4], float (&sc)[4], int64_t u) const {
-    const int64_t tile = u / p.upt;
-    const int kc = (int)(u - tile * p.upt);
+  __device__ __forceinline__ void load(Buf& b, int64_t tile, int kc) const {
     const int64_t f = tile * 64 + 8 * g;
 #pragma unroll
     for (int r = 0; r < 4; ++r) {
       const int k = kc * 16 + 2 * c + (r & 1) + 8 * (r >> 1);
       if (f < p.N && k < p.K) {
-        buf[r] = ldg_stream(p.codes + (int64_t)k * p.ldc + f);
-        sc[r] = __half2float(__ushort_as_half(ldg_u16(p.bmax + ((int64_t)k * p.N + f) / p.gs)));
+        b.q[r] = ldg_stream(p.codes + (int64_t)k * p.ldc + f);
+        b.sc[r] = __half2float(__ushort_as_half(ldg_u16(p.bmax + ((int64_t)k * p.N + f) / p.gs)));
       } else {
-        buf[r] = make_uint4(0, 0, 0, 0);
-        sc[r] = 0.f;
+        b.q[r] = make_uint4(0, 0, 0, 0);
+        b.sc[r] = 0.f;
       }
     }
   }
@@ -114,9 +113,7 @@ struct DualWarp {
     b2h = __fmul_rn(amph, __high2float(csh));
   }
 
-  __device__ __forceinline__ void compute(const uint4 (&buf)[4], const float (&sc)[4], int64_t u) {
-    const int64_t tile = u / p.upt;
-    const int kc = (int)(u - tile * p.upt);
+  __device__ __forceinline__ void compute(const Buf& b, int64_t tile, int kc) {
     const int kbase = kc * 16;
     uint32_t b0[NB], b1[NB];
 #pragma unroll
@@ -130,8 +127,8 @@ struct DualWarp {
       float w1l[4], w2l[4], w1h[4], w2h[4];
 #pragma unroll
       for (int r = 0; r < 4; ++r) {
-        const uint32_t w = j == 0 ? buf[r].x : j == 1 ? buf[r].y : j == 2 ? buf[r].z : buf[r].w;
-        decode2(w, sc[r], w1l[r], w2l[r], w1h[r], w2h[r]);
+        const uint32_t w = j == 0 ? b.q[r].x : j == 1 ? b.q[r].y : j == 2 ? b.q[r].z : b.q[r].w;
+        decode2(w, b.sc[r], w1l[r], w2l[r], w1h[r], w2h[r]);
       }
       // feature t = 2j (low codes) and t = 2j + 1 (high codes)
       const uint32_t al0 = h2u(__floats2half2_rn(w1l[0], w1l[1]));
@@ -151,23 +148,7 @@ struct DualWarp {
   }
 
   // Fragment register j: model (j >> 1), batch 8nb + 2c + (j & 1), feature 8g + t.
-  __device__ __forceinline__ void store_direct(int64_t tile) const {
-#pragma unroll
-    for (int t = 0; t < 8; ++t) {
-      const int64_t f = tile * 64 + 8 * g + t;
-      if (f >= p.N) continue;
-#pragma unroll
-      for (int nb = 0; nb < NB; ++nb)
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const int bat = nb * 8 + 2 * c + (j & 1);
-          if (bat < p.M)
-            p.out[j >> 1][(int64_t)bat * p.ldo_m + f * p.ldo_n] = __float2half_rn(acc[t][nb][j]);
-        }
-    }
-  }
-
-  __device__ __forceinline__ void store_partial(float* slot) const {
+  __device__ __forceinline__ void write_partial(float* red) const {
 #pragma unroll
     for (int t = 0; t < 8; ++t)
 #pragma unroll
@@ -175,94 +156,29 @@ struct DualWarp {
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
           const int bat = nb * 8 + 2 * c + (j & 1);
-          __stcg(slot + ((j >> 1) * kNBat + bat) * kTileW + 8 * g + t, acc[t][nb][j]);
+          red[((j >> 1) * kNBat + bat) * kTileW + 8 * g + t] = acc[t][nb][j];
         }
   }
 
-  __device__ __forceinline__ void finalize(int64_t tile, int64_t w_first, int64_t w_last) const {
-    const int64_t U = p.units, GW = p.active_warps;
-    const int64_t tile_u0 = tile * p.upt;
-    for (int e = lane; e < kSlot; e += 32) {
-      const int model = e / (kNBat * kTileW);
-      const int bat = (e / kTileW) % kNBat;
-      const int64_t f = tile * kTileW + e % kTileW;
-      float sum = 0.f;
-      for (int64_t w = w_first; w <= w_last; ++w) {
-        const int which = (U * w / GW >= tile_u0) ? 0 : 1;
-        sum += __ldcg(p.slots + (w * 2 + which) * kSlot + e);
-      }
-      if (bat < p.M && f < p.N) p.out[model][(int64_t)bat * p.ldo_m + f * p.ldo_n] = __float2half_rn(sum);
-    }
+  __device__ __forceinline__ void store(int model, int bat, int64_t f, float v) const {
+    p.out[model][(int64_t)bat * p.ldo_m + f * p.ldo_n] = __float2half_rn(v);
   }
 };
 
 template <int NB>
+constexpr int dual_red_bytes() {
+  return DualOp<NB>::kWarps * DualOp<NB>::kSlot * 4;
+}
+
+template <int NB>
 __global__ void __launch_bounds__(dual_warps(NB) * 32, 1) dual_gemv_kernel(const DualParams p) {
-  constexpr int kWarps = dual_warps(NB);
   extern __shared__ __align__(1024) uint8_t smem[];
-  build_dual_lut(smem, p.amp_lut, p.cos_lut, p.sin_lut);
+  __shared__ int s_flag;
+  float* red = reinterpret_cast<float*>(smem + kDualLutBytes);
+  build_dual_lut(smem, reinterpret_cast<uint32_t*>(red), p.amp_lut, p.cos_lut, p.sin_lut);
   __syncthreads();
-
-  const int lane = threadIdx.x & 31;
-  const int64_t gw = (int64_t)blockIdx.x * kWarps + (threadIdx.x >> 5);
-  if (gw >= p.active_warps) return;
-  const int64_t U = p.units, GW = p.active_warps;
-  const int64_t u_begin = U * gw / GW, u_end = U * (gw + 1) / GW;
-  const int upt = p.upt;
-
-  DualWarp<NB> wk(p, smem, lane);
-  int64_t pending[2];
-  int npend = 0;
-  const int64_t first_tile = u_begin / upt;
-
-  auto finish_unit = [&](int64_t u) {
-    const int64_t tile = u / upt;
-    const int64_t tile_u0 = tile * upt;
-    if (u - tile_u0 == upt - 1 || u == u_end - 1) {
-      const bool whole = (u_begin <= tile_u0) && (u - tile_u0 == upt - 1);
-      if (whole) {
-        wk.store_direct(tile);
-      } else {
-        const int which = tile == first_tile ? 0 : 1;
-        wk.store_partial(p.slots + (gw * 2 + which) * DualWarp<NB>::kSlot);
-        if (npend < 2) pending[npend++] = tile;
-      }
-      wk.zero();
-    }
-  };
-
-  uint4 bufA[4], bufB[4];
-  float scA[4], scB[4];
-  wk.load(bufA, scA, u_begin);
-  int64_t u = u_begin;
-  while (true) {
-    if (u + 1 < u_end) wk.load(bufB, scB, u + 1);
-    wk.compute(bufA, scA, u);
-    finish_unit(u);
-    if (++u >= u_end) break;
-    if (u + 1 < u_end) wk.load(bufA, scA, u + 1);
-    wk.compute(bufB, scB, u);
-    finish_unit(u);
-    if (++u >= u_end) break;
-  }
-
-  if (npend == 0) return;
-  __threadfence();
-  __syncwarp();
-  for (int i = 0; i < npend; ++i) {
-    const int64_t tile = pending[i];
-    const int64_t w_first = dual_warp_of_unit(tile * upt, U, GW);
-    const int64_t w_last = dual_warp_of_unit(tile * upt + upt - 1, U, GW);
-    int old = 0;
-    if (lane == 0) old = atomicAdd(p.counters + tile, 1);
-    old = __shfl_sync(0xffffffffu, old, 0);
-    if (old == (int)(w_last - w_first)) {
-      __threadfence();
-      wk.finalize(tile, w_first, w_last);
-      __syncwarp();
-      if (lane == 0) p.counters[tile] = 0;
-    }
-  }
+  DualOp<NB> op(p, smem);
+  run_partition(op, p.part, red, &s_flag);
 }
 
 // ------------------------------------------------ generic and decode ----
@@ -318,29 +234,9 @@ __global__ void dual_decode_kernel(const DualGenericParams p) {
 
 namespace {
 
-struct DualPlan {
-  int nb = 1;
-  int64_t tiles = 0, upt = 0, units = 0;
-  int grid = 0, active_warps = 0;
-  size_t counters_bytes = 0, slots_bytes = 0;
-  size_t total() const { return counters_bytes + slots_bytes; }
-};
-
-DualPlan dual_plan(int64_t Mc, int64_t N, int64_t K, int sms) {
-  DualPlan pl;
-  pl.nb = Mc > 8 ? 2 : 1;
-  pl.tiles = cdiv(N, 64);
-  pl.upt = cdiv(K, 16);
-  pl.units = pl.tiles * pl.upt;
-  if (pl.units == 0) return pl;
-  const int warps = dual_warps(pl.nb);
-  const int64_t want = cdiv(pl.units, warps);
-  pl.grid = (int)(want < sms ? want : sms);
-  const int64_t gw = (int64_t)pl.grid * warps;
-  pl.active_warps = (int)(gw < pl.units ? gw : pl.units);
-  pl.counters_bytes = align_up((size_t)pl.tiles * sizeof(int), 256);
-  pl.slots_bytes = (size_t)pl.active_warps * 2 * (2 * 8 * pl.nb * 64) * sizeof(float);
-  return pl;
+PartitionPlan dual_plan(int64_t Mc, int64_t N, int64_t K, int sms) {
+  const int nb = Mc > 8 ? 2 : 1;
+  return plan_partition(cdiv(N, 64), cdiv(K, 16), dual_warps(nb), sms, 2, Mc, 64);
 }
 
 bool g_dual_attr[2][64];
@@ -348,9 +244,11 @@ bool g_dual_attr[2][64];
 template <int NB>
 int launch_dual(const DualParams& prm, int grid, cudaStream_t s) {
   auto kern = dual_gemv_kernel<NB>;
-  int rc = ensure_smem_attr(kern, (int)kDualLutBytes, g_dual_attr[NB - 1]);
+  constexpr int smem = (int)kDualLutBytes + dual_red_bytes<NB>();
+  static_assert(smem <= 227 * 1024, "shared memory budget");
+  int rc = ensure_smem_attr(kern, smem, g_dual_attr[NB - 1]);
   if (rc) return rc;
-  kern<<<grid, dual_warps(NB) * 32, kDualLutBytes, s>>>(prm);
+  kern<<<grid, dual_warps(NB) * 32, smem, s>>>(prm);
   return check_launch("dual_gemv_kernel");
 }
 
@@ -443,18 +341,17 @@ static int dual_run(const void* a, int64_t lda_m, int64_t lda_k, const int16_t* 
   prm.K = (int)K;
   for (int64_t m0 = 0; m0 < M; m0 += 16) {
     const int64_t Mc = (M - m0) < 16 ? (M - m0) : 16;
-    DualPlan pl = dual_plan(Mc, N, K, sms);
+    const PartitionPlan pl = dual_plan(Mc, N, K, sms);
     prm.x = reinterpret_cast<const __half*>(a) + m0 * lda_m;
     prm.out[0] = reinterpret_cast<__half*>(out1) + m0 * ldo_m;
     prm.out[1] = reinterpret_cast<__half*>(out2) + m0 * ldo_m;
     prm.M = (int)Mc;
     prm.xvec = (lda_k == 1 && aligned(prm.x, 4) && (lda_m * 2) % 4 == 0) ? 1 : 0;
-    prm.units = pl.units;
-    prm.upt = (int)pl.upt;
-    prm.active_warps = pl.active_warps;
-    prm.counters = reinterpret_cast<int*>(ws);
-    prm.slots = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(ws) + pl.counters_bytes);
-    rc = pl.nb == 1 ? launch_dual<1>(prm, pl.grid, s) : launch_dual<2>(prm, pl.grid, s);
+    prm.part.units = pl.units;
+    prm.part.upt = (int)pl.upt;
+    prm.part.counters = reinterpret_cast<int*>(ws);
+    prm.part.slots = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(ws) + pl.counters_bytes);
+    rc = Mc <= 8 ? launch_dual<1>(prm, pl.grid, s) : launch_dual<2>(prm, pl.grid, s);
     if (rc) return rc;
   }
   return PP_OK;

@@ -60,22 +60,21 @@ __device__ __forceinline__ uint32_t lut_off(int table) {
   return (uint32_t)(table >> 1) * 65536u + (uint32_t)(table & 1) * 128u;
 }
 
-// Fill the replicated quad tables from the seven FP16[256] tables.
+// Fill the replicated quad tables from the seven FP16[256] tables.  The
+// 1024 source words are first gathered into `stage` (4 KiB of shared memory,
+// all global loads in flight at once), then fanned out to 32 lane copies.
 // Called by every thread of the CTA; caller syncs afterwards.
-__device__ __forceinline__ void build_quad_lut(uint8_t* smem, const __half* const* luts) {
-  const uint16_t* norm = reinterpret_cast<const uint16_t*>(luts[0]);
-  // 4 tables x 256 entries x 8 uint4 stores (32 lane copies of 4 bytes)
+__device__ __forceinline__ void build_quad_lut(uint8_t* smem, uint32_t* stage, const __half* const* luts) {
+  for (int i = threadIdx.x; i < 1024; i += blockDim.x) {
+    const int t = i >> 8, e = i & 255;
+    const uint16_t* a = reinterpret_cast<const uint16_t*>(luts[t == 0 ? 0 : 2 * t - 1]);
+    const uint16_t* b = reinterpret_cast<const uint16_t*>(luts[t == 0 ? 0 : 2 * t]);
+    stage[i] = (uint32_t)ldg_u16(a + e) | ((uint32_t)ldg_u16(b + e) << 16);
+  }
+  __syncthreads();
   for (int idx = threadIdx.x; idx < 4 * 256 * 8; idx += blockDim.x) {
     const int t = idx >> 11, e = (idx >> 3) & 255, part = idx & 7;
-    uint32_t v;
-    if (t == 0) {
-      const uint32_t r = ldg_u16(norm + e);
-      v = r | (r << 16);
-    } else {
-      const uint16_t* c = reinterpret_cast<const uint16_t*>(luts[2 * t - 1]);
-      const uint16_t* s = reinterpret_cast<const uint16_t*>(luts[2 * t]);
-      v = (uint32_t)ldg_u16(c + e) | ((uint32_t)ldg_u16(s + e) << 16);
-    }
+    const uint32_t v = stage[idx >> 3];
     *reinterpret_cast<uint4*>(smem + lut_off(t) + (uint32_t)e * 256u + (uint32_t)part * 16u) =
         make_uint4(v, v, v, v);
   }
@@ -113,25 +112,26 @@ constexpr uint32_t kDualAmpBytes = 64u * 128u;
 constexpr uint32_t kDualPhaseBytes = 1024u * 128u;
 constexpr uint32_t kDualLutBytes = kDualAmpBytes + kDualPhaseBytes;
 
-__device__ __forceinline__ void build_dual_lut(uint8_t* smem, const __half* amp_lut, const __half* cos_lut,
-                                               const __half* sin_lut) {
+__device__ __forceinline__ void build_dual_lut(uint8_t* smem, uint32_t* stage, const __half* amp_lut,
+                                               const __half* cos_lut, const __half* sin_lut) {
   const uint16_t* a = reinterpret_cast<const uint16_t*>(amp_lut);
   const uint16_t* c = reinterpret_cast<const uint16_t*>(cos_lut);
   const uint16_t* s = reinterpret_cast<const uint16_t*>(sin_lut);
-  for (int idx = threadIdx.x; idx < (64 + 1024) * 8; idx += blockDim.x) {
-    const int e = idx >> 3, part = idx & 7;
+  for (int e = threadIdx.x; e < 64 + 1024; e += blockDim.x) {
     uint32_t v;
-    uint32_t off;
     if (e < 64) {
       // stored bits b = ((u >> 10) & 63) ^ 32 where u = p + 32768
-      const float f = __half2float(__ushort_as_half(ldg_u16(a + (e ^ 32))));
-      v = __float_as_uint(f);
-      off = (uint32_t)e * 128u;
+      v = __float_as_uint(__half2float(__ushort_as_half(ldg_u16(a + (e ^ 32)))));
     } else {
-      const int ph = e - 64;
-      v = (uint32_t)ldg_u16(c + ph) | ((uint32_t)ldg_u16(s + ph) << 16);
-      off = kDualAmpBytes + (uint32_t)ph * 128u;
+      v = (uint32_t)ldg_u16(c + (e - 64)) | ((uint32_t)ldg_u16(s + (e - 64)) << 16);
     }
+    stage[e] = v;
+  }
+  __syncthreads();
+  for (int idx = threadIdx.x; idx < (64 + 1024) * 8; idx += blockDim.x) {
+    const int e = idx >> 3, part = idx & 7;
+    const uint32_t v = stage[e];
+    const uint32_t off = e < 64 ? (uint32_t)e * 128u : kDualAmpBytes + (uint32_t)(e - 64) * 128u;
     *reinterpret_cast<uint4*>(smem + off + (uint32_t)part * 16u) = make_uint4(v, v, v, v);
   }
 }

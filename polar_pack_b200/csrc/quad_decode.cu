@@ -25,7 +25,7 @@ struct QuadDecodeParams {
 
 __global__ void __launch_bounds__(512, 1) quad_decode_kernel(const QuadDecodeParams p) {
   extern __shared__ __align__(1024) uint8_t smem[];
-  build_quad_lut(smem, p.luts);
+  build_quad_lut(smem, reinterpret_cast<uint32_t*>(smem + kQuadLutBytes), p.luts);
   __syncthreads();
   const uint32_t laneoff = (threadIdx.x & 31) * 4u;
   const int64_t total = p.R * p.C;
@@ -159,12 +159,13 @@ static int quad_decode_impl(const uint32_t* codes, int64_t ldc_r, int64_t ldc_c,
   prm.scaled = scales ? 1 : 0;
   prm.ldo_r = ldo_r;
   prm.ldo_c = ldo_c;
-  int rc = ensure_smem_attr(quad_decode_kernel, (int)kQuadLutBytes, g_decode_attr);
+  constexpr int smem = (int)kQuadLutBytes + 4096;
+  int rc = ensure_smem_attr(quad_decode_kernel, smem, g_decode_attr);
   if (rc) return rc;
   const int sms = device_sm_count(current_device());
   const int64_t want = cdiv(R * C, 512);
   const int grid = (int)(want < sms ? want : sms);
-  quad_decode_kernel<<<grid > 0 ? grid : 1, 512, kQuadLutBytes, s>>>(prm);
+  quad_decode_kernel<<<grid > 0 ? grid : 1, 512, smem, s>>>(prm);
   return check_launch("quad_decode_kernel");
 }
 

@@ -16,15 +16,9 @@
 // The logical K order inside one mma is a permutation of the physical
 // order; the activation fragment uses the same permutation.
 //
-// Work partition: the units of all tiles (a tile = the output features one
-// warp accumulates) are laid out tile-major and split evenly over all warps
-// of a persistent grid (one 512-thread CTA per SM).  A tile wholly inside
-// one warp's range is stored directly.  A tile shared by several warps is
-// reduced through the workspace: each contributor writes an FP32 partial,
-// fences and bumps the tile's counter; the last arrival sums the partials
-// in fixed contributor order (deterministic), applies the scales, stores,
-// and resets the counter to zero.  Nothing ever waits on another warp.
+// Work partition and the deterministic split-K reduction: pp_engine.cuh.
 #include "pp_common.cuh"
+#include "pp_engine.cuh"
 #include "pp_host.h"
 
 namespace pp {
@@ -50,51 +44,40 @@ struct QuadParams {
   const unsigned long long* pmask;
   const uint32_t* pbase;
   int W;
-  // partition
-  int64_t units;
-  int upt;
-  int active_warps;
-  int* counters;
-  float* slots;
+  Partition part;
   int xvec;
 };
 
-template <bool NK>
-struct QuadGeom {
-  static constexpr int kTileW = NK ? 8 : 32;   // output features per tile
-  static constexpr int kUnitK = NK ? 64 : 16;  // K columns per unit
-  static constexpr int kT = NK ? 1 : 4;        // mma pairs per 16-k step
+struct QuadBuf {
+  uint4 q[4];
 };
 
-template <int NB, bool NK>
-constexpr int slot_floats() { return 4 * 8 * NB * QuadGeom<NK>::kTileW; }
-
-__device__ __forceinline__ int64_t warp_of_unit(int64_t x, int64_t U, int64_t GW) {
-  // largest w with floor(U*w/GW) <= x
-  int64_t w = ((x + 1) * GW + U - 1) / U - 1;
-  return w < GW - 1 ? w : GW - 1;
-}
-
 template <bool NK, int NB, bool PLUG>
-struct QuadWarp {
-  using G = QuadGeom<NK>;
-  static constexpr int kSlot = slot_floats<NB, NK>();
+struct QuadOp {
+  static constexpr int kWarps = quad_warps(NK, NB);
+  static constexpr int kTileW = NK ? 8 : 32;  // output features per tile
+  static constexpr int kT = NK ? 1 : 4;       // mma pairs per 16-k step
+  static constexpr int kNOut = 4;
   static constexpr int kNBat = 8 * NB;
+  static constexpr int kSlot = kNOut * kNBat * kTileW;
+  using Buf = QuadBuf;
 
   const QuadParams& p;
   const uint8_t* lut;
-  int lane, g, c;
+  int g, c;
   uint32_t laneoff;
-  float acc[G::kT][NB][2][4];
+  float acc[kT][NB][2][4];
 
-  __device__ __forceinline__ QuadWarp(const QuadParams& p_, const uint8_t* lut_, int lane_)
-      : p(p_), lut(lut_), lane(lane_), g(lane_ >> 2), c(lane_ & 3), laneoff((uint32_t)lane_ * 4u) {
-    zero();
-  }
+  __device__ __forceinline__ QuadOp(const QuadParams& p_, const uint8_t* lut_)
+      : p(p_), lut(lut_), g((threadIdx.x & 31) >> 2), c(threadIdx.x & 3),
+        laneoff((threadIdx.x & 31) * 4u) {}
+
+  __device__ __forceinline__ int M() const { return p.M; }
+  __device__ __forceinline__ int64_t N() const { return p.N; }
 
   __device__ __forceinline__ void zero() {
 #pragma unroll
-    for (int t = 0; t < G::kT; ++t)
+    for (int t = 0; t < kT; ++t)
 #pragma unroll
       for (int nb = 0; nb < NB; ++nb)
 #pragma unroll
@@ -103,26 +86,23 @@ struct QuadWarp {
           for (int j = 0; j < 4; ++j) acc[t][nb][h][j] = 0.f;
   }
 
-  // ---- loads -----------------------------------------------------------
-  __device__ __forceinline__ void load(uint4 (&buf)[4], int64_t u) const {
-    const int64_t tile = u / p.upt;
-    const int kc = (int)(u - tile * p.upt);
+  __device__ __forceinline__ void load(Buf& b, int64_t tile, int kc) const {
     if constexpr (NK) {
       const int64_t row = tile * 8 + g;
       const int kb = kc * 64 + 4 * c;
       const uint32_t* base = p.codes + row * p.ldc + kb;
 #pragma unroll
       for (int s = 0; s < 4; ++s) {
-        if (row < p.N && kb + 16 * s < p.K) buf[s] = ldg_stream(base + 16 * s);
-        else buf[s] = make_uint4(0, 0, 0, 0);
+        if (row < p.N && kb + 16 * s < p.K) b.q[s] = ldg_stream(base + 16 * s);
+        else b.q[s] = make_uint4(0, 0, 0, 0);
       }
     } else {
       const int64_t f = tile * 32 + 4 * g;
 #pragma unroll
       for (int r = 0; r < 4; ++r) {
         const int k = kc * 16 + 2 * c + (r & 1) + 8 * (r >> 1);
-        if (f < p.N && k < p.K) buf[r] = ldg_stream(p.codes + (int64_t)k * p.ldc + f);
-        else buf[r] = make_uint4(0, 0, 0, 0);
+        if (f < p.N && k < p.K) b.q[r] = ldg_stream(p.codes + (int64_t)k * p.ldc + f);
+        else b.q[r] = make_uint4(0, 0, 0, 0);
       }
     }
   }
@@ -139,7 +119,7 @@ struct QuadWarp {
   }
 
   __device__ __forceinline__ uint2 xquad(int bat, int k) const {
-    // activations (bat, k..k+3); NK path guarantees K % 4 == 0
+    // activations (bat, k..k+3); the NK path guarantees K % 4 == 0
     if (bat >= p.M || k >= p.K) return make_uint2(0u, 0u);
     const __half* row = p.x + (int64_t)bat * p.ldx_m;
     if (p.xvec) return ldg_u2(row + k);
@@ -149,10 +129,7 @@ struct QuadWarp {
     return make_uint2(h[0] | (h[1] << 16), h[2] | (h[3] << 16));
   }
 
-  // ---- one unit ---------------------------------------------------------
-  __device__ __forceinline__ void compute(const uint4 (&buf)[4], int64_t u) {
-    const int64_t tile = u / p.upt;
-    const int kc = (int)(u - tile * p.upt);
+  __device__ __forceinline__ void compute(const Buf& b, int64_t tile, int kc) {
     if constexpr (NK) {
       const int kbase = kc * 64;
       const int64_t row = tile * 8 + g;
@@ -170,10 +147,10 @@ struct QuadWarp {
       for (int s = 0; s < 4; ++s) {
         const int kp = kbase + 16 * s + 4 * c;
         QuadDec d[4];
-        d[0] = decode_quad(buf[s].x, lut, laneoff);
-        d[1] = decode_quad(buf[s].y, lut, laneoff);
-        d[2] = decode_quad(buf[s].z, lut, laneoff);
-        d[3] = decode_quad(buf[s].w, lut, laneoff);
+        d[0] = decode_quad(b.q[s].x, lut, laneoff);
+        d[1] = decode_quad(b.q[s].y, lut, laneoff);
+        d[2] = decode_quad(b.q[s].z, lut, laneoff);
+        d[3] = decode_quad(b.q[s].w, lut, laneoff);
         if constexpr (PLUG) {
           const uint32_t nib = (uint32_t)(pm >> (16 * s + 4 * c)) & 0xFu;
           if (nib) {
@@ -200,9 +177,9 @@ struct QuadWarp {
         }
 #pragma unroll
         for (int nb = 0; nb < NB; ++nb) {
-          const uint2 b = xquad(nb * 8 + g, kp);
-          mma_16816(acc[0][nb][0], a01[0], a01[1], a01[2], a01[3], b.x, b.y);
-          mma_16816(acc[0][nb][1], a23[0], a23[1], a23[2], a23[3], b.x, b.y);
+          const uint2 xb = xquad(nb * 8 + g, kp);
+          mma_16816(acc[0][nb][0], a01[0], a01[1], a01[2], a01[3], xb.x, xb.y);
+          mma_16816(acc[0][nb][1], a23[0], a23[1], a23[2], a23[3], xb.x, xb.y);
         }
       }
     } else {
@@ -222,7 +199,7 @@ struct QuadWarp {
         QuadDec d[4];
 #pragma unroll
         for (int r = 0; r < 4; ++r) {
-          const uint32_t code = t == 0 ? buf[r].x : t == 1 ? buf[r].y : t == 2 ? buf[r].z : buf[r].w;
+          const uint32_t code = t == 0 ? b.q[r].x : t == 1 ? b.q[r].y : t == 2 ? b.q[r].z : b.q[r].w;
           d[r] = decode_quad(code, lut, laneoff);
           if (!rv[r]) d[r] = QuadDec{0u, 0u, 0u};
         }
@@ -239,32 +216,11 @@ struct QuadWarp {
     }
   }
 
-  // ---- results ------------------------------------------------------------
   // Fragment register j of mma half h: model 2h + (j>>1), batch 8nb+2c+(j&1);
   // feature-in-tile g (NK) or 4g + t (KN).
-  __device__ __forceinline__ void store_direct(int64_t tile) const {
+  __device__ __forceinline__ void write_partial(float* red) const {
 #pragma unroll
-    for (int t = 0; t < G::kT; ++t) {
-      const int64_t f = tile * G::kTileW + (NK ? g : 4 * g + t);
-      if (f >= p.N) continue;
-#pragma unroll
-      for (int nb = 0; nb < NB; ++nb)
-#pragma unroll
-        for (int h = 0; h < 2; ++h)
-#pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            const int model = 2 * h + (j >> 1);
-            const int bat = nb * 8 + 2 * c + (j & 1);
-            if (bat < p.M)
-              p.out[model][(int64_t)bat * p.ldo_m + f * p.ldo_n] =
-                  __float2half_rn(acc[t][nb][h][j] * p.scale[model]);
-          }
-    }
-  }
-
-  __device__ __forceinline__ void store_partial(float* slot) const {
-#pragma unroll
-    for (int t = 0; t < G::kT; ++t) {
+    for (int t = 0; t < kT; ++t) {
       const int fi = NK ? g : 4 * g + t;
 #pragma unroll
       for (int nb = 0; nb < NB; ++nb)
@@ -274,95 +230,30 @@ struct QuadWarp {
           for (int j = 0; j < 4; ++j) {
             const int model = 2 * h + (j >> 1);
             const int bat = nb * 8 + 2 * c + (j & 1);
-            __stcg(slot + (model * kNBat + bat) * G::kTileW + fi, acc[t][nb][h][j]);
+            red[(model * kNBat + bat) * kTileW + fi] = acc[t][nb][h][j];
           }
     }
   }
 
-  __device__ __forceinline__ void finalize(int64_t tile, int64_t w_first, int64_t w_last) const {
-    const int64_t U = p.units, GW = p.active_warps;
-    const int64_t tile_u0 = tile * p.upt;
-    for (int e = lane; e < kSlot; e += 32) {
-      const int model = e / (kNBat * G::kTileW);
-      const int bat = (e / G::kTileW) % kNBat;
-      const int64_t f = tile * G::kTileW + e % G::kTileW;
-      float sum = 0.f;
-      for (int64_t w = w_first; w <= w_last; ++w) {
-        const int which = (U * w / GW >= tile_u0) ? 0 : 1;
-        sum += __ldcg(p.slots + (w * 2 + which) * kSlot + e);
-      }
-      if (bat < p.M && f < p.N)
-        p.out[model][(int64_t)bat * p.ldo_m + f * p.ldo_n] = __float2half_rn(sum * p.scale[model]);
-    }
+  __device__ __forceinline__ void store(int model, int bat, int64_t f, float v) const {
+    p.out[model][(int64_t)bat * p.ldo_m + f * p.ldo_n] = __float2half_rn(v * p.scale[model]);
   }
 };
 
 template <bool NK, int NB, bool PLUG>
+constexpr int quad_red_bytes() {
+  return QuadOp<NK, NB, PLUG>::kWarps * QuadOp<NK, NB, PLUG>::kSlot * 4;
+}
+
+template <bool NK, int NB, bool PLUG>
 __global__ void __launch_bounds__(quad_warps(NK, NB) * 32, 1) quad_gemv_kernel(const QuadParams p) {
-  constexpr int kWarps = quad_warps(NK, NB);
   extern __shared__ __align__(1024) uint8_t smem[];
-  build_quad_lut(smem, p.luts);
+  __shared__ int s_flag;
+  float* red = reinterpret_cast<float*>(smem + kQuadLutBytes);
+  build_quad_lut(smem, reinterpret_cast<uint32_t*>(red), p.luts);
   __syncthreads();
-
-  const int lane = threadIdx.x & 31;
-  const int64_t gw = (int64_t)blockIdx.x * kWarps + (threadIdx.x >> 5);
-  if (gw >= p.active_warps) return;
-  const int64_t U = p.units, GW = p.active_warps;
-  const int64_t u_begin = U * gw / GW, u_end = U * (gw + 1) / GW;
-  const int upt = p.upt;
-
-  QuadWarp<NK, NB, PLUG> wk(p, smem, lane);
-  int64_t pending[2];
-  int npend = 0;
-  const int64_t first_tile = u_begin / upt;
-
-  auto finish_unit = [&](int64_t u) {
-    const int64_t tile = u / upt;
-    const int64_t tile_u0 = tile * upt;
-    if (u - tile_u0 == upt - 1 || u == u_end - 1) {
-      const bool whole = (u_begin <= tile_u0) && (u - tile_u0 == upt - 1);
-      if (whole) {
-        wk.store_direct(tile);
-      } else {
-        const int which = tile == first_tile ? 0 : 1;
-        wk.store_partial(p.slots + (gw * 2 + which) * QuadWarp<NK, NB, PLUG>::kSlot);
-        if (npend < 2) pending[npend++] = tile;
-      }
-      wk.zero();
-    }
-  };
-
-  uint4 bufA[4], bufB[4];
-  wk.load(bufA, u_begin);
-  int64_t u = u_begin;
-  while (true) {
-    if (u + 1 < u_end) wk.load(bufB, u + 1);
-    wk.compute(bufA, u);
-    finish_unit(u);
-    if (++u >= u_end) break;
-    if (u + 1 < u_end) wk.load(bufA, u + 1);
-    wk.compute(bufB, u);
-    finish_unit(u);
-    if (++u >= u_end) break;
-  }
-
-  if (npend == 0) return;
-  __threadfence();
-  __syncwarp();
-  for (int i = 0; i < npend; ++i) {
-    const int64_t tile = pending[i];
-    const int64_t w_first = warp_of_unit(tile * upt, U, GW);
-    const int64_t w_last = warp_of_unit(tile * upt + upt - 1, U, GW);
-    int old = 0;
-    if (lane == 0) old = atomicAdd(p.counters + tile, 1);
-    old = __shfl_sync(0xffffffffu, old, 0);
-    if (old == (int)(w_last - w_first)) {
-      __threadfence();
-      wk.finalize(tile, w_first, w_last);
-      __syncwarp();
-      if (lane == 0) p.counters[tile] = 0;
-    }
-  }
+  QuadOp<NK, NB, PLUG> op(p, smem);
+  run_partition(op, p.part, red, &s_flag);
 }
 
 // Generic fallback for layouts the vector paths do not take (unaligned or
@@ -416,33 +307,10 @@ __global__ void quad_generic_kernel(const QuadGenericParams p) {
 // ------------------------------------------------------------------ host --
 namespace {
 
-struct QuadPlan {
-  bool nk = false, generic = false;
-  int nb = 1;
-  int64_t tiles = 0, upt = 0, units = 0;
-  int grid = 0, active_warps = 0;
-  size_t counters_bytes = 0, slots_bytes = 0;
-  size_t total() const { return counters_bytes + slots_bytes; }
-};
-
-QuadPlan make_plan(bool nk, int64_t Mc, int64_t N, int64_t K, int sms) {
-  QuadPlan pl;
-  pl.nk = nk;
-  pl.nb = Mc > 8 ? 2 : 1;
+PartitionPlan quad_plan(bool nk, int64_t Mc, int64_t N, int64_t K, int sms) {
+  const int nb = Mc > 8 ? 2 : 1;
   const int tile_w = nk ? 8 : 32, unit_k = nk ? 64 : 16;
-  pl.tiles = cdiv(N, tile_w);
-  pl.upt = cdiv(K, unit_k);
-  pl.units = pl.tiles * pl.upt;
-  if (pl.units == 0) return pl;
-  const int warps = quad_warps(nk, pl.nb);
-  const int64_t want = cdiv(pl.units, warps);
-  pl.grid = (int)(want < sms ? want : sms);
-  const int64_t gw = (int64_t)pl.grid * warps;
-  pl.active_warps = (int)(gw < pl.units ? gw : pl.units);
-  const int slot = 4 * 8 * pl.nb * tile_w;
-  pl.counters_bytes = align_up((size_t)pl.tiles * sizeof(int), 256);
-  pl.slots_bytes = (size_t)pl.active_warps * 2 * slot * sizeof(float);
-  return pl;
+  return plan_partition(cdiv(N, tile_w), cdiv(K, unit_k), quad_warps(nk, nb), sms, 4, Mc, tile_w);
 }
 
 bool g_attr_done[6][64];
@@ -450,26 +318,26 @@ bool g_attr_done[6][64];
 template <bool NK, int NB, bool PLUG>
 int launch_quad(const QuadParams& prm, int grid, int idx, cudaStream_t s) {
   auto kern = quad_gemv_kernel<NK, NB, PLUG>;
-  int rc = ensure_smem_attr(kern, (int)kQuadLutBytes, g_attr_done[idx]);
+  constexpr int smem = (int)kQuadLutBytes + quad_red_bytes<NK, NB, PLUG>();
+  static_assert(smem <= 227 * 1024, "shared memory budget");
+  int rc = ensure_smem_attr(kern, smem, g_attr_done[idx]);
   if (rc) return rc;
-  kern<<<grid, quad_warps(NK, NB) * 32, kQuadLutBytes, s>>>(prm);
+  kern<<<grid, quad_warps(NK, NB) * 32, smem, s>>>(prm);
   return check_launch("quad_gemv_kernel");
 }
 
-int launch_plan(const QuadPlan& pl, QuadParams prm, void* ws, bool plug, cudaStream_t s) {
-  prm.units = pl.units;
-  prm.upt = (int)pl.upt;
-  prm.active_warps = pl.active_warps;
-  prm.counters = reinterpret_cast<int*>(ws);
-  prm.slots = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(ws) + pl.counters_bytes);
-  if (pl.nk) {
-    if (plug) return pl.nb == 1 ? launch_quad<true, 1, true>(prm, pl.grid, 0, s)
-                                : launch_quad<true, 2, true>(prm, pl.grid, 1, s);
-    return pl.nb == 1 ? launch_quad<true, 1, false>(prm, pl.grid, 2, s)
-                      : launch_quad<true, 2, false>(prm, pl.grid, 3, s);
+int launch_plan(const PartitionPlan& pl, bool nk, int nb, QuadParams prm, void* ws, bool plug,
+                cudaStream_t s) {
+  prm.part.units = pl.units;
+  prm.part.upt = (int)pl.upt;
+  prm.part.counters = reinterpret_cast<int*>(ws);
+  prm.part.slots = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(ws) + pl.counters_bytes);
+  if (nk) {
+    if (plug) return nb == 1 ? launch_quad<true, 1, true>(prm, pl.grid, 0, s)
+                             : launch_quad<true, 2, true>(prm, pl.grid, 1, s);
+    return nb == 1 ? launch_quad<true, 1, false>(prm, pl.grid, 2, s) : launch_quad<true, 2, false>(prm, pl.grid, 3, s);
   }
-  return pl.nb == 1 ? launch_quad<false, 1, false>(prm, pl.grid, 4, s)
-                    : launch_quad<false, 2, false>(prm, pl.grid, 5, s);
+  return nb == 1 ? launch_quad<false, 1, false>(prm, pl.grid, 4, s) : launch_quad<false, 2, false>(prm, pl.grid, 5, s);
 }
 
 bool quad_vector_ok(bool nk, const uint32_t* codes, int64_t ldc_k, int64_t ldc_n, int64_t N, int64_t K) {
@@ -509,7 +377,7 @@ size_t quad_ws_bytes(bool nk, int64_t M, int64_t N, int64_t K) {
   const int sms = device_sm_count(current_device());
   const int64_t Mc = M < 16 ? M : 16;
   if (Mc <= 0) return 0;
-  return make_plan(nk, Mc, N, K, sms > 0 ? sms : 148).total();
+  return quad_plan(nk, Mc, N, K, sms > 0 ? sms : 148).total();
 }
 
 }  // namespace
@@ -591,7 +459,7 @@ static int quad_run(const void* a, int64_t lda_m, int64_t lda_k, const uint32_t*
   prm.pmask = reinterpret_cast<const unsigned long long*>(pmask);
   prm.pbase = pbase;
   prm.W = (int)cdiv(K, 64);
-  const size_t need = make_plan(nk, M < 16 ? M : 16, N, K, sms).total();
+  const size_t need = quad_plan(nk, M < 16 ? M : 16, N, K, sms).total();
   if (ws_bytes < need || (need && !ws) || !aligned(ws, 256)) {
     set_error("workspace of %zu bytes (256-byte aligned, zero-filled) required, got %zu", need, ws_bytes);
     return PP_ERR_WORKSPACE;
@@ -599,13 +467,13 @@ static int quad_run(const void* a, int64_t lda_m, int64_t lda_k, const uint32_t*
   // batch rows in chunks of 16: each chunk is one launch over the codes
   for (int64_t m0 = 0; m0 < M; m0 += 16) {
     const int64_t Mc = (M - m0) < 16 ? (M - m0) : 16;
-    QuadPlan pl = make_plan(nk, Mc, N, K, sms);
+    const PartitionPlan pl = quad_plan(nk, Mc, N, K, sms);
     prm.x = reinterpret_cast<const __half*>(a) + m0 * lda_m;
     for (int i = 0; i < 4; ++i) prm.out[i] = reinterpret_cast<__half*>(out[i]) + m0 * ldo_m;
     prm.M = (int)Mc;
     const int xalign = nk ? 8 : 4;
     prm.xvec = (lda_k == 1 && aligned(prm.x, xalign) && (lda_m * 2) % xalign == 0) ? 1 : 0;
-    if ((rc = launch_plan(pl, prm, ws, plug, s))) return rc;
+    if ((rc = launch_plan(pl, nk, Mc > 8 ? 2 : 1, prm, ws, plug, s))) return rc;
   }
   return PP_OK;
 }

@@ -1,0 +1,79 @@
+"""Row-sharded (column-parallel) packed Linears across the GPUs of one node.
+
+Output features of a Linear are independent, and in the file layout each
+Linear is ``(out, in)`` row-major, so the rows ``[n0, n1)`` owned by one rank
+are one contiguous slice of the code stream (and of the sorted plug table).
+Each rank streams only its slice; the four models' FP16 outputs are then
+all-gathered (NCCL over NVLink on GPUs, gloo in the CPU tests).  There is no
+cross-rank reduction.
+
+The reference runs one model per process on one GPU; this module is new
+(north_star item 3).
+"""
+from __future__ import annotations
+
+from typing import Callable, Sequence
+
+import torch
+import torch.distributed as dist
+
+
+def row_shard(N: int, world: int, rank: int) -> tuple[int, int]:
+    """Rows ``[n0, n1)`` of rank ``rank``: contiguous, sizes differ by at most one."""
+    if world <= 0 or not 0 <= rank < world:
+        raise ValueError(f"bad rank {rank} of {world}")
+    return N * rank // world, N * (rank + 1) // world
+
+
+def shard_width(N: int, world: int) -> int:
+    """Padded per-rank width used for the all-gather (equal sizes on every rank)."""
+    return -(-N // world)
+
+
+class RowShardedLinear:
+    """Runs ``local_fn`` on this rank's rows and all-gathers the outputs.
+
+    ``local_fn(x) -> list of n_out tensors (M, n1 - n0)`` computes the local
+    row shard (on a GPU: one fused kernel launch).  ``__call__`` returns
+    ``n_out`` full ``(M, N)`` tensors.  Every rank must call it with the same
+    ``M`` in the same order (one collective per call).
+    """
+
+    def __init__(self, local_fn: Callable[[torch.Tensor], Sequence[torch.Tensor]], N: int,
+                 group=None, n_out: int = 4):
+        self.local_fn = local_fn
+        self.N = N
+        self.group = group
+        self.world = dist.get_world_size(group) if dist.is_initialized() else 1
+        self.rank = dist.get_rank(group) if dist.is_initialized() else 0
+        self.n0, self.n1 = row_shard(N, self.world, self.rank)
+        self.width = shard_width(N, self.world)
+        self.n_out = n_out
+
+    def __call__(self, x: torch.Tensor) -> list[torch.Tensor]:
+        M = x.shape[0]
+        local = self.local_fn(x)
+        if self.world == 1:
+            return list(local)
+        n_loc = self.n1 - self.n0
+        send = torch.zeros((self.n_out, M, self.width), dtype=local[0].dtype, device=local[0].device)
+        for k in range(self.n_out):
+            send[k, :, :n_loc] = local[k]
+        # concatenated along dim 0 (the form both NCCL and gloo accept)
+        recv = torch.empty((self.world * self.n_out, M, self.width), dtype=send.dtype, device=send.device)
+        dist.all_gather_into_tensor(recv, send, group=self.group)
+        recv = recv.view(self.world, self.n_out, M, self.width)
+        outs = []
+        for k in range(self.n_out):
+            parts = []
+            for r in range(self.world):
+                a, b = row_shard(self.N, self.world, r)
+                parts.append(recv[r, k, :, :b - a])
+            outs.append(torch.cat(parts, dim=1))
+        return outs
+
+
+def shard_quad_linear(pack, offset: int, N: int, K: int, world: int, rank: int):
+    """This rank's row slice of the packed Linear at flat ``offset`` (file layout)."""
+    n0, n1 = row_shard(N, world, rank)
+    return pack.linear(offset + n0 * K, n1 - n0, K)
