@@ -202,7 +202,8 @@ def run_ours(args):
             outs = [obuf[k] for k in range(4)]
             pk = l.pack
             args_c = (x.data_ptr(), x.stride(0), x.stride(1), l.codes.data_ptr(), l.K,
-                      _lib.ptr(l.plug_vals), _lib.ptr(l.plug_mask), _lib.ptr(l.plug_base),
+                      _lib.ptr(l.plug_idx), _lib.ptr(l.plug_vals), _lib.ptr(l.plug_window_base),
+                      ctypes.c_uint32(l.offset & 0xFFFFFFFF),
                       _lib.ptrs(pk.luts, 7), _lib.floats4(pk.scales), _lib.ptrs(outs, 4),
                       outs[0].stride(0), outs[0].stride(1), M, l.N, l.K, ws.data_ptr(), ws.numel(), sh)
             gbuf = None
@@ -299,7 +300,7 @@ def run_ours(args):
                    "per_shape": per_shape},
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(achieved / peak, 4), "peak_source": f"{peak_kind} hbm_gbs",
-                     "kernel": "quad_gemv_kernel<NK,NB=1,PLUG>",
+                     "kernel": "quad_gemv_kernel<NK=1,NB=1,MB=1> (file layout, plug correction, batch 1)",
                      "traffic": traffic},
         "e2e": e2e,
         "gpu_launches": launches_per_step * K_steps,

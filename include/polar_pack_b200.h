@@ -78,44 +78,52 @@ PP_API int pp_quad_gemm(const void* a, int64_t lda_m, int64_t lda_k,
                  int64_t M, int64_t N, int64_t K,
                  void* workspace, size_t workspace_bytes, void* stream);
 
-/* File-layout fused Linear with plug-table patching, the per-Linear decode of
- * a `.quadpack` stream (reference quaternion_packer.py:141-214: codes of one
+/* File-layout fused Linear with plug-table merge, the per-Linear decode of a
+ * `.quadpack` stream (reference quaternion_packer.py:141-214: the codes of one
  * nn.Linear are (out=N, in=K) row-major at a flat stream offset; plug entries
  * replace the decoded normalised 4-tuple, quaternion_packer.py:187-193):
  *
  *   y_k[m][n] = fp16( scales[k] * sum_i x[m][i] * Wp_k[n][i] )
  *   Wp_k[n][i] = plug value if (n*K + i) is plugged, else the FP16 decode.
  *
- * x: (M, K) FP16 with strides (ldx_m, ldx_k).  codes: row n at codes + n*ldw.
- * plug_vals: (P, 4) FP16 plug values of this Linear, in stream order.
- * plug_mask / plug_base: per (row, 64-wide column window) bitmask of
- *   plugged columns and index of the window's first plug in plug_vals, as
- *   built by pp_quad_plug_index().  All three may be NULL when P == 0.
+ * x: (M, K) FP16 with strides (ldx_m, ldx_k).  codes: row n at codes + n*ldw,
+ *   prepared once by pp_quad_prepare_plugs() when the Linear has plugs.
+ * plug_idx / plug_vals: this Linear's slice [p_lo, p_hi) of the stream's plug
+ *   table (uint32 positions, (P, 4) FP16 values), base_lo32 the low 32 bits
+ *   of the Linear's stream offset.  plug_window_base: as built by
+ *   pp_quad_prepare_plugs().  All three pointers may be NULL when P == 0.
  * out[4]: (M, N) FP16 with strides (ldo_m, ldo_n).
+ * The plug values enter as an FP32 sparse correction added to the same
+ * accumulators, so the result equals the substituted-weight product within
+ * the FP32 accumulation tolerance.
  */
 PP_API int pp_quad_linear_workspace_bytes(int64_t M, int64_t N, int64_t K, size_t* bytes);
 
 PP_API int pp_quad_linear(const void* x, int64_t ldx_m, int64_t ldx_k,
-                   const uint32_t* codes, int64_t ldw,
-                   const void* plug_vals, const uint64_t* plug_mask, const uint32_t* plug_base,
-                   const void* const luts[7], const float scales[4],
-                   void* const out[4], int64_t ldo_m, int64_t ldo_n,
-                   int64_t M, int64_t N, int64_t K,
-                   void* workspace, size_t workspace_bytes, void* stream);
+                          const uint32_t* codes, int64_t ldw,
+                          const uint32_t* plug_idx, const void* plug_vals,
+                          const uint32_t* plug_window_base, uint32_t base_lo32,
+                          const void* const luts[7], const float scales[4],
+                          void* const out[4], int64_t ldo_m, int64_t ldo_n,
+                          int64_t M, int64_t N, int64_t K,
+                          void* workspace, size_t workspace_bytes, void* stream);
 
-/* Builds plug_mask (uint64, N * ceil(K/64)) and plug_base (uint32, same
- * count) for one Linear from the slice [p_lo, p_hi) of a `.quadpack` plug
- * index table (uint32 global positions, ascending; reference
- * quaternion_packer.py:97-116).  `base_lo32` is the low 32 bits of the
- * Linear's flat stream offset: position - base (mod 2^32) is the
- * position inside the Linear, so tables whose uint32 positions wrapped
- * past 2^32 still index correctly.  Entries outside the Linear are skipped
- * and counted into *bad_count (device int, may be NULL).  Both outputs are
- * overwritten completely.
+/* Load-time preparation of one Linear's plug entries for pp_quad_linear:
+ *  - plug_window_base[w] (uint32, N * ceil(K/64) + 1 entries) := number of
+ *    entries of the slice [p_lo, p_hi) whose position lies before window
+ *    w = (row, col/64), i.e. the index of its first plug; the last entry is P;
+ *  - the norm byte of every plugged code in `codes` (row stride ldw) is set
+ *    to zero, so the main kernel decodes it to exact zeros (the tables built
+ *    from a stream header have norm[0] == 0, quad_kernels.py:40).
+ * Positions are the stream's uint32 plug index (ascending; reference
+ * quaternion_packer.py:97-116) minus base_lo32 modulo 2^32, so tables whose
+ * positions wrapped past 2^32 still index correctly.  Entries outside the
+ * Linear or out of order are skipped and counted into *bad_count (device
+ * int, may be NULL).  Idempotent.
  */
-PP_API int pp_quad_plug_index(const uint32_t* plug_idx, int64_t p_lo, int64_t p_hi, uint32_t base_lo32,
-                       int64_t N, int64_t K, uint64_t* plug_mask, uint32_t* plug_base,
-                       int* bad_count, void* stream);
+PP_API int pp_quad_prepare_plugs(uint32_t* codes, int64_t ldw, const uint32_t* plug_idx,
+                                 int64_t p_lo, int64_t p_hi, uint32_t base_lo32, int64_t N, int64_t K,
+                                 uint32_t* plug_window_base, int* bad_count, void* stream);
 
 /* FP16 decode of a (R, C) code matrix into four (R, C) FP16 matrices,
  * bit-exact with the reference kernel's chain (quad_kernels.py:103-121).

@@ -36,11 +36,11 @@ _SIGNATURES = {
     "pp_quad_gemm": ([_c_void_p, _i64, _i64, _c_void_p, _i64, _i64, _PTR7, _F4, _PTR4, _i64, _i64,
                       _i64, _i64, _i64, _c_void_p, _size_t, _c_void_p], _int),
     "pp_quad_linear_workspace_bytes": ([_i64, _i64, _i64, ctypes.POINTER(_size_t)], _int),
-    "pp_quad_linear": ([_c_void_p, _i64, _i64, _c_void_p, _i64, _c_void_p, _c_void_p, _c_void_p,
+    "pp_quad_linear": ([_c_void_p, _i64, _i64, _c_void_p, _i64, _c_void_p, _c_void_p, _c_void_p, _u32,
                         _PTR7, _F4, _PTR4, _i64, _i64, _i64, _i64, _i64, _c_void_p, _size_t,
                         _c_void_p], _int),
-    "pp_quad_plug_index": ([_c_void_p, _i64, _i64, _u32, _i64, _i64, _c_void_p, _c_void_p,
-                            _c_void_p, _c_void_p], _int),
+    "pp_quad_prepare_plugs": ([_c_void_p, _i64, _c_void_p, _i64, _i64, _u32, _i64, _i64, _c_void_p,
+                               _c_void_p, _c_void_p], _int),
     "pp_quad_decode": ([_c_void_p, _i64, _i64, _i64, _i64, _PTR7, _c_void_p, _PTR4, _i64, _i64,
                         _c_void_p], _int),
     "pp_quad_unpack": ([_c_void_p, _i64, _c_void_p, _c_void_p, _i64, _i64, _u32, _PTR7, _c_void_p,

@@ -53,14 +53,36 @@ struct DualOp {
   const uint8_t* lut;
   int g, c;
   uint32_t laneoff;
+  int Mv, Nv, Kv;
+  int64_t ldc;
+  const __half* xrow[NB];  // this lane's activation row per batch tile (clamped)
+  bool xok[NB];
   float acc[8][NB][4];
 
   __device__ __forceinline__ DualOp(const DualParams& p_, const uint8_t* lut_)
       : p(p_), lut(lut_), g((threadIdx.x & 31) >> 2), c(threadIdx.x & 3),
-        laneoff((threadIdx.x & 31) * 4u) {}
+        laneoff((threadIdx.x & 31) * 4u), Mv(p_.M), Nv(p_.N), Kv(p_.K), ldc(p_.ldc) {
+#pragma unroll
+    for (int nb = 0; nb < NB; ++nb) {
+      const int bat = nb * 8 + g;
+      xok[nb] = bat < Mv;
+      xrow[nb] = p.x + (int64_t)(xok[nb] ? bat : 0) * p.ldx_m;
+    }
+  }
 
-  __device__ __forceinline__ int M() const { return p.M; }
-  __device__ __forceinline__ int64_t N() const { return p.N; }
+  __device__ __forceinline__ int M() const { return Mv; }
+  __device__ __forceinline__ int64_t N() const { return Nv; }
+
+  __device__ __forceinline__ void prefetch(int64_t tile, int kc) const {
+    // 16 rows x 128 bytes (64 int16 codes), one row per lane 0..15
+    const int lane = threadIdx.x & 31;
+    const int k = kc * 16 + (lane & 15);
+    const int64_t f0 = tile * 64;
+    if (lane < 16 && k < Kv && f0 < Nv) {
+      const int64_t n = Nv - f0 < 64 ? Nv - f0 : 64;
+      prefetch_l2(p.codes + (int64_t)k * ldc + f0, (uint32_t)n * 2u);
+    }
+  }
 
   __device__ __forceinline__ void zero() {
 #pragma unroll
@@ -76,9 +98,9 @@ struct DualOp {
 #pragma unroll
     for (int r = 0; r < 4; ++r) {
       const int k = kc * 16 + 2 * c + (r & 1) + 8 * (r >> 1);
-      if (f < p.N && k < p.K) {
-        b.q[r] = ldg_stream(p.codes + (int64_t)k * p.ldc + f);
-        b.sc[r] = __half2float(__ushort_as_half(ldg_u16(p.bmax + ((int64_t)k * p.N + f) / p.gs)));
+      if (f < Nv && k < Kv) {
+        b.q[r] = ldg_stream(p.codes + (int64_t)k * ldc + f);
+        b.sc[r] = __half2float(__ushort_as_half(ldg_u16(p.bmax + ((int64_t)k * Nv + f) / p.gs)));
       } else {
         b.q[r] = make_uint4(0, 0, 0, 0);
         b.sc[r] = 0.f;
@@ -86,14 +108,15 @@ struct DualOp {
     }
   }
 
-  __device__ __forceinline__ uint32_t xpair(int bat, int k) const {
-    if (bat >= p.M) return 0u;
-    const __half* row = p.x + (int64_t)bat * p.ldx_m;
-    if (p.xvec && k + 1 < p.K) return ldg_u32(row + k);
+  __device__ __forceinline__ uint32_t xpair(int nb, int k) const {
+    if (p.xvec && k + 1 < Kv) {
+      const uint32_t v = ldg_u32(xrow[nb] + k);
+      return xok[nb] ? v : 0u;
+    }
     uint32_t lo = 0, hi = 0;
-    if (k < p.K) lo = ldg_u16(row + (int64_t)k * p.ldx_k);
-    if (k + 1 < p.K) hi = ldg_u16(row + (int64_t)(k + 1) * p.ldx_k);
-    return lo | (hi << 16);
+    if (k < Kv) lo = ldg_u16(xrow[nb] + (int64_t)k * p.ldx_k);
+    if (k + 1 < Kv) hi = ldg_u16(xrow[nb] + (int64_t)(k + 1) * p.ldx_k);
+    return xok[nb] ? (lo | (hi << 16)) : 0u;
   }
 
   // (B1, B2) of the low and high code of word w, FP32, reference rounding
@@ -118,8 +141,8 @@ struct DualOp {
     uint32_t b0[NB], b1[NB];
 #pragma unroll
     for (int nb = 0; nb < NB; ++nb) {
-      b0[nb] = xpair(nb * 8 + g, kbase + 2 * c);
-      b1[nb] = xpair(nb * 8 + g, kbase + 2 * c + 8);
+      b0[nb] = xpair(nb, kbase + 2 * c);
+      b1[nb] = xpair(nb, kbase + 2 * c + 8);
     }
     // rows beyond K: scale 0 gives +-0 weights, activations are 0 there too
 #pragma unroll

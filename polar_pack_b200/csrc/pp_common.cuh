@@ -38,6 +38,11 @@ __device__ __forceinline__ uint16_t ldg_u16(const void* p) {
   return __ldg(reinterpret_cast<const unsigned short*>(p));
 }
 
+// Bulk prefetch of `bytes` (multiple of 16, 16-byte aligned) into L2.
+__device__ __forceinline__ void prefetch_l2(const void* p, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
+}
+
 // D += A(16x16, row) * B(16x8, col), FP16 inputs, FP32 accumulate.
 __device__ __forceinline__ void mma_16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2,
                                           uint32_t a3, uint32_t b0, uint32_t b1) {

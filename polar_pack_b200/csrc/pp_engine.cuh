@@ -15,18 +15,28 @@
 // result and resets the counter to zero.  No CTA ever waits for another.
 // Loads for a warp's next unit are issued before the current unit is
 // decoded, across tile boundaries too, so the barrier at the end of a tile
-// overlaps the next tile's loads.
+// overlaps the next tile's loads; a second cursor runs kPrefetch units
+// further ahead and pulls those units into L2 with bulk prefetches, which
+// keeps enough bytes in flight per SM without spending registers.
 #pragma once
 
 #include <stdint.h>
 
 namespace pp {
 
+// Workspace: a fixed 4 KiB counter block (one arrival counter per CTA,
+// zero between launches) followed by the partial-sum slots.  A tile shared
+// by CTAs c_first < ... < c_last uses counter c_last: c_last contains the
+// tile's last unit and starts inside it, so no CTA is c_last of two shared
+// tiles.  Counters therefore never overlap slot memory of any other plan.
+constexpr int kMaxGrid = 1024;
+constexpr size_t kCounterBytes = kMaxGrid * sizeof(int);
+
 struct Partition {
   int64_t units;  // total units
   int upt;        // units per tile
-  int* counters;  // [tiles] arrival counters (zero between launches)
-  float* slots;   // [grid][2][4 * M * tile_w] cross-CTA partials
+  int* counters;  // [kMaxGrid] arrival counters (zero between launches)
+  float* slots;   // [grid][2][nout * M * tile_w] cross-CTA partials
 };
 
 __device__ __forceinline__ int64_t cta_of_unit(int64_t x, int64_t U, int64_t G) {
@@ -40,6 +50,7 @@ __device__ __forceinline__ int64_t cta_of_unit(int64_t x, int64_t U, int64_t G) 
 //   using Buf = ...;
 //   void zero();                                   accumulators := 0
 //   void load(Buf&, int64_t tile, int kc) const;   issue loads of one unit
+//   void prefetch(int64_t tile, int kc) const;     L2 prefetch of one unit
 //   void compute(const Buf&, int64_t tile, int kc);
 //   void write_partial(float* red) const;          this warp's kSlot floats
 //   int  M() const; int64_t N() const;
@@ -84,9 +95,20 @@ __device__ __forceinline__ void run_partition(Op& op, const Partition& pt, float
 
   typename Op::Buf bufA, bufB;
   cur_ok = first_from(t_first, cur_t, cur_u);
+  // prefetch cursor: kPrefetch units of this warp ahead of the current one
+  constexpr int kPrefetch = 4;
+  int64_t pf_t = cur_t, pf_u = cur_u;
+  bool pf_ok = cur_ok;
   if (cur_ok) {
     op.load(bufA, cur_t, (int)(cur_u - cur_t * upt));
     nxt_ok = advance(cur_t, cur_u, nxt_t, nxt_u);
+    // units cur+2 .. cur+kPrefetch now; cur+1 is loaded into registers
+    pf_ok = nxt_ok && advance(nxt_t, nxt_u, pf_t, pf_u);
+#pragma unroll 1
+    for (int i = 2; i <= kPrefetch && pf_ok; ++i) {
+      op.prefetch(pf_t, (int)(pf_u - pf_t * upt));
+      pf_ok = advance(pf_t, pf_u, pf_t, pf_u);
+    }
   }
 
   int64_t pend[2];
@@ -98,6 +120,10 @@ __device__ __forceinline__ void run_partition(Op& op, const Partition& pt, float
   for (int64_t tt = t_first; tt <= t_last; ++tt) {
     op.zero();
     while (cur_ok && cur_t == tt) {
+      if (pf_ok) {
+        op.prefetch(pf_t, (int)(pf_u - pf_t * upt));
+        pf_ok = advance(pf_t, pf_u, pf_t, pf_u);
+      }
       if (nxt_ok) op.load(bufB, nxt_t, (int)(nxt_u - nxt_t * upt));
       op.compute(bufA, cur_t, (int)(cur_u - cur_t * upt));
       bufA = bufB;
@@ -139,7 +165,7 @@ __device__ __forceinline__ void run_partition(Op& op, const Partition& pt, float
     __threadfence();
     __syncthreads();
     if (tid == 0) {
-      const int old = atomicAdd(pt.counters + tt, 1);
+      const int old = atomicAdd(pt.counters + c_last, 1);
       *s_flag = (old == (int)(c_last - c_first)) ? 1 : 0;
     }
     __syncthreads();
@@ -159,7 +185,7 @@ __device__ __forceinline__ void run_partition(Op& op, const Partition& pt, float
         const int64_t f = tt * TW + fi;
         if (f < op.N()) op.store(o, bat, f, s);
       }
-      if (tid == 0) pt.counters[tt] = 0;
+      if (tid == 0) pt.counters[c_last] = 0;
     }
     __syncthreads();
   }
@@ -182,8 +208,9 @@ inline PartitionPlan plan_partition(int64_t tiles, int64_t upt, int warps, int s
   if (pl.units == 0) return pl;
   // at least ~2 units per warp before another CTA is worth its table set-up
   const int64_t want = (pl.units + 2 * warps - 1) / (2 * warps);
-  pl.grid = (int)(want < sms ? (want > 0 ? want : 1) : sms);
-  pl.counters_bytes = ((size_t)tiles * sizeof(int) + 255) / 256 * 256;
+  const int cap = sms < kMaxGrid ? sms : kMaxGrid;
+  pl.grid = (int)(want < cap ? (want > 0 ? want : 1) : cap);
+  pl.counters_bytes = kCounterBytes;
   pl.slots_bytes = (size_t)pl.grid * 2 * (size_t)(nout * M * tile_w) * sizeof(float);
   return pl;
 }

@@ -5,9 +5,10 @@
 //  * quad_plug_scatter   -- overwrite plugged positions with the plug table's
 //    FP16 4-tuples (optionally scaled), the in-memory merge of
 //    quaternion_packer.py:187-193.
-//  * quad_plug_index     -- per (row, 64-column window) bitmask of plugged
-//    columns and the index of the window's first plug, the form the fused
-//    Linear kernel reads.
+//  * quad_plug_windows / quad_plug_zero -- load-time preparation of a
+//    Linear's plug table for the fused kernel: index of the first plug of
+//    every (row, 64-column window), and the norm byte of plugged codes set to
+//    zero so that they decode to exact zeros in the main loop.
 #include "pp_common.cuh"
 #include "pp_host.h"
 
@@ -78,39 +79,61 @@ __global__ void fill_zero_u32(uint32_t* p, int64_t n) {
     p[i] = 0u;
 }
 
-struct PlugIndexParams {
+struct PlugPrepParams {
+  uint32_t* codes;  // the Linear's (N, K) codes, row stride ldw
+  int64_t ldw;
   const uint32_t* plug_idx;
   int64_t p_lo, p_hi;
   uint32_t base;
   int64_t N, K, W;
-  unsigned long long* mask;
-  uint32_t* first;
+  uint32_t* wbase;  // [N*W + 1]
   int* bad;
 };
 
-__global__ void quad_plug_index_kernel(const PlugIndexParams p) {
+// wbase[w] = number of plug entries of this Linear whose position is below
+// the start of window w = (row, win): row*K + 64*win; wbase[N*W] = P.
+// Lower bound by binary search over the (ascending) slice.
+__global__ void quad_plug_windows_kernel(const PlugPrepParams p) {
+  const int64_t nw = p.N * p.W;
+  const int64_t P = p.p_hi - p.p_lo;
+  for (int64_t w = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; w <= nw;
+       w += (int64_t)gridDim.x * blockDim.x) {
+    uint64_t target;
+    if (w == nw) {
+      target = (uint64_t)p.N * (uint64_t)p.K;
+    } else {
+      const int64_t row = w / p.W, win = w - row * p.W;
+      target = (uint64_t)row * (uint64_t)p.K + (uint64_t)win * 64u;
+    }
+    int64_t lo = 0, hi = P;
+    while (lo < hi) {
+      const int64_t mid = (lo + hi) >> 1;
+      const uint64_t loc = (uint32_t)(__ldg(p.plug_idx + p.p_lo + mid) - p.base);
+      if (loc < target) lo = mid + 1;
+      else hi = mid;
+    }
+    p.wbase[w] = (uint32_t)lo;
+  }
+}
+
+// Zero the norm byte of every plugged code (it then decodes to exact zeros)
+// and count entries that are out of range or out of order.
+__global__ void quad_plug_zero_kernel(const PlugPrepParams p) {
   const uint64_t span = (uint64_t)p.N * (uint64_t)p.K;
   for (int64_t j = p.p_lo + blockIdx.x * (int64_t)blockDim.x + threadIdx.x; j < p.p_hi;
        j += (int64_t)gridDim.x * blockDim.x) {
     const uint32_t loc = __ldg(p.plug_idx + j) - p.base;
     bool ok = (uint64_t)loc < span;
-    bool head = true;
     if (ok && j > p.p_lo) {
       const uint32_t prev = __ldg(p.plug_idx + j - 1) - p.base;
-      if ((uint64_t)prev < span) {
-        if (prev >= loc) ok = false;  // positions must strictly increase
-        head = (prev / (uint64_t)p.K != loc / (uint64_t)p.K) ||
-               ((prev % (uint64_t)p.K) >> 6) != ((loc % (uint64_t)p.K) >> 6);
-      }
+      if ((uint64_t)prev < span && prev >= loc) ok = false;
     }
     if (!ok) {
       if (p.bad) atomicAdd(p.bad, 1);
       continue;
     }
-    const uint64_t n = loc / (uint64_t)p.K, k = loc % (uint64_t)p.K;
-    const int64_t w = (int64_t)n * p.W + (int64_t)(k >> 6);
-    atomicOr(p.mask + w, 1ull << (k & 63));
-    if (head) p.first[w] = (uint32_t)(j - p.p_lo);
+    const uint64_t row = loc / (uint64_t)p.K, k = loc % (uint64_t)p.K;
+    p.codes[row * p.ldw + k] &= 0x00FFFFFFu;
   }
 }
 
@@ -211,31 +234,25 @@ int pp_quad_unpack(const uint32_t* codes, int64_t n, const uint32_t* plug_idx, c
   return pp::check_launch("quad_plug_scatter");
 }
 
-int pp_quad_plug_index(const uint32_t* plug_idx, int64_t p_lo, int64_t p_hi, uint32_t base_lo32, int64_t N,
-                       int64_t K, uint64_t* plug_mask, uint32_t* plug_base, int* bad_count, void* stream) {
+int pp_quad_prepare_plugs(uint32_t* codes, int64_t ldw, const uint32_t* plug_idx, int64_t p_lo, int64_t p_hi,
+                          uint32_t base_lo32, int64_t N, int64_t K, uint32_t* plug_window_base, int* bad_count,
+                          void* stream) {
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-  if (N < 0 || K <= 0 || p_lo < 0 || p_hi < p_lo || !plug_mask || !plug_base) {
-    pp::set_error("invalid arguments to quad plug index");
+  if (N < 0 || K <= 0 || p_lo < 0 || p_hi < p_lo || ldw < K || !plug_window_base || (N > 0 && !codes)) {
+    pp::set_error("invalid arguments to quad prepare plugs");
     return PP_ERR_INVALID;
   }
-  const int64_t W = pp::cdiv(K, 64);
-  const int64_t words = N * W;
-  if (words == 0) return PP_OK;
-  pp::fill_zero_u32<<<pp::grid_for(2 * words, 256), 256, 0, s>>>(reinterpret_cast<uint32_t*>(plug_mask),
-                                                                  2 * words);
-  int rc = pp::check_launch("fill_zero_u32");
-  if (rc) return rc;
-  pp::fill_zero_u32<<<pp::grid_for(words, 256), 256, 0, s>>>(plug_base, words);
-  if ((rc = pp::check_launch("fill_zero_u32"))) return rc;
-  if (p_hi == p_lo) return PP_OK;
-  if (!plug_idx) {
+  if (p_hi > p_lo && !plug_idx) {
     pp::set_error("plug_idx is NULL");
     return PP_ERR_INVALID;
   }
-  pp::PlugIndexParams prm{plug_idx, p_lo, p_hi, base_lo32, N, K, W,
-                          reinterpret_cast<unsigned long long*>(plug_mask), plug_base, bad_count};
-  pp::quad_plug_index_kernel<<<pp::grid_for(p_hi - p_lo, 256), 256, 0, s>>>(prm);
-  return pp::check_launch("quad_plug_index_kernel");
+  const int64_t W = pp::cdiv(K, 64);
+  pp::PlugPrepParams prm{codes, ldw, plug_idx, p_lo, p_hi, base_lo32, N, K, W, plug_window_base, bad_count};
+  pp::quad_plug_windows_kernel<<<pp::grid_for(N * W + 1, 256), 256, 0, s>>>(prm);
+  int rc = pp::check_launch("quad_plug_windows_kernel");
+  if (rc || p_hi == p_lo) return rc;
+  pp::quad_plug_zero_kernel<<<pp::grid_for(p_hi - p_lo, 256), 256, 0, s>>>(prm);
+  return pp::check_launch("quad_plug_zero_kernel");
 }
 
 }  // extern "C"

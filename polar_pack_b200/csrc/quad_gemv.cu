@@ -25,9 +25,10 @@ namespace pp {
 
 int zero_f16(void* p, int64_t R, int64_t C, int64_t ldr, int64_t ldc, cudaStream_t s);
 
-// Warps per CTA: the KN tile keeps 4x more accumulators per lane, so it
-// trades warps for registers (NB = number of 8-row batch tiles).
-__host__ __device__ constexpr int quad_warps(bool nk, int nb) { return nk ? 16 : (nb == 1 ? 12 : 8); }
+// Warps per CTA: the KN tile keeps 4x more accumulators per lane and two
+// batch tiles double them again, so those variants trade warps for
+// registers (NB = number of 8-row batch tiles).
+__host__ __device__ constexpr int quad_warps(bool nk, int nb) { return nb == 2 ? 8 : (nk ? 16 : 12); }
 
 struct QuadParams {
   const __half* x;
@@ -39,10 +40,12 @@ struct QuadParams {
   __half* out[4];
   int64_t ldo_m, ldo_n;
   int M, N, K;
-  // plug tables (NK only)
-  const uint2* plug_vals;
-  const unsigned long long* pmask;
-  const uint32_t* pbase;
+  // plug correction (NK only).  Plugged positions carry a zero norm byte,
+  // so they decode to exact zeros; their FP16 4-tuples are added here.
+  const uint32_t* plug_idx;  // this Linear's slice of the stream positions
+  const uint2* plug_vals;    // same slice, 4 FP16 per entry
+  const uint32_t* wbase;     // [N*W + 1] first plug of each (row, 64-column window)
+  uint32_t base_lo32;        // low 32 bits of the Linear's stream offset
   int W;
   Partition part;
   int xvec;
@@ -52,7 +55,9 @@ struct QuadBuf {
   uint4 q[4];
 };
 
-template <bool NK, int NB, bool PLUG>
+// NK: file layout.  MB > 0 selects the plug-correcting variant for up to MB
+// batch rows (MB in {1, 8, 16}); MB == 0 has no plug table.
+template <bool NK, int NB, int MB>
 struct QuadOp {
   static constexpr int kWarps = quad_warps(NK, NB);
   static constexpr int kTileW = NK ? 8 : 32;  // output features per tile
@@ -60,20 +65,34 @@ struct QuadOp {
   static constexpr int kNOut = 4;
   static constexpr int kNBat = 8 * NB;
   static constexpr int kSlot = kNOut * kNBat * kTileW;
+  static constexpr bool kPlug = MB > 0;
+  static constexpr int kMB = MB > 0 ? MB : 1;
   using Buf = QuadBuf;
 
   const QuadParams& p;
   const uint8_t* lut;
   int g, c;
   uint32_t laneoff;
+  int Mv, Nv, Kv, W;
+  int64_t ldc;
+  const __half* xrow[NB];  // this lane's activation row per batch tile (clamped)
+  bool xok[NB];
   float acc[kT][NB][2][4];
+  float corr[kMB][4];
 
   __device__ __forceinline__ QuadOp(const QuadParams& p_, const uint8_t* lut_)
       : p(p_), lut(lut_), g((threadIdx.x & 31) >> 2), c(threadIdx.x & 3),
-        laneoff((threadIdx.x & 31) * 4u) {}
+        laneoff((threadIdx.x & 31) * 4u), Mv(p_.M), Nv(p_.N), Kv(p_.K), W(p_.W), ldc(p_.ldc) {
+#pragma unroll
+    for (int nb = 0; nb < NB; ++nb) {
+      const int bat = nb * 8 + g;
+      xok[nb] = bat < Mv;
+      xrow[nb] = p.x + (int64_t)(xok[nb] ? bat : 0) * p.ldx_m;
+    }
+  }
 
-  __device__ __forceinline__ int M() const { return p.M; }
-  __device__ __forceinline__ int64_t N() const { return p.N; }
+  __device__ __forceinline__ int M() const { return Mv; }
+  __device__ __forceinline__ int64_t N() const { return Nv; }
 
   __device__ __forceinline__ void zero() {
 #pragma unroll
@@ -84,65 +103,114 @@ struct QuadOp {
         for (int h = 0; h < 2; ++h)
 #pragma unroll
           for (int j = 0; j < 4; ++j) acc[t][nb][h][j] = 0.f;
+#pragma unroll
+    for (int m = 0; m < kMB; ++m)
+#pragma unroll
+      for (int q = 0; q < 4; ++q) corr[m][q] = 0.f;
   }
 
   __device__ __forceinline__ void load(Buf& b, int64_t tile, int kc) const {
     if constexpr (NK) {
       const int64_t row = tile * 8 + g;
       const int kb = kc * 64 + 4 * c;
-      const uint32_t* base = p.codes + row * p.ldc + kb;
+      const uint32_t* base = p.codes + row * ldc + kb;
+      const bool rok = row < Nv;
 #pragma unroll
       for (int s = 0; s < 4; ++s) {
-        if (row < p.N && kb + 16 * s < p.K) b.q[s] = ldg_stream(base + 16 * s);
+        if (rok && kb + 16 * s < Kv) b.q[s] = ldg_stream(base + 16 * s);
         else b.q[s] = make_uint4(0, 0, 0, 0);
       }
     } else {
       const int64_t f = tile * 32 + 4 * g;
+      const bool fok = f < Nv;
 #pragma unroll
       for (int r = 0; r < 4; ++r) {
         const int k = kc * 16 + 2 * c + (r & 1) + 8 * (r >> 1);
-        if (f < p.N && k < p.K) b.q[r] = ldg_stream(p.codes + (int64_t)k * p.ldc + f);
+        if (fok && k < Kv) b.q[r] = ldg_stream(p.codes + (int64_t)k * ldc + f);
         else b.q[r] = make_uint4(0, 0, 0, 0);
       }
     }
   }
 
-  __device__ __forceinline__ uint32_t xpair(int bat, int k) const {
-    // activations (bat, k) and (bat, k+1) as one half2 word, zero outside
-    if (bat >= p.M) return 0u;
-    const __half* row = p.x + (int64_t)bat * p.ldx_m;
-    if (p.xvec && k + 1 < p.K) return ldg_u32(row + k);
-    uint32_t lo = 0, hi = 0;
-    if (k < p.K) lo = ldg_u16(row + (int64_t)k * p.ldx_k);
-    if (k + 1 < p.K) hi = ldg_u16(row + (int64_t)(k + 1) * p.ldx_k);
-    return lo | (hi << 16);
+  __device__ __forceinline__ void prefetch(int64_t tile, int kc) const {
+    if constexpr (NK) {
+      // 8 rows x 256 bytes: one bulk prefetch per row, issued by lane c == 0
+      const int64_t row = tile * 8 + g;
+      const int k0 = kc * 64;
+      if (c == 0 && row < Nv && k0 < Kv) {
+        const int n = Kv - k0 < 64 ? Kv - k0 : 64;
+        prefetch_l2(p.codes + row * ldc + k0, (uint32_t)n * 4u);
+      }
+    } else {
+      // 16 rows x 128 bytes, one row per lane 0..15
+      const int lane = threadIdx.x & 31;
+      const int k = kc * 16 + (lane & 15);
+      const int64_t f0 = tile * 32;
+      if (lane < 16 && k < Kv && f0 < Nv) {
+        const int64_t n = Nv - f0 < 32 ? Nv - f0 : 32;
+        prefetch_l2(p.codes + (int64_t)k * ldc + f0, (uint32_t)n * 4u);
+      }
+    }
   }
 
-  __device__ __forceinline__ uint2 xquad(int bat, int k) const {
+  __device__ __forceinline__ uint32_t xpair(int nb, int k) const {
+    // activations (bat, k) and (bat, k+1) as one half2 word, zero outside
+    if (p.xvec && k + 1 < Kv) {
+      const uint32_t v = ldg_u32(xrow[nb] + k);
+      return xok[nb] ? v : 0u;
+    }
+    uint32_t lo = 0, hi = 0;
+    if (k < Kv) lo = ldg_u16(xrow[nb] + (int64_t)k * p.ldx_k);
+    if (k + 1 < Kv) hi = ldg_u16(xrow[nb] + (int64_t)(k + 1) * p.ldx_k);
+    return xok[nb] ? (lo | (hi << 16)) : 0u;
+  }
+
+  __device__ __forceinline__ uint2 xquad(int nb, int k) const {
     // activations (bat, k..k+3); the NK path guarantees K % 4 == 0
-    if (bat >= p.M || k >= p.K) return make_uint2(0u, 0u);
-    const __half* row = p.x + (int64_t)bat * p.ldx_m;
-    if (p.xvec) return ldg_u2(row + k);
-    uint32_t h[4];
+    uint2 v;
+    if (p.xvec) {
+      v = ldg_u2(xrow[nb] + (k < Kv ? k : 0));
+    } else {
+      uint32_t h[4];
 #pragma unroll
-    for (int i = 0; i < 4; ++i) h[i] = ldg_u16(row + (int64_t)(k + i) * p.ldx_k);
-    return make_uint2(h[0] | (h[1] << 16), h[2] | (h[3] << 16));
+      for (int i = 0; i < 4; ++i) h[i] = k < Kv ? ldg_u16(xrow[nb] + (int64_t)(k + i) * p.ldx_k) : 0u;
+      v = make_uint2(h[0] | (h[1] << 16), h[2] | (h[3] << 16));
+    }
+    const bool ok = xok[nb] && k < Kv;
+    return make_uint2(ok ? v.x : 0u, ok ? v.y : 0u);
+  }
+
+  // Plug entries of (row, window kc): lanes of the row take every 4th entry.
+  __device__ __forceinline__ void plug_correct(int64_t row, int kc) {
+    if constexpr (kPlug) {
+      if (row >= Nv) return;
+      const int64_t wi = row * W + kc;
+      const uint32_t j0 = __ldg(p.wbase + wi), j1 = __ldg(p.wbase + wi + 1);
+      const uint32_t rowbase = p.base_lo32 + (uint32_t)row * (uint32_t)Kv;
+      for (uint32_t j = j0 + c; j < j1; j += 4) {
+        const uint32_t k = __ldg(p.plug_idx + j) - rowbase;
+        const uint2 v = __ldg(p.plug_vals + j);
+        const float pv[4] = {__half2float(__ushort_as_half((uint16_t)(v.x & 0xFFFF))),
+                             __half2float(__ushort_as_half((uint16_t)(v.x >> 16))),
+                             __half2float(__ushort_as_half((uint16_t)(v.y & 0xFFFF))),
+                             __half2float(__ushort_as_half((uint16_t)(v.y >> 16)))};
+#pragma unroll
+        for (int m = 0; m < kMB; ++m) {
+          if (m < Mv) {
+            const float xv = __half2float(__ushort_as_half(
+                ldg_u16(p.x + (int64_t)m * p.ldx_m + (int64_t)k * p.ldx_k)));
+#pragma unroll
+            for (int q = 0; q < 4; ++q) corr[m][q] = fmaf(pv[q], xv, corr[m][q]);
+          }
+        }
+      }
+    }
   }
 
   __device__ __forceinline__ void compute(const Buf& b, int64_t tile, int kc) {
     if constexpr (NK) {
       const int kbase = kc * 64;
-      const int64_t row = tile * 8 + g;
-      unsigned long long pm = 0ull;
-      uint32_t pb = 0u;
-      if constexpr (PLUG) {
-        if (row < p.N) {
-          const int64_t wi = row * p.W + kc;
-          pm = __ldg(p.pmask + wi);
-          if (pm) pb = __ldg(p.pbase + wi);
-        }
-      }
-      const bool full_k = kbase + 64 <= p.K;
+      const bool full_k = kbase + 64 <= Kv;
 #pragma unroll
       for (int s = 0; s < 4; ++s) {
         const int kp = kbase + 16 * s + 4 * c;
@@ -151,49 +219,34 @@ struct QuadOp {
         d[1] = decode_quad(b.q[s].y, lut, laneoff);
         d[2] = decode_quad(b.q[s].z, lut, laneoff);
         d[3] = decode_quad(b.q[s].w, lut, laneoff);
-        if constexpr (PLUG) {
-          const uint32_t nib = (uint32_t)(pm >> (16 * s + 4 * c)) & 0xFu;
-          if (nib) {
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-              if ((nib >> e) & 1u) {
-                const int bit = 16 * s + 4 * c + e;
-                const uint32_t j = pb + (uint32_t)__popcll(pm & ((1ull << bit) - 1ull));
-                const uint2 v = __ldg(p.plug_vals + j);
-                d[e].p1 = v.x;        // low half = model 0
-                d[e].p2 = v.x >> 16;  // low half = model 1
-                d[e].p3 = v.y;        // (model 2, model 3)
-              }
-            }
-          }
-        }
         uint32_t a01[4] = {lo_pair(d[0].p1, d[1].p1), lo_pair(d[0].p2, d[1].p2),
                            lo_pair(d[2].p1, d[3].p1), lo_pair(d[2].p2, d[3].p2)};
         uint32_t a23[4] = {lo_pair(d[0].p3, d[1].p3), hi_pair(d[0].p3, d[1].p3),
                            lo_pair(d[2].p3, d[3].p3), hi_pair(d[2].p3, d[3].p3)};
-        if (!full_k && kp >= p.K) {
+        if (!full_k && kp >= Kv) {
 #pragma unroll
           for (int i = 0; i < 4; ++i) a01[i] = a23[i] = 0u;
         }
 #pragma unroll
         for (int nb = 0; nb < NB; ++nb) {
-          const uint2 xb = xquad(nb * 8 + g, kp);
+          const uint2 xb = xquad(nb, kp);
           mma_16816(acc[0][nb][0], a01[0], a01[1], a01[2], a01[3], xb.x, xb.y);
           mma_16816(acc[0][nb][1], a23[0], a23[1], a23[2], a23[3], xb.x, xb.y);
         }
       }
+      plug_correct(tile * 8 + g, kc);
     } else {
       const int kbase = kc * 16;
-      const bool full_k = kbase + 16 <= p.K;
+      const bool full_k = kbase + 16 <= Kv;
       uint32_t b0[NB], b1[NB];
 #pragma unroll
       for (int nb = 0; nb < NB; ++nb) {
-        b0[nb] = xpair(nb * 8 + g, kbase + 2 * c);
-        b1[nb] = xpair(nb * 8 + g, kbase + 2 * c + 8);
+        b0[nb] = xpair(nb, kbase + 2 * c);
+        b1[nb] = xpair(nb, kbase + 2 * c + 8);
       }
       bool rv[4];
 #pragma unroll
-      for (int r = 0; r < 4; ++r) rv[r] = full_k || (kbase + 2 * c + (r & 1) + 8 * (r >> 1) < p.K);
+      for (int r = 0; r < 4; ++r) rv[r] = full_k || (kbase + 2 * c + (r & 1) + 8 * (r >> 1) < Kv);
 #pragma unroll
       for (int t = 0; t < 4; ++t) {
         QuadDec d[4];
@@ -218,7 +271,29 @@ struct QuadOp {
 
   // Fragment register j of mma half h: model 2h + (j>>1), batch 8nb+2c+(j&1);
   // feature-in-tile g (NK) or 4g + t (KN).
-  __device__ __forceinline__ void write_partial(float* red) const {
+  __device__ __forceinline__ void write_partial(float* red) {
+    if constexpr (kPlug) {
+      // the 4 lanes of a row hold disjoint plug subsets: sum them (the same
+      // order on every lane), then add to the fragment owning (model, batch)
+#pragma unroll
+      for (int m = 0; m < kMB; ++m)
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          corr[m][q] += __shfl_xor_sync(0xffffffffu, corr[m][q], 1);
+          corr[m][q] += __shfl_xor_sync(0xffffffffu, corr[m][q], 2);
+        }
+#pragma unroll
+      for (int nb = 0; nb < NB; ++nb)
+#pragma unroll
+        for (int h = 0; h < 2; ++h)
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const int bat = nb * 8 + 2 * c + (j & 1);
+#pragma unroll
+            for (int m = 0; m < kMB; ++m)
+              if (m == bat) acc[0][nb][h][j] += corr[m][2 * h + (j >> 1)];
+          }
+    }
 #pragma unroll
     for (int t = 0; t < kT; ++t) {
       const int fi = NK ? g : 4 * g + t;
@@ -240,19 +315,19 @@ struct QuadOp {
   }
 };
 
-template <bool NK, int NB, bool PLUG>
+template <bool NK, int NB, int MB>
 constexpr int quad_red_bytes() {
-  return QuadOp<NK, NB, PLUG>::kWarps * QuadOp<NK, NB, PLUG>::kSlot * 4;
+  return QuadOp<NK, NB, MB>::kWarps * QuadOp<NK, NB, MB>::kSlot * 4;
 }
 
-template <bool NK, int NB, bool PLUG>
+template <bool NK, int NB, int MB>
 __global__ void __launch_bounds__(quad_warps(NK, NB) * 32, 1) quad_gemv_kernel(const QuadParams p) {
   extern __shared__ __align__(1024) uint8_t smem[];
   __shared__ int s_flag;
   float* red = reinterpret_cast<float*>(smem + kQuadLutBytes);
   build_quad_lut(smem, reinterpret_cast<uint32_t*>(red), p.luts);
   __syncthreads();
-  QuadOp<NK, NB, PLUG> op(p, smem);
+  QuadOp<NK, NB, MB> op(p, smem);
   run_partition(op, p.part, red, &s_flag);
 }
 
@@ -313,12 +388,12 @@ PartitionPlan quad_plan(bool nk, int64_t Mc, int64_t N, int64_t K, int sms) {
   return plan_partition(cdiv(N, tile_w), cdiv(K, unit_k), quad_warps(nk, nb), sms, 4, Mc, tile_w);
 }
 
-bool g_attr_done[6][64];
+bool g_attr_done[8][64];
 
-template <bool NK, int NB, bool PLUG>
+template <bool NK, int NB, int MB>
 int launch_quad(const QuadParams& prm, int grid, int idx, cudaStream_t s) {
-  auto kern = quad_gemv_kernel<NK, NB, PLUG>;
-  constexpr int smem = (int)kQuadLutBytes + quad_red_bytes<NK, NB, PLUG>();
+  auto kern = quad_gemv_kernel<NK, NB, MB>;
+  constexpr int smem = (int)kQuadLutBytes + quad_red_bytes<NK, NB, MB>();
   static_assert(smem <= 227 * 1024, "shared memory budget");
   int rc = ensure_smem_attr(kern, smem, g_attr_done[idx]);
   if (rc) return rc;
@@ -326,18 +401,22 @@ int launch_quad(const QuadParams& prm, int grid, int idx, cudaStream_t s) {
   return check_launch("quad_gemv_kernel");
 }
 
-int launch_plan(const PartitionPlan& pl, bool nk, int nb, QuadParams prm, void* ws, bool plug,
+int launch_plan(const PartitionPlan& pl, bool nk, int64_t Mc, QuadParams prm, void* ws, bool plug,
                 cudaStream_t s) {
   prm.part.units = pl.units;
   prm.part.upt = (int)pl.upt;
   prm.part.counters = reinterpret_cast<int*>(ws);
   prm.part.slots = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(ws) + pl.counters_bytes);
+  const int nb = Mc > 8 ? 2 : 1;
   if (nk) {
-    if (plug) return nb == 1 ? launch_quad<true, 1, true>(prm, pl.grid, 0, s)
-                             : launch_quad<true, 2, true>(prm, pl.grid, 1, s);
-    return nb == 1 ? launch_quad<true, 1, false>(prm, pl.grid, 2, s) : launch_quad<true, 2, false>(prm, pl.grid, 3, s);
+    if (plug) {
+      if (Mc == 1) return launch_quad<true, 1, 1>(prm, pl.grid, 0, s);
+      if (Mc <= 8) return launch_quad<true, 1, 8>(prm, pl.grid, 1, s);
+      return launch_quad<true, 2, 16>(prm, pl.grid, 2, s);
+    }
+    return nb == 1 ? launch_quad<true, 1, 0>(prm, pl.grid, 3, s) : launch_quad<true, 2, 0>(prm, pl.grid, 4, s);
   }
-  return nb == 1 ? launch_quad<false, 1, false>(prm, pl.grid, 4, s) : launch_quad<false, 2, false>(prm, pl.grid, 5, s);
+  return nb == 1 ? launch_quad<false, 1, 0>(prm, pl.grid, 5, s) : launch_quad<false, 2, 0>(prm, pl.grid, 6, s);
 }
 
 bool quad_vector_ok(bool nk, const uint32_t* codes, int64_t ldc_k, int64_t ldc_n, int64_t N, int64_t K) {
@@ -383,7 +462,8 @@ size_t quad_ws_bytes(bool nk, int64_t M, int64_t N, int64_t K) {
 }  // namespace
 
 static int quad_run(const void* a, int64_t lda_m, int64_t lda_k, const uint32_t* codes, int64_t ldc_k,
-                    int64_t ldc_n, const void* plug_vals, const uint64_t* pmask, const uint32_t* pbase,
+                    int64_t ldc_n, const uint32_t* plug_idx, const void* plug_vals, const uint32_t* wbase,
+                    uint32_t base_lo32,
                     const void* const luts[7], const float scales[4], void* const out[4], int64_t ldo_m,
                     int64_t ldo_n, int64_t M, int64_t N, int64_t K, void* ws, size_t ws_bytes,
                     cudaStream_t s, bool file_layout) {
@@ -400,8 +480,8 @@ static int quad_run(const void* a, int64_t lda_m, int64_t lda_k, const uint32_t*
     return PP_ERR_INVALID;
   }
   const bool plug = file_layout && plug_vals != nullptr;
-  if (plug && (!pmask || !pbase || !aligned(plug_vals, 8))) {
-    set_error("plug_mask/plug_base missing or plug_vals not 8-byte aligned");
+  if (plug && (!plug_idx || !wbase || !aligned(plug_vals, 8))) {
+    set_error("plug_idx / plug_window_base missing or plug_vals not 8-byte aligned");
     return PP_ERR_INVALID;
   }
   const bool nk = file_layout || (ldc_k == 1 && ldc_n != 1);
@@ -455,9 +535,10 @@ static int quad_run(const void* a, int64_t lda_m, int64_t lda_k, const uint32_t*
   prm.ldo_n = ldo_n;
   prm.N = (int)N;
   prm.K = (int)K;
+  prm.plug_idx = plug_idx;
   prm.plug_vals = reinterpret_cast<const uint2*>(plug_vals);
-  prm.pmask = reinterpret_cast<const unsigned long long*>(pmask);
-  prm.pbase = pbase;
+  prm.wbase = wbase;
+  prm.base_lo32 = base_lo32;
   prm.W = (int)cdiv(K, 64);
   const size_t need = quad_plan(nk, M < 16 ? M : 16, N, K, sms).total();
   if (ws_bytes < need || (need && !ws) || !aligned(ws, 256)) {
@@ -473,7 +554,7 @@ static int quad_run(const void* a, int64_t lda_m, int64_t lda_k, const uint32_t*
     prm.M = (int)Mc;
     const int xalign = nk ? 8 : 4;
     prm.xvec = (lda_k == 1 && aligned(prm.x, xalign) && (lda_m * 2) % xalign == 0) ? 1 : 0;
-    if ((rc = launch_plan(pl, nk, Mc > 8 ? 2 : 1, prm, ws, plug, s))) return rc;
+    if ((rc = launch_plan(pl, nk, Mc, prm, ws, plug, s))) return rc;
   }
   return PP_OK;
 }
@@ -497,7 +578,7 @@ int pp_quad_gemm(const void* a, int64_t lda_m, int64_t lda_k, const uint32_t* co
                  int64_t ldc_n, const void* const luts[7], const float scales[4], void* const out[4],
                  int64_t ldo_m, int64_t ldo_n, int64_t M, int64_t N, int64_t K, void* workspace,
                  size_t workspace_bytes, void* stream) {
-  return pp::quad_run(a, lda_m, lda_k, codes, ldc_k, ldc_n, nullptr, nullptr, nullptr, luts, scales, out,
+  return pp::quad_run(a, lda_m, lda_k, codes, ldc_k, ldc_n, nullptr, nullptr, nullptr, 0u, luts, scales, out,
                       ldo_m, ldo_n, M, N, K, workspace, workspace_bytes,
                       reinterpret_cast<cudaStream_t>(stream), false);
 }
@@ -512,11 +593,12 @@ int pp_quad_linear_workspace_bytes(int64_t M, int64_t N, int64_t K, size_t* byte
 }
 
 int pp_quad_linear(const void* x, int64_t ldx_m, int64_t ldx_k, const uint32_t* codes, int64_t ldw,
-                   const void* plug_vals, const uint64_t* plug_mask, const uint32_t* plug_base,
-                   const void* const luts[7], const float scales[4], void* const out[4], int64_t ldo_m,
-                   int64_t ldo_n, int64_t M, int64_t N, int64_t K, void* workspace, size_t workspace_bytes,
-                   void* stream) {
-  return pp::quad_run(x, ldx_m, ldx_k, codes, 1, ldw, plug_vals, plug_mask, plug_base, luts, scales, out,
+                   const uint32_t* plug_idx, const void* plug_vals, const uint32_t* plug_window_base,
+                   uint32_t base_lo32, const void* const luts[7], const float scales[4], void* const out[4],
+                   int64_t ldo_m, int64_t ldo_n, int64_t M, int64_t N, int64_t K, void* workspace,
+                   size_t workspace_bytes, void* stream) {
+  return pp::quad_run(x, ldx_m, ldx_k, codes, 1, ldw, plug_idx, plug_vals, plug_window_base, base_lo32, luts,
+                      scales, out,
                       ldo_m, ldo_n, M, N, K, workspace, workspace_bytes,
                       reinterpret_cast<cudaStream_t>(stream), true);
 }

@@ -123,9 +123,9 @@ class QuadLinearSlice:
     p_lo: int
     p_hi: int
     codes: torch.Tensor
+    plug_idx: torch.Tensor | None
     plug_vals: torch.Tensor | None
-    plug_mask: torch.Tensor | None
-    plug_base: torch.Tensor | None
+    plug_window_base: torch.Tensor | None
     _ws: dict = field(default_factory=dict)
 
     @property
@@ -162,16 +162,16 @@ class QuadPackDevice:
             raise ValueError(f"Linear [{offset}, {offset + N * K}) is outside the coded range [0, {n})")
         p_lo, p_hi = self._plug_range(offset, offset + N * K)
         codes = self.codes[offset:offset + N * K].view(N, K)
-        pv = pm = pb = None
+        pi = pv = wb = None
         if p_hi > p_lo:
-            W = -(-K // 64)
-            pm = torch.empty((N, W), dtype=torch.int64, device=self.device)
-            pb = torch.empty((N, W), dtype=torch.int32, device=self.device)
-            _lib.call("pp_quad_plug_index", self.plug_idx.data_ptr(), p_lo, p_hi,
-                      ctypes.c_uint32(offset & 0xFFFFFFFF), N, K, pm.data_ptr(), pb.data_ptr(),
-                      self._bad.data_ptr(), _lib.stream_handle(self.device))
+            # one-time preparation: window index + zero norm byte of plugged codes
+            wb = torch.empty(N * (-(-K // 64)) + 1, dtype=torch.int32, device=self.device)
+            _lib.call("pp_quad_prepare_plugs", codes.data_ptr(), K, self.plug_idx.data_ptr(), p_lo, p_hi,
+                      ctypes.c_uint32(offset & 0xFFFFFFFF), N, K, wb.data_ptr(), self._bad.data_ptr(),
+                      _lib.stream_handle(self.device))
+            pi = self.plug_idx[p_lo:p_hi]
             pv = self.plug_vals[p_lo:p_hi]
-        return QuadLinearSlice(self, offset, N, K, p_lo, p_hi, codes, pv, pm, pb)
+        return QuadLinearSlice(self, offset, N, K, p_lo, p_hi, codes, pi, pv, wb)
 
     def check_plug_index(self) -> None:
         """Raise if any plug entry fell outside its Linear (syncs the device)."""
@@ -223,7 +223,8 @@ def quad_linear(x: torch.Tensor, layer: QuadLinearSlice, out=None) -> list[torch
     ws = _lib.workspace(dev, nb) if nb else None
     pk = layer.pack
     _lib.call("pp_quad_linear", x.data_ptr(), x.stride(0), x.stride(1), layer.codes.data_ptr(), layer.K,
-              _lib.ptr(layer.plug_vals), _lib.ptr(layer.plug_mask), _lib.ptr(layer.plug_base),
+              _lib.ptr(layer.plug_idx), _lib.ptr(layer.plug_vals), _lib.ptr(layer.plug_window_base),
+              ctypes.c_uint32(layer.offset & 0xFFFFFFFF),
               _lib.ptrs(pk.luts, 7), _lib.floats4(pk.scales), _lib.ptrs(out, 4),
               out[0].stride(0), out[0].stride(1), M, layer.N, layer.K,
               _lib.ptr(ws), ws.numel() if ws is not None else 0, _lib.stream_handle(dev))
