@@ -18,7 +18,9 @@ namespace pp {
 
 int zero_f16(void* p, int64_t R, int64_t C, int64_t ldr, int64_t ldc, cudaStream_t s);
 
-__host__ __device__ constexpr int dual_warps(int nb) { return nb == 1 ? 12 : 8; }
+// Warps per CTA, bounded by shared memory: 136 KiB of tables plus two
+// partial slots per warp.
+__host__ __device__ constexpr int dual_warps(int nb) { return nb == 1 ? 10 : 5; }
 
 struct DualParams {
   const __half* x;
@@ -46,11 +48,9 @@ struct DualOp {
   static constexpr int kTileW = 64;
   static constexpr int kNOut = 2;
   static constexpr int kNBat = 8 * NB;
-  static constexpr int kSlot = kNOut * kNBat * kTileW;
   using Buf = DualBuf;
 
   const DualParams& p;
-  const uint8_t* lut;
   int g, c;
   uint32_t laneoff;
   int Mv, Nv, Kv;
@@ -59,8 +59,8 @@ struct DualOp {
   bool xok[NB];
   float acc[8][NB][4];
 
-  __device__ __forceinline__ DualOp(const DualParams& p_, const uint8_t* lut_)
-      : p(p_), lut(lut_), g((threadIdx.x & 31) >> 2), c(threadIdx.x & 3),
+  __device__ __forceinline__ DualOp(const DualParams& p_)
+      : p(p_), g((threadIdx.x & 31) >> 2), c(threadIdx.x & 3),
         laneoff((threadIdx.x & 31) * 4u), Mv(p_.M), Nv(p_.N), Kv(p_.K), ldc(p_.ldc) {
 #pragma unroll
     for (int nb = 0; nb < NB; ++nb) {
@@ -71,15 +71,15 @@ struct DualOp {
   }
 
   __device__ __forceinline__ int M() const { return Mv; }
-  __device__ __forceinline__ int64_t N() const { return Nv; }
+  __device__ __forceinline__ int N() const { return Nv; }
 
-  __device__ __forceinline__ void prefetch(int64_t tile, int kc) const {
+  __device__ __forceinline__ void prefetch(int tile, int kc) const {
     // 16 rows x 128 bytes (64 int16 codes), one row per lane 0..15
     const int lane = threadIdx.x & 31;
     const int k = kc * 16 + (lane & 15);
-    const int64_t f0 = tile * 64;
+    const int f0 = tile * 64;
     if (lane < 16 && k < Kv && f0 < Nv) {
-      const int64_t n = Nv - f0 < 64 ? Nv - f0 : 64;
+      const int n = Nv - f0 < 64 ? Nv - f0 : 64;
       prefetch_l2(p.codes + (int64_t)k * ldc + f0, (uint32_t)n * 2u);
     }
   }
@@ -93,8 +93,8 @@ struct DualOp {
         for (int j = 0; j < 4; ++j) acc[t][nb][j] = 0.f;
   }
 
-  __device__ __forceinline__ void load(Buf& b, int64_t tile, int kc) const {
-    const int64_t f = tile * 64 + 8 * g;
+  __device__ __forceinline__ void load(Buf& b, int tile, int kc) const {
+    const int f = tile * 64 + 8 * g;
 #pragma unroll
     for (int r = 0; r < 4; ++r) {
       const int k = kc * 16 + 2 * c + (r & 1) + 8 * (r >> 1);
@@ -126,17 +126,17 @@ struct DualOp {
     const uint32_t ah = ((w >> 19) & 0x1F80u) | laneoff;
     const uint32_t pl = ((w << 7) & 0x1FF80u) | laneoff;
     const uint32_t ph = ((w >> 9) & 0x1FF80u) | laneoff;
-    const float ampl = __fmul_rn(*reinterpret_cast<const float*>(lut + al), s);
-    const float amph = __fmul_rn(*reinterpret_cast<const float*>(lut + ah), s);
-    const __half2 csl = u2h(*reinterpret_cast<const uint32_t*>(lut + kDualAmpBytes + pl));
-    const __half2 csh = u2h(*reinterpret_cast<const uint32_t*>(lut + kDualAmpBytes + ph));
+    const float ampl = __fmul_rn(*reinterpret_cast<const float*>(pp_smem + al), s);
+    const float amph = __fmul_rn(*reinterpret_cast<const float*>(pp_smem + ah), s);
+    const __half2 csl = u2h(*reinterpret_cast<const uint32_t*>(pp_smem + kDualAmpBytes + pl));
+    const __half2 csh = u2h(*reinterpret_cast<const uint32_t*>(pp_smem + kDualAmpBytes + ph));
     b1l = __fmul_rn(ampl, __low2float(csl));
     b2l = __fmul_rn(ampl, __high2float(csl));
     b1h = __fmul_rn(amph, __low2float(csh));
     b2h = __fmul_rn(amph, __high2float(csh));
   }
 
-  __device__ __forceinline__ void compute(const Buf& b, int64_t tile, int kc) {
+  __device__ __forceinline__ void compute(const Buf& b, int tile, int kc) {
     const int kbase = kc * 16;
     uint32_t b0[NB], b1[NB];
 #pragma unroll
@@ -171,7 +171,7 @@ struct DualOp {
   }
 
   // Fragment register j: model (j >> 1), batch 8nb + 2c + (j & 1), feature 8g + t.
-  __device__ __forceinline__ void write_partial(float* red) const {
+  __device__ __forceinline__ void write_partial(float* slot, int M) const {
 #pragma unroll
     for (int t = 0; t < 8; ++t)
 #pragma unroll
@@ -179,28 +179,42 @@ struct DualOp {
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
           const int bat = nb * 8 + 2 * c + (j & 1);
-          red[((j >> 1) * kNBat + bat) * kTileW + 8 * g + t] = acc[t][nb][j];
+          if (bat < M) slot[((j >> 1) * M + bat) * kTileW + 8 * g + t] = acc[t][nb][j];
         }
   }
 
-  __device__ __forceinline__ void store(int model, int bat, int64_t f, float v) const {
-    p.out[model][(int64_t)bat * p.ldo_m + f * p.ldo_n] = __float2half_rn(v);
+  __device__ __forceinline__ void store_tile(int tile) const {
+#pragma unroll
+    for (int t = 0; t < 8; ++t) {
+      const int f = tile * 64 + 8 * g + t;
+      if (f >= Nv) continue;
+#pragma unroll
+      for (int nb = 0; nb < NB; ++nb)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const int bat = nb * 8 + 2 * c + (j & 1);
+          if (bat < Mv) store(j >> 1, bat, f, acc[t][nb][j]);
+        }
+    }
+  }
+
+  __device__ __forceinline__ void store(int model, int bat, int f, float v) const {
+    p.out[model][(int64_t)bat * p.ldo_m + (int64_t)f * p.ldo_n] = __float2half_rn(v);
   }
 };
 
-template <int NB>
-constexpr int dual_red_bytes() {
-  return DualOp<NB>::kWarps * DualOp<NB>::kSlot * 4;
+inline size_t dual_smem_bytes(int nb, int64_t M) {
+  const size_t r = red_bytes(dual_warps(nb), 2, M, 64);
+  return kDualLutBytes + (r > 8192 ? r : 8192);
 }
 
 template <int NB>
 __global__ void __launch_bounds__(dual_warps(NB) * 32, 1) dual_gemv_kernel(const DualParams p) {
-  extern __shared__ __align__(1024) uint8_t smem[];
   __shared__ int s_flag;
-  float* red = reinterpret_cast<float*>(smem + kDualLutBytes);
-  build_dual_lut(smem, reinterpret_cast<uint32_t*>(red), p.amp_lut, p.cos_lut, p.sin_lut);
+  float* red = reinterpret_cast<float*>(pp_smem + kDualLutBytes);
+  build_dual_lut(pp_smem, reinterpret_cast<uint32_t*>(red), p.amp_lut, p.cos_lut, p.sin_lut);
   __syncthreads();
-  DualOp<NB> op(p, smem);
+  DualOp<NB> op(p);
   run_partition(op, p.part, red, &s_flag);
 }
 
@@ -267,9 +281,13 @@ bool g_dual_attr[2][64];
 template <int NB>
 int launch_dual(const DualParams& prm, int grid, cudaStream_t s) {
   auto kern = dual_gemv_kernel<NB>;
-  constexpr int smem = (int)kDualLutBytes + dual_red_bytes<NB>();
-  static_assert(smem <= 227 * 1024, "shared memory budget");
-  int rc = ensure_smem_attr(kern, smem, g_dual_attr[NB - 1]);
+  constexpr int max_smem = 227 * 1024;
+  const size_t smem = dual_smem_bytes(NB, prm.M);
+  if (smem > (size_t)max_smem) {
+    set_error("internal: shared memory plan %zu exceeds the per-CTA limit", smem);
+    return PP_ERR_INVALID;
+  }
+  int rc = ensure_smem_attr(kern, max_smem, g_dual_attr[NB - 1]);
   if (rc) return rc;
   kern<<<grid, dual_warps(NB) * 32, smem, s>>>(prm);
   return check_launch("dual_gemv_kernel");
@@ -343,6 +361,10 @@ static int dual_run(const void* a, int64_t lda_m, int64_t lda_k, const int16_t* 
     set_error("cannot query the SM count of the current device");
     return PP_ERR_CUDA;
   }
+  if (cdiv(N, 64) * cdiv(K, 16) >= (int64_t)INT32_MAX) {
+    set_error("matrix too large for one launch (more than 2^31 work units)");
+    return PP_ERR_INVALID;
+  }
   const size_t need = dual_plan(M < 16 ? M : 16, N, K, sms).total();
   if (ws_bytes < need || (need && !ws) || !aligned(ws, 256)) {
     set_error("workspace of %zu bytes (256-byte aligned, zero-filled) required, got %zu", need, ws_bytes);
@@ -370,7 +392,7 @@ static int dual_run(const void* a, int64_t lda_m, int64_t lda_k, const int16_t* 
     prm.out[1] = reinterpret_cast<__half*>(out2) + m0 * ldo_m;
     prm.M = (int)Mc;
     prm.xvec = (lda_k == 1 && aligned(prm.x, 4) && (lda_m * 2) % 4 == 0) ? 1 : 0;
-    prm.part.units = pl.units;
+    prm.part.units = (int)pl.units;
     prm.part.upt = (int)pl.upt;
     prm.part.counters = reinterpret_cast<int*>(ws);
     prm.part.slots = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(ws) + pl.counters_bytes);

@@ -11,6 +11,11 @@
 #include <cuda_fp16.h>
 #include <stdint.h>
 
+// The dynamic shared memory of every kernel in this library.  Addressing
+// the tables through the symbol (not a pointer) lets the table offset fold
+// into the shared-load instruction.
+extern __shared__ __align__(1024) uint8_t pp_smem[];
+
 namespace pp {
 
 constexpr int kWarpSize = 32;
@@ -93,15 +98,15 @@ struct QuadDec {
   uint32_t p1, p2, p3;
 };
 
-__device__ __forceinline__ QuadDec decode_quad(uint32_t code, const uint8_t* lut, uint32_t laneoff) {
+__device__ __forceinline__ QuadDec decode_quad(uint32_t code, uint32_t laneoff) {
   const uint32_t o0 = __byte_perm(code, laneoff, 0x7634);  // norm index (byte 3)
   const uint32_t o1 = __byte_perm(code, laneoff, 0x7624);  // t1 index   (byte 2)
   const uint32_t o2 = __byte_perm(code, laneoff, 0x7614);  // t2 index   (byte 1)
   const uint32_t o3 = __byte_perm(code, laneoff, 0x7604);  // t3 index   (byte 0)
-  const uint32_t rr = *reinterpret_cast<const uint32_t*>(lut + o0);
-  const uint32_t cs1 = *reinterpret_cast<const uint32_t*>(lut + 128u + o1);
-  const uint32_t cs2 = *reinterpret_cast<const uint32_t*>(lut + 65536u + o2);
-  const uint32_t cs3 = *reinterpret_cast<const uint32_t*>(lut + 65536u + 128u + o3);
+  const uint32_t rr = *reinterpret_cast<const uint32_t*>(pp_smem + o0);
+  const uint32_t cs1 = *reinterpret_cast<const uint32_t*>(pp_smem + 128u + o1);
+  const uint32_t cs2 = *reinterpret_cast<const uint32_t*>(pp_smem + 65536u + o2);
+  const uint32_t cs3 = *reinterpret_cast<const uint32_t*>(pp_smem + 65536u + 128u + o3);
   const __half2 p1 = __hmul2_rn(u2h(rr), u2h(cs1));                // (r*c1, r*s1)
   const __half2 p2 = __hmul2_rn(__high2half2(p1), u2h(cs2));       // (rs*c2, rs*s2)
   const __half2 p3 = __hmul2_rn(__high2half2(p2), u2h(cs3));       // (rss*c3, rss*s3)

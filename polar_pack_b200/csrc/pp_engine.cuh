@@ -3,21 +3,23 @@
 //
 // A "tile" is the set of output features one warp accumulates (8 rows for
 // the file layout, 32 or 64 features for the kernel layout); a "unit" is
-// one K chunk of a tile.  Units are numbered tile-major and the grid's CTAs
-// take equal contiguous ranges.  Inside a CTA all warps work on the same
-// tile at a time: warp w takes units seg0 + w, seg0 + w + NW, ... of the
-// CTA's segment of that tile, then the warps' FP32 partials are summed in
-// warp order through shared memory.  A tile that lies wholly inside the
-// CTA's range is stored directly; a tile shared with neighbouring CTAs (at
-// most the first and the last tile of a range) is reduced through the
-// workspace: each CTA writes its partial, fences, bumps the tile counter,
-// and the last CTA to arrive sums all partials in CTA order, stores the
-// result and resets the counter to zero.  No CTA ever waits for another.
-// Loads for a warp's next unit are issued before the current unit is
-// decoded, across tile boundaries too, so the barrier at the end of a tile
-// overlaps the next tile's loads; a second cursor runs kPrefetch units
-// further ahead and pulls those units into L2 with bulk prefetches, which
-// keeps enough bytes in flight per SM without spending registers.
+// one K chunk of a tile.  Units are numbered tile-major.  The grid's CTAs
+// take equal contiguous unit ranges, and each warp of a CTA an equal
+// contiguous piece of its CTA's range, which it streams front to back: a
+// warp's consecutive units are consecutive K chunks of the same rows.
+//
+// A tile that lies wholly inside one warp's range is stored by that warp.
+// A tile cut by a warp boundary leaves FP32 partials in shared memory (at
+// most two per warp); after the only barrier of the kernel the CTA sums
+// them in warp order.  A tile cut by a CTA boundary goes one level further:
+// each CTA writes its partial to the workspace, fences, bumps a counter, and
+// the last CTA to arrive sums all partials in CTA order, stores the result
+// and resets the counter.  No thread ever waits for another CTA, and the
+// summation order is fixed, so results are deterministic.
+//
+// Each warp keeps one unit in flight in registers (loaded before the
+// current unit is decoded) and bulk-prefetches the unit kPrefetch steps
+// ahead into L2.
 #pragma once
 
 #include <stdint.h>
@@ -28,161 +30,157 @@ namespace pp {
 // zero between launches) followed by the partial-sum slots.  A tile shared
 // by CTAs c_first < ... < c_last uses counter c_last: c_last contains the
 // tile's last unit and starts inside it, so no CTA is c_last of two shared
-// tiles.  Counters therefore never overlap slot memory of any other plan.
+// tiles, and counters never overlap slot memory of any other plan.
 constexpr int kMaxGrid = 1024;
 constexpr size_t kCounterBytes = kMaxGrid * sizeof(int);
 
 struct Partition {
-  int64_t units;  // total units
+  int units;      // total units (< 2^31, checked on the host)
   int upt;        // units per tile
   int* counters;  // [kMaxGrid] arrival counters (zero between launches)
   float* slots;   // [grid][2][nout * M * tile_w] cross-CTA partials
 };
 
-__device__ __forceinline__ int64_t cta_of_unit(int64_t x, int64_t U, int64_t G) {
-  // largest c with floor(U*c/G) <= x
-  const int64_t c = ((x + 1) * G + U - 1) / U - 1;
+__device__ __forceinline__ int range_start(int U, int parts, int i) {
+  return (int)(((int64_t)U * i) / parts);
+}
+
+// largest c with range_start(U, G, c) <= x
+__device__ __forceinline__ int part_of_unit(int x, int U, int G) {
+  const int c = (int)((((int64_t)x + 1) * G + U - 1) / U) - 1;
   return c < G - 1 ? c : G - 1;
 }
 
 // Op interface (device struct):
-//   static constexpr int kWarps, kTileW, kNOut, kNBat, kSlot (= kNOut*kNBat*kTileW)
+//   static constexpr int kWarps, kTileW, kNOut, kNBat
 //   using Buf = ...;
-//   void zero();                                   accumulators := 0
-//   void load(Buf&, int64_t tile, int kc) const;   issue loads of one unit
-//   void prefetch(int64_t tile, int kc) const;     L2 prefetch of one unit
-//   void compute(const Buf&, int64_t tile, int kc);
-//   void write_partial(float* red) const;          this warp's kSlot floats
-//   int  M() const; int64_t N() const;
-//   void store(int out, int bat, int64_t f, float v) const;  final FP16 store
+//   void zero();                                accumulators := 0
+//   void load(Buf&, int tile, int kc) const;    issue loads of one unit
+//   void prefetch(int tile, int kc) const;      L2 prefetch of one unit
+//   void compute(const Buf&, int tile, int kc);
+//   void write_partial(float* slot, int M);     compact [out][bat < M][fi]
+//   int  M() const; int N() const;
+//   void store_tile(int tile) const;            whole tile from registers
+//   void store(int out, int bat, int f, float v) const;
+//
+// Shared memory `red` holds kWarps * 2 compact slots of nout * M * tile_w floats.
 template <class Op>
 __device__ __forceinline__ void run_partition(Op& op, const Partition& pt, float* red, int* s_flag) {
   constexpr int NW = Op::kWarps;
+  constexpr int TW = Op::kTileW;
   const int tid = threadIdx.x;
   const int warp = tid >> 5;
-  const int64_t U = pt.units;
-  const int64_t G = gridDim.x;
-  const int64_t cu0 = U * blockIdx.x / G, cu1 = U * (blockIdx.x + 1) / G;
+  const int U = pt.units;
+  const int G = gridDim.x;
+  const int cu0 = range_start(U, G, blockIdx.x), cu1 = range_start(U, G, blockIdx.x + 1);
   if (cu0 >= cu1) return;  // uniform over the CTA
   const int upt = pt.upt;
-  const int64_t t_first = cu0 / upt;
-  const int64_t t_last = (cu1 - 1) / upt;
+  const int M = op.M();
+  const int nval = Op::kNOut * M * TW;
+  const int R = cu1 - cu0;
+  const int wu0 = cu0 + range_start(R, NW, warp), wu1 = cu0 + range_start(R, NW, warp + 1);
 
-  // this warp's unit cursor: (tile, unit); valid == false at the end
-  int64_t cur_t = 0, cur_u = 0, nxt_t = 0, nxt_u = 0;
-  bool cur_ok = false, nxt_ok = false;
-  auto first_from = [&](int64_t tt, int64_t& ot, int64_t& ou) -> bool {
-    for (; tt <= t_last; ++tt) {
-      const int64_t s0 = tt * upt > cu0 ? tt * upt : cu0;
-      const int64_t s1 = (tt + 1) * upt < cu1 ? (tt + 1) * upt : cu1;
-      if (s0 + warp < s1) {
-        ot = tt;
-        ou = s0 + warp;
-        return true;
+  if (wu0 < wu1) {
+    constexpr int kPrefetch = 4;
+    int t = wu0 / upt, kc = wu0 - t * upt;        // current unit
+    const int t_first = t;
+    int pt_t = t, pt_kc = kc;                      // prefetch cursor
+    for (int i = 1; i <= kPrefetch; ++i) {         // units wu0+2 .. wu0+kPrefetch-1 now
+      if (++pt_kc == upt) { pt_kc = 0; ++pt_t; }
+      if (i >= 2 && i < kPrefetch && wu0 + i < wu1) op.prefetch(pt_t, pt_kc);
+    }
+    typename Op::Buf bufA, bufB;
+    op.zero();
+    op.load(bufA, t, kc);
+    int u = wu0;
+    auto step = [&](const typename Op::Buf& cur, typename Op::Buf& nxt) -> bool {
+      // prefetch kPrefetch ahead, load the next unit, decode this one
+      if (u + kPrefetch < wu1) op.prefetch(pt_t, pt_kc);
+      if (++pt_kc == upt) { pt_kc = 0; ++pt_t; }
+      int nt = t, nkc = kc + 1;
+      if (nkc == upt) { nkc = 0; ++nt; }
+      if (u + 1 < wu1) op.load(nxt, nt, nkc);
+      op.compute(cur, t, kc);
+      const bool tile_end = nkc == 0;
+      const bool last = u + 1 == wu1;
+      if (tile_end || last) {
+        const bool whole = (t * upt >= wu0) && tile_end;
+        if (whole) {
+          op.store_tile(t);
+        } else {
+          const int which = t == t_first ? 0 : 1;
+          op.write_partial(red + (warp * 2 + which) * nval, M);
+        }
+        op.zero();
       }
-    }
-    return false;
-  };
-  auto advance = [&](int64_t t, int64_t u, int64_t& ot, int64_t& ou) -> bool {
-    const int64_t s1 = (t + 1) * upt < cu1 ? (t + 1) * upt : cu1;
-    if (u + NW < s1) {
-      ot = t;
-      ou = u + NW;
-      return true;
-    }
-    return first_from(t + 1, ot, ou);
-  };
-
-  typename Op::Buf bufA, bufB;
-  cur_ok = first_from(t_first, cur_t, cur_u);
-  // prefetch cursor: kPrefetch units of this warp ahead of the current one
-  constexpr int kPrefetch = 4;
-  int64_t pf_t = cur_t, pf_u = cur_u;
-  bool pf_ok = cur_ok;
-  if (cur_ok) {
-    op.load(bufA, cur_t, (int)(cur_u - cur_t * upt));
-    nxt_ok = advance(cur_t, cur_u, nxt_t, nxt_u);
-    // units cur+2 .. cur+kPrefetch now; cur+1 is loaded into registers
-    pf_ok = nxt_ok && advance(nxt_t, nxt_u, pf_t, pf_u);
-#pragma unroll 1
-    for (int i = 2; i <= kPrefetch && pf_ok; ++i) {
-      op.prefetch(pf_t, (int)(pf_u - pf_t * upt));
-      pf_ok = advance(pf_t, pf_u, pf_t, pf_u);
+      t = nt;
+      kc = nkc;
+      return ++u < wu1;
+    };
+    while (step(bufA, bufB) && step(bufB, bufA)) {
     }
   }
+  __syncthreads();
 
-  int64_t pend[2];
+  // tiles cut by a warp boundary: sum the warps' partials in warp order
+  const int ct0 = cu0 / upt, ct1 = (cu1 - 1) / upt;
+  int pend[2];
   int npend = 0;
-  const int M = op.M();
-  constexpr int TW = Op::kTileW;
-  const int nval = Op::kNOut * M * TW;  // compact partial: [out][bat < M][fi]
-
-  for (int64_t tt = t_first; tt <= t_last; ++tt) {
-    op.zero();
-    while (cur_ok && cur_t == tt) {
-      if (pf_ok) {
-        op.prefetch(pf_t, (int)(pf_u - pf_t * upt));
-        pf_ok = advance(pf_t, pf_u, pf_t, pf_u);
-      }
-      if (nxt_ok) op.load(bufB, nxt_t, (int)(nxt_u - nxt_t * upt));
-      op.compute(bufA, cur_t, (int)(cur_u - cur_t * upt));
-      bufA = bufB;
-      cur_ok = nxt_ok;
-      cur_t = nxt_t;
-      cur_u = nxt_u;
-      if (cur_ok) nxt_ok = advance(cur_t, cur_u, nxt_t, nxt_u);
-    }
-    op.write_partial(red + warp * Op::kSlot);
-    __syncthreads();
-    const bool whole = (tt * upt >= cu0) && ((tt + 1) * upt <= cu1);
-    const int which = tt == t_first ? 0 : 1;
-    float* slot = pt.slots + ((int64_t)blockIdx.x * 2 + which) * (int64_t)nval;
+  for (int tt = ct0; tt <= ct1; ++tt) {
+    const int a = tt * upt, b = a + upt;  // unit range of the tile
+    const int w_first = part_of_unit((a > cu0 ? a : cu0) - cu0, R, NW);
+    const int w_last = part_of_unit((b < cu1 ? b : cu1) - 1 - cu0, R, NW);
+    const bool one_warp = w_first == w_last && a >= cu0 + range_start(R, NW, w_first) &&
+                          b <= cu0 + range_start(R, NW, w_first + 1);
+    const bool cta_whole = a >= cu0 && b <= cu1;
+    if (one_warp && cta_whole) continue;  // stored by its warp
+    float* slot = pt.slots + ((int64_t)blockIdx.x * 2 + (tt == ct0 ? 0 : 1)) * (int64_t)nval;
     for (int e = tid; e < nval; e += NW * 32) {
-      const int o = e / (M * TW);
-      const int rem = e - o * M * TW;
-      const int bat = rem / TW;
-      const int fi = rem - bat * TW;
-      const int ri = (o * Op::kNBat + bat) * TW + fi;
       float s = 0.f;
-#pragma unroll
-      for (int w = 0; w < NW; ++w) s += red[w * Op::kSlot + ri];
-      if (whole) {
-        const int64_t f = tt * TW + fi;
+      for (int w = w_first; w <= w_last; ++w) {
+        const int ws0 = cu0 + range_start(R, NW, w);
+        if (ws0 == cu0 + range_start(R, NW, w + 1)) continue;  // empty range (fewer units than warps)
+        const int which = (ws0 >= a) ? 0 : 1;  // the tile is w's first tile iff w starts in it
+        s += red[(w * 2 + which) * nval + e];
+      }
+      if (cta_whole) {
+        const int o = e / (M * TW);
+        const int rem = e - o * M * TW;
+        const int bat = rem / TW;
+        const int f = tt * TW + (rem - bat * TW);
         if (f < op.N()) op.store(o, bat, f, s);
       } else {
         __stcg(slot + e, s);
       }
     }
-    if (!whole && npend < 2) pend[npend++] = tt;
-    __syncthreads();
+    if (!cta_whole && npend < 2) pend[npend++] = tt;
   }
 
-  // tiles shared with other CTAs: last arrival reduces in CTA order
+  // tiles cut by a CTA boundary: last arrival reduces in CTA order
   for (int i = 0; i < npend; ++i) {
-    const int64_t tt = pend[i];
-    const int64_t c_first = cta_of_unit(tt * upt, U, G);
-    const int64_t c_last = cta_of_unit(tt * upt + upt - 1, U, G);
+    const int tt = pend[i];
+    const int c_first = part_of_unit(tt * upt, U, G);
+    const int c_last = part_of_unit(tt * upt + upt - 1, U, G);
     __threadfence();
     __syncthreads();
     if (tid == 0) {
       const int old = atomicAdd(pt.counters + c_last, 1);
-      *s_flag = (old == (int)(c_last - c_first)) ? 1 : 0;
+      *s_flag = (old == c_last - c_first) ? 1 : 0;
     }
     __syncthreads();
     if (*s_flag) {
       __threadfence();
       for (int e = tid; e < nval; e += NW * 32) {
+        float s = 0.f;
+        for (int c = c_first; c <= c_last; ++c) {
+          // only the first contributor can have started before the tile
+          const int w = (c == c_first && range_start(U, G, c) < tt * upt) ? 1 : 0;
+          s += __ldcg(pt.slots + ((int64_t)c * 2 + w) * (int64_t)nval + e);
+        }
         const int o = e / (M * TW);
         const int rem = e - o * M * TW;
         const int bat = rem / TW;
-        const int fi = rem - bat * TW;
-        float s = 0.f;
-        for (int64_t c = c_first; c <= c_last; ++c) {
-          // only the first contributor can have started before the tile
-          const int w = (c == c_first && U * c / G < tt * upt) ? 1 : 0;
-          s += __ldcg(pt.slots + (c * 2 + w) * (int64_t)nval + e);
-        }
-        const int64_t f = tt * TW + fi;
+        const int f = tt * TW + (rem - bat * TW);
         if (f < op.N()) op.store(o, bat, f, s);
       }
       if (tid == 0) pt.counters[c_last] = 0;
@@ -213,6 +211,11 @@ inline PartitionPlan plan_partition(int64_t tiles, int64_t upt, int warps, int s
   pl.counters_bytes = kCounterBytes;
   pl.slots_bytes = (size_t)pl.grid * 2 * (size_t)(nout * M * tile_w) * sizeof(float);
   return pl;
+}
+
+// Shared memory for the warps' partial slots of one launch.
+inline size_t red_bytes(int warps, int nout, int64_t M, int tile_w) {
+  return (size_t)warps * 2 * (size_t)(nout * M * tile_w) * sizeof(float);
 }
 
 }  // namespace pp

@@ -25,8 +25,7 @@ struct QuadDecodeParams {
 };
 
 __global__ void __launch_bounds__(512, 1) quad_decode_kernel(const QuadDecodeParams p) {
-  extern __shared__ __align__(1024) uint8_t smem[];
-  build_quad_lut(smem, reinterpret_cast<uint32_t*>(smem + kQuadLutBytes), p.luts);
+  build_quad_lut(pp_smem, reinterpret_cast<uint32_t*>(pp_smem + kQuadLutBytes), p.luts);
   __syncthreads();
   const uint32_t laneoff = (threadIdx.x & 31) * 4u;
   const int64_t total = p.R * p.C;
@@ -34,7 +33,7 @@ __global__ void __launch_bounds__(512, 1) quad_decode_kernel(const QuadDecodePar
        i += (int64_t)gridDim.x * blockDim.x) {
     const int64_t r = i / p.C, c = i - r * p.C;
     const uint32_t code = __ldg(p.codes + r * p.ldc_r + c * p.ldc_c);
-    const QuadDec d = decode_quad(code, smem, laneoff);
+    const QuadDec d = decode_quad(code, laneoff);
     __half w[4] = {__low2half(u2h(d.p1)), __low2half(u2h(d.p2)), __low2half(u2h(d.p3)),
                    __high2half(u2h(d.p3))};
     const int64_t o = r * p.ldo_r + c * p.ldo_c;

@@ -28,7 +28,7 @@ int zero_f16(void* p, int64_t R, int64_t C, int64_t ldr, int64_t ldc, cudaStream
 // Warps per CTA: the KN tile keeps 4x more accumulators per lane and two
 // batch tiles double them again, so those variants trade warps for
 // registers (NB = number of 8-row batch tiles).
-__host__ __device__ constexpr int quad_warps(bool nk, int nb) { return nb == 2 ? 8 : (nk ? 16 : 12); }
+__host__ __device__ constexpr int quad_warps(bool nk, int nb) { return nk ? (nb == 1 ? 16 : 8) : (nb == 1 ? 12 : 6); }
 
 struct QuadParams {
   const __half* x;
@@ -64,13 +64,11 @@ struct QuadOp {
   static constexpr int kT = NK ? 1 : 4;       // mma pairs per 16-k step
   static constexpr int kNOut = 4;
   static constexpr int kNBat = 8 * NB;
-  static constexpr int kSlot = kNOut * kNBat * kTileW;
   static constexpr bool kPlug = MB > 0;
   static constexpr int kMB = MB > 0 ? MB : 1;
   using Buf = QuadBuf;
 
   const QuadParams& p;
-  const uint8_t* lut;
   int g, c;
   uint32_t laneoff;
   int Mv, Nv, Kv, W;
@@ -80,8 +78,8 @@ struct QuadOp {
   float acc[kT][NB][2][4];
   float corr[kMB][4];
 
-  __device__ __forceinline__ QuadOp(const QuadParams& p_, const uint8_t* lut_)
-      : p(p_), lut(lut_), g((threadIdx.x & 31) >> 2), c(threadIdx.x & 3),
+  __device__ __forceinline__ QuadOp(const QuadParams& p_)
+      : p(p_), g((threadIdx.x & 31) >> 2), c(threadIdx.x & 3),
         laneoff((threadIdx.x & 31) * 4u), Mv(p_.M), Nv(p_.N), Kv(p_.K), W(p_.W), ldc(p_.ldc) {
 #pragma unroll
     for (int nb = 0; nb < NB; ++nb) {
@@ -92,7 +90,7 @@ struct QuadOp {
   }
 
   __device__ __forceinline__ int M() const { return Mv; }
-  __device__ __forceinline__ int64_t N() const { return Nv; }
+  __device__ __forceinline__ int N() const { return Nv; }
 
   __device__ __forceinline__ void zero() {
 #pragma unroll
@@ -109,9 +107,9 @@ struct QuadOp {
       for (int q = 0; q < 4; ++q) corr[m][q] = 0.f;
   }
 
-  __device__ __forceinline__ void load(Buf& b, int64_t tile, int kc) const {
+  __device__ __forceinline__ void load(Buf& b, int tile, int kc) const {
     if constexpr (NK) {
-      const int64_t row = tile * 8 + g;
+      const int64_t row = (int64_t)tile * 8 + g;
       const int kb = kc * 64 + 4 * c;
       const uint32_t* base = p.codes + row * ldc + kb;
       const bool rok = row < Nv;
@@ -121,7 +119,7 @@ struct QuadOp {
         else b.q[s] = make_uint4(0, 0, 0, 0);
       }
     } else {
-      const int64_t f = tile * 32 + 4 * g;
+      const int f = tile * 32 + 4 * g;
       const bool fok = f < Nv;
 #pragma unroll
       for (int r = 0; r < 4; ++r) {
@@ -132,10 +130,10 @@ struct QuadOp {
     }
   }
 
-  __device__ __forceinline__ void prefetch(int64_t tile, int kc) const {
+  __device__ __forceinline__ void prefetch(int tile, int kc) const {
     if constexpr (NK) {
       // 8 rows x 256 bytes: one bulk prefetch per row, issued by lane c == 0
-      const int64_t row = tile * 8 + g;
+      const int64_t row = (int64_t)tile * 8 + g;
       const int k0 = kc * 64;
       if (c == 0 && row < Nv && k0 < Kv) {
         const int n = Kv - k0 < 64 ? Kv - k0 : 64;
@@ -145,9 +143,9 @@ struct QuadOp {
       // 16 rows x 128 bytes, one row per lane 0..15
       const int lane = threadIdx.x & 31;
       const int k = kc * 16 + (lane & 15);
-      const int64_t f0 = tile * 32;
+      const int f0 = tile * 32;
       if (lane < 16 && k < Kv && f0 < Nv) {
-        const int64_t n = Nv - f0 < 32 ? Nv - f0 : 32;
+        const int n = Nv - f0 < 32 ? Nv - f0 : 32;
         prefetch_l2(p.codes + (int64_t)k * ldc + f0, (uint32_t)n * 4u);
       }
     }
@@ -207,7 +205,7 @@ struct QuadOp {
     }
   }
 
-  __device__ __forceinline__ void compute(const Buf& b, int64_t tile, int kc) {
+  __device__ __forceinline__ void compute(const Buf& b, int tile, int kc) {
     if constexpr (NK) {
       const int kbase = kc * 64;
       const bool full_k = kbase + 64 <= Kv;
@@ -215,10 +213,10 @@ struct QuadOp {
       for (int s = 0; s < 4; ++s) {
         const int kp = kbase + 16 * s + 4 * c;
         QuadDec d[4];
-        d[0] = decode_quad(b.q[s].x, lut, laneoff);
-        d[1] = decode_quad(b.q[s].y, lut, laneoff);
-        d[2] = decode_quad(b.q[s].z, lut, laneoff);
-        d[3] = decode_quad(b.q[s].w, lut, laneoff);
+        d[0] = decode_quad(b.q[s].x, laneoff);
+        d[1] = decode_quad(b.q[s].y, laneoff);
+        d[2] = decode_quad(b.q[s].z, laneoff);
+        d[3] = decode_quad(b.q[s].w, laneoff);
         uint32_t a01[4] = {lo_pair(d[0].p1, d[1].p1), lo_pair(d[0].p2, d[1].p2),
                            lo_pair(d[2].p1, d[3].p1), lo_pair(d[2].p2, d[3].p2)};
         uint32_t a23[4] = {lo_pair(d[0].p3, d[1].p3), hi_pair(d[0].p3, d[1].p3),
@@ -234,7 +232,7 @@ struct QuadOp {
           mma_16816(acc[0][nb][1], a23[0], a23[1], a23[2], a23[3], xb.x, xb.y);
         }
       }
-      plug_correct(tile * 8 + g, kc);
+      plug_correct((int64_t)tile * 8 + g, kc);
     } else {
       const int kbase = kc * 16;
       const bool full_k = kbase + 16 <= Kv;
@@ -253,7 +251,7 @@ struct QuadOp {
 #pragma unroll
         for (int r = 0; r < 4; ++r) {
           const uint32_t code = t == 0 ? b.q[r].x : t == 1 ? b.q[r].y : t == 2 ? b.q[r].z : b.q[r].w;
-          d[r] = decode_quad(code, lut, laneoff);
+          d[r] = decode_quad(code, laneoff);
           if (!rv[r]) d[r] = QuadDec{0u, 0u, 0u};
         }
         const uint32_t a01[4] = {lo_pair(d[0].p1, d[1].p1), lo_pair(d[0].p2, d[1].p2),
@@ -269,12 +267,10 @@ struct QuadOp {
     }
   }
 
-  // Fragment register j of mma half h: model 2h + (j>>1), batch 8nb+2c+(j&1);
-  // feature-in-tile g (NK) or 4g + t (KN).
-  __device__ __forceinline__ void write_partial(float* red) {
+  // Plug corrections of the 4 lanes of a row are disjoint subsets: sum them
+  // (same order on every lane) and add them to the fragment of (model, batch).
+  __device__ __forceinline__ void fold_corr() {
     if constexpr (kPlug) {
-      // the 4 lanes of a row hold disjoint plug subsets: sum them (the same
-      // order on every lane), then add to the fragment owning (model, batch)
 #pragma unroll
       for (int m = 0; m < kMB; ++m)
 #pragma unroll
@@ -294,6 +290,12 @@ struct QuadOp {
               if (m == bat) acc[0][nb][h][j] += corr[m][2 * h + (j >> 1)];
           }
     }
+  }
+
+  // Fragment register j of mma half h: model 2h + (j>>1), batch 8nb+2c+(j&1);
+  // feature-in-tile g (NK) or 4g + t (KN).
+  __device__ __forceinline__ void write_partial(float* slot, int M) {
+    fold_corr();
 #pragma unroll
     for (int t = 0; t < kT; ++t) {
       const int fi = NK ? g : 4 * g + t;
@@ -303,31 +305,48 @@ struct QuadOp {
         for (int h = 0; h < 2; ++h)
 #pragma unroll
           for (int j = 0; j < 4; ++j) {
-            const int model = 2 * h + (j >> 1);
             const int bat = nb * 8 + 2 * c + (j & 1);
-            red[(model * kNBat + bat) * kTileW + fi] = acc[t][nb][h][j];
+            if (bat < M) slot[((2 * h + (j >> 1)) * M + bat) * kTileW + fi] = acc[t][nb][h][j];
           }
     }
   }
 
-  __device__ __forceinline__ void store(int model, int bat, int64_t f, float v) const {
-    p.out[model][(int64_t)bat * p.ldo_m + f * p.ldo_n] = __float2half_rn(v * p.scale[model]);
+  __device__ __forceinline__ void store_tile(int tile) {
+    fold_corr();
+#pragma unroll
+    for (int t = 0; t < kT; ++t) {
+      const int f = tile * kTileW + (NK ? g : 4 * g + t);
+      if (f >= Nv) continue;
+#pragma unroll
+      for (int nb = 0; nb < NB; ++nb)
+#pragma unroll
+        for (int h = 0; h < 2; ++h)
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const int bat = nb * 8 + 2 * c + (j & 1);
+            if (bat < Mv) store(2 * h + (j >> 1), bat, f, acc[t][nb][h][j]);
+          }
+    }
+  }
+
+  __device__ __forceinline__ void store(int model, int bat, int f, float v) const {
+    p.out[model][(int64_t)bat * p.ldo_m + (int64_t)f * p.ldo_n] = __float2half_rn(v * p.scale[model]);
   }
 };
 
-template <bool NK, int NB, int MB>
-constexpr int quad_red_bytes() {
-  return QuadOp<NK, NB, MB>::kWarps * QuadOp<NK, NB, MB>::kSlot * 4;
+// LUT + the warps' partial slots (at least the 4 KiB the table build stages in)
+inline size_t quad_smem_bytes(bool nk, int nb, int64_t M) {
+  const size_t r = red_bytes(quad_warps(nk, nb), 4, M, nk ? 8 : 32);
+  return kQuadLutBytes + (r > 4096 ? r : 4096);
 }
 
 template <bool NK, int NB, int MB>
 __global__ void __launch_bounds__(quad_warps(NK, NB) * 32, 1) quad_gemv_kernel(const QuadParams p) {
-  extern __shared__ __align__(1024) uint8_t smem[];
   __shared__ int s_flag;
-  float* red = reinterpret_cast<float*>(smem + kQuadLutBytes);
-  build_quad_lut(smem, reinterpret_cast<uint32_t*>(red), p.luts);
+  float* red = reinterpret_cast<float*>(pp_smem + kQuadLutBytes);
+  build_quad_lut(pp_smem, reinterpret_cast<uint32_t*>(red), p.luts);
   __syncthreads();
-  QuadOp<NK, NB, MB> op(p, smem);
+  QuadOp<NK, NB, MB> op(p);
   run_partition(op, p.part, red, &s_flag);
 }
 
@@ -393,9 +412,13 @@ bool g_attr_done[8][64];
 template <bool NK, int NB, int MB>
 int launch_quad(const QuadParams& prm, int grid, int idx, cudaStream_t s) {
   auto kern = quad_gemv_kernel<NK, NB, MB>;
-  constexpr int smem = (int)kQuadLutBytes + quad_red_bytes<NK, NB, MB>();
-  static_assert(smem <= 227 * 1024, "shared memory budget");
-  int rc = ensure_smem_attr(kern, smem, g_attr_done[idx]);
+  constexpr int max_smem = 227 * 1024;
+  const size_t smem = quad_smem_bytes(NK, NB, prm.M);
+  if (smem > (size_t)max_smem) {
+    set_error("internal: shared memory plan %zu exceeds the per-CTA limit", smem);
+    return PP_ERR_INVALID;
+  }
+  int rc = ensure_smem_attr(kern, max_smem, g_attr_done[idx]);
   if (rc) return rc;
   kern<<<grid, quad_warps(NK, NB) * 32, smem, s>>>(prm);
   return check_launch("quad_gemv_kernel");
@@ -403,7 +426,7 @@ int launch_quad(const QuadParams& prm, int grid, int idx, cudaStream_t s) {
 
 int launch_plan(const PartitionPlan& pl, bool nk, int64_t Mc, QuadParams prm, void* ws, bool plug,
                 cudaStream_t s) {
-  prm.part.units = pl.units;
+  prm.part.units = (int)pl.units;
   prm.part.upt = (int)pl.upt;
   prm.part.counters = reinterpret_cast<int*>(ws);
   prm.part.slots = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(ws) + pl.counters_bytes);
@@ -540,6 +563,10 @@ static int quad_run(const void* a, int64_t lda_m, int64_t lda_k, const uint32_t*
   prm.wbase = wbase;
   prm.base_lo32 = base_lo32;
   prm.W = (int)cdiv(K, 64);
+  if (cdiv(N, nk ? 8 : 32) * cdiv(K, nk ? 64 : 16) >= (int64_t)INT32_MAX) {
+    set_error("matrix too large for one launch (more than 2^31 work units)");
+    return PP_ERR_INVALID;
+  }
   const size_t need = quad_plan(nk, M < 16 ? M : 16, N, K, sms).total();
   if (ws_bytes < need || (need && !ws) || !aligned(ws, 256)) {
     set_error("workspace of %zu bytes (256-byte aligned, zero-filled) required, got %zu", need, ws_bytes);
