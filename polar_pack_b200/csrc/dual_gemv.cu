@@ -277,18 +277,19 @@ PartitionPlan dual_plan(int64_t Mc, int64_t N, int64_t K, int sms) {
 }
 
 bool g_dual_attr[2][64];
+int g_dual_limit[2][64];
 
 template <int NB>
 int launch_dual(const DualParams& prm, int grid, cudaStream_t s) {
   auto kern = dual_gemv_kernel<NB>;
-  constexpr int max_smem = 227 * 1024;
+  int max_smem = 0;
+  int rc = ensure_smem_attr(kern, g_dual_attr[NB - 1], g_dual_limit[NB - 1], &max_smem);
+  if (rc) return rc;
   const size_t smem = dual_smem_bytes(NB, prm.M);
   if (smem > (size_t)max_smem) {
-    set_error("internal: shared memory plan %zu exceeds the per-CTA limit", smem);
+    set_error("shared memory plan of %zu bytes exceeds the per-CTA limit %d", smem, max_smem);
     return PP_ERR_INVALID;
   }
-  int rc = ensure_smem_attr(kern, max_smem, g_dual_attr[NB - 1]);
-  if (rc) return rc;
   kern<<<grid, dual_warps(NB) * 32, smem, s>>>(prm);
   return check_launch("dual_gemv_kernel");
 }

@@ -20,19 +20,31 @@ int check_launch(const char* what);
 int device_sm_count(int device);
 int current_device();
 
-// Kernel attribute set-up done once per device (dynamic shared memory).
+// Raises a kernel's dynamic shared memory limit to the device's opt-in
+// maximum minus the kernel's static shared memory, once per device, and
+// returns that limit in *max_dynamic.
 template <typename K>
-int ensure_smem_attr(K kernel, int bytes, bool* done_flags) {
+int ensure_smem_attr(K kernel, bool* done_flags, int* limits, int* max_dynamic) {
   const int dev = current_device();
-  if (dev < 0 || dev >= 64) return PP_ERR_CUDA;
+  if (dev < 0 || dev >= 64) {
+    set_error("no current CUDA device");
+    return PP_ERR_CUDA;
+  }
   if (!done_flags[dev]) {
-    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    int optin = 0;
+    cudaFuncAttributes fa{};
+    cudaError_t e = cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+    if (e == cudaSuccess) e = cudaFuncGetAttributes(&fa, kernel);
+    const int lim = optin - (int)fa.sharedSizeBytes;
+    if (e == cudaSuccess) e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, lim);
     if (e != cudaSuccess) {
-      set_error("cudaFuncSetAttribute(max dynamic smem %d): %s", bytes, cudaGetErrorString(e));
+      set_error("shared memory attribute set-up: %s", cudaGetErrorString(e));
       return PP_ERR_CUDA;
     }
+    limits[dev] = lim;
     done_flags[dev] = true;
   }
+  *max_dynamic = limits[dev];
   return PP_OK;
 }
 

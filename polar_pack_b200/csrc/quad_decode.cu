@@ -138,6 +138,7 @@ __global__ void quad_plug_zero_kernel(const PlugPrepParams p) {
 
 namespace {
 bool g_decode_attr[64];
+int g_decode_limit[64];
 
 int grid_for(int64_t n, int threads) {
   const int64_t b = cdiv(n, threads);
@@ -182,7 +183,8 @@ static int quad_decode_impl(const uint32_t* codes, int64_t ldc_r, int64_t ldc_c,
   prm.ldo_r = ldo_r;
   prm.ldo_c = ldo_c;
   constexpr int smem = (int)kQuadLutBytes + 4096;
-  int rc = ensure_smem_attr(quad_decode_kernel, smem, g_decode_attr);
+  int max_smem = 0;
+  int rc = ensure_smem_attr(quad_decode_kernel, g_decode_attr, g_decode_limit, &max_smem);
   if (rc) return rc;
   const int sms = device_sm_count(current_device());
   const int64_t want = cdiv(R * C, 512);

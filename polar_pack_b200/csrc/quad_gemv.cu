@@ -408,18 +408,19 @@ PartitionPlan quad_plan(bool nk, int64_t Mc, int64_t N, int64_t K, int sms) {
 }
 
 bool g_attr_done[8][64];
+int g_attr_limit[8][64];
 
 template <bool NK, int NB, int MB>
 int launch_quad(const QuadParams& prm, int grid, int idx, cudaStream_t s) {
   auto kern = quad_gemv_kernel<NK, NB, MB>;
-  constexpr int max_smem = 227 * 1024;
+  int max_smem = 0;
+  int rc = ensure_smem_attr(kern, g_attr_done[idx], g_attr_limit[idx], &max_smem);
+  if (rc) return rc;
   const size_t smem = quad_smem_bytes(NK, NB, prm.M);
   if (smem > (size_t)max_smem) {
-    set_error("internal: shared memory plan %zu exceeds the per-CTA limit", smem);
+    set_error("shared memory plan of %zu bytes exceeds the per-CTA limit %d", smem, max_smem);
     return PP_ERR_INVALID;
   }
-  int rc = ensure_smem_attr(kern, max_smem, g_attr_done[idx]);
-  if (rc) return rc;
   kern<<<grid, quad_warps(NK, NB) * 32, smem, s>>>(prm);
   return check_launch("quad_gemv_kernel");
 }
