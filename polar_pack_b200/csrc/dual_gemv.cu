@@ -74,14 +74,11 @@ struct DualOp {
   __device__ __forceinline__ int N() const { return Nv; }
 
   __device__ __forceinline__ void prefetch(int tile, int kc) const {
-    // 16 rows x 128 bytes (64 int16 codes), one row per lane 0..15
+    // 16 rows x 128 bytes (64 int16 codes): lane l touches row l & 15, half l >> 4
     const int lane = threadIdx.x & 31;
     const int k = kc * 16 + (lane & 15);
-    const int f0 = tile * 64;
-    if (lane < 16 && k < Kv && f0 < Nv) {
-      const int n = Nv - f0 < 64 ? Nv - f0 : 64;
-      prefetch_l2(p.codes + (int64_t)k * ldc + f0, (uint32_t)n * 2u);
-    }
+    const int f = tile * 64 + 32 * (lane >> 4);
+    if (k < Kv && f < Nv) prefetch_l2(p.codes + (int64_t)k * ldc + f);
   }
 
   __device__ __forceinline__ void zero() {
@@ -109,14 +106,13 @@ struct DualOp {
   }
 
   __device__ __forceinline__ uint32_t xpair(int nb, int k) const {
-    if (p.xvec && k + 1 < Kv) {
-      const uint32_t v = ldg_u32(xrow[nb] + k);
-      return xok[nb] ? v : 0u;
+    uint32_t v;
+    if (k + 1 < Kv) {
+      v = ldg_u32(xrow[nb] + k);
+    } else {
+      v = k < Kv ? (uint32_t)ldg_u16(xrow[nb] + k) : 0u;
     }
-    uint32_t lo = 0, hi = 0;
-    if (k < Kv) lo = ldg_u16(xrow[nb] + (int64_t)k * p.ldx_k);
-    if (k + 1 < Kv) hi = ldg_u16(xrow[nb] + (int64_t)(k + 1) * p.ldx_k);
-    return xok[nb] ? (lo | (hi << 16)) : 0u;
+    return xok[nb] ? v : 0u;
   }
 
   // (B1, B2) of the low and high code of word w, FP32, reference rounding
@@ -326,7 +322,8 @@ static int dual_run(const void* a, int64_t lda_m, int64_t lda_k, const int16_t* 
     set_error("a NULL tensor argument");
     return PP_ERR_INVALID;
   }
-  if (!dual_vector_ok(packed, ldp_k, ldp_n, N, gs)) {
+  const bool xcontig = lda_k == 1 && aligned(a, 4) && (lda_m * 2) % 4 == 0;
+  if (!xcontig || !dual_vector_ok(packed, ldp_k, ldp_n, N, gs)) {
     DualGenericParams g{};
     g.x = reinterpret_cast<const __half*>(a);
     g.ldx_m = lda_m;
@@ -392,7 +389,7 @@ static int dual_run(const void* a, int64_t lda_m, int64_t lda_k, const int16_t* 
     prm.out[0] = reinterpret_cast<__half*>(out1) + m0 * ldo_m;
     prm.out[1] = reinterpret_cast<__half*>(out2) + m0 * ldo_m;
     prm.M = (int)Mc;
-    prm.xvec = (lda_k == 1 && aligned(prm.x, 4) && (lda_m * 2) % 4 == 0) ? 1 : 0;
+    prm.xvec = 1;
     prm.part.units = (int)pl.units;
     prm.part.upt = (int)pl.upt;
     prm.part.counters = reinterpret_cast<int*>(ws);

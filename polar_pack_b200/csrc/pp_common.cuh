@@ -43,9 +43,10 @@ __device__ __forceinline__ uint16_t ldg_u16(const void* p) {
   return __ldg(reinterpret_cast<const unsigned short*>(p));
 }
 
-// Bulk prefetch of `bytes` (multiple of 16, 16-byte aligned) into L2.
-__device__ __forceinline__ void prefetch_l2(const void* p, uint32_t bytes) {
-  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
+// Per-thread prefetch of the cache line holding `p` into L2 (one
+// instruction for a whole warp's worth of different rows).
+__device__ __forceinline__ void prefetch_l2(const void* p) {
+  asm volatile("prefetch.global.L2::evict_last [%0];" ::"l"(p));
 }
 
 // D += A(16x16, row) * B(16x8, col), FP16 inputs, FP32 accumulate.

@@ -72,7 +72,13 @@ struct QuadOp {
   int g, c;
   uint32_t laneoff;
   int Mv, Nv, Kv, W;
-  int64_t ldc;
+  int64_t ldc, ldx_m;
+  const uint32_t* codes;
+  const __half* x;
+  const uint32_t* plug_idx;
+  const uint2* plug_vals;
+  const uint32_t* wbase;
+  uint32_t base_lo32;
   const __half* xrow[NB];  // this lane's activation row per batch tile (clamped)
   bool xok[NB];
   float acc[kT][NB][2][4];
@@ -80,12 +86,14 @@ struct QuadOp {
 
   __device__ __forceinline__ QuadOp(const QuadParams& p_)
       : p(p_), g((threadIdx.x & 31) >> 2), c(threadIdx.x & 3),
-        laneoff((threadIdx.x & 31) * 4u), Mv(p_.M), Nv(p_.N), Kv(p_.K), W(p_.W), ldc(p_.ldc) {
+        laneoff((threadIdx.x & 31) * 4u), Mv(p_.M), Nv(p_.N), Kv(p_.K), W(p_.W), ldc(p_.ldc),
+        ldx_m(p_.ldx_m), codes(p_.codes), x(p_.x), plug_idx(p_.plug_idx), plug_vals(p_.plug_vals),
+        wbase(p_.wbase), base_lo32(p_.base_lo32) {
 #pragma unroll
     for (int nb = 0; nb < NB; ++nb) {
       const int bat = nb * 8 + g;
       xok[nb] = bat < Mv;
-      xrow[nb] = p.x + (int64_t)(xok[nb] ? bat : 0) * p.ldx_m;
+      xrow[nb] = x + (int64_t)(xok[nb] ? bat : 0) * ldx_m;
     }
   }
 
@@ -111,7 +119,7 @@ struct QuadOp {
     if constexpr (NK) {
       const int64_t row = (int64_t)tile * 8 + g;
       const int kb = kc * 64 + 4 * c;
-      const uint32_t* base = p.codes + row * ldc + kb;
+      const uint32_t* base = codes + row * ldc + kb;
       const bool rok = row < Nv;
 #pragma unroll
       for (int s = 0; s < 4; ++s) {
@@ -124,7 +132,7 @@ struct QuadOp {
 #pragma unroll
       for (int r = 0; r < 4; ++r) {
         const int k = kc * 16 + 2 * c + (r & 1) + 8 * (r >> 1);
-        if (fok && k < Kv) b.q[r] = ldg_stream(p.codes + (int64_t)k * ldc + f);
+        if (fok && k < Kv) b.q[r] = ldg_stream(codes + (int64_t)k * ldc + f);
         else b.q[r] = make_uint4(0, 0, 0, 0);
       }
     }
@@ -132,49 +140,34 @@ struct QuadOp {
 
   __device__ __forceinline__ void prefetch(int tile, int kc) const {
     if constexpr (NK) {
-      // 8 rows x 256 bytes: one bulk prefetch per row, issued by lane c == 0
+      // 8 rows x 256 bytes: lane (g, c) touches row g at byte 64c
       const int64_t row = (int64_t)tile * 8 + g;
-      const int k0 = kc * 64;
-      if (c == 0 && row < Nv && k0 < Kv) {
-        const int n = Kv - k0 < 64 ? Kv - k0 : 64;
-        prefetch_l2(p.codes + row * ldc + k0, (uint32_t)n * 4u);
-      }
+      const int k = kc * 64 + 16 * c;
+      if (row < Nv && k < Kv) prefetch_l2(codes + row * ldc + k);
     } else {
-      // 16 rows x 128 bytes, one row per lane 0..15
+      // 16 rows x 128 bytes: lane l touches row l & 15, half l >> 4
       const int lane = threadIdx.x & 31;
       const int k = kc * 16 + (lane & 15);
-      const int f0 = tile * 32;
-      if (lane < 16 && k < Kv && f0 < Nv) {
-        const int n = Nv - f0 < 32 ? Nv - f0 : 32;
-        prefetch_l2(p.codes + (int64_t)k * ldc + f0, (uint32_t)n * 4u);
-      }
+      const int f = tile * 32 + 16 * (lane >> 4);
+      if (k < Kv && f < Nv) prefetch_l2(codes + (int64_t)k * ldc + f);
     }
   }
 
   __device__ __forceinline__ uint32_t xpair(int nb, int k) const {
     // activations (bat, k) and (bat, k+1) as one half2 word, zero outside
-    if (p.xvec && k + 1 < Kv) {
-      const uint32_t v = ldg_u32(xrow[nb] + k);
-      return xok[nb] ? v : 0u;
+    uint32_t v;
+    if (k + 1 < Kv) {
+      v = ldg_u32(xrow[nb] + k);
+    } else {
+      v = k < Kv ? (uint32_t)ldg_u16(xrow[nb] + k) : 0u;
     }
-    uint32_t lo = 0, hi = 0;
-    if (k < Kv) lo = ldg_u16(xrow[nb] + (int64_t)k * p.ldx_k);
-    if (k + 1 < Kv) hi = ldg_u16(xrow[nb] + (int64_t)(k + 1) * p.ldx_k);
-    return xok[nb] ? (lo | (hi << 16)) : 0u;
+    return xok[nb] ? v : 0u;
   }
 
   __device__ __forceinline__ uint2 xquad(int nb, int k) const {
     // activations (bat, k..k+3); the NK path guarantees K % 4 == 0
-    uint2 v;
-    if (p.xvec) {
-      v = ldg_u2(xrow[nb] + (k < Kv ? k : 0));
-    } else {
-      uint32_t h[4];
-#pragma unroll
-      for (int i = 0; i < 4; ++i) h[i] = k < Kv ? ldg_u16(xrow[nb] + (int64_t)(k + i) * p.ldx_k) : 0u;
-      v = make_uint2(h[0] | (h[1] << 16), h[2] | (h[3] << 16));
-    }
     const bool ok = xok[nb] && k < Kv;
+    const uint2 v = ldg_u2(xrow[nb] + (ok ? k : 0));
     return make_uint2(ok ? v.x : 0u, ok ? v.y : 0u);
   }
 
@@ -183,11 +176,11 @@ struct QuadOp {
     if constexpr (kPlug) {
       if (row >= Nv) return;
       const int64_t wi = row * W + kc;
-      const uint32_t j0 = __ldg(p.wbase + wi), j1 = __ldg(p.wbase + wi + 1);
-      const uint32_t rowbase = p.base_lo32 + (uint32_t)row * (uint32_t)Kv;
+      const uint32_t j0 = __ldg(wbase + wi), j1 = __ldg(wbase + wi + 1);
+      const uint32_t rowbase = base_lo32 + (uint32_t)row * (uint32_t)Kv;
       for (uint32_t j = j0 + c; j < j1; j += 4) {
-        const uint32_t k = __ldg(p.plug_idx + j) - rowbase;
-        const uint2 v = __ldg(p.plug_vals + j);
+        const uint32_t k = __ldg(plug_idx + j) - rowbase;
+        const uint2 v = __ldg(plug_vals + j);
         const float pv[4] = {__half2float(__ushort_as_half((uint16_t)(v.x & 0xFFFF))),
                              __half2float(__ushort_as_half((uint16_t)(v.x >> 16))),
                              __half2float(__ushort_as_half((uint16_t)(v.y & 0xFFFF))),
@@ -195,8 +188,7 @@ struct QuadOp {
 #pragma unroll
         for (int m = 0; m < kMB; ++m) {
           if (m < Mv) {
-            const float xv = __half2float(__ushort_as_half(
-                ldg_u16(p.x + (int64_t)m * p.ldx_m + (int64_t)k * p.ldx_k)));
+            const float xv = __half2float(__ushort_as_half(ldg_u16(x + (int64_t)m * ldx_m + k)));
 #pragma unroll
             for (int q = 0; q < 4; ++q) corr[m][q] = fmaf(pv[q], xv, corr[m][q]);
           }
@@ -509,10 +501,13 @@ static int quad_run(const void* a, int64_t lda_m, int64_t lda_k, const uint32_t*
     return PP_ERR_INVALID;
   }
   const bool nk = file_layout || (ldc_k == 1 && ldc_n != 1);
-  const bool vec = quad_vector_ok(nk, codes, ldc_k, ldc_n, N, K);
+  // activation rows must be contiguous and aligned for the vector loads
+  const bool xcontig = lda_k == 1 && aligned(a, nk ? 8 : 4) && (lda_m * 2) % (nk ? 8 : 4) == 0;
+  const bool vec = xcontig && quad_vector_ok(nk, codes, ldc_k, ldc_n, N, K);
   if (!vec) {
     if (plug) {
-      set_error("file-layout codes need 16-byte alignment, K %% 4 == 0 and row stride %% 4 == 0");
+      set_error("file-layout Linear needs 16-byte aligned codes, K %% 4 == 0, row stride %% 4 == 0 and "
+                "contiguous 8-byte aligned activation rows");
       return PP_ERR_INVALID;
     }
     QuadGenericParams g{};
@@ -580,8 +575,7 @@ static int quad_run(const void* a, int64_t lda_m, int64_t lda_k, const uint32_t*
     prm.x = reinterpret_cast<const __half*>(a) + m0 * lda_m;
     for (int i = 0; i < 4; ++i) prm.out[i] = reinterpret_cast<__half*>(out[i]) + m0 * ldo_m;
     prm.M = (int)Mc;
-    const int xalign = nk ? 8 : 4;
-    prm.xvec = (lda_k == 1 && aligned(prm.x, xalign) && (lda_m * 2) % xalign == 0) ? 1 : 0;
+    prm.xvec = 1;
     if ((rc = launch_plan(pl, nk, Mc, prm, ws, plug, s))) return rc;
   }
   return PP_OK;

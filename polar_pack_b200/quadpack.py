@@ -216,6 +216,8 @@ def quad_linear(x: torch.Tensor, layer: QuadLinearSlice, out=None) -> list[torch
     if x.dtype != torch.float16:
         raise ValueError("x must be fp16")
     dev = _lib.require_cuda(x, layer.codes)
+    if x.stride(1) != 1 or x.data_ptr() % 8 or (x.stride(0) * 2) % 8:
+        x = x.contiguous() if x.stride(1) != 1 else x.clone()  # the kernel reads 8-byte activation groups
     M = x.shape[0]
     if out is None:
         out = [torch.empty((M, layer.N), dtype=torch.float16, device=dev) for _ in range(4)]
