@@ -75,7 +75,7 @@ __device__ __forceinline__ uint32_t lut_off(int table) {
 // 1024 source words are first gathered into `stage` (4 KiB of shared memory,
 // all global loads in flight at once), then fanned out to 32 lane copies.
 // Called by every thread of the CTA; caller syncs afterwards.
-__device__ __forceinline__ void build_quad_lut(uint8_t* smem, uint32_t* stage, const __half* const* luts) {
+__device__ __forceinline__ void build_quad_lut(uint8_t* lut, uint32_t* stage, const __half* const* luts) {
   for (int i = threadIdx.x; i < 1024; i += blockDim.x) {
     const int t = i >> 8, e = i & 255;
     const uint16_t* a = reinterpret_cast<const uint16_t*>(luts[t == 0 ? 0 : 2 * t - 1]);
@@ -86,7 +86,7 @@ __device__ __forceinline__ void build_quad_lut(uint8_t* smem, uint32_t* stage, c
   for (int idx = threadIdx.x; idx < 4 * 256 * 8; idx += blockDim.x) {
     const int t = idx >> 11, e = (idx >> 3) & 255, part = idx & 7;
     const uint32_t v = stage[idx >> 3];
-    *reinterpret_cast<uint4*>(smem + lut_off(t) + (uint32_t)e * 256u + (uint32_t)part * 16u) =
+    *reinterpret_cast<uint4*>(lut + lut_off(t) + (uint32_t)e * 256u + (uint32_t)part * 16u) =
         make_uint4(v, v, v, v);
   }
 }
@@ -99,15 +99,44 @@ struct QuadDec {
   uint32_t p1, p2, p3;
 };
 
-__device__ __forceinline__ QuadDec decode_quad(uint32_t code, uint32_t laneoff) {
-  const uint32_t o0 = __byte_perm(code, laneoff, 0x7634);  // norm index (byte 3)
-  const uint32_t o1 = __byte_perm(code, laneoff, 0x7624);  // t1 index   (byte 2)
-  const uint32_t o2 = __byte_perm(code, laneoff, 0x7614);  // t2 index   (byte 1)
-  const uint32_t o3 = __byte_perm(code, laneoff, 0x7604);  // t3 index   (byte 0)
-  const uint32_t rr = *reinterpret_cast<const uint32_t*>(pp_smem + o0);
-  const uint32_t cs1 = *reinterpret_cast<const uint32_t*>(pp_smem + 128u + o1);
-  const uint32_t cs2 = *reinterpret_cast<const uint32_t*>(pp_smem + 65536u + o2);
-  const uint32_t cs3 = *reinterpret_cast<const uint32_t*>(pp_smem + 65536u + 128u + o3);
+// Shared-memory placement of the quad tables.  DIRECT: the first 64 KiB
+// boundary at or after the dynamic shared memory base.  With the tables
+// there, __byte_perm(code, lanebase, 0x76b4) -- code byte b in bits 8..15,
+// the lane offset in bits 0..7, the 64 KiB-aligned table address in bits
+// 16..31 -- is the complete shared address of a gather, and the table
+// offsets (+128, +65536, +65664) are load immediates: no add per gather.
+// Otherwise the tables start at the base and each gather adds it.
+// The host requests kQuadLutBytes (+ 65536 of alignment slack if DIRECT)
+// plus the partial-slot bytes, which follow the tables.
+template <bool DIRECT>
+__device__ __forceinline__ uint32_t quad_lut_saddr() {
+  const uint32_t base = (uint32_t)__cvta_generic_to_shared(pp_smem);
+  return DIRECT ? ((base + 0xFFFFu) & ~0xFFFFu) : base;
+}
+
+__device__ __forceinline__ uint8_t* quad_lut_ptr(uint32_t lut_saddr) {
+  return pp_smem + (lut_saddr - (uint32_t)__cvta_generic_to_shared(pp_smem));
+}
+
+template <int OFF>
+__device__ __forceinline__ uint32_t lds_off(uint32_t saddr) {
+  uint32_t v;
+  asm("ld.shared.b32 %0, [%1+%2];" : "=r"(v) : "r"(saddr), "n"(OFF));
+  return v;
+}
+
+// DIRECT: lanebase = lut_saddr | (4 * lane), lut_add = 0.
+// Otherwise lanebase = 4 * lane and lut_add = lut_saddr.
+template <bool DIRECT>
+__device__ __forceinline__ QuadDec decode_quad(uint32_t code, uint32_t lanebase, uint32_t lut_add) {
+  const uint32_t a0 = __byte_perm(code, lanebase, 0x7634) + (DIRECT ? 0u : lut_add);  // norm (byte 3)
+  const uint32_t a1 = __byte_perm(code, lanebase, 0x7624) + (DIRECT ? 0u : lut_add);  // t1   (byte 2)
+  const uint32_t a2 = __byte_perm(code, lanebase, 0x7614) + (DIRECT ? 0u : lut_add);  // t2   (byte 1)
+  const uint32_t a3 = __byte_perm(code, lanebase, 0x7604) + (DIRECT ? 0u : lut_add);  // t3   (byte 0)
+  const uint32_t rr = lds_off<0>(a0);
+  const uint32_t cs1 = lds_off<128>(a1);
+  const uint32_t cs2 = lds_off<65536>(a2);
+  const uint32_t cs3 = lds_off<65536 + 128>(a3);
   const __half2 p1 = __hmul2_rn(u2h(rr), u2h(cs1));                // (r*c1, r*s1)
   const __half2 p2 = __hmul2_rn(__high2half2(p1), u2h(cs2));       // (rs*c2, rs*s2)
   const __half2 p3 = __hmul2_rn(__high2half2(p2), u2h(cs3));       // (rss*c3, rss*s3)

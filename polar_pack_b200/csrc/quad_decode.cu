@@ -25,15 +25,17 @@ struct QuadDecodeParams {
 };
 
 __global__ void __launch_bounds__(512, 1) quad_decode_kernel(const QuadDecodeParams p) {
-  build_quad_lut(pp_smem, reinterpret_cast<uint32_t*>(pp_smem + kQuadLutBytes), p.luts);
+  const uint32_t lut_saddr = quad_lut_saddr<true>();
+  uint8_t* lut = quad_lut_ptr(lut_saddr);
+  build_quad_lut(lut, reinterpret_cast<uint32_t*>(lut + kQuadLutBytes), p.luts);
   __syncthreads();
-  const uint32_t laneoff = (threadIdx.x & 31) * 4u;
+  const uint32_t lanebase = lut_saddr | ((threadIdx.x & 31) * 4u);
   const int64_t total = p.R * p.C;
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
        i += (int64_t)gridDim.x * blockDim.x) {
     const int64_t r = i / p.C, c = i - r * p.C;
     const uint32_t code = __ldg(p.codes + r * p.ldc_r + c * p.ldc_c);
-    const QuadDec d = decode_quad(code, laneoff);
+    const QuadDec d = decode_quad<true>(code, lanebase, 0u);
     __half w[4] = {__low2half(u2h(d.p1)), __low2half(u2h(d.p2)), __low2half(u2h(d.p3)),
                    __high2half(u2h(d.p3))};
     const int64_t o = r * p.ldo_r + c * p.ldo_c;
@@ -182,7 +184,7 @@ static int quad_decode_impl(const uint32_t* codes, int64_t ldc_r, int64_t ldc_c,
   prm.scaled = scales ? 1 : 0;
   prm.ldo_r = ldo_r;
   prm.ldo_c = ldo_c;
-  constexpr int smem = (int)kQuadLutBytes + 4096;
+  constexpr int smem = (int)kQuadLutBytes + 65536 + 4096;
   int max_smem = 0;
   int rc = ensure_smem_attr(quad_decode_kernel, g_decode_attr, g_decode_limit, &max_smem);
   if (rc) return rc;

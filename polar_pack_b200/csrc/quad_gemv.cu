@@ -56,8 +56,9 @@ struct QuadBuf {
 };
 
 // NK: file layout.  MB > 0 selects the plug-correcting variant for up to MB
-// batch rows (MB in {1, 8, 16}); MB == 0 has no plug table.
-template <bool NK, int NB, int MB>
+// batch rows (MB in {1, 8, 16}); MB == 0 has no plug table.  DIRECT: tables
+// at a 64 KiB-aligned shared address (see quad_lut_saddr).
+template <bool NK, int NB, int MB, bool DIRECT>
 struct QuadOp {
   static constexpr int kWarps = quad_warps(NK, NB);
   static constexpr int kTileW = NK ? 8 : 32;  // output features per tile
@@ -70,7 +71,7 @@ struct QuadOp {
 
   const QuadParams& p;
   int g, c;
-  uint32_t laneoff;
+  uint32_t lanebase, lut_add;
   int Mv, Nv, Kv, W;
   int64_t ldc, ldx_m;
   const uint32_t* codes;
@@ -84,9 +85,9 @@ struct QuadOp {
   float acc[kT][NB][2][4];
   float corr[kMB][4];
 
-  __device__ __forceinline__ QuadOp(const QuadParams& p_)
+  __device__ __forceinline__ QuadOp(const QuadParams& p_, uint32_t lut_saddr)
       : p(p_), g((threadIdx.x & 31) >> 2), c(threadIdx.x & 3),
-        laneoff((threadIdx.x & 31) * 4u), Mv(p_.M), Nv(p_.N), Kv(p_.K), W(p_.W), ldc(p_.ldc),
+        lanebase((DIRECT ? lut_saddr : 0u) | ((threadIdx.x & 31) * 4u)), lut_add(DIRECT ? 0u : lut_saddr), Mv(p_.M), Nv(p_.N), Kv(p_.K), W(p_.W), ldc(p_.ldc),
         ldx_m(p_.ldx_m), codes(p_.codes), x(p_.x), plug_idx(p_.plug_idx), plug_vals(p_.plug_vals),
         wbase(p_.wbase), base_lo32(p_.base_lo32) {
 #pragma unroll
@@ -115,25 +116,30 @@ struct QuadOp {
       for (int q = 0; q < 4; ++q) corr[m][q] = 0.f;
   }
 
+  // Out-of-range rows / columns read a clamped in-range address instead:
+  // rows beyond N are never stored, and columns beyond K get zero weights
+  // in compute(), so no load is predicated in the steady state.
   __device__ __forceinline__ void load(Buf& b, int tile, int kc) const {
     if constexpr (NK) {
-      const int64_t row = (int64_t)tile * 8 + g;
+      int row = tile * 8 + g;
+      row = row < Nv ? row : Nv - 1;
       const int kb = kc * 64 + 4 * c;
-      const uint32_t* base = codes + row * ldc + kb;
-      const bool rok = row < Nv;
+      const uint32_t* base = codes + (int64_t)row * ldc;
+      if (kb + 48 < Kv) {
 #pragma unroll
-      for (int s = 0; s < 4; ++s) {
-        if (rok && kb + 16 * s < Kv) b.q[s] = ldg_stream(base + 16 * s);
-        else b.q[s] = make_uint4(0, 0, 0, 0);
+        for (int s = 0; s < 4; ++s) b.q[s] = ldg_stream(base + kb + 16 * s);
+      } else {
+#pragma unroll
+        for (int s = 0; s < 4; ++s) b.q[s] = ldg_stream(base + (kb + 16 * s < Kv ? kb + 16 * s : 0));
       }
     } else {
-      const int f = tile * 32 + 4 * g;
-      const bool fok = f < Nv;
+      int f = tile * 32 + 4 * g;
+      f = f < Nv ? f : Nv - 4;
 #pragma unroll
       for (int r = 0; r < 4; ++r) {
-        const int k = kc * 16 + 2 * c + (r & 1) + 8 * (r >> 1);
-        if (fok && k < Kv) b.q[r] = ldg_stream(codes + (int64_t)k * ldc + f);
-        else b.q[r] = make_uint4(0, 0, 0, 0);
+        int k = kc * 16 + 2 * c + (r & 1) + 8 * (r >> 1);
+        k = k < Kv ? k : 0;
+        b.q[r] = ldg_stream(codes + (int64_t)k * ldc + f);
       }
     }
   }
@@ -153,22 +159,17 @@ struct QuadOp {
     }
   }
 
+  // Activation fragments.  Batch columns >= M read row 0 (clamped): their
+  // mma output column is never stored.  Columns k >= K read as zero.
   __device__ __forceinline__ uint32_t xpair(int nb, int k) const {
-    // activations (bat, k) and (bat, k+1) as one half2 word, zero outside
-    uint32_t v;
-    if (k + 1 < Kv) {
-      v = ldg_u32(xrow[nb] + k);
-    } else {
-      v = k < Kv ? (uint32_t)ldg_u16(xrow[nb] + k) : 0u;
-    }
-    return xok[nb] ? v : 0u;
+    if (k + 1 < Kv) return ldg_u32(xrow[nb] + k);
+    return k < Kv ? (uint32_t)ldg_u16(xrow[nb] + k) : 0u;
   }
 
   __device__ __forceinline__ uint2 xquad(int nb, int k) const {
     // activations (bat, k..k+3); the NK path guarantees K % 4 == 0
-    const bool ok = xok[nb] && k < Kv;
-    const uint2 v = ldg_u2(xrow[nb] + (ok ? k : 0));
-    return make_uint2(ok ? v.x : 0u, ok ? v.y : 0u);
+    if (k < Kv) return ldg_u2(xrow[nb] + k);
+    return make_uint2(0u, 0u);
   }
 
   // Plug entries of (row, window kc): lanes of the row take every 4th entry.
@@ -205,10 +206,10 @@ struct QuadOp {
       for (int s = 0; s < 4; ++s) {
         const int kp = kbase + 16 * s + 4 * c;
         QuadDec d[4];
-        d[0] = decode_quad(b.q[s].x, laneoff);
-        d[1] = decode_quad(b.q[s].y, laneoff);
-        d[2] = decode_quad(b.q[s].z, laneoff);
-        d[3] = decode_quad(b.q[s].w, laneoff);
+        d[0] = decode_quad<DIRECT>(b.q[s].x, lanebase, lut_add);
+        d[1] = decode_quad<DIRECT>(b.q[s].y, lanebase, lut_add);
+        d[2] = decode_quad<DIRECT>(b.q[s].z, lanebase, lut_add);
+        d[3] = decode_quad<DIRECT>(b.q[s].w, lanebase, lut_add);
         uint32_t a01[4] = {lo_pair(d[0].p1, d[1].p1), lo_pair(d[0].p2, d[1].p2),
                            lo_pair(d[2].p1, d[3].p1), lo_pair(d[2].p2, d[3].p2)};
         uint32_t a23[4] = {lo_pair(d[0].p3, d[1].p3), hi_pair(d[0].p3, d[1].p3),
@@ -243,7 +244,7 @@ struct QuadOp {
 #pragma unroll
         for (int r = 0; r < 4; ++r) {
           const uint32_t code = t == 0 ? b.q[r].x : t == 1 ? b.q[r].y : t == 2 ? b.q[r].z : b.q[r].w;
-          d[r] = decode_quad(code, laneoff);
+          d[r] = decode_quad<DIRECT>(code, lanebase, lut_add);
           if (!rv[r]) d[r] = QuadDec{0u, 0u, 0u};
         }
         const uint32_t a01[4] = {lo_pair(d[0].p1, d[1].p1), lo_pair(d[0].p2, d[1].p2),
@@ -326,19 +327,26 @@ struct QuadOp {
   }
 };
 
-// LUT + the warps' partial slots (at least the 4 KiB the table build stages in)
-inline size_t quad_smem_bytes(bool nk, int nb, int64_t M) {
+// Partial slots (at least the 4 KiB the table build stages in).
+inline size_t quad_red_bytes(bool nk, int nb, int64_t M) {
   const size_t r = red_bytes(quad_warps(nk, nb), 4, M, nk ? 8 : 32);
-  return kQuadLutBytes + (r > 4096 ? r : 4096);
+  return r > 4096 ? r : 4096;
 }
 
-template <bool NK, int NB, int MB>
+// Tables, alignment slack when DIRECT, then the partial slots.
+inline size_t quad_smem_bytes(bool nk, int nb, int64_t M, bool direct) {
+  return kQuadLutBytes + (direct ? 65536u : 0u) + quad_red_bytes(nk, nb, M);
+}
+
+template <bool NK, int NB, int MB, bool DIRECT>
 __global__ void __launch_bounds__(quad_warps(NK, NB) * 32, 1) quad_gemv_kernel(const QuadParams p) {
   __shared__ int s_flag;
-  float* red = reinterpret_cast<float*>(pp_smem + kQuadLutBytes);
-  build_quad_lut(pp_smem, reinterpret_cast<uint32_t*>(red), p.luts);
+  const uint32_t lut_saddr = quad_lut_saddr<DIRECT>();
+  uint8_t* lut = quad_lut_ptr(lut_saddr);
+  float* red = reinterpret_cast<float*>(lut + kQuadLutBytes);
+  build_quad_lut(lut, reinterpret_cast<uint32_t*>(red), p.luts);
   __syncthreads();
-  QuadOp<NK, NB, MB> op(p);
+  QuadOp<NK, NB, MB, DIRECT> op(p, lut_saddr);
   run_partition(op, p.part, red, &s_flag);
 }
 
@@ -399,22 +407,30 @@ PartitionPlan quad_plan(bool nk, int64_t Mc, int64_t N, int64_t K, int sms) {
   return plan_partition(cdiv(N, tile_w), cdiv(K, unit_k), quad_warps(nk, nb), sms, 4, Mc, tile_w);
 }
 
-bool g_attr_done[8][64];
-int g_attr_limit[8][64];
+bool g_attr_done[16][64];
+int g_attr_limit[16][64];
 
-template <bool NK, int NB, int MB>
-int launch_quad(const QuadParams& prm, int grid, int idx, cudaStream_t s) {
-  auto kern = quad_gemv_kernel<NK, NB, MB>;
+template <bool NK, int NB, int MB, bool DIRECT>
+int launch_quad_v(const QuadParams& prm, int grid, int idx, cudaStream_t s) {
+  auto kern = quad_gemv_kernel<NK, NB, MB, DIRECT>;
   int max_smem = 0;
   int rc = ensure_smem_attr(kern, g_attr_done[idx], g_attr_limit[idx], &max_smem);
   if (rc) return rc;
-  const size_t smem = quad_smem_bytes(NK, NB, prm.M);
+  const size_t smem = quad_smem_bytes(NK, NB, prm.M, DIRECT);
   if (smem > (size_t)max_smem) {
     set_error("shared memory plan of %zu bytes exceeds the per-CTA limit %d", smem, max_smem);
     return PP_ERR_INVALID;
   }
   kern<<<grid, quad_warps(NK, NB) * 32, smem, s>>>(prm);
   return check_launch("quad_gemv_kernel");
+}
+
+// Direct table addressing whenever the 64 KiB alignment slack fits.
+template <bool NK, int NB, int MB>
+int launch_quad(const QuadParams& prm, int grid, int idx, cudaStream_t s) {
+  if (quad_smem_bytes(NK, NB, prm.M, true) <= 227u * 1024u - 1024u)
+    return launch_quad_v<NK, NB, MB, true>(prm, grid, 2 * idx, s);
+  return launch_quad_v<NK, NB, MB, false>(prm, grid, 2 * idx + 1, s);
 }
 
 int launch_plan(const PartitionPlan& pl, bool nk, int64_t Mc, QuadParams prm, void* ws, bool plug,
