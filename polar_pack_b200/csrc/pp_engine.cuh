@@ -51,6 +51,81 @@ __device__ __forceinline__ int part_of_unit(int x, int U, int G) {
   return c < G - 1 ? c : G - 1;
 }
 
+// The reduction of a CTA's tiles after its warps finished their ranges
+// (shared by both engines): warp partials in warp order, then the
+// cross-CTA protocol for the (at most two) tiles cut by a CTA boundary.
+template <class Op>
+__device__ __forceinline__ void reduce_partials(Op& op, const Partition& pt, const float* red, int* s_flag,
+                                                int cu0, int cu1, int nval) {
+  constexpr int NW = Op::kWarps;
+  constexpr int TW = Op::kTileW;
+  const int tid = threadIdx.x;
+  const int U = pt.units, G = gridDim.x, upt = pt.upt, M = op.M();
+  const int R = cu1 - cu0;
+  const int ct0 = cu0 / upt, ct1 = (cu1 - 1) / upt;
+  int pend[2];
+  int npend = 0;
+  for (int tt = ct0; tt <= ct1; ++tt) {
+    const int a = tt * upt, b = a + upt;  // unit range of the tile
+    const int w_first = part_of_unit((a > cu0 ? a : cu0) - cu0, R, NW);
+    const int w_last = part_of_unit((b < cu1 ? b : cu1) - 1 - cu0, R, NW);
+    const bool one_warp = w_first == w_last && a >= cu0 + range_start(R, NW, w_first) &&
+                          b <= cu0 + range_start(R, NW, w_first + 1);
+    const bool cta_whole = a >= cu0 && b <= cu1;
+    if (one_warp && cta_whole) continue;  // stored by its warp
+    float* slot = pt.slots + ((int64_t)blockIdx.x * 2 + (tt == ct0 ? 0 : 1)) * (int64_t)nval;
+    for (int e = tid; e < nval; e += NW * 32) {
+      float s = 0.f;
+      for (int w = w_first; w <= w_last; ++w) {
+        const int ws0 = cu0 + range_start(R, NW, w);
+        if (ws0 == cu0 + range_start(R, NW, w + 1)) continue;  // empty range (fewer units than warps)
+        const int which = (ws0 >= a) ? 0 : 1;  // the tile is w's first tile iff w starts in it
+        s += red[(w * 2 + which) * nval + e];
+      }
+      if (cta_whole) {
+        const int o = e / (M * TW);
+        const int rem = e - o * M * TW;
+        const int bat = rem / TW;
+        const int f = tt * TW + (rem - bat * TW);
+        if (f < op.N()) op.store(o, bat, f, s);
+      } else {
+        __stcg(slot + e, s);
+      }
+    }
+    if (!cta_whole && npend < 2) pend[npend++] = tt;
+  }
+  for (int i = 0; i < npend; ++i) {
+    const int tt = pend[i];
+    const int c_first = part_of_unit(tt * upt, U, G);
+    const int c_last = part_of_unit(tt * upt + upt - 1, U, G);
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) {
+      const int old = atomicAdd(pt.counters + c_last, 1);
+      *s_flag = (old == c_last - c_first) ? 1 : 0;
+    }
+    __syncthreads();
+    if (*s_flag) {
+      __threadfence();
+      for (int e = tid; e < nval; e += NW * 32) {
+        float s = 0.f;
+        for (int c = c_first; c <= c_last; ++c) {
+          // only the first contributor can have started before the tile
+          const int w = (c == c_first && range_start(U, G, c) < tt * upt) ? 1 : 0;
+          s += __ldcg(pt.slots + ((int64_t)c * 2 + w) * (int64_t)nval + e);
+        }
+        const int o = e / (M * TW);
+        const int rem = e - o * M * TW;
+        const int bat = rem / TW;
+        const int f = tt * TW + (rem - bat * TW);
+        if (f < op.N()) op.store(o, bat, f, s);
+      }
+      if (tid == 0) pt.counters[c_last] = 0;
+    }
+    __syncthreads();
+  }
+}
+
 // Op interface (device struct):
 //   static constexpr int kWarps, kTileW, kNOut, kNBat
 //   using Buf = ...;
@@ -121,72 +196,80 @@ __device__ __forceinline__ void run_partition(Op& op, const Partition& pt, float
     }
   }
   __syncthreads();
+  reduce_partials(op, pt, red, s_flag, cu0, cu1, nval);
+}
 
-  // tiles cut by a warp boundary: sum the warps' partials in warp order
-  const int ct0 = cu0 / upt, ct1 = (cu1 - 1) / upt;
-  int pend[2];
-  int npend = 0;
-  for (int tt = ct0; tt <= ct1; ++tt) {
-    const int a = tt * upt, b = a + upt;  // unit range of the tile
-    const int w_first = part_of_unit((a > cu0 ? a : cu0) - cu0, R, NW);
-    const int w_last = part_of_unit((b < cu1 ? b : cu1) - 1 - cu0, R, NW);
-    const bool one_warp = w_first == w_last && a >= cu0 + range_start(R, NW, w_first) &&
-                          b <= cu0 + range_start(R, NW, w_first + 1);
-    const bool cta_whole = a >= cu0 && b <= cu1;
-    if (one_warp && cta_whole) continue;  // stored by its warp
-    float* slot = pt.slots + ((int64_t)blockIdx.x * 2 + (tt == ct0 ? 0 : 1)) * (int64_t)nval;
-    for (int e = tid; e < nval; e += NW * 32) {
-      float s = 0.f;
-      for (int w = w_first; w <= w_last; ++w) {
-        const int ws0 = cu0 + range_start(R, NW, w);
-        if (ws0 == cu0 + range_start(R, NW, w + 1)) continue;  // empty range (fewer units than warps)
-        const int which = (ws0 >= a) ? 0 : 1;  // the tile is w's first tile iff w starts in it
-        s += red[(w * 2 + which) * nval + e];
-      }
-      if (cta_whole) {
-        const int o = e / (M * TW);
-        const int rem = e - o * M * TW;
-        const int bat = rem / TW;
-        const int f = tt * TW + (rem - bat * TW);
-        if (f < op.N()) op.store(o, bat, f, s);
-      } else {
-        __stcg(slot + e, s);
-      }
-    }
-    if (!cta_whole && npend < 2) pend[npend++] = tt;
-  }
+// TMA engine: same partition and reduction, but each warp streams its range
+// through a private ring of S shared-memory slots filled by TMA.  Lane 0
+// keeps the next S units of the warp's range in flight (one mbarrier per
+// slot, phase = fill count & 1); all lanes wait for the slot, copy the unit
+// into registers, sync, and lane 0 refills the slot with the unit S ahead
+// before the unit is decoded.  Waits are bounded (mbar_wait_bounded).
+//
+// Op additions: kUnitBytes; void issue(uint32_t slot, uint32_t bar, int tile,
+// int kc) const (lane 0 only); void read(Buf&, uint32_t slot) const.
+template <class Op>
+__device__ __forceinline__ void run_partition_tma(Op& op, const Partition& pt, float* red, int* s_flag,
+                                                  uint32_t ring, uint32_t bars, int S, int* status) {
+  constexpr int NW = Op::kWarps;
+  const int tid = threadIdx.x;
+  const int warp = tid >> 5, lane = tid & 31;
+  const int U = pt.units;
+  const int G = gridDim.x;
+  const int cu0 = range_start(U, G, blockIdx.x), cu1 = range_start(U, G, blockIdx.x + 1);
+  if (cu0 >= cu1) return;  // uniform over the CTA
+  const int upt = pt.upt;
+  const int M = op.M();
+  const int nval = Op::kNOut * M * Op::kTileW;
+  const int R = cu1 - cu0;
+  const int wu0 = cu0 + range_start(R, NW, warp), wu1 = cu0 + range_start(R, NW, warp + 1);
+  const uint32_t my_ring = ring + (uint32_t)(warp * S * Op::kUnitBytes);
+  const uint32_t my_bar = bars + (uint32_t)(warp * S * 8);
 
-  // tiles cut by a CTA boundary: last arrival reduces in CTA order
-  for (int i = 0; i < npend; ++i) {
-    const int tt = pend[i];
-    const int c_first = part_of_unit(tt * upt, U, G);
-    const int c_last = part_of_unit(tt * upt + upt - 1, U, G);
-    __threadfence();
-    __syncthreads();
-    if (tid == 0) {
-      const int old = atomicAdd(pt.counters + c_last, 1);
-      *s_flag = (old == c_last - c_first) ? 1 : 0;
+  if (wu0 < wu1) {
+    if (lane == 0) {
+      for (int i = 0; i < S; ++i) mbar_init(my_bar + 8u * i, 1);
+      fence_mbar_init();
     }
-    __syncthreads();
-    if (*s_flag) {
-      __threadfence();
-      for (int e = tid; e < nval; e += NW * 32) {
-        float s = 0.f;
-        for (int c = c_first; c <= c_last; ++c) {
-          // only the first contributor can have started before the tile
-          const int w = (c == c_first && range_start(U, G, c) < tt * upt) ? 1 : 0;
-          s += __ldcg(pt.slots + ((int64_t)c * 2 + w) * (int64_t)nval + e);
+    __syncwarp();
+    int t = wu0 / upt, kc = wu0 - t * upt;  // current unit
+    const int t_first = t;
+    int it = t, ikc = kc;                   // next unit to issue
+    for (int i = 0; i < S && wu0 + i < wu1; ++i) {
+      if (lane == 0) op.issue(my_ring + (uint32_t)(i * Op::kUnitBytes), my_bar + 8u * i, it, ikc);
+      if (++ikc == upt) { ikc = 0; ++it; }
+    }
+    int slot = 0;
+    uint32_t parity = 0;
+    op.zero();
+    typename Op::Buf buf;
+    for (int u = wu0; u < wu1; ++u) {
+      const uint32_t sl = my_ring + (uint32_t)(slot * Op::kUnitBytes);
+      mbar_wait_bounded(my_bar + 8u * slot, parity, status);
+      op.read(buf, sl);
+      __syncwarp();
+      if (u + S < wu1) {
+        if (lane == 0) op.issue(sl, my_bar + 8u * slot, it, ikc);
+        if (++ikc == upt) { ikc = 0; ++it; }
+      }
+      if (++slot == S) { slot = 0; parity ^= 1u; }
+      op.compute(buf, t, kc);
+      int nt = t, nkc = kc + 1;
+      if (nkc == upt) { nkc = 0; ++nt; }
+      if (nkc == 0 || u + 1 == wu1) {
+        if ((t * upt >= wu0) && nkc == 0) {
+          op.store_tile(t);
+        } else {
+          op.write_partial(red + (warp * 2 + (t == t_first ? 0 : 1)) * nval, M);
         }
-        const int o = e / (M * TW);
-        const int rem = e - o * M * TW;
-        const int bat = rem / TW;
-        const int f = tt * TW + (rem - bat * TW);
-        if (f < op.N()) op.store(o, bat, f, s);
+        op.zero();
       }
-      if (tid == 0) pt.counters[c_last] = 0;
+      t = nt;
+      kc = nkc;
     }
-    __syncthreads();
   }
+  __syncthreads();
+  reduce_partials(op, pt, red, s_flag, cu0, cu1, nval);
 }
 
 // Host-side partition sizing shared by the launchers.

@@ -1,6 +1,7 @@
 // Host-side helpers shared by the C-ABI translation units.
 #pragma once
 
+#include <cuda.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -19,6 +20,12 @@ int check_launch(const char* what);
 
 int device_sm_count(int device);
 int current_device();
+
+// 2D tensor map over a row-major uint32 matrix (dim0 contiguous), box
+// box0 x box1, 128-byte swizzle, zero fill out of bounds.  Requires a
+// 16-byte aligned base, stride1_bytes % 16 == 0 and box0 * 4 <= 128.
+int encode_tmap_u32_2d(CUtensorMap* map, const void* base, uint64_t dim0, uint64_t dim1, uint64_t stride1_bytes,
+                       uint32_t box0, uint32_t box1);
 
 // Raises a kernel's dynamic shared memory limit to the device's opt-in
 // maximum minus the kernel's static shared memory, once per device, and

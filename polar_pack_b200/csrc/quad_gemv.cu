@@ -25,12 +25,14 @@ namespace pp {
 
 int zero_f16(void* p, int64_t R, int64_t C, int64_t ldr, int64_t ldc, cudaStream_t s);
 
-// Warps per CTA: the KN tile keeps 4x more accumulators per lane and two
-// batch tiles double them again, so those variants trade warps for
-// registers (NB = number of 8-row batch tiles).
-__host__ __device__ constexpr int quad_warps(bool nk, int nb) { return nk ? (nb == 1 ? 16 : 8) : (nb == 1 ? 12 : 6); }
+// Warps per CTA.  Shared memory holds the 128 KiB tables, each warp's TMA
+// ring (2 KiB per slot) and two partial slots per warp; the KN tile keeps
+// 4x more accumulators and partials per warp, and two batch tiles double
+// them again, so those variants use fewer warps (NB = 8-row batch tiles).
+__host__ __device__ constexpr int quad_warps(bool nk, int nb) { return nk ? (nb == 1 ? 12 : 8) : (nb == 1 ? 8 : 4); }
 
 struct QuadParams {
+  CUtensorMap tmap;  // 2D map over the codes, 128-byte swizzle (first: 64-byte aligned)
   const __half* x;
   int64_t ldx_m, ldx_k;
   const uint32_t* codes;
@@ -49,6 +51,7 @@ struct QuadParams {
   int W;
   Partition part;
   int xvec;
+  int stages;  // TMA ring slots per warp
 };
 
 struct QuadBuf {
@@ -67,10 +70,12 @@ struct QuadOp {
   static constexpr int kNBat = 8 * NB;
   static constexpr bool kPlug = MB > 0;
   static constexpr int kMB = MB > 0 ? MB : 1;
+  static constexpr int kUnitBytes = 2048;
   using Buf = QuadBuf;
 
   const QuadParams& p;
   int g, c;
+  int pr;  // NK: physical row of mma row g inside the 8-row tile (see read())
   uint32_t lanebase, lut_add;
   int Mv, Nv, Kv, W;
   int64_t ldc, ldx_m;
@@ -87,6 +92,7 @@ struct QuadOp {
 
   __device__ __forceinline__ QuadOp(const QuadParams& p_, uint32_t lut_saddr)
       : p(p_), g((threadIdx.x & 31) >> 2), c(threadIdx.x & 3),
+        pr((((threadIdx.x & 31) >> 2) >> 1) | ((((threadIdx.x & 31) >> 2) & 1) << 2)),
         lanebase((DIRECT ? lut_saddr : 0u) | ((threadIdx.x & 31) * 4u)), lut_add(DIRECT ? 0u : lut_saddr), Mv(p_.M), Nv(p_.N), Kv(p_.K), W(p_.W), ldc(p_.ldc),
         ldx_m(p_.ldx_m), codes(p_.codes), x(p_.x), plug_idx(p_.plug_idx), plug_vals(p_.plug_vals),
         wbase(p_.wbase), base_lo32(p_.base_lo32) {
@@ -116,46 +122,37 @@ struct QuadOp {
       for (int q = 0; q < 4; ++q) corr[m][q] = 0.f;
   }
 
-  // Out-of-range rows / columns read a clamped in-range address instead:
-  // rows beyond N are never stored, and columns beyond K get zero weights
-  // in compute(), so no load is predicated in the steady state.
-  __device__ __forceinline__ void load(Buf& b, int tile, int kc) const {
+  // One unit by TMA into a 2 KiB ring slot (lane 0 only).  NK: 8 rows x 64
+  // codes as two 8 x 32 boxes (128-byte rows, 128-byte swizzle); KN: 16 rows
+  // x 32 features, one box.  Out-of-range elements arrive as zeros.
+  __device__ __forceinline__ void issue(uint32_t slot, uint32_t bar, int tile, int kc) const {
+    mbar_expect_tx(bar, kUnitBytes);
     if constexpr (NK) {
-      int row = tile * 8 + g;
-      row = row < Nv ? row : Nv - 1;
-      const int kb = kc * 64 + 4 * c;
-      const uint32_t* base = codes + (int64_t)row * ldc;
-      if (kb + 48 < Kv) {
-#pragma unroll
-        for (int s = 0; s < 4; ++s) b.q[s] = ldg_stream(base + kb + 16 * s);
-      } else {
-#pragma unroll
-        for (int s = 0; s < 4; ++s) b.q[s] = ldg_stream(base + (kb + 16 * s < Kv ? kb + 16 * s : 0));
-      }
+      tma_load_2d(slot, &p.tmap, kc * 64, tile * 8, bar);
+      tma_load_2d(slot + 1024u, &p.tmap, kc * 64 + 32, tile * 8, bar);
     } else {
-      int f = tile * 32 + 4 * g;
-      f = f < Nv ? f : Nv - 4;
-#pragma unroll
-      for (int r = 0; r < 4; ++r) {
-        int k = kc * 16 + 2 * c + (r & 1) + 8 * (r >> 1);
-        k = k < Kv ? k : 0;
-        b.q[r] = ldg_stream(codes + (int64_t)k * ldc + f);
-      }
+      tma_load_2d(slot, &p.tmap, tile * 32, kc * 16, bar);
     }
   }
 
-  __device__ __forceinline__ void prefetch(int tile, int kc) const {
+  // 16-byte chunk j of box row r sits at r*128 + 16*(j ^ (r & 7)) (128-byte
+  // swizzle).  NK: lane (g, c) needs row pr, chunk 4*(s&1) + c of box s>>1;
+  // mma row g maps to tile row pr = (g>>1) | ((g&1)<<2), so the two rows of
+  // a quarter-warp differ in bit 2 and their chunks never share banks.
+  // KN: lane (g, c) needs chunk g of rows 2c, 2c+1, 2c+8, 2c+9.
+  __device__ __forceinline__ void read(Buf& b, uint32_t slot) const {
     if constexpr (NK) {
-      // 8 rows x 256 bytes: lane (g, c) touches row g at byte 64c
-      const int64_t row = (int64_t)tile * 8 + g;
-      const int k = kc * 64 + 16 * c;
-      if (row < Nv && k < Kv) prefetch_l2(codes + row * ldc + k);
+#pragma unroll
+      for (int s = 0; s < 4; ++s) {
+        const int j = 4 * (s & 1) + c;
+        b.q[s] = lds128(slot + (uint32_t)((s >> 1) * 1024 + pr * 128 + ((j ^ pr) << 4)));
+      }
     } else {
-      // 16 rows x 128 bytes: lane l touches row l & 15, half l >> 4
-      const int lane = threadIdx.x & 31;
-      const int k = kc * 16 + (lane & 15);
-      const int f = tile * 32 + 16 * (lane >> 4);
-      if (k < Kv && f < Nv) prefetch_l2(codes + (int64_t)k * ldc + f);
+#pragma unroll
+      for (int r = 0; r < 4; ++r) {
+        const int row = 2 * c + (r & 1) + 8 * (r >> 1);
+        b.q[r] = lds128(slot + (uint32_t)(row * 128 + ((g ^ (row & 7)) << 4)));
+      }
     }
   }
 
@@ -225,7 +222,7 @@ struct QuadOp {
           mma_16816(acc[0][nb][1], a23[0], a23[1], a23[2], a23[3], xb.x, xb.y);
         }
       }
-      plug_correct((int64_t)tile * 8 + g, kc);
+      plug_correct((int64_t)tile * 8 + pr, kc);
     } else {
       const int kbase = kc * 16;
       const bool full_k = kbase + 16 <= Kv;
@@ -291,7 +288,7 @@ struct QuadOp {
     fold_corr();
 #pragma unroll
     for (int t = 0; t < kT; ++t) {
-      const int fi = NK ? g : 4 * g + t;
+      const int fi = NK ? pr : 4 * g + t;
 #pragma unroll
       for (int nb = 0; nb < NB; ++nb)
 #pragma unroll
@@ -308,7 +305,7 @@ struct QuadOp {
     fold_corr();
 #pragma unroll
     for (int t = 0; t < kT; ++t) {
-      const int f = tile * kTileW + (NK ? g : 4 * g + t);
+      const int f = tile * kTileW + (NK ? pr : 4 * g + t);
       if (f >= Nv) continue;
 #pragma unroll
       for (int nb = 0; nb < NB; ++nb)
@@ -327,27 +324,46 @@ struct QuadOp {
   }
 };
 
-// Partial slots (at least the 4 KiB the table build stages in).
-inline size_t quad_red_bytes(bool nk, int nb, int64_t M) {
-  const size_t r = red_bytes(quad_warps(nk, nb), 4, M, nk ? 8 : 32);
-  return r > 4096 ? r : 4096;
-}
+// Dynamic shared memory: [tables 128 KiB][TMA ring][mbarriers][partial
+// slots (at least the 4 KiB the table build stages in)].
+struct QuadSmem {
+  size_t ring, bars, red, total;
+};
 
-// Tables, alignment slack when DIRECT, then the partial slots.
-inline size_t quad_smem_bytes(bool nk, int nb, int64_t M, bool direct) {
-  return kQuadLutBytes + (direct ? 65536u : 0u) + quad_red_bytes(nk, nb, M);
+inline QuadSmem quad_smem(bool nk, int nb, int64_t M, int stages) {
+  const int nw = quad_warps(nk, nb);
+  QuadSmem m;
+  m.ring = (size_t)nw * stages * 2048;
+  m.bars = align_up((size_t)nw * stages * 8, 1024);
+  const size_t r = red_bytes(nw, 4, M, nk ? 8 : 32);
+  m.red = r > 4096 ? r : 4096;
+  m.total = kQuadLutBytes + 1024 + m.ring + m.bars + m.red;  // +1 KiB: ring aligned to 1 KiB
+  return m;
 }
 
 template <bool NK, int NB, int MB, bool DIRECT>
-__global__ void __launch_bounds__(quad_warps(NK, NB) * 32, 1) quad_gemv_kernel(const QuadParams p) {
+__device__ __forceinline__ void quad_body(const QuadParams& p, uint32_t base, uint32_t ring, uint32_t bars,
+                                          float* red, int* s_flag) {
+  QuadOp<NK, NB, MB, DIRECT> op(p, base);
+  run_partition_tma(op, p.part, red, s_flag, ring, bars, p.stages, p.part.counters + (kMaxGrid - 1));
+}
+
+template <bool NK, int NB, int MB>
+__global__ void __launch_bounds__(quad_warps(NK, NB) * 32, 1) quad_gemv_kernel(const __grid_constant__ QuadParams p) {
   __shared__ int s_flag;
-  const uint32_t lut_saddr = quad_lut_saddr<DIRECT>();
-  uint8_t* lut = quad_lut_ptr(lut_saddr);
-  float* red = reinterpret_cast<float*>(lut + kQuadLutBytes);
-  build_quad_lut(lut, reinterpret_cast<uint32_t*>(red), p.luts);
+  constexpr int NW = quad_warps(NK, NB);
+  const uint32_t base = (uint32_t)__cvta_generic_to_shared(pp_smem);
+  // 128-byte swizzled TMA boxes need 1 KiB-aligned destinations
+  const uint32_t ring = (base + kQuadLutBytes + 1023u) & ~1023u;
+  const uint32_t ring_bytes = (uint32_t)(NW * p.stages * 2048);
+  const uint32_t bars = ring + ring_bytes;
+  const uint32_t bar_bytes = ((uint32_t)(NW * p.stages * 8) + 1023u) & ~1023u;
+  float* red = reinterpret_cast<float*>(pp_smem + (bars + bar_bytes - base));
+  build_quad_lut(pp_smem, reinterpret_cast<uint32_t*>(red), p.luts);
   __syncthreads();
-  QuadOp<NK, NB, MB, DIRECT> op(p, lut_saddr);
-  run_partition(op, p.part, red, &s_flag);
+  // tables on a 64 KiB boundary: gather addresses come straight from PRMT
+  if ((base & 0xFFFFu) == 0) quad_body<NK, NB, MB, true>(p, base, ring, bars, red, &s_flag);
+  else quad_body<NK, NB, MB, false>(p, base, ring, bars, red, &s_flag);
 }
 
 // Generic fallback for layouts the vector paths do not take (unaligned or
@@ -407,30 +423,26 @@ PartitionPlan quad_plan(bool nk, int64_t Mc, int64_t N, int64_t K, int sms) {
   return plan_partition(cdiv(N, tile_w), cdiv(K, unit_k), quad_warps(nk, nb), sms, 4, Mc, tile_w);
 }
 
-bool g_attr_done[16][64];
-int g_attr_limit[16][64];
+bool g_attr_done[8][64];
+int g_attr_limit[8][64];
 
-template <bool NK, int NB, int MB, bool DIRECT>
-int launch_quad_v(const QuadParams& prm, int grid, int idx, cudaStream_t s) {
-  auto kern = quad_gemv_kernel<NK, NB, MB, DIRECT>;
+template <bool NK, int NB, int MB>
+int launch_quad(QuadParams& prm, int grid, int idx, cudaStream_t s) {
+  auto kern = quad_gemv_kernel<NK, NB, MB>;
   int max_smem = 0;
   int rc = ensure_smem_attr(kern, g_attr_done[idx], g_attr_limit[idx], &max_smem);
   if (rc) return rc;
-  const size_t smem = quad_smem_bytes(NK, NB, prm.M, DIRECT);
-  if (smem > (size_t)max_smem) {
-    set_error("shared memory plan of %zu bytes exceeds the per-CTA limit %d", smem, max_smem);
+  // deepest TMA ring (up to 4 slots per warp) that fits
+  int stages = 4;
+  while (stages > 1 && quad_smem(NK, NB, prm.M, stages).total > (size_t)max_smem) --stages;
+  const QuadSmem sm = quad_smem(NK, NB, prm.M, stages);
+  if (sm.total > (size_t)max_smem) {
+    set_error("shared memory plan of %zu bytes exceeds the per-CTA limit %d", sm.total, max_smem);
     return PP_ERR_INVALID;
   }
-  kern<<<grid, quad_warps(NK, NB) * 32, smem, s>>>(prm);
+  prm.stages = stages;
+  kern<<<grid, quad_warps(NK, NB) * 32, sm.total, s>>>(prm);
   return check_launch("quad_gemv_kernel");
-}
-
-// Direct table addressing whenever the 64 KiB alignment slack fits.
-template <bool NK, int NB, int MB>
-int launch_quad(const QuadParams& prm, int grid, int idx, cudaStream_t s) {
-  if (quad_smem_bytes(NK, NB, prm.M, true) <= 227u * 1024u - 1024u)
-    return launch_quad_v<NK, NB, MB, true>(prm, grid, 2 * idx, s);
-  return launch_quad_v<NK, NB, MB, false>(prm, grid, 2 * idx + 1, s);
 }
 
 int launch_plan(const PartitionPlan& pl, bool nk, int64_t Mc, QuadParams prm, void* ws, bool plug,
@@ -579,6 +591,10 @@ static int quad_run(const void* a, int64_t lda_m, int64_t lda_k, const uint32_t*
     set_error("matrix too large for one launch (more than 2^31 work units)");
     return PP_ERR_INVALID;
   }
+  // codes as a 2D tensor for TMA: NK rows n of K codes, KN rows k of N codes
+  if ((rc = nk ? encode_tmap_u32_2d(&prm.tmap, codes, (uint64_t)K, (uint64_t)N, (uint64_t)ldc_n * 4, 32, 8)
+               : encode_tmap_u32_2d(&prm.tmap, codes, (uint64_t)N, (uint64_t)K, (uint64_t)ldc_k * 4, 32, 16)))
+    return rc;
   const size_t need = quad_plan(nk, M < 16 ? M : 16, N, K, sms).total();
   if (ws_bytes < need || (need && !ws) || !aligned(ws, 256)) {
     set_error("workspace of %zu bytes (256-byte aligned, zero-filled) required, got %zu", need, ws_bytes);
