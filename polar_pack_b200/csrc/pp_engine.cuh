@@ -134,6 +134,8 @@ __device__ __forceinline__ void reduce_partials(Op& op, const Partition& pt, con
 //   void prefetch(int tile, int kc) const;      L2 prefetch of one unit
 //   void compute(const Buf&, int tile, int kc);
 //   void write_partial(float* slot, int M);     compact [out][bat < M][fi]
+//   void begin(int tile, int kc); void preload(int tile, int kc);
+//                                               side data of the first / next unit
 //   int  M() const; int N() const;
 //   void store_tile(int tile) const;            whole tile from registers
 //   void store(int out, int bat, int f, float v) const;
@@ -242,6 +244,7 @@ __device__ __forceinline__ void run_partition_tma(Op& op, const Partition& pt, f
     int slot = 0;
     uint32_t parity = 0;
     op.zero();
+    op.begin(t, kc);
     typename Op::Buf buf;
     for (int u = wu0; u < wu1; ++u) {
       const uint32_t sl = my_ring + (uint32_t)(slot * Op::kUnitBytes);
@@ -253,9 +256,10 @@ __device__ __forceinline__ void run_partition_tma(Op& op, const Partition& pt, f
         if (++ikc == upt) { ikc = 0; ++it; }
       }
       if (++slot == S) { slot = 0; parity ^= 1u; }
-      op.compute(buf, t, kc);
       int nt = t, nkc = kc + 1;
       if (nkc == upt) { nkc = 0; ++nt; }
+      if (u + 1 < wu1) op.preload(nt, nkc);
+      op.compute(buf, t, kc);
       if (nkc == 0 || u + 1 == wu1) {
         if ((t * upt >= wu0) && nkc == 0) {
           op.store_tile(t);
@@ -297,7 +301,7 @@ inline PartitionPlan plan_partition(int64_t tiles, int64_t upt, int warps, int s
 }
 
 // Shared memory for the warps' partial slots of one launch.
-inline size_t red_bytes(int warps, int nout, int64_t M, int tile_w) {
+__host__ __device__ inline size_t red_bytes(int warps, int nout, int64_t M, int tile_w) {
   return (size_t)warps * 2 * (size_t)(nout * M * tile_w) * sizeof(float);
 }
 

@@ -89,6 +89,8 @@ struct QuadOp {
   bool xok[NB];
   float acc[kT][NB][2][4];
   float corr[kMB][4];
+  // plug window bounds of the unit being decoded and of the next unit
+  uint32_t cur_j0 = 0, cur_j1 = 0, nxt_j0 = 0, nxt_j1 = 0;
 
   __device__ __forceinline__ QuadOp(const QuadParams& p_, uint32_t lut_saddr)
       : p(p_), g((threadIdx.x & 31) >> 2), c(threadIdx.x & 3),
@@ -169,28 +171,38 @@ struct QuadOp {
     return make_uint2(0u, 0u);
   }
 
-  // Plug entries of (row, window kc): lanes of the row take every 4th entry.
-  __device__ __forceinline__ void plug_correct(int64_t row, int kc) {
+  // Window bounds of the next unit's plug entries, loaded one unit ahead so
+  // the dependent loads (bounds -> entries -> activation) leave the
+  // critical path.  The engine calls preload(next) before compute(current).
+  __device__ __forceinline__ void preload(int tile, int kc) {
     if constexpr (kPlug) {
-      if (row >= Nv) return;
-      const int64_t wi = row * W + kc;
-      const uint32_t j0 = __ldg(wbase + wi), j1 = __ldg(wbase + wi + 1);
-      const uint32_t rowbase = base_lo32 + (uint32_t)row * (uint32_t)Kv;
-      for (uint32_t j = j0 + c; j < j1; j += 4) {
-        const uint32_t k = __ldg(plug_idx + j) - rowbase;
-        const uint2 v = __ldg(plug_vals + j);
-        const float pv[4] = {__half2float(__ushort_as_half((uint16_t)(v.x & 0xFFFF))),
-                             __half2float(__ushort_as_half((uint16_t)(v.x >> 16))),
-                             __half2float(__ushort_as_half((uint16_t)(v.y & 0xFFFF))),
-                             __half2float(__ushort_as_half((uint16_t)(v.y >> 16)))};
+      const int row = tile * 8 + pr;
+      if (row < Nv) {
+        const int64_t wi = (int64_t)row * W + kc;
+        nxt_j0 = __ldg(wbase + wi);
+        nxt_j1 = __ldg(wbase + wi + 1);
+      } else {
+        nxt_j0 = nxt_j1 = 0u;
+      }
+    }
+  }
+  __device__ __forceinline__ void begin(int tile, int kc) {
+    preload(tile, kc);
+    cur_j0 = nxt_j0;
+    cur_j1 = nxt_j1;
+  }
+
+  __device__ __forceinline__ void plug_accumulate(uint32_t k, uint2 v) {
+    const float pv[4] = {__half2float(__ushort_as_half((uint16_t)(v.x & 0xFFFF))),
+                         __half2float(__ushort_as_half((uint16_t)(v.x >> 16))),
+                         __half2float(__ushort_as_half((uint16_t)(v.y & 0xFFFF))),
+                         __half2float(__ushort_as_half((uint16_t)(v.y >> 16)))};
 #pragma unroll
-        for (int m = 0; m < kMB; ++m) {
-          if (m < Mv) {
-            const float xv = __half2float(__ushort_as_half(ldg_u16(x + (int64_t)m * ldx_m + k)));
+    for (int m = 0; m < kMB; ++m) {
+      if (m < Mv) {
+        const float xv = __half2float(__ushort_as_half(ldg_u16(x + (int64_t)m * ldx_m + k)));
 #pragma unroll
-            for (int q = 0; q < 4; ++q) corr[m][q] = fmaf(pv[q], xv, corr[m][q]);
-          }
-        }
+        for (int q = 0; q < 4; ++q) corr[m][q] = fmaf(pv[q], xv, corr[m][q]);
       }
     }
   }
@@ -199,6 +211,21 @@ struct QuadOp {
     if constexpr (NK) {
       const int kbase = kc * 64;
       const bool full_k = kbase + 64 <= Kv;
+      // this lane's first plug entry of the unit (lanes of a row take every 4th)
+      const uint32_t j0 = cur_j0 + c, j1 = cur_j1;
+      uint32_t pidx = 0;
+      uint2 pval = make_uint2(0u, 0u);
+      if constexpr (kPlug) {
+        if (j0 < j1) {
+          pidx = __ldg(plug_idx + j0);
+          pval = __ldg(plug_vals + j0);
+        }
+      }
+      uint2 xb[4][NB];
+#pragma unroll
+      for (int s = 0; s < 4; ++s)
+#pragma unroll
+        for (int nb = 0; nb < NB; ++nb) xb[s][nb] = xquad(nb, kbase + 16 * s + 4 * c);
 #pragma unroll
       for (int s = 0; s < 4; ++s) {
         const int kp = kbase + 16 * s + 4 * c;
@@ -217,12 +244,19 @@ struct QuadOp {
         }
 #pragma unroll
         for (int nb = 0; nb < NB; ++nb) {
-          const uint2 xb = xquad(nb, kp);
-          mma_16816(acc[0][nb][0], a01[0], a01[1], a01[2], a01[3], xb.x, xb.y);
-          mma_16816(acc[0][nb][1], a23[0], a23[1], a23[2], a23[3], xb.x, xb.y);
+          mma_16816(acc[0][nb][0], a01[0], a01[1], a01[2], a01[3], xb[s][nb].x, xb[s][nb].y);
+          mma_16816(acc[0][nb][1], a23[0], a23[1], a23[2], a23[3], xb[s][nb].x, xb[s][nb].y);
         }
       }
-      plug_correct((int64_t)tile * 8 + pr, kc);
+      if constexpr (kPlug) {
+        const uint32_t rowbase = base_lo32 + (uint32_t)(tile * 8 + pr) * (uint32_t)Kv;
+        if (j0 < j1) {
+          plug_accumulate(pidx - rowbase, pval);
+          for (uint32_t j = j0 + 4; j < j1; j += 4) plug_accumulate(__ldg(plug_idx + j) - rowbase, __ldg(plug_vals + j));
+        }
+        cur_j0 = nxt_j0;
+        cur_j1 = nxt_j1;
+      }
     } else {
       const int kbase = kc * 16;
       const bool full_k = kbase + 16 <= Kv;
@@ -337,7 +371,7 @@ inline QuadSmem quad_smem(bool nk, int nb, int64_t M, int stages) {
   m.bars = align_up((size_t)nw * stages * 8, 1024);
   const size_t r = red_bytes(nw, 4, M, nk ? 8 : 32);
   m.red = r > 4096 ? r : 4096;
-  m.total = kQuadLutBytes + 1024 + m.ring + m.bars + m.red;  // +1 KiB: ring aligned to 1 KiB
+  m.total = kQuadLutBytes + 1024 + m.ring + m.bars + m.red + 16;  // +1 KiB ring alignment, flag
   return m;
 }
 
@@ -348,9 +382,10 @@ __device__ __forceinline__ void quad_body(const QuadParams& p, uint32_t base, ui
   run_partition_tma(op, p.part, red, s_flag, ring, bars, p.stages, p.part.counters + (kMaxGrid - 1));
 }
 
+// No static shared memory: the dynamic region then starts at shared address
+// 0 on current drivers, a 64 KiB boundary, which enables DIRECT addressing.
 template <bool NK, int NB, int MB>
 __global__ void __launch_bounds__(quad_warps(NK, NB) * 32, 1) quad_gemv_kernel(const __grid_constant__ QuadParams p) {
-  __shared__ int s_flag;
   constexpr int NW = quad_warps(NK, NB);
   const uint32_t base = (uint32_t)__cvta_generic_to_shared(pp_smem);
   // 128-byte swizzled TMA boxes need 1 KiB-aligned destinations
@@ -359,11 +394,13 @@ __global__ void __launch_bounds__(quad_warps(NK, NB) * 32, 1) quad_gemv_kernel(c
   const uint32_t bars = ring + ring_bytes;
   const uint32_t bar_bytes = ((uint32_t)(NW * p.stages * 8) + 1023u) & ~1023u;
   float* red = reinterpret_cast<float*>(pp_smem + (bars + bar_bytes - base));
+  const int red_floats = (int)(red_bytes(NW, 4, p.M, NK ? 8 : 32) / 4);
+  int* s_flag = reinterpret_cast<int*>(red + (red_floats > 1024 ? red_floats : 1024));
   build_quad_lut(pp_smem, reinterpret_cast<uint32_t*>(red), p.luts);
   __syncthreads();
   // tables on a 64 KiB boundary: gather addresses come straight from PRMT
-  if ((base & 0xFFFFu) == 0) quad_body<NK, NB, MB, true>(p, base, ring, bars, red, &s_flag);
-  else quad_body<NK, NB, MB, false>(p, base, ring, bars, red, &s_flag);
+  if ((base & 0xFFFFu) == 0) quad_body<NK, NB, MB, true>(p, base, ring, bars, red, s_flag);
+  else quad_body<NK, NB, MB, false>(p, base, ring, bars, red, s_flag);
 }
 
 // Generic fallback for layouts the vector paths do not take (unaligned or
