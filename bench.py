@@ -185,7 +185,9 @@ def run_ours(args):
     full_sets = [layer_slices(s, SHAPES, 0, 1) for s in streams] if world > 1 else sets
 
     lib = _lib.load()
-    stream = torch.cuda.current_stream(dev)
+    # everything runs on one side stream, which is also the graph-capture stream
+    stream = torch.cuda.Stream(dev)
+    torch.cuda.set_stream(stream)
     sh = stream.cuda_stream
     g = torch.Generator(device=dev)
     g.manual_seed(7)
@@ -217,13 +219,9 @@ def run_ours(args):
         if rc:
             _lib.check(rc)
 
-    def step(i, evs=None):
-        for j, (args_c, outs, gbuf, l) in enumerate(calls[i % len(calls)]):
-            if evs is not None:
-                evs[j][0].record(stream)
+    def step(i):
+        for args_c, outs, gbuf, l in calls[i % len(calls)]:
             launch(args_c)
-            if evs is not None:
-                evs[j][1].record(stream)
             if gbuf is not None:
                 # the 4 models' row shards, gathered over ranks
                 dist.all_gather_into_tensor(gbuf[1], gbuf[0])
@@ -231,7 +229,7 @@ def run_ours(args):
     per_step_bytes = sum(layer_bytes(l.N, l.K, l.p_hi - l.p_lo, M) for l in full_sets[0])
     avg_bytes = statistics.mean(sum(layer_bytes(l.N, l.K, l.p_hi - l.p_lo, M) for l in fs) for fs in full_sets)
 
-    # correctness gate before timing: one shard output vs the public API path
+    # correctness gate before timing: the pre-built launch vs the public API path
     ref = quad_linear(xs[0], sets[0][0])
     launch(calls[0][0][0])
     torch.cuda.synchronize(dev)
@@ -242,13 +240,29 @@ def run_ours(args):
     for i in range(args.warmup):
         step(i)
     torch.cuda.synchronize(dev)
+
+    # one CUDA graph per replica set: the timed loop replays whole steps, so
+    # host launch latency is not part of the measurement
+    graphs = []
+    use_graphs = not args.eager
+    if use_graphs:
+        try:
+            for r in range(len(calls)):
+                g = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(g, stream=stream):
+                    step(r)
+                graphs.append(g)
+            for g in graphs:
+                g.replay()
+            torch.cuda.synchronize(dev)
+        except Exception as e:  # capture unsupported (e.g. collectives): time eager launches
+            print(f"graph capture failed, timing eager launches: {e}", file=sys.stderr)
+            graphs, use_graphs = [], False
     if world > 1:
         dist.barrier()
 
     K_steps = args.steps
-    launches_per_step = len(SHAPES)
-    evs = [[[torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)]
-            for _ in SHAPES] for _ in range(K_steps)]
+    launches_per_step = sum(2 if l.plug_vals is not None else 1 for l in sets[0])
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     clocks = ClockSampler(local)
     clocks.start()
@@ -258,29 +272,61 @@ def run_ours(args):
         dist.barrier()
     t0.record(stream)
     for i in range(K_steps):
-        step(args.warmup + i, evs[i])
+        if use_graphs:
+            graphs[(args.warmup + i) % len(graphs)].replay()
+        else:
+            step(args.warmup + i)
     t1.record(stream)
     torch.cuda.synchronize(dev)
     if world > 1:
         dist.barrier()
     clk = clocks.stop()
     ms = t0.elapsed_time(t1)
-    kernel_ms = sum(e[0].elapsed_time(e[1]) for step_evs in evs for e in step_evs)
-    kernel_bytes = 0
-    for i in range(K_steps):
-        for l in sets[(args.warmup + i) % len(sets)]:
-            kernel_bytes += layer_bytes(l.N, l.K, l.p_hi - l.p_lo, M)
     if world > 1:
         t = torch.tensor([ms], dtype=torch.float64, device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms = float(t.item())
     total_bytes = avg_bytes * K_steps
     value = total_bytes / (ms * 1e-3) / 1e9
-    per_shape = {}
+
+    # the fused GEMV kernel alone, per shape: a graph of its launches over the
+    # replica streams (rotating, so every launch reads codes L2 does not hold)
+    per_shape, kernel_bytes, kernel_ms = {}, 0.0, 0.0
     for j, (K, N) in enumerate(SHAPES):
-        tj = sum(evs[i][j][0].elapsed_time(evs[i][j][1]) for i in range(K_steps)) / K_steps
+        gemv_args = []
+        for st in sets:
+            l = st[j]
+            outs = [torch.empty((M, l.N), dtype=torch.float16, device=dev) for _ in range(4)]
+            gemv_args.append((xs[j].data_ptr(), xs[j].stride(0), xs[j].stride(1), l.codes.data_ptr(), 1, l.K,
+                              _lib.ptrs(l.pack.luts, 7), _lib.floats4(l.pack.scales), _lib.ptrs(outs, 4),
+                              outs[0].stride(0), outs[0].stride(1), M, l.N, l.K, ws.data_ptr(), ws.numel(), sh,
+                              outs))
+        def gemv_pass():
+            for a_ in gemv_args:
+                _lib.check(lib.pp_quad_gemm(*a_[:-1]))
+        gemv_pass()
+        reps = max(4, K_steps // 2)
+        torch.cuda.synchronize(dev)
+        if use_graphs:
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=stream):
+                gemv_pass()
+            g.replay()
+            torch.cuda.synchronize(dev)
+            run = g.replay
+        else:
+            run = gemv_pass
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(reps):
+            run()
+        e1.record(stream)
+        torch.cuda.synchronize(dev)
+        tj = e0.elapsed_time(e1) / (reps * len(sets))
         bj = statistics.mean(layer_bytes(st[j].N, st[j].K, st[j].p_hi - st[j].p_lo, M) for st in sets)
         per_shape[f"{K}x{N}"] = {"us": round(tj * 1e3, 2), "GB/s": round(bj / (tj * 1e-3) / 1e9, 1)}
+        kernel_bytes += bj
+        kernel_ms += tj
 
     # e2e through the public API with host buffers (pinned), 1 GPU view of rank's work
     e2e = run_e2e(torch, dist, sets, xs, dev, args, world, M)
@@ -297,13 +343,16 @@ def run_ours(args):
                    "bytes_per_step": int(per_step_bytes), "l2": "inputs per step ~200 MB > 126 MB L2, "
                    "4 rotating replica streams (no flush)",
                    "parallelism": f"row-sharded x{world} + NCCL all-gather" if world > 1 else "single GPU",
-                   "per_shape": per_shape},
+                   "timing": "CUDA graph replay of whole steps" if use_graphs else "eager launches",
+                   "per_shape_gemv_kernel": per_shape},
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(achieved / peak, 4), "peak_source": f"{peak_kind} hbm_gbs",
-                     "kernel": "quad_gemv_kernel<NK=1,NB=1,MB=1> (file layout, plug correction, batch 1)",
+                     "kernel": "quad_gemv_kernel<NK=1,NB=1> (file layout, batch 1)",
+                     "achieved_from": "bytes-weighted mean over the 4 shapes of per-launch CUDA-event time",
                      "traffic": traffic},
         "e2e": e2e,
         "gpu_launches": launches_per_step * K_steps,
+        "gpu_launches_note": "per Linear: the plug-correction kernel and the fused GEMV kernel",
         "clocks": clk,
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -525,6 +574,7 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--ref-fraction", type=float, default=1 / 32)
+    ap.add_argument("--eager", action="store_true", help="time eager launches instead of CUDA graphs")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

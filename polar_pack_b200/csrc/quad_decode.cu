@@ -259,3 +259,81 @@ int pp_quad_prepare_plugs(uint32_t* codes, int64_t ldw, const uint32_t* plug_idx
 }
 
 }  // extern "C"
+
+namespace pp {
+
+// Plug-table correction of one file-layout Linear, as a CSR sparse product:
+//   corr[q][m][n] = sum over plug entries j of row n of  pv_j[q] * x[m][k_j]
+// (FP32).  The fused kernel decodes plugged codes to exact zeros (their norm
+// byte was cleared by pp_quad_prepare_plugs) and adds corr before the
+// per-model scale and the FP16 store, so the result equals the product with
+// the plug values substituted, up to FP32 summation order.  One warp per
+// row; lanes take every 32nd entry and the warp sums lane totals in a fixed
+// butterfly order, so results are deterministic.
+struct PlugCorrParams {
+  const __half* x;
+  int64_t ldx_m;
+  const uint32_t* plug_idx;  // this Linear's slice
+  const uint2* plug_vals;
+  const uint32_t* wbase;     // [N*W + 1]
+  uint32_t base_lo32;
+  int M, N, K, W;
+  float* corr;               // [4][M][N]
+};  // (declared identically in quad_gemv.cu)
+
+template <int MB>
+__global__ void __launch_bounds__(256) quad_plug_corr_kernel(const PlugCorrParams p) {
+  const int lane = threadIdx.x & 31;
+  const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (row >= p.N) return;
+  const uint32_t j0 = __ldg(p.wbase + (int64_t)row * p.W), j1 = __ldg(p.wbase + (int64_t)(row + 1) * p.W);
+  const uint32_t rowbase = p.base_lo32 + (uint32_t)row * (uint32_t)p.K;
+  float acc[MB][4];
+#pragma unroll
+  for (int m = 0; m < MB; ++m)
+#pragma unroll
+    for (int q = 0; q < 4; ++q) acc[m][q] = 0.f;
+  for (uint32_t j = j0 + lane; j < j1; j += 32) {
+    const uint32_t k = __ldg(p.plug_idx + j) - rowbase;
+    const uint2 v = __ldg(p.plug_vals + j);
+    const float pv[4] = {__half2float(__ushort_as_half((uint16_t)(v.x & 0xFFFF))),
+                         __half2float(__ushort_as_half((uint16_t)(v.x >> 16))),
+                         __half2float(__ushort_as_half((uint16_t)(v.y & 0xFFFF))),
+                         __half2float(__ushort_as_half((uint16_t)(v.y >> 16)))};
+#pragma unroll
+    for (int m = 0; m < MB; ++m) {
+      if (m < p.M) {
+        const float xv = __half2float(p.x[(int64_t)m * p.ldx_m + k]);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) acc[m][q] = fmaf(pv[q], xv, acc[m][q]);
+      }
+    }
+  }
+#pragma unroll
+  for (int m = 0; m < MB; ++m)
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      float v = acc[m][q];
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+      acc[m][q] = v;
+    }
+  if (lane == 0) {
+#pragma unroll
+    for (int m = 0; m < MB; ++m)
+      if (m < p.M)
+#pragma unroll
+        for (int q = 0; q < 4; ++q) p.corr[((int64_t)q * p.M + m) * p.N + row] = acc[m][q];
+  }
+}
+
+int launch_plug_corr(const PlugCorrParams& prm, cudaStream_t s) {
+  const int warps = 8;
+  const int grid = (int)cdiv(prm.N, warps);
+  if (prm.M == 1) quad_plug_corr_kernel<1><<<grid, warps * 32, 0, s>>>(prm);
+  else if (prm.M <= 8) quad_plug_corr_kernel<8><<<grid, warps * 32, 0, s>>>(prm);
+  else quad_plug_corr_kernel<16><<<grid, warps * 32, 0, s>>>(prm);
+  return check_launch("quad_plug_corr_kernel");
+}
+
+}  // namespace pp

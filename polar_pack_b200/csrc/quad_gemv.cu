@@ -25,6 +25,19 @@ namespace pp {
 
 int zero_f16(void* p, int64_t R, int64_t C, int64_t ldr, int64_t ldc, cudaStream_t s);
 
+// quad_decode.cu: CSR plug-table correction of one file-layout Linear
+struct PlugCorrParams {
+  const __half* x;
+  int64_t ldx_m;
+  const uint32_t* plug_idx;
+  const uint2* plug_vals;
+  const uint32_t* wbase;
+  uint32_t base_lo32;
+  int M, N, K, W;
+  float* corr;
+};
+int launch_plug_corr(const PlugCorrParams& prm, cudaStream_t s);
+
 // Warps per CTA.  Shared memory holds the 128 KiB tables, each warp's TMA
 // ring (2 KiB per slot) and two partial slots per warp; the KN tile keeps
 // 4x more accumulators and partials per warp, and two batch tiles double
@@ -42,13 +55,8 @@ struct QuadParams {
   __half* out[4];
   int64_t ldo_m, ldo_n;
   int M, N, K;
-  // plug correction (NK only).  Plugged positions carry a zero norm byte,
-  // so they decode to exact zeros; their FP16 4-tuples are added here.
-  const uint32_t* plug_idx;  // this Linear's slice of the stream positions
-  const uint2* plug_vals;    // same slice, 4 FP16 per entry
-  const uint32_t* wbase;     // [N*W + 1] first plug of each (row, 64-column window)
-  uint32_t base_lo32;        // low 32 bits of the Linear's stream offset
-  int W;
+  // plug-table correction [4][M][N] FP32 added before the scale (NULL: none)
+  const float* corr;
   Partition part;
   int xvec;
   int stages;  // TMA ring slots per warp
@@ -58,18 +66,15 @@ struct QuadBuf {
   uint4 q[4];
 };
 
-// NK: file layout.  MB > 0 selects the plug-correcting variant for up to MB
-// batch rows (MB in {1, 8, 16}); MB == 0 has no plug table.  DIRECT: tables
-// at a 64 KiB-aligned shared address (see quad_lut_saddr).
-template <bool NK, int NB, int MB, bool DIRECT>
+// NK: file layout.  DIRECT: tables at a 64 KiB-aligned shared address (see
+// quad_lut_saddr).
+template <bool NK, int NB, bool DIRECT>
 struct QuadOp {
   static constexpr int kWarps = quad_warps(NK, NB);
   static constexpr int kTileW = NK ? 8 : 32;  // output features per tile
   static constexpr int kT = NK ? 1 : 4;       // mma pairs per 16-k step
   static constexpr int kNOut = 4;
   static constexpr int kNBat = 8 * NB;
-  static constexpr bool kPlug = MB > 0;
-  static constexpr int kMB = MB > 0 ? MB : 1;
   static constexpr int kUnitBytes = 2048;
   using Buf = QuadBuf;
 
@@ -77,32 +82,22 @@ struct QuadOp {
   int g, c;
   int pr;  // NK: physical row of mma row g inside the 8-row tile (see read())
   uint32_t lanebase, lut_add;
-  int Mv, Nv, Kv, W;
+  int Mv, Nv, Kv;
   int64_t ldc, ldx_m;
   const uint32_t* codes;
   const __half* x;
-  const uint32_t* plug_idx;
-  const uint2* plug_vals;
-  const uint32_t* wbase;
-  uint32_t base_lo32;
   const __half* xrow[NB];  // this lane's activation row per batch tile (clamped)
-  bool xok[NB];
   float acc[kT][NB][2][4];
-  float corr[kMB][4];
-  // plug window bounds of the unit being decoded and of the next unit
-  uint32_t cur_j0 = 0, cur_j1 = 0, nxt_j0 = 0, nxt_j1 = 0;
 
   __device__ __forceinline__ QuadOp(const QuadParams& p_, uint32_t lut_saddr)
       : p(p_), g((threadIdx.x & 31) >> 2), c(threadIdx.x & 3),
         pr((((threadIdx.x & 31) >> 2) >> 1) | ((((threadIdx.x & 31) >> 2) & 1) << 2)),
-        lanebase((DIRECT ? lut_saddr : 0u) | ((threadIdx.x & 31) * 4u)), lut_add(DIRECT ? 0u : lut_saddr), Mv(p_.M), Nv(p_.N), Kv(p_.K), W(p_.W), ldc(p_.ldc),
-        ldx_m(p_.ldx_m), codes(p_.codes), x(p_.x), plug_idx(p_.plug_idx), plug_vals(p_.plug_vals),
-        wbase(p_.wbase), base_lo32(p_.base_lo32) {
+        lanebase((DIRECT ? lut_saddr : 0u) | ((threadIdx.x & 31) * 4u)), lut_add(DIRECT ? 0u : lut_saddr),
+        Mv(p_.M), Nv(p_.N), Kv(p_.K), ldc(p_.ldc), ldx_m(p_.ldx_m), codes(p_.codes), x(p_.x) {
 #pragma unroll
     for (int nb = 0; nb < NB; ++nb) {
       const int bat = nb * 8 + g;
-      xok[nb] = bat < Mv;
-      xrow[nb] = x + (int64_t)(xok[nb] ? bat : 0) * ldx_m;
+      xrow[nb] = x + (int64_t)(bat < Mv ? bat : 0) * ldx_m;
     }
   }
 
@@ -118,11 +113,10 @@ struct QuadOp {
         for (int h = 0; h < 2; ++h)
 #pragma unroll
           for (int j = 0; j < 4; ++j) acc[t][nb][h][j] = 0.f;
-#pragma unroll
-    for (int m = 0; m < kMB; ++m)
-#pragma unroll
-      for (int q = 0; q < 4; ++q) corr[m][q] = 0.f;
   }
+
+  __device__ __forceinline__ void begin(int, int) {}
+  __device__ __forceinline__ void preload(int, int) {}
 
   // One unit by TMA into a 2 KiB ring slot (lane 0 only).  NK: 8 rows x 64
   // codes as two 8 x 32 boxes (128-byte rows, 128-byte swizzle); KN: 16 rows
@@ -171,56 +165,10 @@ struct QuadOp {
     return make_uint2(0u, 0u);
   }
 
-  // Window bounds of the next unit's plug entries, loaded one unit ahead so
-  // the dependent loads (bounds -> entries -> activation) leave the
-  // critical path.  The engine calls preload(next) before compute(current).
-  __device__ __forceinline__ void preload(int tile, int kc) {
-    if constexpr (kPlug) {
-      const int row = tile * 8 + pr;
-      if (row < Nv) {
-        const int64_t wi = (int64_t)row * W + kc;
-        nxt_j0 = __ldg(wbase + wi);
-        nxt_j1 = __ldg(wbase + wi + 1);
-      } else {
-        nxt_j0 = nxt_j1 = 0u;
-      }
-    }
-  }
-  __device__ __forceinline__ void begin(int tile, int kc) {
-    preload(tile, kc);
-    cur_j0 = nxt_j0;
-    cur_j1 = nxt_j1;
-  }
-
-  __device__ __forceinline__ void plug_accumulate(uint32_t k, uint2 v) {
-    const float pv[4] = {__half2float(__ushort_as_half((uint16_t)(v.x & 0xFFFF))),
-                         __half2float(__ushort_as_half((uint16_t)(v.x >> 16))),
-                         __half2float(__ushort_as_half((uint16_t)(v.y & 0xFFFF))),
-                         __half2float(__ushort_as_half((uint16_t)(v.y >> 16)))};
-#pragma unroll
-    for (int m = 0; m < kMB; ++m) {
-      if (m < Mv) {
-        const float xv = __half2float(__ushort_as_half(ldg_u16(x + (int64_t)m * ldx_m + k)));
-#pragma unroll
-        for (int q = 0; q < 4; ++q) corr[m][q] = fmaf(pv[q], xv, corr[m][q]);
-      }
-    }
-  }
-
   __device__ __forceinline__ void compute(const Buf& b, int tile, int kc) {
     if constexpr (NK) {
       const int kbase = kc * 64;
       const bool full_k = kbase + 64 <= Kv;
-      // this lane's first plug entry of the unit (lanes of a row take every 4th)
-      const uint32_t j0 = cur_j0 + c, j1 = cur_j1;
-      uint32_t pidx = 0;
-      uint2 pval = make_uint2(0u, 0u);
-      if constexpr (kPlug) {
-        if (j0 < j1) {
-          pidx = __ldg(plug_idx + j0);
-          pval = __ldg(plug_vals + j0);
-        }
-      }
       uint2 xb[4][NB];
 #pragma unroll
       for (int s = 0; s < 4; ++s)
@@ -247,15 +195,6 @@ struct QuadOp {
           mma_16816(acc[0][nb][0], a01[0], a01[1], a01[2], a01[3], xb[s][nb].x, xb[s][nb].y);
           mma_16816(acc[0][nb][1], a23[0], a23[1], a23[2], a23[3], xb[s][nb].x, xb[s][nb].y);
         }
-      }
-      if constexpr (kPlug) {
-        const uint32_t rowbase = base_lo32 + (uint32_t)(tile * 8 + pr) * (uint32_t)Kv;
-        if (j0 < j1) {
-          plug_accumulate(pidx - rowbase, pval);
-          for (uint32_t j = j0 + 4; j < j1; j += 4) plug_accumulate(__ldg(plug_idx + j) - rowbase, __ldg(plug_vals + j));
-        }
-        cur_j0 = nxt_j0;
-        cur_j1 = nxt_j1;
       }
     } else {
       const int kbase = kc * 16;
@@ -291,35 +230,9 @@ struct QuadOp {
     }
   }
 
-  // Plug corrections of the 4 lanes of a row are disjoint subsets: sum them
-  // (same order on every lane) and add them to the fragment of (model, batch).
-  __device__ __forceinline__ void fold_corr() {
-    if constexpr (kPlug) {
-#pragma unroll
-      for (int m = 0; m < kMB; ++m)
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          corr[m][q] += __shfl_xor_sync(0xffffffffu, corr[m][q], 1);
-          corr[m][q] += __shfl_xor_sync(0xffffffffu, corr[m][q], 2);
-        }
-#pragma unroll
-      for (int nb = 0; nb < NB; ++nb)
-#pragma unroll
-        for (int h = 0; h < 2; ++h)
-#pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            const int bat = nb * 8 + 2 * c + (j & 1);
-#pragma unroll
-            for (int m = 0; m < kMB; ++m)
-              if (m == bat) acc[0][nb][h][j] += corr[m][2 * h + (j >> 1)];
-          }
-    }
-  }
-
   // Fragment register j of mma half h: model 2h + (j>>1), batch 8nb+2c+(j&1);
   // feature-in-tile g (NK) or 4g + t (KN).
   __device__ __forceinline__ void write_partial(float* slot, int M) {
-    fold_corr();
 #pragma unroll
     for (int t = 0; t < kT; ++t) {
       const int fi = NK ? pr : 4 * g + t;
@@ -336,7 +249,6 @@ struct QuadOp {
   }
 
   __device__ __forceinline__ void store_tile(int tile) {
-    fold_corr();
 #pragma unroll
     for (int t = 0; t < kT; ++t) {
       const int f = tile * kTileW + (NK ? pr : 4 * g + t);
@@ -354,6 +266,7 @@ struct QuadOp {
   }
 
   __device__ __forceinline__ void store(int model, int bat, int f, float v) const {
+    if (p.corr) v += __ldg(p.corr + ((int64_t)model * Mv + bat) * Nv + f);
     p.out[model][(int64_t)bat * p.ldo_m + (int64_t)f * p.ldo_n] = __float2half_rn(v * p.scale[model]);
   }
 };
@@ -375,16 +288,16 @@ inline QuadSmem quad_smem(bool nk, int nb, int64_t M, int stages) {
   return m;
 }
 
-template <bool NK, int NB, int MB, bool DIRECT>
+template <bool NK, int NB, bool DIRECT>
 __device__ __forceinline__ void quad_body(const QuadParams& p, uint32_t base, uint32_t ring, uint32_t bars,
                                           float* red, int* s_flag) {
-  QuadOp<NK, NB, MB, DIRECT> op(p, base);
+  QuadOp<NK, NB, DIRECT> op(p, base);
   run_partition_tma(op, p.part, red, s_flag, ring, bars, p.stages, p.part.counters + (kMaxGrid - 1));
 }
 
 // No static shared memory: the dynamic region then starts at shared address
 // 0 on current drivers, a 64 KiB boundary, which enables DIRECT addressing.
-template <bool NK, int NB, int MB>
+template <bool NK, int NB>
 __global__ void __launch_bounds__(quad_warps(NK, NB) * 32, 1) quad_gemv_kernel(const __grid_constant__ QuadParams p) {
   constexpr int NW = quad_warps(NK, NB);
   const uint32_t base = (uint32_t)__cvta_generic_to_shared(pp_smem);
@@ -399,8 +312,8 @@ __global__ void __launch_bounds__(quad_warps(NK, NB) * 32, 1) quad_gemv_kernel(c
   build_quad_lut(pp_smem, reinterpret_cast<uint32_t*>(red), p.luts);
   __syncthreads();
   // tables on a 64 KiB boundary: gather addresses come straight from PRMT
-  if ((base & 0xFFFFu) == 0) quad_body<NK, NB, MB, true>(p, base, ring, bars, red, s_flag);
-  else quad_body<NK, NB, MB, false>(p, base, ring, bars, red, s_flag);
+  if ((base & 0xFFFFu) == 0) quad_body<NK, NB, true>(p, base, ring, bars, red, s_flag);
+  else quad_body<NK, NB, false>(p, base, ring, bars, red, s_flag);
 }
 
 // Generic fallback for layouts the vector paths do not take (unaligned or
@@ -463,9 +376,9 @@ PartitionPlan quad_plan(bool nk, int64_t Mc, int64_t N, int64_t K, int sms) {
 bool g_attr_done[8][64];
 int g_attr_limit[8][64];
 
-template <bool NK, int NB, int MB>
+template <bool NK, int NB>
 int launch_quad(QuadParams& prm, int grid, int idx, cudaStream_t s) {
-  auto kern = quad_gemv_kernel<NK, NB, MB>;
+  auto kern = quad_gemv_kernel<NK, NB>;
   int max_smem = 0;
   int rc = ensure_smem_attr(kern, g_attr_done[idx], g_attr_limit[idx], &max_smem);
   if (rc) return rc;
@@ -482,22 +395,18 @@ int launch_quad(QuadParams& prm, int grid, int idx, cudaStream_t s) {
   return check_launch("quad_gemv_kernel");
 }
 
-int launch_plan(const PartitionPlan& pl, bool nk, int64_t Mc, QuadParams prm, void* ws, bool plug,
+// Workspace: [counter block 4 KiB][plug correction 4 x 16 x N floats][partial slots]
+inline size_t corr_bytes(int64_t N) { return align_up((size_t)4 * 16 * N * sizeof(float), 256); }
+
+int launch_plan(const PartitionPlan& pl, bool nk, int64_t Mc, QuadParams prm, void* ws, size_t corr_sz,
                 cudaStream_t s) {
   prm.part.units = (int)pl.units;
   prm.part.upt = (int)pl.upt;
   prm.part.counters = reinterpret_cast<int*>(ws);
-  prm.part.slots = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(ws) + pl.counters_bytes);
+  prm.part.slots = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(ws) + pl.counters_bytes + corr_sz);
   const int nb = Mc > 8 ? 2 : 1;
-  if (nk) {
-    if (plug) {
-      if (Mc == 1) return launch_quad<true, 1, 1>(prm, pl.grid, 0, s);
-      if (Mc <= 8) return launch_quad<true, 1, 8>(prm, pl.grid, 1, s);
-      return launch_quad<true, 2, 16>(prm, pl.grid, 2, s);
-    }
-    return nb == 1 ? launch_quad<true, 1, 0>(prm, pl.grid, 3, s) : launch_quad<true, 2, 0>(prm, pl.grid, 4, s);
-  }
-  return nb == 1 ? launch_quad<false, 1, 0>(prm, pl.grid, 5, s) : launch_quad<false, 2, 0>(prm, pl.grid, 6, s);
+  if (nk) return nb == 1 ? launch_quad<true, 1>(prm, pl.grid, 0, s) : launch_quad<true, 2>(prm, pl.grid, 1, s);
+  return nb == 1 ? launch_quad<false, 1>(prm, pl.grid, 2, s) : launch_quad<false, 2>(prm, pl.grid, 3, s);
 }
 
 bool quad_vector_ok(bool nk, const uint32_t* codes, int64_t ldc_k, int64_t ldc_n, int64_t N, int64_t K) {
@@ -533,11 +442,11 @@ int check_common(const void* const luts[7], const float scales[4], void* const o
   return PP_OK;
 }
 
-size_t quad_ws_bytes(bool nk, int64_t M, int64_t N, int64_t K) {
+size_t quad_ws_bytes(bool nk, int64_t M, int64_t N, int64_t K, bool plug) {
   const int sms = device_sm_count(current_device());
   const int64_t Mc = M < 16 ? M : 16;
   if (Mc <= 0) return 0;
-  return quad_plan(nk, Mc, N, K, sms > 0 ? sms : 148).total();
+  return quad_plan(nk, Mc, N, K, sms > 0 ? sms : 148).total() + (plug ? corr_bytes(N) : 0);
 }
 
 }  // namespace
@@ -619,11 +528,6 @@ static int quad_run(const void* a, int64_t lda_m, int64_t lda_k, const uint32_t*
   prm.ldo_n = ldo_n;
   prm.N = (int)N;
   prm.K = (int)K;
-  prm.plug_idx = plug_idx;
-  prm.plug_vals = reinterpret_cast<const uint2*>(plug_vals);
-  prm.wbase = wbase;
-  prm.base_lo32 = base_lo32;
-  prm.W = (int)cdiv(K, 64);
   if (cdiv(N, nk ? 8 : 32) * cdiv(K, nk ? 64 : 16) >= (int64_t)INT32_MAX) {
     set_error("matrix too large for one launch (more than 2^31 work units)");
     return PP_ERR_INVALID;
@@ -632,11 +536,13 @@ static int quad_run(const void* a, int64_t lda_m, int64_t lda_k, const uint32_t*
   if ((rc = nk ? encode_tmap_u32_2d(&prm.tmap, codes, (uint64_t)K, (uint64_t)N, (uint64_t)ldc_n * 4, 32, 8)
                : encode_tmap_u32_2d(&prm.tmap, codes, (uint64_t)N, (uint64_t)K, (uint64_t)ldc_k * 4, 32, 16)))
     return rc;
-  const size_t need = quad_plan(nk, M < 16 ? M : 16, N, K, sms).total();
+  const size_t csz = plug ? corr_bytes(N) : 0;
+  const size_t need = quad_plan(nk, M < 16 ? M : 16, N, K, sms).total() + csz;
   if (ws_bytes < need || (need && !ws) || !aligned(ws, 256)) {
     set_error("workspace of %zu bytes (256-byte aligned, zero-filled) required, got %zu", need, ws_bytes);
     return PP_ERR_WORKSPACE;
   }
+  float* corr = plug ? reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(ws) + kCounterBytes) : nullptr;
   // batch rows in chunks of 16: each chunk is one launch over the codes
   for (int64_t m0 = 0; m0 < M; m0 += 16) {
     const int64_t Mc = (M - m0) < 16 ? (M - m0) : 16;
@@ -645,7 +551,13 @@ static int quad_run(const void* a, int64_t lda_m, int64_t lda_k, const uint32_t*
     for (int i = 0; i < 4; ++i) prm.out[i] = reinterpret_cast<__half*>(out[i]) + m0 * ldo_m;
     prm.M = (int)Mc;
     prm.xvec = 1;
-    if ((rc = launch_plan(pl, nk, Mc, prm, ws, plug, s))) return rc;
+    prm.corr = corr;
+    if (plug) {
+      PlugCorrParams cp{prm.x, lda_m, plug_idx, reinterpret_cast<const uint2*>(plug_vals), wbase, base_lo32,
+                        (int)Mc, (int)N, (int)K, (int)cdiv(K, 64), corr};
+      if ((rc = launch_plug_corr(cp, s))) return rc;
+    }
+    if ((rc = launch_plan(pl, nk, Mc, prm, ws, csz, s))) return rc;
   }
   return PP_OK;
 }
@@ -661,7 +573,7 @@ int pp_quad_gemm_workspace_bytes(int64_t M, int64_t N, int64_t K, int64_t ldc_k,
     return PP_ERR_INVALID;
   }
   const bool nk = ldc_k == 1 && ldc_n != 1;
-  *bytes = pp::quad_ws_bytes(nk, M, N, K);
+  *bytes = pp::quad_ws_bytes(nk, M, N, K, false);
   return PP_OK;
 }
 
@@ -679,7 +591,7 @@ int pp_quad_linear_workspace_bytes(int64_t M, int64_t N, int64_t K, size_t* byte
     pp::set_error("invalid arguments");
     return PP_ERR_INVALID;
   }
-  *bytes = pp::quad_ws_bytes(true, M, N, K);
+  *bytes = pp::quad_ws_bytes(true, M, N, K, true);
   return PP_OK;
 }
 
