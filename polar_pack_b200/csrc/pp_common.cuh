@@ -58,6 +58,14 @@ __device__ __forceinline__ void fence_mbar_init() {
   asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
 }
 
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+
+__device__ __forceinline__ void prefetch_tmap(const void* tmap) {
+  asm volatile("prefetch.tensormap [%0];" ::"l"(tmap) : "memory");
+}
+
 __device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
   asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
 }
@@ -74,11 +82,12 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
 
 // Waits for phase `parity` of the barrier, giving up after a bounded number
 // of polls (each try_wait already suspends for a while): on timeout the
-// status word is set and the caller proceeds, so the kernel always ends.
-__device__ __forceinline__ void mbar_wait_bounded(uint32_t bar, uint32_t parity, int* status) {
+// status word is set and false is returned, so the kernel always ends.
+__device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity, int* status) {
   for (int i = 0; i < (1 << 21); ++i)
-    if (mbar_try_wait(bar, parity)) return;
+    if (mbar_try_wait(bar, parity)) return true;
   atomicExch(status, 1);
+  return false;
 }
 
 // 2D tiled TMA load (no multicast) completing on `bar`.  x is the innermost
@@ -119,24 +128,53 @@ __device__ __forceinline__ uint32_t lut_off(int table) {
   return (uint32_t)(table >> 1) * 65536u + (uint32_t)(table & 1) * 128u;
 }
 
-// Fill the replicated quad tables from the seven FP16[256] tables.  The
-// 1024 source words are first gathered into `stage` (4 KiB of shared memory,
-// all global loads in flight at once), then fanned out to 32 lane copies.
-// Called by every thread of the CTA; caller syncs afterwards.
-__device__ __forceinline__ void build_quad_lut(uint8_t* lut, uint32_t* stage, const __half* const* luts) {
-  for (int i = threadIdx.x; i < 1024; i += blockDim.x) {
-    const int t = i >> 8, e = i & 255;
-    const uint16_t* a = reinterpret_cast<const uint16_t*>(luts[t == 0 ? 0 : 2 * t - 1]);
-    const uint16_t* b = reinterpret_cast<const uint16_t*>(luts[t == 0 ? 0 : 2 * t]);
-    stage[i] = (uint32_t)ldg_u16(a + e) | ((uint32_t)ldg_u16(b + e) << 16);
+// Fill the replicated quad tables from the seven FP16[256] tables in three
+// steps: every thread loads its share of the 1024 table words into
+// registers (all global loads of a thread in flight at once; blockDim.x >=
+// 128), stores them to `stage` (4 KiB of shared memory), and after a CTA
+// barrier the words fan out to the 32 lane copies with 16-byte stores,
+// eight consecutive threads per 128-byte entry row.
+constexpr int kLutWordsPerThread = 8;
+
+__device__ __forceinline__ void quad_lut_load(uint32_t (&v)[kLutWordsPerThread], const __half* const* luts) {
+#pragma unroll
+  for (int j = 0; j < kLutWordsPerThread; ++j) {
+    const int i = threadIdx.x + j * (int)blockDim.x;
+    v[j] = 0u;
+    if (i < 1024) {
+      const int t = i >> 8, e = i & 255;
+      const uint16_t* lo = reinterpret_cast<const uint16_t*>(luts[t == 0 ? 0 : 2 * t - 1]);
+      const uint16_t* hi = reinterpret_cast<const uint16_t*>(luts[t == 0 ? 0 : 2 * t]);
+      v[j] = (uint32_t)ldg_u16(lo + e) | ((uint32_t)ldg_u16(hi + e) << 16);
+    }
   }
-  __syncthreads();
+}
+
+__device__ __forceinline__ void quad_lut_stage(uint32_t* stage, const uint32_t (&v)[kLutWordsPerThread]) {
+#pragma unroll
+  for (int j = 0; j < kLutWordsPerThread; ++j) {
+    const int i = threadIdx.x + j * (int)blockDim.x;
+    if (i < 1024) stage[i] = v[j];
+  }
+}
+
+// after a barrier that follows quad_lut_stage
+__device__ __forceinline__ void quad_lut_fanout(uint8_t* lut, const uint32_t* stage) {
   for (int idx = threadIdx.x; idx < 4 * 256 * 8; idx += blockDim.x) {
     const int t = idx >> 11, e = (idx >> 3) & 255, part = idx & 7;
-    const uint32_t v = stage[idx >> 3];
+    const uint32_t w = stage[idx >> 3];
     *reinterpret_cast<uint4*>(lut + lut_off(t) + (uint32_t)e * 256u + (uint32_t)part * 16u) =
-        make_uint4(v, v, v, v);
+        make_uint4(w, w, w, w);
   }
+}
+
+// All three steps; called by every thread of the CTA, caller syncs after.
+__device__ __forceinline__ void build_quad_lut(uint8_t* lut, uint32_t* stage, const __half* const* luts) {
+  uint32_t v[kLutWordsPerThread];
+  quad_lut_load(v, luts);
+  quad_lut_stage(stage, v);
+  __syncthreads();
+  quad_lut_fanout(lut, stage);
 }
 
 // Decoded tuple as three half2 words:
@@ -147,24 +185,12 @@ struct QuadDec {
   uint32_t p1, p2, p3;
 };
 
-// Shared-memory placement of the quad tables.  DIRECT: the first 64 KiB
-// boundary at or after the dynamic shared memory base.  With the tables
-// there, __byte_perm(code, lanebase, 0x76b4) -- code byte b in bits 8..15,
-// the lane offset in bits 0..7, the 64 KiB-aligned table address in bits
-// 16..31 -- is the complete shared address of a gather, and the table
-// offsets (+128, +65536, +65664) are load immediates: no add per gather.
-// Otherwise the tables start at the base and each gather adds it.
-// The host requests kQuadLutBytes (+ 65536 of alignment slack if DIRECT)
-// plus the partial-slot bytes, which follow the tables.
-template <bool DIRECT>
-__device__ __forceinline__ uint32_t quad_lut_saddr() {
-  const uint32_t base = (uint32_t)__cvta_generic_to_shared(pp_smem);
-  return DIRECT ? ((base + 0xFFFFu) & ~0xFFFFu) : base;
-}
-
-__device__ __forceinline__ uint8_t* quad_lut_ptr(uint32_t lut_saddr) {
-  return pp_smem + (lut_saddr - (uint32_t)__cvta_generic_to_shared(pp_smem));
-}
+// Shared-memory placement of the quad tables.  DIRECT: the tables start at
+// a 64 KiB boundary.  Then __byte_perm(code, lb, 0x7634) -- code byte 3 in
+// bits 8..15, the lane offset in bits 0..7, the 64 KiB-aligned region
+// address in bits 16..31 -- is the complete shared address of a gather,
+// and the second table of a region (+128) is a load immediate: no add per
+// gather.  Otherwise each gather adds the table base.
 
 template <int OFF>
 __device__ __forceinline__ uint32_t lds_off(uint32_t saddr) {
@@ -173,18 +199,20 @@ __device__ __forceinline__ uint32_t lds_off(uint32_t saddr) {
   return v;
 }
 
-// DIRECT: lanebase = lut_saddr | (4 * lane), lut_add = 0.
-// Otherwise lanebase = 4 * lane and lut_add = lut_saddr.
+// DIRECT: lb0 = lut_saddr | (4 * lane) and lb1 = (lut_saddr + 65536) |
+// (4 * lane) address the two 64 KiB table regions, add0 = add1 = 0.
+// Otherwise lb0 = lb1 = 4 * lane, add0 = lut_saddr, add1 = lut_saddr + 65536.
 template <bool DIRECT>
-__device__ __forceinline__ QuadDec decode_quad(uint32_t code, uint32_t lanebase, uint32_t lut_add) {
-  const uint32_t a0 = __byte_perm(code, lanebase, 0x7634) + (DIRECT ? 0u : lut_add);  // norm (byte 3)
-  const uint32_t a1 = __byte_perm(code, lanebase, 0x7624) + (DIRECT ? 0u : lut_add);  // t1   (byte 2)
-  const uint32_t a2 = __byte_perm(code, lanebase, 0x7614) + (DIRECT ? 0u : lut_add);  // t2   (byte 1)
-  const uint32_t a3 = __byte_perm(code, lanebase, 0x7604) + (DIRECT ? 0u : lut_add);  // t3   (byte 0)
+__device__ __forceinline__ QuadDec decode_quad(uint32_t code, uint32_t lb0, uint32_t lb1, uint32_t add0,
+                                               uint32_t add1) {
+  const uint32_t a0 = __byte_perm(code, lb0, 0x7634) + (DIRECT ? 0u : add0);  // norm (byte 3)
+  const uint32_t a1 = __byte_perm(code, lb0, 0x7624) + (DIRECT ? 0u : add0);  // t1   (byte 2)
+  const uint32_t a2 = __byte_perm(code, lb1, 0x7614) + (DIRECT ? 0u : add1);  // t2   (byte 1)
+  const uint32_t a3 = __byte_perm(code, lb1, 0x7604) + (DIRECT ? 0u : add1);  // t3   (byte 0)
   const uint32_t rr = lds_off<0>(a0);
   const uint32_t cs1 = lds_off<128>(a1);
-  const uint32_t cs2 = lds_off<65536>(a2);
-  const uint32_t cs3 = lds_off<65536 + 128>(a3);
+  const uint32_t cs2 = lds_off<0>(a2);
+  const uint32_t cs3 = lds_off<128>(a3);
   const __half2 p1 = __hmul2_rn(u2h(rr), u2h(cs1));                // (r*c1, r*s1)
   const __half2 p2 = __hmul2_rn(__high2half2(p1), u2h(cs2));       // (rs*c2, rs*s2)
   const __half2 p3 = __hmul2_rn(__high2half2(p2), u2h(cs3));       // (rss*c3, rss*s3)

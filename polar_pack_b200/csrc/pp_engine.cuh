@@ -17,9 +17,11 @@
 // and resets the counter.  No thread ever waits for another CTA, and the
 // summation order is fixed, so results are deterministic.
 //
-// Each warp keeps one unit in flight in registers (loaded before the
-// current unit is decoded) and bulk-prefetches the unit kPrefetch steps
-// ahead into L2.
+// Two streaming engines share this partition: a register engine (each warp
+// keeps one unit in flight in registers, prefetches ahead into L2 and
+// reduces split tiles after a CTA barrier) and a TMA engine (each warp
+// refills its own shared-memory ring and reduces split tiles at warp
+// level, described below).
 #pragma once
 
 #include <stdint.h>
@@ -74,7 +76,7 @@ __device__ __forceinline__ void reduce_partials(Op& op, const Partition& pt, con
     const bool cta_whole = a >= cu0 && b <= cu1;
     if (one_warp && cta_whole) continue;  // stored by its warp
     float* slot = pt.slots + ((int64_t)blockIdx.x * 2 + (tt == ct0 ? 0 : 1)) * (int64_t)nval;
-    for (int e = tid; e < nval; e += NW * 32) {
+    for (int e = tid; e < nval; e += (int)blockDim.x) {
       float s = 0.f;
       for (int w = w_first; w <= w_last; ++w) {
         const int ws0 = cu0 + range_start(R, NW, w);
@@ -107,7 +109,7 @@ __device__ __forceinline__ void reduce_partials(Op& op, const Partition& pt, con
     __syncthreads();
     if (*s_flag) {
       __threadfence();
-      for (int e = tid; e < nval; e += NW * 32) {
+      for (int e = tid; e < nval; e += (int)blockDim.x) {
         float s = 0.f;
         for (int c = c_first; c <= c_last; ++c) {
           // only the first contributor can have started before the tile
@@ -201,79 +203,230 @@ __device__ __forceinline__ void run_partition(Op& op, const Partition& pt, float
   reduce_partials(op, pt, red, s_flag, cu0, cu1, nval);
 }
 
-// TMA engine: same partition and reduction, but each warp streams its range
-// through a private ring of S shared-memory slots filled by TMA.  Lane 0
-// keeps the next S units of the warp's range in flight (one mbarrier per
-// slot, phase = fill count & 1); all lanes wait for the slot, copy the unit
-// into registers, sync, and lane 0 refills the slot with the unit S ahead
-// before the unit is decoded.  Waits are bounded (mbar_wait_bounded).
+// ------------------------------------------------------------ TMA engine --
+// Each warp streams its unit range through a private ring of S shared-memory
+// slots filled by TMA, one mbarrier per slot (one arrival plus the
+// transaction bytes of the copy).  Before the CTA builds its tables, lane 0
+// initialises the ring and issues the first S units, so those copies are in
+// flight during the build.  In the loop all lanes wait for the slot, copy
+// the unit into registers and sync; lane 0 refills the slot with the unit S
+// ahead before the unit is decoded.  Every wait is bounded
+// (mbar_wait_bounded); after a timeout the status word is set and the warp
+// stops streaming, so the kernel always ends.
 //
-// Op additions: kUnitBytes; void issue(uint32_t slot, uint32_t bar, int tile,
-// int kc) const (lane 0 only); void read(Buf&, uint32_t slot) const.
-template <class Op>
-__device__ __forceinline__ void run_partition_tma(Op& op, const Partition& pt, float* red, int* s_flag,
-                                                  uint32_t ring, uint32_t bars, int S, int* status) {
-  constexpr int NW = Op::kWarps;
-  const int tid = threadIdx.x;
-  const int warp = tid >> 5, lane = tid & 31;
-  const int U = pt.units;
-  const int G = gridDim.x;
-  const int cu0 = range_start(U, G, blockIdx.x), cu1 = range_start(U, G, blockIdx.x + 1);
-  if (cu0 >= cu1) return;  // uniform over the CTA
-  const int upt = pt.upt;
-  const int M = op.M();
-  const int nval = Op::kNOut * M * Op::kTileW;
-  const int R = cu1 - cu0;
-  const int wu0 = cu0 + range_start(R, NW, warp), wu1 = cu0 + range_start(R, NW, warp + 1);
-  const uint32_t my_ring = ring + (uint32_t)(warp * S * Op::kUnitBytes);
-  const uint32_t my_bar = bars + (uint32_t)(warp * S * 8);
+// Split tiles are reduced at warp level, with no CTA barrier after the
+// table build.  A warp's range is cut into up to three segments, processed
+// in this order: the part of its last tile when that tile continues into
+// the next warp (split tail), the part of its first tile when that tile is
+// shared with a neighbour (split head), then whole tiles.  Split tiles thus
+// finish early in every warp.  Ending a split tile, a warp writes its FP32
+// partial to its shared-memory slot (slot 0: the tile holding its first
+// unit, slot 1: the tile holding its last unit), fences and bumps the
+// tile's arrival counter; the warp that arrives last sums the partials of
+// all warps touching the tile, in warp order, and stores the tile if it
+// lies inside the CTA.  A tile cut by a CTA boundary (at most two per CTA)
+// then goes through the workspace: the same warp writes the CTA's sum to
+// the CTA's workspace slot, fences and bumps the tile's counter, and the
+// warp whose CTA arrives last sums all CTA slots in CTA order and stores
+// the tile.  No warp ever waits for another, and every sum has a fixed
+// order, so results are deterministic.
+//
+// Op additions: kUnitBytes; static void issue(const Params&, uint32_t slot,
+// uint32_t bar, int tile, int kc) (one lane); void read(Buf&, uint32_t
+// slot) const.
 
-  if (wu0 < wu1) {
-    if (lane == 0) {
-      for (int i = 0; i < S; ++i) mbar_init(my_bar + 8u * i, 1);
-      fence_mbar_init();
-    }
-    __syncwarp();
-    int t = wu0 / upt, kc = wu0 - t * upt;  // current unit
-    const int t_first = t;
-    int it = t, ikc = kc;                   // next unit to issue
-    for (int i = 0; i < S && wu0 + i < wu1; ++i) {
-      if (lane == 0) op.issue(my_ring + (uint32_t)(i * Op::kUnitBytes), my_bar + 8u * i, it, ikc);
-      if (++ikc == upt) { ikc = 0; ++it; }
-    }
-    int slot = 0;
-    uint32_t parity = 0;
-    op.zero();
-    op.begin(t, kc);
-    typename Op::Buf buf;
-    for (int u = wu0; u < wu1; ++u) {
-      const uint32_t sl = my_ring + (uint32_t)(slot * Op::kUnitBytes);
-      mbar_wait_bounded(my_bar + 8u * slot, parity, status);
-      op.read(buf, sl);
-      __syncwarp();
-      if (u + S < wu1) {
-        if (lane == 0) op.issue(sl, my_bar + 8u * slot, it, ikc);
-        if (++ikc == upt) { ikc = 0; ++it; }
-      }
-      if (++slot == S) { slot = 0; parity ^= 1u; }
-      int nt = t, nkc = kc + 1;
-      if (nkc == upt) { nkc = 0; ++nt; }
-      if (u + 1 < wu1) op.preload(nt, nkc);
-      op.compute(buf, t, kc);
-      if (nkc == 0 || u + 1 == wu1) {
-        if ((t * upt >= wu0) && nkc == 0) {
-          op.store_tile(t);
-        } else {
-          op.write_partial(red + (warp * 2 + (t == t_first ? 0 : 1)) * nval, M);
-        }
-        op.zero();
-      }
-      t = nt;
-      kc = nkc;
+// Per-CTA tables in shared memory, filled before the table-build barrier.
+struct CtaTables {
+  int* wstart;  // [NW + 1] warp range starts, wstart[NW] = end of the CTA range
+  int* wtile;   // [NW + 1] tile of wstart[w]
+  int* cnt;     // [2 * NW] split-tile arrival counters, indexed 2 * (first warp) + slot
+};
+
+template <int NW>
+__device__ __forceinline__ void cta_tables_init(const CtaTables& tb, int cu0, int cu1, int upt) {
+  const int i = threadIdx.x;
+  if (i <= NW) {
+    const int w0 = cu0 + range_start(cu1 - cu0, NW, i);
+    tb.wstart[i] = w0;
+    tb.wtile[i] = w0 / upt;
+  }
+  if (i < 2 * NW) tb.cnt[i] = 0;
+}
+
+// The unit order of one warp: segments [a0,b0) split tail, [a1,b1) split
+// head, [a2,b2) whole tiles (seg 3 = done).
+struct UnitSeq {
+  int a0, b0, a1, b1, a2, b2;
+  int seg, u, t, kc, upt;
+
+  __device__ __forceinline__ int seg_end() const { return seg == 0 ? b0 : seg == 1 ? b1 : b2; }
+
+  __device__ __forceinline__ void enter(int sg) {
+    seg = sg;
+    while (seg < 3 && (seg == 0 ? a0 == b0 : seg == 1 ? a1 == b1 : a2 == b2)) ++seg;
+    if (seg < 3) {
+      u = seg == 0 ? a0 : seg == 1 ? a1 : a2;
+      t = u / upt;
+      kc = u - t * upt;
     }
   }
-  __syncthreads();
-  reduce_partials(op, pt, red, s_flag, cu0, cu1, nval);
+
+  // non-empty range [wu0, wu1)
+  __device__ __forceinline__ void init(int wu0, int wu1, int upt_) {
+    upt = upt_;
+    const int tf = wu0 / upt, tl = (wu1 - 1) / upt;
+    const int hf = (tf + 1) * upt;
+    const bool head_whole = wu0 == tf * upt && wu1 >= hf;
+    const bool split_tail = tl > tf && wu1 < (tl + 1) * upt;
+    a0 = split_tail ? tl * upt : wu1;
+    b0 = wu1;
+    a1 = wu0;
+    b1 = head_whole ? wu0 : (wu1 < hf ? wu1 : hf);
+    a2 = b1;
+    b2 = split_tail ? tl * upt : wu1;
+    enter(0);
+  }
+
+  __device__ __forceinline__ void advance() {
+    ++u;
+    if (++kc == upt) {
+      kc = 0;
+      ++t;
+    }
+    if (u == seg_end()) enter(seg + 1);
+  }
+};
+
+struct TmaRing {
+  uint32_t ring, bars;  // this warp's S slots and S mbarriers
+  int S;
+  UnitSeq next;         // next unit to issue
+
+  // every lane advances the cursor; only `leader` issues
+  template <class Issue>
+  __device__ __forceinline__ void issue_next(const Issue& issue, int s, uint32_t unit, bool leader) {
+    if (leader) issue(ring + (uint32_t)s * unit, bars + 8u * (uint32_t)s, next.t, next.kc);
+    next.advance();
+  }
+
+  // lane 0: barriers and the first min(S, units) copies
+  template <class Issue>
+  __device__ __forceinline__ void prologue(const Issue& issue, uint32_t unit) {
+    for (int i = 0; i < S; ++i) mbar_init(bars + 8u * (uint32_t)i, 1);
+    fence_mbar_init();
+    for (int i = 0; i < S && next.seg < 3; ++i) issue_next(issue, i, unit, true);
+  }
+};
+
+// Ends split tile T of warp `warp` (slot `which`), see above.
+template <class Op>
+__device__ __forceinline__ void close_split(Op& op, const Partition& pt, const CtaTables& tb, float* red,
+                                            int warp, int T, int which, int cu0, int cu1) {
+  constexpr int NW = Op::kWarps;
+  constexpr int TW = Op::kTileW;
+  const int lane = threadIdx.x & 31;
+  const int upt = pt.upt;
+  const int M = op.M();
+  const int nval = Op::kNOut * M * TW;
+  op.write_partial(red + (warp * 2 + which) * nval, M);
+  const int x0 = T * upt > cu0 ? T * upt : cu0;                    // first unit of T in the CTA
+  const int x1 = T * upt + upt < cu1 ? T * upt + upt : cu1;        // end of T in the CTA
+  int wf = warp;
+  while (wf > 0 && tb.wstart[wf] > x0) --wf;                       // warp holding x0
+  int n = 0;
+  for (int w = wf; w < NW && tb.wstart[w] < x1; ++w) n += tb.wstart[w + 1] > tb.wstart[w] ? 1 : 0;
+  __syncwarp();
+  int last = 0;
+  if (lane == 0) {
+    __threadfence_block();
+    last = atomicAdd(tb.cnt + 2 * wf + (tb.wtile[wf] == T ? 0 : 1), 1) == n - 1;
+  }
+  last = __shfl_sync(0xffffffffu, last, 0);
+  if (!last) return;
+  __syncwarp();
+  __threadfence_block();
+  const bool inside = T * upt >= cu0 && T * upt + upt <= cu1;
+  float* gslot = pt.slots + ((int64_t)blockIdx.x * 2 + (T == tb.wtile[0] ? 0 : 1)) * (int64_t)nval;
+  for (int e = lane; e < nval; e += 32) {
+    float sum = 0.f;
+    for (int w = wf; w < NW && tb.wstart[w] < x1; ++w) {
+      if (tb.wstart[w + 1] == tb.wstart[w]) continue;
+      sum += red[(w * 2 + (tb.wtile[w] == T ? 0 : 1)) * nval + e];
+    }
+    if (inside) {
+      const int o = e / (M * TW);
+      const int rem = e - o * M * TW;
+      const int bat = rem / TW;
+      const int f = T * TW + (rem - bat * TW);
+      if (f < op.N()) op.store(o, bat, f, sum);
+    } else {
+      __stcg(gslot + e, sum);
+    }
+  }
+  if (inside) return;
+  // tile cut by a CTA boundary
+  const int U = pt.units, G = gridDim.x;
+  const int c_first = part_of_unit(T * upt, U, G);
+  const int c_last = part_of_unit(T * upt + upt - 1, U, G);
+  __threadfence();
+  __syncwarp();
+  int lastc = 0;
+  if (lane == 0) lastc = atomicAdd(pt.counters + c_last, 1) == c_last - c_first;
+  lastc = __shfl_sync(0xffffffffu, lastc, 0);
+  if (!lastc) return;
+  __threadfence();
+  for (int e = lane; e < nval; e += 32) {
+    float sum = 0.f;
+    for (int c = c_first; c <= c_last; ++c) {
+      // only the first contributor can have started before the tile
+      const int w = (c == c_first && range_start(U, G, c) < T * upt) ? 1 : 0;
+      sum += __ldcg(pt.slots + ((int64_t)c * 2 + w) * (int64_t)nval + e);
+    }
+    const int o = e / (M * TW);
+    const int rem = e - o * M * TW;
+    const int bat = rem / TW;
+    const int f = T * TW + (rem - bat * TW);
+    if (f < op.N()) op.store(o, bat, f, sum);
+  }
+  if (lane == 0) pt.counters[c_last] = 0;
+}
+
+// Streams the range [wu0, wu1) of warp `warp` (non-empty; the prologue ran
+// on lane 0, so the other lanes first replay its cursor advances).
+template <class Op, class Issue>
+__device__ __forceinline__ void tma_stream(Op& op, const Issue& issue, TmaRing& rg, const Partition& pt,
+                                           const CtaTables& tb, float* red, int warp, int wu0, int wu1,
+                                           int cu0, int cu1, int* status) {
+  const bool leader = (threadIdx.x & 31) == 0;
+  if (!leader)
+    for (int i = 0; i < rg.S && rg.next.seg < 3; ++i) rg.issue_next(issue, i, Op::kUnitBytes, false);
+  UnitSeq sq;
+  sq.init(wu0, wu1, pt.upt);
+  int s = 0;
+  uint32_t ph = 0;
+  op.zero();
+  typename Op::Buf buf;
+  while (sq.seg < 3) {
+    if (!mbar_wait_bounded(rg.bars + 8u * (uint32_t)s, ph, status)) break;
+    op.read(buf, rg.ring + (uint32_t)s * Op::kUnitBytes);
+    __syncwarp();
+    if (rg.next.seg < 3) rg.issue_next(issue, s, Op::kUnitBytes, leader);  // warp-uniform test
+    if (++s == rg.S) {
+      s = 0;
+      ph ^= 1u;
+    }
+    op.compute(buf, sq.t, sq.kc);
+    if (sq.seg == 2) {
+      if (sq.kc + 1 == pt.upt) {
+        op.store_tile(sq.t);
+        op.zero();
+      }
+    } else if (sq.u + 1 == sq.seg_end()) {
+      close_split(op, pt, tb, red, warp, sq.t, sq.seg == 0 ? 1 : 0, cu0, cu1);
+      op.zero();
+    }
+    sq.advance();
+  }
 }
 
 // Host-side partition sizing shared by the launchers.

@@ -42,6 +42,22 @@ int device_sm_count(int device) {
   return cache[device];
 }
 
+int reserved_smem(int device) {
+  static int cache[64];
+  static bool done[64];
+  if (device < 0 || device >= 64) return 0;
+  if (!done[device]) {
+    int r = 0;
+    if (cudaDeviceGetAttribute(&r, cudaDevAttrReservedSharedMemoryPerBlock, device) != cudaSuccess) {
+      cudaGetLastError();
+      r = 0;
+    }
+    cache[device] = r;
+    done[device] = true;
+  }
+  return cache[device];
+}
+
 typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);

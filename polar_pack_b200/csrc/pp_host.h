@@ -21,6 +21,11 @@ int check_launch(const char* what);
 int device_sm_count(int device);
 int current_device();
 
+// Shared memory the driver reserves at the start of every CTA's window
+// (the dynamic region of a kernel without static shared memory starts
+// there); 0 if the query fails.
+int reserved_smem(int device);
+
 // 2D tensor map over a row-major uint32 matrix (dim0 contiguous), box
 // box0 x box1, 128-byte swizzle, zero fill out of bounds.  Requires a
 // 16-byte aligned base, stride1_bytes % 16 == 0 and box0 * 4 <= 128.

@@ -25,17 +25,21 @@ struct QuadDecodeParams {
 };
 
 __global__ void __launch_bounds__(512, 1) quad_decode_kernel(const QuadDecodeParams p) {
-  const uint32_t lut_saddr = quad_lut_saddr<true>();
-  uint8_t* lut = quad_lut_ptr(lut_saddr);
+  // tables at the first 64 KiB boundary of the window (the host requests
+  // 64 KiB of slack), table stage right after them
+  const uint32_t base = (uint32_t)__cvta_generic_to_shared(pp_smem);
+  const uint32_t lut_saddr = (base + 0xFFFFu) & ~0xFFFFu;
+  uint8_t* lut = pp_smem + (lut_saddr - base);
   build_quad_lut(lut, reinterpret_cast<uint32_t*>(lut + kQuadLutBytes), p.luts);
   __syncthreads();
-  const uint32_t lanebase = lut_saddr | ((threadIdx.x & 31) * 4u);
+  const uint32_t lb0 = lut_saddr | ((threadIdx.x & 31) * 4u);
+  const uint32_t lb1 = (lut_saddr + 65536u) | ((threadIdx.x & 31) * 4u);
   const int64_t total = p.R * p.C;
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
        i += (int64_t)gridDim.x * blockDim.x) {
     const int64_t r = i / p.C, c = i - r * p.C;
     const uint32_t code = __ldg(p.codes + r * p.ldc_r + c * p.ldc_c);
-    const QuadDec d = decode_quad<true>(code, lanebase, 0u);
+    const QuadDec d = decode_quad<true>(code, lb0, lb1, 0u, 0u);
     __half w[4] = {__low2half(u2h(d.p1)), __low2half(u2h(d.p2)), __low2half(u2h(d.p3)),
                    __high2half(u2h(d.p3))};
     const int64_t o = r * p.ldo_r + c * p.ldo_c;

@@ -20,8 +20,11 @@
 #include "pp_common.cuh"
 #include "pp_engine.cuh"
 #include "pp_host.h"
+#include "quad_layout.h"
 
 namespace pp {
+
+static_assert(kQuadTableBytes == kQuadLutBytes, "table size shared with the layout planner");
 
 int zero_f16(void* p, int64_t R, int64_t C, int64_t ldr, int64_t ldc, cudaStream_t s);
 
@@ -58,8 +61,8 @@ struct QuadParams {
   // plug-table correction [4][M][N] FP32 added before the scale (NULL: none)
   const float* corr;
   Partition part;
-  int xvec;
-  int stages;  // TMA ring slots per warp
+  int stages;           // TMA ring slots per warp
+  uint32_t smem_bytes;  // dynamic shared memory of the launch
 };
 
 struct QuadBuf {
@@ -67,7 +70,7 @@ struct QuadBuf {
 };
 
 // NK: file layout.  DIRECT: tables at a 64 KiB-aligned shared address (see
-// quad_lut_saddr).
+// decode_quad).
 template <bool NK, int NB, bool DIRECT>
 struct QuadOp {
   static constexpr int kWarps = quad_warps(NK, NB);
@@ -81,7 +84,7 @@ struct QuadOp {
   const QuadParams& p;
   int g, c;
   int pr;  // NK: physical row of mma row g inside the 8-row tile (see read())
-  uint32_t lanebase, lut_add;
+  uint32_t lb0, lb1, add0, add1;  // table addressing (decode_quad)
   int Mv, Nv, Kv;
   int64_t ldc, ldx_m;
   const uint32_t* codes;
@@ -92,7 +95,9 @@ struct QuadOp {
   __device__ __forceinline__ QuadOp(const QuadParams& p_, uint32_t lut_saddr)
       : p(p_), g((threadIdx.x & 31) >> 2), c(threadIdx.x & 3),
         pr((((threadIdx.x & 31) >> 2) >> 1) | ((((threadIdx.x & 31) >> 2) & 1) << 2)),
-        lanebase((DIRECT ? lut_saddr : 0u) | ((threadIdx.x & 31) * 4u)), lut_add(DIRECT ? 0u : lut_saddr),
+        lb0((DIRECT ? lut_saddr : 0u) | ((threadIdx.x & 31) * 4u)),
+        lb1((DIRECT ? lut_saddr + 65536u : 0u) | ((threadIdx.x & 31) * 4u)), add0(DIRECT ? 0u : lut_saddr),
+        add1(DIRECT ? 0u : lut_saddr + 65536u),
         Mv(p_.M), Nv(p_.N), Kv(p_.K), ldc(p_.ldc), ldx_m(p_.ldx_m), codes(p_.codes), x(p_.x) {
 #pragma unroll
     for (int nb = 0; nb < NB; ++nb) {
@@ -118,16 +123,17 @@ struct QuadOp {
   __device__ __forceinline__ void begin(int, int) {}
   __device__ __forceinline__ void preload(int, int) {}
 
-  // One unit by TMA into a 2 KiB ring slot (lane 0 only).  NK: 8 rows x 64
-  // codes as two 8 x 32 boxes (128-byte rows, 128-byte swizzle); KN: 16 rows
-  // x 32 features, one box.  Out-of-range elements arrive as zeros.
-  __device__ __forceinline__ void issue(uint32_t slot, uint32_t bar, int tile, int kc) const {
+  // One unit by TMA into a 2 KiB ring slot (one lane).  NK: 8
+  // rows x 64 codes as two 8 x 32 boxes (128-byte rows, 128-byte swizzle);
+  // KN: 16 rows x 32 features, one box.  Out-of-range elements arrive as
+  // zeros.
+  static __device__ __forceinline__ void issue(const QuadParams& q, uint32_t slot, uint32_t bar, int tile, int kc) {
     mbar_expect_tx(bar, kUnitBytes);
     if constexpr (NK) {
-      tma_load_2d(slot, &p.tmap, kc * 64, tile * 8, bar);
-      tma_load_2d(slot + 1024u, &p.tmap, kc * 64 + 32, tile * 8, bar);
+      tma_load_2d(slot, &q.tmap, kc * 64, tile * 8, bar);
+      tma_load_2d(slot + 1024u, &q.tmap, kc * 64 + 32, tile * 8, bar);
     } else {
-      tma_load_2d(slot, &p.tmap, tile * 32, kc * 16, bar);
+      tma_load_2d(slot, &q.tmap, tile * 32, kc * 16, bar);
     }
   }
 
@@ -153,40 +159,48 @@ struct QuadOp {
   }
 
   // Activation fragments.  Batch columns >= M read row 0 (clamped): their
-  // mma output column is never stored.  Columns k >= K read as zero.
+  // mma output column is never stored.  FULL units lie wholly below K and
+  // load without checks; in the last K chunk, columns k >= K read as zero.
+  template <bool FULL>
   __device__ __forceinline__ uint32_t xpair(int nb, int k) const {
-    if (k + 1 < Kv) return ldg_u32(xrow[nb] + k);
+    if (FULL || k + 1 < Kv) return ldg_u32(xrow[nb] + k);
     return k < Kv ? (uint32_t)ldg_u16(xrow[nb] + k) : 0u;
   }
 
+  template <bool FULL>
   __device__ __forceinline__ uint2 xquad(int nb, int k) const {
     // activations (bat, k..k+3); the NK path guarantees K % 4 == 0
-    if (k < Kv) return ldg_u2(xrow[nb] + k);
+    if (FULL || k < Kv) return ldg_u2(xrow[nb] + k);
     return make_uint2(0u, 0u);
   }
 
   __device__ __forceinline__ void compute(const Buf& b, int tile, int kc) {
+    if (kc * (NK ? 64 : 16) + (NK ? 64 : 16) <= Kv) compute_unit<true>(b, kc);
+    else compute_unit<false>(b, kc);
+  }
+
+  template <bool FULL>
+  __device__ __forceinline__ void compute_unit(const Buf& b, int kc) {
     if constexpr (NK) {
       const int kbase = kc * 64;
-      const bool full_k = kbase + 64 <= Kv;
       uint2 xb[4][NB];
 #pragma unroll
       for (int s = 0; s < 4; ++s)
 #pragma unroll
-        for (int nb = 0; nb < NB; ++nb) xb[s][nb] = xquad(nb, kbase + 16 * s + 4 * c);
+        for (int nb = 0; nb < NB; ++nb) xb[s][nb] = xquad<FULL>(nb, kbase + 16 * s + 4 * c);
 #pragma unroll
       for (int s = 0; s < 4; ++s) {
         const int kp = kbase + 16 * s + 4 * c;
         QuadDec d[4];
-        d[0] = decode_quad<DIRECT>(b.q[s].x, lanebase, lut_add);
-        d[1] = decode_quad<DIRECT>(b.q[s].y, lanebase, lut_add);
-        d[2] = decode_quad<DIRECT>(b.q[s].z, lanebase, lut_add);
-        d[3] = decode_quad<DIRECT>(b.q[s].w, lanebase, lut_add);
+        d[0] = decode_quad<DIRECT>(b.q[s].x, lb0, lb1, add0, add1);
+        d[1] = decode_quad<DIRECT>(b.q[s].y, lb0, lb1, add0, add1);
+        d[2] = decode_quad<DIRECT>(b.q[s].z, lb0, lb1, add0, add1);
+        d[3] = decode_quad<DIRECT>(b.q[s].w, lb0, lb1, add0, add1);
         uint32_t a01[4] = {lo_pair(d[0].p1, d[1].p1), lo_pair(d[0].p2, d[1].p2),
                            lo_pair(d[2].p1, d[3].p1), lo_pair(d[2].p2, d[3].p2)};
         uint32_t a23[4] = {lo_pair(d[0].p3, d[1].p3), hi_pair(d[0].p3, d[1].p3),
                            lo_pair(d[2].p3, d[3].p3), hi_pair(d[2].p3, d[3].p3)};
-        if (!full_k && kp >= Kv) {
+        if (!FULL && kp >= Kv) {
 #pragma unroll
           for (int i = 0; i < 4; ++i) a01[i] = a23[i] = 0u;
         }
@@ -198,23 +212,22 @@ struct QuadOp {
       }
     } else {
       const int kbase = kc * 16;
-      const bool full_k = kbase + 16 <= Kv;
       uint32_t b0[NB], b1[NB];
 #pragma unroll
       for (int nb = 0; nb < NB; ++nb) {
-        b0[nb] = xpair(nb, kbase + 2 * c);
-        b1[nb] = xpair(nb, kbase + 2 * c + 8);
+        b0[nb] = xpair<FULL>(nb, kbase + 2 * c);
+        b1[nb] = xpair<FULL>(nb, kbase + 2 * c + 8);
       }
       bool rv[4];
 #pragma unroll
-      for (int r = 0; r < 4; ++r) rv[r] = full_k || (kbase + 2 * c + (r & 1) + 8 * (r >> 1) < Kv);
+      for (int r = 0; r < 4; ++r) rv[r] = FULL || (kbase + 2 * c + (r & 1) + 8 * (r >> 1) < Kv);
 #pragma unroll
       for (int t = 0; t < 4; ++t) {
         QuadDec d[4];
 #pragma unroll
         for (int r = 0; r < 4; ++r) {
           const uint32_t code = t == 0 ? b.q[r].x : t == 1 ? b.q[r].y : t == 2 ? b.q[r].z : b.q[r].w;
-          d[r] = decode_quad<DIRECT>(code, lanebase, lut_add);
+          d[r] = decode_quad<DIRECT>(code, lb0, lb1, add0, add1);
           if (!rv[r]) d[r] = QuadDec{0u, 0u, 0u};
         }
         const uint32_t a01[4] = {lo_pair(d[0].p1, d[1].p1), lo_pair(d[0].p2, d[1].p2),
@@ -271,49 +284,70 @@ struct QuadOp {
   }
 };
 
-// Dynamic shared memory: [tables 128 KiB][TMA ring][mbarriers][partial
-// slots (at least the 4 KiB the table build stages in)].
-struct QuadSmem {
-  size_t ring, bars, red, total;
-};
-
-inline QuadSmem quad_smem(bool nk, int nb, int64_t M, int stages) {
-  const int nw = quad_warps(nk, nb);
-  QuadSmem m;
-  m.ring = (size_t)nw * stages * 2048;
-  m.bars = align_up((size_t)nw * stages * 8, 1024);
-  const size_t r = red_bytes(nw, 4, M, nk ? 8 : 32);
-  m.red = r > 4096 ? r : 4096;
-  m.total = kQuadLutBytes + 1024 + m.ring + m.bars + m.red + 16;  // +1 KiB ring alignment, flag
-  return m;
-}
-
 template <bool NK, int NB, bool DIRECT>
-__device__ __forceinline__ void quad_body(const QuadParams& p, uint32_t base, uint32_t ring, uint32_t bars,
-                                          float* red, int* s_flag) {
-  QuadOp<NK, NB, DIRECT> op(p, base);
-  run_partition_tma(op, p.part, red, s_flag, ring, bars, p.stages, p.part.counters + (kMaxGrid - 1));
+__device__ __forceinline__ void quad_body(const QuadParams& p, const QuadLayout& L, TmaRing& rg,
+                                          const CtaTables& tb, int cu0, int cu1, int wu0, int wu1, int* status) {
+  using Op = QuadOp<NK, NB, DIRECT>;
+  const uint32_t base = (uint32_t)__cvta_generic_to_shared(pp_smem);
+  float* red = reinterpret_cast<float*>(pp_smem + (L.scratch - base));
+  Op op(p, L.lut);
+  tma_stream(op, [&](uint32_t slot, uint32_t bar, int tile, int kc) { Op::issue(p, slot, bar, tile, kc); }, rg,
+             p.part, tb, red, threadIdx.x >> 5, wu0, wu1, cu0, cu1, status);
 }
 
-// No static shared memory: the dynamic region then starts at shared address
-// 0 on current drivers, a 64 KiB boundary, which enables DIRECT addressing.
+// Partial-sum scratch of a CTA: two slots per warp.
+__host__ __device__ inline uint32_t quad_scratch_bytes(bool nk, int nb, int M) {
+  return (uint32_t)red_bytes(quad_warps(nk, nb), 4, M, nk ? 8 : 32);
+}
+
+// Before the first barrier: the per-CTA int tables and the table words
+// (loaded to registers, then staged).  Between the barriers lane 0 of every
+// warp initialises its ring and issues its first S units, whose copies
+// then overlap the fan-out of the tables.  After the second barrier every
+// warp streams and reduces on its own; there is no closing barrier.
 template <bool NK, int NB>
 __global__ void __launch_bounds__(quad_warps(NK, NB) * 32, 1) quad_gemv_kernel(const __grid_constant__ QuadParams p) {
   constexpr int NW = quad_warps(NK, NB);
   const uint32_t base = (uint32_t)__cvta_generic_to_shared(pp_smem);
-  // 128-byte swizzled TMA boxes need 1 KiB-aligned destinations
-  const uint32_t ring = (base + kQuadLutBytes + 1023u) & ~1023u;
-  const uint32_t ring_bytes = (uint32_t)(NW * p.stages * 2048);
-  const uint32_t bars = ring + ring_bytes;
-  const uint32_t bar_bytes = ((uint32_t)(NW * p.stages * 8) + 1023u) & ~1023u;
-  float* red = reinterpret_cast<float*>(pp_smem + (bars + bar_bytes - base));
-  const int red_floats = (int)(red_bytes(NW, 4, p.M, NK ? 8 : 32) / 4);
-  int* s_flag = reinterpret_cast<int*>(red + (red_floats > 1024 ? red_floats : 1024));
-  build_quad_lut(pp_smem, reinterpret_cast<uint32_t*>(red), p.luts);
+  int* status = p.part.counters + (kMaxGrid - 1);
+  const QuadLayout L = quad_layout(base, p.smem_bytes, NW, p.stages, quad_scratch_bytes(NK, NB, p.M), true);
+  if (!L.ok) {  // the host plans for this never to happen
+    if (threadIdx.x == 0) atomicExch(status, 2);
+    return;
+  }
+  const int U = p.part.units, G = gridDim.x;
+  const int cu0 = range_start(U, G, blockIdx.x), cu1 = range_start(U, G, blockIdx.x + 1);
+  if (cu0 >= cu1) return;  // uniform over the CTA
+  uint32_t v[kLutWordsPerThread];
+  quad_lut_load(v, p.luts);
+  int* ti = reinterpret_cast<int*>(pp_smem + (L.tables - base));
+  const CtaTables tb{ti, ti + (NW + 1), ti + 2 * (NW + 1)};
+  cta_tables_init<NW>(tb, cu0, cu1, p.part.upt);
+  const int warp = threadIdx.x >> 5;
+  const int R = cu1 - cu0;
+  const int wu0 = cu0 + range_start(R, NW, warp), wu1 = cu0 + range_start(R, NW, warp + 1);
+  TmaRing rg;
+  if (wu0 < wu1) {
+    const uint32_t rw = (uint32_t)p.stages * 2048u;
+    rg.ring = warp < L.splitw ? L.ringA + (uint32_t)warp * rw : L.ringB + (uint32_t)(warp - L.splitw) * rw;
+    rg.bars = L.bars + 8u * (uint32_t)(warp * p.stages);
+    rg.S = p.stages;
+    rg.next.init(wu0, wu1, p.part.upt);
+  }
+  uint32_t* stage = reinterpret_cast<uint32_t*>(pp_smem + (L.scratch - base));
+  quad_lut_stage(stage, v);
   __syncthreads();
-  // tables on a 64 KiB boundary: gather addresses come straight from PRMT
-  if ((base & 0xFFFFu) == 0) quad_body<NK, NB, true>(p, base, ring, bars, red, s_flag);
-  else quad_body<NK, NB, false>(p, base, ring, bars, red, s_flag);
+  if (wu0 < wu1 && (threadIdx.x & 31) == 0) {
+    if (warp == 0) prefetch_tmap(&p.tmap);
+    rg.prologue([&](uint32_t slot, uint32_t bar, int tile, int kc) {
+      QuadOp<NK, NB, false>::issue(p, slot, bar, tile, kc);
+    }, 2048u);
+  }
+  quad_lut_fanout(pp_smem + (L.lut - base), stage);
+  __syncthreads();
+  if (wu0 >= wu1) return;
+  if (L.direct) quad_body<NK, NB, true>(p, L, rg, tb, cu0, cu1, wu0, wu1, status);
+  else quad_body<NK, NB, false>(p, L, rg, tb, cu0, cu1, wu0, wu1, status);
 }
 
 // Generic fallback for layouts the vector paths do not take (unaligned or
@@ -376,22 +410,37 @@ PartitionPlan quad_plan(bool nk, int64_t Mc, int64_t N, int64_t K, int sms) {
 bool g_attr_done[8][64];
 int g_attr_limit[8][64];
 
+// Deepest ring (up to 4 slots per consumer) with the tables at a 64 KiB
+// boundary for a dynamic region at the reserved-memory offset, else the
+// deepest that fits with the tables at the base.  Both must also fit with
+// the tables at the base, which the kernel falls back to if the runtime
+// base differs.  Returns 0 if nothing fits.
+int quad_stages(int nw, uint32_t redb, uint32_t reserved, uint32_t size) {
+  int plain = 0;
+  for (int S = 4; S >= 1; --S) {
+    if (!quad_layout(reserved, size, nw, S, redb, false).ok) continue;
+    if (!plain) plain = S;
+    if (S >= 2 && quad_layout(reserved, size, nw, S, redb, true).direct) return S;
+  }
+  return plain;
+}
+
 template <bool NK, int NB>
 int launch_quad(QuadParams& prm, int grid, int idx, cudaStream_t s) {
+  constexpr int NW = quad_warps(NK, NB);
   auto kern = quad_gemv_kernel<NK, NB>;
   int max_smem = 0;
   int rc = ensure_smem_attr(kern, g_attr_done[idx], g_attr_limit[idx], &max_smem);
   if (rc) return rc;
-  // deepest TMA ring (up to 4 slots per warp) that fits
-  int stages = 4;
-  while (stages > 1 && quad_smem(NK, NB, prm.M, stages).total > (size_t)max_smem) --stages;
-  const QuadSmem sm = quad_smem(NK, NB, prm.M, stages);
-  if (sm.total > (size_t)max_smem) {
-    set_error("shared memory plan of %zu bytes exceeds the per-CTA limit %d", sm.total, max_smem);
+  const uint32_t redb = quad_scratch_bytes(NK, NB, prm.M);
+  const int stages = quad_stages(NW, redb, (uint32_t)reserved_smem(current_device()), (uint32_t)max_smem);
+  if (stages == 0) {
+    set_error("no shared memory layout fits the per-CTA limit %d", max_smem);
     return PP_ERR_INVALID;
   }
   prm.stages = stages;
-  kern<<<grid, quad_warps(NK, NB) * 32, sm.total, s>>>(prm);
+  prm.smem_bytes = (uint32_t)max_smem;
+  kern<<<grid, NW * 32, (size_t)max_smem, s>>>(prm);
   return check_launch("quad_gemv_kernel");
 }
 
@@ -550,7 +599,6 @@ static int quad_run(const void* a, int64_t lda_m, int64_t lda_k, const uint32_t*
     prm.x = reinterpret_cast<const __half*>(a) + m0 * lda_m;
     for (int i = 0; i < 4; ++i) prm.out[i] = reinterpret_cast<__half*>(out[i]) + m0 * ldo_m;
     prm.M = (int)Mc;
-    prm.xvec = 1;
     prm.corr = corr;
     if (plug) {
       PlugCorrParams cp{prm.x, lda_m, plug_idx, reinterpret_cast<const uint2*>(plug_vals), wbase, base_lo32,

@@ -95,3 +95,115 @@ def test_partition_covers_every_unit_once(upt, NW):
         for G in sorted({1, 2, 3, min(148, want), min(148, U)}):
             if G <= U:
                 simulate(U, upt, G, NW)
+
+
+# ---------------------------------------------------------------- TMA engine
+# Model of the TMA engine's warp-level protocol (csrc/pp_engine.cuh:
+# UnitSeq, close_split, cta_tables_init): unit order per warp, split-tile
+# arrival counters by first toucher, sums in warp order, the cross-CTA
+# workspace protocol.
+class UnitSeq:
+    def __init__(self, wu0, wu1, upt):
+        tf, tl = wu0 // upt, (wu1 - 1) // upt
+        hf = (tf + 1) * upt
+        head_whole = wu0 == tf * upt and wu1 >= hf
+        split_tail = tl > tf and wu1 < (tl + 1) * upt
+        a0, b0 = (tl * upt if split_tail else wu1), wu1
+        a1, b1 = wu0, (wu0 if head_whole else min(wu1, hf))
+        a2, b2 = b1, (tl * upt if split_tail else wu1)
+        self.segs = [(a0, b0), (a1, b1), (a2, b2)]
+        self.upt = upt
+
+    def units(self):
+        for seg, (a, b) in enumerate(self.segs):
+            for u in range(a, b):
+                yield seg, u, u + 1 == b
+
+
+def simulate_tma(U, upt, G, NW):
+    tiles = U // upt
+    stores, gslots, counters = {}, {}, {}
+    for b in range(G):
+        cu0, cu1 = rs(U, G, b), rs(U, G, b + 1)
+        assert cu0 < cu1
+        R = cu1 - cu0
+        wstart = [cu0 + rs(R, NW, i) for i in range(NW + 1)]
+        wtile = [x // upt for x in wstart]
+        red, arrivals, closers = {}, {}, {}
+        for w in range(NW):
+            wu0, wu1 = wstart[w], wstart[w + 1]
+            if wu0 >= wu1:
+                continue
+            seen, acc = [], set()
+            for seg, u, seg_end in UnitSeq(wu0, wu1, upt).units():
+                seen.append(u)
+                acc.add(u)
+                t, kc = u // upt, u % upt
+                if seg == 2:
+                    if kc + 1 == upt:
+                        assert acc == set(range(t * upt, t * upt + upt))
+                        assert t not in stores
+                        stores[t] = acc
+                        acc = set()
+                elif seg_end:
+                    which = 1 if seg == 0 else 0
+                    assert (w, which) not in red
+                    red[(w, which)] = (t, acc)
+                    acc = set()
+                    x0, x1 = max(t * upt, cu0), min(t * upt + upt, cu1)
+                    wf = w
+                    while wf > 0 and wstart[wf] > x0:
+                        wf -= 1
+                    n, ww = 0, wf
+                    while ww < NW and wstart[ww] < x1:
+                        n += wstart[ww + 1] > wstart[ww]
+                        ww += 1
+                    idx = 2 * wf + (0 if wtile[wf] == t else 1)
+                    arrivals.setdefault(idx, []).append((t, n, wf, x1))
+            assert sorted(seen) == list(range(wu0, wu1))
+            assert acc == set()
+        # close every split tile (whoever is last sums the same slots)
+        for idx, arr in arrivals.items():
+            t, n, wf, x1 = arr[0]
+            assert all(a == arr[0] for a in arr), arr
+            assert len(arr) == n, (arr, n)
+            s, ww = set(), wf
+            while ww < NW and wstart[ww] < x1:
+                if wstart[ww + 1] > wstart[ww]:
+                    t_, part = red[(ww, 0 if wtile[ww] == t else 1)]
+                    assert t_ == t and not (s & part)
+                    s |= part
+                ww += 1
+            assert s == set(range(max(t * upt, cu0), min(t * upt + upt, cu1)))
+            if t * upt >= cu0 and t * upt + upt <= cu1:
+                assert t not in stores
+                stores[t] = s
+            else:
+                key = (b, 0 if t == wtile[0] else 1)
+                assert key not in gslots
+                gslots[key] = (t, s)
+                cf, cl = pou(t * upt, U, G), pou(t * upt + upt - 1, U, G)
+                counters.setdefault(cl, []).append((t, cf))
+    for cl, arr in counters.items():
+        t, cf = arr[0]
+        assert all(a == arr[0] for a in arr) and len(arr) == cl - cf + 1
+        tot = set()
+        for c in range(cf, cl + 1):
+            t_, s = gslots[(c, 1 if (c == cf and rs(U, G, c) < t * upt) else 0)]
+            assert t_ == t and not (tot & s)
+            tot |= s
+        assert t not in stores
+        stores[t] = tot
+    for t in range(tiles):
+        assert stores[t] == set(range(t * upt, t * upt + upt)), t
+
+
+@pytest.mark.parametrize("upt", [1, 2, 3, 5, 16, 32, 33, 172])
+@pytest.mark.parametrize("NW", [4, 8, 12, 16])
+def test_tma_engine_closes_every_tile_once(upt, NW):
+    for tiles in [1, 2, 3, 7, 32, 64, 257]:
+        U = upt * tiles
+        want = max(1, -(-U // (2 * NW)))
+        for G in sorted({1, 2, 3, min(148, want), min(148, U)}):
+            if G <= U:  # the host never plans more CTAs than units
+                simulate_tma(U, upt, G, NW)
