@@ -78,6 +78,24 @@ PP_API int pp_quad_gemm(const void* a, int64_t lda_m, int64_t lda_k,
                  int64_t M, int64_t N, int64_t K,
                  void* workspace, size_t workspace_bytes, void* stream);
 
+/* pp_quad_gemm with its split-K scratch in a file-scope device array of the
+ * library instead of a caller-provided workspace.  No counterpart in the
+ * reference (its Triton launch needs no scratch); it exists for callers that
+ * cannot call cudaMalloc: plugin hosts that pass only tensor pointers while
+ * their own pool owns all device memory, and code that must not allocate
+ * because cudaMalloc can synchronise the device.  It allocates nothing.
+ * Limit: 1 MiB of scratch per device (the file layout at any batch size; the
+ * kernel layout up to at least M = 6 on a 148-SM device); larger plans fail
+ * with PP_ERR_WORKSPACE before anything is enqueued.  All calls on a device
+ * share the one array: calls that can overlap (different streams or host
+ * threads) race on it and must be serialised by the caller.
+ */
+PP_API int pp_quad_gemm_static_scratch(const void* a, int64_t lda_m, int64_t lda_k,
+                                       const uint32_t* codes, int64_t ldc_k, int64_t ldc_n,
+                                       const void* const luts[7], const float scales[4],
+                                       void* const out[4], int64_t ldo_m, int64_t ldo_n,
+                                       int64_t M, int64_t N, int64_t K, void* stream);
+
 /* File-layout fused Linear with plug-table merge, the per-Linear decode of a
  * `.quadpack` stream (reference quaternion_packer.py:141-214: the codes of one
  * nn.Linear are (out=N, in=K) row-major at a flat stream offset; plug entries

@@ -35,6 +35,8 @@ _SIGNATURES = {
     "pp_quad_gemm_workspace_bytes": ([_i64, _i64, _i64, _i64, _i64, ctypes.POINTER(_size_t)], _int),
     "pp_quad_gemm": ([_c_void_p, _i64, _i64, _c_void_p, _i64, _i64, _PTR7, _F4, _PTR4, _i64, _i64,
                       _i64, _i64, _i64, _c_void_p, _size_t, _c_void_p], _int),
+    "pp_quad_gemm_static_scratch": ([_c_void_p, _i64, _i64, _c_void_p, _i64, _i64, _PTR7, _F4, _PTR4, _i64,
+                                     _i64, _i64, _i64, _i64, _c_void_p], _int),
     "pp_quad_linear_workspace_bytes": ([_i64, _i64, _i64, ctypes.POINTER(_size_t)], _int),
     "pp_quad_linear": ([_c_void_p, _i64, _i64, _c_void_p, _i64, _c_void_p, _c_void_p, _c_void_p, _u32,
                         _PTR7, _F4, _PTR4, _i64, _i64, _i64, _i64, _i64, _c_void_p, _size_t,
