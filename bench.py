@@ -6,15 +6,20 @@
 Workload: the quad-pack single-layer sweep -- four correlated synthetic models
 (base N(0,0.02) + delta N(0,0.002), 0.1% entries x20, FP16), packed into
 ``.quadpack`` v2 streams (plug cap 5%), Linear shapes in x out = 2048x2048,
-2048x11008, 11008x2048, 2048x256, batch 1.  One step = one fused kernel launch
-per shape (4 outputs per pass over the codes, plug table merged in-kernel).
+2048x11008, 11008x2048, 2048x256, batch 1.  One step = the four Linears
+(4 outputs per pass over the codes).
 R = 4 replica streams rotate step to step, so each step reads ~200 MB of
 codes that were last touched 3 steps (~600 MB) earlier: inputs exceed the
-126 MB L2 and no flush is needed.
+126 MB L2 and no flush is needed.  A Linear is two kernels: the CSR
+plug-table correction and the fused GEMV, which adds it before the scale.
+Kernels run with launch overlap (programmatic dependent launch: each may
+start its weight-only prologue while the previous one finishes), unless
+``--no-overlap``.
 
 Metric: packed-stream GB/s = algorithmic bytes / device time, where the
 bytes of one Linear are 4*N*K (codes) + 12*P (plug index + values) +
-2*M*K (activations) + 8*M*N (four FP16 outputs).
+2*M*K (activations) + 8*M*N (four FP16 outputs).  The roofline entry times
+the fused GEMV kernel alone (no plug table: 4*N*K + 2*M*K + 8*M*N bytes).
 
 With N > 1 GPUs (launched by torch.distributed.run) each Linear is
 row-sharded (column-parallel): rank r owns output rows [r*N/P, (r+1)*N/P),
@@ -178,6 +183,7 @@ def run_ours(args):
         dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=120))
 
     M = args.batch
+    _lib.set_launch_overlap(not args.no_overlap)
     streams = build_streams(torch, args.replicas, dev)
     sets = [layer_slices(s, SHAPES, rank, world) for s in streams]
     for s in streams:
@@ -323,7 +329,7 @@ def run_ours(args):
         e1.record(stream)
         torch.cuda.synchronize(dev)
         tj = e0.elapsed_time(e1) / (reps * len(sets))
-        bj = statistics.mean(layer_bytes(st[j].N, st[j].K, st[j].p_hi - st[j].p_lo, M) for st in sets)
+        bj = statistics.mean(layer_bytes(st[j].N, st[j].K, 0, M) for st in sets)  # the GEMV reads no plugs
         per_shape[f"{K}x{N}"] = {"us": round(tj * 1e3, 2), "GB/s": round(bj / (tj * 1e-3) / 1e9, 1)}
         kernel_bytes += bj
         kernel_ms += tj
@@ -343,13 +349,16 @@ def run_ours(args):
                    "bytes_per_step": int(per_step_bytes), "l2": "inputs per step ~200 MB > 126 MB L2, "
                    "4 rotating replica streams (no flush)",
                    "parallelism": f"row-sharded x{world} + NCCL all-gather" if world > 1 else "single GPU",
-                   "timing": "CUDA graph replay of whole steps" if use_graphs else "eager launches",
+                   "timing": ("CUDA graph replay of whole steps" if use_graphs else "eager launches") +
+                             ("; launch overlap on" if not args.no_overlap else ""),
                    "per_shape_gemv_kernel": per_shape},
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(achieved / peak, 4), "peak_source": f"{peak_kind} hbm_gbs",
                      "kernel": "quad_gemv_kernel<NK=1,NB=1> (file layout, batch 1)",
-                     "achieved_from": "bytes-weighted mean over the 4 shapes of per-launch CUDA-event time",
-                     "traffic": traffic},
+                     "achieved_from": "GEMV algorithmic bytes (4NK + 2MK + 8MN) over the 4 shapes / their "
+                                      "per-launch CUDA-event time (graph of back-to-back launches)",
+                     "traffic": traffic,
+                     "traffic_of": "one 2048x11008 launch (ncu dram read + write; profiles/quad_gemv_2048x11008.md)"},
         "e2e": e2e,
         "gpu_launches": launches_per_step * K_steps,
         "gpu_launches_note": "per Linear: the plug-correction kernel and the fused GEMV kernel",
@@ -575,6 +584,7 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--ref-fraction", type=float, default=1 / 32)
     ap.add_argument("--eager", action="store_true", help="time eager launches instead of CUDA graphs")
+    ap.add_argument("--no-overlap", action="store_true", help="launch kernels without programmatic overlap")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

@@ -52,6 +52,18 @@ PP_API int pp_version(void);
 /* Number of SMs of `device` (what the work partition is sized for). */
 PP_API int pp_device_sm_count(int device);
 
+/* Launch overlap (programmatic dependent launch), process-wide, off by
+ * default; returns the previous setting.  No counterpart in the reference.
+ * When on, pp_quad_gemm / pp_quad_linear kernels are launched so that they
+ * may start while the previous kernel of their stream is still running:
+ * they build their tables and start streaming codes, then wait for that
+ * kernel to complete before reading activations or writing anything.
+ * Contract while on: the codes, tables and plug arrays passed to those
+ * calls must not be written by the kernel launched immediately before them
+ * on the same stream (weights loaded earlier, as usual, are fine).
+ */
+PP_API int pp_set_launch_overlap(int enable);
+
 /* ------------------------------------------------------------------ quad --
  * Kernel-layout fused dequant GEMM, the drop-in for `quad_bitpacked`
  * (reference quad_kernels.py:146-159) and its Triton kernel

@@ -32,6 +32,7 @@ _SIGNATURES = {
     "pp_last_error": ([], ctypes.c_char_p),
     "pp_version": ([], _int),
     "pp_device_sm_count": ([_int], _int),
+    "pp_set_launch_overlap": ([_int], _int),
     "pp_quad_gemm_workspace_bytes": ([_i64, _i64, _i64, _i64, _i64, ctypes.POINTER(_size_t)], _int),
     "pp_quad_gemm": ([_c_void_p, _i64, _i64, _c_void_p, _i64, _i64, _PTR7, _F4, _PTR4, _i64, _i64,
                       _i64, _i64, _i64, _c_void_p, _size_t, _c_void_p], _int),
@@ -140,6 +141,16 @@ def require_cuda(*tensors) -> torch.device:
         elif t.device != dev:
             raise ValueError(f"tensors on different devices: {dev} and {t.device}")
     return dev
+
+
+def set_launch_overlap(enable: bool) -> bool:
+    """Programmatic dependent launch for the quad GEMV kernels (process-wide).
+
+    While on, the codes, tables and plug arrays of a call must not be
+    written by the kernel launched immediately before it on the same
+    stream.  Returns the previous setting.
+    """
+    return bool(load().pp_set_launch_overlap(1 if enable else 0))
 
 
 # ------------------------------------------------------------- workspace --

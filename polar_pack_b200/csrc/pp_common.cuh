@@ -43,10 +43,29 @@ __device__ __forceinline__ uint16_t ldg_u16(const void* p) {
   return __ldg(reinterpret_cast<const unsigned short*>(p));
 }
 
+// Coherent loads for data that the previous kernel of the stream may have
+// written while this one was already running (launch overlap): activations
+// and the plug correction.  The read-only path above is for weights only.
+__device__ __forceinline__ uint2 ld_u2(const void* p) { return *reinterpret_cast<const uint2*>(p); }
+__device__ __forceinline__ uint32_t ld_u32(const void* p) { return *reinterpret_cast<const uint32_t*>(p); }
+__device__ __forceinline__ uint16_t ld_u16(const void* p) { return *reinterpret_cast<const uint16_t*>(p); }
+
 // Per-thread prefetch of the cache line holding `p` into L2 (one
 // instruction for a whole warp's worth of different rows).
 __device__ __forceinline__ void prefetch_l2(const void* p) {
   asm volatile("prefetch.global.L2::evict_last [%0];" ::"l"(p));
+}
+
+// ------------------------------------------- programmatic dependent launch --
+// A kernel launched with programmatic stream serialisation may start while
+// the previous kernel of its stream is still running.  pdl_wait() blocks
+// until that kernel has completed and its memory is visible; everything a
+// kernel does before it must not depend on the previous kernel's output.
+// pdl_launch_dependents() lets the next such kernel start launching.  Both
+// are no-ops for an ordinary launch.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
 
 // ------------------------------------------------------ TMA + mbarrier --

@@ -254,18 +254,18 @@ __device__ __forceinline__ void cta_tables_init(const CtaTables& tb, int cu0, in
 }
 
 // The unit order of one warp: segments [a0,b0) split tail, [a1,b1) split
-// head, [a2,b2) whole tiles (seg 3 = done).
+// head, [a2,b2) whole tiles (seg 3 = done).  `end` caches the end of the
+// current segment.
 struct UnitSeq {
   int a0, b0, a1, b1, a2, b2;
-  int seg, u, t, kc, upt;
-
-  __device__ __forceinline__ int seg_end() const { return seg == 0 ? b0 : seg == 1 ? b1 : b2; }
+  int seg, u, t, kc, upt, end;
 
   __device__ __forceinline__ void enter(int sg) {
     seg = sg;
     while (seg < 3 && (seg == 0 ? a0 == b0 : seg == 1 ? a1 == b1 : a2 == b2)) ++seg;
     if (seg < 3) {
       u = seg == 0 ? a0 : seg == 1 ? a1 : a2;
+      end = seg == 0 ? b0 : seg == 1 ? b1 : b2;
       t = u / upt;
       kc = u - t * upt;
     }
@@ -287,13 +287,24 @@ struct UnitSeq {
     enter(0);
   }
 
+  // n units forward (n > 0, not past the segment end)
+  __device__ __forceinline__ void skip(int n) {
+    u += n;
+    kc += n;
+    while (kc >= upt) {
+      kc -= upt;
+      ++t;
+    }
+    if (u == end) enter(seg + 1);
+  }
+
   __device__ __forceinline__ void advance() {
     ++u;
     if (++kc == upt) {
       kc = 0;
       ++t;
     }
-    if (u == seg_end()) enter(seg + 1);
+    if (u == end) enter(seg + 1);
   }
 };
 
@@ -392,7 +403,9 @@ __device__ __forceinline__ void close_split(Op& op, const Partition& pt, const C
 }
 
 // Streams the range [wu0, wu1) of warp `warp` (non-empty; the prologue ran
-// on lane 0, so the other lanes first replay its cursor advances).
+// on lane 0, so the other lanes first replay its cursor advances).  The
+// loop runs chunk by chunk -- the units of one tile inside one segment --
+// so the per-unit body carries no tile or segment bookkeeping.
 template <class Op, class Issue>
 __device__ __forceinline__ void tma_stream(Op& op, const Issue& issue, TmaRing& rg, const Partition& pt,
                                            const CtaTables& tb, float* red, int warp, int wu0, int wu1,
@@ -400,32 +413,30 @@ __device__ __forceinline__ void tma_stream(Op& op, const Issue& issue, TmaRing& 
   const bool leader = (threadIdx.x & 31) == 0;
   if (!leader)
     for (int i = 0; i < rg.S && rg.next.seg < 3; ++i) rg.issue_next(issue, i, Op::kUnitBytes, false);
+  const int upt = pt.upt;
   UnitSeq sq;
-  sq.init(wu0, wu1, pt.upt);
+  sq.init(wu0, wu1, upt);
   int s = 0;
   uint32_t ph = 0;
-  op.zero();
   typename Op::Buf buf;
   while (sq.seg < 3) {
-    if (!mbar_wait_bounded(rg.bars + 8u * (uint32_t)s, ph, status)) break;
-    op.read(buf, rg.ring + (uint32_t)s * Op::kUnitBytes);
-    __syncwarp();
-    if (rg.next.seg < 3) rg.issue_next(issue, s, Op::kUnitBytes, leader);  // warp-uniform test
-    if (++s == rg.S) {
-      s = 0;
-      ph ^= 1u;
-    }
-    op.compute(buf, sq.t, sq.kc);
-    if (sq.seg == 2) {
-      if (sq.kc + 1 == pt.upt) {
-        op.store_tile(sq.t);
-        op.zero();
+    const int t = sq.t, kc0 = sq.kc;
+    const int n = (upt - kc0) < (sq.end - sq.u) ? (upt - kc0) : (sq.end - sq.u);
+    op.zero();
+    for (int kc = kc0; kc < kc0 + n; ++kc) {
+      if (!mbar_wait_bounded(rg.bars + 8u * (uint32_t)s, ph, status)) return;
+      op.read(buf, rg.ring + (uint32_t)s * Op::kUnitBytes);
+      __syncwarp();
+      if (rg.next.seg < 3) rg.issue_next(issue, s, Op::kUnitBytes, leader);  // warp-uniform test
+      if (++s == rg.S) {
+        s = 0;
+        ph ^= 1u;
       }
-    } else if (sq.u + 1 == sq.seg_end()) {
-      close_split(op, pt, tb, red, warp, sq.t, sq.seg == 0 ? 1 : 0, cu0, cu1);
-      op.zero();
+      op.compute(buf, t, kc);
     }
-    sq.advance();
+    if (sq.seg == 2) op.store_tile(t);
+    else close_split(op, pt, tb, red, warp, t, sq.seg == 0 ? 1 : 0, cu0, cu1);
+    sq.skip(n);
   }
 }
 

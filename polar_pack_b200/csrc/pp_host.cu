@@ -3,9 +3,14 @@
 
 #include <cuda_fp16.h>
 
+#include <atomic>
 #include <cstring>
 
 namespace pp {
+
+static std::atomic<int> g_launch_overlap{0};
+
+bool launch_overlap() { return g_launch_overlap.load(std::memory_order_relaxed) != 0; }
 
 static thread_local char g_err[512] = "";
 
@@ -125,5 +130,10 @@ const char* pp_last_error(void) { return pp::g_err; }
 int pp_version(void) { return PP_VERSION; }
 
 int pp_device_sm_count(int device) { return pp::device_sm_count(device); }
+
+int pp_set_launch_overlap(int enable) {
+  const int old = pp::g_launch_overlap.exchange(enable ? 1 : 0);
+  return old;
+}
 
 }  // extern "C"

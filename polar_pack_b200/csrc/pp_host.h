@@ -7,6 +7,7 @@
 
 #include <cstdarg>
 #include <cstdio>
+#include <utility>
 
 #include "../../include/polar_pack_b200.h"
 
@@ -58,6 +59,34 @@ int ensure_smem_attr(K kernel, bool* done_flags, int* limits, int* max_dynamic) 
   }
   *max_dynamic = limits[dev];
   return PP_OK;
+}
+
+// Launch overlap (programmatic dependent launch) for the kernels that
+// support it, switched by pp_set_launch_overlap().
+bool launch_overlap();
+
+// cudaLaunchKernelEx with programmatic stream serialisation when
+// `overlap` is set; records launch errors.
+template <typename... KArgs, typename... Args>
+int launch_kernel(const char* what, bool overlap, void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                  cudaStream_t stream, Args&&... args) {
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = overlap ? 1 : 0;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    set_error("%s: %s", what, cudaGetErrorString(e));
+    return PP_ERR_CUDA;
+  }
+  return check_launch(what);
 }
 
 inline bool aligned(const void* p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }

@@ -272,8 +272,8 @@ namespace pp {
 // byte was cleared by pp_quad_prepare_plugs) and adds corr before the
 // per-model scale and the FP16 store, so the result equals the product with
 // the plug values substituted, up to FP32 summation order.  One warp per
-// row; lanes take every 32nd entry and the warp sums lane totals in a fixed
-// butterfly order, so results are deterministic.
+// row; lanes take every 32nd entry (four per lane in flight) and the warp
+// sums lane totals in a fixed butterfly order, so results are deterministic.
 struct PlugCorrParams {
   const __half* x;
   int64_t ldx_m;
@@ -287,9 +287,14 @@ struct PlugCorrParams {
 
 template <int MB>
 __global__ void __launch_bounds__(256) quad_plug_corr_kernel(const PlugCorrParams p) {
+  constexpr int U = 4;  // entries per lane in flight
+  pdl_launch_dependents();
   const int lane = threadIdx.x & 31;
   const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
-  if (row >= p.N) return;
+  if (row >= p.N) {
+    pdl_wait();
+    return;
+  }
   const uint32_t j0 = __ldg(p.wbase + (int64_t)row * p.W), j1 = __ldg(p.wbase + (int64_t)(row + 1) * p.W);
   const uint32_t rowbase = p.base_lo32 + (uint32_t)row * (uint32_t)p.K;
   float acc[MB][4];
@@ -297,19 +302,34 @@ __global__ void __launch_bounds__(256) quad_plug_corr_kernel(const PlugCorrParam
   for (int m = 0; m < MB; ++m)
 #pragma unroll
     for (int q = 0; q < 4; ++q) acc[m][q] = 0.f;
-  for (uint32_t j = j0 + lane; j < j1; j += 32) {
-    const uint32_t k = __ldg(p.plug_idx + j) - rowbase;
-    const uint2 v = __ldg(p.plug_vals + j);
-    const float pv[4] = {__half2float(__ushort_as_half((uint16_t)(v.x & 0xFFFF))),
-                         __half2float(__ushort_as_half((uint16_t)(v.x >> 16))),
-                         __half2float(__ushort_as_half((uint16_t)(v.y & 0xFFFF))),
-                         __half2float(__ushort_as_half((uint16_t)(v.y >> 16)))};
+  for (uint32_t jb = j0; jb < j1; jb += 32u * U) {
+    // the plug arrays are weights: load a batch before waiting
+    uint32_t kk[U];
+    uint2 vv[U];
 #pragma unroll
-    for (int m = 0; m < MB; ++m) {
-      if (m < p.M) {
-        const float xv = __half2float(p.x[(int64_t)m * p.ldx_m + k]);
+    for (int u = 0; u < U; ++u) {
+      const uint32_t j = jb + (uint32_t)lane + 32u * u;
+      kk[u] = 0u;
+      vv[u] = make_uint2(0u, 0u);  // zero values: the entry contributes nothing
+      if (j < j1) {
+        kk[u] = __ldg(p.plug_idx + j) - rowbase;
+        vv[u] = __ldg(p.plug_vals + j);
+      }
+    }
+    pdl_wait();  // activations may come from the previous kernel
 #pragma unroll
-        for (int q = 0; q < 4; ++q) acc[m][q] = fmaf(pv[q], xv, acc[m][q]);
+    for (int u = 0; u < U; ++u) {
+      const float pv[4] = {__half2float(__ushort_as_half((uint16_t)(vv[u].x & 0xFFFF))),
+                           __half2float(__ushort_as_half((uint16_t)(vv[u].x >> 16))),
+                           __half2float(__ushort_as_half((uint16_t)(vv[u].y & 0xFFFF))),
+                           __half2float(__ushort_as_half((uint16_t)(vv[u].y >> 16)))};
+#pragma unroll
+      for (int m = 0; m < MB; ++m) {
+        if (m < p.M) {
+          const float xv = __half2float(p.x[(int64_t)m * p.ldx_m + kk[u]]);
+#pragma unroll
+          for (int q = 0; q < 4; ++q) acc[m][q] = fmaf(pv[q], xv, acc[m][q]);
+        }
       }
     }
   }
@@ -322,6 +342,7 @@ __global__ void __launch_bounds__(256) quad_plug_corr_kernel(const PlugCorrParam
       for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
       acc[m][q] = v;
     }
+  pdl_wait();  // the previous kernel may still read the correction buffer
   if (lane == 0) {
 #pragma unroll
     for (int m = 0; m < MB; ++m)
@@ -334,10 +355,9 @@ __global__ void __launch_bounds__(256) quad_plug_corr_kernel(const PlugCorrParam
 int launch_plug_corr(const PlugCorrParams& prm, cudaStream_t s) {
   const int warps = 8;
   const int grid = (int)cdiv(prm.N, warps);
-  if (prm.M == 1) quad_plug_corr_kernel<1><<<grid, warps * 32, 0, s>>>(prm);
-  else if (prm.M <= 8) quad_plug_corr_kernel<8><<<grid, warps * 32, 0, s>>>(prm);
-  else quad_plug_corr_kernel<16><<<grid, warps * 32, 0, s>>>(prm);
-  return check_launch("quad_plug_corr_kernel");
+  auto kern = prm.M == 1 ? quad_plug_corr_kernel<1> : prm.M <= 8 ? quad_plug_corr_kernel<8>
+                                                                   : quad_plug_corr_kernel<16>;
+  return launch_kernel("quad_plug_corr_kernel", launch_overlap(), kern, dim3(grid), dim3(warps * 32), 0, s, prm);
 }
 
 }  // namespace pp

@@ -85,11 +85,12 @@ struct QuadOp {
   int g, c;
   int pr;  // NK: physical row of mma row g inside the 8-row tile (see read())
   uint32_t lb0, lb1, add0, add1;  // table addressing (decode_quad)
+  uint32_t roff[4];               // this lane's 16-byte reads inside a ring slot (see read())
   int Mv, Nv, Kv;
   int64_t ldc, ldx_m;
   const uint32_t* codes;
   const __half* x;
-  const __half* xrow[NB];  // this lane's activation row per batch tile (clamped)
+  const __half* xrow[NB];  // this lane's activation row per batch tile (clamped); NK: + 4c
   float acc[kT][NB][2][4];
 
   __device__ __forceinline__ QuadOp(const QuadParams& p_, uint32_t lut_saddr)
@@ -102,7 +103,17 @@ struct QuadOp {
 #pragma unroll
     for (int nb = 0; nb < NB; ++nb) {
       const int bat = nb * 8 + g;
-      xrow[nb] = x + (int64_t)(bat < Mv ? bat : 0) * ldx_m;
+      xrow[nb] = x + (int64_t)(bat < Mv ? bat : 0) * ldx_m + (NK ? 4 * c : 0);
+    }
+#pragma unroll
+    for (int s = 0; s < 4; ++s) {
+      if constexpr (NK) {
+        const int j = 4 * (s & 1) + c;
+        roff[s] = (uint32_t)((s >> 1) * 1024 + pr * 128 + ((j ^ pr) << 4));
+      } else {
+        const int row = 2 * c + (s & 1) + 8 * (s >> 1);
+        roff[s] = (uint32_t)(row * 128 + ((g ^ (row & 7)) << 4));
+      }
     }
   }
 
@@ -143,34 +154,25 @@ struct QuadOp {
   // a quarter-warp differ in bit 2 and their chunks never share banks.
   // KN: lane (g, c) needs chunk g of rows 2c, 2c+1, 2c+8, 2c+9.
   __device__ __forceinline__ void read(Buf& b, uint32_t slot) const {
-    if constexpr (NK) {
 #pragma unroll
-      for (int s = 0; s < 4; ++s) {
-        const int j = 4 * (s & 1) + c;
-        b.q[s] = lds128(slot + (uint32_t)((s >> 1) * 1024 + pr * 128 + ((j ^ pr) << 4)));
-      }
-    } else {
-#pragma unroll
-      for (int r = 0; r < 4; ++r) {
-        const int row = 2 * c + (r & 1) + 8 * (r >> 1);
-        b.q[r] = lds128(slot + (uint32_t)(row * 128 + ((g ^ (row & 7)) << 4)));
-      }
-    }
+    for (int s = 0; s < 4; ++s) b.q[s] = lds128(slot + roff[s]);
   }
+
 
   // Activation fragments.  Batch columns >= M read row 0 (clamped): their
   // mma output column is never stored.  FULL units lie wholly below K and
   // load without checks; in the last K chunk, columns k >= K read as zero.
   template <bool FULL>
   __device__ __forceinline__ uint32_t xpair(int nb, int k) const {
-    if (FULL || k + 1 < Kv) return ldg_u32(xrow[nb] + k);
-    return k < Kv ? (uint32_t)ldg_u16(xrow[nb] + k) : 0u;
+    if (FULL || k + 1 < Kv) return ld_u32(xrow[nb] + k);
+    return k < Kv ? (uint32_t)ld_u16(xrow[nb] + k) : 0u;
   }
 
+  // NK: activations (bat, kbase + 16s + 4c .. +3) from xrow (which holds
+  // the + 4c); the NK path guarantees K % 4 == 0
   template <bool FULL>
-  __device__ __forceinline__ uint2 xquad(int nb, int k) const {
-    // activations (bat, k..k+3); the NK path guarantees K % 4 == 0
-    if (FULL || k < Kv) return ldg_u2(xrow[nb] + k);
+  __device__ __forceinline__ uint2 xquad(int nb, int kbase, int s) const {
+    if (FULL || kbase + 16 * s + 4 * c < Kv) return ld_u2(xrow[nb] + kbase + 16 * s);
     return make_uint2(0u, 0u);
   }
 
@@ -187,7 +189,7 @@ struct QuadOp {
 #pragma unroll
       for (int s = 0; s < 4; ++s)
 #pragma unroll
-        for (int nb = 0; nb < NB; ++nb) xb[s][nb] = xquad<FULL>(nb, kbase + 16 * s + 4 * c);
+        for (int nb = 0; nb < NB; ++nb) xb[s][nb] = xquad<FULL>(nb, kbase, s);
 #pragma unroll
       for (int s = 0; s < 4; ++s) {
         const int kp = kbase + 16 * s + 4 * c;
@@ -279,7 +281,7 @@ struct QuadOp {
   }
 
   __device__ __forceinline__ void store(int model, int bat, int f, float v) const {
-    if (p.corr) v += __ldg(p.corr + ((int64_t)model * Mv + bat) * Nv + f);
+    if (p.corr) v += p.corr[((int64_t)model * Mv + bat) * Nv + f];
     p.out[model][(int64_t)bat * p.ldo_m + (int64_t)f * p.ldo_n] = __float2half_rn(v * p.scale[model]);
   }
 };
@@ -300,14 +302,17 @@ __host__ __device__ inline uint32_t quad_scratch_bytes(bool nk, int nb, int M) {
   return (uint32_t)red_bytes(quad_warps(nk, nb), 4, M, nk ? 8 : 32);
 }
 
-// Before the first barrier: the per-CTA int tables and the table words
-// (loaded to registers, then staged).  Between the barriers lane 0 of every
+// Before the first barrier: the table words (their loads issued first, to
+// registers, then staged) and the per-CTA int tables.  Between the barriers lane 0 of every
 // warp initialises its ring and issues its first S units, whose copies
 // then overlap the fan-out of the tables.  After the second barrier every
 // warp streams and reduces on its own; there is no closing barrier.
 template <bool NK, int NB>
 __global__ void __launch_bounds__(quad_warps(NK, NB) * 32, 1) quad_gemv_kernel(const __grid_constant__ QuadParams p) {
   constexpr int NW = quad_warps(NK, NB);
+  pdl_launch_dependents();
+  uint32_t v[kLutWordsPerThread];
+  quad_lut_load(v, p.luts);
   const uint32_t base = (uint32_t)__cvta_generic_to_shared(pp_smem);
   int* status = p.part.counters + (kMaxGrid - 1);
   const QuadLayout L = quad_layout(base, p.smem_bytes, NW, p.stages, quad_scratch_bytes(NK, NB, p.M), true);
@@ -318,8 +323,6 @@ __global__ void __launch_bounds__(quad_warps(NK, NB) * 32, 1) quad_gemv_kernel(c
   const int U = p.part.units, G = gridDim.x;
   const int cu0 = range_start(U, G, blockIdx.x), cu1 = range_start(U, G, blockIdx.x + 1);
   if (cu0 >= cu1) return;  // uniform over the CTA
-  uint32_t v[kLutWordsPerThread];
-  quad_lut_load(v, p.luts);
   int* ti = reinterpret_cast<int*>(pp_smem + (L.tables - base));
   const CtaTables tb{ti, ti + (NW + 1), ti + 2 * (NW + 1)};
   cta_tables_init<NW>(tb, cu0, cu1, p.part.upt);
@@ -345,6 +348,9 @@ __global__ void __launch_bounds__(quad_warps(NK, NB) * 32, 1) quad_gemv_kernel(c
   }
   quad_lut_fanout(pp_smem + (L.lut - base), stage);
   __syncthreads();
+  // everything above reads only weights; activations, the workspace and the
+  // outputs may belong to the previous kernel of the stream
+  pdl_wait();
   if (wu0 >= wu1) return;
   if (L.direct) quad_body<NK, NB, true>(p, L, rg, tb, cu0, cu1, wu0, wu1, status);
   else quad_body<NK, NB, false>(p, L, rg, tb, cu0, cu1, wu0, wu1, status);
@@ -440,8 +446,8 @@ int launch_quad(QuadParams& prm, int grid, int idx, cudaStream_t s) {
   }
   prm.stages = stages;
   prm.smem_bytes = (uint32_t)max_smem;
-  kern<<<grid, NW * 32, (size_t)max_smem, s>>>(prm);
-  return check_launch("quad_gemv_kernel");
+  return launch_kernel("quad_gemv_kernel", launch_overlap(), kern, dim3(grid), dim3(NW * 32), (size_t)max_smem, s,
+                       prm);
 }
 
 // Workspace: [counter block 4 KiB][plug correction 4 x 16 x N floats][partial slots]
