@@ -41,7 +41,25 @@ struct Partition {
   int upt;        // units per tile
   int* counters;  // [kMaxGrid] arrival counters (zero between launches)
   float* slots;   // [grid][2][nout * M * tile_w] cross-CTA partials
+  // TMA engine only: unit start of every CTA (cta_start[G] = units), a
+  // table the host fills; NULL for the register engine (equal split)
+  const int* cta_start;
 };
+
+// CTA ranges of the TMA engine come from a host-filled table of at most
+// kMaxCtaTable + 1 starts, passed in the kernel parameters.
+constexpr int kMaxCtaTable = 256;
+
+// largest c < G with start[c] <= x (binary search over the table)
+__device__ __forceinline__ int cta_of_unit(const int* start, int G, int x) {
+  int lo = 0, hi = G - 1;
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    if (start[mid] <= x) lo = mid;
+    else hi = mid - 1;
+  }
+  return lo;
+}
 
 __device__ __forceinline__ int range_start(int U, int parts, int i) {
   return (int)(((int64_t)U * i) / parts);
@@ -242,11 +260,18 @@ struct CtaTables {
   int* cnt;     // [2 * NW] split-tile arrival counters, indexed 2 * (first warp) + slot
 };
 
+// Warp w of the CTA range [cu0, cu1) starts at cu0 + (cu1 - cu0) * w / NW;
+// the host keeps (cu1 - cu0) * NW below 2^31.
+template <int NW>
+__device__ __forceinline__ int warp_start(int cu0, int cu1, int w) {
+  return cu0 + (int)((uint32_t)((cu1 - cu0) * w) / (uint32_t)NW);
+}
+
 template <int NW>
 __device__ __forceinline__ void cta_tables_init(const CtaTables& tb, int cu0, int cu1, int upt) {
   const int i = threadIdx.x;
   if (i <= NW) {
-    const int w0 = cu0 + range_start(cu1 - cu0, NW, i);
+    const int w0 = warp_start<NW>(cu0, cu1, i);
     tb.wstart[i] = w0;
     tb.wtile[i] = w0 / upt;
   }
@@ -376,9 +401,9 @@ __device__ __forceinline__ void close_split(Op& op, const Partition& pt, const C
   }
   if (inside) return;
   // tile cut by a CTA boundary
-  const int U = pt.units, G = gridDim.x;
-  const int c_first = part_of_unit(T * upt, U, G);
-  const int c_last = part_of_unit(T * upt + upt - 1, U, G);
+  const int G = gridDim.x;
+  const int c_first = cta_of_unit(pt.cta_start, G, T * upt);
+  const int c_last = cta_of_unit(pt.cta_start, G, T * upt + upt - 1);
   __threadfence();
   __syncwarp();
   int lastc = 0;
@@ -390,7 +415,7 @@ __device__ __forceinline__ void close_split(Op& op, const Partition& pt, const C
     float sum = 0.f;
     for (int c = c_first; c <= c_last; ++c) {
       // only the first contributor can have started before the tile
-      const int w = (c == c_first && range_start(U, G, c) < T * upt) ? 1 : 0;
+      const int w = (c == c_first && pt.cta_start[c] < T * upt) ? 1 : 0;
       sum += __ldcg(pt.slots + ((int64_t)c * 2 + w) * (int64_t)nval + e);
     }
     const int o = e / (M * TW);
@@ -444,9 +469,23 @@ __device__ __forceinline__ void tma_stream(Op& op, const Issue& issue, TmaRing& 
 struct PartitionPlan {
   int64_t tiles = 0, upt = 0, units = 0;
   int grid = 0;
+  bool tile_aligned = false;  // CTA ranges start on tile boundaries (no cross-CTA tiles)
   size_t counters_bytes = 0, slots_bytes = 0;
   size_t total() const { return counters_bytes + slots_bytes; }
 };
+
+// Unit start of every CTA of a TMA-engine launch (start[grid] = units).
+// Equal unit ranges by default.  When giving every CTA whole tiles costs at
+// most `slack` units of imbalance (the most loaded CTA against the mean),
+// the ranges are tile-aligned instead: no tile is then split across CTAs,
+// which saves the cross-CTA reduction at the end of the launch.
+inline void fill_cta_starts(PartitionPlan& pl, int* start, int64_t slack) {
+  const int G = pl.grid;
+  const int64_t max_tiles = (pl.tiles + G - 1) / G;
+  pl.tile_aligned = max_tiles * pl.upt * G - pl.units <= slack * G;
+  for (int c = 0; c <= G; ++c)
+    start[c] = pl.tile_aligned ? (int)(pl.tiles * c / G * pl.upt) : (int)(pl.units * c / G);
+}
 
 inline PartitionPlan plan_partition(int64_t tiles, int64_t upt, int warps, int sms, int nout, int64_t M,
                                     int tile_w) {

@@ -63,6 +63,11 @@ struct QuadParams {
   Partition part;
   int stages;           // TMA ring slots per warp
   uint32_t smem_bytes;  // dynamic shared memory of the launch
+  // shared-memory layout planned on the host for a dynamic region at
+  // layout_base (the kernel recomputes it if its base differs)
+  QuadLayout layout;
+  uint32_t layout_base;
+  int cta_start[kMaxCtaTable + 1];  // unit start of every CTA (fill_cta_starts)
 };
 
 struct QuadBuf {
@@ -287,14 +292,14 @@ struct QuadOp {
 };
 
 template <bool NK, int NB, bool DIRECT>
-__device__ __forceinline__ void quad_body(const QuadParams& p, const QuadLayout& L, TmaRing& rg,
+__device__ __forceinline__ void quad_body(const QuadParams& p, const Partition& pt, const QuadLayout& L, TmaRing& rg,
                                           const CtaTables& tb, int cu0, int cu1, int wu0, int wu1, int* status) {
   using Op = QuadOp<NK, NB, DIRECT>;
   const uint32_t base = (uint32_t)__cvta_generic_to_shared(pp_smem);
   float* red = reinterpret_cast<float*>(pp_smem + (L.scratch - base));
   Op op(p, L.lut);
   tma_stream(op, [&](uint32_t slot, uint32_t bar, int tile, int kc) { Op::issue(p, slot, bar, tile, kc); }, rg,
-             p.part, tb, red, threadIdx.x >> 5, wu0, wu1, cu0, cu1, status);
+             pt, tb, red, threadIdx.x >> 5, wu0, wu1, cu0, cu1, status);
 }
 
 // Partial-sum scratch of a CTA: two slots per warp.
@@ -315,20 +320,22 @@ __global__ void __launch_bounds__(quad_warps(NK, NB) * 32, 1) quad_gemv_kernel(c
   quad_lut_load(v, p.luts);
   const uint32_t base = (uint32_t)__cvta_generic_to_shared(pp_smem);
   int* status = p.part.counters + (kMaxGrid - 1);
-  const QuadLayout L = quad_layout(base, p.smem_bytes, NW, p.stages, quad_scratch_bytes(NK, NB, p.M), true);
+  const QuadLayout L = base == p.layout_base
+                           ? p.layout
+                           : quad_layout(base, p.smem_bytes, NW, p.stages, quad_scratch_bytes(NK, NB, p.M), true);
   if (!L.ok) {  // the host plans for this never to happen
     if (threadIdx.x == 0) atomicExch(status, 2);
     return;
   }
-  const int U = p.part.units, G = gridDim.x;
-  const int cu0 = range_start(U, G, blockIdx.x), cu1 = range_start(U, G, blockIdx.x + 1);
+  const int cu0 = p.cta_start[blockIdx.x], cu1 = p.cta_start[blockIdx.x + 1];
   if (cu0 >= cu1) return;  // uniform over the CTA
+  Partition pt = p.part;
+  pt.cta_start = p.cta_start;
   int* ti = reinterpret_cast<int*>(pp_smem + (L.tables - base));
   const CtaTables tb{ti, ti + (NW + 1), ti + 2 * (NW + 1)};
   cta_tables_init<NW>(tb, cu0, cu1, p.part.upt);
   const int warp = threadIdx.x >> 5;
-  const int R = cu1 - cu0;
-  const int wu0 = cu0 + range_start(R, NW, warp), wu1 = cu0 + range_start(R, NW, warp + 1);
+  const int wu0 = warp_start<NW>(cu0, cu1, warp), wu1 = warp_start<NW>(cu0, cu1, warp + 1);
   TmaRing rg;
   if (wu0 < wu1) {
     const uint32_t rw = (uint32_t)p.stages * 2048u;
@@ -352,8 +359,8 @@ __global__ void __launch_bounds__(quad_warps(NK, NB) * 32, 1) quad_gemv_kernel(c
   // outputs may belong to the previous kernel of the stream
   pdl_wait();
   if (wu0 >= wu1) return;
-  if (L.direct) quad_body<NK, NB, true>(p, L, rg, tb, cu0, cu1, wu0, wu1, status);
-  else quad_body<NK, NB, false>(p, L, rg, tb, cu0, cu1, wu0, wu1, status);
+  if (L.direct) quad_body<NK, NB, true>(p, pt, L, rg, tb, cu0, cu1, wu0, wu1, status);
+  else quad_body<NK, NB, false>(p, pt, L, rg, tb, cu0, cu1, wu0, wu1, status);
 }
 
 // Generic fallback for layouts the vector paths do not take (unaligned or
@@ -407,10 +414,29 @@ __global__ void quad_generic_kernel(const QuadGenericParams p) {
 // ------------------------------------------------------------------ host --
 namespace {
 
-PartitionPlan quad_plan(bool nk, int64_t Mc, int64_t N, int64_t K, int sms) {
+// Imbalance (units on the most loaded CTA above the mean) accepted to keep
+// every tile inside one CTA; about the time of the cross-CTA reduction.
+constexpr int64_t kAlignSlackUnits = 32;
+
+PartitionPlan quad_plan(bool nk, int64_t Mc, int64_t N, int64_t K, int sms, int* starts = nullptr) {
   const int nb = Mc > 8 ? 2 : 1;
   const int tile_w = nk ? 8 : 32, unit_k = nk ? 64 : 16;
-  return plan_partition(cdiv(N, tile_w), cdiv(K, unit_k), quad_warps(nk, nb), sms, 4, Mc, tile_w);
+  const int cap = sms < kMaxCtaTable ? sms : kMaxCtaTable;
+  PartitionPlan pl = plan_partition(cdiv(N, tile_w), cdiv(K, unit_k), quad_warps(nk, nb), cap, 4, Mc, tile_w);
+  if (pl.units > 0) {
+    int tmp[kMaxCtaTable + 1];
+    int* st = starts ? starts : tmp;
+    if (pl.grid > pl.tiles) {  // tile-aligned candidates never need more CTAs than tiles
+      PartitionPlan t = pl;
+      t.grid = (int)pl.tiles;
+      fill_cta_starts(t, st, kAlignSlackUnits);
+      if (t.tile_aligned) pl = t;
+      else fill_cta_starts(pl, st, kAlignSlackUnits);
+    } else {
+      fill_cta_starts(pl, st, kAlignSlackUnits);
+    }
+  }
+  return pl;
 }
 
 bool g_attr_done[8][64];
@@ -446,6 +472,8 @@ int launch_quad(QuadParams& prm, int grid, int idx, cudaStream_t s) {
   }
   prm.stages = stages;
   prm.smem_bytes = (uint32_t)max_smem;
+  prm.layout_base = (uint32_t)reserved_smem(current_device());
+  prm.layout = quad_layout(prm.layout_base, prm.smem_bytes, NW, stages, redb, true);
   return launch_kernel("quad_gemv_kernel", launch_overlap(), kern, dim3(grid), dim3(NW * 32), (size_t)max_smem, s,
                        prm);
 }
@@ -601,7 +629,12 @@ static int quad_run(const void* a, int64_t lda_m, int64_t lda_k, const uint32_t*
   // batch rows in chunks of 16: each chunk is one launch over the codes
   for (int64_t m0 = 0; m0 < M; m0 += 16) {
     const int64_t Mc = (M - m0) < 16 ? (M - m0) : 16;
-    const PartitionPlan pl = quad_plan(nk, Mc, N, K, sms);
+    const PartitionPlan pl = quad_plan(nk, Mc, N, K, sms, prm.cta_start);
+    for (int c = 0; c < pl.grid; ++c)  // warp split in 32-bit arithmetic (warp_start)
+      if ((int64_t)(prm.cta_start[c + 1] - prm.cta_start[c]) * quad_warps(nk, Mc > 8 ? 2 : 1) >= INT32_MAX) {
+        set_error("matrix too large for one launch (units per thread block)");
+        return PP_ERR_INVALID;
+      }
     prm.x = reinterpret_cast<const __half*>(a) + m0 * lda_m;
     for (int i = 0; i < 4; ++i) prm.out[i] = reinterpret_cast<__half*>(out[i]) + m0 * ldo_m;
     prm.M = (int)Mc;

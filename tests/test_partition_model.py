@@ -120,11 +120,34 @@ class UnitSeq:
                 yield seg, u, u + 1 == b
 
 
-def simulate_tma(U, upt, G, NW):
+def fill_cta_starts(tiles, upt, G, slack):
+    """pp_engine.cuh fill_cta_starts: equal units, or tile-aligned when cheap."""
+    U = tiles * upt
+    max_tiles = -(-tiles // G)
+    aligned = max_tiles * upt * G - U <= slack * G
+    starts = [(tiles * c // G) * upt if aligned else U * c // G for c in range(G + 1)]
+    return starts, aligned
+
+
+def cta_of_unit(starts, G, x):
+    """Largest c < G with starts[c] <= x (binary search in the kernel)."""
+    lo, hi = 0, G - 1
+    while lo < hi:
+        mid = (lo + hi + 1) // 2
+        if starts[mid] <= x:
+            lo = mid
+        else:
+            hi = mid - 1
+    return lo
+
+
+def simulate_tma(U, upt, G, NW, starts=None):
     tiles = U // upt
+    if starts is None:
+        starts = [rs(U, G, b) for b in range(G + 1)]
     stores, gslots, counters = {}, {}, {}
     for b in range(G):
-        cu0, cu1 = rs(U, G, b), rs(U, G, b + 1)
+        cu0, cu1 = starts[b], starts[b + 1]
         assert cu0 < cu1
         R = cu1 - cu0
         wstart = [cu0 + rs(R, NW, i) for i in range(NW + 1)]
@@ -182,14 +205,14 @@ def simulate_tma(U, upt, G, NW):
                 key = (b, 0 if t == wtile[0] else 1)
                 assert key not in gslots
                 gslots[key] = (t, s)
-                cf, cl = pou(t * upt, U, G), pou(t * upt + upt - 1, U, G)
+                cf, cl = cta_of_unit(starts, G, t * upt), cta_of_unit(starts, G, t * upt + upt - 1)
                 counters.setdefault(cl, []).append((t, cf))
     for cl, arr in counters.items():
         t, cf = arr[0]
         assert all(a == arr[0] for a in arr) and len(arr) == cl - cf + 1
         tot = set()
         for c in range(cf, cl + 1):
-            t_, s = gslots[(c, 1 if (c == cf and rs(U, G, c) < t * upt) else 0)]
+            t_, s = gslots[(c, 1 if (c == cf and starts[c] < t * upt) else 0)]
             assert t_ == t and not (tot & s)
             tot |= s
         assert t not in stores
@@ -207,3 +230,44 @@ def test_tma_engine_closes_every_tile_once(upt, NW):
         for G in sorted({1, 2, 3, min(148, want), min(148, U)}):
             if G <= U:  # the host never plans more CTAs than units
                 simulate_tma(U, upt, G, NW)
+
+
+@pytest.mark.parametrize("upt", [1, 3, 16, 32, 172])
+@pytest.mark.parametrize("NW", [4, 8, 12])
+def test_tma_engine_with_host_cta_table(upt, NW):
+    """The host's CTA-start table, in both modes, as quad_plan builds it."""
+    for tiles in [1, 5, 32, 256, 1376]:
+        U = upt * tiles
+        G = min(148, max(1, -(-U // (2 * NW))))
+        if G > tiles:
+            st, aligned = fill_cta_starts(tiles, upt, tiles, 32)
+            if aligned:
+                G = tiles
+            else:
+                st, aligned = fill_cta_starts(tiles, upt, G, 32)
+        else:
+            st, aligned = fill_cta_starts(tiles, upt, G, 32)
+        assert all(st[c] < st[c + 1] for c in range(G))    # no empty CTA
+        if aligned:
+            assert all(x % upt == 0 for x in st)
+        simulate_tma(U, upt, G, NW, starts=st)
+        if aligned:
+            pass  # no tile crossed a CTA boundary: simulate_tma stored every tile in-CTA
+
+
+def test_sweep_shapes_plan():
+    """Which BASELINE shapes get tile-aligned CTA ranges (12 warps, 148 SMs)."""
+    plans = {}
+    for (K, N) in [(2048, 2048), (2048, 11008), (11008, 2048), (2048, 256)]:
+        tiles, upt = -(-N // 8), -(-K // 64)
+        U = tiles * upt
+        G = min(148, -(-U // 24))
+        if G > tiles:
+            _, al = fill_cta_starts(tiles, upt, tiles, 32)
+            G = tiles if al else G
+        _, al = fill_cta_starts(tiles, upt, G, 32)
+        plans[(K, N)] = (G, al)
+    assert plans[(2048, 256)] == (32, True)
+    assert plans[(2048, 2048)] == (148, True)
+    assert plans[(2048, 11008)] == (148, True)
+    assert plans[(11008, 2048)] == (148, False)
