@@ -201,36 +201,41 @@ def run_ours(args):
     ws_bytes = max(quad_linear_workspace_bytes(M, l.N, l.K) for st in sets for l in st)
     ws = torch.zeros(max(ws_bytes, 256), dtype=torch.uint8, device=dev)
 
-    # pre-built C-ABI argument tuples: no Python allocation inside the timed loop
-    calls = []
+    # pre-built C-ABI argument tuples: no Python allocation inside the timed loop.
+    # With N > 1 GPUs the four Linears of a step are independent, so their
+    # outputs go straight into one send buffer (column block per Linear,
+    # strided outputs) and ONE all-gather per step collects every rank's rows.
+    calls, gathers = [], []
     for st in sets:
         row = []
+        widths = [l.N for l in st]
+        send = torch.zeros((4, M, sum(widths)), dtype=torch.float16, device=dev)
+        col = 0
         for l, x in zip(st, xs):
-            obuf = torch.empty((4, M, l.N), dtype=torch.float16, device=dev)
-            outs = [obuf[k] for k in range(4)]
+            outs = [send[k, :, col:col + l.N] for k in range(4)]
+            col += l.N
             pk = l.pack
             args_c = (x.data_ptr(), x.stride(0), x.stride(1), l.codes.data_ptr(), l.K,
                       _lib.ptr(l.plug_idx), _lib.ptr(l.plug_vals), _lib.ptr(l.plug_window_base),
                       ctypes.c_uint32(l.offset & 0xFFFFFFFF),
-                      _lib.ptrs(pk.luts, 7), _lib.floats4(pk.scales), _lib.ptrs(outs, 4),
+                      pk.tables.data_ptr(), _lib.floats4(pk.scales), _lib.ptrs(outs, 4),
                       outs[0].stride(0), outs[0].stride(1), M, l.N, l.K, ws.data_ptr(), ws.numel(), sh)
-            gbuf = None
-            if world > 1:
-                gbuf = (obuf, torch.empty((world, 4, M, l.N), dtype=torch.float16, device=dev))
-            row.append((args_c, outs, gbuf, l))
+            row.append((args_c, outs, l))
         calls.append(row)
+        recv = torch.empty((world * 4, M, sum(widths)), dtype=torch.float16, device=dev) if world > 1 else None
+        gathers.append((send, recv))
 
     def launch(args_c):
-        rc = lib.pp_quad_linear(*args_c)
+        rc = lib.pp_quad_linear_prepared(*args_c)
         if rc:
             _lib.check(rc)
 
     def step(i):
-        for args_c, outs, gbuf, l in calls[i % len(calls)]:
+        for args_c, outs, l in calls[i % len(calls)]:
             launch(args_c)
-            if gbuf is not None:
-                # the 4 models' row shards, gathered over ranks
-                dist.all_gather_into_tensor(gbuf[1], gbuf[0])
+        if world > 1:
+            send, recv = gathers[i % len(gathers)]
+            dist.all_gather_into_tensor(recv, send)   # the 4 models' row shards of all 4 Linears
 
     per_step_bytes = sum(layer_bytes(l.N, l.K, l.p_hi - l.p_lo, M) for l in full_sets[0])
     avg_bytes = statistics.mean(sum(layer_bytes(l.N, l.K, l.p_hi - l.p_lo, M) for l in fs) for fs in full_sets)
@@ -304,12 +309,12 @@ def run_ours(args):
             l = st[j]
             outs = [torch.empty((M, l.N), dtype=torch.float16, device=dev) for _ in range(4)]
             gemv_args.append((xs[j].data_ptr(), xs[j].stride(0), xs[j].stride(1), l.codes.data_ptr(), 1, l.K,
-                              _lib.ptrs(l.pack.luts, 7), _lib.floats4(l.pack.scales), _lib.ptrs(outs, 4),
+                              l.pack.tables.data_ptr(), _lib.floats4(l.pack.scales), _lib.ptrs(outs, 4),
                               outs[0].stride(0), outs[0].stride(1), M, l.N, l.K, ws.data_ptr(), ws.numel(), sh,
                               outs))
         def gemv_pass():
             for a_ in gemv_args:
-                _lib.check(lib.pp_quad_gemm(*a_[:-1]))
+                _lib.check(lib.pp_quad_gemm_prepared(*a_[:-1]))
         gemv_pass()
         reps = max(4, K_steps // 2)
         torch.cuda.synchronize(dev)
@@ -335,7 +340,7 @@ def run_ours(args):
         kernel_ms += tj
 
     # e2e through the public API with host buffers (pinned), 1 GPU view of rank's work
-    e2e = run_e2e(torch, dist, sets, xs, dev, args, world, M)
+    e2e = run_e2e(torch, dist, sets, xs, dev, args, world, M, full_sets)
 
     peak, peak_kind = measured_peak()
     achieved = kernel_bytes / (kernel_ms * 1e-3) / 1e9
@@ -348,7 +353,8 @@ def run_ours(args):
         "config": {"workload": WORKLOAD, "batch": M, "replica_streams": args.replicas,
                    "bytes_per_step": int(per_step_bytes), "l2": "inputs per step ~200 MB > 126 MB L2, "
                    "4 rotating replica streams (no flush)",
-                   "parallelism": f"row-sharded x{world} + NCCL all-gather" if world > 1 else "single GPU",
+                   "parallelism": f"row-sharded x{world}, one NCCL all-gather per step" if world > 1
+                                  else "single GPU",
                    "timing": ("CUDA graph replay of whole steps" if use_graphs else "eager launches") +
                              ("; launch overlap on" if not args.no_overlap else ""),
                    "per_shape_gemv_kernel": per_shape},
@@ -366,6 +372,9 @@ def run_ours(args):
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         res["cpu_baseline"] = cpu_baseline(streams[0], M, budget_s=args.cpu_seconds)
+    # graphs that hold NCCL calls must be released before the process group
+    graphs.clear()
+    torch.cuda.synchronize(dev)
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
@@ -373,25 +382,31 @@ def run_ours(args):
         print(json.dumps(res))
 
 
-def run_e2e(torch, dist, sets, xs, dev, args, world, M):
+def run_e2e(torch, dist, sets, xs, dev, args, world, M, full_sets):
     """Same metric through the public API: pinned H2D of each step's inputs,
-    the Linear calls, D2H of the four outputs, all inside the timed region."""
+    the Linear calls (with N > 1 GPUs the row-sharded Linear, whose outputs
+    are all-gathered over NCCL), D2H of the four full outputs, all inside the
+    timed region."""
+    from polar_pack_b200.parallel import RowShardedGroup
     from polar_pack_b200.quadpack import quad_linear
     stream = torch.cuda.current_stream(dev)
     hx = [x.cpu().pin_memory() for x in xs]
     h2d = sum(x.numel() * 2 for x in hx)
     d2h = 0
     host_out = []
-    for l in sets[0]:
-        host_out.append([torch.empty((M, l.N), dtype=torch.float16).pin_memory() for _ in range(4)])
-        d2h += 4 * M * l.N * 2
+    full_n = [N for _, N in SHAPES]
+    for N in full_n:
+        host_out.append([torch.empty((M, N), dtype=torch.float16).pin_memory() for _ in range(4)])
+        d2h += 4 * M * N * 2
     dx = [torch.empty_like(x) for x in xs]
+    # the four independent Linears as one row-sharded group: one all-gather per step
+    groups = [RowShardedGroup([lambda x, l=l: quad_linear(x, l) for l in st], full_n) for st in sets]
 
     def step(i):
-        st = sets[i % len(sets)]
-        for j, l in enumerate(st):
+        for j in range(len(dx)):
             dx[j].copy_(hx[j], non_blocking=True)
-            ys = quad_linear(dx[j], l)
+        yss = groups[i % len(groups)](dx)
+        for j, ys in enumerate(yss):
             for k in range(4):
                 host_out[j][k].copy_(ys[k], non_blocking=True)
 
@@ -411,11 +426,10 @@ def run_e2e(torch, dist, sets, xs, dev, args, world, M):
         t = torch.tensor([ms], dtype=torch.float64, device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms = float(t.item())
-    total = 0
+    total = 0  # whole-job bytes: the full Linears (every rank streams its row shard)
     for i in range(args.steps):
-        for l in sets[(args.warmup + i) % len(sets)]:
+        for l in full_sets[(args.warmup + i) % len(full_sets)]:
             total += layer_bytes(l.N, l.K, l.p_hi - l.p_lo, M)
-    total *= world  # every rank streams its shard
     return {"value": round(total / (ms * 1e-3) / 1e9, 1), "unit": UNIT, "h2d_bytes_per_step": int(h2d),
             "d2h_bytes_per_step": int(d2h), "api": "polar_pack_b200.quadpack.quad_linear"}
 

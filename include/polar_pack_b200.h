@@ -108,6 +108,27 @@ PP_API int pp_quad_gemm_static_scratch(const void* a, int64_t lda_m, int64_t lda
                                        void* const out[4], int64_t ldo_m, int64_t ldo_n,
                                        int64_t M, int64_t N, int64_t K, void* stream);
 
+/* Prepared tables: the replicated shared-memory image of the seven FP16
+ * tables (128 KiB, pp_quad_tables_bytes), written once by
+ * pp_quad_prepare_tables into a caller-allocated, 16-byte aligned device
+ * buffer.  The *_prepared entry points take it instead of `luts`: their
+ * kernels copy it into shared memory with bulk copies instead of building
+ * the replicas, which shortens every launch.  No counterpart in the
+ * reference (its kernel reads the seven tables directly).  The image must
+ * be prepared again whenever the tables change.
+ */
+PP_API int pp_quad_tables_bytes(size_t* bytes);
+
+PP_API int pp_quad_prepare_tables(const void* const luts[7], void* tables, void* stream);
+
+/* pp_quad_gemm with prepared tables. */
+PP_API int pp_quad_gemm_prepared(const void* a, int64_t lda_m, int64_t lda_k,
+                                 const uint32_t* codes, int64_t ldc_k, int64_t ldc_n,
+                                 const void* tables, const float scales[4],
+                                 void* const out[4], int64_t ldo_m, int64_t ldo_n,
+                                 int64_t M, int64_t N, int64_t K,
+                                 void* workspace, size_t workspace_bytes, void* stream);
+
 /* File-layout fused Linear with plug-table merge, the per-Linear decode of a
  * `.quadpack` stream (reference quaternion_packer.py:141-214: the codes of one
  * nn.Linear are (out=N, in=K) row-major at a flat stream offset; plug entries
@@ -137,6 +158,16 @@ PP_API int pp_quad_linear(const void* x, int64_t ldx_m, int64_t ldx_k,
                           void* const out[4], int64_t ldo_m, int64_t ldo_n,
                           int64_t M, int64_t N, int64_t K,
                           void* workspace, size_t workspace_bytes, void* stream);
+
+/* pp_quad_linear with prepared tables. */
+PP_API int pp_quad_linear_prepared(const void* x, int64_t ldx_m, int64_t ldx_k,
+                                   const uint32_t* codes, int64_t ldw,
+                                   const uint32_t* plug_idx, const void* plug_vals,
+                                   const uint32_t* plug_window_base, uint32_t base_lo32,
+                                   const void* tables, const float scales[4],
+                                   void* const out[4], int64_t ldo_m, int64_t ldo_n,
+                                   int64_t M, int64_t N, int64_t K,
+                                   void* workspace, size_t workspace_bytes, void* stream);
 
 /* Load-time preparation of one Linear's plug entries for pp_quad_linear:
  *  - plug_window_base[w] (uint32, N * ceil(K/64) + 1 entries) := number of

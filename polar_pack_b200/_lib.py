@@ -38,6 +38,13 @@ _SIGNATURES = {
                       _i64, _i64, _i64, _c_void_p, _size_t, _c_void_p], _int),
     "pp_quad_gemm_static_scratch": ([_c_void_p, _i64, _i64, _c_void_p, _i64, _i64, _PTR7, _F4, _PTR4, _i64,
                                      _i64, _i64, _i64, _i64, _c_void_p], _int),
+    "pp_quad_tables_bytes": ([ctypes.POINTER(_size_t)], _int),
+    "pp_quad_prepare_tables": ([_PTR7, _c_void_p, _c_void_p], _int),
+    "pp_quad_gemm_prepared": ([_c_void_p, _i64, _i64, _c_void_p, _i64, _i64, _c_void_p, _F4, _PTR4, _i64, _i64,
+                               _i64, _i64, _i64, _c_void_p, _size_t, _c_void_p], _int),
+    "pp_quad_linear_prepared": ([_c_void_p, _i64, _i64, _c_void_p, _i64, _c_void_p, _c_void_p, _c_void_p, _u32,
+                                 _c_void_p, _F4, _PTR4, _i64, _i64, _i64, _i64, _i64, _c_void_p, _size_t,
+                                 _c_void_p], _int),
     "pp_quad_linear_workspace_bytes": ([_i64, _i64, _i64, ctypes.POINTER(_size_t)], _int),
     "pp_quad_linear": ([_c_void_p, _i64, _i64, _c_void_p, _i64, _c_void_p, _c_void_p, _c_void_p, _u32,
                         _PTR7, _F4, _PTR4, _i64, _i64, _i64, _i64, _i64, _c_void_p, _size_t,
@@ -151,6 +158,36 @@ def set_launch_overlap(enable: bool) -> bool:
     stream.  Returns the previous setting.
     """
     return bool(load().pp_set_launch_overlap(1 if enable else 0))
+
+
+# -------------------------------------------------------- prepared tables --
+_tables: dict = {}
+_TABLES_MAX = 64
+
+
+def prepare_tables(luts, device: torch.device) -> torch.Tensor:
+    """The 128 KiB replicated-table image of seven FP16[256] tables
+    (``pp_quad_prepare_tables``), on the current stream of ``device``."""
+    nbytes = _size_t()
+    check(load().pp_quad_tables_bytes(ctypes.byref(nbytes)))
+    t = torch.empty(nbytes.value, dtype=torch.uint8, device=device)
+    call("pp_quad_prepare_tables", ptrs(luts, 7), t.data_ptr(), stream_handle(device))
+    return t
+
+
+def cached_tables(luts, device: torch.device) -> torch.Tensor:
+    """Prepared tables for ``luts``, cached by the tensors' storage address
+    and version counter (an in-place change of a table misses the cache).
+    Each entry keeps references to its seven tensors, so no other tensor can
+    take over one of those addresses while the entry exists."""
+    key = (device.index,) + tuple((t.data_ptr(), t._version) for t in luts)
+    hit = _tables.get(key)
+    if hit is None:
+        if len(_tables) >= _TABLES_MAX:
+            _tables.pop(next(iter(_tables)))
+        hit = (list(luts), prepare_tables(luts, device))
+        _tables[key] = hit
+    return hit[1]
 
 
 # ------------------------------------------------------------- workspace --

@@ -109,13 +109,23 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity,
   return false;
 }
 
-// 2D tiled TMA load (no multicast) completing on `bar`.  x is the innermost
+// 2D tiled TMA load into this CTA's shared memory, completing on `bar`.  x is the innermost
 // coordinate; x * element size must be a multiple of 16 bytes.
 __device__ __forceinline__ void tma_load_2d(uint32_t dst, const void* tmap, int x, int y, uint32_t bar) {
   asm volatile(
       "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], "
       "[%4];" ::"r"(dst),
       "l"(tmap), "r"(x), "r"(y), "r"(bar)
+      : "memory");
+}
+
+// Bulk copy (no tensor map, no multicast) of `bytes` from global memory to
+// this CTA's shared memory, completing on `bar`.  Both addresses 16-byte
+// aligned, bytes a multiple of 16.
+__device__ __forceinline__ void bulk_load(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
+      "l"(src), "r"(bytes), "r"(bar)
       : "memory");
 }
 
@@ -185,6 +195,15 @@ __device__ __forceinline__ void quad_lut_fanout(uint8_t* lut, const uint32_t* st
     *reinterpret_cast<uint4*>(lut + lut_off(t) + (uint32_t)e * 256u + (uint32_t)part * 16u) =
         make_uint4(w, w, w, w);
   }
+}
+
+// Prepared tables: the same 128 KiB image, written once to global memory
+// (pp_quad_prepare_tables) and copied into shared memory as is.  Thread
+// `i` of the preparing grid writes 16-byte chunk i.
+__device__ __forceinline__ uint32_t quad_table_word(const __half* const* luts, int t, int e) {
+  const uint16_t* lo = reinterpret_cast<const uint16_t*>(luts[t == 0 ? 0 : 2 * t - 1]);
+  const uint16_t* hi = reinterpret_cast<const uint16_t*>(luts[t == 0 ? 0 : 2 * t]);
+  return (uint32_t)ldg_u16(lo + e) | ((uint32_t)ldg_u16(hi + e) << 16);
 }
 
 // All three steps; called by every thread of the CTA, caller syncs after.

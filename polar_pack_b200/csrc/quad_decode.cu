@@ -201,7 +201,52 @@ static int quad_decode_impl(const uint32_t* codes, int64_t ldc_r, int64_t ldc_c,
 
 }  // namespace pp
 
+namespace pp {
+
+// The 128 KiB shared-memory image of the replicated quad tables (the same
+// bytes quad_lut_fanout writes): thread i writes 16-byte chunk i.
+struct QuadLutPtrs {
+  const __half* luts[7];
+};
+
+__global__ void __launch_bounds__(256) quad_prepare_tables_kernel(const QuadLutPtrs p, uint8_t* tables) {
+  const int idx = blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= 4 * 256 * 8) return;
+  const int t = idx >> 11, e = (idx >> 3) & 255, part = idx & 7;
+  const uint32_t w = quad_table_word(p.luts, t, e);
+  *reinterpret_cast<uint4*>(tables + lut_off(t) + (uint32_t)e * 256u + (uint32_t)part * 16u) = make_uint4(w, w, w, w);
+}
+
+}  // namespace pp
+
 extern "C" {
+
+int pp_quad_tables_bytes(size_t* bytes) {
+  if (!bytes) {
+    pp::set_error("bytes must not be NULL");
+    return PP_ERR_INVALID;
+  }
+  *bytes = pp::kQuadLutBytes;
+  return PP_OK;
+}
+
+int pp_quad_prepare_tables(const void* const luts[7], void* tables, void* stream) {
+  if (!luts || !tables || !pp::aligned(tables, 16)) {
+    pp::set_error("luts and a 16-byte aligned tables buffer are required");
+    return PP_ERR_INVALID;
+  }
+  pp::QuadLutPtrs prm{};
+  for (int i = 0; i < 7; ++i) {
+    if (!luts[i]) {
+      pp::set_error("luts[%d] is NULL", i);
+      return PP_ERR_INVALID;
+    }
+    prm.luts[i] = reinterpret_cast<const __half*>(luts[i]);
+  }
+  pp::quad_prepare_tables_kernel<<<32, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      prm, reinterpret_cast<uint8_t*>(tables));
+  return pp::check_launch("quad_prepare_tables_kernel");
+}
 
 int pp_quad_decode(const uint32_t* codes, int64_t ldc_r, int64_t ldc_c, int64_t R, int64_t C,
                    const void* const luts[7], const float* scales, void* const out[4], int64_t ldo_r,

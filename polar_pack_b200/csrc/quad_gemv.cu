@@ -54,6 +54,7 @@ struct QuadParams {
   const uint32_t* codes;
   int64_t ldc;  // NK: stride between rows n; KN: stride between rows k
   const __half* luts[7];
+  const uint8_t* tables;  // prepared 128 KiB table image (NULL: build from luts)
   float scale[4];
   __half* out[4];
   int64_t ldo_m, ldo_n;
@@ -307,17 +308,20 @@ __host__ __device__ inline uint32_t quad_scratch_bytes(bool nk, int nb, int M) {
   return (uint32_t)red_bytes(quad_warps(nk, nb), 4, M, nk ? 8 : 32);
 }
 
-// Before the first barrier: the table words (their loads issued first, to
-// registers, then staged) and the per-CTA int tables.  Between the barriers lane 0 of every
-// warp initialises its ring and issues its first S units, whose copies
-// then overlap the fan-out of the tables.  After the second barrier every
-// warp streams and reduces on its own; there is no closing barrier.
+// Tables either come prepared (thread 0 bulk-copies the 128 KiB image, which
+// every thread then waits for on one mbarrier) or are built here (the table
+// words, their loads issued first, are staged before the first barrier and
+// fanned out after it).  Before the first barrier the per-CTA int tables
+// are filled; after it lane 0 of every warp initialises its ring and issues
+// its first S units, whose copies overlap the table build or copy.  Then
+// every warp streams and reduces on its own; there is no closing barrier.
 template <bool NK, int NB>
 __global__ void __launch_bounds__(quad_warps(NK, NB) * 32, 1) quad_gemv_kernel(const __grid_constant__ QuadParams p) {
   constexpr int NW = quad_warps(NK, NB);
   pdl_launch_dependents();
+  const bool prepared = p.tables != nullptr;
   uint32_t v[kLutWordsPerThread];
-  quad_lut_load(v, p.luts);
+  if (!prepared) quad_lut_load(v, p.luts);
   const uint32_t base = (uint32_t)__cvta_generic_to_shared(pp_smem);
   int* status = p.part.counters + (kMaxGrid - 1);
   const QuadLayout L = base == p.layout_base
@@ -329,6 +333,13 @@ __global__ void __launch_bounds__(quad_warps(NK, NB) * 32, 1) quad_gemv_kernel(c
   }
   const int cu0 = p.cta_start[blockIdx.x], cu1 = p.cta_start[blockIdx.x + 1];
   if (cu0 >= cu1) return;  // uniform over the CTA
+  const uint32_t tbar = L.flag;  // mbarrier of the prepared-table copies
+  if (prepared && threadIdx.x == 0) {
+    mbar_init(tbar, 1);
+    fence_mbar_init();
+    mbar_expect_tx(tbar, kQuadLutBytes);
+    for (uint32_t off = 0; off < kQuadLutBytes; off += 16384u) bulk_load(L.lut + off, p.tables + off, 16384u, tbar);
+  }
   Partition pt = p.part;
   pt.cta_start = p.cta_start;
   int* ti = reinterpret_cast<int*>(pp_smem + (L.tables - base));
@@ -345,7 +356,7 @@ __global__ void __launch_bounds__(quad_warps(NK, NB) * 32, 1) quad_gemv_kernel(c
     rg.next.init(wu0, wu1, p.part.upt);
   }
   uint32_t* stage = reinterpret_cast<uint32_t*>(pp_smem + (L.scratch - base));
-  quad_lut_stage(stage, v);
+  if (!prepared) quad_lut_stage(stage, v);
   __syncthreads();
   if (wu0 < wu1 && (threadIdx.x & 31) == 0) {
     if (warp == 0) prefetch_tmap(&p.tmap);
@@ -353,8 +364,12 @@ __global__ void __launch_bounds__(quad_warps(NK, NB) * 32, 1) quad_gemv_kernel(c
       QuadOp<NK, NB, false>::issue(p, slot, bar, tile, kc);
     }, 2048u);
   }
-  quad_lut_fanout(pp_smem + (L.lut - base), stage);
-  __syncthreads();
+  if (prepared) {
+    mbar_wait_bounded(tbar, 0u, status);
+  } else {
+    quad_lut_fanout(pp_smem + (L.lut - base), stage);
+    __syncthreads();
+  }
   // everything above reads only weights; activations, the workspace and the
   // outputs may belong to the previous kernel of the stream
   pdl_wait();
@@ -371,6 +386,7 @@ struct QuadGenericParams {
   const uint32_t* codes;
   int64_t ldc_k, ldc_n;
   const __half* luts[7];
+  const uint8_t* tables;  // prepared image (NULL: read luts)
   float scale[4];
   __half* out[4];
   int64_t ldo_m, ldo_n;
@@ -382,7 +398,9 @@ __global__ void quad_generic_kernel(const QuadGenericParams p) {
   for (int i = threadIdx.x; i < 1024; i += blockDim.x) {
     const int t = i >> 8, e = i & 255;
     uint32_t v;
-    if (t == 0) {
+    if (p.tables) {  // lane copy 0 of entry e of table t
+      v = __ldg(reinterpret_cast<const uint32_t*>(p.tables + lut_off(t) + (uint32_t)e * 256u));
+    } else if (t == 0) {
       const uint32_t r = ldg_u16(reinterpret_cast<const uint16_t*>(p.luts[0]) + e);
       v = r | (r << 16);
     } else {
@@ -498,8 +516,8 @@ bool quad_vector_ok(bool nk, const uint32_t* codes, int64_t ldc_k, int64_t ldc_n
   return ldc_n == 1 && ldc_k % 4 == 0 && N % 4 == 0 && ldc_k >= N;
 }
 
-int check_common(const void* const luts[7], const float scales[4], void* const out[4], int64_t M,
-                 int64_t N, int64_t K) {
+int check_common(const void* const luts[7], const void* tables, const float scales[4], void* const out[4],
+                 int64_t M, int64_t N, int64_t K) {
   if (M < 0 || N < 0 || K < 0) {
     set_error("negative shape M=%lld N=%lld K=%lld", (long long)M, (long long)N, (long long)K);
     return PP_ERR_INVALID;
@@ -508,15 +526,20 @@ int check_common(const void* const luts[7], const float scales[4], void* const o
     set_error("N and K must fit in 32 bits");
     return PP_ERR_INVALID;
   }
-  if (!luts || !scales || !out) {
-    set_error("luts, scales and out must not be NULL");
+  if (!scales || !out || (!luts && !tables)) {
+    set_error("luts (or prepared tables), scales and out must not be NULL");
     return PP_ERR_INVALID;
   }
-  for (int i = 0; i < 7; ++i)
-    if (!luts[i]) {
-      set_error("luts[%d] is NULL", i);
-      return PP_ERR_INVALID;
-    }
+  if (tables && !aligned(tables, 16)) {
+    set_error("prepared tables must be 16-byte aligned");
+    return PP_ERR_INVALID;
+  }
+  if (!tables)
+    for (int i = 0; i < 7; ++i)
+      if (!luts[i]) {
+        set_error("luts[%d] is NULL", i);
+        return PP_ERR_INVALID;
+      }
   for (int i = 0; i < 4; ++i)
     if (!out[i] && M > 0 && N > 0) {
       set_error("out[%d] is NULL", i);
@@ -537,10 +560,10 @@ size_t quad_ws_bytes(bool nk, int64_t M, int64_t N, int64_t K, bool plug) {
 static int quad_run(const void* a, int64_t lda_m, int64_t lda_k, const uint32_t* codes, int64_t ldc_k,
                     int64_t ldc_n, const uint32_t* plug_idx, const void* plug_vals, const uint32_t* wbase,
                     uint32_t base_lo32,
-                    const void* const luts[7], const float scales[4], void* const out[4], int64_t ldo_m,
-                    int64_t ldo_n, int64_t M, int64_t N, int64_t K, void* ws, size_t ws_bytes,
+                    const void* const luts[7], const void* tables, const float scales[4], void* const out[4],
+                    int64_t ldo_m, int64_t ldo_n, int64_t M, int64_t N, int64_t K, void* ws, size_t ws_bytes,
                     cudaStream_t s, bool file_layout) {
-  int rc = check_common(luts, scales, out, M, N, K);
+  int rc = check_common(luts, tables, scales, out, M, N, K);
   if (rc) return rc;
   if (M == 0 || N == 0) return PP_OK;
   if (K == 0) {
@@ -574,7 +597,8 @@ static int quad_run(const void* a, int64_t lda_m, int64_t lda_k, const uint32_t*
     g.codes = codes;
     g.ldc_k = ldc_k;
     g.ldc_n = ldc_n;
-    for (int i = 0; i < 7; ++i) g.luts[i] = reinterpret_cast<const __half*>(luts[i]);
+    for (int i = 0; i < 7; ++i) g.luts[i] = luts ? reinterpret_cast<const __half*>(luts[i]) : nullptr;
+    g.tables = reinterpret_cast<const uint8_t*>(tables);
     for (int i = 0; i < 4; ++i) {
       g.scale[i] = scales[i];
       g.out[i] = reinterpret_cast<__half*>(out[i]);
@@ -605,7 +629,8 @@ static int quad_run(const void* a, int64_t lda_m, int64_t lda_k, const uint32_t*
   prm.ldx_k = lda_k;
   prm.codes = codes;
   prm.ldc = nk ? ldc_n : ldc_k;
-  for (int i = 0; i < 7; ++i) prm.luts[i] = reinterpret_cast<const __half*>(luts[i]);
+  for (int i = 0; i < 7; ++i) prm.luts[i] = luts ? reinterpret_cast<const __half*>(luts[i]) : nullptr;
+  prm.tables = reinterpret_cast<const uint8_t*>(tables);
   for (int i = 0; i < 4; ++i) prm.scale[i] = scales[i];
   prm.ldo_m = ldo_m;
   prm.ldo_n = ldo_n;
@@ -668,8 +693,21 @@ int pp_quad_gemm(const void* a, int64_t lda_m, int64_t lda_k, const uint32_t* co
                  int64_t ldc_n, const void* const luts[7], const float scales[4], void* const out[4],
                  int64_t ldo_m, int64_t ldo_n, int64_t M, int64_t N, int64_t K, void* workspace,
                  size_t workspace_bytes, void* stream) {
-  return pp::quad_run(a, lda_m, lda_k, codes, ldc_k, ldc_n, nullptr, nullptr, nullptr, 0u, luts, scales, out,
-                      ldo_m, ldo_n, M, N, K, workspace, workspace_bytes,
+  return pp::quad_run(a, lda_m, lda_k, codes, ldc_k, ldc_n, nullptr, nullptr, nullptr, 0u, luts, nullptr, scales,
+                      out, ldo_m, ldo_n, M, N, K, workspace, workspace_bytes,
+                      reinterpret_cast<cudaStream_t>(stream), false);
+}
+
+int pp_quad_gemm_prepared(const void* a, int64_t lda_m, int64_t lda_k, const uint32_t* codes, int64_t ldc_k,
+                          int64_t ldc_n, const void* tables, const float scales[4], void* const out[4],
+                          int64_t ldo_m, int64_t ldo_n, int64_t M, int64_t N, int64_t K, void* workspace,
+                          size_t workspace_bytes, void* stream) {
+  if (!tables) {
+    pp::set_error("tables must not be NULL");
+    return PP_ERR_INVALID;
+  }
+  return pp::quad_run(a, lda_m, lda_k, codes, ldc_k, ldc_n, nullptr, nullptr, nullptr, 0u, nullptr, tables,
+                      scales, out, ldo_m, ldo_n, M, N, K, workspace, workspace_bytes,
                       reinterpret_cast<cudaStream_t>(stream), false);
 }
 
@@ -688,8 +726,21 @@ int pp_quad_linear(const void* x, int64_t ldx_m, int64_t ldx_k, const uint32_t* 
                    int64_t ldo_m, int64_t ldo_n, int64_t M, int64_t N, int64_t K, void* workspace,
                    size_t workspace_bytes, void* stream) {
   return pp::quad_run(x, ldx_m, ldx_k, codes, 1, ldw, plug_idx, plug_vals, plug_window_base, base_lo32, luts,
-                      scales, out,
-                      ldo_m, ldo_n, M, N, K, workspace, workspace_bytes,
+                      nullptr, scales, out, ldo_m, ldo_n, M, N, K, workspace, workspace_bytes,
+                      reinterpret_cast<cudaStream_t>(stream), true);
+}
+
+int pp_quad_linear_prepared(const void* x, int64_t ldx_m, int64_t ldx_k, const uint32_t* codes, int64_t ldw,
+                            const uint32_t* plug_idx, const void* plug_vals, const uint32_t* plug_window_base,
+                            uint32_t base_lo32, const void* tables, const float scales[4], void* const out[4],
+                            int64_t ldo_m, int64_t ldo_n, int64_t M, int64_t N, int64_t K, void* workspace,
+                            size_t workspace_bytes, void* stream) {
+  if (!tables) {
+    pp::set_error("tables must not be NULL");
+    return PP_ERR_INVALID;
+  }
+  return pp::quad_run(x, ldx_m, ldx_k, codes, 1, ldw, plug_idx, plug_vals, plug_window_base, base_lo32, nullptr,
+                      tables, scales, out, ldo_m, ldo_n, M, N, K, workspace, workspace_bytes,
                       reinterpret_cast<cudaStream_t>(stream), true);
 }
 

@@ -73,6 +73,58 @@ class RowShardedLinear:
         return outs
 
 
+class RowShardedGroup:
+    """Several independent row-sharded Linears with ONE all-gather.
+
+    For Linears that do not feed each other (q/k/v, gate/up, or the
+    benchmark's sweep), every rank computes its row shard of each, packs the
+    ``n_out`` outputs of all of them into one buffer, and a single collective
+    gathers everything; ``__call__(xs)`` returns, per Linear, ``n_out`` full
+    ``(M, N_j)`` tensors.  One collective instead of one per Linear.
+    """
+
+    def __init__(self, local_fns: Sequence[Callable[[torch.Tensor], Sequence[torch.Tensor]]],
+                 Ns: Sequence[int], group=None, n_out: int = 4):
+        if len(local_fns) != len(Ns):
+            raise ValueError("one local function per Linear")
+        self.local_fns = list(local_fns)
+        self.Ns = list(Ns)
+        self.group = group
+        self.world = dist.get_world_size(group) if dist.is_initialized() else 1
+        self.rank = dist.get_rank(group) if dist.is_initialized() else 0
+        self.widths = [shard_width(N, self.world) for N in self.Ns]
+        self.n_out = n_out
+
+    def __call__(self, xs: Sequence[torch.Tensor]) -> list[list[torch.Tensor]]:
+        M = xs[0].shape[0]
+        locals_ = [fn(x) for fn, x in zip(self.local_fns, xs)]
+        if self.world == 1:
+            return [list(l) for l in locals_]
+        total = sum(self.widths)
+        dev, dt = locals_[0][0].device, locals_[0][0].dtype
+        send = torch.zeros((self.n_out, M, total), dtype=dt, device=dev)
+        col = 0
+        for loc, w in zip(locals_, self.widths):
+            for k in range(self.n_out):
+                send[k, :, col:col + loc[k].shape[1]] = loc[k]
+            col += w
+        recv = torch.empty((self.world * self.n_out, M, total), dtype=dt, device=dev)
+        dist.all_gather_into_tensor(recv, send, group=self.group)
+        recv = recv.view(self.world, self.n_out, M, total)
+        res, col = [], 0
+        for N, w in zip(self.Ns, self.widths):
+            outs = []
+            for k in range(self.n_out):
+                parts = []
+                for r in range(self.world):
+                    a, b = row_shard(N, self.world, r)
+                    parts.append(recv[r, k, :, col:col + b - a])
+                outs.append(torch.cat(parts, dim=1))
+            res.append(outs)
+            col += w
+        return res
+
+
 def shard_quad_linear(pack, offset: int, N: int, K: int, world: int, rank: int):
     """This rank's row slice of the packed Linear at flat ``offset`` (file layout)."""
     n0, n1 = row_shard(N, world, rank)

@@ -95,9 +95,10 @@ def quad_bitpacked(a, codes, luts, scales):
     _lib.check(lib.pp_quad_gemm_workspace_bytes(M, N, K, codes.stride(0), codes.stride(1),
                                                 _lib.ctypes.byref(nbytes)))
     ws = _lib.workspace(dev, nbytes.value) if nbytes.value else None
-    _lib.call("pp_quad_gemm", a.data_ptr(), a.stride(0), a.stride(1),
+    tables = _lib.cached_tables(luts, dev)   # replicated image, prepared once per table set
+    _lib.call("pp_quad_gemm_prepared", a.data_ptr(), a.stride(0), a.stride(1),
               codes.data_ptr(), codes.stride(0), codes.stride(1),
-              _lib.ptrs(luts, 7), _lib.floats4(scales), _lib.ptrs(outs, 4),
+              tables.data_ptr(), _lib.floats4(scales), _lib.ptrs(outs, 4),
               outs[0].stride(0), outs[0].stride(1), M, N, K,
               _lib.ptr(ws), ws.numel() if ws is not None else 0, _lib.stream_handle(dev))
     return outs

@@ -149,6 +149,8 @@ class QuadPackDevice:
         self.plug_idx = torch.from_numpy(np.asarray(f.plug_idx).view(np.int32)).to(self.device)
         self.plug_vals = torch.from_numpy(np.ascontiguousarray(f.plug_vals)).to(self.device)
         self.luts = [t.to(self.device) for t in quad_luts(h.r_max, MU)]
+        # replicated shared-memory image of the tables, copied in by each launch
+        self.tables = _lib.prepare_tables(self.luts, self.device)
         self.scales = [float(s) for s in h.scales]
         self._bad = torch.zeros(1, dtype=torch.int32, device=self.device)
 
@@ -224,10 +226,10 @@ def quad_linear(x: torch.Tensor, layer: QuadLinearSlice, out=None) -> list[torch
     nb = quad_linear_workspace_bytes(M, layer.N, layer.K)
     ws = _lib.workspace(dev, nb) if nb else None
     pk = layer.pack
-    _lib.call("pp_quad_linear", x.data_ptr(), x.stride(0), x.stride(1), layer.codes.data_ptr(), layer.K,
+    _lib.call("pp_quad_linear_prepared", x.data_ptr(), x.stride(0), x.stride(1), layer.codes.data_ptr(), layer.K,
               _lib.ptr(layer.plug_idx), _lib.ptr(layer.plug_vals), _lib.ptr(layer.plug_window_base),
               ctypes.c_uint32(layer.offset & 0xFFFFFFFF),
-              _lib.ptrs(pk.luts, 7), _lib.floats4(pk.scales), _lib.ptrs(out, 4),
+              pk.tables.data_ptr(), _lib.floats4(pk.scales), _lib.ptrs(out, 4),
               out[0].stride(0), out[0].stride(1), M, layer.N, layer.K,
               _lib.ptr(ws), ws.numel() if ws is not None else 0, _lib.stream_handle(dev))
     return out
@@ -352,6 +354,7 @@ class DevicePackedStream(QuadPackDevice):
             torch.zeros(0, dtype=torch.int32, device=self.device)
         self.plug_vals = p["plug_vals"].contiguous()
         self.luts = [t.to(self.device) for t in quad_luts(p["r_max"], MU)]
+        self.tables = _lib.prepare_tables(self.luts, self.device)
         self.scales = [float(x) for x in p["scales"]]
         self._bad = torch.zeros(1, dtype=torch.int32, device=self.device)
 

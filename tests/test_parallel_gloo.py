@@ -76,6 +76,50 @@ def test_row_sharded_gather_matches_full(N):
     assert all(shapes == [(M, N)] * 4 for _, _, shapes in res)
 
 
+def _worker_group(rank, world, port, Ns, K, M, q):
+    try:
+        sys.path.insert(0, str(ROOT))
+        from polar_pack_b200.parallel import RowShardedGroup, row_shard
+        _init(rank, world, port)
+        rng = np.random.default_rng(1)
+        wss = [[rng.normal(0, 0.02, (N, K)).astype(np.float16) for _ in range(4)] for N in Ns]
+        xs = [rng.normal(0, 1, (M, K)).astype(np.float16) for _ in Ns]
+
+        def make(ws, N):
+            n0, n1 = row_shard(N, world, rank)
+            return lambda xt: [torch.from_numpy((xt.numpy().astype(np.float64) @ w[n0:n1].T.astype(np.float64))
+                                                .astype(np.float16)) for w in ws]
+
+        grp = RowShardedGroup([make(ws, N) for ws, N in zip(wss, Ns)], Ns)
+        outs = grp([torch.from_numpy(x) for x in xs])
+        ok = True
+        for o, ws, x in zip(outs, wss, xs):
+            full = [(x.astype(np.float64) @ w.T.astype(np.float64)).astype(np.float16) for w in ws]
+            ok &= all(np.array_equal(a.numpy(), f) for a, f in zip(o, full))
+        q.put((rank, ok, [tuple(t.shape) for o in outs for t in o]))
+        dist.destroy_process_group()
+    except Exception as e:
+        q.put((rank, False, repr(e)))
+
+
+def test_grouped_gather_matches_full():
+    """Several Linears of different widths (one not divisible by the world
+    size) gathered by one collective."""
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    world, K, M, Ns = 2, 20, 2, [16, 13, 6]
+    port = free_port()
+    procs = [ctx.Process(target=_worker_group, args=(r, world, port, Ns, K, M, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = [q.get(timeout=120) for _ in procs]
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    assert all(ok for _, ok, _ in res), res
+    assert all(shapes == [(M, N) for N in Ns for _ in range(4)] for _, _, shapes in res)
+
+
 def test_row_shard_bounds():
     from polar_pack_b200.parallel import row_shard, shard_width
     for N in (1, 7, 256, 2048, 11008):
