@@ -211,7 +211,9 @@ def quad_linear(x: torch.Tensor, layer: QuadLinearSlice, out=None) -> list[torch
     """``[y_k]``, ``y_k = fp16(s_k * x @ Wp_k^T)`` for one packed Linear.
 
     ``x`` is FP16 ``(M, K)`` (any strides).  ``Wp_k`` is the FP16 decode with
-    plug values substituted; one kernel launch streams the codes once.
+    plug values substituted; one kernel launch streams the codes once.  The
+    per-Linear C arguments are built once and kept on the slice, so a call
+    costs one output allocation and one library call.
     """
     if x.dim() != 2 or x.shape[1] != layer.K:
         raise ValueError(f"x must be (M, {layer.K}), got {tuple(x.shape)}")
@@ -222,16 +224,22 @@ def quad_linear(x: torch.Tensor, layer: QuadLinearSlice, out=None) -> list[torch
         x = x.contiguous() if x.stride(1) != 1 else x.clone()  # the kernel reads 8-byte activation groups
     M = x.shape[0]
     if out is None:
-        out = [torch.empty((M, layer.N), dtype=torch.float16, device=dev) for _ in range(4)]
-    nb = quad_linear_workspace_bytes(M, layer.N, layer.K)
+        buf = torch.empty((4, M, layer.N), dtype=torch.float16, device=dev)
+        out = [buf[0], buf[1], buf[2], buf[3]]
+    c = layer._ws.get("args")
+    if c is None:
+        pk = layer.pack
+        c = (_lib.load().pp_quad_linear_prepared, layer.codes.data_ptr(), layer.K, _lib.ptr(layer.plug_idx),
+             _lib.ptr(layer.plug_vals), _lib.ptr(layer.plug_window_base), ctypes.c_uint32(layer.offset & 0xFFFFFFFF),
+             pk.tables.data_ptr(), _lib.floats4(pk.scales))
+        layer._ws["args"] = c
+    nb = layer._ws.get(("ws", M))
+    if nb is None:
+        nb = layer._ws[("ws", M)] = quad_linear_workspace_bytes(M, layer.N, layer.K)
     ws = _lib.workspace(dev, nb) if nb else None
-    pk = layer.pack
-    _lib.call("pp_quad_linear_prepared", x.data_ptr(), x.stride(0), x.stride(1), layer.codes.data_ptr(), layer.K,
-              _lib.ptr(layer.plug_idx), _lib.ptr(layer.plug_vals), _lib.ptr(layer.plug_window_base),
-              ctypes.c_uint32(layer.offset & 0xFFFFFFFF),
-              pk.tables.data_ptr(), _lib.floats4(pk.scales), _lib.ptrs(out, 4),
-              out[0].stride(0), out[0].stride(1), M, layer.N, layer.K,
-              _lib.ptr(ws), ws.numel() if ws is not None else 0, _lib.stream_handle(dev))
+    _lib.check(c[0](x.data_ptr(), x.stride(0), x.stride(1), c[1], c[2], c[3], c[4], c[5], c[6], c[7], c[8],
+                    _lib.ptrs(out, 4), out[0].stride(0), out[0].stride(1), M, layer.N, layer.K,
+                    _lib.ptr(ws), ws.numel() if ws is not None else 0, _lib.stream_handle(dev)))
     return out
 
 
