@@ -42,10 +42,12 @@ struct PlugCorrParams {
 int launch_plug_corr(const PlugCorrParams& prm, cudaStream_t s);
 
 // Warps per CTA.  Shared memory holds the 128 KiB tables, each warp's TMA
-// ring (2 KiB per slot) and two partial slots per warp; the KN tile keeps
-// 4x more accumulators and partials per warp, and two batch tiles double
-// them again, so those variants use fewer warps (NB = 8-row batch tiles).
-__host__ __device__ constexpr int quad_warps(bool nk, int nb) { return nk ? (nb == 1 ? 12 : 8) : (nb == 1 ? 8 : 4); }
+// ring (2 KiB per slot) and two partial slots per warp.  The batch-1 file
+// layout runs 16 warps of two ring slots (more warps hide the decode
+// latencies better than deeper rings); the KN tile keeps 4x more
+// accumulators and partials per warp, and two batch tiles double them
+// again, so those variants use fewer warps (NB = 8-row batch tiles).
+__host__ __device__ constexpr int quad_warps(bool nk, int nb) { return nk ? (nb == 1 ? 16 : 8) : (nb == 1 ? 8 : 4); }
 
 struct QuadParams {
   CUtensorMap tmap;  // 2D map over the codes, 128-byte swizzle (first: 64-byte aligned)

@@ -75,7 +75,7 @@ int main() {
   const struct {
     const char* name;
     int nw, tile_w, mmax;
-  } variants[] = {{"nk1", 12, 8, 8}, {"nk2", 8, 8, 16}, {"kn1", 8, 32, 8}, {"kn2", 4, 32, 16}};
+  } variants[] = {{"nk1", 16, 8, 8}, {"nk2", 8, 8, 16}, {"kn1", 8, 32, 8}, {"kn2", 4, 32, 16}};
   const uint32_t bases[] = {0u, 16u, 1024u, 2048u, 4096u, 40000u, 65536u - 1024u, 65536u};
   const uint32_t sizes[] = {232448u, 200000u, 166912u};
   long n = 0;

@@ -233,7 +233,7 @@ def test_tma_engine_closes_every_tile_once(upt, NW):
 
 
 @pytest.mark.parametrize("upt", [1, 3, 16, 32, 172])
-@pytest.mark.parametrize("NW", [4, 8, 12])
+@pytest.mark.parametrize("NW", [4, 8, 12, 16])
 def test_tma_engine_with_host_cta_table(upt, NW):
     """The host's CTA-start table, in both modes, as quad_plan builds it."""
     for tiles in [1, 5, 32, 256, 1376]:
@@ -256,12 +256,12 @@ def test_tma_engine_with_host_cta_table(upt, NW):
 
 
 def test_sweep_shapes_plan():
-    """Which BASELINE shapes get tile-aligned CTA ranges (12 warps, 148 SMs)."""
+    """Which BASELINE shapes get tile-aligned CTA ranges (16 warps, 148 SMs)."""
     plans = {}
     for (K, N) in [(2048, 2048), (2048, 11008), (11008, 2048), (2048, 256)]:
         tiles, upt = -(-N // 8), -(-K // 64)
         U = tiles * upt
-        G = min(148, -(-U // 24))
+        G = min(148, -(-U // 32))
         if G > tiles:
             _, al = fill_cta_starts(tiles, upt, tiles, 32)
             G = tiles if al else G
