@@ -81,8 +81,8 @@ static EncodeTiledFn encode_fn() {
   return fn;
 }
 
-int encode_tmap_u32_2d(CUtensorMap* map, const void* base, uint64_t dim0, uint64_t dim1, uint64_t stride1_bytes,
-                       uint32_t box0, uint32_t box1) {
+int encode_tmap_2d(CUtensorMap* map, CUtensorMapDataType dtype, const void* base, uint64_t dim0, uint64_t dim1,
+                   uint64_t stride1_bytes, uint32_t box0, uint32_t box1, CUtensorMapSwizzle swizzle) {
   EncodeTiledFn fn = encode_fn();
   if (!fn) {
     set_error("cuTensorMapEncodeTiled is not available from the driver");
@@ -92,15 +92,20 @@ int encode_tmap_u32_2d(CUtensorMap* map, const void* base, uint64_t dim0, uint64
   const cuuint64_t strides[1] = {stride1_bytes};
   const cuuint32_t box[2] = {box0, box1};
   const cuuint32_t estr[2] = {1, 1};
-  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT32, 2, const_cast<void*>(base), dims, strides, box, estr,
-                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  CUresult r = fn(map, dtype, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) {
     set_error("cuTensorMapEncodeTiled failed (%d) for dims %llu x %llu stride %llu", (int)r,
               (unsigned long long)dim0, (unsigned long long)dim1, (unsigned long long)stride1_bytes);
     return PP_ERR_CUDA;
   }
   return PP_OK;
+}
+
+int encode_tmap_u32_2d(CUtensorMap* map, const void* base, uint64_t dim0, uint64_t dim1, uint64_t stride1_bytes,
+                       uint32_t box0, uint32_t box1) {
+  return encode_tmap_2d(map, CU_TENSOR_MAP_DATA_TYPE_UINT32, base, dim0, dim1, stride1_bytes, box0, box1,
+                        CU_TENSOR_MAP_SWIZZLE_128B);
 }
 
 // Writes zeros into an (R, C) FP16 matrix with arbitrary element strides.

@@ -33,6 +33,10 @@ int reserved_smem(int device);
 int encode_tmap_u32_2d(CUtensorMap* map, const void* base, uint64_t dim0, uint64_t dim1, uint64_t stride1_bytes,
                        uint32_t box0, uint32_t box1);
 
+// General 2D tiled tensor map (dim0 contiguous), zero fill out of bounds.
+int encode_tmap_2d(CUtensorMap* map, CUtensorMapDataType dtype, const void* base, uint64_t dim0, uint64_t dim1,
+                   uint64_t stride1_bytes, uint32_t box0, uint32_t box1, CUtensorMapSwizzle swizzle);
+
 // Raises a kernel's dynamic shared memory limit to the device's opt-in
 // maximum minus the kernel's static shared memory, once per device, and
 // returns that limit in *max_dynamic.

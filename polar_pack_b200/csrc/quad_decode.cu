@@ -327,7 +327,8 @@ struct PlugCorrParams {
   const uint32_t* wbase;     // [N*W + 1]
   uint32_t base_lo32;
   int M, N, K, W;
-  float* corr;               // [4][M][N]
+  float* corr;               // corr[q * ldq + m * N + n]
+  int64_t ldq;               // model stride of corr (M * N for a dense [4][M][N] buffer)
 };  // (declared identically in quad_gemv.cu)
 
 template <int MB>
@@ -393,7 +394,7 @@ __global__ void __launch_bounds__(256) quad_plug_corr_kernel(const PlugCorrParam
     for (int m = 0; m < MB; ++m)
       if (m < p.M)
 #pragma unroll
-        for (int q = 0; q < 4; ++q) p.corr[((int64_t)q * p.M + m) * p.N + row] = acc[m][q];
+        for (int q = 0; q < 4; ++q) p.corr[(int64_t)q * p.ldq + (int64_t)m * p.N + row] = acc[m][q];
   }
 }
 

@@ -38,8 +38,19 @@ struct PlugCorrParams {
   uint32_t base_lo32;
   int M, N, K, W;
   float* corr;
+  int64_t ldq;
 };
 int launch_plug_corr(const PlugCorrParams& prm, cudaStream_t s);
+
+// quad_tc.cu: batched tensor-core path (file layout, prepared tables)
+bool quad_tc_ok(int64_t M, int64_t N, int64_t K, const uint32_t* codes, int64_t ldw, const void* x, int64_t ldx_m,
+                int64_t ldx_k);
+size_t quad_tc_slots_bytes(int64_t M, int64_t N, int64_t K, int sms);
+int launch_quad_tc(const void* x, int64_t ldx_m, const uint32_t* codes, int64_t ldw, const void* tables,
+                   const float scales[4], void* const out[4], int64_t ldo_m, int64_t ldo_n, const float* corr,
+                   int64_t corr_q, int64_t Mc, int64_t N, int64_t K, int* counters, float* slots,
+                   cudaStream_t s);
+constexpr int64_t kTcLaunchRows = 128;
 
 // Warps per CTA.  Shared memory holds the 128 KiB tables, each warp's TMA
 // ring (2 KiB per slot) and two partial slots per warp.  The batch-1 file
@@ -550,11 +561,23 @@ int check_common(const void* const luts[7], const void* tables, const float scal
   return PP_OK;
 }
 
+// Tensor-core path workspace: [counter block][plug correction 4 x Mc x N][split-K slots]
+inline size_t tc_corr_bytes(int64_t M, int64_t N) {
+  const int64_t Mc = M < kTcLaunchRows ? M : kTcLaunchRows;
+  return align_up((size_t)4 * Mc * N * sizeof(float), 256);
+}
+
 size_t quad_ws_bytes(bool nk, int64_t M, int64_t N, int64_t K, bool plug) {
   const int sms = device_sm_count(current_device());
   const int64_t Mc = M < 16 ? M : 16;
   if (Mc <= 0) return 0;
-  return quad_plan(nk, Mc, N, K, sms > 0 ? sms : 148).total() + (plug ? corr_bytes(N) : 0);
+  size_t need = quad_plan(nk, Mc, N, K, sms > 0 ? sms : 148).total() + (plug ? corr_bytes(N) : 0);
+  if (nk && M > 16) {  // the batched tensor-core path (taken with prepared tables)
+    const size_t tc = kCounterBytes + (plug ? tc_corr_bytes(M, N) : 0) +
+                      quad_tc_slots_bytes(M, N, K, sms > 0 ? sms : 148);
+    need = tc > need ? tc : need;
+  }
+  return need;
 }
 
 }  // namespace
@@ -626,6 +649,35 @@ static int quad_run(const void* a, int64_t lda_m, int64_t lda_k, const uint32_t*
     set_error("cannot query the SM count of the current device");
     return PP_ERR_CUDA;
   }
+  if (tables && nk && quad_tc_ok(M, N, K, codes, ldc_n, a, lda_m, lda_k)) {
+    // batched tensor-core path: every code decoded once for up to 128 batch rows
+    const size_t csz = plug ? tc_corr_bytes(M, N) : 0;
+    const size_t need = kCounterBytes + csz + quad_tc_slots_bytes(M, N, K, sms);
+    if (ws_bytes < need || !ws || !aligned(ws, 256)) {
+      set_error("workspace of %zu bytes (256-byte aligned, zero-filled) required, got %zu", need, ws_bytes);
+      return PP_ERR_WORKSPACE;
+    }
+    int* counters = reinterpret_cast<int*>(ws);
+    float* corr = plug ? reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(ws) + kCounterBytes) : nullptr;
+    float* slots = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(ws) + kCounterBytes + csz);
+    for (int64_t m0 = 0; m0 < M; m0 += kTcLaunchRows) {
+      const int64_t Mc = (M - m0) < kTcLaunchRows ? (M - m0) : kTcLaunchRows;
+      const __half* xc = reinterpret_cast<const __half*>(a) + m0 * lda_m;
+      void* oc[4];
+      for (int i = 0; i < 4; ++i) oc[i] = reinterpret_cast<__half*>(out[i]) + m0 * ldo_m;
+      if (plug)
+        for (int64_t m1 = 0; m1 < Mc; m1 += 16) {
+          const int64_t Mcc = (Mc - m1) < 16 ? (Mc - m1) : 16;
+          PlugCorrParams cp{xc + m1 * lda_m, lda_m, plug_idx, reinterpret_cast<const uint2*>(plug_vals), wbase,
+                            base_lo32, (int)Mcc, (int)N, (int)K, (int)cdiv(K, 64), corr + m1 * N, Mc * N};
+          if ((rc = launch_plug_corr(cp, s))) return rc;
+        }
+      if ((rc = launch_quad_tc(xc, lda_m, codes, ldc_n, tables, scales, oc, ldo_m, ldo_n, corr, Mc * N, Mc, N, K,
+                               counters, slots, s)))
+        return rc;
+    }
+    return PP_OK;
+  }
   QuadParams prm{};
   prm.ldx_m = lda_m;
   prm.ldx_k = lda_k;
@@ -668,7 +720,7 @@ static int quad_run(const void* a, int64_t lda_m, int64_t lda_k, const uint32_t*
     prm.corr = corr;
     if (plug) {
       PlugCorrParams cp{prm.x, lda_m, plug_idx, reinterpret_cast<const uint2*>(plug_vals), wbase, base_lo32,
-                        (int)Mc, (int)N, (int)K, (int)cdiv(K, 64), corr};
+                        (int)Mc, (int)N, (int)K, (int)cdiv(K, 64), corr, Mc * N};
       if ((rc = launch_plug_corr(cp, s))) return rc;
     }
     if ((rc = launch_plan(pl, nk, Mc, prm, ws, csz, s))) return rc;
