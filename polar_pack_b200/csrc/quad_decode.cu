@@ -316,9 +316,8 @@ namespace pp {
 // (FP32).  The fused kernel decodes plugged codes to exact zeros (their norm
 // byte was cleared by pp_quad_prepare_plugs) and adds corr before the
 // per-model scale and the FP16 store, so the result equals the product with
-// the plug values substituted, up to FP32 summation order.  One warp per
-// row; lanes take every 32nd entry (four per lane in flight) and the warp
-// sums lane totals in a fixed butterfly order, so results are deterministic.
+// the plug values substituted, up to FP32 summation order.  The warp sums
+// lane totals in a fixed butterfly order, so results are deterministic.
 struct PlugCorrParams {
   const __half* x;
   int64_t ldx_m;
@@ -331,79 +330,116 @@ struct PlugCorrParams {
   int64_t ldq;               // model stride of corr (M * N for a dense [4][M][N] buffer)
 };  // (declared identically in quad_gemv.cu)
 
-template <int MB>
+// A warp owns RPW consecutive rows, whose entries are one contiguous range
+// of the sorted plug table; lanes take every 32nd entry, U per lane in
+// flight.  Two rows per warp when rows are short halves the warps, so the
+// largest layers fit one wave; long rows keep one row per warp.
+template <int MB, int RPW, int U>
 __global__ void __launch_bounds__(256) quad_plug_corr_kernel(const PlugCorrParams p) {
-  constexpr int U = 4;  // entries per lane in flight
   pdl_launch_dependents();
   const int lane = threadIdx.x & 31;
-  const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
-  if (row >= p.N) {
+  const int row0 = (blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5)) * RPW;
+  const int nrows = row0 < p.N ? (p.N - row0 < RPW ? p.N - row0 : RPW) : 0;
+  if (nrows == 0) {
     pdl_wait();
     return;
   }
-  const uint32_t j0 = __ldg(p.wbase + (int64_t)row * p.W), j1 = __ldg(p.wbase + (int64_t)(row + 1) * p.W);
-  const uint32_t rowbase = p.base_lo32 + (uint32_t)row * (uint32_t)p.K;
-  float acc[MB][4];
+  // row pointers: lane r holds the first entry of row row0 + r (r <= nrows)
+  uint32_t rp = 0u;
+  if (lane <= nrows) rp = __ldg(p.wbase + (int64_t)(row0 + lane) * p.W);
+  uint32_t rs[RPW + 1];
 #pragma unroll
-  for (int m = 0; m < MB; ++m)
+  for (int r = 0; r <= RPW; ++r) rs[r] = __shfl_sync(0xffffffffu, rp, r <= nrows ? r : nrows);
+  const uint32_t j0 = rs[0], j1 = rs[nrows];
+  float acc[RPW][MB][4];
 #pragma unroll
-    for (int q = 0; q < 4; ++q) acc[m][q] = 0.f;
+  for (int r = 0; r < RPW; ++r)
+#pragma unroll
+    for (int m = 0; m < MB; ++m)
+#pragma unroll
+      for (int q = 0; q < 4; ++q) acc[r][m][q] = 0.f;
   for (uint32_t jb = j0; jb < j1; jb += 32u * U) {
-    // the plug arrays are weights: load a batch before waiting
+    // the plug arrays are weights: loads of a batch are issued before the wait
     uint32_t kk[U];
     uint2 vv[U];
 #pragma unroll
     for (int u = 0; u < U; ++u) {
       const uint32_t j = jb + (uint32_t)lane + 32u * u;
       kk[u] = 0u;
-      vv[u] = make_uint2(0u, 0u);  // zero values: the entry contributes nothing
+      vv[u] = make_uint2(0u, 0u);
       if (j < j1) {
-        kk[u] = __ldg(p.plug_idx + j) - rowbase;
+        kk[u] = __ldg(p.plug_idx + j);
         vv[u] = __ldg(p.plug_vals + j);
       }
     }
     pdl_wait();  // activations may come from the previous kernel
 #pragma unroll
     for (int u = 0; u < U; ++u) {
+      const uint32_t j = jb + (uint32_t)lane + 32u * u;
+      if (j >= j1) continue;
       const float pv[4] = {__half2float(__ushort_as_half((uint16_t)(vv[u].x & 0xFFFF))),
                            __half2float(__ushort_as_half((uint16_t)(vv[u].x >> 16))),
                            __half2float(__ushort_as_half((uint16_t)(vv[u].y & 0xFFFF))),
                            __half2float(__ushort_as_half((uint16_t)(vv[u].y >> 16)))};
 #pragma unroll
-      for (int m = 0; m < MB; ++m) {
-        if (m < p.M) {
-          const float xv = __half2float(p.x[(int64_t)m * p.ldx_m + kk[u]]);
+      for (int r = 0; r < RPW; ++r) {
+        if (RPW == 1 || (j >= rs[r] && j < rs[r + 1])) {
+          const uint32_t k = kk[u] - (p.base_lo32 + (uint32_t)(row0 + r) * (uint32_t)p.K);
 #pragma unroll
-          for (int q = 0; q < 4; ++q) acc[m][q] = fmaf(pv[q], xv, acc[m][q]);
+          for (int m = 0; m < MB; ++m) {
+            if (m < p.M) {
+              const float xv = __half2float(p.x[(int64_t)m * p.ldx_m + k]);
+#pragma unroll
+              for (int q = 0; q < 4; ++q) acc[r][m][q] = fmaf(pv[q], xv, acc[r][m][q]);
+            }
+          }
         }
       }
     }
   }
 #pragma unroll
-  for (int m = 0; m < MB; ++m)
+  for (int r = 0; r < RPW; ++r)
 #pragma unroll
-    for (int q = 0; q < 4; ++q) {
-      float v = acc[m][q];
+    for (int m = 0; m < MB; ++m)
 #pragma unroll
-      for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-      acc[m][q] = v;
-    }
+      for (int q = 0; q < 4; ++q) {
+        float v = acc[r][m][q];
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+        acc[r][m][q] = v;
+      }
   pdl_wait();  // the previous kernel may still read the correction buffer
   if (lane == 0) {
 #pragma unroll
-    for (int m = 0; m < MB; ++m)
-      if (m < p.M)
+    for (int r = 0; r < RPW; ++r)
+      if (r < nrows)
 #pragma unroll
-        for (int q = 0; q < 4; ++q) p.corr[(int64_t)q * p.ldq + (int64_t)m * p.N + row] = acc[m][q];
+        for (int m = 0; m < MB; ++m)
+          if (m < p.M)
+#pragma unroll
+            for (int q = 0; q < 4; ++q) p.corr[(int64_t)q * p.ldq + (int64_t)m * p.N + row0 + r] = acc[r][m][q];
   }
 }
 
 int launch_plug_corr(const PlugCorrParams& prm, cudaStream_t s) {
   const int warps = 8;
+  const bool ov = launch_overlap();
+  if (prm.M == 1) {
+    if (prm.K <= 4096) {  // short rows: two per warp
+      const int grid = (int)cdiv(prm.N, warps * 2);
+      return launch_kernel("quad_plug_corr_kernel", ov, quad_plug_corr_kernel<1, 2, 8>, dim3(grid), dim3(warps * 32),
+                           0, s, prm);
+    }
+    const int grid = (int)cdiv(prm.N, warps);
+    return launch_kernel("quad_plug_corr_kernel", ov, quad_plug_corr_kernel<1, 1, 8>, dim3(grid), dim3(warps * 32),
+                         0, s, prm);
+  }
   const int grid = (int)cdiv(prm.N, warps);
-  auto kern = prm.M == 1 ? quad_plug_corr_kernel<1> : prm.M <= 8 ? quad_plug_corr_kernel<8>
-                                                                   : quad_plug_corr_kernel<16>;
-  return launch_kernel("quad_plug_corr_kernel", launch_overlap(), kern, dim3(grid), dim3(warps * 32), 0, s, prm);
+  if (prm.M <= 8)
+    return launch_kernel("quad_plug_corr_kernel", ov, quad_plug_corr_kernel<8, 1, 4>, dim3(grid), dim3(warps * 32), 0,
+                         s, prm);
+  return launch_kernel("quad_plug_corr_kernel", ov, quad_plug_corr_kernel<16, 1, 4>, dim3(grid), dim3(warps * 32), 0,
+                       s, prm);
 }
 
 }  // namespace pp
