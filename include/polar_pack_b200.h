@@ -186,6 +186,47 @@ PP_API int pp_quad_prepare_plugs(uint32_t* codes, int64_t ldw, const uint32_t* p
                                  int64_t p_lo, int64_t p_hi, uint32_t base_lo32, int64_t N, int64_t K,
                                  uint32_t* plug_window_base, int* bad_count, void* stream);
 
+/* Unit-major copy of one Linear's plug entries, streamed by the GEMV beside
+ * the codes so that the plug correction needs no kernel of its own (no
+ * reference counterpart: a load-time layout of the plug table that
+ * quaternion_packer.py:187-193 merges on the host).  Work unit
+ * u = t * ceil(K/64) + kc covers rows 8t..8t+7 and columns 64kc..64kc+63;
+ * its segment starts at byte unit_plug_off[u] (a multiple of 16):
+ *   16-byte header of eight uint16: entries of rows 8t..8t+r, r = 0..7;
+ *   the n entries' FP16x4 values (row-major, column ascending);
+ *   their n column bytes (column - 64kc); zeros to a multiple of 16.
+ * unit_plug_off has ceil(N/8) * ceil(K/64) + 1 entries; the last is the
+ * stream's length.  pp_quad_unit_plugs_bytes gives a size that always
+ * suffices and the number of offsets.  Inputs: the Linear's plug slice and
+ * plug_window_base as for pp_quad_linear (run pp_quad_prepare_plugs first).
+ */
+PP_API int pp_quad_unit_plugs_bytes(int64_t N, int64_t K, int64_t n_plugs, size_t* stream_bytes,
+                                    int64_t* n_offsets);
+
+PP_API int pp_quad_prepare_unit_plugs(const uint32_t* plug_idx, const void* plug_vals, int64_t n_plugs,
+                                      uint32_t base_lo32, const uint32_t* plug_window_base, int64_t N,
+                                      int64_t K, void* unit_plugs, size_t unit_plugs_bytes,
+                                      uint32_t* unit_plug_off, void* stream);
+
+/* pp_quad_linear_prepared with the plug correction inside the GEMV when
+ * the batch is one row (M == 1) and every warp's share of the work units
+ * fits its offset table (at most 63 units, i.e. about 148 * 16 * 63 units
+ * per launch); otherwise identical to pp_quad_linear_prepared, which is why
+ * the CSR arguments are required as well.  unit_plugs / unit_plug_off: as
+ * built by pp_quad_prepare_unit_plugs (both NULL for a Linear without
+ * plugs).  Same result within the FP32
+ * accumulation tolerance; the summation order of the plug terms differs.
+ */
+PP_API int pp_quad_linear_fused(const void* x, int64_t ldx_m, int64_t ldx_k,
+                                const uint32_t* codes, int64_t ldw,
+                                const uint32_t* plug_idx, const void* plug_vals,
+                                const uint32_t* plug_window_base, uint32_t base_lo32,
+                                const void* unit_plugs, const uint32_t* unit_plug_off,
+                                const void* tables, const float scales[4],
+                                void* const out[4], int64_t ldo_m, int64_t ldo_n,
+                                int64_t M, int64_t N, int64_t K,
+                                void* workspace, size_t workspace_bytes, void* stream);
+
 /* FP16 decode of a (R, C) code matrix into four (R, C) FP16 matrices,
  * bit-exact with the reference kernel's chain (quad_kernels.py:103-121).
  * scales == NULL keeps the normalised weights; otherwise each is multiplied

@@ -51,6 +51,12 @@ _SIGNATURES = {
                         _c_void_p], _int),
     "pp_quad_prepare_plugs": ([_c_void_p, _i64, _c_void_p, _i64, _i64, _u32, _i64, _i64, _c_void_p,
                                _c_void_p, _c_void_p], _int),
+    "pp_quad_unit_plugs_bytes": ([_i64, _i64, _i64, ctypes.POINTER(_size_t), ctypes.POINTER(_i64)], _int),
+    "pp_quad_prepare_unit_plugs": ([_c_void_p, _c_void_p, _i64, _u32, _c_void_p, _i64, _i64, _c_void_p, _size_t,
+                                    _c_void_p, _c_void_p], _int),
+    "pp_quad_linear_fused": ([_c_void_p, _i64, _i64, _c_void_p, _i64, _c_void_p, _c_void_p, _c_void_p, _u32,
+                              _c_void_p, _c_void_p, _c_void_p, _F4, _PTR4, _i64, _i64, _i64, _i64, _i64,
+                              _c_void_p, _size_t, _c_void_p], _int),
     "pp_quad_decode": ([_c_void_p, _i64, _i64, _i64, _i64, _PTR7, _c_void_p, _PTR4, _i64, _i64,
                         _c_void_p], _int),
     "pp_quad_unpack": ([_c_void_p, _i64, _c_void_p, _c_void_p, _i64, _i64, _u32, _PTR7, _c_void_p,

@@ -249,9 +249,13 @@ __device__ __forceinline__ void run_partition(Op& op, const Partition& pt, float
 // the tile.  No warp ever waits for another, and every sum has a fixed
 // order, so results are deterministic.
 //
-// Op additions: kUnitBytes; static void issue(const Params&, uint32_t slot,
-// uint32_t bar, int tile, int kc) (one lane); void read(Buf&, uint32_t
-// slot) const.
+// Op additions: kUnitBytes; void read(Buf&, uint32_t slot) const;
+// void side(int p, int u, int kc) (side data of unit u in side slot p; a
+// warp has one side slot more than ring slots, so the slot of the unit
+// being computed is not refilled before the next unit's wait); void
+// end_chunk() (before the accumulators of a chunk are stored or reduced).
+// The issue functor is called on lane 0 as issue(slot address, mbarrier,
+// side slot index, tile, kc).
 
 // Per-CTA tables in shared memory, filled before the table-build barrier.
 struct CtaTables {
@@ -336,13 +340,15 @@ struct UnitSeq {
 struct TmaRing {
   uint32_t ring, bars;  // this warp's S slots and S mbarriers
   int S;
+  int P = 1, pn = 0;    // side slots (S + 1) and the side slot of the next issue
   UnitSeq next;         // next unit to issue
 
-  // every lane advances the cursor; only `leader` issues
+  // every lane advances the cursors; only `leader` issues
   template <class Issue>
   __device__ __forceinline__ void issue_next(const Issue& issue, int s, uint32_t unit, bool leader) {
-    if (leader) issue(ring + (uint32_t)s * unit, bars + 8u * (uint32_t)s, next.t, next.kc);
+    if (leader) issue(ring + (uint32_t)s * unit, bars + 8u * (uint32_t)s, pn, next.t, next.kc);
     next.advance();
+    if (++pn == P) pn = 0;
   }
 
   // lane 0: barriers and the first min(S, units) copies
@@ -441,7 +447,7 @@ __device__ __forceinline__ void tma_stream(Op& op, const Issue& issue, TmaRing& 
   const int upt = pt.upt;
   UnitSeq sq;
   sq.init(wu0, wu1, upt);
-  int s = 0;
+  int s = 0, sp = 0;
   uint32_t ph = 0;
   typename Op::Buf buf;
   while (sq.seg < 3) {
@@ -453,12 +459,15 @@ __device__ __forceinline__ void tma_stream(Op& op, const Issue& issue, TmaRing& 
       op.read(buf, rg.ring + (uint32_t)s * Op::kUnitBytes);
       __syncwarp();
       if (rg.next.seg < 3) rg.issue_next(issue, s, Op::kUnitBytes, leader);  // warp-uniform test
+      op.side(sp, t * upt + kc, kc);
+      if (++sp == rg.P) sp = 0;
       if (++s == rg.S) {
         s = 0;
         ph ^= 1u;
       }
       op.compute(buf, t, kc);
     }
+    op.end_chunk();
     if (sq.seg == 2) op.store_tile(t);
     else close_split(op, pt, tb, red, warp, t, sq.seg == 0 ? 1 : 0, cu0, cu1);
     sq.skip(n);

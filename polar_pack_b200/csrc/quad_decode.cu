@@ -9,6 +9,9 @@
 //    Linear's plug table for the fused kernel: index of the first plug of
 //    every (row, 64-column window), and the norm byte of plugged codes set to
 //    zero so that they decode to exact zeros in the main loop.
+//  * unit_plug_size / unit_plug_scan / unit_plug_fill -- load-time copy of
+//    a Linear's plug table in unit-major order (one segment per 8-row x
+//    64-column work unit), which the GEMV streams beside the codes.
 #include "pp_common.cuh"
 #include "pp_host.h"
 
@@ -443,3 +446,160 @@ int launch_plug_corr(const PlugCorrParams& prm, cudaStream_t s) {
 }
 
 }  // namespace pp
+
+// ------------------------------------------------------------ unit plugs --
+// Unit-major plug stream of one file-layout Linear (N, K) for the fused
+// correction of quad_gemv.cu.  Unit u = t * W + kc (W = ceil(K / 64))
+// covers rows 8t..8t+7 and columns 64kc..64kc+63.  Its segment starts at
+// byte off[u], a multiple of 16, and holds its n plug entries in table
+// order (row-major, k ascending):
+//   bytes [0, 16)          eight u16: entries of rows 8t..8t+r, r = 0..7
+//   bytes [16, 16 + 8n)    the entries' FP16x4 values (as in plug_vals)
+//   bytes [16 + 8n, 16+9n) the entries' columns k - 64kc
+// then zeros up to the next multiple of 16.  off[U] = total bytes.
+namespace pp {
+
+struct UnitPlugParams {
+  const uint32_t* plug_idx;  // this Linear's slice
+  const uint2* plug_vals;
+  const uint32_t* wbase;     // [N*W + 1] (quad_plug_windows_kernel)
+  uint32_t base;
+  int64_t N, K, W, U;
+  uint8_t* out;
+  uint32_t* off;             // [U + 1]
+};
+
+__host__ __device__ inline uint32_t unit_plug_seg_bytes(uint32_t n) { return (16u + 9u * n + 15u) & ~15u; }
+
+__global__ void unit_plug_size_kernel(const UnitPlugParams p) {
+  for (int64_t u = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; u <= p.U; u += (int64_t)gridDim.x * blockDim.x) {
+    if (u == p.U) {
+      p.off[u] = 0u;
+      continue;
+    }
+    const int64_t t = u / p.W, kc = u - t * p.W;
+    uint32_t n = 0;
+    for (int r = 0; r < 8; ++r) {
+      const int64_t row = 8 * t + r;
+      if (row < p.N) n += __ldg(p.wbase + row * p.W + kc + 1) - __ldg(p.wbase + row * p.W + kc);
+    }
+    p.off[u] = unit_plug_seg_bytes(n);
+  }
+}
+
+// In-place exclusive scan of off[0..n) by one CTA of 1024 threads, each
+// owning a contiguous chunk.
+__global__ void __launch_bounds__(1024) unit_plug_scan_kernel(uint32_t* off, int64_t n) {
+  __shared__ uint32_t part[1024];
+  const int tid = threadIdx.x;
+  const int64_t chunk = (n + 1023) / 1024;
+  const int64_t i0 = tid * chunk < n ? tid * chunk : n, i1 = i0 + chunk < n ? i0 + chunk : n;
+  uint32_t sum = 0;
+  for (int64_t i = i0; i < i1; ++i) sum += off[i];
+  part[tid] = sum;
+  __syncthreads();
+  for (int d = 1; d < 1024; d <<= 1) {  // Hillis-Steele inclusive scan
+    const uint32_t v = tid >= d ? part[tid - d] : 0u;
+    __syncthreads();
+    part[tid] += v;
+    __syncthreads();
+  }
+  uint32_t run = part[tid] - sum;
+  for (int64_t i = i0; i < i1; ++i) {
+    const uint32_t v = off[i];
+    off[i] = run;
+    run += v;
+  }
+}
+
+// One warp per unit: lanes 0..7 own the tile rows (their entry ranges),
+// then all lanes copy each row's entries.
+__global__ void unit_plug_fill_kernel(const UnitPlugParams p) {
+  const int lane = threadIdx.x & 31;
+  const int64_t nwarps = (int64_t)gridDim.x * (blockDim.x >> 5);
+  for (int64_t u = blockIdx.x * (int64_t)(blockDim.x >> 5) + (threadIdx.x >> 5); u < p.U; u += nwarps) {
+    const int64_t t = u / p.W, kc = u - t * p.W;
+    const int64_t row = 8 * t + lane;
+    uint32_t a = 0, cnt = 0;
+    if (lane < 8 && row < p.N) {
+      a = __ldg(p.wbase + row * p.W + kc);
+      cnt = __ldg(p.wbase + row * p.W + kc + 1) - a;
+    }
+    uint32_t h = cnt;  // inclusive scan over lanes 0..7
+#pragma unroll
+    for (int d = 1; d < 8; d <<= 1) {
+      const uint32_t v = __shfl_up_sync(0xffffffffu, h, d);
+      if (lane >= d) h += v;
+    }
+    const uint32_t n = __shfl_sync(0xffffffffu, h, 7);
+    uint8_t* seg = p.out + __ldg(p.off + u);
+    const uint32_t len = __ldg(p.off + u + 1) - __ldg(p.off + u);
+    if (lane < 8) reinterpret_cast<uint16_t*>(seg)[lane] = (uint16_t)h;
+    for (int r = 0; r < 8; ++r) {
+      const uint32_t ar = __shfl_sync(0xffffffffu, a, r);
+      const uint32_t cr = __shfl_sync(0xffffffffu, cnt, r);
+      const uint32_t e0 = __shfl_sync(0xffffffffu, h, r) - cr;
+      const uint32_t rowbase = p.base + (uint32_t)(8 * t + r) * (uint32_t)p.K + (uint32_t)(64 * kc);
+      for (uint32_t j = lane; j < cr; j += 32) {
+        const uint32_t e = e0 + j;
+        reinterpret_cast<uint2*>(seg + 16)[e] = __ldg(p.plug_vals + ar + j);
+        seg[16 + 8 * n + e] = (uint8_t)(__ldg(p.plug_idx + ar + j) - rowbase);
+      }
+    }
+    for (uint32_t b = 16 + 9 * n + lane; b < len; b += 32) seg[b] = 0;
+  }
+}
+
+}  // namespace pp
+
+extern "C" {
+
+int pp_quad_unit_plugs_bytes(int64_t N, int64_t K, int64_t n_plugs, size_t* stream_bytes, int64_t* n_offsets) {
+  if (N < 0 || K < 0 || n_plugs < 0 || !stream_bytes || !n_offsets) {
+    pp::set_error("invalid arguments to quad unit plugs bytes");
+    return PP_ERR_INVALID;
+  }
+  const int64_t U = pp::cdiv(N, 8) * pp::cdiv(K, 64);
+  // a segment takes at most 16 + 9n + 15 bytes
+  *stream_bytes = pp::align_up((size_t)U * 31u + (size_t)n_plugs * 9u, 256);
+  *n_offsets = U + 1;
+  return PP_OK;
+}
+
+int pp_quad_prepare_unit_plugs(const uint32_t* plug_idx, const void* plug_vals, int64_t n_plugs, uint32_t base_lo32,
+                               const uint32_t* plug_window_base, int64_t N, int64_t K, void* unit_plugs,
+                               size_t unit_plugs_bytes, uint32_t* unit_plug_off, void* stream) {
+  size_t need = 0;
+  int64_t noff = 0;
+  int rc = pp_quad_unit_plugs_bytes(N, K, n_plugs, &need, &noff);
+  if (rc) return rc;
+  if (N == 0 || K == 0) {
+    pp::set_error("empty Linear");
+    return PP_ERR_INVALID;
+  }
+  if (!plug_window_base || !unit_plugs || !unit_plug_off || (n_plugs > 0 && (!plug_idx || !plug_vals)) ||
+      !pp::aligned(unit_plugs, 16) || !pp::aligned(unit_plug_off, 4) || (plug_vals && !pp::aligned(plug_vals, 8))) {
+    pp::set_error("unit plugs: NULL or misaligned pointer (stream 16-byte, values 8-byte aligned)");
+    return PP_ERR_INVALID;
+  }
+  if (unit_plugs_bytes < need) {
+    pp::set_error("unit plug stream of %zu bytes required, got %zu", need, unit_plugs_bytes);
+    return PP_ERR_WORKSPACE;
+  }
+  if (need > 0xFFFFFFF0ull) {
+    pp::set_error("unit plug stream above 4 GiB (32-bit offsets)");
+    return PP_ERR_INVALID;
+  }
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  const int64_t W = pp::cdiv(K, 64);
+  pp::UnitPlugParams prm{plug_idx, reinterpret_cast<const uint2*>(plug_vals), plug_window_base, base_lo32, N, K,
+                         W, noff - 1, reinterpret_cast<uint8_t*>(unit_plugs), unit_plug_off};
+  pp::unit_plug_size_kernel<<<pp::grid_for(noff, 256), 256, 0, s>>>(prm);
+  if ((rc = pp::check_launch("unit_plug_size_kernel"))) return rc;
+  pp::unit_plug_scan_kernel<<<1, 1024, 0, s>>>(unit_plug_off, noff);
+  if ((rc = pp::check_launch("unit_plug_scan_kernel"))) return rc;
+  pp::unit_plug_fill_kernel<<<pp::grid_for((noff - 1) * 32, 256), 256, 0, s>>>(prm);
+  return pp::check_launch("unit_plug_fill_kernel");
+}
+
+}  // extern "C"

@@ -16,6 +16,14 @@
 // The logical K order inside one mma is a permutation of the physical
 // order; the activation fragment uses the same permutation.
 //
+// Plug correction fused into the stream (file layout, batch 1): each unit's
+// plug entries come as one segment of a unit-major plug stream (built at
+// load time by pp_quad_prepare_unit_plugs, quad_decode.cu), copied into a
+// slot beside the unit's ring slot on the same mbarrier.  Plugged codes
+// decode to zeros; lane (g, c) adds value * x[k] of the plug entries of its
+// tile row with index = c mod 4 into four FP32 sums, which the row's four
+// lanes combine into the accumulators before the tile is stored or reduced.
+//
 // Work partition and the deterministic split-K reduction: pp_engine.cuh.
 #include "pp_common.cuh"
 #include "pp_engine.cuh"
@@ -81,6 +89,11 @@ struct QuadParams {
   // layout_base (the kernel recomputes it if its base differs)
   QuadLayout layout;
   uint32_t layout_base;
+  // fused plug correction: unit-major plug stream, its unit byte offsets
+  // (units + 1) and the plug slot size (a multiple of 16)
+  const uint8_t* uplugs;
+  const uint32_t* uplug_off;
+  uint32_t pcap;
   int cta_start[kMaxCtaTable + 1];  // unit start of every CTA (fill_cta_starts)
 };
 
@@ -89,9 +102,10 @@ struct QuadBuf {
 };
 
 // NK: file layout.  DIRECT: tables at a 64 KiB-aligned shared address (see
-// decode_quad).
-template <bool NK, int NB, bool DIRECT>
+// decode_quad).  PLUG: fused plug correction (NK, NB == 1, batch 1).
+template <bool NK, int NB, bool DIRECT, bool PLUG = false>
 struct QuadOp {
+  static_assert(!PLUG || (NK && NB == 1), "fused plugs: file layout, one batch tile");
   static constexpr int kWarps = quad_warps(NK, NB);
   static constexpr int kTileW = NK ? 8 : 32;  // output features per tile
   static constexpr int kT = NK ? 1 : 4;       // mma pairs per 16-k step
@@ -111,6 +125,15 @@ struct QuadOp {
   const __half* x;
   const __half* xrow[NB];  // this lane's activation row per batch tile (clamped); NK: + 4c
   float acc[kT][NB][2][4];
+  // PLUG: this warp's plug slots and unit-offset table (shared addresses),
+  // its first unit, and the lane's plug sums per model
+  uint32_t pring = 0u, ptab = 0u;
+  int pwu0 = 0;
+  float pacc[4] = {0.f, 0.f, 0.f, 0.f};
+  // PLUG: the lane's first two entries of the current unit (values and raw
+  // FP16 activations), loaded by side() and applied after the decode
+  uint2 pv0, pv1;
+  uint32_t px;
 
   __device__ __forceinline__ QuadOp(const QuadParams& p_, uint32_t lut_saddr)
       : p(p_), g((threadIdx.x & 31) >> 2), c(threadIdx.x & 3),
@@ -153,12 +176,23 @@ struct QuadOp {
   __device__ __forceinline__ void begin(int, int) {}
   __device__ __forceinline__ void preload(int, int) {}
 
+  __device__ __forceinline__ void plug_init(uint32_t ring, uint32_t tab, int wu0) {
+    pring = ring;
+    ptab = tab;
+    pwu0 = wu0;
+  }
+
   // One unit by TMA into a 2 KiB ring slot (one lane).  NK: 8
   // rows x 64 codes as two 8 x 32 boxes (128-byte rows, 128-byte swizzle);
   // KN: 16 rows x 32 features, one box.  Out-of-range elements arrive as
-  // zeros.
-  static __device__ __forceinline__ void issue(const QuadParams& q, uint32_t slot, uint32_t bar, int tile, int kc) {
-    mbar_expect_tx(bar, kUnitBytes);
+  // zeros.  ARRIVE: arrive on the barrier expecting the unit plus `extra`
+  // bytes of side copies; else only raise its transaction count by the
+  // unit, leaving the arrival to a later side copy.
+  template <bool ARRIVE = true>
+  static __device__ __forceinline__ void issue(const QuadParams& q, uint32_t slot, uint32_t bar, int tile, int kc,
+                                               uint32_t extra = 0u) {
+    if (ARRIVE) mbar_expect_tx(bar, kUnitBytes + extra);
+    else mbar_expect_tx_only(bar, kUnitBytes);
     if constexpr (NK) {
       tma_load_2d(slot, &q.tmap, kc * 64, tile * 8, bar);
       tma_load_2d(slot + 1024u, &q.tmap, kc * 64 + 32, tile * 8, bar);
@@ -195,9 +229,81 @@ struct QuadOp {
     return make_uint2(0u, 0u);
   }
 
+  // PLUG: plug entries of unit u (column chunk kc) from plug slot sp.  The
+  // segment is a 16-byte header of eight u16 cumulative entry counts (rows
+  // 0..r of the tile), n FP16x4 values, then n column bytes (k - 64 kc);
+  // staged whole when 16 + 9n <= pcap, else read from HBM.  Lane (g, c)
+  // takes the entries of tile row pr whose index within the row is
+  // c mod 4.  Its first two are loaded here with their activations and
+  // applied after the unit's decode (plug_finish), which hides the load
+  // latency; further ones (rows of more than 8 entries) are applied now.
+  __device__ __forceinline__ void side(int sp, int u, int kc) {
+    if constexpr (PLUG) {
+      const uint32_t ps = pring + (uint32_t)sp * p.pcap;
+      const uint32_t n = lds_u16(ps + 14u);
+      const uint32_t hi = lds_u16(ps + 2u * (uint32_t)pr);
+      const uint32_t lo = pr ? lds_u16(ps + 2u * (uint32_t)pr - 2u) : 0u;
+      const __half* xk = x + kc * 64;
+      const uint32_t e0 = lo + (uint32_t)c, e1 = e0 + 4u;
+      pv0 = pv1 = make_uint2(0u, 0u);
+      px = 0u;
+      if (16u + 9u * n <= p.pcap) {
+        const uint32_t vb = ps + 16u, kb = ps + 16u + 8u * n;
+        if (e0 < hi) {
+          pv0 = lds_u2(vb + 8u * e0);
+          px = ld_u16(xk + lds_u8(kb + e0));
+        }
+        if (e1 < hi) {
+          pv1 = lds_u2(vb + 8u * e1);
+          px |= (uint32_t)ld_u16(xk + lds_u8(kb + e1)) << 16;
+        }
+        for (uint32_t e = e1 + 4u; e < hi; e += 4u) plug_fma(lds_u2(vb + 8u * e), ld_u16(xk + lds_u8(kb + e)));
+      } else {
+        const uint8_t* gs = p.uplugs + lds_u32(ptab + 4u * (uint32_t)(u - pwu0));
+        for (uint32_t e = e0; e < hi; e += 4u)
+          plug_fma(__ldg(reinterpret_cast<const uint2*>(gs + 16u + 8u * e)), ld_u16(xk + __ldg(gs + 16u + 8u * n + e)));
+      }
+    }
+  }
+
+  __device__ __forceinline__ void plug_finish() {
+    if constexpr (PLUG) {
+      plug_fma(pv0, px & 0xFFFFu);
+      plug_fma(pv1, px >> 16);
+    }
+  }
+
+  // pacc[q] += value q * x with the FP16 operands taken as they are (their
+  // product is exact in FP32) and one FP32 rounding, as cvt + fmaf would.
+  __device__ __forceinline__ void plug_fma(uint2 v, uint32_t xbits) {
+    asm("{\n .reg .f16 v0, v1, v2, v3, xh;\n"
+        " mov.b32 {v0, v1}, %4;\n mov.b32 {v2, v3}, %5;\n mov.b32 {xh, _}, %6;\n"
+        " fma.rn.f32.f16 %0, v0, xh, %0;\n fma.rn.f32.f16 %1, v1, xh, %1;\n"
+        " fma.rn.f32.f16 %2, v2, xh, %2;\n fma.rn.f32.f16 %3, v3, xh, %3;\n}"
+        : "+f"(pacc[0]), "+f"(pacc[1]), "+f"(pacc[2]), "+f"(pacc[3])
+        : "r"(v.x), "r"(v.y), "r"(xbits));
+  }
+
+  // PLUG: the four lanes of each row sum their plug sums (fixed butterfly)
+  // and lane c = 0, which holds batch row 0, adds them to model q's
+  // accumulator (fragment register 2 (q & 1) of half q >> 1).
+  __device__ __forceinline__ void end_chunk() {
+    if constexpr (PLUG) {
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        float v = pacc[q];
+        v += __shfl_xor_sync(0xffffffffu, v, 1);
+        v += __shfl_xor_sync(0xffffffffu, v, 2);
+        if (c == 0) acc[0][0][q >> 1][(q & 1) << 1] += v;
+        pacc[q] = 0.f;
+      }
+    }
+  }
+
   __device__ __forceinline__ void compute(const Buf& b, int tile, int kc) {
     if (kc * (NK ? 64 : 16) + (NK ? 64 : 16) <= Kv) compute_unit<true>(b, kc);
     else compute_unit<false>(b, kc);
+    plug_finish();
   }
 
   template <bool FULL>
@@ -305,15 +411,38 @@ struct QuadOp {
   }
 };
 
-template <bool NK, int NB, bool DIRECT>
+// PLUG: lane 0 copies the plug segment of unit u into plug slot s, at most
+// pcap bytes, with the offsets from the warp's table.  Returns its bytes.
+__device__ __forceinline__ uint32_t plug_bytes(const QuadParams& p, uint32_t ptab, int wu0, int u, uint32_t* off) {
+  const uint32_t o0 = lds_u32(ptab + 4u * (uint32_t)(u - wu0));
+  const uint32_t len = lds_u32(ptab + 4u * (uint32_t)(u - wu0 + 1)) - o0;
+  *off = o0;
+  return len < p.pcap ? len : p.pcap;
+}
+
+template <bool NK, int NB, bool DIRECT, bool PLUG>
 __device__ __forceinline__ void quad_body(const QuadParams& p, const Partition& pt, const QuadLayout& L, TmaRing& rg,
                                           const CtaTables& tb, int cu0, int cu1, int wu0, int wu1, int* status) {
-  using Op = QuadOp<NK, NB, DIRECT>;
+  using Op = QuadOp<NK, NB, DIRECT, PLUG>;
   const uint32_t base = (uint32_t)__cvta_generic_to_shared(pp_smem);
   float* red = reinterpret_cast<float*>(pp_smem + (L.scratch - base));
+  const int warp = threadIdx.x >> 5;
   Op op(p, L.lut);
-  tma_stream(op, [&](uint32_t slot, uint32_t bar, int tile, int kc) { Op::issue(p, slot, bar, tile, kc); }, rg,
-             pt, tb, red, threadIdx.x >> 5, wu0, wu1, cu0, cu1, status);
+  if constexpr (PLUG) {
+    const uint32_t pring = L.plug + (uint32_t)(warp * (p.stages + 1)) * p.pcap;
+    const uint32_t ptab = L.ptab + (uint32_t)warp * (kPlugTabEntries * 4u);
+    op.plug_init(pring, ptab, wu0);
+    const int upt = pt.upt;
+    tma_stream(op, [&](uint32_t slot, uint32_t bar, int s, int tile, int kc) {
+      uint32_t off;
+      const uint32_t pb = plug_bytes(p, ptab, wu0, tile * upt + kc, &off);
+      Op::template issue<true>(p, slot, bar, tile, kc, pb);
+      bulk_load(pring + (uint32_t)s * p.pcap, p.uplugs + off, pb, bar);  // s: side slot
+    }, rg, pt, tb, red, warp, wu0, wu1, cu0, cu1, status);
+  } else {
+    tma_stream(op, [&](uint32_t slot, uint32_t bar, int, int tile, int kc) { Op::issue(p, slot, bar, tile, kc); },
+               rg, pt, tb, red, warp, wu0, wu1, cu0, cu1, status);
+  }
 }
 
 // Partial-sum scratch of a CTA: two slots per warp.
@@ -328,7 +457,7 @@ __host__ __device__ inline uint32_t quad_scratch_bytes(bool nk, int nb, int M) {
 // are filled; after it lane 0 of every warp initialises its ring and issues
 // its first S units, whose copies overlap the table build or copy.  Then
 // every warp streams and reduces on its own; there is no closing barrier.
-template <bool NK, int NB>
+template <bool NK, int NB, bool PLUG>
 __global__ void __launch_bounds__(quad_warps(NK, NB) * 32, 1) quad_gemv_kernel(const __grid_constant__ QuadParams p) {
   constexpr int NW = quad_warps(NK, NB);
   pdl_launch_dependents();
@@ -339,7 +468,8 @@ __global__ void __launch_bounds__(quad_warps(NK, NB) * 32, 1) quad_gemv_kernel(c
   int* status = p.part.counters + (kMaxGrid - 1);
   const QuadLayout L = base == p.layout_base
                            ? p.layout
-                           : quad_layout(base, p.smem_bytes, NW, p.stages, quad_scratch_bytes(NK, NB, p.M), true);
+                           : quad_layout(base, p.smem_bytes, NW, p.stages, quad_scratch_bytes(NK, NB, p.M), true,
+                                         PLUG ? p.pcap : 0u);
   if (!L.ok) {  // the host plans for this never to happen
     if (threadIdx.x == 0) atomicExch(status, 2);
     return;
@@ -358,14 +488,23 @@ __global__ void __launch_bounds__(quad_warps(NK, NB) * 32, 1) quad_gemv_kernel(c
   int* ti = reinterpret_cast<int*>(pp_smem + (L.tables - base));
   const CtaTables tb{ti, ti + (NW + 1), ti + 2 * (NW + 1)};
   cta_tables_init<NW>(tb, cu0, cu1, p.part.upt);
-  const int warp = threadIdx.x >> 5;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int wu0 = warp_start<NW>(cu0, cu1, warp), wu1 = warp_start<NW>(cu0, cu1, warp + 1);
+  // PLUG: the plug-stream offsets of units wu0..wu1 (the host keeps
+  // wu1 - wu0 < kPlugTabEntries), loaded now, stored after the table wait
+  uint32_t po0 = 0u, po1 = 0u;
+  if constexpr (PLUG) {
+    const int nu = wu1 - wu0;
+    if (nu > 0 && lane <= nu) po0 = __ldg(p.uplug_off + wu0 + lane);
+    if (nu > 0 && lane + 32 <= nu) po1 = __ldg(p.uplug_off + wu0 + lane + 32);
+  }
   TmaRing rg;
   if (wu0 < wu1) {
     const uint32_t rw = (uint32_t)p.stages * 2048u;
     rg.ring = warp < L.splitw ? L.ringA + (uint32_t)warp * rw : L.ringB + (uint32_t)(warp - L.splitw) * rw;
     rg.bars = L.bars + 8u * (uint32_t)(warp * p.stages);
     rg.S = p.stages;
+    rg.P = PLUG ? p.stages + 1 : p.stages;
     rg.next.init(wu0, wu1, p.part.upt);
   }
   uint32_t* stage = reinterpret_cast<uint32_t*>(pp_smem + (L.scratch - base));
@@ -373,8 +512,10 @@ __global__ void __launch_bounds__(quad_warps(NK, NB) * 32, 1) quad_gemv_kernel(c
   __syncthreads();
   if (wu0 < wu1 && (threadIdx.x & 31) == 0) {
     if (warp == 0) prefetch_tmap(&p.tmap);
-    rg.prologue([&](uint32_t slot, uint32_t bar, int tile, int kc) {
-      QuadOp<NK, NB, false>::issue(p, slot, bar, tile, kc);
+    // PLUG: codes only for now; the plug copies, which need the offsets,
+    // arrive on the barriers after the table wait
+    rg.prologue([&](uint32_t slot, uint32_t bar, int, int tile, int kc) {
+      QuadOp<NK, NB, false>::template issue<!PLUG>(p, slot, bar, tile, kc);
     }, 2048u);
   }
   if (prepared) {
@@ -383,12 +524,34 @@ __global__ void __launch_bounds__(quad_warps(NK, NB) * 32, 1) quad_gemv_kernel(c
     quad_lut_fanout(pp_smem + (L.lut - base), stage);
     __syncthreads();
   }
+  if constexpr (PLUG) {
+    if (wu0 < wu1) {
+      const uint32_t ptab = L.ptab + (uint32_t)warp * (kPlugTabEntries * 4u);
+      const int nu = wu1 - wu0;
+      if (lane <= nu) sts_u32(ptab + 4u * (uint32_t)lane, po0);
+      if (lane + 32 <= nu) sts_u32(ptab + 4u * (uint32_t)(lane + 32), po1);
+      __syncwarp();
+      if (lane == 0) {  // the plug copies of the prologue units, in the same order
+        const uint32_t pring = L.plug + (uint32_t)(warp * (p.stages + 1)) * p.pcap;
+        UnitSeq q;
+        q.init(wu0, wu1, p.part.upt);
+        for (int i = 0; i < p.stages && q.seg < 3; ++i) {
+          uint32_t off;
+          const uint32_t pb = plug_bytes(p, ptab, wu0, q.t * p.part.upt + q.kc, &off);
+          const uint32_t bar = rg.bars + 8u * (uint32_t)i;
+          mbar_expect_tx(bar, pb);
+          bulk_load(pring + (uint32_t)i * p.pcap, p.uplugs + off, pb, bar);
+          q.advance();
+        }
+      }
+    }
+  }
   // everything above reads only weights; activations, the workspace and the
   // outputs may belong to the previous kernel of the stream
   pdl_wait();
   if (wu0 >= wu1) return;
-  if (L.direct) quad_body<NK, NB, true>(p, pt, L, rg, tb, cu0, cu1, wu0, wu1, status);
-  else quad_body<NK, NB, false>(p, pt, L, rg, tb, cu0, cu1, wu0, wu1, status);
+  if (L.direct) quad_body<NK, NB, true, PLUG>(p, pt, L, rg, tb, cu0, cu1, wu0, wu1, status);
+  else quad_body<NK, NB, false, PLUG>(p, pt, L, rg, tb, cu0, cu1, wu0, wu1, status);
 }
 
 // Generic fallback for layouts the vector paths do not take (unaligned or
@@ -473,30 +636,37 @@ PartitionPlan quad_plan(bool nk, int64_t Mc, int64_t N, int64_t K, int sms, int*
 bool g_attr_done[8][64];
 int g_attr_limit[8][64];
 
+// Plug slot beside every ring slot of the fused plug correction: a segment
+// of up to (512 - 16) / 9 = 55 entries is staged; larger ones are read from
+// HBM by the lanes.
+constexpr uint32_t kPlugCap = 512u;
+
 // Deepest ring (up to 4 slots per consumer) with the tables at a 64 KiB
 // boundary for a dynamic region at the reserved-memory offset, else the
 // deepest that fits with the tables at the base.  Both must also fit with
 // the tables at the base, which the kernel falls back to if the runtime
 // base differs.  Returns 0 if nothing fits.
-int quad_stages(int nw, uint32_t redb, uint32_t reserved, uint32_t size) {
+int quad_stages(int nw, uint32_t redb, uint32_t reserved, uint32_t size, uint32_t pcap = 0u) {
   int plain = 0;
   for (int S = 4; S >= 1; --S) {
-    if (!quad_layout(reserved, size, nw, S, redb, false).ok) continue;
+    if (!quad_layout(reserved, size, nw, S, redb, false, pcap).ok) continue;
     if (!plain) plain = S;
-    if (S >= 2 && quad_layout(reserved, size, nw, S, redb, true).direct) return S;
+    if (S >= 2 && quad_layout(reserved, size, nw, S, redb, true, pcap).direct) return S;
   }
   return plain;
 }
 
-template <bool NK, int NB>
+template <bool NK, int NB, bool PLUG>
 int launch_quad(QuadParams& prm, int grid, int idx, cudaStream_t s) {
   constexpr int NW = quad_warps(NK, NB);
-  auto kern = quad_gemv_kernel<NK, NB>;
+  auto kern = quad_gemv_kernel<NK, NB, PLUG>;
   int max_smem = 0;
   int rc = ensure_smem_attr(kern, g_attr_done[idx], g_attr_limit[idx], &max_smem);
   if (rc) return rc;
   const uint32_t redb = quad_scratch_bytes(NK, NB, prm.M);
-  const int stages = quad_stages(NW, redb, (uint32_t)reserved_smem(current_device()), (uint32_t)max_smem);
+  prm.pcap = PLUG ? kPlugCap : 0u;
+  const int stages =
+      quad_stages(NW, redb, (uint32_t)reserved_smem(current_device()), (uint32_t)max_smem, prm.pcap);
   if (stages == 0) {
     set_error("no shared memory layout fits the per-CTA limit %d", max_smem);
     return PP_ERR_INVALID;
@@ -504,7 +674,7 @@ int launch_quad(QuadParams& prm, int grid, int idx, cudaStream_t s) {
   prm.stages = stages;
   prm.smem_bytes = (uint32_t)max_smem;
   prm.layout_base = (uint32_t)reserved_smem(current_device());
-  prm.layout = quad_layout(prm.layout_base, prm.smem_bytes, NW, stages, redb, true);
+  prm.layout = quad_layout(prm.layout_base, prm.smem_bytes, NW, stages, redb, true, prm.pcap);
   return launch_kernel("quad_gemv_kernel", launch_overlap(), kern, dim3(grid), dim3(NW * 32), (size_t)max_smem, s,
                        prm);
 }
@@ -513,14 +683,31 @@ int launch_quad(QuadParams& prm, int grid, int idx, cudaStream_t s) {
 inline size_t corr_bytes(int64_t N) { return align_up((size_t)4 * 16 * N * sizeof(float), 256); }
 
 int launch_plan(const PartitionPlan& pl, bool nk, int64_t Mc, QuadParams prm, void* ws, size_t corr_sz,
-                cudaStream_t s) {
+                cudaStream_t s, bool fused_plugs = false) {
   prm.part.units = (int)pl.units;
   prm.part.upt = (int)pl.upt;
   prm.part.counters = reinterpret_cast<int*>(ws);
   prm.part.slots = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(ws) + pl.counters_bytes + corr_sz);
+  if (fused_plugs) return launch_quad<true, 1, true>(prm, pl.grid, 4, s);
   const int nb = Mc > 8 ? 2 : 1;
-  if (nk) return nb == 1 ? launch_quad<true, 1>(prm, pl.grid, 0, s) : launch_quad<true, 2>(prm, pl.grid, 1, s);
-  return nb == 1 ? launch_quad<false, 1>(prm, pl.grid, 2, s) : launch_quad<false, 2>(prm, pl.grid, 3, s);
+  if (nk)
+    return nb == 1 ? launch_quad<true, 1, false>(prm, pl.grid, 0, s) : launch_quad<true, 2, false>(prm, pl.grid, 1, s);
+  return nb == 1 ? launch_quad<false, 1, false>(prm, pl.grid, 2, s) : launch_quad<false, 2, false>(prm, pl.grid, 3, s);
+}
+
+// The fused plug correction runs when the batch is one row, every warp's
+// unit range fits its offset table and the layout with plug slots fits.
+bool fused_plugs_ok(const PartitionPlan& pl, const int* starts, int64_t Mc) {
+  if (Mc != 1) return false;
+  constexpr int NW = quad_warps(true, 1);
+  for (int c = 0; c < pl.grid; ++c) {
+    const int64_t r = (int64_t)starts[c + 1] - starts[c];
+    if ((r + NW - 1) / NW >= (int64_t)kPlugTabEntries) return false;
+  }
+  int lim = 0;
+  if (ensure_smem_attr(quad_gemv_kernel<true, 1, true>, g_attr_done[4], g_attr_limit[4], &lim)) return false;
+  return quad_stages(NW, quad_scratch_bytes(true, 1, 1), (uint32_t)reserved_smem(current_device()), (uint32_t)lim,
+                     kPlugCap) > 0;
 }
 
 bool quad_vector_ok(bool nk, const uint32_t* codes, int64_t ldc_k, int64_t ldc_n, int64_t N, int64_t K) {
@@ -584,7 +771,7 @@ size_t quad_ws_bytes(bool nk, int64_t M, int64_t N, int64_t K, bool plug) {
 
 static int quad_run(const void* a, int64_t lda_m, int64_t lda_k, const uint32_t* codes, int64_t ldc_k,
                     int64_t ldc_n, const uint32_t* plug_idx, const void* plug_vals, const uint32_t* wbase,
-                    uint32_t base_lo32,
+                    uint32_t base_lo32, const uint8_t* uplugs, const uint32_t* uplug_off,
                     const void* const luts[7], const void* tables, const float scales[4], void* const out[4],
                     int64_t ldo_m, int64_t ldo_n, int64_t M, int64_t N, int64_t K, void* ws, size_t ws_bytes,
                     cudaStream_t s, bool file_layout) {
@@ -603,6 +790,10 @@ static int quad_run(const void* a, int64_t lda_m, int64_t lda_k, const uint32_t*
   const bool plug = file_layout && plug_vals != nullptr;
   if (plug && (!plug_idx || !wbase || !aligned(plug_vals, 8))) {
     set_error("plug_idx / plug_window_base missing or plug_vals not 8-byte aligned");
+    return PP_ERR_INVALID;
+  }
+  if (uplugs && (!plug || !uplug_off || !aligned(uplugs, 16) || !aligned(uplug_off, 4))) {
+    set_error("unit plugs need the plug table too, their offsets, and 16-byte alignment");
     return PP_ERR_INVALID;
   }
   const bool nk = file_layout || (ldc_k == 1 && ldc_n != 1);
@@ -718,6 +909,13 @@ static int quad_run(const void* a, int64_t lda_m, int64_t lda_k, const uint32_t*
     for (int i = 0; i < 4; ++i) prm.out[i] = reinterpret_cast<__half*>(out[i]) + m0 * ldo_m;
     prm.M = (int)Mc;
     prm.corr = corr;
+    if (uplugs && fused_plugs_ok(pl, prm.cta_start, Mc)) {
+      prm.corr = nullptr;
+      prm.uplugs = uplugs;
+      prm.uplug_off = uplug_off;
+      if ((rc = launch_plan(pl, nk, Mc, prm, ws, csz, s, true))) return rc;
+      continue;
+    }
     if (plug) {
       PlugCorrParams cp{prm.x, lda_m, plug_idx, reinterpret_cast<const uint2*>(plug_vals), wbase, base_lo32,
                         (int)Mc, (int)N, (int)K, (int)cdiv(K, 64), corr, Mc * N};
@@ -747,7 +945,8 @@ int pp_quad_gemm(const void* a, int64_t lda_m, int64_t lda_k, const uint32_t* co
                  int64_t ldc_n, const void* const luts[7], const float scales[4], void* const out[4],
                  int64_t ldo_m, int64_t ldo_n, int64_t M, int64_t N, int64_t K, void* workspace,
                  size_t workspace_bytes, void* stream) {
-  return pp::quad_run(a, lda_m, lda_k, codes, ldc_k, ldc_n, nullptr, nullptr, nullptr, 0u, luts, nullptr, scales,
+  return pp::quad_run(a, lda_m, lda_k, codes, ldc_k, ldc_n, nullptr, nullptr, nullptr, 0u, nullptr, nullptr, luts,
+                      nullptr, scales,
                       out, ldo_m, ldo_n, M, N, K, workspace, workspace_bytes,
                       reinterpret_cast<cudaStream_t>(stream), false);
 }
@@ -760,8 +959,8 @@ int pp_quad_gemm_prepared(const void* a, int64_t lda_m, int64_t lda_k, const uin
     pp::set_error("tables must not be NULL");
     return PP_ERR_INVALID;
   }
-  return pp::quad_run(a, lda_m, lda_k, codes, ldc_k, ldc_n, nullptr, nullptr, nullptr, 0u, nullptr, tables,
-                      scales, out, ldo_m, ldo_n, M, N, K, workspace, workspace_bytes,
+  return pp::quad_run(a, lda_m, lda_k, codes, ldc_k, ldc_n, nullptr, nullptr, nullptr, 0u, nullptr, nullptr,
+                      nullptr, tables, scales, out, ldo_m, ldo_n, M, N, K, workspace, workspace_bytes,
                       reinterpret_cast<cudaStream_t>(stream), false);
 }
 
@@ -779,8 +978,8 @@ int pp_quad_linear(const void* x, int64_t ldx_m, int64_t ldx_k, const uint32_t* 
                    uint32_t base_lo32, const void* const luts[7], const float scales[4], void* const out[4],
                    int64_t ldo_m, int64_t ldo_n, int64_t M, int64_t N, int64_t K, void* workspace,
                    size_t workspace_bytes, void* stream) {
-  return pp::quad_run(x, ldx_m, ldx_k, codes, 1, ldw, plug_idx, plug_vals, plug_window_base, base_lo32, luts,
-                      nullptr, scales, out, ldo_m, ldo_n, M, N, K, workspace, workspace_bytes,
+  return pp::quad_run(x, ldx_m, ldx_k, codes, 1, ldw, plug_idx, plug_vals, plug_window_base, base_lo32, nullptr,
+                      nullptr, luts, nullptr, scales, out, ldo_m, ldo_n, M, N, K, workspace, workspace_bytes,
                       reinterpret_cast<cudaStream_t>(stream), true);
 }
 
@@ -794,8 +993,24 @@ int pp_quad_linear_prepared(const void* x, int64_t ldx_m, int64_t ldx_k, const u
     return PP_ERR_INVALID;
   }
   return pp::quad_run(x, ldx_m, ldx_k, codes, 1, ldw, plug_idx, plug_vals, plug_window_base, base_lo32, nullptr,
-                      tables, scales, out, ldo_m, ldo_n, M, N, K, workspace, workspace_bytes,
+                      nullptr, nullptr, tables, scales, out, ldo_m, ldo_n, M, N, K, workspace, workspace_bytes,
                       reinterpret_cast<cudaStream_t>(stream), true);
+}
+
+int pp_quad_linear_fused(const void* x, int64_t ldx_m, int64_t ldx_k, const uint32_t* codes, int64_t ldw,
+                         const uint32_t* plug_idx, const void* plug_vals, const uint32_t* plug_window_base,
+                         uint32_t base_lo32, const void* unit_plugs, const uint32_t* unit_plug_off,
+                         const void* tables, const float scales[4], void* const out[4], int64_t ldo_m,
+                         int64_t ldo_n, int64_t M, int64_t N, int64_t K, void* workspace, size_t workspace_bytes,
+                         void* stream) {
+  if (!tables || (unit_plugs && (!unit_plug_off || !plug_vals))) {
+    pp::set_error("tables must not be NULL; unit plugs need their offsets and the plug table");
+    return PP_ERR_INVALID;
+  }
+  return pp::quad_run(x, ldx_m, ldx_k, codes, 1, ldw, plug_idx, plug_vals, plug_window_base, base_lo32,
+                      reinterpret_cast<const uint8_t*>(unit_plugs), unit_plug_off, nullptr, tables, scales, out,
+                      ldo_m, ldo_n, M, N, K, workspace, workspace_bytes, reinterpret_cast<cudaStream_t>(stream),
+                      true);
 }
 
 }  // extern "C"

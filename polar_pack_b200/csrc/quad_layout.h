@@ -14,28 +14,41 @@ namespace pp {
 
 constexpr uint32_t kQuadTableBytes = 2u * 65536u;  // the four replicated tables
 constexpr uint32_t kQuadUnitBytes = 2048u;         // one TMA ring slot
+// fused plug correction: unit offsets each warp keeps in shared memory (its
+// unit range [wu0, wu1] inclusive, so at most kPlugTabEntries - 1 units)
+constexpr uint32_t kPlugTabEntries = 64u;
 
 // Shared-memory layout of one CTA, computed identically on the host (for
 // the expected dynamic base) and in the kernel (for the actual one).  The
 // tables go to the first 64 KiB boundary when everything else fits around
 // them (DIRECT gathers); the consumer rings fill the gap below the tables
 // (region A), then the space above (region B); the ring mbarriers, a flag
-// word, the per-CTA int tables and the scratch block go where room is left.  The scratch block stages the
-// table build and afterwards holds the consumers' partial slots (written
-// while other rings are still streaming, so it never overlaps a ring).
-// Without room for the aligned placement the tables start at the base.
+// word, the per-CTA int tables, the scratch block and (with a fused plug
+// correction) the plug region go where room is left.  The scratch block
+// stages the table build and afterwards holds the consumers' partial slots
+// (written while other rings are still streaming, so it never overlaps a
+// ring).  The plug region holds, per warp, S + 1 plug slots of pcap bytes
+// (one more than ring slots, so the unit being computed keeps its slot
+// while the next ones arrive), then the warps' unit-offset tables.  Without room for the aligned placement the tables start
+// at the base.
 struct QuadLayout {
-  uint32_t lut, ringA, ringB, bars, flag, tables, scratch;
+  uint32_t lut, ringA, ringB, bars, flag, tables, scratch, plug, ptab;
   int splitw, direct, ok;
 };
+
+// bytes of the plug region for nw warps of S + 1 slots of pcap bytes (0: none)
+PP_HD inline uint32_t quad_plug_region_bytes(int nw, int S, uint32_t pcap) {
+  return pcap ? (uint32_t)nw * ((uint32_t)(S + 1) * pcap + kPlugTabEntries * 4u) : 0u;
+}
 
 // bytes of the per-CTA int tables (warp range starts, their tiles, split
 // tile counters: 4 * warps + 2 ints, at most 16 warps)
 constexpr uint32_t kQuadTablesBytes = 512u;
 
 PP_HD inline QuadLayout quad_layout(uint32_t base, uint32_t size, int nw, int S, uint32_t redb,
-                                                  bool allow_direct) {
+                                    bool allow_direct, uint32_t pcap = 0u) {
   QuadLayout L{};
+  const uint32_t plugb = quad_plug_region_bytes(nw, S, pcap);
   const uint32_t rw = (uint32_t)S * kQuadUnitBytes;
   const uint32_t barb = ((uint32_t)(nw * S * 8) + 15u) & ~15u;
   const uint32_t smallb = barb + 16u + kQuadTablesBytes;  // bars, flag, tables
@@ -60,6 +73,12 @@ PP_HD inline QuadLayout quad_layout(uint32_t base, uint32_t size, int nw, int S,
     at = (fa + scr <= lut) ? &fa : &fb;
     L.scratch = (uint32_t)*at;
     *at += scr;
+    if (plugb) {
+      at = (fa + plugb <= lut) ? &fa : &fb;
+      L.plug = (uint32_t)*at;
+      L.ptab = L.plug + (uint32_t)nw * (uint32_t)(S + 1) * pcap;
+      *at += plugb;
+    }
     if (fb <= end) {
       L.direct = 1;
       L.ok = 1;
@@ -79,6 +98,11 @@ PP_HD inline QuadLayout quad_layout(uint32_t base, uint32_t size, int nw, int S,
   p += smallb;
   L.scratch = (uint32_t)p;
   p += scr;
+  if (plugb) {
+    L.plug = (uint32_t)p;
+    L.ptab = L.plug + (uint32_t)nw * (uint32_t)(S + 1) * pcap;
+    p += plugb;
+  }
   L.ok = p <= end;
   return L;
 }

@@ -126,6 +126,10 @@ class QuadLinearSlice:
     plug_idx: torch.Tensor | None
     plug_vals: torch.Tensor | None
     plug_window_base: torch.Tensor | None
+    # unit-major copy of the plug slice (pp_quad_prepare_unit_plugs): the
+    # GEMV streams it beside the codes and needs no correction kernel
+    unit_plugs: torch.Tensor | None = None
+    unit_plug_off: torch.Tensor | None = None
     _ws: dict = field(default_factory=dict)
 
     @property
@@ -173,6 +177,8 @@ class QuadPackDevice:
                       _lib.stream_handle(self.device))
             pi = self.plug_idx[p_lo:p_hi]
             pv = self.plug_vals[p_lo:p_hi]
+            up, uo = prepare_unit_plugs(pi, pv, wb, offset, N, K, self.device)
+            return QuadLinearSlice(self, offset, N, K, p_lo, p_hi, codes, pi, pv, wb, up, uo)
         return QuadLinearSlice(self, offset, N, K, p_lo, p_hi, codes, pi, pv, wb)
 
     def check_plug_index(self) -> None:
@@ -199,6 +205,20 @@ class QuadPackDevice:
                   ctypes.cast(sc, ctypes.c_void_p) if sc is not None else None,
                   _lib.ptrs(outs, 4), _lib.stream_handle(self.device))
         return outs
+
+
+def prepare_unit_plugs(plug_idx: torch.Tensor, plug_vals: torch.Tensor, window_base: torch.Tensor, offset: int,
+                       N: int, K: int, device) -> tuple[torch.Tensor, torch.Tensor]:
+    """Unit-major plug stream and its unit offsets for one Linear's plug slice."""
+    nbytes, noff = _lib._size_t(), ctypes.c_int64()
+    P = int(plug_idx.numel())
+    _lib.check(_lib.load().pp_quad_unit_plugs_bytes(N, K, P, ctypes.byref(nbytes), ctypes.byref(noff)))
+    stream = torch.empty(max(nbytes.value, 16), dtype=torch.uint8, device=device)
+    off = torch.empty(noff.value, dtype=torch.int32, device=device)
+    _lib.call("pp_quad_prepare_unit_plugs", _lib.ptr(plug_idx), _lib.ptr(plug_vals), P,
+              ctypes.c_uint32(offset & 0xFFFFFFFF), window_base.data_ptr(), N, K, stream.data_ptr(),
+              stream.numel(), off.data_ptr(), _lib.stream_handle(torch.device(device)))
+    return stream, off
 
 
 def quad_linear_workspace_bytes(M: int, N: int, K: int) -> int:
@@ -229,15 +249,20 @@ def quad_linear(x: torch.Tensor, layer: QuadLinearSlice, out=None) -> list[torch
     c = layer._ws.get("args")
     if c is None:
         pk = layer.pack
-        c = (_lib.load().pp_quad_linear_prepared, layer.codes.data_ptr(), layer.K, _lib.ptr(layer.plug_idx),
-             _lib.ptr(layer.plug_vals), _lib.ptr(layer.plug_window_base), ctypes.c_uint32(layer.offset & 0xFFFFFFFF),
-             pk.tables.data_ptr(), _lib.floats4(pk.scales))
+        lib = _lib.load()
+        head = (layer.codes.data_ptr(), layer.K, _lib.ptr(layer.plug_idx), _lib.ptr(layer.plug_vals),
+                _lib.ptr(layer.plug_window_base), ctypes.c_uint32(layer.offset & 0xFFFFFFFF))
+        if layer.unit_plugs is not None:
+            c = (lib.pp_quad_linear_fused, *head, layer.unit_plugs.data_ptr(), layer.unit_plug_off.data_ptr(),
+                 pk.tables.data_ptr(), _lib.floats4(pk.scales))
+        else:
+            c = (lib.pp_quad_linear_prepared, *head, pk.tables.data_ptr(), _lib.floats4(pk.scales))
         layer._ws["args"] = c
     nb = layer._ws.get(("ws", M))
     if nb is None:
         nb = layer._ws[("ws", M)] = quad_linear_workspace_bytes(M, layer.N, layer.K)
     ws = _lib.workspace(dev, nb) if nb else None
-    _lib.check(c[0](x.data_ptr(), x.stride(0), x.stride(1), c[1], c[2], c[3], c[4], c[5], c[6], c[7], c[8],
+    _lib.check(c[0](x.data_ptr(), x.stride(0), x.stride(1), *c[1:],
                     _lib.ptrs(out, 4), out[0].stride(0), out[0].stride(1), M, layer.N, layer.K,
                     _lib.ptr(ws), ws.numel() if ws is not None else 0, _lib.stream_handle(dev)))
     return out

@@ -16,8 +16,8 @@ struct Blk {
   const char* what;
 };
 
-static int check(uint32_t base, uint32_t size, int nw, int S, uint32_t redb, bool direct_ok) {
-  const QuadLayout L = quad_layout(base, size, nw, S, redb, direct_ok);
+static int check(uint32_t base, uint32_t size, int nw, int S, uint32_t redb, bool direct_ok, uint32_t pcap) {
+  const QuadLayout L = quad_layout(base, size, nw, S, redb, direct_ok, pcap);
   if (!L.ok) return 0;
   const uint64_t end = (uint64_t)base + size;
   const uint32_t rw = (uint32_t)S * kQuadUnitBytes;
@@ -48,6 +48,14 @@ static int check(uint32_t base, uint32_t size, int nw, int S, uint32_t redb, boo
     return -1;
   }
   b.push_back({L.scratch, (uint64_t)L.scratch + scr, "scratch"});
+  if (pcap) {
+    if (L.plug % 16 || L.ptab % 16 || L.ptab != L.plug + (uint32_t)nw * (S + 1) * pcap) {
+      printf("FAIL plug region misaligned or misplaced\n");
+      return -1;
+    }
+    b.push_back({L.plug, (uint64_t)L.plug + (uint64_t)nw * (S + 1) * pcap, "plug slots"});
+    b.push_back({L.ptab, (uint64_t)L.ptab + (uint64_t)nw * kPlugTabEntries * 4u, "plug tables"});
+  }
   if (L.direct && (L.lut % 65536u)) {
     printf("FAIL direct tables not 64 KiB aligned\n");
     return -1;
@@ -75,7 +83,9 @@ int main() {
   const struct {
     const char* name;
     int nw, tile_w, mmax;
-  } variants[] = {{"nk1", 16, 8, 8}, {"nk2", 8, 8, 16}, {"kn1", 8, 32, 8}, {"kn2", 4, 32, 16}};
+    uint32_t pcap;
+  } variants[] = {{"nk1", 16, 8, 8, 0u},  {"nk2", 8, 8, 16, 0u}, {"kn1", 8, 32, 8, 0u},
+                  {"kn2", 4, 32, 16, 0u}, {"nk1plug", 16, 8, 1, 512u}};
   const uint32_t bases[] = {0u, 16u, 1024u, 2048u, 4096u, 40000u, 65536u - 1024u, 65536u};
   const uint32_t sizes[] = {232448u, 200000u, 166912u};
   long n = 0;
@@ -86,15 +96,15 @@ int main() {
         for (uint32_t size : sizes)
           for (int S = 1; S <= 4; ++S)
             for (int d = 0; d < 2; ++d) {
-              if (check(base, size, v.nw, S, redb, d != 0) < 0) return 1;
+              if (check(base, size, v.nw, S, redb, d != 0, v.pcap) < 0) return 1;
               ++n;
             }
       // what the host planner picks for the usual window (1 KiB reserved, 227 KiB)
       int plain = 0, pick = 0, direct = 0;
       for (int S = 4; S >= 1 && !pick; --S) {
-        if (!quad_layout(1024u, 232448u, v.nw, S, redb, false).ok) continue;
+        if (!quad_layout(1024u, 232448u, v.nw, S, redb, false, v.pcap).ok) continue;
         if (!plain) plain = S;
-        if (S >= 2 && quad_layout(1024u, 232448u, v.nw, S, redb, true).direct) pick = S, direct = 1;
+        if (S >= 2 && quad_layout(1024u, 232448u, v.nw, S, redb, true, v.pcap).direct) pick = S, direct = 1;
       }
       if (!pick) pick = plain;
       if (M == 1 || M == v.mmax) printf("%s M=%d stages=%d direct=%d\n", v.name, M, pick, direct);

@@ -25,3 +25,4 @@ def test_quad_layout_blocks_disjoint_and_aligned(tmp_path):
     # batch-1 file-layout kernel (16 warps): two ring slots per warp with the
     # tables on a 64 KiB boundary (direct gathers)
     assert "nk1 M=1 stages=2 direct=1" in out.stdout
+    assert "nk1plug M=1 stages=2 direct=1" in out.stdout  # fused plug slots keep the batch-1 layout
