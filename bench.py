@@ -19,7 +19,8 @@ start its weight-only prologue while the previous one finishes), unless
 Metric: packed-stream GB/s = algorithmic bytes / device time, where the
 bytes of one Linear are 4*N*K (codes) + 12*P (plug index + values) +
 2*M*K (activations) + 8*M*N (four FP16 outputs).  The roofline entry times
-the fused GEMV kernel alone (no plug table: 4*N*K + 2*M*K + 8*M*N bytes).
+the dominant kernel, the GEMV with the plug correction fused in, one shape at
+a time over the same bytes.
 
 With N > 1 GPUs (launched by torch.distributed.run) each Linear is
 row-sharded (column-parallel): rank r owns output rows [r*N/P, (r+1)*N/P),
@@ -303,7 +304,7 @@ def run_ours(args):
     total_bytes = avg_bytes * K_steps
     value = total_bytes / (ms * 1e-3) / 1e9
 
-    # the fused GEMV kernel alone, per shape: a graph of its launches over the
+    # the dominant kernel alone, per shape: a graph of its launches over the
     # replica streams (rotating, so every launch reads codes L2 does not hold)
     per_shape, kernel_bytes, kernel_ms = {}, 0.0, 0.0
     for j, (K, N) in enumerate(SHAPES):
@@ -311,13 +312,15 @@ def run_ours(args):
         for st in sets:
             l = st[j]
             outs = [torch.empty((M, l.N), dtype=torch.float16, device=dev) for _ in range(4)]
-            gemv_args.append((xs[j].data_ptr(), xs[j].stride(0), xs[j].stride(1), l.codes.data_ptr(), 1, l.K,
-                              l.pack.tables.data_ptr(), _lib.floats4(l.pack.scales), _lib.ptrs(outs, 4),
-                              outs[0].stride(0), outs[0].stride(1), M, l.N, l.K, ws.data_ptr(), ws.numel(), sh,
-                              outs))
+            gemv_args.append((xs[j].data_ptr(), xs[j].stride(0), xs[j].stride(1), l.codes.data_ptr(), l.K,
+                              _lib.ptr(l.plug_idx), _lib.ptr(l.plug_vals), _lib.ptr(l.plug_window_base),
+                              ctypes.c_uint32(l.offset & 0xFFFFFFFF), _lib.ptr(l.unit_plugs),
+                              _lib.ptr(l.unit_plug_off), l.pack.tables.data_ptr(), _lib.floats4(l.pack.scales),
+                              _lib.ptrs(outs, 4), outs[0].stride(0), outs[0].stride(1), M, l.N, l.K,
+                              ws.data_ptr(), ws.numel(), sh, outs))
         def gemv_pass():
             for a_ in gemv_args:
-                _lib.check(lib.pp_quad_gemm_prepared(*a_[:-1]))
+                _lib.check(lib.pp_quad_linear_fused(*a_[:-1]))
         gemv_pass()
         reps = max(4, K_steps // 2)
         torch.cuda.synchronize(dev)
@@ -337,7 +340,7 @@ def run_ours(args):
         e1.record(stream)
         torch.cuda.synchronize(dev)
         tj = e0.elapsed_time(e1) / (reps * len(sets))
-        bj = statistics.mean(layer_bytes(st[j].N, st[j].K, 0, M) for st in sets)  # the GEMV reads no plugs
+        bj = statistics.mean(layer_bytes(st[j].N, st[j].K, st[j].p_hi - st[j].p_lo, M) for st in sets)
         per_shape[f"{K}x{N}"] = {"us": round(tj * 1e3, 2), "GB/s": round(bj / (tj * 1e-3) / 1e9, 1)}
         kernel_bytes += bj
         kernel_ms += tj
@@ -353,7 +356,8 @@ def run_ours(args):
         "warmup": args.warmup, "ms_per_step": round(ms / K_steps, 4), "higher_is_better": True,
         "scaling": "strong", "vs_baseline": None, "dtype": "u32 codes -> fp16 weights, fp32 accumulate",
         "data": "synthetic (seeded random-init correlated weights; no checkpoints available)",
-        "config": {"workload": WORKLOAD, "batch": M, "replica_streams": args.replicas,
+        "config": {"workload": WORKLOAD if not args.shapes else f"subset {args.shapes} of: {WORKLOAD}",
+                   "batch": M, "replica_streams": args.replicas,
                    "bytes_per_step": int(per_step_bytes), "l2": "inputs per step ~200 MB > 126 MB L2, "
                    "4 rotating replica streams (no flush)",
                    "parallelism": f"row-sharded x{world}, one NCCL all-gather per step" if world > 1
@@ -363,11 +367,12 @@ def run_ours(args):
                    "per_shape_gemv_kernel": per_shape},
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(achieved / peak, 4), "peak_source": f"{peak_kind} hbm_gbs",
-                     "kernel": "quad_gemv_kernel<NK=1,NB=1> (file layout, batch 1)",
-                     "achieved_from": "GEMV algorithmic bytes (4NK + 2MK + 8MN) over the 4 shapes / their "
+                     "kernel": "quad_gemv_kernel<NK=1,NB=1,PLUG=1> (file layout, batch 1, plugs fused)",
+                     "achieved_from": "algorithmic bytes (4NK + 12P + 2MK + 8MN) over the 4 shapes / their "
                                       "per-launch CUDA-event time (graph of back-to-back launches)",
                      "traffic": traffic,
-                     "traffic_of": "one 2048x11008 launch (ncu dram read + write; profiles/quad_gemv_2048x11008.md)"},
+                     "traffic_of": "one 2048x11008 launch (ncu dram read + write; "
+                                   "profiles/quad_gemv_fused_2048x11008.md)"},
         "e2e": e2e,
         "gpu_launches": launches_per_step * K_steps,
         "gpu_launches_note": "per Linear: the GEMV kernel with the plug correction fused in (batch 1)",
@@ -386,32 +391,36 @@ def run_ours(args):
 
 
 def run_e2e(torch, dist, sets, xs, dev, args, world, M, full_sets):
-    """Same metric through the public API: pinned H2D of each step's inputs,
-    the Linear calls (with N > 1 GPUs the row-sharded Linear, whose outputs
-    are all-gathered over NCCL), D2H of the four full outputs, all inside the
-    timed region."""
+    """Same metric through the public API: every step copies that step's
+    inputs from pinned host memory to the GPU, runs the Linears as one
+    RowShardedGroup (with N > 1 GPUs each rank computes its row shards and
+    one NCCL all-gather collects them), and copies the step's result (the
+    four models' outputs of every Linear, gathered) back to pinned host
+    memory -- one copy each way, all inside the timed region."""
     from polar_pack_b200.parallel import RowShardedGroup
     from polar_pack_b200.quadpack import quad_linear
     stream = torch.cuda.current_stream(dev)
-    hx = [x.cpu().pin_memory() for x in xs]
-    h2d = sum(x.numel() * 2 for x in hx)
-    d2h = 0
-    host_out = []
+    sizes = [x.numel() for x in xs]
+    hx = torch.cat([x.reshape(-1) for x in xs]).cpu().pin_memory()   # all inputs, one pinned buffer
+    dxf = torch.empty_like(hx, device=dev)
+    dx, o = [], 0
+    for x, n in zip(xs, sizes):
+        dx.append(dxf[o:o + n].view(x.shape))
+        o += n
     full_n = [N for _, N in SHAPES]
-    for N in full_n:
-        host_out.append([torch.empty((M, N), dtype=torch.float16).pin_memory() for _ in range(4)])
-        d2h += 4 * M * N * 2
-    dx = [torch.empty_like(x) for x in xs]
-    # the four independent Linears as one row-sharded group: one all-gather per step
-    groups = [RowShardedGroup([lambda x, l=l: quad_linear(x, l) for l in st], full_n) for st in sets]
+    # the independent Linears as one row-sharded group writing into its send buffer
+    groups = [RowShardedGroup([lambda x, out, l=l: quad_linear(x, l, out=out) for l in st], full_n,
+                              writes_out=True) for st in sets]
+    for g_ in groups:
+        g_(dx)
+    host_out = torch.empty(groups[0].raw().shape, dtype=torch.float16).pin_memory()
+    h2d, d2h = hx.numel() * 2, host_out.numel() * 2
 
     def step(i):
-        for j in range(len(dx)):
-            dx[j].copy_(hx[j], non_blocking=True)
-        yss = groups[i % len(groups)](dx)
-        for j, ys in enumerate(yss):
-            for k in range(4):
-                host_out[j][k].copy_(ys[k], non_blocking=True)
+        dxf.copy_(hx, non_blocking=True)
+        grp = groups[i % len(groups)]
+        grp(dx)
+        host_out.copy_(grp.raw(), non_blocking=True)
 
     for i in range(args.warmup):
         step(i)
@@ -434,7 +443,8 @@ def run_e2e(torch, dist, sets, xs, dev, args, world, M, full_sets):
         for l in full_sets[(args.warmup + i) % len(full_sets)]:
             total += layer_bytes(l.N, l.K, l.p_hi - l.p_lo, M)
     return {"value": round(total / (ms * 1e-3) / 1e9, 1), "unit": UNIT, "h2d_bytes_per_step": int(h2d),
-            "d2h_bytes_per_step": int(d2h), "api": "polar_pack_b200.quadpack.quad_linear"}
+            "d2h_bytes_per_step": int(d2h),
+            "api": "polar_pack_b200.parallel.RowShardedGroup of polar_pack_b200.quadpack.quad_linear"}
 
 
 def load_traffic():
@@ -442,7 +452,7 @@ def load_traffic():
     if not p.exists():
         return None
     try:
-        return json.loads(p.read_text()).get("dram_bytes_per_launch_2048x11008")
+        return json.loads(p.read_text()).get("dram_bytes_per_launch_2048x11008_fused")
     except Exception:
         return None
 
@@ -602,9 +612,17 @@ def main():
     ap.add_argument("--ref-fraction", type=float, default=1 / 32)
     ap.add_argument("--eager", action="store_true", help="time eager launches instead of CUDA graphs")
     ap.add_argument("--no-overlap", action="store_true", help="launch kernels without programmatic overlap")
+    ap.add_argument("--shapes", default="", help="subset of the sweep as KxN,KxN (in x out), e.g. for profiling "
+                                                 "one Linear; the line then names the subset")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
+    if args.shapes:
+        want = [tuple(int(v) for v in t.split("x")) for t in args.shapes.split(",")]
+        bad = [w for w in want if w not in SHAPES]
+        if bad:
+            raise SystemExit(f"--shapes: {bad} not in the sweep {SHAPES}")
+        SHAPES[:] = want
     if args.impl == "reference":
         run_reference(args)
     else:

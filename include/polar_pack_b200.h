@@ -192,7 +192,8 @@ PP_API int pp_quad_prepare_plugs(uint32_t* codes, int64_t ldw, const uint32_t* p
  * quaternion_packer.py:187-193 merges on the host).  Work unit
  * u = t * ceil(K/64) + kc covers rows 8t..8t+7 and columns 64kc..64kc+63;
  * its segment starts at byte unit_plug_off[u] (a multiple of 16):
- *   16-byte header of eight uint16: entries of rows 8t..8t+r, r = 0..7;
+ *   32-byte header of eight uint32, one per tile row r:
+ *     start_r | end_r << 10 | n << 20 (row 8t + r owns entries [start_r, end_r));
  *   the n entries' FP16x4 values (row-major, column ascending);
  *   their n column bytes (column - 64kc); zeros to a multiple of 16.
  * unit_plug_off has ceil(N/8) * ceil(K/64) + 1 entries; the last is the

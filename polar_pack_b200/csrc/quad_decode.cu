@@ -453,10 +453,13 @@ int launch_plug_corr(const PlugCorrParams& prm, cudaStream_t s) {
 // covers rows 8t..8t+7 and columns 64kc..64kc+63.  Its segment starts at
 // byte off[u], a multiple of 16, and holds its n plug entries in table
 // order (row-major, k ascending):
-//   bytes [0, 16)          eight u16: entries of rows 8t..8t+r, r = 0..7
-//   bytes [16, 16 + 8n)    the entries' FP16x4 values (as in plug_vals)
-//   bytes [16 + 8n, 16+9n) the entries' columns k - 64kc
-// then zeros up to the next multiple of 16.  off[U] = total bytes.
+//   bytes [0, 32)          eight u32, one per tile row r:
+//                          start_r | end_r << 10 | n << 20
+//                          (entries [start_r, end_r) belong to row 8t + r)
+//   bytes [32, 32 + 8n)    the entries' FP16x4 values (as in plug_vals)
+//   bytes [32 + 8n, 32+9n) the entries' columns k - 64kc
+// then zeros up to the next multiple of 16.  off[U] = total bytes.  One
+// 32-bit read gives a lane its row's range and the segment's size.
 namespace pp {
 
 struct UnitPlugParams {
@@ -469,7 +472,7 @@ struct UnitPlugParams {
   uint32_t* off;             // [U + 1]
 };
 
-__host__ __device__ inline uint32_t unit_plug_seg_bytes(uint32_t n) { return (16u + 9u * n + 15u) & ~15u; }
+__host__ __device__ inline uint32_t unit_plug_seg_bytes(uint32_t n) { return (32u + 9u * n + 15u) & ~15u; }
 
 __global__ void unit_plug_size_kernel(const UnitPlugParams p) {
   for (int64_t u = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; u <= p.U; u += (int64_t)gridDim.x * blockDim.x) {
@@ -534,7 +537,7 @@ __global__ void unit_plug_fill_kernel(const UnitPlugParams p) {
     const uint32_t n = __shfl_sync(0xffffffffu, h, 7);
     uint8_t* seg = p.out + __ldg(p.off + u);
     const uint32_t len = __ldg(p.off + u + 1) - __ldg(p.off + u);
-    if (lane < 8) reinterpret_cast<uint16_t*>(seg)[lane] = (uint16_t)h;
+    if (lane < 8) reinterpret_cast<uint32_t*>(seg)[lane] = (h - cnt) | (h << 10) | (n << 20);
     for (int r = 0; r < 8; ++r) {
       const uint32_t ar = __shfl_sync(0xffffffffu, a, r);
       const uint32_t cr = __shfl_sync(0xffffffffu, cnt, r);
@@ -542,11 +545,11 @@ __global__ void unit_plug_fill_kernel(const UnitPlugParams p) {
       const uint32_t rowbase = p.base + (uint32_t)(8 * t + r) * (uint32_t)p.K + (uint32_t)(64 * kc);
       for (uint32_t j = lane; j < cr; j += 32) {
         const uint32_t e = e0 + j;
-        reinterpret_cast<uint2*>(seg + 16)[e] = __ldg(p.plug_vals + ar + j);
-        seg[16 + 8 * n + e] = (uint8_t)(__ldg(p.plug_idx + ar + j) - rowbase);
+        reinterpret_cast<uint2*>(seg + 32)[e] = __ldg(p.plug_vals + ar + j);
+        seg[32 + 8 * n + e] = (uint8_t)(__ldg(p.plug_idx + ar + j) - rowbase);
       }
     }
-    for (uint32_t b = 16 + 9 * n + lane; b < len; b += 32) seg[b] = 0;
+    for (uint32_t b = 32 + 9 * n + lane; b < len; b += 32) seg[b] = 0;
   }
 }
 
@@ -560,8 +563,8 @@ int pp_quad_unit_plugs_bytes(int64_t N, int64_t K, int64_t n_plugs, size_t* stre
     return PP_ERR_INVALID;
   }
   const int64_t U = pp::cdiv(N, 8) * pp::cdiv(K, 64);
-  // a segment takes at most 16 + 9n + 15 bytes
-  *stream_bytes = pp::align_up((size_t)U * 31u + (size_t)n_plugs * 9u, 256);
+  // a segment takes at most 32 + 9n + 15 bytes
+  *stream_bytes = pp::align_up((size_t)U * 47u + (size_t)n_plugs * 9u, 256);
   *n_offsets = U + 1;
   return PP_OK;
 }

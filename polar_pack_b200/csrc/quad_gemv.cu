@@ -101,6 +101,11 @@ struct QuadBuf {
   uint4 q[4];
 };
 
+// Plug slot of the fused plug correction (one more per warp than ring
+// slots): a segment of up to (512 - 32) / 9 = 53 entries is staged; larger
+// ones are read from HBM by the lanes.
+constexpr uint32_t kPlugCap = 512u;
+
 // NK: file layout.  DIRECT: tables at a 64 KiB-aligned shared address (see
 // decode_quad).  PLUG: fused plug correction (NK, NB == 1, batch 1).
 template <bool NK, int NB, bool DIRECT, bool PLUG = false>
@@ -125,13 +130,10 @@ struct QuadOp {
   const __half* x;
   const __half* xrow[NB];  // this lane's activation row per batch tile (clamped); NK: + 4c
   float acc[kT][NB][2][4];
-  // PLUG: this warp's plug slots and unit-offset table (shared addresses),
-  // its first unit, and the lane's plug sums per model
-  uint32_t pring = 0u, ptab = 0u;
-  int pwu0 = 0;
-  float pacc[4] = {0.f, 0.f, 0.f, 0.f};
-  // PLUG: the lane's first two entries of the current unit (values and raw
-  // FP16 activations), loaded by side() and applied after the decode
+  // PLUG: this warp's plug slots (shared address); the lane's first two
+  // entries of the current unit (values and raw FP16 activations), loaded
+  // by side() and applied after the decode
+  uint32_t pring = 0u;
   uint2 pv0, pv1;
   uint32_t px;
 
@@ -176,11 +178,7 @@ struct QuadOp {
   __device__ __forceinline__ void begin(int, int) {}
   __device__ __forceinline__ void preload(int, int) {}
 
-  __device__ __forceinline__ void plug_init(uint32_t ring, uint32_t tab, int wu0) {
-    pring = ring;
-    ptab = tab;
-    pwu0 = wu0;
-  }
+  __device__ __forceinline__ void plug_init(uint32_t ring) { pring = ring; }
 
   // One unit by TMA into a 2 KiB ring slot (one lane).  NK: 8
   // rows x 64 codes as two 8 x 32 boxes (128-byte rows, 128-byte swizzle);
@@ -230,25 +228,28 @@ struct QuadOp {
   }
 
   // PLUG: plug entries of unit u (column chunk kc) from plug slot sp.  The
-  // segment is a 16-byte header of eight u16 cumulative entry counts (rows
-  // 0..r of the tile), n FP16x4 values, then n column bytes (k - 64 kc);
-  // staged whole when 16 + 9n <= pcap, else read from HBM.  Lane (g, c)
-  // takes the entries of tile row pr whose index within the row is
-  // c mod 4.  Its first two are loaded here with their activations and
-  // applied after the unit's decode (plug_finish), which hides the load
-  // latency; further ones (rows of more than 8 entries) are applied now.
+  // segment starts with eight u32 header words, one per tile row r:
+  // start_r | end_r << 10 | n << 20; then n FP16x4 values and n column
+  // bytes (k - 64 kc).  It is staged whole when 32 + 9n <= kPlugCap, else
+  // read from HBM.  Lane (g, c) takes the entries of tile row pr whose index
+  // within the row is c mod 4.  Its first two are loaded here with their
+  // activations and applied after the unit's decode (plug_finish), which
+  // hides the load latency; further ones (rows of more than 8 entries) are
+  // applied now.  The terms go to the lane's accumulators of batch column
+  // 2c, which hold zeros for c > 0 (the PLUG kernel runs batch 1 and feeds
+  // zero activations to the other columns); end_chunk sums the row's four
+  // lanes.
   __device__ __forceinline__ void side(int sp, int u, int kc) {
     if constexpr (PLUG) {
-      const uint32_t ps = pring + (uint32_t)sp * p.pcap;
-      const uint32_t n = lds_u16(ps + 14u);
-      const uint32_t hi = lds_u16(ps + 2u * (uint32_t)pr);
-      const uint32_t lo = pr ? lds_u16(ps + 2u * (uint32_t)pr - 2u) : 0u;
+      const uint32_t ps = pring + (uint32_t)sp * kPlugCap;
+      const uint32_t h = lds_u32(ps + 4u * (uint32_t)pr);
+      const uint32_t lo = h & 1023u, hi = (h >> 10) & 1023u, n = h >> 20;
       const __half* xk = x + kc * 64;
       const uint32_t e0 = lo + (uint32_t)c, e1 = e0 + 4u;
       pv0 = pv1 = make_uint2(0u, 0u);
       px = 0u;
-      if (16u + 9u * n <= p.pcap) {
-        const uint32_t vb = ps + 16u, kb = ps + 16u + 8u * n;
+      if (32u + 9u * n <= kPlugCap) {
+        const uint32_t vb = ps + 32u, kb = ps + 32u + 8u * n;
         if (e0 < hi) {
           pv0 = lds_u2(vb + 8u * e0);
           px = ld_u16(xk + lds_u8(kb + e0));
@@ -259,9 +260,9 @@ struct QuadOp {
         }
         for (uint32_t e = e1 + 4u; e < hi; e += 4u) plug_fma(lds_u2(vb + 8u * e), ld_u16(xk + lds_u8(kb + e)));
       } else {
-        const uint8_t* gs = p.uplugs + lds_u32(ptab + 4u * (uint32_t)(u - pwu0));
+        const uint8_t* gs = p.uplugs + __ldg(p.uplug_off + u);
         for (uint32_t e = e0; e < hi; e += 4u)
-          plug_fma(__ldg(reinterpret_cast<const uint2*>(gs + 16u + 8u * e)), ld_u16(xk + __ldg(gs + 16u + 8u * n + e)));
+          plug_fma(__ldg(reinterpret_cast<const uint2*>(gs + 32u + 8u * e)), ld_u16(xk + __ldg(gs + 32u + 8u * n + e)));
       }
     }
   }
@@ -273,30 +274,33 @@ struct QuadOp {
     }
   }
 
-  // pacc[q] += value q * x with the FP16 operands taken as they are (their
-  // product is exact in FP32) and one FP32 rounding, as cvt + fmaf would.
+  // acc(model q, batch column 2c) += value q * x with the FP16 operands
+  // taken as they are (their product is exact in FP32) and one FP32
+  // rounding, as cvt + fmaf would.
   __device__ __forceinline__ void plug_fma(uint2 v, uint32_t xbits) {
     asm("{\n .reg .f16 v0, v1, v2, v3, xh;\n"
         " mov.b32 {v0, v1}, %4;\n mov.b32 {v2, v3}, %5;\n mov.b32 {xh, _}, %6;\n"
         " fma.rn.f32.f16 %0, v0, xh, %0;\n fma.rn.f32.f16 %1, v1, xh, %1;\n"
         " fma.rn.f32.f16 %2, v2, xh, %2;\n fma.rn.f32.f16 %3, v3, xh, %3;\n}"
-        : "+f"(pacc[0]), "+f"(pacc[1]), "+f"(pacc[2]), "+f"(pacc[3])
+        : "+f"(acc[0][0][0][0]), "+f"(acc[0][0][0][2]), "+f"(acc[0][0][1][0]), "+f"(acc[0][0][1][2])
         : "r"(v.x), "r"(v.y), "r"(xbits));
   }
 
-  // PLUG: the four lanes of each row sum their plug sums (fixed butterfly)
-  // and lane c = 0, which holds batch row 0, adds them to model q's
-  // accumulator (fragment register 2 (q & 1) of half q >> 1).
+  // PLUG: the four lanes of each row sum their batch column 2c (a fixed
+  // butterfly): lane c = 0 then holds the product plus every plug term of
+  // the row in batch column 0 (fragment register 2 (q & 1) of half q >> 1
+  // for model q).
   __device__ __forceinline__ void end_chunk() {
     if constexpr (PLUG) {
 #pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        float v = pacc[q];
-        v += __shfl_xor_sync(0xffffffffu, v, 1);
-        v += __shfl_xor_sync(0xffffffffu, v, 2);
-        if (c == 0) acc[0][0][q >> 1][(q & 1) << 1] += v;
-        pacc[q] = 0.f;
-      }
+      for (int h = 0; h < 2; ++h)
+#pragma unroll
+        for (int j = 0; j < 4; j += 2) {
+          float v = acc[0][0][h][j];
+          v += __shfl_xor_sync(0xffffffffu, v, 1);
+          v += __shfl_xor_sync(0xffffffffu, v, 2);
+          acc[0][0][h][j] = v;
+        }
     }
   }
 
@@ -314,7 +318,10 @@ struct QuadOp {
 #pragma unroll
       for (int s = 0; s < 4; ++s)
 #pragma unroll
-        for (int nb = 0; nb < NB; ++nb) xb[s][nb] = xquad<FULL>(nb, kbase, s);
+        for (int nb = 0; nb < NB; ++nb)
+          // PLUG (batch 1): only lanes g = 0 feed activations; the other
+          // batch columns stay zero for side()'s plug terms
+          xb[s][nb] = (PLUG && g != 0) ? make_uint2(0u, 0u) : xquad<FULL>(nb, kbase, s);
 #pragma unroll
       for (int s = 0; s < 4; ++s) {
         const int kp = kbase + 16 * s + 4 * c;
@@ -417,7 +424,7 @@ __device__ __forceinline__ uint32_t plug_bytes(const QuadParams& p, uint32_t pta
   const uint32_t o0 = lds_u32(ptab + 4u * (uint32_t)(u - wu0));
   const uint32_t len = lds_u32(ptab + 4u * (uint32_t)(u - wu0 + 1)) - o0;
   *off = o0;
-  return len < p.pcap ? len : p.pcap;
+  return len < kPlugCap ? len : kPlugCap;
 }
 
 template <bool NK, int NB, bool DIRECT, bool PLUG>
@@ -429,15 +436,15 @@ __device__ __forceinline__ void quad_body(const QuadParams& p, const Partition& 
   const int warp = threadIdx.x >> 5;
   Op op(p, L.lut);
   if constexpr (PLUG) {
-    const uint32_t pring = L.plug + (uint32_t)(warp * (p.stages + 1)) * p.pcap;
+    const uint32_t pring = L.plug + (uint32_t)(warp * (p.stages + 1)) * kPlugCap;
     const uint32_t ptab = L.ptab + (uint32_t)warp * (kPlugTabEntries * 4u);
-    op.plug_init(pring, ptab, wu0);
+    op.plug_init(pring);
     const int upt = pt.upt;
     tma_stream(op, [&](uint32_t slot, uint32_t bar, int s, int tile, int kc) {
       uint32_t off;
       const uint32_t pb = plug_bytes(p, ptab, wu0, tile * upt + kc, &off);
       Op::template issue<true>(p, slot, bar, tile, kc, pb);
-      bulk_load(pring + (uint32_t)s * p.pcap, p.uplugs + off, pb, bar);  // s: side slot
+      bulk_load(pring + (uint32_t)s * kPlugCap, p.uplugs + off, pb, bar);  // s: side slot
     }, rg, pt, tb, red, warp, wu0, wu1, cu0, cu1, status);
   } else {
     tma_stream(op, [&](uint32_t slot, uint32_t bar, int, int tile, int kc) { Op::issue(p, slot, bar, tile, kc); },
@@ -532,7 +539,7 @@ __global__ void __launch_bounds__(quad_warps(NK, NB) * 32, 1) quad_gemv_kernel(c
       if (lane + 32 <= nu) sts_u32(ptab + 4u * (uint32_t)(lane + 32), po1);
       __syncwarp();
       if (lane == 0) {  // the plug copies of the prologue units, in the same order
-        const uint32_t pring = L.plug + (uint32_t)(warp * (p.stages + 1)) * p.pcap;
+        const uint32_t pring = L.plug + (uint32_t)(warp * (p.stages + 1)) * kPlugCap;
         UnitSeq q;
         q.init(wu0, wu1, p.part.upt);
         for (int i = 0; i < p.stages && q.seg < 3; ++i) {
@@ -540,7 +547,7 @@ __global__ void __launch_bounds__(quad_warps(NK, NB) * 32, 1) quad_gemv_kernel(c
           const uint32_t pb = plug_bytes(p, ptab, wu0, q.t * p.part.upt + q.kc, &off);
           const uint32_t bar = rg.bars + 8u * (uint32_t)i;
           mbar_expect_tx(bar, pb);
-          bulk_load(pring + (uint32_t)i * p.pcap, p.uplugs + off, pb, bar);
+          bulk_load(pring + (uint32_t)i * kPlugCap, p.uplugs + off, pb, bar);
           q.advance();
         }
       }
@@ -636,10 +643,7 @@ PartitionPlan quad_plan(bool nk, int64_t Mc, int64_t N, int64_t K, int sms, int*
 bool g_attr_done[8][64];
 int g_attr_limit[8][64];
 
-// Plug slot beside every ring slot of the fused plug correction: a segment
-// of up to (512 - 16) / 9 = 55 entries is staged; larger ones are read from
-// HBM by the lanes.
-constexpr uint32_t kPlugCap = 512u;
+
 
 // Deepest ring (up to 4 slots per consumer) with the tables at a 64 KiB
 // boundary for a dynamic region at the reserved-memory offset, else the

@@ -77,14 +77,25 @@ class RowShardedGroup:
     """Several independent row-sharded Linears with ONE all-gather.
 
     For Linears that do not feed each other (q/k/v, gate/up, or the
-    benchmark's sweep), every rank computes its row shard of each, packs the
-    ``n_out`` outputs of all of them into one buffer, and a single collective
-    gathers everything; ``__call__(xs)`` returns, per Linear, ``n_out`` full
-    ``(M, N_j)`` tensors.  One collective instead of one per Linear.
+    benchmark's sweep), every rank computes its row shard of each into one
+    send buffer of ``n_out`` blocks ``(M, sum of shard widths)`` and a single
+    collective gathers everything.  ``__call__(xs)`` returns, per Linear,
+    ``n_out`` full ``(M, N_j)`` tensors; one collective instead of one per
+    Linear.
+
+    ``writes_out=True`` means ``local_fns[j](x, out)`` writes its outputs
+    into ``out`` (``n_out`` strided ``(M, rows of this rank)`` views of the
+    send buffer, as ``quad_linear(x, layer, out=...)`` accepts); otherwise
+    ``local_fns[j](x)`` returns them and they are copied in.  The send and
+    receive buffers are kept per batch size and reused: on one GPU the
+    returned tensors are views of the send buffer, and ``raw()`` is the last
+    call's buffer (``(n_out, M, total)`` on one GPU, ``(world * n_out, M,
+    total)`` gathered, rank-major) for callers that read the result once,
+    e.g. a single device-to-host copy.
     """
 
-    def __init__(self, local_fns: Sequence[Callable[[torch.Tensor], Sequence[torch.Tensor]]],
-                 Ns: Sequence[int], group=None, n_out: int = 4):
+    def __init__(self, local_fns: Sequence[Callable], Ns: Sequence[int], group=None, n_out: int = 4,
+                 writes_out: bool = False):
         if len(local_fns) != len(Ns):
             raise ValueError("one local function per Linear")
         self.local_fns = list(local_fns)
@@ -94,33 +105,55 @@ class RowShardedGroup:
         self.rank = dist.get_rank(group) if dist.is_initialized() else 0
         self.widths = [shard_width(N, self.world) for N in self.Ns]
         self.n_out = n_out
+        self.writes_out = writes_out
+        self._bufs: dict = {}
+        self._last = None
 
-    def __call__(self, xs: Sequence[torch.Tensor]) -> list[list[torch.Tensor]]:
+    def _buffers(self, M, dev, dt):
+        key = (M, dev, dt)
+        b = self._bufs.get(key)
+        if b is None:
+            total = sum(self.widths)
+            # zero-filled once: the padding columns of short shards stay zero
+            send = torch.zeros((self.n_out, M, total), dtype=dt, device=dev)
+            recv = torch.empty((self.world * self.n_out, M, total), dtype=dt, device=dev) \
+                if self.world > 1 else None
+            outs, col = [], 0
+            for N, w in zip(self.Ns, self.widths):
+                a, b_ = row_shard(N, self.world, self.rank)
+                outs.append([send[k, :, col:col + b_ - a] for k in range(self.n_out)])
+                col += w
+            b = self._bufs[key] = (send, recv, outs)
+        return b
+
+    def raw(self) -> torch.Tensor:
+        return self._last
+
+    def __call__(self, xs: Sequence[torch.Tensor], dtype=torch.float16) -> list[list[torch.Tensor]]:
         M = xs[0].shape[0]
-        locals_ = [fn(x) for fn, x in zip(self.local_fns, xs)]
+        send, recv, outs = self._buffers(M, xs[0].device, dtype)
+        for fn, x, out in zip(self.local_fns, xs, outs):
+            if self.writes_out:
+                fn(x, out)
+            else:
+                for dst, src in zip(out, fn(x)):
+                    dst.copy_(src)
         if self.world == 1:
-            return [list(l) for l in locals_]
-        total = sum(self.widths)
-        dev, dt = locals_[0][0].device, locals_[0][0].dtype
-        send = torch.zeros((self.n_out, M, total), dtype=dt, device=dev)
-        col = 0
-        for loc, w in zip(locals_, self.widths):
-            for k in range(self.n_out):
-                send[k, :, col:col + loc[k].shape[1]] = loc[k]
-            col += w
-        recv = torch.empty((self.world * self.n_out, M, total), dtype=dt, device=dev)
+            self._last = send
+            return [list(o) for o in outs]
         dist.all_gather_into_tensor(recv, send, group=self.group)
-        recv = recv.view(self.world, self.n_out, M, total)
+        self._last = recv
+        rv = recv.view(self.world, self.n_out, M, -1)
         res, col = [], 0
         for N, w in zip(self.Ns, self.widths):
-            outs = []
+            outs_j = []
             for k in range(self.n_out):
                 parts = []
                 for r in range(self.world):
                     a, b = row_shard(N, self.world, r)
-                    parts.append(recv[r, k, :, col:col + b - a])
-                outs.append(torch.cat(parts, dim=1))
-            res.append(outs)
+                    parts.append(rv[r, k, :, col:col + b - a])
+                outs_j.append(torch.cat(parts, dim=1))
+            res.append(outs_j)
             col += w
         return res
 

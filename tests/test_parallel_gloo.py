@@ -76,7 +76,7 @@ def test_row_sharded_gather_matches_full(N):
     assert all(shapes == [(M, N)] * 4 for _, _, shapes in res)
 
 
-def _worker_group(rank, world, port, Ns, K, M, q):
+def _worker_group(rank, world, port, Ns, K, M, q, writes_out=False):
     try:
         sys.path.insert(0, str(ROOT))
         from polar_pack_b200.parallel import RowShardedGroup, row_shard
@@ -87,11 +87,19 @@ def _worker_group(rank, world, port, Ns, K, M, q):
 
         def make(ws, N):
             n0, n1 = row_shard(N, world, rank)
-            return lambda xt: [torch.from_numpy((xt.numpy().astype(np.float64) @ w[n0:n1].T.astype(np.float64))
-                                                .astype(np.float16)) for w in ws]
+            fn = lambda xt: [torch.from_numpy((xt.numpy().astype(np.float64) @ w[n0:n1].T.astype(np.float64))
+                                              .astype(np.float16)) for w in ws]
+            if not writes_out:
+                return fn
 
-        grp = RowShardedGroup([make(ws, N) for ws, N in zip(wss, Ns)], Ns)
+            def into(xt, out):  # writes into the group's send-buffer views
+                for dst, src in zip(out, fn(xt)):
+                    dst.copy_(src)
+            return into
+
+        grp = RowShardedGroup([make(ws, N) for ws, N in zip(wss, Ns)], Ns, writes_out=writes_out)
         outs = grp([torch.from_numpy(x) for x in xs])
+        outs = grp([torch.from_numpy(x) for x in xs])  # buffers are reused: a second call gives the same
         ok = True
         for o, ws, x in zip(outs, wss, xs):
             full = [(x.astype(np.float64) @ w.T.astype(np.float64)).astype(np.float16) for w in ws]
@@ -102,14 +110,17 @@ def _worker_group(rank, world, port, Ns, K, M, q):
         q.put((rank, False, repr(e)))
 
 
-def test_grouped_gather_matches_full():
+@pytest.mark.parametrize("writes_out", [False, True])
+def test_grouped_gather_matches_full(writes_out):
     """Several Linears of different widths (one not divisible by the world
-    size) gathered by one collective."""
+    size) gathered by one collective, with local functions that return
+    their outputs or write them into the send buffer."""
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     world, K, M, Ns = 2, 20, 2, [16, 13, 6]
     port = free_port()
-    procs = [ctx.Process(target=_worker_group, args=(r, world, port, Ns, K, M, q)) for r in range(world)]
+    procs = [ctx.Process(target=_worker_group, args=(r, world, port, Ns, K, M, q, writes_out))
+             for r in range(world)]
     for p in procs:
         p.start()
     res = [q.get(timeout=120) for _ in procs]
@@ -167,3 +178,19 @@ def test_missing_rank_fails_on_host_not_hang():
         p.join(timeout=60)
     assert res[1] == "left"
     assert res[0].startswith("error")
+
+
+def test_grouped_single_rank_views():
+    """One rank: the outputs are views of the reused send buffer."""
+    from polar_pack_b200.parallel import RowShardedGroup
+    Ns, M = [5, 3], 2
+
+    def fn(v):
+        return lambda x, out: [o.fill_(v + k) for k, o in enumerate(out)]
+    grp = RowShardedGroup([fn(10), fn(20)], Ns, writes_out=True)
+    outs = grp([torch.zeros(M, 4), torch.zeros(M, 4)])
+    raw = grp.raw()
+    assert raw.shape == (4, M, sum(Ns))
+    assert [tuple(o.shape) for o in outs[0]] == [(M, 5)] * 4 and [tuple(o.shape) for o in outs[1]] == [(M, 3)] * 4
+    assert float(raw[2, 0, 0]) == 12 and float(raw[3, 1, 6]) == 23
+    assert outs[1][0].data_ptr() == raw[0, :, 5:].data_ptr()

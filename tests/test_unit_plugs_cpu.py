@@ -58,5 +58,5 @@ def test_size_bound_covers_worst_case(N, K, P):
     T, W, U = upr.shape_units(N, K)
     assert noff.value == U + 1
     # worst case: every unit's count leaves 15 bytes of padding
-    worst = U * 16 + 9 * P + 15 * U
+    worst = U * 32 + 9 * P + 15 * U
     assert nbytes.value >= worst and nbytes.value % 256 == 0

@@ -41,20 +41,21 @@ def build(loc: np.ndarray, vals: np.ndarray, N: int, K: int) -> tuple[np.ndarray
     row, col = loc // K, loc % K
     unit = (row // 8) * W + col // 64
     counts = np.bincount(unit, minlength=U).astype(np.int64)
-    seg = (16 + 9 * counts + 15) // 16 * 16
+    seg = (32 + 9 * counts + 15) // 16 * 16
     off = np.zeros(U + 1, dtype=np.int64)
     off[1:] = np.cumsum(seg)
     out = np.zeros(int(off[-1]), dtype=np.uint8)
     rows = np.bincount(unit * 8 + row % 8, minlength=U * 8).reshape(U, 8)
-    hdr = rows.cumsum(axis=1).astype("<u2")
-    out[off[:U, None] + np.arange(16)] = hdr.view(np.uint8).reshape(U, 16)
+    end = rows.cumsum(axis=1)
+    hdr = ((end - rows) | (end << 10) | (counts[:, None] << 20)).astype("<u4")
+    out[off[:U, None] + np.arange(32)] = hdr.view(np.uint8).reshape(U, 32)
     order = np.argsort(unit, kind="stable")  # positions ascend, so rows then columns ascend in a unit
     us = unit[order]
     first = np.zeros(U + 1, dtype=np.int64)
     first[1:] = np.cumsum(counts)
     e = np.arange(loc.size) - first[us]
-    out[(off[us] + 16 + 8 * e)[:, None] + np.arange(8)] = vals[order].view(np.uint8).reshape(-1, 8)
-    out[off[us] + 16 + 8 * counts[us] + e] = (col[order] % 64).astype(np.uint8)
+    out[(off[us] + 32 + 8 * e)[:, None] + np.arange(8)] = vals[order].view(np.uint8).reshape(-1, 8)
+    out[off[us] + 32 + 8 * counts[us] + e] = (col[order] % 64).astype(np.uint8)
     return out, off.astype(np.uint32)
 
 
@@ -66,18 +67,22 @@ def parse(stream: np.ndarray, off: np.ndarray, N: int, K: int):
     for u in range(U):
         o = int(off[u])
         t, kc = divmod(u, W)
-        h = stream[o:o + 16].view("<u2").astype(np.int64)
-        n = int(h[7])
-        assert int(off[u + 1]) - o == (16 + 9 * n + 15) // 16 * 16
-        v = stream[o + 16:o + 16 + 8 * n].view(np.float16).reshape(n, 4)
-        k = stream[o + 16 + 8 * n:o + 16 + 9 * n].astype(np.int64)
-        assert not stream[o + 16 + 9 * n:int(off[u + 1])].any()
+        h = stream[o:o + 32].view("<u4").astype(np.int64)
+        n = int(h[0] >> 20)
+        assert (h >> 20 == n).all()
+        assert int(off[u + 1]) - o == (32 + 9 * n + 15) // 16 * 16
+        v = stream[o + 32:o + 32 + 8 * n].view(np.float16).reshape(n, 4)
+        k = stream[o + 32 + 8 * n:o + 32 + 9 * n].astype(np.int64)
+        assert not stream[o + 32 + 9 * n:int(off[u + 1])].any()
         start = 0
         for r in range(8):
-            for e in range(start, int(h[r])):
+            lo, hi = int(h[r] & 1023), int((h[r] >> 10) & 1023)
+            assert lo == start and hi >= lo
+            for e in range(lo, hi):
                 locs.append((8 * t + r) * K + 64 * kc + int(k[e]))
                 vals.append(v[e])
-            start = int(h[r])
+            start = hi
+        assert start == n
     return np.array(locs, dtype=np.int64), np.array(vals, dtype=np.float16).reshape(-1, 4)
 
 
