@@ -10,11 +10,16 @@ Workload: the quad-pack single-layer sweep -- four correlated synthetic models
 (4 outputs per pass over the codes).
 R = 4 replica streams rotate step to step, so each step reads ~200 MB of
 codes that were last touched 3 steps (~600 MB) earlier: inputs exceed the
-126 MB L2 and no flush is needed.  A Linear is two kernels: the CSR
-plug-table correction and the fused GEMV, which adds it before the scale.
-Kernels run with launch overlap (programmatic dependent launch: each may
-start its weight-only prologue while the previous one finishes), unless
-``--no-overlap``.
+126 MB L2 and no flush is needed.  A Linear is one kernel launch: the
+fused GEMV with the plug-table correction inside (batch 1; larger batches
+add the CSR correction kernel).  Kernels run with launch overlap
+(programmatic dependent launch: each may start its weight-only prologue
+while the previous one finishes), unless ``--no-overlap``.
+
+A second leg times the packed Linears of a 3B-class decode step (BASELINE
+36 layers of qkv / o / gate_up / down launches plus the lm_head,
+batch 1) and reports 4-model decode tokens/s under
+``config.decode_step_3b`` (``--no-decode`` skips it).
 
 Metric: packed-stream GB/s = algorithmic bytes / device time, where the
 bytes of one Linear are 4*N*K (codes) + 12*P (plug index + values) +
@@ -24,8 +29,9 @@ a time over the same bytes.
 
 With N > 1 GPUs (launched by torch.distributed.run) each Linear is
 row-sharded (column-parallel): rank r owns output rows [r*N/P, (r+1)*N/P),
-which are a contiguous slice of the file-layout stream, and the four FP16
-outputs are all-gathered over NCCL after every Linear.  Total work is fixed
+which are a contiguous slice of the file-layout stream; the sweep's four
+Linears are independent, so one NCCL all-gather per step collects their
+outputs (the decode leg gathers after every launch, as a layer needs).  Total work is fixed
 (strong scaling); time is the max over ranks of CUDA-event time.
 
 ``--impl reference`` times the reference's own CPU path (the oracle's
@@ -125,6 +131,22 @@ class ClockSampler:
                     reasons.add(name)
         return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx,
                 "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# 3B-class dense decoder of BASELINE configs[2] (hidden 2048, intermediate
+# 11008, 16 q / 2 kv heads of 128, vocab 151936, 36 layers)
+DECODE_3B = {"layers": 36, "hidden": 2048, "inter": 11008, "q_heads": 16, "kv_heads": 2, "head_dim": 128,
+             "vocab": 151936}
+
+
+def decode_groups(cfg):
+    """Launch groups of one decoder layer as (name, out N, in K), in stream
+    order.  q/k/v and gate/up are consecutive Linears with one input, so in
+    the `.quadpack` stream (each Linear (out, in) row-major, layer-map order)
+    each group is one contiguous (sum of outs, in) matrix: one launch."""
+    h, i = cfg["hidden"], cfg["inter"]
+    q, kv = cfg["q_heads"] * cfg["head_dim"], cfg["kv_heads"] * cfg["head_dim"]
+    return [("qkv", q + 2 * kv, h), ("o", h, q), ("gate_up", 2 * i, h), ("down", h, i)]
 
 
 # ------------------------------------------------------------ workload ----
@@ -348,6 +370,11 @@ def run_ours(args):
     # e2e through the public API with host buffers (pinned), 1 GPU view of rank's work
     e2e = run_e2e(torch, dist, sets, xs, dev, args, world, M, full_sets)
 
+    # the second half of the metric: 4-model decode tokens/s of a 3B-class step
+    decode = None
+    if not args.no_decode and not args.shapes and M == 1:
+        decode = run_decode_step(torch, dist, dev, args, world, rank, lib, stream)
+
     peak, peak_kind = measured_peak()
     achieved = kernel_bytes / (kernel_ms * 1e-3) / 1e9
     traffic = load_traffic()
@@ -364,7 +391,8 @@ def run_ours(args):
                                   else "single GPU",
                    "timing": ("CUDA graph replay of whole steps" if use_graphs else "eager launches") +
                              ("; launch overlap on" if not args.no_overlap else ""),
-                   "per_shape_gemv_kernel": per_shape},
+                   "per_shape_gemv_kernel": per_shape,
+                   "decode_step_3b": decode},
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(achieved / peak, 4), "peak_source": f"{peak_kind} hbm_gbs",
                      "kernel": "quad_gemv_kernel<NK=1,NB=1,PLUG=1> (file layout, batch 1, plugs fused)",
@@ -388,6 +416,143 @@ def run_ours(args):
         dist.destroy_process_group()
     if rank == 0:
         print(json.dumps(res))
+
+
+def run_decode_step(torch, dist, dev, args, world, rank, lib, stream):
+    """The packed Linears of one 3B-class decode step at batch 1: 36 layers of
+    four launches (qkv, o, gate_up, down) plus the lm_head, each launch one
+    fused GEMV with its plug correction.  Two distinct layer weight sets
+    (616 MB of codes, more than L2) alternate over the 36 layers, so every
+    launch streams codes L2 does not hold; the lm_head (1.24 GB) is its own.
+    Inputs are fixed random vectors: the attention, norms and activation
+    functions between the Linears are outside this path and not run.  With
+    N > 1 GPUs each launch computes the rank's row shard and one all-gather
+    per launch collects the outputs, as the layer's next step needs them.
+    Returns the leg's summary for the JSON line."""
+    import ctypes as C
+    from polar_pack_b200 import _lib
+    from polar_pack_b200.parallel import row_shard, shard_width
+    from polar_pack_b200.quadpack import DevicePackedStream, pack_quad_device, quad_linear_workspace_bytes
+    cfg, M = DECODE_3B, 1
+    groups = decode_groups(cfg)
+    per_layer = sum(N * K for _, N, K in groups)
+    distinct = 2
+    head_nk = (cfg["vocab"], cfg["hidden"])
+    n = distinct * per_layer + head_nk[0] * head_nk[1]
+    models = synth_models(torch, n, 3000, dev)
+    p = pack_quad_device(models, plug_cap=0.05, seed=42, windows=16, window=1_000_000)
+    del models
+    torch.cuda.empty_cache()
+    st = DevicePackedStream(p)
+    del p
+    st.check_plug_index()
+    g = torch.Generator(device=dev)
+    g.manual_seed(11)
+    xin = {K: torch.randn(M, K, generator=g, device=dev).half() for K in {K for _, _, K in groups}}
+
+    def shard(off, N, K):
+        n0, n1 = row_shard(N, world, rank)
+        return st.linear(off + n0 * K, n1 - n0, K)
+
+    units, off = [], 0   # per distinct layer: its groups; then the head
+    for _ in range(distinct):
+        row = []
+        for name, N, K in groups:
+            row.append((N, K, shard(off, N, K)))
+            off += N * K
+        units.append(row)
+    head = (head_nk[0], head_nk[1], shard(off, *head_nk))
+    lins = [u for row in units for u in row] + [head]
+    ws_bytes = max(quad_linear_workspace_bytes(M, l.N, l.K) for _, _, l in lins)
+    ws = torch.zeros(max(ws_bytes, 256), dtype=torch.uint8, device=dev)
+    sh = stream.cuda_stream
+
+    def prep(N, K, l):
+        w = shard_width(N, world)
+        send = torch.zeros((4, M, w), dtype=torch.float16, device=dev)
+        recv = torch.empty((world * 4, M, w), dtype=torch.float16, device=dev) if world > 1 else None
+        outs = [send[k, :, :l.N] for k in range(4)]
+        x = xin[K]
+        a = (x.data_ptr(), x.stride(0), x.stride(1), l.codes.data_ptr(), l.K, _lib.ptr(l.plug_idx),
+             _lib.ptr(l.plug_vals), _lib.ptr(l.plug_window_base), C.c_uint32(l.offset & 0xFFFFFFFF),
+             _lib.ptr(l.unit_plugs), _lib.ptr(l.unit_plug_off), l.pack.tables.data_ptr(), _lib.floats4(l.pack.scales),
+             _lib.ptrs(outs, 4), outs[0].stride(0), outs[0].stride(1), M, l.N, l.K, ws.data_ptr(), ws.numel(), sh)
+        return a, send, recv, outs
+
+    calls = [[prep(N, K, l) for N, K, l in row] for row in units]
+    head_call = prep(*head)
+
+    def launch(c):
+        rc = lib.pp_quad_linear_fused(*c[0])
+        if rc:
+            _lib.check(rc)
+        if world > 1:
+            dist.all_gather_into_tensor(c[2], c[1])
+
+    def step():
+        for layer in range(cfg["layers"]):
+            for c in calls[layer % distinct]:
+                launch(c)
+        launch(head_call)
+
+    for _ in range(2):
+        step()
+    torch.cuda.synchronize(dev)
+    graph = None
+    if not args.eager:
+        try:
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph, stream=stream):
+                step()
+            graph.replay()
+            torch.cuda.synchronize(dev)
+        except Exception as e:  # capture unsupported: time eager launches
+            print(f"decode graph capture failed, timing eager launches: {e}", file=sys.stderr)
+            graph = None
+    run = graph.replay if graph is not None else step
+    for _ in range(args.warmup):
+        run()
+    torch.cuda.synchronize(dev)
+    if world > 1:
+        dist.barrier()
+    steps = max(3, min(args.steps, 10))
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0.record(stream)
+    for _ in range(steps):
+        run()
+    t1.record(stream)
+    torch.cuda.synchronize(dev)
+    ms = t0.elapsed_time(t1) / steps
+    if world > 1:
+        t = torch.tensor([ms], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    del graph
+    # whole-job algorithmic bytes of one step: the full Linears (all ranks' shards)
+    full_p = []
+    off = 0
+    for _ in range(distinct):
+        row = []
+        for name, N, K in groups:
+            lo, hi = st._plug_range(off, off + N * K)
+            row.append(layer_bytes(N, K, hi - lo, M))
+            off += N * K
+        full_p.append(row)
+    lo, hi = st._plug_range(off, off + head_nk[0] * head_nk[1])
+    step_bytes = sum(sum(full_p[l % distinct]) for l in range(cfg["layers"])) + \
+        layer_bytes(head_nk[0], head_nk[1], hi - lo, M)
+    launches = cfg["layers"] * len(groups) + 1
+    res = {"tok_s": round(4 * M / (ms * 1e-3), 1), "ms_per_step": round(ms, 3),
+           "GB/s": round(step_bytes / (ms * 1e-3) / 1e9, 1), "bytes_per_step": int(step_bytes),
+           "launches_per_step": launches, "all_gathers_per_step": launches if world > 1 else 0,
+           "what": "4-model tokens/s of the packed Linears of a 3B-class decode step at batch 1 "
+                   "(36 layers x [qkv 2560x2048, o 2048x2048, gate_up 22016x2048, down 2048x11008] + lm_head "
+                   "151936x2048; 2 distinct layer weight sets alternate); attention, norms and activations "
+                   "between them are outside the path and not run",
+           "timing": "CUDA graph of one whole step" if run is not step else "eager launches"}
+    del calls, head_call, units, head, lins, st
+    torch.cuda.empty_cache()
+    return res
 
 
 def run_e2e(torch, dist, sets, xs, dev, args, world, M, full_sets):
@@ -612,6 +777,7 @@ def main():
     ap.add_argument("--ref-fraction", type=float, default=1 / 32)
     ap.add_argument("--eager", action="store_true", help="time eager launches instead of CUDA graphs")
     ap.add_argument("--no-overlap", action="store_true", help="launch kernels without programmatic overlap")
+    ap.add_argument("--no-decode", action="store_true", help="skip the 3B decode-step leg")
     ap.add_argument("--shapes", default="", help="subset of the sweep as KxN,KxN (in x out), e.g. for profiling "
                                                  "one Linear; the line then names the subset")
     args = ap.parse_args()

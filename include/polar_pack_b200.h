@@ -210,10 +210,11 @@ PP_API int pp_quad_prepare_unit_plugs(const uint32_t* plug_idx, const void* plug
                                       uint32_t* unit_plug_off, void* stream);
 
 /* pp_quad_linear_prepared with the plug correction inside the GEMV when
- * the batch is one row (M == 1) and every warp's share of the work units
- * fits its offset table (at most 63 units, i.e. about 148 * 16 * 63 units
- * per launch); otherwise identical to pp_quad_linear_prepared, which is why
- * the CSR arguments are required as well.  unit_plugs / unit_plug_off: as
+ * the batch is one row (M == 1): one launch when every warp's share of the
+ * work units fits its offset table (at most 63 units, i.e. about
+ * 148 * 16 * 63 units per launch), else one launch per chunk of rows that
+ * fits.  Other batch sizes run as pp_quad_linear_prepared, which is why the
+ * CSR arguments are required as well.  unit_plugs / unit_plug_off: as
  * built by pp_quad_prepare_unit_plugs (both NULL for a Linear without
  * plugs).  Same result within the FP32
  * accumulation tolerance; the summation order of the plug terms differs.

@@ -758,6 +758,41 @@ inline size_t tc_corr_bytes(int64_t M, int64_t N) {
   return align_up((size_t)4 * Mc * N * sizeof(float), 256);
 }
 
+// Fused plug correction over row chunks of a batch-1 Linear too large for
+// one launch's offset tables: each chunk is a launch over rows [n0, n0 +
+// rows) whose warps hold at most 63 units.  Every chunk is planned first;
+// if one does not fit, nothing is launched and *done stays false.
+int launch_fused_chunks(const QuadParams& base, const uint32_t* codes, int64_t ldw, int64_t ldo_n, int64_t N,
+                        int64_t K, int sms, const uint8_t* uplugs, const uint32_t* uplug_off, void* ws, size_t csz,
+                        cudaStream_t s, bool* done) {
+  *done = false;
+  const int64_t W = cdiv(K, 64);
+  const int64_t cap = (int64_t)sms * quad_warps(true, 1) * ((int64_t)kPlugTabEntries - 1) * 9 / 10;
+  const int64_t rows = cap / W * 8;
+  if (rows <= 0) return PP_OK;
+  int starts[kMaxCtaTable + 1];
+  for (int64_t n0 = 0; n0 < N; n0 += rows) {
+    const int64_t Nc = N - n0 < rows ? N - n0 : rows;
+    if (!fused_plugs_ok(quad_plan(true, 1, Nc, K, sms, starts), starts, 1)) return PP_OK;
+  }
+  for (int64_t n0 = 0; n0 < N; n0 += rows) {
+    const int64_t Nc = N - n0 < rows ? N - n0 : rows;
+    QuadParams c = base;
+    c.N = (int)Nc;
+    c.codes = codes + n0 * ldw;
+    int rc = encode_tmap_u32_2d(&c.tmap, c.codes, (uint64_t)K, (uint64_t)Nc, (uint64_t)ldw * 4, 32, 8);
+    if (rc) return rc;
+    for (int i = 0; i < 4; ++i) c.out[i] = base.out[i] + n0 * ldo_n;
+    c.corr = nullptr;
+    c.uplugs = uplugs;
+    c.uplug_off = uplug_off + (n0 / 8) * W;
+    const PartitionPlan pl = quad_plan(true, 1, Nc, K, sms, c.cta_start);
+    if ((rc = launch_plan(pl, true, 1, c, ws, csz, s, true))) return rc;
+  }
+  *done = true;
+  return PP_OK;
+}
+
 size_t quad_ws_bytes(bool nk, int64_t M, int64_t N, int64_t K, bool plug) {
   const int sms = device_sm_count(current_device());
   const int64_t Mc = M < 16 ? M : 16;
@@ -919,6 +954,12 @@ static int quad_run(const void* a, int64_t lda_m, int64_t lda_k, const uint32_t*
       prm.uplug_off = uplug_off;
       if ((rc = launch_plan(pl, nk, Mc, prm, ws, csz, s, true))) return rc;
       continue;
+    }
+    if (uplugs && Mc == 1) {  // too long for one launch's offset tables: row chunks
+      bool done = false;
+      if ((rc = launch_fused_chunks(prm, codes, ldc_n, ldo_n, N, K, sms, uplugs, uplug_off, ws, csz, s, &done)))
+        return rc;
+      if (done) continue;
     }
     if (plug) {
       PlugCorrParams cp{prm.x, lda_m, plug_idx, reinterpret_cast<const uint2*>(plug_vals), wbase, base_lo32,
