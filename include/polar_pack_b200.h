@@ -277,6 +277,53 @@ PP_API int pp_dual_decode(const int16_t* packed, int64_t ldp_k, int64_t ldp_n, i
                    const void* amp_lut, const void* cos_lut, const void* sin_lut,
                    void* out1, void* out2, int64_t ldo_k, int64_t ldo_n, void* stream);
 
+/* ------------------------------------------------------- peer gather --
+ * Row-sharded Linears on the GPUs of one node without a separate
+ * all-gather (no counterpart in the reference, which runs one model per
+ * process on one GPU; replaces the NCCL all-gather of the outputs).  Each
+ * rank's GEMV stores its output rows straight into every rank's gather
+ * buffer over NVLink, then publishes a per-buffer epoch to every rank;
+ * pp_gather_wait makes a stream wait until every rank has published.
+ *
+ * Buffers are ordinary device allocations shared between the processes with
+ * CUDA IPC: pp_ipc_handle gives the 64-byte handle of the allocation that
+ * holds `ptr` and ptr's offset in it; a peer maps it with pp_ipc_open (add
+ * the offset) and unmaps with pp_ipc_close.
+ */
+#define PP_IPC_HANDLE_BYTES 64
+
+PP_API int pp_ipc_handle(const void* ptr, void* handle, size_t* offset);
+PP_API int pp_ipc_open(const void* handle, void** base);
+PP_API int pp_ipc_close(void* base);
+
+/* pp_quad_linear_fused at batch 1 (x is (1, K) with element stride ldx_k)
+ * whose four outputs are gathered: for every rank q < world, model k's
+ * output row n goes to element k * gather_ld + gather_row0 + n of
+ * gather_out[q] (FP16; rank q's buffer as mapped in this process).  After
+ * the launch's last store the kernel advances *gather_epoch (this rank's
+ * count of launches into the buffer, device memory, initially 0) and writes
+ * it to *gather_flag[q] (this rank's flag word in rank q's flag array) with
+ * release semantics at system scope.  Readers call pp_gather_wait first.
+ * The buffer must not be rewritten while a peer may still read it: with a
+ * wait after every use, alternating two buffers suffices.
+ */
+PP_API int pp_quad_linear_gather(const void* x, int64_t ldx_k, const uint32_t* codes, int64_t ldw,
+                                 const uint32_t* plug_idx, const void* plug_vals,
+                                 const uint32_t* plug_window_base, uint32_t base_lo32,
+                                 const void* unit_plugs, const uint32_t* unit_plug_off,
+                                 const void* tables, const float scales[4], int world,
+                                 void* const gather_out[], int64_t gather_ld, int64_t gather_row0,
+                                 uint32_t* const gather_flag[], uint32_t* gather_epoch,
+                                 int64_t N, int64_t K, void* workspace, size_t workspace_bytes,
+                                 void* stream);
+
+/* Makes `stream` wait until flags[q] (rank q's flag word in this rank's
+ * flag array, q < world) has reached *epoch.  The wait is bounded (about a
+ * second); a rank that never publishes sets *status to 3 (device int) and
+ * the stream continues.  world <= 8.
+ */
+PP_API int pp_gather_wait(const uint32_t* flags, int world, const uint32_t* epoch, int* status, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -57,6 +57,13 @@ _SIGNATURES = {
     "pp_quad_linear_fused": ([_c_void_p, _i64, _i64, _c_void_p, _i64, _c_void_p, _c_void_p, _c_void_p, _u32,
                               _c_void_p, _c_void_p, _c_void_p, _F4, _PTR4, _i64, _i64, _i64, _i64, _i64,
                               _c_void_p, _size_t, _c_void_p], _int),
+    "pp_ipc_handle": ([_c_void_p, _c_void_p, ctypes.POINTER(_size_t)], _int),
+    "pp_ipc_open": ([_c_void_p, ctypes.POINTER(_c_void_p)], _int),
+    "pp_ipc_close": ([_c_void_p], _int),
+    "pp_quad_linear_gather": ([_c_void_p, _i64, _c_void_p, _i64, _c_void_p, _c_void_p, _c_void_p, _u32,
+                               _c_void_p, _c_void_p, _c_void_p, _F4, _int, _c_void_p, _i64, _i64, _c_void_p,
+                               _c_void_p, _i64, _i64, _c_void_p, _size_t, _c_void_p], _int),
+    "pp_gather_wait": ([_c_void_p, _int, _c_void_p, _c_void_p, _c_void_p], _int),
     "pp_quad_decode": ([_c_void_p, _i64, _i64, _i64, _i64, _PTR7, _c_void_p, _PTR4, _i64, _i64,
                         _c_void_p], _int),
     "pp_quad_unpack": ([_c_void_p, _i64, _c_void_p, _c_void_p, _i64, _i64, _u32, _PTR7, _c_void_p,

@@ -125,7 +125,7 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const void* tmap, int 
       : "memory");
 }
 
-// Bulk copy (no tensor map, no multicast) of `bytes` from global memory to
+// Bulk copy (no tensor map, one destination CTA) of `bytes` from global memory to
 // this CTA's shared memory, completing on `bar`.  Both addresses 16-byte
 // aligned, bytes a multiple of 16.
 __device__ __forceinline__ void bulk_load(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {

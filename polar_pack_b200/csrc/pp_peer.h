@@ -1,0 +1,57 @@
+// Outputs gathered over the GPUs of one node through peer memory.
+//
+// A row-sharded Linear on `world` GPUs needs every rank's output rows on
+// every rank.  Instead of a separate all-gather, the GEMV's epilogue stores
+// each output element into the gather buffer of every rank (mapped into
+// this process with CUDA IPC; plain point-to-point stores over NVLink).  The
+// last warp of the launch to finish then bumps this launch's epoch and
+// writes it, with release semantics at system scope, into this rank's flag
+// word on every rank.  A reader waits (gather_wait_kernel, bounded) until
+// every rank's flag has reached its own epoch count, which is the number of
+// launches it made into the buffer, identical on all ranks.  Epochs live in
+// device memory and advance on the device, so CUDA-graph replays stay in
+// step.  Reuse of a buffer while a peer may still read it is the caller's
+// concern: alternating two buffers is enough when every use is followed by
+// a wait on every rank.
+#pragma once
+
+#include <cuda_fp16.h>
+#include <stdint.h>
+
+namespace pp {
+
+constexpr int kMaxPeers = 8;
+
+struct PeerGather {
+  __half* out[kMaxPeers];     // rank q's gather buffer, model-major: element model * ld + row
+  uint32_t* flag[kMaxPeers];  // this rank's flag word in rank q's flag array
+  int64_t ld;                 // elements between the model blocks
+  int64_t row0;               // the launch's first output row in the buffer
+  uint32_t* epoch;            // launches made into this buffer by this rank (device)
+  uint32_t* done;             // warps of the launch that finished (zero between launches)
+  int world;                  // 0: no gather (outputs go to `out` as usual)
+  int warps;                  // warps in the grid
+};
+
+#ifdef __CUDACC__
+// Called by every warp of the launch at its end: the warp's stores are
+// fenced at system scope; the last warp advances the epoch and publishes it
+// to every rank.
+__device__ __forceinline__ void gather_signal(const PeerGather& g) {
+  __syncwarp();
+  asm volatile("fence.acq_rel.sys;" ::: "memory");
+  if ((threadIdx.x & 31) != 0) return;
+  uint32_t old;
+  asm volatile("atom.add.acq_rel.gpu.global.u32 %0, [%1], 1;" : "=r"(old) : "l"(g.done) : "memory");
+  if (old != (uint32_t)g.warps - 1u) return;
+  *g.done = 0u;  // the next launch on the stream starts its epilogue after this one has completed
+  const uint32_t e = *g.epoch + 1u;
+  *g.epoch = e;
+  asm volatile("fence.acq_rel.sys;" ::: "memory");
+#pragma unroll
+  for (int q = 0; q < kMaxPeers; ++q)
+    if (q < g.world) asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(g.flag[q]), "r"(e) : "memory");
+}
+#endif
+
+}  // namespace pp

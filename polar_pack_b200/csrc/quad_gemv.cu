@@ -28,6 +28,7 @@
 #include "pp_common.cuh"
 #include "pp_engine.cuh"
 #include "pp_host.h"
+#include "pp_peer.h"
 #include "quad_layout.h"
 
 namespace pp {
@@ -94,6 +95,8 @@ struct QuadParams {
   const uint8_t* uplugs;
   const uint32_t* uplug_off;
   uint32_t pcap;
+  // outputs gathered into every rank's buffer (batch 1; world 0: none)
+  PeerGather gather;
   int cta_start[kMaxCtaTable + 1];  // unit start of every CTA (fill_cta_starts)
 };
 
@@ -414,7 +417,15 @@ struct QuadOp {
 
   __device__ __forceinline__ void store(int model, int bat, int f, float v) const {
     if (p.corr) v += p.corr[((int64_t)model * Mv + bat) * Nv + f];
-    p.out[model][(int64_t)bat * p.ldo_m + (int64_t)f * p.ldo_n] = __float2half_rn(v * p.scale[model]);
+    const __half h = __float2half_rn(v * p.scale[model]);
+    if (p.gather.world) {  // batch 1: element (model, row0 + f) of every rank's buffer
+      const int64_t o = (int64_t)model * p.gather.ld + p.gather.row0 + f;
+#pragma unroll
+      for (int q = 0; q < kMaxPeers; ++q)
+        if (q < p.gather.world) p.gather.out[q][o] = h;
+      return;
+    }
+    p.out[model][(int64_t)bat * p.ldo_m + (int64_t)f * p.ldo_n] = h;
   }
 };
 
@@ -465,7 +476,7 @@ __host__ __device__ inline uint32_t quad_scratch_bytes(bool nk, int nb, int M) {
 // its first S units, whose copies overlap the table build or copy.  Then
 // every warp streams and reduces on its own; there is no closing barrier.
 template <bool NK, int NB, bool PLUG>
-__global__ void __launch_bounds__(quad_warps(NK, NB) * 32, 1) quad_gemv_kernel(const __grid_constant__ QuadParams p) {
+__device__ __forceinline__ void quad_gemv_run(const QuadParams& p) {
   constexpr int NW = quad_warps(NK, NB);
   pdl_launch_dependents();
   const bool prepared = p.tables != nullptr;
@@ -559,6 +570,14 @@ __global__ void __launch_bounds__(quad_warps(NK, NB) * 32, 1) quad_gemv_kernel(c
   if (wu0 >= wu1) return;
   if (L.direct) quad_body<NK, NB, true, PLUG>(p, pt, L, rg, tb, cu0, cu1, wu0, wu1, status);
   else quad_body<NK, NB, false, PLUG>(p, pt, L, rg, tb, cu0, cu1, wu0, wu1, status);
+}
+
+// Every warp leaves quad_gemv_run, whatever path it took, and then takes
+// part in the gather's completion signal.
+template <bool NK, int NB, bool PLUG>
+__global__ void __launch_bounds__(quad_warps(NK, NB) * 32, 1) quad_gemv_kernel(const __grid_constant__ QuadParams p) {
+  quad_gemv_run<NK, NB, PLUG>(p);
+  if (p.gather.world) gather_signal(p.gather);
 }
 
 // Generic fallback for layouts the vector paths do not take (unaligned or
@@ -679,6 +698,10 @@ int launch_quad(QuadParams& prm, int grid, int idx, cudaStream_t s) {
   prm.smem_bytes = (uint32_t)max_smem;
   prm.layout_base = (uint32_t)reserved_smem(current_device());
   prm.layout = quad_layout(prm.layout_base, prm.smem_bytes, NW, stages, redb, true, prm.pcap);
+  if (prm.gather.world) {  // completion count of this launch: the counter below the status word
+    prm.gather.warps = grid * NW;
+    prm.gather.done = reinterpret_cast<uint32_t*>(prm.part.counters + (kMaxGrid - 2));
+  }
   return launch_kernel("quad_gemv_kernel", launch_overlap(), kern, dim3(grid), dim3(NW * 32), (size_t)max_smem, s,
                        prm);
 }
@@ -783,6 +806,7 @@ int launch_fused_chunks(const QuadParams& base, const uint32_t* codes, int64_t l
     int rc = encode_tmap_u32_2d(&c.tmap, c.codes, (uint64_t)K, (uint64_t)Nc, (uint64_t)ldw * 4, 32, 8);
     if (rc) return rc;
     for (int i = 0; i < 4; ++i) c.out[i] = base.out[i] + n0 * ldo_n;
+    c.gather.row0 = base.gather.row0 + n0;
     c.corr = nullptr;
     c.uplugs = uplugs;
     c.uplug_off = uplug_off + (n0 / 8) * W;
@@ -813,9 +837,13 @@ static int quad_run(const void* a, int64_t lda_m, int64_t lda_k, const uint32_t*
                     uint32_t base_lo32, const uint8_t* uplugs, const uint32_t* uplug_off,
                     const void* const luts[7], const void* tables, const float scales[4], void* const out[4],
                     int64_t ldo_m, int64_t ldo_n, int64_t M, int64_t N, int64_t K, void* ws, size_t ws_bytes,
-                    cudaStream_t s, bool file_layout) {
+                    cudaStream_t s, bool file_layout, const PeerGather* gather = nullptr) {
   int rc = check_common(luts, tables, scales, out, M, N, K);
   if (rc) return rc;
+  if (gather && (M != 1 || K == 0 || N == 0)) {
+    set_error("a gathered Linear needs batch 1 and a non-empty (N, K)");
+    return PP_ERR_INVALID;
+  }
   if (M == 0 || N == 0) return PP_OK;
   if (K == 0) {
     for (int i = 0; i < 4; ++i)
@@ -839,6 +867,10 @@ static int quad_run(const void* a, int64_t lda_m, int64_t lda_k, const uint32_t*
   // activation rows must be contiguous and aligned for the vector loads
   const bool xcontig = lda_k == 1 && aligned(a, nk ? 8 : 4) && (lda_m * 2) % (nk ? 8 : 4) == 0;
   const bool vec = xcontig && quad_vector_ok(nk, codes, ldc_k, ldc_n, N, K);
+  if (!vec && gather) {
+    set_error("a gathered Linear needs the vector path (aligned codes and activations)");
+    return PP_ERR_INVALID;
+  }
   if (!vec) {
     if (plug) {
       set_error("file-layout Linear needs 16-byte aligned codes, K %% 4 == 0, row stride %% 4 == 0 and "
@@ -909,6 +941,7 @@ static int quad_run(const void* a, int64_t lda_m, int64_t lda_k, const uint32_t*
     return PP_OK;
   }
   QuadParams prm{};
+  if (gather) prm.gather = *gather;
   prm.ldx_m = lda_m;
   prm.ldx_k = lda_k;
   prm.codes = codes;
@@ -1056,6 +1089,44 @@ int pp_quad_linear_fused(const void* x, int64_t ldx_m, int64_t ldx_k, const uint
                       reinterpret_cast<const uint8_t*>(unit_plugs), unit_plug_off, nullptr, tables, scales, out,
                       ldo_m, ldo_n, M, N, K, workspace, workspace_bytes, reinterpret_cast<cudaStream_t>(stream),
                       true);
+}
+
+int pp_quad_linear_gather(const void* x, int64_t ldx_k, const uint32_t* codes, int64_t ldw,
+                          const uint32_t* plug_idx, const void* plug_vals, const uint32_t* plug_window_base,
+                          uint32_t base_lo32, const void* unit_plugs, const uint32_t* unit_plug_off,
+                          const void* tables, const float scales[4], int world, void* const gather_out[],
+                          int64_t gather_ld, int64_t gather_row0, uint32_t* const gather_flag[],
+                          uint32_t* gather_epoch, int64_t N, int64_t K, void* workspace, size_t workspace_bytes,
+                          void* stream) {
+  if (!tables || (unit_plugs && (!unit_plug_off || !plug_vals))) {
+    pp::set_error("tables must not be NULL; unit plugs need their offsets and the plug table");
+    return PP_ERR_INVALID;
+  }
+  if (world < 1 || world > pp::kMaxPeers || !gather_out || !gather_flag || !gather_epoch || gather_ld < N ||
+      gather_row0 < 0) {
+    pp::set_error("gather: world must be 1..%d, buffers, flags and epoch non-NULL, ld >= N, row0 >= 0",
+                  pp::kMaxPeers);
+    return PP_ERR_INVALID;
+  }
+  pp::PeerGather g{};
+  for (int q = 0; q < world; ++q) {
+    if (!gather_out[q] || !gather_flag[q] || !pp::aligned(gather_out[q], 2) || !pp::aligned(gather_flag[q], 4)) {
+      pp::set_error("gather buffer or flag of rank %d is NULL or misaligned", q);
+      return PP_ERR_INVALID;
+    }
+    g.out[q] = reinterpret_cast<__half*>(gather_out[q]);
+    g.flag[q] = gather_flag[q];
+  }
+  g.ld = gather_ld;
+  g.row0 = gather_row0;
+  g.epoch = gather_epoch;
+  g.world = world;
+  // the ordinary output pointers are not written when gathering; the checks want them set
+  void* out[4];
+  for (int i = 0; i < 4; ++i) out[i] = g.out[0] + (int64_t)i * gather_ld + gather_row0;
+  return pp::quad_run(x, K, ldx_k, codes, 1, ldw, plug_idx, plug_vals, plug_window_base, base_lo32,
+                      reinterpret_cast<const uint8_t*>(unit_plugs), unit_plug_off, nullptr, tables, scales, out, 1,
+                      1, 1, N, K, workspace, workspace_bytes, reinterpret_cast<cudaStream_t>(stream), true, &g);
 }
 
 }  // extern "C"

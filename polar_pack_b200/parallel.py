@@ -162,3 +162,145 @@ def shard_quad_linear(pack, offset: int, N: int, K: int, world: int, rank: int):
     """This rank's row slice of the packed Linear at flat ``offset`` (file layout)."""
     n0, n1 = row_shard(N, world, rank)
     return pack.linear(offset + n0 * K, n1 - n0, K)
+
+
+# ------------------------------------------------------- peer gather ----
+def _align(n: int, a: int = 256) -> int:
+    return -(-n // a) * a
+
+
+class PeerBuffers:
+    """Gather buffers that every rank of a process group can write.
+
+    One device allocation per rank holds ``nbuf`` buffers of ``elems`` FP16
+    elements (the gathered outputs, model-major), a flag array per buffer
+    (``world`` u32: rank q's latest published epoch in word q) and this
+    rank's epoch counters (one u32 per buffer).  Every rank maps every other
+    rank's allocation through CUDA IPC (handles exchanged over the process
+    group), so a kernel on this GPU can store into all of them over NVLink.
+    Zero-filled once; epochs and flags only grow afterwards.
+    """
+
+    def __init__(self, elems: int, nbuf: int = 2, group=None, device=None):
+        import ctypes
+
+        from . import _lib
+        self.group = group
+        self.world = dist.get_world_size(group) if dist.is_initialized() else 1
+        self.rank = dist.get_rank(group) if dist.is_initialized() else 0
+        if self.world > 8:
+            raise ValueError("peer gather supports up to 8 ranks")
+        self.device = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
+        self.elems, self.nbuf = elems, nbuf
+        self.data_bytes = _align(elems * 2)
+        self.flags_off = nbuf * self.data_bytes
+        self.epoch_off = self.flags_off + _align(nbuf * self.world * 4)
+        total = self.epoch_off + _align(nbuf * 4)
+        self.mem = torch.zeros(total, dtype=torch.uint8, device=self.device)
+        self.status = torch.zeros(1, dtype=torch.int32, device=self.device)
+        handle = (ctypes.c_char * 64)()
+        off = _lib._size_t()
+        _lib.call("pp_ipc_handle", self.mem.data_ptr(), handle, ctypes.byref(off))
+        mine = (bytes(handle), int(off.value))
+        allh = [None] * self.world
+        if self.world > 1:
+            dist.all_gather_object(allh, mine, group=group)
+        else:
+            allh = [mine]
+        self.bases, self._opened = [], []
+        for q, (h, o) in enumerate(allh):
+            if q == self.rank:
+                self.bases.append(self.mem.data_ptr())
+                continue
+            p = ctypes.c_void_p()
+            _lib.call("pp_ipc_open", ctypes.create_string_buffer(h, 64), ctypes.byref(p))
+            self._opened.append(p.value)
+            self.bases.append(p.value + o)
+        if self.world > 1:
+            dist.barrier(group=group)
+
+    def out_ptrs(self, b: int) -> list[int]:
+        """Buffer ``b`` of every rank, as mapped here."""
+        return [base + b * self.data_bytes for base in self.bases]
+
+    def flag_ptrs(self, b: int) -> list[int]:
+        """This rank's flag word of buffer ``b`` in every rank's flag array."""
+        return [base + self.flags_off + (b * self.world + self.rank) * 4 for base in self.bases]
+
+    def local_flags(self, b: int) -> int:
+        return self.mem.data_ptr() + self.flags_off + b * self.world * 4
+
+    def epoch_ptr(self, b: int) -> int:
+        return self.mem.data_ptr() + self.epoch_off + b * 4
+
+    def view(self, b: int) -> torch.Tensor:
+        """This rank's buffer ``b`` as FP16 elements."""
+        return self.mem[b * self.data_bytes:b * self.data_bytes + self.elems * 2].view(torch.float16)
+
+    def wait(self, b: int, stream=None) -> None:
+        """Make the stream wait until every rank has published buffer ``b``."""
+        from . import _lib
+        s = stream if stream is not None else torch.cuda.current_stream(self.device).cuda_stream
+        _lib.call("pp_gather_wait", self.local_flags(b), self.world, self.epoch_ptr(b), self.status.data_ptr(), s)
+
+    def close(self) -> None:
+        from . import _lib
+        if self.world > 1:
+            torch.cuda.synchronize(self.device)
+            dist.barrier(group=self.group)  # no peer still writes into a mapping about to go
+        for p in self._opened:
+            _lib.call("pp_ipc_close", p)
+        self._opened = []
+
+
+class PeerShardedGroup:
+    """Row-sharded batch-1 Linears whose outputs are gathered through peer
+    memory instead of an all-gather.
+
+    ``layers[j]`` is this rank's row shard (a ``QuadLinearSlice`` with its
+    unit plugs) of a Linear with ``Ns[j]`` rows; ``row0s[j]`` is the shard's
+    first row.  A call launches every Linear with ``pp_quad_linear_gather``
+    into buffer ``b`` (model-major: model k, Linear j, row n at
+    ``k * sum(Ns) + offset_j + n``), then waits for every rank.  The result
+    is ``peers.view(b)`` viewed as ``(4, sum(Ns))``, which the next call into
+    the same buffer overwrites: alternate the buffers.
+    """
+
+    def __init__(self, layers, Ns, row0s, peers: PeerBuffers):
+        import ctypes
+
+        from . import _lib
+        from .quadpack import quad_linear_workspace_bytes
+        self.layers, self.Ns, self.peers = list(layers), list(Ns), peers
+        self.total = sum(self.Ns)
+        if 4 * self.total > peers.elems:
+            raise ValueError("peer buffers too small for the group")
+        self.cols = [sum(self.Ns[:j]) for j in range(len(self.Ns))]
+        self.row0s = list(row0s)
+        dev = peers.device
+        nb = max(quad_linear_workspace_bytes(1, l.N, l.K) for l in self.layers)
+        self.ws = torch.zeros(max(nb, 256), dtype=torch.uint8, device=dev)
+        self._lib = _lib.load()
+        self._args = {}
+        for b in range(peers.nbuf):
+            outs = (ctypes.c_void_p * 8)(*peers.out_ptrs(b))
+            flags = (ctypes.c_void_p * 8)(*peers.flag_ptrs(b))
+            row = []
+            for l, c, r0 in zip(self.layers, self.cols, self.row0s):
+                row.append((l.codes.data_ptr(), l.K, _lib.ptr(l.plug_idx), _lib.ptr(l.plug_vals),
+                            _lib.ptr(l.plug_window_base), ctypes.c_uint32(l.offset & 0xFFFFFFFF),
+                            _lib.ptr(l.unit_plugs), _lib.ptr(l.unit_plug_off), l.pack.tables.data_ptr(),
+                            _lib.floats4(l.pack.scales), peers.world, outs, self.total, c + r0, flags,
+                            peers.epoch_ptr(b), l.N, l.K))
+            self._args[b] = (row, outs, flags)
+
+    def __call__(self, xs, b: int, stream=None) -> torch.Tensor:
+        from . import _lib
+        s = stream if stream is not None else torch.cuda.current_stream(self.peers.device).cuda_stream
+        for x, a in zip(xs, self._args[b][0]):
+            rc = self._lib.pp_quad_linear_gather(x.data_ptr(), x.stride(-1), *a, self.ws.data_ptr(),
+                                                 self.ws.numel(), s)
+            if rc:
+                _lib.check(rc)
+        self.peers.wait(b, s)
+        return self.peers.view(b)[:4 * self.total].view(4, self.total)
