@@ -254,7 +254,22 @@ def run_ours(args):
         if rc:
             _lib.check(rc)
 
+    # N > 1 GPUs at batch 1: every rank's GEMVs store their rows straight into
+    # all ranks' gather buffers (peer memory over NVLink) and one bounded wait
+    # per step makes the stream wait for every rank; two buffers alternate
+    use_peer = world > 1 and M == 1 and not args.nccl_gather
+    peers, pgroups = None, []
+    if use_peer:
+        from polar_pack_b200.parallel import PeerBuffers, PeerShardedGroup, row_shard
+        Ns = [N for _, N in SHAPES]
+        peers = PeerBuffers(4 * sum(Ns), nbuf=2, device=dev)
+        r0s = [row_shard(N, world, rank)[0] for N in Ns]
+        pgroups = [PeerShardedGroup(st, Ns, r0s, peers) for st in sets]
+
     def step(i):
+        if use_peer:
+            pgroups[i % len(pgroups)](xs, i % 2, sh)
+            return
         for args_c, outs, l in calls[i % len(calls)]:
             launch(args_c)
         if world > 1:
@@ -299,7 +314,7 @@ def run_ours(args):
     K_steps = args.steps
     # batch 1 with unit plugs: one fused launch per Linear; else a plug-correction launch too
     launches_per_step = sum(1 if (l.unit_plugs is not None and M == 1) or l.plug_vals is None else 2
-                            for l in sets[0])
+                            for l in sets[0]) + (1 if use_peer else 0)   # + the gather wait
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     clocks = ClockSampler(local)
     clocks.start()
@@ -368,7 +383,7 @@ def run_ours(args):
         kernel_ms += tj
 
     # e2e through the public API with host buffers (pinned), 1 GPU view of rank's work
-    e2e = run_e2e(torch, dist, sets, xs, dev, args, world, M, full_sets)
+    e2e = run_e2e(torch, dist, sets, xs, dev, args, world, M, full_sets, pgroups)
 
     # the second half of the metric: 4-model decode tokens/s of a 3B-class step
     decode = None
@@ -387,7 +402,9 @@ def run_ours(args):
                    "batch": M, "replica_streams": args.replicas,
                    "bytes_per_step": int(per_step_bytes), "l2": "inputs per step ~200 MB > 126 MB L2, "
                    "4 rotating replica streams (no flush)",
-                   "parallelism": f"row-sharded x{world}, one NCCL all-gather per step" if world > 1
+                   "parallelism": (f"row-sharded x{world}, outputs stored into every rank's buffer over NVLink "
+                                   "by the GEMV, one gather wait per step" if use_peer else
+                                   f"row-sharded x{world}, one NCCL all-gather per step") if world > 1
                                   else "single GPU",
                    "timing": ("CUDA graph replay of whole steps" if use_graphs else "eager launches") +
                              ("; launch overlap on" if not args.no_overlap else ""),
@@ -403,7 +420,8 @@ def run_ours(args):
                                    "profiles/quad_gemv_fused_2048x11008.md)"},
         "e2e": e2e,
         "gpu_launches": launches_per_step * K_steps,
-        "gpu_launches_note": "per Linear: the GEMV kernel with the plug correction fused in (batch 1)",
+        "gpu_launches_note": "per Linear: the GEMV kernel with the plug correction fused in (batch 1)" +
+                             ("; per step: one gather wait kernel" if use_peer else ""),
         "clocks": clk,
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -411,6 +429,8 @@ def run_ours(args):
     # graphs that hold NCCL calls must be released before the process group
     graphs.clear()
     torch.cuda.synchronize(dev)
+    if peers is not None:
+        peers.close()   # unmaps the peers' buffers once no rank writes into them
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
@@ -479,10 +499,48 @@ def run_decode_step(torch, dist, dev, args, world, rank, lib, stream):
              _lib.ptrs(outs, 4), outs[0].stride(0), outs[0].stride(1), M, l.N, l.K, ws.data_ptr(), ws.numel(), sh)
         return a, send, recv, outs
 
-    calls = [[prep(N, K, l) for N, K, l in row] for row in units]
-    head_call = prep(*head)
+    # N > 1 GPUs: each launch stores its rows into every rank's gather
+    # buffer (peer memory) and a bounded wait follows it; the layers' launches
+    # alternate buffers 0 and 1, the lm_head uses buffer 2, so no buffer is
+    # written twice in a row, across steps either
+    use_peer = world > 1 and not args.nccl_gather
+    peers = None
+    if use_peer:
+        from polar_pack_b200.parallel import PeerBuffers
+        peers = PeerBuffers(4 * max(N for N, _, _ in lins), nbuf=3, device=dev)
+
+    def prep_peer(N, K, l, b):
+        n0, _ = row_shard(N, world, rank)
+        outs = (C.c_void_p * 8)(*peers.out_ptrs(b))
+        flags = (C.c_void_p * 8)(*peers.flag_ptrs(b))
+        x = xin[K]
+        a = (x.data_ptr(), x.stride(1), l.codes.data_ptr(), l.K, _lib.ptr(l.plug_idx), _lib.ptr(l.plug_vals),
+             _lib.ptr(l.plug_window_base), C.c_uint32(l.offset & 0xFFFFFFFF), _lib.ptr(l.unit_plugs),
+             _lib.ptr(l.unit_plug_off), l.pack.tables.data_ptr(), _lib.floats4(l.pack.scales), world, outs, N, n0,
+             flags, peers.epoch_ptr(b), l.N, l.K, ws.data_ptr(), ws.numel(), sh)
+        return ("peer", a, b, outs, flags)
+
+    if use_peer:
+        k = 0
+        calls = []
+        for row in units:
+            r_ = []
+            for N, K, l in row:
+                r_.append(prep_peer(N, K, l, k % 2))
+                k += 1
+            calls.append(r_)
+        head_call = prep_peer(*head, 2)
+    else:
+        calls = [[prep(N, K, l) for N, K, l in row] for row in units]
+        head_call = prep(*head)
 
     def launch(c):
+        if c[0] == "peer":
+            rc = lib.pp_quad_linear_gather(*c[1])
+            if rc:
+                _lib.check(rc)
+            peers.wait(c[2], sh)
+            return
         rc = lib.pp_quad_linear_fused(*c[0])
         if rc:
             _lib.check(rc)
@@ -544,18 +602,22 @@ def run_decode_step(torch, dist, dev, args, world, rank, lib, stream):
     launches = cfg["layers"] * len(groups) + 1
     res = {"tok_s": round(4 * M / (ms * 1e-3), 1), "ms_per_step": round(ms, 3),
            "GB/s": round(step_bytes / (ms * 1e-3) / 1e9, 1), "bytes_per_step": int(step_bytes),
-           "launches_per_step": launches, "all_gathers_per_step": launches if world > 1 else 0,
+           "launches_per_step": launches * (2 if use_peer else 1),
+           "gather": ("peer stores + one wait kernel per GEMV" if use_peer else
+                      "NCCL all-gather per GEMV") if world > 1 else "none",
            "what": "4-model tokens/s of the packed Linears of a 3B-class decode step at batch 1 "
                    "(36 layers x [qkv 2560x2048, o 2048x2048, gate_up 22016x2048, down 2048x11008] + lm_head "
                    "151936x2048; 2 distinct layer weight sets alternate); attention, norms and activations "
                    "between them are outside the path and not run",
            "timing": "CUDA graph of one whole step" if run is not step else "eager launches"}
     del calls, head_call, units, head, lins, st
+    if peers is not None:
+        peers.close()
     torch.cuda.empty_cache()
     return res
 
 
-def run_e2e(torch, dist, sets, xs, dev, args, world, M, full_sets):
+def run_e2e(torch, dist, sets, xs, dev, args, world, M, full_sets, pgroups=None):
     """Same metric through the public API: every step copies that step's
     inputs from pinned host memory to the GPU, runs the Linears as one
     RowShardedGroup (with N > 1 GPUs each rank computes its row shards and
@@ -573,19 +635,28 @@ def run_e2e(torch, dist, sets, xs, dev, args, world, M, full_sets):
         dx.append(dxf[o:o + n].view(x.shape))
         o += n
     full_n = [N for _, N in SHAPES]
-    # the independent Linears as one row-sharded group writing into its send buffer
-    groups = [RowShardedGroup([lambda x, out, l=l: quad_linear(x, l, out=out) for l in st], full_n,
-                              writes_out=True) for st in sets]
-    for g_ in groups:
-        g_(dx)
-    host_out = torch.empty(groups[0].raw().shape, dtype=torch.float16).pin_memory()
-    h2d, d2h = hx.numel() * 2, host_out.numel() * 2
+    if pgroups:
+        # N > 1 GPUs: the peer-gathered group; its result is complete on every rank
+        host_out = torch.empty((4, sum(full_n)), dtype=torch.float16).pin_memory()
 
-    def step(i):
-        dxf.copy_(hx, non_blocking=True)
-        grp = groups[i % len(groups)]
-        grp(dx)
-        host_out.copy_(grp.raw(), non_blocking=True)
+        def step(i):
+            dxf.copy_(hx, non_blocking=True)
+            y = pgroups[i % len(pgroups)](dx, i % 2)
+            host_out.copy_(y, non_blocking=True)
+    else:
+        # the independent Linears as one row-sharded group writing into its send buffer
+        groups = [RowShardedGroup([lambda x, out, l=l: quad_linear(x, l, out=out) for l in st], full_n,
+                                  writes_out=True) for st in sets]
+        for g_ in groups:
+            g_(dx)
+        host_out = torch.empty(groups[0].raw().shape, dtype=torch.float16).pin_memory()
+
+        def step(i):
+            dxf.copy_(hx, non_blocking=True)
+            grp = groups[i % len(groups)]
+            grp(dx)
+            host_out.copy_(grp.raw(), non_blocking=True)
+    h2d, d2h = hx.numel() * 2, host_out.numel() * 2
 
     for i in range(args.warmup):
         step(i)
@@ -609,7 +680,8 @@ def run_e2e(torch, dist, sets, xs, dev, args, world, M, full_sets):
             total += layer_bytes(l.N, l.K, l.p_hi - l.p_lo, M)
     return {"value": round(total / (ms * 1e-3) / 1e9, 1), "unit": UNIT, "h2d_bytes_per_step": int(h2d),
             "d2h_bytes_per_step": int(d2h),
-            "api": "polar_pack_b200.parallel.RowShardedGroup of polar_pack_b200.quadpack.quad_linear"}
+            "api": "polar_pack_b200.parallel.PeerShardedGroup (pp_quad_linear_gather)" if pgroups else
+                   "polar_pack_b200.parallel.RowShardedGroup of polar_pack_b200.quadpack.quad_linear"}
 
 
 def load_traffic():
@@ -778,6 +850,8 @@ def main():
     ap.add_argument("--eager", action="store_true", help="time eager launches instead of CUDA graphs")
     ap.add_argument("--no-overlap", action="store_true", help="launch kernels without programmatic overlap")
     ap.add_argument("--no-decode", action="store_true", help="skip the 3B decode-step leg")
+    ap.add_argument("--nccl-gather", action="store_true",
+                    help="with N > 1 GPUs gather the outputs with an NCCL all-gather instead of peer stores")
     ap.add_argument("--shapes", default="", help="subset of the sweep as KxN,KxN (in x out), e.g. for profiling "
                                                  "one Linear; the line then names the subset")
     args = ap.parse_args()

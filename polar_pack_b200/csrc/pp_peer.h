@@ -34,12 +34,16 @@ struct PeerGather {
 };
 
 #ifdef __CUDACC__
-// Called by every warp of the launch at its end: the warp's stores are
-// fenced at system scope; the last warp advances the epoch and publishes it
-// to every rank.
+// Called by every warp of the launch at its end.  The warp's stores are
+// ordered before its lane 0 (__syncwarp) and lane 0's release of the
+// arrival counter (GPU scope: all warps run on this GPU); the last warp to
+// arrive acquires them all, advances the epoch and publishes it with a
+// system-scope fence and release stores, which carry every store that
+// happens before them to the peers (cumulativity).  One system-scope fence
+// per launch: a fence in every warp would wait for each warp's stores to
+// reach the peers.
 __device__ __forceinline__ void gather_signal(const PeerGather& g) {
   __syncwarp();
-  asm volatile("fence.acq_rel.sys;" ::: "memory");
   if ((threadIdx.x & 31) != 0) return;
   uint32_t old;
   asm volatile("atom.add.acq_rel.gpu.global.u32 %0, [%1], 1;" : "=r"(old) : "l"(g.done) : "memory");
