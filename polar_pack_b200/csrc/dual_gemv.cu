@@ -18,6 +18,13 @@ namespace pp {
 
 int zero_f16(void* p, int64_t R, int64_t C, int64_t ldr, int64_t ldc, cudaStream_t s);
 
+// dual_tma.cu: batch 1 on the TMA engine
+bool dual_tma_ok(int64_t M, int64_t N, int64_t K, int64_t gs, const void* x, int64_t ldx_k, const int16_t* codes,
+                 int64_t ldp_k, int64_t ldp_n, const void* bmax);
+int launch_dual_tma(const void* x, const int16_t* codes, int64_t ldp_k, const void* bmax, const void* amp_lut,
+                    const void* cos_lut, const void* sin_lut, void* out1, void* out2, int64_t ldo_n, int64_t N,
+                    int64_t K, void* ws, size_t ws_bytes, int sms, cudaStream_t s);
+
 // Warps per CTA, bounded by shared memory: 136 KiB of tables plus two
 // partial slots per warp.
 __host__ __device__ constexpr int dual_warps(int nb) { return nb == 1 ? 10 : 5; }
@@ -368,6 +375,9 @@ static int dual_run(const void* a, int64_t lda_m, int64_t lda_k, const int16_t* 
     set_error("workspace of %zu bytes (256-byte aligned, zero-filled) required, got %zu", need, ws_bytes);
     return PP_ERR_WORKSPACE;
   }
+  if (dual_tma_ok(M, N, K, gs, a, lda_k, packed, ldp_k, ldp_n, bmax))
+    return launch_dual_tma(a, packed, ldp_k, bmax, amp_lut, cos_lut, sin_lut, out1, out2, ldo_n, N, K, ws, ws_bytes,
+                           sms, s);
   DualParams prm{};
   prm.ldx_m = lda_m;
   prm.ldx_k = lda_k;

@@ -299,8 +299,11 @@ constexpr uint32_t kDualAmpBytes = 64u * 128u;
 constexpr uint32_t kDualPhaseBytes = 1024u * 128u;
 constexpr uint32_t kDualLutBytes = kDualAmpBytes + kDualPhaseBytes;
 
-__device__ __forceinline__ void build_dual_lut(uint8_t* smem, uint32_t* stage, const __half* amp_lut,
-                                               const __half* cos_lut, const __half* sin_lut) {
+// Dual tables in two steps, like the quad ones: the 64 + 1024 table words
+// are staged (4352 bytes), then after a CTA barrier fanned out to the 32
+// lane copies.
+__device__ __forceinline__ void dual_lut_stage(uint32_t* stage, const __half* amp_lut, const __half* cos_lut,
+                                               const __half* sin_lut) {
   const uint16_t* a = reinterpret_cast<const uint16_t*>(amp_lut);
   const uint16_t* c = reinterpret_cast<const uint16_t*>(cos_lut);
   const uint16_t* s = reinterpret_cast<const uint16_t*>(sin_lut);
@@ -314,13 +317,23 @@ __device__ __forceinline__ void build_dual_lut(uint8_t* smem, uint32_t* stage, c
     }
     stage[e] = v;
   }
-  __syncthreads();
+}
+
+// after a barrier that follows dual_lut_stage
+__device__ __forceinline__ void dual_lut_fanout(uint8_t* smem, const uint32_t* stage) {
   for (int idx = threadIdx.x; idx < (64 + 1024) * 8; idx += blockDim.x) {
     const int e = idx >> 3, part = idx & 7;
     const uint32_t v = stage[e];
     const uint32_t off = e < 64 ? (uint32_t)e * 128u : kDualAmpBytes + (uint32_t)(e - 64) * 128u;
     *reinterpret_cast<uint4*>(smem + off + (uint32_t)part * 16u) = make_uint4(v, v, v, v);
   }
+}
+
+__device__ __forceinline__ void build_dual_lut(uint8_t* smem, uint32_t* stage, const __half* amp_lut,
+                                               const __half* cos_lut, const __half* sin_lut) {
+  dual_lut_stage(stage, amp_lut, cos_lut, sin_lut);
+  __syncthreads();
+  dual_lut_fanout(smem, stage);
 }
 
 }  // namespace pp

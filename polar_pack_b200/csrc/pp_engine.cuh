@@ -249,7 +249,8 @@ __device__ __forceinline__ void run_partition(Op& op, const Partition& pt, float
 // the tile.  No warp ever waits for another, and every sum has a fixed
 // order, so results are deterministic.
 //
-// Op additions: kUnitBytes; void read(Buf&, uint32_t slot) const;
+// Op additions: kUnitBytes; void read(Buf&, uint32_t slot, int s, int tile)
+// const (the unit in ring slot s, before the slot is refilled);
 // void side(int p, int u, int kc) (side data of unit u in side slot p; a
 // warp has one side slot more than ring slots, so the slot of the unit
 // being computed is not refilled before the next unit's wait); void
@@ -456,7 +457,7 @@ __device__ __forceinline__ void tma_stream(Op& op, const Issue& issue, TmaRing& 
     op.zero();
     for (int kc = kc0; kc < kc0 + n; ++kc) {
       if (!mbar_wait_bounded(rg.bars + 8u * (uint32_t)s, ph, status)) return;
-      op.read(buf, rg.ring + (uint32_t)s * Op::kUnitBytes);
+      op.read(buf, rg.ring + (uint32_t)s * Op::kUnitBytes, s, t);
       __syncwarp();
       if (rg.next.seg < 3) rg.issue_next(issue, s, Op::kUnitBytes, leader);  // warp-uniform test
       op.side(sp, t * upt + kc, kc);
@@ -484,16 +485,25 @@ struct PartitionPlan {
 };
 
 // Unit start of every CTA of a TMA-engine launch (start[grid] = units).
-// Equal unit ranges by default.  When giving every CTA whole tiles costs at
-// most `slack` units of imbalance (the most loaded CTA against the mean),
-// the ranges are tile-aligned instead: no tile is then split across CTAs,
-// which saves the cross-CTA reduction at the end of the launch.
-inline void fill_cta_starts(PartitionPlan& pl, int* start, int64_t slack) {
-  const int G = pl.grid;
-  const int64_t max_tiles = (pl.tiles + G - 1) / G;
-  pl.tile_aligned = max_tiles * pl.upt * G - pl.units <= slack * G;
-  for (int c = 0; c <= G; ++c)
-    start[c] = pl.tile_aligned ? (int)(pl.tiles * c / G * pl.upt) : (int)(pl.units * c / G);
+// Tile-aligned ranges save the cross-CTA reduction at the end of the
+// launch (no tile is split across CTAs), so they are taken when cheap:
+// whole tiles on min(grid, tiles)
+// CTAs when the busiest of them holds at most `slack` units more than the
+// busiest CTA of the equal split over all pl.grid CTAs, else the equal
+// split.  (Fewer tiles than CTAs must not shrink the grid: a tall, narrow
+// matrix would then leave most SMs idle.)
+inline void plan_cta_starts(PartitionPlan& pl, int* start, int64_t slack) {
+  const int64_t split_max = (pl.units + pl.grid - 1) / pl.grid;
+  const int G2 = pl.grid < pl.tiles ? pl.grid : (int)pl.tiles;
+  const int64_t aligned_max = (pl.tiles + G2 - 1) / G2 * pl.upt;
+  if (aligned_max <= split_max + slack) {
+    pl.grid = G2;
+    pl.tile_aligned = true;
+    for (int c = 0; c <= G2; ++c) start[c] = (int)(pl.tiles * c / G2 * pl.upt);
+  } else {
+    pl.tile_aligned = false;
+    for (int c = 0; c <= pl.grid; ++c) start[c] = (int)(pl.units * c / pl.grid);
+  }
 }
 
 inline PartitionPlan plan_partition(int64_t tiles, int64_t upt, int warps, int sms, int nout, int64_t M,

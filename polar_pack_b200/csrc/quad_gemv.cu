@@ -97,7 +97,7 @@ struct QuadParams {
   uint32_t pcap;
   // outputs gathered into every rank's buffer (batch 1; world 0: none)
   PeerGather gather;
-  int cta_start[kMaxCtaTable + 1];  // unit start of every CTA (fill_cta_starts)
+  int cta_start[kMaxCtaTable + 1];  // unit start of every CTA (plan_cta_starts)
 };
 
 struct QuadBuf {
@@ -207,7 +207,7 @@ struct QuadOp {
   // mma row g maps to tile row pr = (g>>1) | ((g&1)<<2), so the two rows of
   // a quarter-warp differ in bit 2 and their chunks never share banks.
   // KN: lane (g, c) needs chunk g of rows 2c, 2c+1, 2c+8, 2c+9.
-  __device__ __forceinline__ void read(Buf& b, uint32_t slot) const {
+  __device__ __forceinline__ void read(Buf& b, uint32_t slot, int = 0, int = 0) const {
 #pragma unroll
     for (int s = 0; s < 4; ++s) b.q[s] = lds128(slot + roff[s]);
   }
@@ -645,16 +645,7 @@ PartitionPlan quad_plan(bool nk, int64_t Mc, int64_t N, int64_t K, int sms, int*
   PartitionPlan pl = plan_partition(cdiv(N, tile_w), cdiv(K, unit_k), quad_warps(nk, nb), cap, 4, Mc, tile_w);
   if (pl.units > 0) {
     int tmp[kMaxCtaTable + 1];
-    int* st = starts ? starts : tmp;
-    if (pl.grid > pl.tiles) {  // tile-aligned candidates never need more CTAs than tiles
-      PartitionPlan t = pl;
-      t.grid = (int)pl.tiles;
-      fill_cta_starts(t, st, kAlignSlackUnits);
-      if (t.tile_aligned) pl = t;
-      else fill_cta_starts(pl, st, kAlignSlackUnits);
-    } else {
-      fill_cta_starts(pl, st, kAlignSlackUnits);
-    }
+    plan_cta_starts(pl, starts ? starts : tmp, kAlignSlackUnits);
   }
   return pl;
 }

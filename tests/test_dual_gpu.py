@@ -46,8 +46,11 @@ def test_decode_bit_exact(cuda, dual_golden, tag):
         np.testing.assert_array_equal(bits(b[j].cpu().numpy()), bits(ref[j]))
 
 
+# batch 1 with N % 256 == 0 (and the default group of 32) runs on the TMA
+# engine (dual_tma.cu), ragged K included; the rest on the register engine
 SHAPES = [(1, 64, 96), (1, 2048, 256), (3, 37, 56), (4, 100, 64), (8, 256, 128), (9, 64, 64),
-          (16, 512, 192), (17, 96, 40), (2, 33, 7), (1, 4096, 512)]
+          (16, 512, 192), (17, 96, 40), (2, 33, 7), (1, 4096, 512), (1, 100, 256), (1, 37, 768),
+          (1, 1000, 1024)]
 
 
 @pytest.mark.parametrize("M,K,N", SHAPES)
@@ -82,7 +85,7 @@ def test_k_mismatch_raises_assertion(cuda):
                              torch.ones(8, dtype=torch.float16, device=cuda), amp, c, s)
 
 
-@pytest.mark.parametrize("K,N", [(2048, 2048), (2048, 11008)])
+@pytest.mark.parametrize("K,N", [(2048, 2048), (2048, 11008), (11008, 2048)])
 def test_full_size(cuda, K, N):
     from polar_pack_b200.polar_kernels import dual_decode, polar_dual_bitpacked, quantize_polar_bitpacked
     g = torch.Generator(device="cpu").manual_seed(K + N)

@@ -120,13 +120,16 @@ class UnitSeq:
                 yield seg, u, u + 1 == b
 
 
-def fill_cta_starts(tiles, upt, G, slack):
-    """pp_engine.cuh fill_cta_starts: equal units, or tile-aligned when cheap."""
+def plan_cta_starts(tiles, upt, G, slack):
+    """pp_engine.cuh plan_cta_starts: whole tiles on min(G, tiles) CTAs when
+    its busiest CTA holds at most `slack` units more than the equal split's
+    busiest, else the equal split over G.  Returns (starts, aligned, grid)."""
     U = tiles * upt
-    max_tiles = -(-tiles // G)
-    aligned = max_tiles * upt * G - U <= slack * G
-    starts = [(tiles * c // G) * upt if aligned else U * c // G for c in range(G + 1)]
-    return starts, aligned
+    split_max = -(-U // G)
+    G2 = min(G, tiles)
+    if -(-tiles // G2) * upt <= split_max + slack:
+        return [tiles * c // G2 * upt for c in range(G2 + 1)], True, G2
+    return [U * c // G for c in range(G + 1)], False, G
 
 
 def cta_of_unit(starts, G, x):
@@ -239,14 +242,7 @@ def test_tma_engine_with_host_cta_table(upt, NW):
     for tiles in [1, 5, 32, 256, 1376]:
         U = upt * tiles
         G = min(148, max(1, -(-U // (2 * NW))))
-        if G > tiles:
-            st, aligned = fill_cta_starts(tiles, upt, tiles, 32)
-            if aligned:
-                G = tiles
-            else:
-                st, aligned = fill_cta_starts(tiles, upt, G, 32)
-        else:
-            st, aligned = fill_cta_starts(tiles, upt, G, 32)
+        st, aligned, G = plan_cta_starts(tiles, upt, G, 32)
         assert all(st[c] < st[c + 1] for c in range(G))    # no empty CTA
         if aligned:
             assert all(x % upt == 0 for x in st)
@@ -262,12 +258,22 @@ def test_sweep_shapes_plan():
         tiles, upt = -(-N // 8), -(-K // 64)
         U = tiles * upt
         G = min(148, -(-U // 32))
-        if G > tiles:
-            _, al = fill_cta_starts(tiles, upt, tiles, 32)
-            G = tiles if al else G
-        _, al = fill_cta_starts(tiles, upt, G, 32)
+        _, al, G = plan_cta_starts(tiles, upt, G, 32)
         plans[(K, N)] = (G, al)
     assert plans[(2048, 256)] == (32, True)
     assert plans[(2048, 2048)] == (148, True)
     assert plans[(2048, 11008)] == (148, True)
     assert plans[(11008, 2048)] == (148, False)
+
+
+def test_narrow_tall_keeps_every_sm():
+    """Fewer tiles than SMs must not shrink the grid when tiles are long: the
+    dual kernel's 11008 x 2048 (32 tiles of 688 units) keeps 148 CTAs."""
+    tiles, upt = 2048 // 64, 11008 // 16
+    G = min(148, -(-tiles * upt // 32))
+    st, aligned, G2 = plan_cta_starts(tiles, upt, G, 32)
+    assert (G2, aligned) == (148, False)
+    assert max(b - a for a, b in zip(st, st[1:])) <= -(-tiles * upt // 148)
+    # short tiles with few of them: whole tiles win
+    st, aligned, G2 = plan_cta_starts(32, 32, 32, 32)
+    assert (G2, aligned) == (32, True)
