@@ -19,7 +19,9 @@ while the previous one finishes), unless ``--no-overlap``.
 A second leg times the packed Linears of a 3B-class decode step (BASELINE
 36 layers of qkv / o / gate_up / down launches plus the lm_head,
 batch 1) and reports 4-model decode tokens/s under
-``config.decode_step_3b`` (``--no-decode`` skips it).
+``config.decode_step_3b`` (``--no-decode`` skips it).  A third times the
+dual-pack kernel (2 models of 16-bit polar codes) on the sweep shapes at
+batch 1 under ``config.dual_gemv_b1`` (``--no-dual`` skips it).
 
 Metric: packed-stream GB/s = algorithmic bytes / device time, where the
 bytes of one Linear are 4*N*K (codes) + 12*P (plug index + values) +
@@ -389,6 +391,10 @@ def run_ours(args):
     decode = None
     if not args.no_decode and not args.shapes and M == 1:
         decode = run_decode_step(torch, dist, dev, args, world, rank, lib, stream)
+    # the dual-pack kernel on the same shapes (one GPU's kernel time)
+    dual = None
+    if not args.no_dual and M == 1:
+        dual = run_dual_leg(torch, dev, args, lib, stream)
 
     peak, peak_kind = measured_peak()
     achieved = kernel_bytes / (kernel_ms * 1e-3) / 1e9
@@ -409,7 +415,8 @@ def run_ours(args):
                    "timing": ("CUDA graph replay of whole steps" if use_graphs else "eager launches") +
                              ("; launch overlap on" if not args.no_overlap else ""),
                    "per_shape_gemv_kernel": per_shape,
-                   "decode_step_3b": decode},
+                   "decode_step_3b": decode,
+                   "dual_gemv_b1": dual},
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(achieved / peak, 4), "peak_source": f"{peak_kind} hbm_gbs",
                      "kernel": "quad_gemv_kernel<NK=1,NB=1,PLUG=1> (file layout, batch 1, plugs fused)",
@@ -436,6 +443,76 @@ def run_ours(args):
         dist.destroy_process_group()
     if rank == 0:
         print(json.dumps(res))
+
+
+def run_dual_leg(torch, dev, args, lib, stream):
+    """The dual-pack kernel (polar_dual_bitpacked, 2 models of 16-bit polar
+    codes, kernel layout (K, N)) on the sweep shapes at batch 1.  Each shape
+    is packed once from synthetic weights of the BASELINE distribution and
+    copied into enough replicas that every launch reads codes L2 does not
+    hold; a graph of back-to-back launches is timed per shape.  Bytes of one
+    call: 2KN (codes) + 2 ceil(KN/32) (group scales) + 2MK + 4MN."""
+    from polar_pack_b200 import _lib
+    from polar_pack_b200.polar_kernels import _pad_table, quantize_polar_bitpacked
+    M = 1
+    per_shape, tot_b, tot_t = {}, 0.0, 0.0
+    g = torch.Generator(device=dev)
+    g.manual_seed(21)
+    sh = stream.cuda_stream
+    for K, N in SHAPES:
+        base = torch.randn(K, N, generator=g, device=dev) * 0.02
+        w1 = base + torch.randn(K, N, generator=g, device=dev) * 0.002
+        w2 = base + torch.randn(K, N, generator=g, device=dev) * 0.002
+        packed, bmax, amp, cs, sn = quantize_polar_bitpacked(w1, w2)
+        del base, w1, w2
+        amp, cs, sn = _pad_table(amp, 64), _pad_table(cs, 1024), _pad_table(sn, 1024)
+        reps = max(2, -(-(400 << 20) // (K * N * 2)))
+        packs = [(packed.clone(), bmax.clone()) for _ in range(reps)]
+        x = torch.randn(M, K, generator=g, device=dev).half()
+        o1 = torch.empty(M, N, device=dev, dtype=torch.float16)
+        o2 = torch.empty_like(o1)
+        nb = _lib._size_t()
+        _lib.check(lib.pp_dual_gemm_workspace_bytes(M, N, K, N, 1, ctypes.byref(nb)))
+        ws = torch.zeros(max(nb.value, 256), dtype=torch.uint8, device=dev)
+        calls = [(x.data_ptr(), K, 1, pk.data_ptr(), N, 1, bm.data_ptr(), 32, amp.data_ptr(), cs.data_ptr(),
+                  sn.data_ptr(), o1.data_ptr(), o2.data_ptr(), N, 1, M, N, K, ws.data_ptr(), ws.numel(), sh)
+                 for pk, bm in packs]
+
+        def run():
+            for c in calls:
+                rc = lib.pp_dual_gemm(*c)
+                if rc:
+                    _lib.check(rc)
+        run()
+        torch.cuda.synchronize(dev)
+        graph = None
+        if not args.eager:
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph, stream=stream):
+                run()
+            graph.replay()
+            torch.cuda.synchronize(dev)
+        go = graph.replay if graph is not None else run
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        rounds = max(2, 80 // reps)
+        e0.record(stream)
+        for _ in range(rounds):
+            go()
+        e1.record(stream)
+        torch.cuda.synchronize(dev)
+        t = e0.elapsed_time(e1) / (rounds * reps)
+        b = 2 * K * N + 2 * (-(-K * N // 32)) + 2 * M * K + 4 * M * N
+        per_shape[f"{K}x{N}"] = {"us": round(t * 1e3, 2), "GB/s": round(b / (t * 1e-3) / 1e9, 1)}
+        tot_b += b
+        tot_t += t
+        del graph, packs, calls
+        torch.cuda.empty_cache()
+    peak, _ = measured_peak()
+    gbs = tot_b / (tot_t * 1e-3) / 1e9
+    return {"per_shape": per_shape, "GB/s": round(gbs, 1), "frac_of_measured_hbm": round(gbs / peak, 4),
+            "kernel": "dual_tma_kernel (batch 1, TMA engine)", "batch": M,
+            "what": "polar_dual_bitpacked on the sweep shapes (in x out), graph of back-to-back launches over "
+                    "replicas larger than L2, launch overlap on"}
 
 
 def run_decode_step(torch, dist, dev, args, world, rank, lib, stream):
@@ -850,6 +927,7 @@ def main():
     ap.add_argument("--eager", action="store_true", help="time eager launches instead of CUDA graphs")
     ap.add_argument("--no-overlap", action="store_true", help="launch kernels without programmatic overlap")
     ap.add_argument("--no-decode", action="store_true", help="skip the 3B decode-step leg")
+    ap.add_argument("--no-dual", action="store_true", help="skip the dual-pack kernel leg")
     ap.add_argument("--nccl-gather", action="store_true",
                     help="with N > 1 GPUs gather the outputs with an NCCL all-gather instead of peer stores")
     ap.add_argument("--shapes", default="", help="subset of the sweep as KxN,KxN (in x out), e.g. for profiling "
