@@ -21,7 +21,10 @@ configs[2]: 36 layers of qkv / o / gate_up / down launches plus the lm_head,
 batch 1) and reports 4-model decode tokens/s under
 ``config.decode_step_3b`` (``--no-decode`` skips it).  A third times the
 dual-pack kernel (2 models of 16-bit polar codes) on the sweep shapes at
-batch 1 under ``config.dual_gemv_b1`` (``--no-dual`` skips it).
+batch 1 under ``config.dual_gemv_b1`` (``--no-dual`` skips it), and a fourth
+the quad path at 16 and 64 batch rows (the tcgen05
+tile kernel where it applies) under ``config.batched_rows``
+(``--no-batched`` skips it).
 
 Metric: packed-stream GB/s = algorithmic bytes / device time, where the
 bytes of one Linear are 4*N*K (codes) + 12*P (plug index + values) +
@@ -391,6 +394,10 @@ def run_ours(args):
     decode = None
     if not args.no_decode and not args.shapes and M == 1:
         decode = run_decode_step(torch, dist, dev, args, world, rank, lib, stream)
+    # batched rows on the same shapes (one GPU's kernel time)
+    batched = None
+    if not args.no_batched and M == 1:
+        batched = run_batched_leg(torch, dev, args, lib, stream, sets)
     # the dual-pack kernel on the same shapes (one GPU's kernel time)
     dual = None
     if not args.no_dual and M == 1:
@@ -416,7 +423,8 @@ def run_ours(args):
                              ("; launch overlap on" if not args.no_overlap else ""),
                    "per_shape_gemv_kernel": per_shape,
                    "decode_step_3b": decode,
-                   "dual_gemv_b1": dual},
+                   "dual_gemv_b1": dual,
+                   "batched_rows": batched},
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(achieved / peak, 4), "peak_source": f"{peak_kind} hbm_gbs",
                      "kernel": "quad_gemv_kernel<NK=1,NB=1,PLUG=1> (file layout, batch 1, plugs fused)",
@@ -443,6 +451,74 @@ def run_ours(args):
         dist.destroy_process_group()
     if rank == 0:
         print(json.dumps(res))
+
+
+def run_batched_leg(torch, dev, args, lib, stream, sets, rows=(16, 64)):
+    """configs[3]-style batched rows on the sweep shapes, through the same
+    entry point as the step (pp_quad_linear_fused; above one row the plug
+    correction is its own kernel).  At more than 16 rows and N or K >= 4096
+    the tcgen05 tile kernel runs, else the mma.sync GEMV in 16-row chunks.
+    Per shape: a graph of back-to-back calls over the replica streams."""
+    from polar_pack_b200 import _lib
+    from polar_pack_b200.quadpack import quad_linear_workspace_bytes
+    sh = stream.cuda_stream
+    g = torch.Generator(device=dev)
+    g.manual_seed(31)
+    res = {}
+    for M in rows:
+        per_shape, tot_b, tot_f, tot_t = {}, 0.0, 0.0, 0.0
+        for j, (K, N) in enumerate(SHAPES):
+            x = torch.randn(M, K, generator=g, device=dev).half()
+            nb = max(quad_linear_workspace_bytes(M, st[j].N, st[j].K) for st in sets)
+            ws = torch.zeros(max(nb, 256), dtype=torch.uint8, device=dev)
+            calls, keep = [], []
+            for st in sets:
+                l = st[j]
+                outs = [torch.empty((M, l.N), dtype=torch.float16, device=dev) for _ in range(4)]
+                keep.append(outs)
+                calls.append((x.data_ptr(), x.stride(0), x.stride(1), l.codes.data_ptr(), l.K,
+                              _lib.ptr(l.plug_idx), _lib.ptr(l.plug_vals), _lib.ptr(l.plug_window_base),
+                              ctypes.c_uint32(l.offset & 0xFFFFFFFF), _lib.ptr(l.unit_plugs),
+                              _lib.ptr(l.unit_plug_off), l.pack.tables.data_ptr(), _lib.floats4(l.pack.scales),
+                              _lib.ptrs(outs, 4), outs[0].stride(0), outs[0].stride(1), M, l.N, l.K,
+                              ws.data_ptr(), ws.numel(), sh))
+
+            def run():
+                for c in calls:
+                    rc = lib.pp_quad_linear_fused(*c)
+                    if rc:
+                        _lib.check(rc)
+            run()
+            torch.cuda.synchronize(dev)
+            graph = None
+            if not args.eager:
+                graph = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(graph, stream=stream):
+                    run()
+                graph.replay()
+                torch.cuda.synchronize(dev)
+            go = graph.replay if graph is not None else run
+            rounds = 6
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            for _ in range(rounds):
+                go()
+            e1.record(stream)
+            torch.cuda.synchronize(dev)
+            t = e0.elapsed_time(e1) / (rounds * len(calls))
+            b = statistics.mean(layer_bytes(st[j].N, st[j].K, st[j].p_hi - st[j].p_lo, M) for st in sets)
+            fl = 2.0 * M * K * N * 4
+            path = "tcgen05" if M > 16 and (N >= 4096 or K >= 4096) else "mma.sync GEMV"
+            per_shape[f"{K}x{N}"] = {"us": round(t * 1e3, 2), "GB/s": round(b / (t * 1e-3) / 1e9, 1),
+                                     "TFLOP/s": round(fl / (t * 1e-3) / 1e12, 1), "path": path}
+            tot_b, tot_f, tot_t = tot_b + b, tot_f + fl, tot_t + t
+            del graph, calls, keep
+        res[f"M{M}"] = {"per_shape": per_shape, "GB/s": round(tot_b / (tot_t * 1e-3) / 1e9, 1),
+                        "TFLOP/s": round(tot_f / (tot_t * 1e-3) / 1e12, 1)}
+    torch.cuda.empty_cache()
+    res["what"] = ("batched rows through pp_quad_linear_fused on the sweep shapes (in x out), 4 models; "
+                   "TFLOP/s = 8 M K N / time; graph of back-to-back calls over the replica streams")
+    return res
 
 
 def run_dual_leg(torch, dev, args, lib, stream):
@@ -928,6 +1004,7 @@ def main():
     ap.add_argument("--no-overlap", action="store_true", help="launch kernels without programmatic overlap")
     ap.add_argument("--no-decode", action="store_true", help="skip the 3B decode-step leg")
     ap.add_argument("--no-dual", action="store_true", help="skip the dual-pack kernel leg")
+    ap.add_argument("--no-batched", action="store_true", help="skip the batched-rows leg")
     ap.add_argument("--nccl-gather", action="store_true",
                     help="with N > 1 GPUs gather the outputs with an NCCL all-gather instead of peer stores")
     ap.add_argument("--shapes", default="", help="subset of the sweep as KxN,KxN (in x out), e.g. for profiling "

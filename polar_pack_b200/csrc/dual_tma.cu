@@ -194,6 +194,8 @@ struct DualTOp {
   __device__ __forceinline__ void store(int model, int, int f, float v) const {
     p.out[model][(int64_t)f * p.ldo_n] = __float2half_rn(v);
   }
+  __device__ __forceinline__ float corr_at(int, int, int) const { return 0.f; }
+  __device__ __forceinline__ void store_raw(int model, int bat, int f, float v) const { store(model, bat, f, v); }
 };
 
 // Table words are staged and the per-CTA tables filled before the first

@@ -361,6 +361,32 @@ struct TmaRing {
   }
 };
 
+// Stores U reduced elements e0, e0 + step, ... (< nval) of tile T.  The
+// elements' plug corrections (Op::corr_at) are all loaded before the first
+// store: a load after a store would otherwise wait for it, as the compiler
+// cannot rule out that output and correction alias.
+template <class Op, int U>
+__device__ __forceinline__ void store_outputs(const Op& op, int e0, int step, int nval, int T, const float (&sv)[U]) {
+  constexpr int TW = Op::kTileW;
+  const int M = op.M();
+  float cv[U];
+  int ob[U], fb[U];
+#pragma unroll
+  for (int u = 0; u < U; ++u) {
+    const int e = e0 + step * u;
+    const int o = e / (M * TW);
+    const int rem = e - o * M * TW;
+    const int bat = rem / TW;
+    const int f = T * TW + (rem - bat * TW);
+    ob[u] = o * 65536 + bat;
+    fb[u] = (e < nval && f < op.N()) ? f : -1;
+    cv[u] = fb[u] >= 0 ? op.corr_at(o, bat, f) : 0.f;
+  }
+#pragma unroll
+  for (int u = 0; u < U; ++u)
+    if (fb[u] >= 0) op.store_raw(ob[u] >> 16, ob[u] & 0xFFFF, fb[u], sv[u] + cv[u]);
+}
+
 // Ends split tile T of warp `warp` (slot `which`), see above.
 template <class Op>
 __device__ __forceinline__ void close_split(Op& op, const Partition& pt, const CtaTables& tb, float* red,
@@ -390,20 +416,43 @@ __device__ __forceinline__ void close_split(Op& op, const Partition& pt, const C
   __threadfence_block();
   const bool inside = T * upt >= cu0 && T * upt + upt <= cu1;
   float* gslot = pt.slots + ((int64_t)blockIdx.x * 2 + (T == tb.wtile[0] ? 0 : 1)) * (int64_t)nval;
-  for (int e = lane; e < nval; e += 32) {
-    float sum = 0.f;
-    for (int w = wf; w < NW && tb.wstart[w] < x1; ++w) {
-      if (tb.wstart[w + 1] == tb.wstart[w]) continue;
-      sum += red[(w * 2 + (tb.wtile[w] == T ? 0 : 1)) * nval + e];
+  // one element per lane (batch 1): plain stores; larger tiles take eight
+  // elements per lane at a time, whose plug corrections are loaded before
+  // any of them is stored (store_outputs)
+  if (nval <= 32) {
+    if (lane < nval) {
+      float sum = 0.f;
+      for (int w = wf; w < NW && tb.wstart[w] < x1; ++w) {
+        if (tb.wstart[w + 1] == tb.wstart[w]) continue;
+        sum += red[(w * 2 + (tb.wtile[w] == T ? 0 : 1)) * nval + lane];
+      }
+      if (inside) {
+        const float sv[1] = {sum};
+        store_outputs<Op, 1>(op, lane, 32, nval, T, sv);
+      } else {
+        __stcg(gslot + lane, sum);
+      }
+    }
+  } else
+  for (int e0 = lane; e0 < nval; e0 += 32 * 8) {
+    float sv[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int e = e0 + 32 * u;
+      float sum = 0.f;
+      if (e < nval)
+        for (int w = wf; w < NW && tb.wstart[w] < x1; ++w) {
+          if (tb.wstart[w + 1] == tb.wstart[w]) continue;
+          sum += red[(w * 2 + (tb.wtile[w] == T ? 0 : 1)) * nval + e];
+        }
+      sv[u] = sum;
     }
     if (inside) {
-      const int o = e / (M * TW);
-      const int rem = e - o * M * TW;
-      const int bat = rem / TW;
-      const int f = T * TW + (rem - bat * TW);
-      if (f < op.N()) op.store(o, bat, f, sum);
+      store_outputs<Op, 8>(op, e0, 32, nval, T, sv);
     } else {
-      __stcg(gslot + e, sum);
+#pragma unroll
+      for (int u = 0; u < 8; ++u)
+        if (e0 + 32 * u < nval) __stcg(gslot + e0 + 32 * u, sv[u]);
     }
   }
   if (inside) return;
@@ -418,18 +467,32 @@ __device__ __forceinline__ void close_split(Op& op, const Partition& pt, const C
   lastc = __shfl_sync(0xffffffffu, lastc, 0);
   if (!lastc) return;
   __threadfence();
-  for (int e = lane; e < nval; e += 32) {
-    float sum = 0.f;
-    for (int c = c_first; c <= c_last; ++c) {
-      // only the first contributor can have started before the tile
-      const int w = (c == c_first && pt.cta_start[c] < T * upt) ? 1 : 0;
-      sum += __ldcg(pt.slots + ((int64_t)c * 2 + w) * (int64_t)nval + e);
+  if (nval <= 32) {
+    if (lane < nval) {
+      float sum = 0.f;
+      for (int c = c_first; c <= c_last; ++c) {
+        const int w = (c == c_first && pt.cta_start[c] < T * upt) ? 1 : 0;
+        sum += __ldcg(pt.slots + ((int64_t)c * 2 + w) * (int64_t)nval + lane);
+      }
+      const float sv[1] = {sum};
+      store_outputs<Op, 1>(op, lane, 32, nval, T, sv);
     }
-    const int o = e / (M * TW);
-    const int rem = e - o * M * TW;
-    const int bat = rem / TW;
-    const int f = T * TW + (rem - bat * TW);
-    if (f < op.N()) op.store(o, bat, f, sum);
+  } else
+  for (int e0 = lane; e0 < nval; e0 += 32 * 8) {
+    float sv[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int e = e0 + 32 * u;
+      float sum = 0.f;
+      if (e < nval)
+        for (int c = c_first; c <= c_last; ++c) {
+          // only the first contributor can have started before the tile
+          const int w = (c == c_first && pt.cta_start[c] < T * upt) ? 1 : 0;
+          sum += __ldcg(pt.slots + ((int64_t)c * 2 + w) * (int64_t)nval + e);
+        }
+      sv[u] = sum;
+    }
+    store_outputs<Op, 8>(op, e0, 32, nval, T, sv);
   }
   if (lane == 0) pt.counters[c_last] = 0;
 }

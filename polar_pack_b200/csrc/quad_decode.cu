@@ -331,6 +331,7 @@ struct PlugCorrParams {
   int M, N, K, W;
   float* corr;               // corr[q * ldq + m * N + n]
   int64_t ldq;               // model stride of corr (M * N for a dense [4][M][N] buffer)
+  __half* xt;                // M > 1: scratch for x transposed, K x 128 halves
 };  // (declared identically in quad_gemv.cu)
 
 // A warp owns RPW consecutive rows, whose entries are one contiguous range
@@ -424,9 +425,157 @@ __global__ void __launch_bounds__(256) quad_plug_corr_kernel(const PlugCorrParam
   }
 }
 
+// Batched rows (M > 1): the correction is a sparse (N x K) times dense
+// (K x M) product.  x is first transposed into scratch, xt[k * ldt + m], so
+// the M activations of one plug column are one contiguous row.  WPR warps
+// share a row, each a contiguous range of its entries.  A warp loads 32
+// entries at a time (lane l entry l, one coalesced load) and hands them out
+// by shuffle: its lanes form 32 / MPAD groups of MPAD lanes, lane m of a
+// group holding batch rows m, m + 32, ... (MPL of them), and the groups take
+// the entries round robin, four activation loads in flight per lane.  The
+// row's warps are summed in warp order through shared memory and the
+// groups in a fixed butterfly, so results are deterministic.
+__global__ void transpose_x_kernel(const __half* x, int64_t ldx_m, int M, int K, __half* xt, int ldt) {
+  pdl_launch_dependents();
+  pdl_wait();  // activations may come from the previous kernel
+  const int64_t total = (int64_t)K * M;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t m = i / K, k = i - m * K;  // reads along k are coalesced
+    xt[k * ldt + m] = x[m * ldx_m + k];
+  }
+}
+
+template <int MPAD, int MPL, int WPR>
+__global__ void __launch_bounds__(256) quad_plug_corr_t_kernel(const PlugCorrParams p, int ldt) {
+  constexpr int EG = 32 / MPAD, RPC = 8 / WPR;
+  __shared__ float red[8][MPL][4][32];
+  pdl_launch_dependents();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, eg = lane / MPAD, ml = lane % MPAD;
+  const int row = blockIdx.x * RPC + warp / WPR, wr = warp % WPR;
+  float acc[MPL][4];
+#pragma unroll
+  for (int i = 0; i < MPL; ++i)
+#pragma unroll
+    for (int q = 0; q < 4; ++q) acc[i][q] = 0.f;
+  if (row < p.N) {
+    const uint32_t j0 = __ldg(p.wbase + (int64_t)row * p.W), j1 = __ldg(p.wbase + (int64_t)(row + 1) * p.W);
+    const uint32_t a = j0 + (uint32_t)((uint64_t)(j1 - j0) * wr / WPR);
+    const uint32_t b = j0 + (uint32_t)((uint64_t)(j1 - j0) * (wr + 1) / WPR);
+    const uint32_t rowbase = p.base_lo32 + (uint32_t)row * (uint32_t)p.K;
+    pdl_wait();  // xt is written by the transpose launched just before
+    for (uint32_t jb = a; jb < b; jb += 32u) {
+      const uint32_t j = jb + (uint32_t)lane;
+      uint32_t kk = 0u;
+      uint2 vv = make_uint2(0u, 0u);  // past the range: zero values, column 0
+      if (j < b) {
+        kk = __ldg(p.plug_idx + j) - rowbase;
+        vv = __ldg(p.plug_vals + j);
+      }
+#pragma unroll
+      for (int e = 0; e < 32; e += EG * 4) {
+        uint32_t k4[4], v4x[4], v4y[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const int src = e + EG * u + eg;
+          k4[u] = __shfl_sync(0xffffffffu, kk, src);
+          v4x[u] = __shfl_sync(0xffffffffu, vv.x, src);
+          v4y[u] = __shfl_sync(0xffffffffu, vv.y, src);
+        }
+        float xv[4][MPL];
+#pragma unroll
+        for (int u = 0; u < 4; ++u)
+#pragma unroll
+          for (int i = 0; i < MPL; ++i) xv[u][i] = __half2float(p.xt[(int64_t)k4[u] * ldt + ml + 32 * i]);
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const float2 va = __half22float2(u2h(v4x[u])), vb = __half22float2(u2h(v4y[u]));
+#pragma unroll
+          for (int i = 0; i < MPL; ++i) {
+            acc[i][0] = fmaf(va.x, xv[u][i], acc[i][0]);
+            acc[i][1] = fmaf(va.y, xv[u][i], acc[i][1]);
+            acc[i][2] = fmaf(vb.x, xv[u][i], acc[i][2]);
+            acc[i][3] = fmaf(vb.y, xv[u][i], acc[i][3]);
+          }
+        }
+      }
+    }
+  } else {
+    pdl_wait();
+  }
+  if (WPR > 1) {
+#pragma unroll
+    for (int i = 0; i < MPL; ++i)
+#pragma unroll
+      for (int q = 0; q < 4; ++q) red[warp][i][q][lane] = acc[i][q];
+    __syncthreads();
+    if (wr != 0) return;
+#pragma unroll
+    for (int i = 0; i < MPL; ++i)
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        float v = red[warp][i][q][lane];
+#pragma unroll
+        for (int w = 1; w < WPR; ++w) v += red[warp + w][i][q][lane];
+        acc[i][q] = v;
+      }
+  }
+#pragma unroll
+  for (int o = MPAD; o < 32; o <<= 1)
+#pragma unroll
+    for (int i = 0; i < MPL; ++i)
+#pragma unroll
+      for (int q = 0; q < 4; ++q) acc[i][q] += __shfl_xor_sync(0xffffffffu, acc[i][q], o);
+  if (eg != 0 || row >= p.N) return;
+#pragma unroll
+  for (int i = 0; i < MPL; ++i) {
+    const int m = ml + 32 * i;
+    if (m < p.M)
+#pragma unroll
+      for (int q = 0; q < 4; ++q) p.corr[(int64_t)q * p.ldq + (int64_t)m * p.N + row] = acc[i][q];
+  }
+}
+
+// Warps per row for about 64 entries per warp, 1..8, from the row length:
+// the packer caps plugs at 5% of the codes, so a row holds about K / 20.
+// (The count itself lives on the device; the choice only affects speed.)
+template <int MPAD, int MPL>
+int launch_corr_t(const PlugCorrParams& prm, cudaStream_t s) {
+  const int ldt = MPAD * MPL;
+  const int64_t total = (int64_t)prm.K * prm.M;
+  const int tg = (int)(cdiv(total, 256) < 4096 ? cdiv(total, 256) : 4096);
+  int rc = launch_kernel("transpose_x_kernel", launch_overlap(), transpose_x_kernel, dim3(tg), dim3(256), 0, s,
+                         prm.x, prm.ldx_m, prm.M, prm.K, prm.xt, ldt);
+  if (rc) return rc;
+  const int64_t per_row = prm.K / 20;
+  const bool ov = launch_overlap();
+  if (per_row >= 384)
+    return launch_kernel("quad_plug_corr_t_kernel", ov, quad_plug_corr_t_kernel<MPAD, MPL, 8>,
+                         dim3((unsigned)prm.N), dim3(256), 0, s, prm, ldt);
+  if (per_row >= 192)
+    return launch_kernel("quad_plug_corr_t_kernel", ov, quad_plug_corr_t_kernel<MPAD, MPL, 4>,
+                         dim3((unsigned)cdiv(prm.N, 2)), dim3(256), 0, s, prm, ldt);
+  if (per_row >= 96)
+    return launch_kernel("quad_plug_corr_t_kernel", ov, quad_plug_corr_t_kernel<MPAD, MPL, 2>,
+                         dim3((unsigned)cdiv(prm.N, 4)), dim3(256), 0, s, prm, ldt);
+  return launch_kernel("quad_plug_corr_t_kernel", ov, quad_plug_corr_t_kernel<MPAD, MPL, 1>,
+                       dim3((unsigned)cdiv(prm.N, 8)), dim3(256), 0, s, prm, ldt);
+}
+
 int launch_plug_corr(const PlugCorrParams& prm, cudaStream_t s) {
   const int warps = 8;
   const bool ov = launch_overlap();
+  if (prm.M > 1 && prm.xt) {
+    if (prm.M > 128) {
+      set_error("plug correction: at most 128 batch rows per launch");
+      return PP_ERR_INVALID;
+    }
+    if (prm.M <= 4) return launch_corr_t<4, 1>(prm, s);
+    if (prm.M <= 8) return launch_corr_t<8, 1>(prm, s);
+    if (prm.M <= 16) return launch_corr_t<16, 1>(prm, s);
+    if (prm.M <= 32) return launch_corr_t<32, 1>(prm, s);
+    if (prm.M <= 64) return launch_corr_t<32, 2>(prm, s);
+    return launch_corr_t<32, 4>(prm, s);
+  }
   if (prm.M == 1) {
     if (prm.K <= 4096) {  // short rows: two per warp
       const int grid = (int)cdiv(prm.N, warps * 2);

@@ -48,8 +48,12 @@ struct PlugCorrParams {
   int M, N, K, W;
   float* corr;
   int64_t ldq;
+  __half* xt;  // M > 1: scratch for x transposed, K x 128 halves
 };
 int launch_plug_corr(const PlugCorrParams& prm, cudaStream_t s);
+
+// workspace for the transposed activations of the batched plug correction
+inline size_t xt_bytes(int64_t K) { return ((size_t)K * 128 * 2 + 255) / 256 * 256; }
 
 // quad_tc.cu: batched tensor-core path (file layout, prepared tables)
 bool quad_tc_ok(int64_t M, int64_t N, int64_t K, const uint32_t* codes, int64_t ldw, const void* x, int64_t ldx_m,
@@ -398,25 +402,45 @@ struct QuadOp {
     }
   }
 
+  // The plug corrections of a batch tile are loaded before its outputs are
+  // stored: otherwise each load would wait for the store before it (the
+  // compiler cannot rule out that they alias).
   __device__ __forceinline__ void store_tile(int tile) {
 #pragma unroll
     for (int t = 0; t < kT; ++t) {
       const int f = tile * kTileW + (NK ? pr : 4 * g + t);
       if (f >= Nv) continue;
 #pragma unroll
-      for (int nb = 0; nb < NB; ++nb)
+      for (int nb = 0; nb < NB; ++nb) {
+        float cv[2][4];
 #pragma unroll
         for (int h = 0; h < 2; ++h)
 #pragma unroll
           for (int j = 0; j < 4; ++j) {
             const int bat = nb * 8 + 2 * c + (j & 1);
-            if (bat < Mv) store(2 * h + (j >> 1), bat, f, acc[t][nb][h][j]);
+            cv[h][j] = (p.corr && bat < Mv) ? __ldcg(p.corr + ((int64_t)(2 * h + (j >> 1)) * Mv + bat) * Nv + f) : 0.f;
           }
+#pragma unroll
+        for (int h = 0; h < 2; ++h)
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const int bat = nb * 8 + 2 * c + (j & 1);
+            if (bat < Mv) store_raw(2 * h + (j >> 1), bat, f, acc[t][nb][h][j] + cv[h][j]);
+          }
+      }
     }
   }
 
+  __device__ __forceinline__ float corr_at(int model, int bat, int f) const {
+    return p.corr ? __ldcg(p.corr + ((int64_t)model * Mv + bat) * Nv + f) : 0.f;
+  }
+
   __device__ __forceinline__ void store(int model, int bat, int f, float v) const {
-    if (p.corr) v += p.corr[((int64_t)model * Mv + bat) * Nv + f];
+    store_raw(model, bat, f, v + corr_at(model, bat, f));
+  }
+
+  // v already includes the plug correction
+  __device__ __forceinline__ void store_raw(int model, int bat, int f, float v) const {
     const __half h = __float2half_rn(v * p.scale[model]);
     if (p.gather.world) {  // batch 1: element (model, row0 + f) of every rank's buffer
       const int64_t o = (int64_t)model * p.gather.ld + p.gather.row0 + f;
@@ -812,10 +836,11 @@ size_t quad_ws_bytes(bool nk, int64_t M, int64_t N, int64_t K, bool plug) {
   const int sms = device_sm_count(current_device());
   const int64_t Mc = M < 16 ? M : 16;
   if (Mc <= 0) return 0;
-  size_t need = quad_plan(nk, Mc, N, K, sms > 0 ? sms : 148).total() + (plug ? corr_bytes(N) : 0);
+  const size_t xt = plug && M > 1 ? xt_bytes(K) : 0;
+  size_t need = quad_plan(nk, Mc, N, K, sms > 0 ? sms : 148).total() + (plug ? corr_bytes(N) : 0) + xt;
   if (nk && M > 16) {  // the batched tensor-core path (taken with prepared tables)
     const size_t tc = kCounterBytes + (plug ? tc_corr_bytes(M, N) : 0) +
-                      quad_tc_slots_bytes(M, N, K, sms > 0 ? sms : 148);
+                      quad_tc_slots_bytes(M, N, K, sms > 0 ? sms : 148) + xt;
     need = tc > need ? tc : need;
   }
   return need;
@@ -905,7 +930,8 @@ static int quad_run(const void* a, int64_t lda_m, int64_t lda_k, const uint32_t*
   if (tables && nk && quad_tc_ok(M, N, K, codes, ldc_n, a, lda_m, lda_k)) {
     // batched tensor-core path: every code decoded once for up to 128 batch rows
     const size_t csz = plug ? tc_corr_bytes(M, N) : 0;
-    const size_t need = kCounterBytes + csz + quad_tc_slots_bytes(M, N, K, sms);
+    const size_t ssz = quad_tc_slots_bytes(M, N, K, sms);
+    const size_t need = kCounterBytes + csz + ssz + (plug ? xt_bytes(K) : 0);
     if (ws_bytes < need || !ws || !aligned(ws, 256)) {
       set_error("workspace of %zu bytes (256-byte aligned, zero-filled) required, got %zu", need, ws_bytes);
       return PP_ERR_WORKSPACE;
@@ -913,18 +939,18 @@ static int quad_run(const void* a, int64_t lda_m, int64_t lda_k, const uint32_t*
     int* counters = reinterpret_cast<int*>(ws);
     float* corr = plug ? reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(ws) + kCounterBytes) : nullptr;
     float* slots = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(ws) + kCounterBytes + csz);
+    __half* xt = plug ? reinterpret_cast<__half*>(reinterpret_cast<uint8_t*>(ws) + kCounterBytes + csz + ssz)
+                      : nullptr;
     for (int64_t m0 = 0; m0 < M; m0 += kTcLaunchRows) {
       const int64_t Mc = (M - m0) < kTcLaunchRows ? (M - m0) : kTcLaunchRows;
       const __half* xc = reinterpret_cast<const __half*>(a) + m0 * lda_m;
       void* oc[4];
       for (int i = 0; i < 4; ++i) oc[i] = reinterpret_cast<__half*>(out[i]) + m0 * ldo_m;
-      if (plug)
-        for (int64_t m1 = 0; m1 < Mc; m1 += 16) {
-          const int64_t Mcc = (Mc - m1) < 16 ? (Mc - m1) : 16;
-          PlugCorrParams cp{xc + m1 * lda_m, lda_m, plug_idx, reinterpret_cast<const uint2*>(plug_vals), wbase,
-                            base_lo32, (int)Mcc, (int)N, (int)K, (int)cdiv(K, 64), corr + m1 * N, Mc * N};
-          if ((rc = launch_plug_corr(cp, s))) return rc;
-        }
+      if (plug) {  // all rows of the launch in one correction
+        PlugCorrParams cp{xc, lda_m, plug_idx, reinterpret_cast<const uint2*>(plug_vals), wbase, base_lo32,
+                          (int)Mc, (int)N, (int)K, (int)cdiv(K, 64), corr, Mc * N, xt};
+        if ((rc = launch_plug_corr(cp, s))) return rc;
+      }
       if ((rc = launch_quad_tc(xc, lda_m, codes, ldc_n, tables, scales, oc, ldo_m, ldo_n, corr, Mc * N, Mc, N, K,
                                counters, slots, s)))
         return rc;
@@ -953,12 +979,15 @@ static int quad_run(const void* a, int64_t lda_m, int64_t lda_k, const uint32_t*
                : encode_tmap_u32_2d(&prm.tmap, codes, (uint64_t)N, (uint64_t)K, (uint64_t)ldc_k * 4, 32, 16)))
     return rc;
   const size_t csz = plug ? corr_bytes(N) : 0;
-  const size_t need = quad_plan(nk, M < 16 ? M : 16, N, K, sms).total() + csz;
+  const size_t plan_bytes = quad_plan(nk, M < 16 ? M : 16, N, K, sms).total();
+  const size_t need = plan_bytes + csz + (plug && M > 1 ? xt_bytes(K) : 0);
   if (ws_bytes < need || (need && !ws) || !aligned(ws, 256)) {
     set_error("workspace of %zu bytes (256-byte aligned, zero-filled) required, got %zu", need, ws_bytes);
     return PP_ERR_WORKSPACE;
   }
   float* corr = plug ? reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(ws) + kCounterBytes) : nullptr;
+  __half* xt = plug && M > 1 ? reinterpret_cast<__half*>(reinterpret_cast<uint8_t*>(ws) + plan_bytes + csz)
+                             : nullptr;
   // batch rows in chunks of 16: each chunk is one launch over the codes
   for (int64_t m0 = 0; m0 < M; m0 += 16) {
     const int64_t Mc = (M - m0) < 16 ? (M - m0) : 16;
@@ -987,7 +1016,7 @@ static int quad_run(const void* a, int64_t lda_m, int64_t lda_k, const uint32_t*
     }
     if (plug) {
       PlugCorrParams cp{prm.x, lda_m, plug_idx, reinterpret_cast<const uint2*>(plug_vals), wbase, base_lo32,
-                        (int)Mc, (int)N, (int)K, (int)cdiv(K, 64), corr, Mc * N};
+                        (int)Mc, (int)N, (int)K, (int)cdiv(K, 64), corr, Mc * N, xt};
       if ((rc = launch_plug_corr(cp, s))) return rc;
     }
     if ((rc = launch_plan(pl, nk, Mc, prm, ws, csz, s))) return rc;

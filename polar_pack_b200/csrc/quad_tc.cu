@@ -305,16 +305,25 @@ __global__ void __launch_bounds__(kTcThreads, 1) quad_tc_kernel(const __grid_con
           float v[16];
           tc_ld16(tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)(q * p.nmma + cb), v);
           if (!fin) continue;
+          if (split_k) {
+#pragma unroll
+            for (int j = 0; j < 16; ++j) __stcg(slot + ((int64_t)q * p.nmma + cb + j) * kTcRows + rl, v[j]);
+            continue;
+          }
+          // the chunk's plug corrections are loaded before any output is
+          // stored: otherwise each load would wait for the store before it
+          // (the compiler cannot rule out that they alias)
+          float cv[16];
+#pragma unroll
+          for (int j = 0; j < 16; ++j)
+            cv[j] = (p.corr && cb + j < p.M && row < p.N)
+                        ? __ldcg(p.corr + (int64_t)q * p.corr_q + (int64_t)(cb + j) * p.N + row)
+                        : 0.f;
 #pragma unroll
           for (int j = 0; j < 16; ++j) {
             const int m = cb + j;
-            if (split_k) {
-              __stcg(slot + ((int64_t)q * p.nmma + m) * kTcRows + rl, v[j]);
-            } else if (m < p.M && row < p.N) {
-              float a = v[j];
-              if (p.corr) a += p.corr[(int64_t)q * p.corr_q + (int64_t)m * p.N + row];
-              p.out[q][(int64_t)m * p.ldo_m + (int64_t)row * p.ldo_n] = __float2half_rn(a * p.scale[q]);
-            }
+            if (m < p.M && row < p.N)
+              p.out[q][(int64_t)m * p.ldo_m + (int64_t)row * p.ldo_n] = __float2half_rn((v[j] + cv[j]) * p.scale[q]);
           }
         }
     }

@@ -186,3 +186,14 @@ def test_long_partition_runs_in_row_chunks(cuda):
         assert oq.rel_err(a[k], b[k]) <= TOL, k
     del lin
     torch.cuda.empty_cache()
+
+
+@pytest.mark.parametrize("M", [3, 17, 64, 130])
+def test_batched_plugs_tensor_core_path(cuda, M):
+    """N >= 4096 above 16 rows takes the tcgen05 kernel, with the plug
+    correction for all of a launch's rows (up to 128) in one kernel over
+    the transposed activations; 130 rows are launches of 128 and 2."""
+    lin = Linear(cuda, 4096, 320, 0.05, True, seed=100 + M)
+    x = np.random.default_rng(M).normal(0, 1, size=(M, 320)).astype(np.float16)
+    y = lin.run(torch.from_numpy(x).to(cuda))
+    check_against_oracle(lin, y, x)
