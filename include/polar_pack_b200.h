@@ -100,7 +100,11 @@ PP_API int pp_quad_gemm(const void* a, int64_t lda_m, int64_t lda_k,
  * kernel layout up to at least M = 6 on a 148-SM device); larger plans fail
  * with PP_ERR_WORKSPACE before anything is enqueued.  All calls on a device
  * share the one array: calls that can overlap (different streams or host
- * threads) race on it and must be serialised by the caller.
+ * threads) race on it and must be serialised by the caller.  The first call
+ * on a device looks up the array's device address (cudaGetSymbolAddress,
+ * with that device current) and keeps it; make that first call before any
+ * stream capture on the device.  Each call clears the counters at the front
+ * of the array on its stream before the kernel runs.
  */
 PP_API int pp_quad_gemm_static_scratch(const void* a, int64_t lda_m, int64_t lda_k,
                                        const uint32_t* codes, int64_t ldc_k, int64_t ldc_n,

@@ -17,6 +17,12 @@
 // the same time (on different streams, or from different host threads)
 // race on it and corrupt each other's results; such callers must
 // serialise them.
+//
+// The host cannot pass g_quad_scratch itself to a kernel: in host code the
+// name is a host-side stand-in, not a device address.  The first call on a
+// device therefore looks the address up with cudaGetSymbolAddress while
+// that device is current and keeps it for later calls; that first call
+// should come before any stream capture on the device.
 #include <mutex>
 
 #include "pp_common.cuh"
