@@ -387,23 +387,31 @@ __device__ __forceinline__ void store_outputs(const Op& op, int e0, int step, in
     if (fb[u] >= 0) op.store_raw(ob[u] >> 16, ob[u] & 0xFFFF, fb[u], sv[u] + cv[u]);
 }
 
-// Ends split tile T of warp `warp` (slot `which`), see above.
+// Ends split tile T of warp `warp` (slot `which`), see above.  The warps
+// that hold units of T are found in parallel (lane w checks warp w) and
+// their partial-slot offsets broadcast once, so the closing warp's sums
+// issue independent loads; the additions stay in warp order.
 template <class Op>
 __device__ __forceinline__ void close_split(Op& op, const Partition& pt, const CtaTables& tb, float* red,
                                             int warp, int T, int which, int cu0, int cu1) {
   constexpr int NW = Op::kWarps;
-  constexpr int TW = Op::kTileW;
+  static_assert(NW <= 31, "one lane per warp of the CTA, plus the range end");
   const int lane = threadIdx.x & 31;
   const int upt = pt.upt;
   const int M = op.M();
-  const int nval = Op::kNOut * M * TW;
+  const int nval = Op::kNOut * M * Op::kTileW;
   op.write_partial(red + (warp * 2 + which) * nval, M);
   const int x0 = T * upt > cu0 ? T * upt : cu0;                    // first unit of T in the CTA
   const int x1 = T * upt + upt < cu1 ? T * upt + upt : cu1;        // end of T in the CTA
-  int wf = warp;
-  while (wf > 0 && tb.wstart[wf] > x0) --wf;                       // warp holding x0
-  int n = 0;
-  for (int w = wf; w < NW && tb.wstart[w] < x1; ++w) n += tb.wstart[w + 1] > tb.wstart[w] ? 1 : 0;
+  // lane w < NW: warp w's range [s0, s1) overlaps [x0, x1); the tile is
+  // the warp's first (slot 0) iff the warp starts in it
+  const int wl = lane < NW ? lane : NW;
+  const int s0 = tb.wstart[wl], s1 = tb.wstart[lane < NW ? lane + 1 : NW];
+  const bool holds = lane < NW && s1 > s0 && s0 < x1 && s1 > x0;
+  const int myoff = holds ? (2 * lane + (tb.wtile[wl] == T ? 0 : 1)) * nval : -1;
+  const uint32_t mask = __ballot_sync(0xffffffffu, holds);
+  const int wf = __ffs((int)mask) - 1;  // holds x0, owns the tile's counter
+  const int n = __popc(mask);
   __syncwarp();
   int last = 0;
   if (lane == 0) {
@@ -412,6 +420,9 @@ __device__ __forceinline__ void close_split(Op& op, const Partition& pt, const C
   }
   last = __shfl_sync(0xffffffffu, last, 0);
   if (!last) return;
+  int so[NW];
+#pragma unroll
+  for (int w = 0; w < NW; ++w) so[w] = __shfl_sync(0xffffffffu, myoff, w);
   __syncwarp();
   __threadfence_block();
   const bool inside = T * upt >= cu0 && T * upt + upt <= cu1;
@@ -422,10 +433,9 @@ __device__ __forceinline__ void close_split(Op& op, const Partition& pt, const C
   if (nval <= 32) {
     if (lane < nval) {
       float sum = 0.f;
-      for (int w = wf; w < NW && tb.wstart[w] < x1; ++w) {
-        if (tb.wstart[w + 1] == tb.wstart[w]) continue;
-        sum += red[(w * 2 + (tb.wtile[w] == T ? 0 : 1)) * nval + lane];
-      }
+#pragma unroll
+      for (int w = 0; w < NW; ++w)
+        if (so[w] >= 0) sum += red[so[w] + lane];
       if (inside) {
         const float sv[1] = {sum};
         store_outputs<Op, 1>(op, lane, 32, nval, T, sv);
@@ -437,15 +447,13 @@ __device__ __forceinline__ void close_split(Op& op, const Partition& pt, const C
   for (int e0 = lane; e0 < nval; e0 += 32 * 8) {
     float sv[8];
 #pragma unroll
-    for (int u = 0; u < 8; ++u) {
-      const int e = e0 + 32 * u;
-      float sum = 0.f;
-      if (e < nval)
-        for (int w = wf; w < NW && tb.wstart[w] < x1; ++w) {
-          if (tb.wstart[w + 1] == tb.wstart[w]) continue;
-          sum += red[(w * 2 + (tb.wtile[w] == T ? 0 : 1)) * nval + e];
-        }
-      sv[u] = sum;
+    for (int u = 0; u < 8; ++u) sv[u] = 0.f;
+#pragma unroll
+    for (int w = 0; w < NW; ++w) {
+      if (so[w] < 0) continue;
+#pragma unroll
+      for (int u = 0; u < 8; ++u)
+        if (e0 + 32 * u < nval) sv[u] += red[so[w] + e0 + 32 * u];
     }
     if (inside) {
       store_outputs<Op, 8>(op, e0, 32, nval, T, sv);
@@ -481,16 +489,14 @@ __device__ __forceinline__ void close_split(Op& op, const Partition& pt, const C
   for (int e0 = lane; e0 < nval; e0 += 32 * 8) {
     float sv[8];
 #pragma unroll
-    for (int u = 0; u < 8; ++u) {
-      const int e = e0 + 32 * u;
-      float sum = 0.f;
-      if (e < nval)
-        for (int c = c_first; c <= c_last; ++c) {
-          // only the first contributor can have started before the tile
-          const int w = (c == c_first && pt.cta_start[c] < T * upt) ? 1 : 0;
-          sum += __ldcg(pt.slots + ((int64_t)c * 2 + w) * (int64_t)nval + e);
-        }
-      sv[u] = sum;
+    for (int u = 0; u < 8; ++u) sv[u] = 0.f;
+    for (int c = c_first; c <= c_last; ++c) {
+      // only the first contributor can have started before the tile
+      const int w = (c == c_first && pt.cta_start[c] < T * upt) ? 1 : 0;
+      const float* src = pt.slots + ((int64_t)c * 2 + w) * (int64_t)nval;
+#pragma unroll
+      for (int u = 0; u < 8; ++u)
+        if (e0 + 32 * u < nval) sv[u] += __ldcg(src + e0 + 32 * u);
     }
     store_outputs<Op, 8>(op, e0, 32, nval, T, sv);
   }
