@@ -429,73 +429,106 @@ __global__ void __launch_bounds__(256) quad_plug_corr_kernel(const PlugCorrParam
 // (K x M) product.  x is first transposed into scratch, xt[k * ldt + m], so
 // the M activations of one plug column are one contiguous row.  WPR warps
 // share a row, each a contiguous range of its entries.  A warp loads 32
-// entries at a time (lane l entry l, one coalesced load) and hands them out
-// by shuffle: its lanes form 32 / MPAD groups of MPAD lanes, lane m of a
-// group holding batch rows m, m + 32, ... (MPL of them), and the groups take
-// the entries round robin, four activation loads in flight per lane.  The
-// row's warps are summed in warp order through shared memory and the
-// groups in a fixed butterfly, so results are deterministic.
-__global__ void transpose_x_kernel(const __half* x, int64_t ldx_m, int M, int K, __half* xt, int ldt) {
+// entries at a time (lane l entry l, one coalesced load; the next 32 are
+// loaded before the current ones are used) and hands them out by shuffle:
+// its lanes form EG = 32 / MPAD groups of MPAD lanes, lane l of a group
+// holding the FP16 pairs of batch rows 2l + {0, 1} + 64 i (i < MPL), and
+// group g takes the entries g, g + EG, ...  A lane issues the activation
+// loads (one 4-byte pair per row pair) of up to 16 / MPL entries before it
+// uses the first, and applies an entry with eight FP16 x FP16 + FP32 FMAs
+// per row pair (the product is exact, one rounding, as fmaf on the
+// converted values).  The row's warps are summed in warp order through
+// shared memory and the groups in a fixed butterfly, so results are
+// deterministic.
+//
+// The transpose: a CTA takes 64 columns k of all M rows (coalesced row
+// reads into shared memory) and writes their xt rows (coalesced along m).
+__global__ void __launch_bounds__(256) transpose_x_kernel(const __half* x, int64_t ldx_m, int M, int K, __half* xt,
+                                                          int ldt) {
+  __shared__ uint16_t tile[128][66];  // [m][k], M <= 128
   pdl_launch_dependents();
   pdl_wait();  // activations may come from the previous kernel
-  const int64_t total = (int64_t)K * M;
-  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t m = i / K, k = i - m * K;  // reads along k are coalesced
-    xt[k * ldt + m] = x[m * ldx_m + k];
+  const int k0 = blockIdx.x * 64, kl = threadIdx.x & 63;
+  const uint16_t* xs = reinterpret_cast<const uint16_t*>(x);
+  for (int m = threadIdx.x >> 6; m < M; m += 4)
+    tile[m][kl] = k0 + kl < K ? xs[(int64_t)m * ldx_m + k0 + kl] : (uint16_t)0;
+  __syncthreads();
+  uint16_t* xo = reinterpret_cast<uint16_t*>(xt);
+  const int kn = K - k0 < 64 ? K - k0 : 64;
+  for (int i = threadIdx.x; i < kn * M; i += 256) {
+    const int k = i / M, m = i - k * M;
+    xo[(int64_t)(k0 + k) * ldt + m] = tile[m][k];
   }
+}
+
+// acc[q] += value q * x.lo, acc[4 + q] += value q * x.hi: FP16 operands,
+// FP32 accumulation
+__device__ __forceinline__ void corr_fma8(float (&acc)[8], uint32_t v01, uint32_t v23, uint32_t xpair) {
+  asm("{\n .reg .f16 v0, v1, v2, v3, xl, xh;\n"
+      " mov.b32 {v0, v1}, %8;\n mov.b32 {v2, v3}, %9;\n mov.b32 {xl, xh}, %10;\n"
+      " fma.rn.f32.f16 %0, v0, xl, %0;\n fma.rn.f32.f16 %1, v1, xl, %1;\n"
+      " fma.rn.f32.f16 %2, v2, xl, %2;\n fma.rn.f32.f16 %3, v3, xl, %3;\n"
+      " fma.rn.f32.f16 %4, v0, xh, %4;\n fma.rn.f32.f16 %5, v1, xh, %5;\n"
+      " fma.rn.f32.f16 %6, v2, xh, %6;\n fma.rn.f32.f16 %7, v3, xh, %7;\n}"
+      : "+f"(acc[0]), "+f"(acc[1]), "+f"(acc[2]), "+f"(acc[3]), "+f"(acc[4]), "+f"(acc[5]), "+f"(acc[6]),
+        "+f"(acc[7])
+      : "r"(v01), "r"(v23), "r"(xpair));
 }
 
 template <int MPAD, int MPL, int WPR>
 __global__ void __launch_bounds__(256) quad_plug_corr_t_kernel(const PlugCorrParams p, int ldt) {
   constexpr int EG = 32 / MPAD, RPC = 8 / WPR;
-  __shared__ float red[8][MPL][4][32];
+  constexpr int EPL = MPAD;                                 // entries per lane group and chunk
+  constexpr int BATCH = EPL < 16 / MPL ? EPL : 16 / MPL;    // activation loads in flight per lane
+  __shared__ float red[8][MPL][8][32];
   pdl_launch_dependents();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, eg = lane / MPAD, ml = lane % MPAD;
   const int row = blockIdx.x * RPC + warp / WPR, wr = warp % WPR;
-  float acc[MPL][4];
+  const int ldp = ldt / 2;  // row pairs per xt row
+  const uint32_t* xs = reinterpret_cast<const uint32_t*>(p.xt) + ml;
+  float acc[MPL][8];
 #pragma unroll
   for (int i = 0; i < MPL; ++i)
 #pragma unroll
-    for (int q = 0; q < 4; ++q) acc[i][q] = 0.f;
+    for (int q = 0; q < 8; ++q) acc[i][q] = 0.f;
   if (row < p.N) {
     const uint32_t j0 = __ldg(p.wbase + (int64_t)row * p.W), j1 = __ldg(p.wbase + (int64_t)(row + 1) * p.W);
     const uint32_t a = j0 + (uint32_t)((uint64_t)(j1 - j0) * wr / WPR);
     const uint32_t b = j0 + (uint32_t)((uint64_t)(j1 - j0) * (wr + 1) / WPR);
     const uint32_t rowbase = p.base_lo32 + (uint32_t)row * (uint32_t)p.K;
+    // entry a + lane of the first chunk; past the range: zero values, column 0
+    uint32_t nk = 0u;
+    uint2 nv = make_uint2(0u, 0u);
+    if (a + (uint32_t)lane < b) {
+      nk = __ldg(p.plug_idx + a + lane) - rowbase;
+      nv = __ldg(p.plug_vals + a + lane);
+    }
     pdl_wait();  // xt is written by the transpose launched just before
     for (uint32_t jb = a; jb < b; jb += 32u) {
-      const uint32_t j = jb + (uint32_t)lane;
-      uint32_t kk = 0u;
-      uint2 vv = make_uint2(0u, 0u);  // past the range: zero values, column 0
-      if (j < b) {
-        kk = __ldg(p.plug_idx + j) - rowbase;
-        vv = __ldg(p.plug_vals + j);
+      const uint32_t kk = nk;
+      const uint2 vv = nv;
+      const uint32_t jn = jb + 32u + (uint32_t)lane;
+      nk = 0u;
+      nv = make_uint2(0u, 0u);
+      if (jn < b) {
+        nk = __ldg(p.plug_idx + jn) - rowbase;
+        nv = __ldg(p.plug_vals + jn);
       }
 #pragma unroll
-      for (int e = 0; e < 32; e += EG * 4) {
-        uint32_t k4[4], v4x[4], v4y[4];
+      for (int e0 = 0; e0 < EPL; e0 += BATCH) {
+        uint32_t kb[BATCH], xw[BATCH][MPL];
 #pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          const int src = e + EG * u + eg;
-          k4[u] = __shfl_sync(0xffffffffu, kk, src);
-          v4x[u] = __shfl_sync(0xffffffffu, vv.x, src);
-          v4y[u] = __shfl_sync(0xffffffffu, vv.y, src);
-        }
-        float xv[4][MPL];
+        for (int t = 0; t < BATCH; ++t) kb[t] = __shfl_sync(0xffffffffu, kk, (e0 + t) * EG + eg);
 #pragma unroll
-        for (int u = 0; u < 4; ++u)
+        for (int t = 0; t < BATCH; ++t)
 #pragma unroll
-          for (int i = 0; i < MPL; ++i) xv[u][i] = __half2float(p.xt[(int64_t)k4[u] * ldt + ml + 32 * i]);
+          for (int i = 0; i < MPL; ++i) xw[t][i] = __ldg(xs + kb[t] * (uint32_t)ldp + 32 * i);
 #pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          const float2 va = __half22float2(u2h(v4x[u])), vb = __half22float2(u2h(v4y[u]));
+        for (int t = 0; t < BATCH; ++t) {
+          const int src = (e0 + t) * EG + eg;
+          const uint32_t v01 = __shfl_sync(0xffffffffu, vv.x, src), v23 = __shfl_sync(0xffffffffu, vv.y, src);
 #pragma unroll
-          for (int i = 0; i < MPL; ++i) {
-            acc[i][0] = fmaf(va.x, xv[u][i], acc[i][0]);
-            acc[i][1] = fmaf(va.y, xv[u][i], acc[i][1]);
-            acc[i][2] = fmaf(vb.x, xv[u][i], acc[i][2]);
-            acc[i][3] = fmaf(vb.y, xv[u][i], acc[i][3]);
-          }
+          for (int i = 0; i < MPL; ++i) corr_fma8(acc[i], v01, v23, xw[t][i]);
         }
       }
     }
@@ -506,13 +539,13 @@ __global__ void __launch_bounds__(256) quad_plug_corr_t_kernel(const PlugCorrPar
 #pragma unroll
     for (int i = 0; i < MPL; ++i)
 #pragma unroll
-      for (int q = 0; q < 4; ++q) red[warp][i][q][lane] = acc[i][q];
+      for (int q = 0; q < 8; ++q) red[warp][i][q][lane] = acc[i][q];
     __syncthreads();
     if (wr != 0) return;
 #pragma unroll
     for (int i = 0; i < MPL; ++i)
 #pragma unroll
-      for (int q = 0; q < 4; ++q) {
+      for (int q = 0; q < 8; ++q) {
         float v = red[warp][i][q][lane];
 #pragma unroll
         for (int w = 1; w < WPR; ++w) v += red[warp + w][i][q][lane];
@@ -524,15 +557,17 @@ __global__ void __launch_bounds__(256) quad_plug_corr_t_kernel(const PlugCorrPar
 #pragma unroll
     for (int i = 0; i < MPL; ++i)
 #pragma unroll
-      for (int q = 0; q < 4; ++q) acc[i][q] += __shfl_xor_sync(0xffffffffu, acc[i][q], o);
+      for (int q = 0; q < 8; ++q) acc[i][q] += __shfl_xor_sync(0xffffffffu, acc[i][q], o);
   if (eg != 0 || row >= p.N) return;
 #pragma unroll
-  for (int i = 0; i < MPL; ++i) {
-    const int m = ml + 32 * i;
-    if (m < p.M)
+  for (int i = 0; i < MPL; ++i)
 #pragma unroll
-      for (int q = 0; q < 4; ++q) p.corr[(int64_t)q * p.ldq + (int64_t)m * p.N + row] = acc[i][q];
-  }
+    for (int h = 0; h < 2; ++h) {
+      const int m = 64 * i + 2 * ml + h;
+      if (m < p.M)
+#pragma unroll
+        for (int q = 0; q < 4; ++q) p.corr[(int64_t)q * p.ldq + (int64_t)m * p.N + row] = acc[i][4 * h + q];
+    }
 }
 
 // Warps per row for about 64 entries per warp, 1..8, from the row length:
@@ -540,11 +575,10 @@ __global__ void __launch_bounds__(256) quad_plug_corr_t_kernel(const PlugCorrPar
 // (The count itself lives on the device; the choice only affects speed.)
 template <int MPAD, int MPL>
 int launch_corr_t(const PlugCorrParams& prm, cudaStream_t s) {
-  const int ldt = MPAD * MPL;
-  const int64_t total = (int64_t)prm.K * prm.M;
-  const int tg = (int)(cdiv(total, 256) < 4096 ? cdiv(total, 256) : 4096);
-  int rc = launch_kernel("transpose_x_kernel", launch_overlap(), transpose_x_kernel, dim3(tg), dim3(256), 0, s,
-                         prm.x, prm.ldx_m, prm.M, prm.K, prm.xt, ldt);
+  const int ldt = 2 * MPAD * MPL;
+  int rc = launch_kernel("transpose_x_kernel", launch_overlap(), transpose_x_kernel,
+                         dim3((unsigned)cdiv(prm.K, 64)), dim3(256), 0, s, prm.x, prm.ldx_m, prm.M, prm.K, prm.xt,
+                         ldt);
   if (rc) return rc;
   const int64_t per_row = prm.K / 20;
   const bool ov = launch_overlap();
@@ -569,12 +603,13 @@ int launch_plug_corr(const PlugCorrParams& prm, cudaStream_t s) {
       set_error("plug correction: at most 128 batch rows per launch");
       return PP_ERR_INVALID;
     }
-    if (prm.M <= 4) return launch_corr_t<4, 1>(prm, s);
-    if (prm.M <= 8) return launch_corr_t<8, 1>(prm, s);
-    if (prm.M <= 16) return launch_corr_t<16, 1>(prm, s);
-    if (prm.M <= 32) return launch_corr_t<32, 1>(prm, s);
-    if (prm.M <= 64) return launch_corr_t<32, 2>(prm, s);
-    return launch_corr_t<32, 4>(prm, s);
+    // MPAD lanes of row pairs per entry: 2 * MPAD * MPL >= M
+    if (prm.M <= 4) return launch_corr_t<2, 1>(prm, s);
+    if (prm.M <= 8) return launch_corr_t<4, 1>(prm, s);
+    if (prm.M <= 16) return launch_corr_t<8, 1>(prm, s);
+    if (prm.M <= 32) return launch_corr_t<16, 1>(prm, s);
+    if (prm.M <= 64) return launch_corr_t<32, 1>(prm, s);
+    return launch_corr_t<32, 2>(prm, s);
   }
   if (prm.M == 1) {
     if (prm.K <= 4096) {  // short rows: two per warp
