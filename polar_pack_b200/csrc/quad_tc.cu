@@ -341,26 +341,42 @@ __global__ void __launch_bounds__(kTcThreads, 1) quad_tc_kernel(const __grid_con
       __threadfence();
       const float* tslots = p.slots + (int64_t)tile * p.splits * 4 * p.nmma * kTcRows;
       const int per_split = 4 * p.nmma * kTcRows;
-      for (int e = tid; e < 4 * p.M * kTcRows; e += kTcThreads) {
-        const int rl = e & (kTcRows - 1), qm = e >> 7;
-        const int q = qm / p.M, m = qm - q * p.M;
-        const int row = n0 + rl;
-        const float* src = tslots + ((int64_t)q * p.nmma + m) * kTcRows + rl;
-        float a = 0.f;
-        int j = 0;
-        for (; j + 4 <= p.splits; j += 4) {  // four loads in flight, summed in split order
-          const float v0 = __ldcg(src + (int64_t)j * per_split), v1 = __ldcg(src + (int64_t)(j + 1) * per_split);
-          const float v2 = __ldcg(src + (int64_t)(j + 2) * per_split), v3 = __ldcg(src + (int64_t)(j + 3) * per_split);
-          a += v0;
-          a += v1;
-          a += v2;
-          a += v3;
+      const int total = 4 * p.M * kTcRows;
+      // eight elements per thread at a time: every split's partial and the
+      // plug correction of all eight are loaded before any output is stored
+      // (a load after a store would wait for it: they may alias), and each
+      // element sums its splits in split order
+      for (int e0 = tid; e0 < total; e0 += 8 * kTcThreads) {
+        int off[8], qv[8], mv[8];
+        float a[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+          const int e = e0 + u * kTcThreads;
+          const int rl = e & (kTcRows - 1), qm = e >> 7;
+          qv[u] = qm / p.M;
+          mv[u] = qm - qv[u] * p.M;
+          off[u] = (e < total && n0 + rl < p.N) ? (qv[u] * p.nmma + mv[u]) * kTcRows + rl : -1;
+          a[u] = 0.f;
         }
-        for (; j < p.splits; ++j) a += __ldcg(src + (int64_t)j * per_split);
-        if (row < p.N) {
-          if (p.corr) a += p.corr[(int64_t)q * p.corr_q + (int64_t)m * p.N + row];
-          p.out[q][(int64_t)m * p.ldo_m + (int64_t)row * p.ldo_n] = __float2half_rn(a * p.scale[q]);
+#pragma unroll 2
+        for (int j = 0; j < p.splits; ++j) {
+          const float* src = tslots + (int64_t)j * per_split;
+#pragma unroll
+          for (int u = 0; u < 8; ++u)
+            if (off[u] >= 0) a[u] += __ldcg(src + off[u]);
         }
+        if (p.corr) {
+#pragma unroll
+          for (int u = 0; u < 8; ++u)
+            if (off[u] >= 0)
+              a[u] += __ldcg(p.corr + (int64_t)qv[u] * p.corr_q + (int64_t)mv[u] * p.N + n0 + (off[u] & (kTcRows - 1)));
+        }
+#pragma unroll
+        for (int u = 0; u < 8; ++u)
+          if (off[u] >= 0) {
+            const int row = n0 + (off[u] & (kTcRows - 1));
+            p.out[qv[u]][(int64_t)mv[u] * p.ldo_m + (int64_t)row * p.ldo_n] = __float2half_rn(a[u] * p.scale[qv[u]]);
+          }
       }
       if (tid == 0) p.counters[tile] = 0;
     }
