@@ -63,6 +63,7 @@ struct DualTOp {
   static constexpr int kNOut = 2;
   static constexpr int kNBat = 8;
   static constexpr int kUnitBytes = (int)kDualTUnit;
+  static constexpr int kPrefetch = 0;
   using Buf = DualTBuf;
 
   const DualTParams& p;
@@ -116,6 +117,7 @@ struct DualTOp {
     }
   }
 
+  __device__ __forceinline__ void prefetch(int, int) const {}
   __device__ __forceinline__ void side(int, int, int) {}
   __device__ __forceinline__ void end_chunk() {}
 

@@ -520,14 +520,21 @@ __device__ __forceinline__ void tma_stream(Op& op, const Issue& issue, TmaRing& 
   int s = 0, sp = 0;
   uint32_t ph = 0;
   typename Op::Buf buf;
+  // L2 prefetch: unit kc + S + D of a chunk is prefetched when unit kc + S
+  // is copied into the ring (D = Op::kPrefetch), the chunk's units S .. S +
+  // D - 1 when the chunk starts
+  constexpr int D = Op::kPrefetch;
   while (sq.seg < 3) {
     const int t = sq.t, kc0 = sq.kc;
     const int n = (upt - kc0) < (sq.end - sq.u) ? (upt - kc0) : (sq.end - sq.u);
+    if (D > 0 && leader)
+      for (int i = 0; i < D && rg.S + i < n; ++i) op.prefetch(t, kc0 + rg.S + i);
     op.zero();
     for (int kc = kc0; kc < kc0 + n; ++kc) {
       if (!mbar_wait_bounded(rg.bars + 8u * (uint32_t)s, ph, status)) return;
       op.read(buf, rg.ring + (uint32_t)s * Op::kUnitBytes, s, t);
       __syncwarp();
+      if (D > 0 && leader && kc + rg.S + D < kc0 + n) op.prefetch(t, kc + rg.S + D);
       if (rg.next.seg < 3) rg.issue_next(issue, s, Op::kUnitBytes, leader);  // warp-uniform test
       op.side(sp, t * upt + kc, kc);
       if (++sp == rg.P) sp = 0;

@@ -124,6 +124,7 @@ struct QuadOp {
   static constexpr int kNOut = 4;
   static constexpr int kNBat = 8 * NB;
   static constexpr int kUnitBytes = 2048;
+  static constexpr int kPrefetch = 0;  // units of a chunk prefetched into L2 ahead of the ring (0: none)
   using Buf = QuadBuf;
 
   const QuadParams& p;
@@ -203,6 +204,16 @@ struct QuadOp {
       tma_load_2d(slot + 1024u, &q.tmap, kc * 64 + 32, tile * 8, bar);
     } else {
       tma_load_2d(slot, &q.tmap, tile * 32, kc * 16, bar);
+    }
+  }
+
+  // L2 prefetch of unit (tile, kc): the same boxes as issue()
+  __device__ __forceinline__ void prefetch(int tile, int kc) const {
+    if constexpr (NK) {
+      tma_prefetch_2d(&p.tmap, kc * 64, tile * 8);
+      tma_prefetch_2d(&p.tmap, kc * 64 + 32, tile * 8);
+    } else {
+      tma_prefetch_2d(&p.tmap, tile * 32, kc * 16);
     }
   }
 
@@ -549,17 +560,18 @@ __device__ __forceinline__ void quad_gemv_run(const QuadParams& p) {
     rg.P = PLUG ? p.stages + 1 : p.stages;
     rg.next.init(wu0, wu1, p.part.upt);
   }
-  uint32_t* stage = reinterpret_cast<uint32_t*>(pp_smem + (L.scratch - base));
-  if (!prepared) quad_lut_stage(stage, v);
-  __syncthreads();
+  // lane 0 of each warp initialises its ring and issues its first units
+  // before the barrier (the rings overlap nothing written before it).
+  // PLUG: codes only for now; the plug copies, which need the offsets,
+  // arrive on the barriers after the table wait
   if (wu0 < wu1 && (threadIdx.x & 31) == 0) {
-    if (warp == 0) prefetch_tmap(&p.tmap);
-    // PLUG: codes only for now; the plug copies, which need the offsets,
-    // arrive on the barriers after the table wait
     rg.prologue([&](uint32_t slot, uint32_t bar, int, int tile, int kc) {
       QuadOp<NK, NB, false>::template issue<!PLUG>(p, slot, bar, tile, kc);
     }, 2048u);
   }
+  uint32_t* stage = reinterpret_cast<uint32_t*>(pp_smem + (L.scratch - base));
+  if (!prepared) quad_lut_stage(stage, v);
+  __syncthreads();
   if (prepared) {
     mbar_wait_bounded(tbar, 0u, status);
   } else {
