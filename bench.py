@@ -773,13 +773,17 @@ def run_decode_step(torch, dist, dev, args, world, rank, lib, stream):
 def run_e2e(torch, dist, sets, xs, dev, args, world, M, full_sets, pgroups=None):
     """Same metric through the public API: every step copies that step's
     inputs from pinned host memory to the GPU, runs the Linears as one
-    RowShardedGroup (with N > 1 GPUs each rank computes its row shards and
-    one NCCL all-gather collects them), and copies the step's result (the
-    four models' outputs of every Linear, gathered) back to pinned host
-    memory -- one copy each way, all inside the timed region."""
-    from polar_pack_b200.parallel import RowShardedGroup
+    group (RowShardedGroup on one GPU; with N > 1 GPUs each rank computes
+    its row shards, gathered through peer memory by PeerShardedGroup, or by
+    one NCCL all-gather with --nccl-gather), and copies the step's result
+    (the four models' outputs of every Linear, gathered) back to pinned host
+    memory -- one copy each way, all inside the timed region.  Except with
+    --nccl-gather, a step is one GraphedStep replay (copies and launches in
+    one CUDA graph)."""
+    from polar_pack_b200.parallel import GraphedStep, RowShardedGroup
     from polar_pack_b200.quadpack import quad_linear
     stream = torch.cuda.current_stream(dev)
+    cap = torch.cuda.Stream(dev)  # capture stream of the graphed steps
     sizes = [x.numel() for x in xs]
     hx = torch.cat([x.reshape(-1) for x in xs]).cpu().pin_memory()   # all inputs, one pinned buffer
     dxf = torch.empty_like(hx, device=dev)
@@ -789,13 +793,23 @@ def run_e2e(torch, dist, sets, xs, dev, args, world, M, full_sets, pgroups=None)
         o += n
     full_n = [N for _, N in SHAPES]
     if pgroups:
-        # N > 1 GPUs: the peer-gathered group; its result is complete on every rank
-        host_out = torch.empty((4, sum(full_n)), dtype=torch.float16).pin_memory()
+        # N > 1 GPUs: the peer-gathered group; its result is complete on every
+        # rank.  One graph per (group, buffer): calls alternate the buffers.
+        graphs = [[GraphedStep(lambda g=g, b=b: g(dx, b), hx, dxf, cap) for b in (0, 1)] for g in pgroups]
+        host_out = graphs[0][0].host_out
 
         def step(i):
-            dxf.copy_(hx, non_blocking=True)
-            y = pgroups[i % len(pgroups)](dx, i % 2)
-            host_out.copy_(y, non_blocking=True)
+            graphs[i % len(graphs)][i % 2]()
+    elif world == 1:
+        # the independent Linears as one row-sharded group writing into its
+        # send buffer, replayed with the copies from one graph per replica
+        groups = [RowShardedGroup([lambda x, out, l=l: quad_linear(x, l, out=out) for l in st], full_n,
+                                  writes_out=True) for st in sets]
+        graphs = [GraphedStep(lambda g=g: (g(dx), g.raw())[1], hx, dxf, cap) for g in groups]
+        host_out = graphs[0].host_out
+
+        def step(i):
+            graphs[i % len(graphs)]()
     else:
         # the independent Linears as one row-sharded group writing into its send buffer
         groups = [RowShardedGroup([lambda x, out, l=l: quad_linear(x, l, out=out) for l in st], full_n,
@@ -833,8 +847,11 @@ def run_e2e(torch, dist, sets, xs, dev, args, world, M, full_sets, pgroups=None)
             total += layer_bytes(l.N, l.K, l.p_hi - l.p_lo, M)
     return {"value": round(total / (ms * 1e-3) / 1e9, 1), "unit": UNIT, "h2d_bytes_per_step": int(h2d),
             "d2h_bytes_per_step": int(d2h),
-            "api": "polar_pack_b200.parallel.PeerShardedGroup (pp_quad_linear_gather)" if pgroups else
-                   "polar_pack_b200.parallel.RowShardedGroup of polar_pack_b200.quadpack.quad_linear"}
+            "api": "polar_pack_b200.parallel.GraphedStep of a PeerShardedGroup (pp_quad_linear_gather)" if pgroups
+                   else "polar_pack_b200.parallel.GraphedStep of a RowShardedGroup of quadpack.quad_linear"
+                   if world == 1 else "polar_pack_b200.parallel.RowShardedGroup of quadpack.quad_linear",
+            "timing": "each step: pinned host inputs -> device, the Linears, result -> pinned host, "
+                      "one CUDA graph launch per step" if (pgroups or world == 1) else "eager calls"}
 
 
 def load_traffic():

@@ -304,3 +304,43 @@ class PeerShardedGroup:
                 _lib.check(rc)
         self.peers.wait(b, s)
         return self.peers.view(b)[:4 * self.total].view(4, self.total)
+
+
+# ---------------------------------------------------------- graphed step ----
+class GraphedStep:
+    """One serving step from pinned host memory to pinned host memory,
+    replayed from a single CUDA graph.
+
+    The graph holds the copy of ``host_in`` into ``dev_in``, ``fn()`` (which
+    reads ``dev_in`` and returns the device tensor of the step's result) and
+    the copy of that result into a pinned host buffer, so a call costs one
+    graph launch instead of one library call per Linear.  ``fn`` must be
+    capturable: fixed buffers and no host synchronisation, as the groups of
+    this module and ``quad_linear`` with a preallocated ``out`` are.  It runs
+    once on ``stream`` before the capture (argument caches, workspaces).
+    A call returns the pinned host result; read it after synchronising the
+    stream the call ran on (the current stream).
+    """
+
+    def __init__(self, fn: Callable[[], torch.Tensor], host_in: torch.Tensor, dev_in: torch.Tensor,
+                 stream: torch.cuda.Stream):
+        if not host_in.is_pinned():
+            raise ValueError("host_in must be pinned")
+        if host_in.shape != dev_in.shape or host_in.dtype != dev_in.dtype:
+            raise ValueError("host_in and dev_in must match in shape and dtype")
+        self.host_in, self.dev_in = host_in, dev_in
+        with torch.cuda.stream(stream):
+            dev_in.copy_(host_in, non_blocking=True)
+            y = fn()
+        stream.synchronize()
+        self.host_out = torch.empty(y.shape, dtype=y.dtype).pin_memory()
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph, stream=stream):
+            dev_in.copy_(host_in, non_blocking=True)
+            y = fn()
+            self.host_out.copy_(y, non_blocking=True)
+
+    def __call__(self) -> torch.Tensor:
+        self.graph.replay()
+        return self.host_out
+
