@@ -28,13 +28,17 @@ namespace pp {
 
 constexpr int kTcRows = 128;                                // tile rows = MMA M
 constexpr int kTcK = 16;                                    // K per stage = MMA K
-constexpr int kTcDecodeWarps = 8;
+constexpr int kTcGroupWarps = 8;                            // decoder warps of one stage
+constexpr int kTcGroups = 2;                                // decoder groups, alternate stages
+constexpr int kTcDecodeWarps = kTcGroupWarps * kTcGroups;
 constexpr int kTcThreads = (kTcDecodeWarps + 2) * 32;       // + producer + MMA warp
 constexpr uint32_t kTcCodeBytes = kTcRows * kTcK * 4;       // 8 KiB
 constexpr uint32_t kTcXBytes = 128 * kTcK * 2;              // activations, nmma <= 128 rows
 constexpr uint32_t kTcATileBytes = kTcRows * kTcK * 2;      // 4 KiB per model
-constexpr uint32_t kTcStageBytes = kTcCodeBytes + kTcXBytes + 4 * kTcATileBytes;  // 28 KiB
-constexpr int kTcMaxStages = 4;
+constexpr uint32_t kTcCSlotBytes = kTcCodeBytes + kTcXBytes;  // 12 KiB: one stage's TMA data
+constexpr uint32_t kTcASlotBytes = 4 * kTcATileBytes;       // 16 KiB: one stage's four A tiles
+constexpr int kTcMaxStages = 8;                             // code slots
+constexpr int kTcASlots = 3;                                // A-tile slots
 constexpr int kTcMaxRows = 128;                             // batch rows per launch
 
 struct QuadTcParams {
@@ -49,7 +53,7 @@ struct QuadTcParams {
   int M, N, K;
   int nmma;                // batch rows rounded up to 16
   int splits, kchunks;     // K splits per tile, K chunks of 16
-  int stages;
+  int stages;              // code slots (stages of codes and activations in flight)
   uint32_t tmem_cols;
   uint32_t smem_bytes;
   float* slots;            // split-K partials [tiles * splits][4][nmma][128]
@@ -57,38 +61,51 @@ struct QuadTcParams {
 };
 
 // Shared memory: tables at the first 64 KiB boundary when they fit (direct
-// gathers), else at the base; stages (1 KiB aligned) first-fit below and
-// above the tables; then the mbarriers and the tensor-memory address slot.
+// gathers), else at the base; then, first-fit below and above the tables
+// (1 KiB aligned), S code slots (a stage's codes and activations, filled by
+// TMA) and two A-tile slots (a stage's decoded weights), then the
+// mbarriers and the tensor-memory address slot.  The code ring runs ahead
+// of the decode by up to S stages, so more code slots hide more HBM
+// latency; the A tiles only need to cover the MMA of the previous stage.
+// A ring of equal slots: slots [0, n0) from b0 (below the tables), the rest
+// from b1 (above them), so a slot address is plain arithmetic (no indexed
+// array, which would live in local memory).
+struct TcRing {
+  uint32_t b0, n0, b1;
+  __host__ __device__ uint32_t at(int i, uint32_t bytes) const {
+    return (uint32_t)i < n0 ? b0 + (uint32_t)i * bytes : b1 + ((uint32_t)i - n0) * bytes;
+  }
+};
+
 struct TcLayout {
-  uint32_t lut, stage[kTcMaxStages], bars, tslot;
+  uint32_t lut, bars, tslot;
+  TcRing cr, ar;  // code slots (kTcCSlotBytes), A-tile slots (kTcASlotBytes)
   int direct, ok;
 };
 
 __host__ __device__ inline TcLayout tc_layout(uint32_t base, uint32_t size, int S) {
   TcLayout L{};
   const uint64_t end = (uint64_t)base + size;
-  const uint32_t small = 256;  // (3 * S + 2) mbarriers + tmem slot
+  const uint32_t small = 256;  // (2 S + 2 kTcASlots + 2) mbarriers + tmem slot
   for (int direct = 1; direct >= 0; --direct) {
     L = TcLayout{};
     const uint32_t lut = direct ? ((base + 0xFFFFu) & ~0xFFFFu) : base;
     if ((uint64_t)lut + kQuadLutBytes > end) continue;
-    // free ranges: [base, lut) and [lut + 128 KiB, end)
-    uint64_t fa = ((uint64_t)base + 1023u) & ~1023ull, ea = lut;
+    // free ranges: [fa, lut) and [fb, end); a ring takes as many slots as
+    // fit below the tables, then the rest above them
+    uint64_t fa = ((uint64_t)base + 1023u) & ~1023ull;
     uint64_t fb = ((uint64_t)lut + kQuadLutBytes + 1023u) & ~1023ull;
-    int s = 0;
-    for (; s < S; ++s) {
-      if (fa + kTcStageBytes <= ea) {
-        L.stage[s] = (uint32_t)fa;
-        fa += kTcStageBytes;
-      } else if (fb + kTcStageBytes <= end) {
-        L.stage[s] = (uint32_t)fb;
-        fb += kTcStageBytes;
-      } else {
-        break;
-      }
-    }
-    if (s < S) continue;
-    if (fa + small <= ea) L.bars = (uint32_t)fa;
+    auto ring = [&](int n, uint32_t bytes, TcRing* r) {
+      const uint64_t below = fa < lut ? (lut - fa) / bytes : 0;
+      r->n0 = (uint32_t)(below < (uint64_t)n ? below : (uint64_t)n);
+      r->b0 = (uint32_t)fa;
+      fa += (uint64_t)r->n0 * bytes;
+      r->b1 = (uint32_t)fb;
+      fb += (uint64_t)(n - (int)r->n0) * bytes;
+      return fb <= end;
+    };
+    if (!ring(kTcASlots, kTcASlotBytes, &L.ar) || !ring(S, kTcCSlotBytes, &L.cr)) continue;
+    if (fa + small <= lut) L.bars = (uint32_t)fa;
     else if (fb + small <= end) L.bars = (uint32_t)fb;
     else continue;
     L.tslot = L.bars + 240u;
@@ -162,7 +179,7 @@ __host__ __device__ constexpr uint32_t tc_idesc(int n) {
 template <bool DIRECT>
 __device__ __forceinline__ void tc_decode_stage(uint32_t codes, uint32_t a_tiles, uint32_t lb0, uint32_t lb1,
                                                 uint32_t add0, uint32_t add1) {
-  const int i = threadIdx.x;          // decoder threads 0..255
+  const int i = threadIdx.x & 255;    // thread of the decoder group, 0..255
   const int row = i & 127, h = i >> 7;  // row of the tile, 8-code half of the stage
   // codes: row at row * 64, 16-byte chunk c at (c ^ ((row >> 1) & 3)) * 16 (64-byte swizzle)
   const uint32_t rbase = codes + (uint32_t)row * 64u;
@@ -209,14 +226,19 @@ __global__ void __launch_bounds__(kTcThreads, 1) quad_tc_kernel(const __grid_con
   const int c1 = (int)((int64_t)(split + 1) * p.kchunks / p.splits);
   const int nst = c1 - c0;  // stages of this CTA (>= 1, checked on the host)
   const int n0 = tile * kTcRows;
-  // mbarriers: full[S], afull[S], empty[S], done, tables
-  const uint32_t full = L.bars, afull = L.bars + 8u * S, empty = L.bars + 16u * S;
-  const uint32_t done = L.bars + 24u * S, tbar = done + 8u;
+  // mbarriers: full[S], empty[S] (code slots), afull[2], aempty[2] (A-tile
+  // slots), done, tables
+  const uint32_t full = L.bars, empty = L.bars + 8u * S;
+  const uint32_t afull = L.bars + 16u * S, aempty = afull + 8u * kTcASlots;
+  const uint32_t done = aempty + 8u * kTcASlots, tbar = done + 8u;
   if (tid == 0) {
     for (int s = 0; s < S; ++s) {
       mbar_init(full + 8u * s, 1);
-      mbar_init(afull + 8u * s, kTcDecodeWarps);
       mbar_init(empty + 8u * s, 1);
+    }
+    for (int a = 0; a < kTcASlots; ++a) {
+      mbar_init(afull + 8u * a, kTcGroupWarps);
+      mbar_init(aempty + 8u * a, 1);
     }
     mbar_init(done, 1);
     mbar_init(tbar, 1);
@@ -243,16 +265,17 @@ __global__ void __launch_bounds__(kTcThreads, 1) quad_tc_kernel(const __grid_con
       const int pre = nst < S ? nst : S;
       for (int r = 0; r < pre; ++r) {
         mbar_expect_tx(full + 8u * r, kTcCodeBytes + xbytes);
-        tma_load_2d(L.stage[r], &p.tmap_codes, (c0 + r) * kTcK, n0, full + 8u * r);
+        tma_load_2d(L.cr.at(r, kTcCSlotBytes), &p.tmap_codes, (c0 + r) * kTcK, n0, full + 8u * r);
       }
       pdl_wait();  // activations may come from the previous kernel
-      for (int r = 0; r < pre; ++r) tma_load_2d(L.stage[r] + kTcCodeBytes, &p.tmap_x, (c0 + r) * kTcK, 0, full + 8u * r);
+      for (int r = 0; r < pre; ++r) tma_load_2d(L.cr.at(r, kTcCSlotBytes) + kTcCodeBytes, &p.tmap_x, (c0 + r) * kTcK, 0, full + 8u * r);
       for (int r = S; r < nst; ++r) {
         const int s = r % S;
+        // the slot's last stage has been decoded and multiplied
         if (!mbar_wait_bounded(empty + 8u * s, (uint32_t)((r / S) - 1) & 1u, status)) break;
         mbar_expect_tx(full + 8u * s, kTcCodeBytes + xbytes);
-        tma_load_2d(L.stage[s], &p.tmap_codes, (c0 + r) * kTcK, n0, full + 8u * s);
-        tma_load_2d(L.stage[s] + kTcCodeBytes, &p.tmap_x, (c0 + r) * kTcK, 0, full + 8u * s);
+        tma_load_2d(L.cr.at(s, kTcCSlotBytes), &p.tmap_codes, (c0 + r) * kTcK, n0, full + 8u * s);
+        tma_load_2d(L.cr.at(s, kTcCSlotBytes) + kTcCodeBytes, &p.tmap_x, (c0 + r) * kTcK, 0, full + 8u * s);
       }
     }
   } else if (warp == kTcDecodeWarps + 1) {
@@ -261,17 +284,18 @@ __global__ void __launch_bounds__(kTcThreads, 1) quad_tc_kernel(const __grid_con
       const uint32_t idesc = tc_idesc(p.nmma);
       bool ok = true;
       for (int r = 0; r < nst && ok; ++r) {
-        const int s = r % S;
-        const uint32_t par = (uint32_t)(r / S) & 1u;
-        ok = mbar_wait_bounded(full + 8u * s, par, status) && mbar_wait_bounded(afull + 8u * s, par, status);
+        const int s = r % S, a = r % kTcASlots;
+        ok = mbar_wait_bounded(full + 8u * s, (uint32_t)(r / S) & 1u, status) &&
+             mbar_wait_bounded(afull + 8u * a, (uint32_t)(r / kTcASlots) & 1u, status);
         if (!ok) break;
         tc_fence_after();
-        const uint64_t bdesc = sw32_desc(L.stage[s] + kTcCodeBytes);
+        const uint64_t bdesc = sw32_desc(L.cr.at(s, kTcCSlotBytes) + kTcCodeBytes);
 #pragma unroll
         for (int q = 0; q < 4; ++q)
-          tc_mma(tmem + (uint32_t)(q * p.nmma), sw32_desc(L.stage[s] + kTcCodeBytes + kTcXBytes + q * kTcATileBytes),
-                 bdesc, idesc, r > 0 ? 1u : 0u);
-        tc_commit(empty + 8u * s);
+          tc_mma(tmem + (uint32_t)(q * p.nmma), sw32_desc(L.ar.at(a, kTcASlotBytes) + q * kTcATileBytes), bdesc, idesc,
+                 r > 0 ? 1u : 0u);
+        tc_commit(empty + 8u * s);   // code slot free (its activations were read)
+        tc_commit(aempty + 8u * a);  // A-tile slot free
       }
       tc_commit(done);  // fires once every MMA issued above has completed
     }
@@ -281,14 +305,19 @@ __global__ void __launch_bounds__(kTcThreads, 1) quad_tc_kernel(const __grid_con
       const uint32_t lb0 = (L.direct ? L.lut : 0u) | ((uint32_t)lane * 4u);
       const uint32_t lb1 = (L.direct ? L.lut + 65536u : 0u) | ((uint32_t)lane * 4u);
       const uint32_t add0 = L.direct ? 0u : L.lut, add1 = L.direct ? 0u : L.lut + 65536u;
-      for (int r = 0; r < nst; ++r) {
-        const int s = r % S;
+      // group g decodes stages g, g + kTcGroups, ...
+      for (int r = warp / kTcGroupWarps; r < nst; r += kTcGroups) {
+        const int s = r % S, a = r % kTcASlots;
         if (!mbar_wait_bounded(full + 8u * s, (uint32_t)(r / S) & 1u, status)) break;
-        if (L.direct) tc_decode_stage<true>(L.stage[s], L.stage[s] + kTcCodeBytes + kTcXBytes, lb0, lb1, 0u, 0u);
-        else tc_decode_stage<false>(L.stage[s], L.stage[s] + kTcCodeBytes + kTcXBytes, lb0, lb1, add0, add1);
+        // the A-tile slot's previous stage has been multiplied
+        if (r >= kTcASlots &&
+            !mbar_wait_bounded(aempty + 8u * a, (uint32_t)((r / kTcASlots) - 1) & 1u, status))
+          break;
+        if (L.direct) tc_decode_stage<true>(L.cr.at(s, kTcCSlotBytes), L.ar.at(a, kTcASlotBytes), lb0, lb1, 0u, 0u);
+        else tc_decode_stage<false>(L.cr.at(s, kTcCSlotBytes), L.ar.at(a, kTcASlotBytes), lb0, lb1, add0, add1);
         fence_proxy_async();  // the A tiles are read by the tensor core (async proxy)
         __syncwarp();
-        if (lane == 0) mbar_arrive(afull + 8u * s);
+        if (lane == 0) mbar_arrive(afull + 8u * a);
       }
     }
     // ------------------------------------------------------------ epilogue
