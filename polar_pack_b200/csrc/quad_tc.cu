@@ -447,8 +447,9 @@ inline QuadTcPlan quad_tc_plan(int64_t Mc, int64_t N, int64_t K, int sms) {
 // tables).  Besides the operand constraints it needs either enough 128-row
 // tiles or a long enough K: with few tiles and a short K the split-K
 // partials move about as many bytes as the codes, and the GEMV kernel in
-// 16-row chunks was faster on B200 (2048 x 2048: 53 vs 79 us at 32 rows;
-// 2048 x 11008 and 11008 x 2048 went the other way, 1.2-3.8x).
+// 16-row chunks is about as fast on B200 (2048 x 2048: 36 vs 42 us at 32
+// rows, 68 vs 64 us at 64; 2048 x 256: 55 vs 82 us at 64 rows), while
+// 2048 x 11008 and 11008 x 2048 go the other way (1.9-2.6x at 64 rows).
 bool quad_tc_ok(int64_t M, int64_t N, int64_t K, const uint32_t* codes, int64_t ldw, const void* x, int64_t ldx_m,
                 int64_t ldx_k) {
   return M > 16 && (N >= 4096 || K >= 4096) && K % kTcK == 0 && K >= kTcK && ldx_k == 1 && aligned(x, 16) &&
