@@ -206,6 +206,10 @@ struct DualTOp {
 // barrier every warp streams and reduces on its own.
 __global__ void __launch_bounds__(kDualTWarps * 32, 1) dual_tma_kernel(const __grid_constant__ DualTParams p) {
   constexpr int NW = kDualTWarps;
+  if (threadIdx.x == 0) {  // the first copies need the tensor maps
+    prefetch_tmap(&p.tcodes);
+    prefetch_tmap(&p.tscale);
+  }
   pdl_launch_dependents();
   const uint32_t base = (uint32_t)__cvta_generic_to_shared(pp_smem);
   int* status = p.part.counters + (kMaxGrid - 1);
@@ -235,10 +239,6 @@ __global__ void __launch_bounds__(kDualTWarps * 32, 1) dual_tma_kernel(const __g
     DualTOp::issue(p, slot, bar, side + (uint32_t)sp * kDualTSide, tile, kc);
   };
   if (wu0 < wu1 && lane == 0) {
-    if (warp == 0) {
-      prefetch_tmap(&p.tcodes);
-      prefetch_tmap(&p.tscale);
-    }
     rg.prologue(issue, kDualTUnit);
   }
   dual_lut_fanout(pp_smem, stage);

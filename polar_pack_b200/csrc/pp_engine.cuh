@@ -468,13 +468,18 @@ __device__ __forceinline__ void close_split(Op& op, const Partition& pt, const C
   const int G = gridDim.x;
   const int c_first = cta_of_unit(pt.cta_start, G, T * upt);
   const int c_last = cta_of_unit(pt.cta_start, G, T * upt + upt - 1);
-  __threadfence();
+  // the warp's slot stores are ordered before lane 0 (__syncwarp) and its
+  // acquire-release arrival at GPU scope; the last CTA's lanes read the
+  // slots after that arrival (shuffle)
   __syncwarp();
   int lastc = 0;
-  if (lane == 0) lastc = atomicAdd(pt.counters + c_last, 1) == c_last - c_first;
+  if (lane == 0) {
+    int old;
+    asm volatile("atom.add.acq_rel.gpu.global.s32 %0, [%1], 1;" : "=r"(old) : "l"(pt.counters + c_last) : "memory");
+    lastc = old == c_last - c_first;
+  }
   lastc = __shfl_sync(0xffffffffu, lastc, 0);
   if (!lastc) return;
-  __threadfence();
   if (nval <= 32) {
     if (lane < nval) {
       float sum = 0.f;

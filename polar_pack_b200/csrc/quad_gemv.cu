@@ -513,6 +513,9 @@ __host__ __device__ inline uint32_t quad_scratch_bytes(bool nk, int nb, int M) {
 template <bool NK, int NB, bool PLUG>
 __device__ __forceinline__ void quad_gemv_run(const QuadParams& p) {
   constexpr int NW = quad_warps(NK, NB);
+  // the first code copies need the tensor map: fetch it while the
+  // parameters and per-CTA tables are read
+  if (threadIdx.x == 0) prefetch_tmap(&p.tmap);
   pdl_launch_dependents();
   const bool prepared = p.tables != nullptr;
   uint32_t v[kLutWordsPerThread];

@@ -434,7 +434,9 @@ inline QuadTcPlan quad_tc_plan(int64_t Mc, int64_t N, int64_t K, int sms) {
   pl.nmma = (int)((Mc + 15) / 16 * 16);
   pl.tiles = (int)cdiv(N, kTcRows);
   pl.kchunks = (int)(K / kTcK);
-  // at most one wave of CTAs, at least 8 stages of K each
+  // at most one wave of CTAs, at least 8 stages of K each (more splits in
+  // several waves measured slower at 64 rows: the partials cost more than
+  // the idle SMs of one wave)
   int sp = sms / pl.tiles;
   const int cap = pl.kchunks / 8 > 1 ? pl.kchunks / 8 : 1;
   pl.splits = sp < cap ? sp : cap;
