@@ -547,7 +547,7 @@ __device__ __forceinline__ void quad_gemv_run(const QuadParams& p) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int wu0 = warp_start<NW>(cu0, cu1, warp), wu1 = warp_start<NW>(cu0, cu1, warp + 1);
   // PLUG: the plug-stream offsets of units wu0..wu1 (the host keeps
-  // wu1 - wu0 < kPlugTabEntries), loaded now, stored after the table wait
+  // wu1 - wu0 < kPlugTabEntries), loaded now, stored after the CTA barrier
   uint32_t po0 = 0u, po1 = 0u;
   if constexpr (PLUG) {
     const int nu = wu1 - wu0;
@@ -566,7 +566,7 @@ __device__ __forceinline__ void quad_gemv_run(const QuadParams& p) {
   // lane 0 of each warp initialises its ring and issues its first units
   // before the barrier (the rings overlap nothing written before it).
   // PLUG: codes only for now; the plug copies, which need the offsets,
-  // arrive on the barriers after the table wait
+  // arrive on the same barriers after the CTA barrier
   if (wu0 < wu1 && (threadIdx.x & 31) == 0) {
     rg.prologue([&](uint32_t slot, uint32_t bar, int, int tile, int kc) {
       QuadOp<NK, NB, false>::template issue<!PLUG>(p, slot, bar, tile, kc);
@@ -575,12 +575,8 @@ __device__ __forceinline__ void quad_gemv_run(const QuadParams& p) {
   uint32_t* stage = reinterpret_cast<uint32_t*>(pp_smem + (L.scratch - base));
   if (!prepared) quad_lut_stage(stage, v);
   __syncthreads();
-  if (prepared) {
-    mbar_wait_bounded(tbar, 0u, status);
-  } else {
-    quad_lut_fanout(pp_smem + (L.lut - base), stage);
-    __syncthreads();
-  }
+  // PLUG: the plug copies of the prologue units go out as soon as the
+  // warp's unit offsets have arrived, before the table wait
   if constexpr (PLUG) {
     if (wu0 < wu1) {
       const uint32_t ptab = L.ptab + (uint32_t)warp * (kPlugTabEntries * 4u);
@@ -602,6 +598,12 @@ __device__ __forceinline__ void quad_gemv_run(const QuadParams& p) {
         }
       }
     }
+  }
+  if (prepared) {
+    mbar_wait_bounded(tbar, 0u, status);
+  } else {
+    quad_lut_fanout(pp_smem + (L.lut - base), stage);
+    __syncthreads();
   }
   // everything above reads only weights; activations, the workspace and the
   // outputs may belong to the previous kernel of the stream
