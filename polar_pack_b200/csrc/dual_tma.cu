@@ -64,6 +64,7 @@ struct DualTOp {
   static constexpr int kNBat = 8;
   static constexpr int kUnitBytes = (int)kDualTUnit;
   static constexpr int kPrefetch = 0;
+  static constexpr bool kGather16 = false;
   using Buf = DualTBuf;
 
   const DualTParams& p;

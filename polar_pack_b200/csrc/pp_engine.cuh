@@ -262,7 +262,8 @@ __device__ __forceinline__ void run_partition(Op& op, const Partition& pt, float
 struct CtaTables {
   int* wstart;  // [NW + 1] warp range starts, wstart[NW] = end of the CTA range
   int* wtile;   // [NW + 1] tile of wstart[w]
-  int* cnt;     // [2 * NW] split-tile arrival counters, indexed 2 * (first warp) + slot
+  int* cnt;     // [2 * NW] split-tile arrival counters, indexed 2 * (first warp) + slot;
+                // cnt[2 * NW]: warps of the CTA done (the gather's completion signal)
 };
 
 // Warp w of the CTA range [cu0, cu1) starts at cu0 + (cu1 - cu0) * w / NW;
@@ -280,7 +281,7 @@ __device__ __forceinline__ void cta_tables_init(const CtaTables& tb, int cu0, in
     tb.wstart[i] = w0;
     tb.wtile[i] = w0 / upt;
   }
-  if (i < 2 * NW) tb.cnt[i] = 0;
+  if (i <= 2 * NW) tb.cnt[i] = 0;
 }
 
 // The unit order of one warp: segments [a0,b0) split tail, [a1,b1) split
@@ -431,11 +432,19 @@ __device__ __forceinline__ void close_split(Op& op, const Partition& pt, const C
   // elements per lane at a time, whose plug corrections are loaded before
   // any of them is stored (store_outputs)
   if (nval <= 32) {
+    float sum = 0.f;
     if (lane < nval) {
-      float sum = 0.f;
 #pragma unroll
       for (int w = 0; w < NW; ++w)
         if (so[w] >= 0) sum += red[so[w] + lane];
+    }
+    if constexpr (Op::kGather16) {  // batch-1 gather: 16-byte stores (all lanes)
+      if (inside && nval == 32 && op.gather16(T)) {
+        op.gather_store16(T, sum);
+        return;
+      }
+    }
+    if (lane < nval) {
       if (inside) {
         const float sv[1] = {sum};
         store_outputs<Op, 1>(op, lane, 32, nval, T, sv);
@@ -481,12 +490,20 @@ __device__ __forceinline__ void close_split(Op& op, const Partition& pt, const C
   lastc = __shfl_sync(0xffffffffu, lastc, 0);
   if (!lastc) return;
   if (nval <= 32) {
-    if (lane < nval) {
-      float sum = 0.f;
+    float sum = 0.f;
+    if (lane < nval)
       for (int c = c_first; c <= c_last; ++c) {
         const int w = (c == c_first && pt.cta_start[c] < T * upt) ? 1 : 0;
         sum += __ldcg(pt.slots + ((int64_t)c * 2 + w) * (int64_t)nval + lane);
       }
+    bool done16 = false;
+    if constexpr (Op::kGather16) {  // batch-1 gather: 16-byte stores (all lanes)
+      if (nval == 32 && op.gather16(T)) {
+        op.gather_store16(T, sum);
+        done16 = true;
+      }
+    }
+    if (!done16 && lane < nval) {
       const float sv[1] = {sum};
       store_outputs<Op, 1>(op, lane, 32, nval, T, sv);
     }

@@ -413,10 +413,51 @@ struct QuadOp {
     }
   }
 
+  // Batch-1 gather with 16-byte stores: an 8-row tile is 8 consecutive
+  // elements of each model's block, so one store per model and rank
+  // replaces eight 2-byte stores (each a separate NVLink write to a peer).
+  static constexpr bool kGather16 = NK && NB == 1;
+  __device__ __forceinline__ bool gather16(int tile) const {
+    return p.gather.world && p.gather.vec && tile * 8 + 8 <= Nv;
+  }
+  // lane = element (model lane >> 3, row lane & 7) of tile `tile`; v is the
+  // sum before the plug correction and the scale
+  __device__ __forceinline__ void gather_store16(int tile, float v) const {
+    const int lane = threadIdx.x & 31, q = lane >> 3;
+    const uint32_t hv = __half_as_ushort(__float2half_rn((v + corr_at(q, 0, tile * 8 + (lane & 7))) * p.scale[q]));
+    const uint32_t pair = hv | (__shfl_down_sync(0xffffffffu, hv, 1) << 16);
+    const uint32_t p1 = __shfl_down_sync(0xffffffffu, pair, 2);
+    const uint32_t p2 = __shfl_down_sync(0xffffffffu, pair, 4);
+    const uint32_t p3 = __shfl_down_sync(0xffffffffu, pair, 6);
+    if ((lane & 7) == 0) {
+      const int64_t o = (int64_t)q * p.gather.ld + p.gather.row0 + (int64_t)tile * 8;
+      const uint4 w = make_uint4(pair, p1, p2, p3);
+#pragma unroll
+      for (int r = 0; r < kMaxPeers; ++r)
+        if (r < p.gather.world) *reinterpret_cast<uint4*>(p.gather.out[r] + o) = w;
+    }
+  }
+
   // The plug corrections of a batch tile are loaded before its outputs are
   // stored: otherwise each load would wait for the store before it (the
   // compiler cannot rule out that they alias).
   __device__ __forceinline__ void store_tile(int tile) {
+    if constexpr (kGather16) {
+      if (gather16(tile)) {  // warp-uniform
+        // lane (g, 0) holds row pr(g)'s four model sums; row r is on lane
+        // 4 g_r with g_r = ((r & 3) << 1) | (r >> 2)
+        const int lane = threadIdx.x & 31, q = lane >> 3, r = lane & 7;
+        const int src = 4 * (((r & 3) << 1) | (r >> 2));
+        // (the value a shuffle passes is the source lane's: fetch all four
+        // models, then choose by this lane's model)
+        const float m0 = __shfl_sync(0xffffffffu, acc[0][0][0][0], src);
+        const float m1 = __shfl_sync(0xffffffffu, acc[0][0][0][2], src);
+        const float m2 = __shfl_sync(0xffffffffu, acc[0][0][1][0], src);
+        const float m3 = __shfl_sync(0xffffffffu, acc[0][0][1][2], src);
+        gather_store16(tile, q == 0 ? m0 : q == 1 ? m1 : q == 2 ? m2 : m3);
+        return;
+      }
+    }
 #pragma unroll
     for (int t = 0; t < kT; ++t) {
       const int f = tile * kTileW + (NK ? pr : 4 * g + t);
@@ -511,7 +552,7 @@ __host__ __device__ inline uint32_t quad_scratch_bytes(bool nk, int nb, int M) {
 // its first S units, whose copies overlap the table build or copy.  Then
 // every warp streams and reduces on its own; there is no closing barrier.
 template <bool NK, int NB, bool PLUG>
-__device__ __forceinline__ void quad_gemv_run(const QuadParams& p) {
+__device__ __forceinline__ int* quad_gemv_run(const QuadParams& p) {
   constexpr int NW = quad_warps(NK, NB);
   // the first code copies need the tensor map: fetch it while the
   // parameters and per-CTA tables are read
@@ -528,10 +569,10 @@ __device__ __forceinline__ void quad_gemv_run(const QuadParams& p) {
                                          PLUG ? p.pcap : 0u);
   if (!L.ok) {  // the host plans for this never to happen
     if (threadIdx.x == 0) atomicExch(status, 2);
-    return;
+    return nullptr;
   }
   const int cu0 = p.cta_start[blockIdx.x], cu1 = p.cta_start[blockIdx.x + 1];
-  if (cu0 >= cu1) return;  // uniform over the CTA
+  if (cu0 >= cu1) return nullptr;  // uniform over the CTA
   const uint32_t tbar = L.flag;  // mbarrier of the prepared-table copies
   if (prepared && threadIdx.x == 0) {
     mbar_init(tbar, 1);
@@ -608,17 +649,18 @@ __device__ __forceinline__ void quad_gemv_run(const QuadParams& p) {
   // everything above reads only weights; activations, the workspace and the
   // outputs may belong to the previous kernel of the stream
   pdl_wait();
-  if (wu0 >= wu1) return;
+  if (wu0 >= wu1) return tb.cnt + 2 * NW;
   if (L.direct) quad_body<NK, NB, true, PLUG>(p, pt, L, rg, tb, cu0, cu1, wu0, wu1, status);
   else quad_body<NK, NB, false, PLUG>(p, pt, L, rg, tb, cu0, cu1, wu0, wu1, status);
+  return tb.cnt + 2 * NW;
 }
 
 // Every warp leaves quad_gemv_run, whatever path it took, and then takes
 // part in the gather's completion signal.
 template <bool NK, int NB, bool PLUG>
 __global__ void __launch_bounds__(quad_warps(NK, NB) * 32, 1) quad_gemv_kernel(const __grid_constant__ QuadParams p) {
-  quad_gemv_run<NK, NB, PLUG>(p);
-  if (p.gather.world) gather_signal(p.gather);
+  int* const cta_arrivals = quad_gemv_run<NK, NB, PLUG>(p);
+  if (p.gather.world) gather_signal(p.gather, cta_arrivals, quad_warps(NK, NB));
 }
 
 // Generic fallback for layouts the vector paths do not take (unaligned or
@@ -731,7 +773,10 @@ int launch_quad(QuadParams& prm, int grid, int idx, cudaStream_t s) {
   prm.layout_base = (uint32_t)reserved_smem(current_device());
   prm.layout = quad_layout(prm.layout_base, prm.smem_bytes, NW, stages, redb, true, prm.pcap);
   if (prm.gather.world) {  // completion count of this launch: the counter below the status word
-    prm.gather.warps = grid * NW;
+    prm.gather.ctas = grid;
+    prm.gather.vec = (prm.gather.ld % 8 == 0 && prm.gather.row0 % 8 == 0) ? 1 : 0;
+    for (int q = 0; q < prm.gather.world; ++q)
+      if (!aligned(prm.gather.out[q], 16)) prm.gather.vec = 0;
     prm.gather.done = reinterpret_cast<uint32_t*>(prm.part.counters + (kMaxGrid - 2));
   }
   return launch_kernel("quad_gemv_kernel", launch_overlap(), kern, dim3(grid), dim3(NW * 32), (size_t)max_smem, s,
