@@ -295,6 +295,8 @@ def run_ours(args):
     for i in range(args.warmup):
         step(i)
     torch.cuda.synchronize(dev)
+    parity = gathered_parity(torch, dist, step, sets, full_sets, xs, pgroups, gathers, world, dev, M) \
+        if world > 1 else None
 
     # one CUDA graph per replica set: the timed loop replays whole steps, so
     # host launch latency is not part of the measurement
@@ -343,6 +345,12 @@ def run_ours(args):
         t = torch.tensor([ms], dtype=torch.float64, device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms = float(t.item())
+        if peers is not None:   # a bounded gather wait that gave up during the timed steps fails the run
+            st_ = torch.tensor([int(peers.status.item())], dtype=torch.int64, device=dev)
+            dist.all_reduce(st_, op=dist.ReduceOp.MAX)
+            parity["wait_status_after_timing"] = int(st_.item())
+            if int(st_.item()) != 0:
+                raise RuntimeError(f"a gather wait gave up during the timed steps (status {int(st_.item())})")
     total_bytes = avg_bytes * K_steps
     value = total_bytes / (ms * 1e-3) / 1e9
 
@@ -422,6 +430,7 @@ def run_ours(args):
                    "timing": ("CUDA graph replay of whole steps" if use_graphs else "eager launches") +
                              ("; launch overlap on" if not args.no_overlap else ""),
                    "per_shape_gemv_kernel": per_shape,
+                   "parity": parity,
                    "decode_step_3b": decode,
                    "dual_gemv_b1": dual,
                    "batched_rows": batched},
@@ -431,8 +440,7 @@ def run_ours(args):
                      "achieved_from": "algorithmic bytes (4NK + 12P + 2MK + 8MN) over the 4 shapes / their "
                                       "per-launch CUDA-event time (graph of back-to-back launches)",
                      "traffic": traffic,
-                     "traffic_of": "one 2048x11008 launch (ncu dram read + write; "
-                                   "profiles/quad_gemv_fused_2048x11008.md)"},
+                     "traffic_of": "one 2048x11008 launch (ncu dram read + write)"},
         "e2e": e2e,
         "gpu_launches": launches_per_step * K_steps,
         "gpu_launches_note": "per Linear: the GEMV kernel with the plug correction fused in (batch 1)" +
@@ -451,6 +459,49 @@ def run_ours(args):
         dist.destroy_process_group()
     if rank == 0:
         print(json.dumps(res))
+
+
+def gathered_parity(torch, dist, step, sets, full_sets, xs, pgroups, gathers, world, dev, M):
+    """One gathered step on every rank against the full (unsharded) Linears
+    on this GPU; raises on a mismatch so that a multi-GPU line always
+    carries a checked result.  The shards' split-K order differs from the
+    full Linear's, so the bar is the tests' tolerance, not bit equality."""
+    from polar_pack_b200.parallel import row_shard
+    from polar_pack_b200.quadpack import quad_linear
+    step(0)
+    torch.cuda.synchronize(dev)
+    if pgroups:
+        res = pgroups[0].peers.view(0)[:4 * pgroups[0].total].view(4, 1, -1).clone()
+        cols = pgroups[0].cols
+        got = [[res[k, :, cols[j]:cols[j] + l.N] for k in range(4)] for j, l in enumerate(full_sets[0])]
+        status = int(pgroups[0].peers.status.item())
+    else:
+        send, recv = gathers[0]
+        rv = recv.view(world, 4, M, -1)
+        got, col = [], 0
+        for l in full_sets[0]:
+            w = -(-l.N // world)
+            got.append([torch.cat([rv[r, k, :, col:col + row_shard(l.N, world, r)[1] - row_shard(l.N, world, r)[0]]
+                                   for r in range(world)], dim=1) for k in range(4)])
+            col += w
+        status = 0
+    worst = 0.0
+    for j, l in enumerate(full_sets[0]):
+        ref = quad_linear(xs[j], l)
+        for k in range(4):
+            den = float(ref[k].double().abs().max())
+            err = float((got[j][k].double() - ref[k].double()).abs().max()) / (den if den > 0 else 1.0)
+            worst = max(worst, err)
+    t = torch.tensor([worst, float(status)], dtype=torch.float64, device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    worst, status = float(t[0]), int(t[1])
+    ok = worst <= 1e-3 and status == 0
+    if not ok:
+        raise RuntimeError(f"gathered outputs disagree with the full Linears: max rel err {worst:.3g}, "
+                           f"wait status {status}")
+    return {"ok": True, "max_rel_err": worst, "wait_status": status, "ranks_checked": world,
+            "what": "every rank's gathered outputs of one step vs the unsharded Linears on its GPU "
+                    "(max over ranks and models of max|y-y_full|/max|y_full|, bar 1e-3)"}
 
 
 def run_batched_leg(torch, dev, args, lib, stream, sets, rows=(16, 64)):

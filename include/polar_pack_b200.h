@@ -253,6 +253,23 @@ PP_API int pp_quad_unpack(const uint32_t* codes, int64_t n, const uint32_t* plug
                    const void* const luts[7], const float* scales,
                    void* const out[4], void* stream);
 
+/* Plain FP16 Linear for the rows of a `.quadpack` Linear past the coded
+ * range: the per-model FP16 tails, which the reference writes raw for every
+ * model longer than n_min (quaternion_packer.py:118-126) and restores as is
+ * (quaternion_packer.py:201-210).  For every model k with w[k] != NULL:
+ *
+ *   out_k[m][r] = fp16( sum_i x_k[m][i] * w_k[r][i] )   (FP32 accumulate)
+ *
+ * x_k = x + k * ldx_model (ldx_model = 0: all models read the same (M, K)
+ * activations, row stride ldx_m, contiguous rows).  w[k]: R rows of K FP16
+ * weights, row stride ldw >= K, any alignment (tail rows start wherever the
+ * Linear crosses n_min).  out[k]: (M, R) FP16 with strides (ldo_m, ldo_n);
+ * models with w[k] == NULL are not written.
+ */
+PP_API int pp_f16_linear(const void* x, int64_t ldx_m, int64_t ldx_model, int64_t M, int64_t K,
+                         const void* const w[4], int64_t ldw, int64_t R, void* const out[4], int64_t ldo_m,
+                         int64_t ldo_n, void* stream);
+
 /* ------------------------------------------------------------------ dual --
  * Kernel-layout fused dequant GEMM, the drop-in for `polar_dual_bitpacked`
  * (reference polar_kernels.py:98-115, kernel 30-95):

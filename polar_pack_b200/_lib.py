@@ -68,6 +68,7 @@ _SIGNATURES = {
                         _c_void_p], _int),
     "pp_quad_unpack": ([_c_void_p, _i64, _c_void_p, _c_void_p, _i64, _i64, _u32, _PTR7, _c_void_p,
                         _PTR4, _c_void_p], _int),
+    "pp_f16_linear": ([_c_void_p, _i64, _i64, _i64, _i64, _PTR4, _i64, _i64, _PTR4, _i64, _i64, _c_void_p], _int),
     "pp_dual_gemm_workspace_bytes": ([_i64, _i64, _i64, _i64, _i64, ctypes.POINTER(_size_t)], _int),
     "pp_dual_gemm": ([_c_void_p, _i64, _i64, _c_void_p, _i64, _i64, _c_void_p, _i64, _c_void_p,
                       _c_void_p, _c_void_p, _c_void_p, _c_void_p, _i64, _i64, _i64, _i64, _i64,

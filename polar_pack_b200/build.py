@@ -10,6 +10,7 @@ than all sources.  nvcc cross-compiles, so no GPU is needed.
 from __future__ import annotations
 
 import argparse
+import concurrent.futures as cf
 import os
 import shutil
 import subprocess
@@ -56,10 +57,17 @@ def build(force: bool = False, verbose: bool = False) -> Path:
     objdir.mkdir(exist_ok=True)
     objs = []
     log = []
-    for src in sources():
+
+    def compile_one(src: Path):
         obj = objdir / (src.stem + ".o")
         cmd = [nvcc, *ARCH_FLAGS, *NVCC_FLAGS, "-c", str(src), "-o", str(obj)]
         r = subprocess.run(cmd, capture_output=True, text=True)
+        return src, obj, cmd, r
+
+    # the translation units are independent: compile them in parallel
+    with cf.ThreadPoolExecutor(max_workers=max(1, min(len(sources()), os.cpu_count() or 1))) as pool:
+        results = list(pool.map(compile_one, sources()))
+    for src, obj, cmd, r in results:
         log.append(f"$ {' '.join(cmd)}\n{r.stdout}{r.stderr}")
         if r.returncode != 0:
             sys.stderr.write("\n".join(log))

@@ -149,25 +149,65 @@ class QuadPackDevice:
         self.header = f.header
         self.device = torch.device(device)
         h = f.header
-        self.codes = torch.from_numpy(np.asarray(f.codes)).to(self.device)
-        self.plug_idx = torch.from_numpy(np.asarray(f.plug_idx).view(np.int32)).to(self.device)
-        self.plug_vals = torch.from_numpy(np.ascontiguousarray(f.plug_vals)).to(self.device)
+        self.codes = upload(f.codes, np.int32, self.device)
+        self.plug_idx = upload(f.plug_idx, np.int32, self.device)
+        self.plug_vals = upload(f.plug_vals, np.float16, self.device)
+        # raw FP16 weights of each model beyond n_min (quaternion_packer.py:118-126)
+        self.tails = [upload(t, np.float16, self.device) for t in f.tails]
         self.luts = [t.to(self.device) for t in quad_luts(h.r_max, MU)]
         # replicated shared-memory image of the tables, copied in by each launch
         self.tables = _lib.prepare_tables(self.luts, self.device)
         self.scales = [float(s) for s in h.scales]
         self._bad = torch.zeros(1, dtype=torch.int32, device=self.device)
+        self._linears: dict = {}
 
     def _plug_range(self, start: int, stop: int) -> tuple[int, int]:
         return self.file.plug_range(start, stop)
 
-    def linear(self, offset: int, N: int, K: int) -> QuadLinearSlice:
-        """The Linear whose ``(N, K)`` weights start at flat position ``offset``."""
+    def model_length(self, k: int) -> int:
+        """Weights of model k: the coded range plus its FP16 tail."""
+        return self.header.n + int(self.header.tails[k])
+
+    def linear(self, offset: int, N: int, K: int):
+        """The Linear whose ``(N, K)`` weights start at flat position ``offset``.
+
+        A range inside the coded part ``[0, n_min)`` gives a
+        :class:`QuadLinearSlice` (all four models, one fused launch).  A range
+        that reaches past ``n_min`` gives a :class:`QuadTailedLinear`: its
+        rows below ``n_min`` are served by the fused kernel, the rest from the
+        FP16 tails of the models long enough to hold the whole Linear.
+
+        The first call for a range prepares its plug entries in place (the
+        norm byte of every plugged code of ``self.codes`` is zeroed, so it
+        decodes to zeros and the plug value enters as a correction; see
+        ``pp_quad_prepare_plugs``) and the slice is kept: later calls for the
+        same range return it without preparing again.  :meth:`unpack` stays
+        exact on prepared ranges because it substitutes every plugged
+        position; a plain table decode of ``self.codes`` (``quad_decode``)
+        does not and gives zeros at plugged positions.
+        """
         n = self.header.n
-        if offset < 0 or offset + N * K > n:
-            raise ValueError(f"Linear [{offset}, {offset + N * K}) is outside the coded range [0, {n})")
+        longest = max(self.model_length(k) for k in range(N_MODELS))
+        if offset < 0 or N < 0 or K < 0 or offset + N * K > longest:
+            raise ValueError(f"Linear [{offset}, {offset + N * K}) is outside every model (longest {longest})")
+        key = (offset, N, K)
+        hit = self._linears.get(key)
+        if hit is None:
+            if offset + N * K <= n:
+                hit = self._make_linear(offset, N, K)
+            else:
+                hit = QuadTailedLinear(self, offset, N, K)
+            self._linears[key] = hit
+        return hit
+
+    def _make_linear(self, offset: int, N: int, K: int) -> QuadLinearSlice:
         p_lo, p_hi = self._plug_range(offset, offset + N * K)
         codes = self.codes[offset:offset + N * K].view(N, K)
+        if codes.data_ptr() % 16 and K % 4 == 0:
+            # the streaming kernels read 16-byte aligned rows: a Linear at an
+            # offset that is not a multiple of 4 codes gets its own aligned
+            # copy, prepared instead of the stream's
+            codes = codes.clone()
         pi = pv = wb = None
         if p_hi > p_lo:
             # one-time preparation: window index + zero norm byte of plugged codes
@@ -205,6 +245,116 @@ class QuadPackDevice:
                   ctypes.cast(sc, ctypes.c_void_p) if sc is not None else None,
                   _lib.ptrs(outs, 4), _lib.stream_handle(self.device))
         return outs
+
+
+@dataclass(frozen=True)
+class TailSplit:
+    """How a Linear at flat ``offset`` with ``(N, K)`` weights splits at ``n_min``.
+
+    Rows ``[0, coded)`` lie wholly in the coded range; row ``coded`` is cut
+    by ``n_min`` when ``straddle``; rows ``[first_tail, N)`` lie wholly past
+    it, and their weights start ``tail_start`` elements into each model's
+    tail.  ``present[k]``: model k is long enough to hold the whole Linear
+    (quaternion_packer.py:55-57: model k has ``n_min + tails_k`` weights).
+    """
+    coded: int
+    straddle: bool
+    first_tail: int
+    tail_start: int
+    present: tuple
+
+
+def tail_split(offset: int, N: int, K: int, n: int, tails) -> TailSplit:
+    end = offset + N * K
+    if offset >= n:
+        coded, straddle = 0, False
+    else:
+        coded = min(N, (n - offset) // K) if K else N
+        straddle = coded < N and offset + coded * K < n
+    first = coded + (1 if straddle else 0)
+    present = tuple(end <= n + int(t) for t in tails)
+    return TailSplit(coded, straddle, first, offset + first * K - n, present)
+
+
+class QuadTailedLinear:
+    """A packed Linear whose flat range reaches past ``n_min``.
+
+    The reference stores every weight of model k beyond the shortest model's
+    length ``n_min`` as raw FP16 in that model's tail (quaternion_packer.py:
+    118-126) and appends it unchanged when restoring (201-210).  Rows below
+    ``n_min`` run on the fused quad kernel (all four models); the row cut by
+    ``n_min`` is assembled once per model from its GPU-unpacked coded part
+    (``fp16(w * s_k)``, plugs substituted) and its tail part; rows past
+    ``n_min`` read each model's tail in place (``pp_f16_linear``).  A call
+    returns four outputs ``(M, N)``; models whose weights end before the
+    Linear does have no such Linear and get ``None``.
+    """
+
+    def __init__(self, pack: "QuadPackDevice", offset: int, N: int, K: int):
+        h = pack.header
+        self.pack, self.offset, self.N, self.K = pack, offset, N, K
+        self.split = sp = tail_split(offset, N, K, h.n, h.tails)
+        if not any(sp.present):
+            raise ValueError(f"no model holds the Linear [{offset}, {offset + N * K})")
+        self.coded = pack._make_linear(offset, sp.coded, K) if sp.coded else None
+        self.straddle_rows = [None] * N_MODELS
+        if sp.straddle:
+            r0 = offset + sp.coded * K
+            dec = pack.unpack(r0, h.n, scaled=True)
+            for k in range(N_MODELS):
+                if sp.present[k]:
+                    row = torch.empty(K, dtype=torch.float16, device=pack.device)
+                    row[:h.n - r0] = dec[k]
+                    row[h.n - r0:] = pack.tails[k][:r0 + K - h.n]
+                    self.straddle_rows[k] = row
+        R = N - sp.first_tail
+        self.tail_ptrs = [pack.tails[k][sp.tail_start:].data_ptr() if (sp.present[k] and R > 0) else None
+                          for k in range(N_MODELS)]
+
+    @property
+    def present(self) -> tuple:
+        return self.split.present
+
+    def __call__(self, x: torch.Tensor, out=None) -> list:
+        if x.dim() != 2 or x.shape[1] != self.K:
+            raise ValueError(f"x must be (M, {self.K}), got {tuple(x.shape)}")
+        if x.dtype != torch.float16:
+            raise ValueError("x must be fp16")
+        dev = _lib.require_cuda(x)
+        if x.stride(1) != 1:
+            x = x.contiguous()
+        M, sp = x.shape[0], self.split
+        if out is None:
+            buf = torch.empty((N_MODELS, M, self.N), dtype=torch.float16, device=dev)
+            out = [buf[k] for k in range(N_MODELS)]
+        if self.coded is not None:
+            quad_linear(x, self.coded, out=[o[:, :sp.coded] for o in out])
+        lib, s = _lib.load(), _lib.stream_handle(dev)
+        if sp.straddle:
+            w = (ctypes.c_void_p * 4)(*[_lib.ptr(r) for r in self.straddle_rows])
+            o = _lib.ptrs([o_[:, sp.coded:] for o_ in out], 4)
+            _lib.check(lib.pp_f16_linear(x.data_ptr(), x.stride(0), 0, M, self.K, w, self.K, 1, o,
+                                         out[0].stride(0), out[0].stride(1), s))
+        R = self.N - sp.first_tail
+        if R > 0:
+            w = (ctypes.c_void_p * 4)(*self.tail_ptrs)
+            o = _lib.ptrs([o_[:, sp.first_tail:] for o_ in out], 4)
+            _lib.check(lib.pp_f16_linear(x.data_ptr(), x.stride(0), 0, M, self.K, w, self.K, R, o,
+                                         out[0].stride(0), out[0].stride(1), s))
+        return [out[k] if sp.present[k] else None for k in range(N_MODELS)]
+
+
+def upload(arr, view_dtype, device, chunk: int = 1 << 26) -> torch.Tensor:
+    """Copy a host array (read-only memmaps included) to ``device`` in
+    chunks, viewed as ``view_dtype``; each chunk is copied into a writable
+    host buffer first, so no tensor ever aliases read-only memory."""
+    a = np.asarray(arr).view(view_dtype)
+    out = torch.empty(a.shape, dtype=torch.from_numpy(np.empty(0, view_dtype)).dtype, device=device)
+    flat_in, flat_out = a.reshape(-1), out.view(-1)
+    for i in range(0, flat_in.size, chunk):
+        j = min(i + chunk, flat_in.size)
+        flat_out[i:j].copy_(torch.from_numpy(np.array(flat_in[i:j], copy=True)))
+    return out
 
 
 def prepare_unit_plugs(plug_idx: torch.Tensor, plug_vals: torch.Tensor, window_base: torch.Tensor, offset: int,
@@ -386,10 +536,12 @@ class DevicePackedStream(QuadPackDevice):
         self.plug_idx = (pos & 0xFFFFFFFF).to(torch.int64).to(torch.int32) if pos.numel() else \
             torch.zeros(0, dtype=torch.int32, device=self.device)
         self.plug_vals = p["plug_vals"].contiguous()
+        self.tails = [t.contiguous() for t in p["tail_vals"]]
         self.luts = [t.to(self.device) for t in quad_luts(p["r_max"], MU)]
         self.tables = _lib.prepare_tables(self.luts, self.device)
         self.scales = [float(x) for x in p["scales"]]
         self._bad = torch.zeros(1, dtype=torch.int32, device=self.device)
+        self._linears = {}
 
     def _plug_range(self, start: int, stop: int) -> tuple[int, int]:
         return (int(np.searchsorted(self._pos_host, start)), int(np.searchsorted(self._pos_host, stop)))

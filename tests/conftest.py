@@ -55,3 +55,25 @@ def cuda():
     from polar_pack_b200 import _lib
     _lib.load()
     return torch.device("cuda", 0)
+
+
+@pytest.fixture(scope="session")
+def quadpack_small_stream(quadpack_golden):
+    """The complete reference-written ``.quadpack`` of ``quadpack_small.npz``.
+
+    The fixture file keeps only the header, two code windows and the tails;
+    the oracle writer rebuilds the whole stream from the recorded seed, and
+    its SHA-256 must equal the one recorded from the reference's own
+    ``pack_quad`` -- so the bytes returned are the reference's bytes.
+    """
+    import hashlib
+
+    from make_golden import correlated_models
+    from oracle import formats as of
+    g = quadpack_golden
+    seed, n, *extra = (int(x) for x in g["seed_models"])
+    flat = correlated_models(np.random.default_rng(seed), 4, (n + max(extra),))
+    models = [flat[k][: n + extra[k]].astype(np.float32) for k in range(4)]
+    buf = of.pack_quad_bytes(models)
+    assert hashlib.sha256(buf).hexdigest() == str(g["sha256"])
+    return buf

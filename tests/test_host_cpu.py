@@ -110,3 +110,19 @@ def test_product_never_imports_oracle():
     for p in pkg.rglob("*.py"):
         src = p.read_text()
         assert "import oracle" not in src and "from oracle" not in src, p
+
+
+def test_tail_split_rows():
+    """Row split of a Linear at n_min (quaternion_packer.py:55-57, 118-126)."""
+    from polar_pack_b200.quadpack import tail_split
+    n, tails = 1000, [0, 40, 0, 17]
+    s = tail_split(980, 7, 8, n, tails)             # rows 0,1 coded, row 2 cut, rows 3.. tail
+    assert (s.coded, s.straddle, s.first_tail, s.tail_start) == (2, True, 3, 4)
+    assert s.present == (False, True, False, False)
+    s = tail_split(988, 7, 4, n, tails)             # rows end exactly at n_min
+    assert (s.coded, s.straddle, s.first_tail, s.tail_start) == (3, False, 3, 0)
+    assert s.present == (False, True, False, True)
+    s = tail_split(1008, 4, 8, n, tails)            # wholly in the tails
+    assert (s.coded, s.straddle, s.first_tail, s.tail_start) == (0, False, 0, 8)
+    s = tail_split(0, 10, 8, n, tails)              # wholly coded
+    assert (s.coded, s.straddle) == (10, False) and all(s.present)

@@ -45,9 +45,14 @@ def _stream(dev, shapes, seed=5):
 
 
 SHAPES = [(256, 512), (2048, 256), (8, 64), (1000, 1028)]  # (N out, K in)
+# rows not a multiple of 8: the first launch mixes 16-byte tile stores with a
+# 2-byte tail tile, the second starts at row 1001 (2-byte stores throughout),
+# the third at the aligned row 1008 again
+RAGGED = [(1001, 512), (7, 64), (256, 128)]
 
 
-def test_gather_single_rank_matches_fused(cuda):
+@pytest.mark.parametrize("SHAPES", [SHAPES, RAGGED], ids=["aligned", "ragged"])
+def test_gather_single_rank_matches_fused(cuda, SHAPES):
     from polar_pack_b200.parallel import PeerBuffers, PeerShardedGroup
     from polar_pack_b200.quadpack import quad_linear
     st = _stream(cuda, SHAPES)

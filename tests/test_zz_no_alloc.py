@@ -71,6 +71,28 @@ def test_static_scratch_matches_workspace_entry_point(cuda, layout, K, N, M):
             np.testing.assert_array_equal(got[k].numpy().view(np.uint16), ref[k].numpy().view(np.uint16))
 
 
+def test_static_scratch_allocates_no_device_memory(cuda):
+    """The entry point's reason to exist: free device memory (cudaMemGetInfo)
+    is the same before and after two calls, with every buffer allocated
+    before the first measurement."""
+    codes, luts, x = _problem(2048, 11008, 3, "nk", seed=9)
+    codes, luts, x = codes.to(cuda), [t.to(cuda) for t in luts], x.to(cuda)
+    cv, ldk, ldn = _views(codes, "nk")
+    K, N = cv.shape
+    outs = [torch.empty((3, N), dtype=torch.half, device=cuda) for _ in range(4)]
+    L = _lib.load()
+    args = (x.data_ptr(), x.stride(0), x.stride(1), cv.data_ptr(), ldk, ldn, _lib.ptrs(luts, 7),
+            _lib.floats4([0.5, 1.0, 1.5, 2.0]), _lib.ptrs(outs, 4), outs[0].stride(0), outs[0].stride(1),
+            3, N, K, _lib.stream_handle(cuda))
+    _lib.check(L.pp_quad_gemm_static_scratch(*args))            # warm-up: the first call's set-up
+    torch.cuda.synchronize(cuda)
+    free0 = torch.cuda.mem_get_info(cuda)[0]
+    for _ in range(2):
+        _lib.check(L.pp_quad_gemm_static_scratch(*args))
+    torch.cuda.synchronize(cuda)
+    assert torch.cuda.mem_get_info(cuda)[0] == free0
+
+
 def test_static_scratch_rejects_plans_beyond_its_size(cuda):
     # kernel layout at 16 batch rows: ~2.4 MB of partial slots on a 148-SM part
     codes, luts, x = _problem(4096, 8192, 16, "kn", seed=5)
