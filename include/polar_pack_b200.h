@@ -233,6 +233,46 @@ PP_API int pp_quad_linear_fused(const void* x, int64_t ldx_m, int64_t ldx_k,
                                 int64_t M, int64_t N, int64_t K,
                                 void* workspace, size_t workspace_bytes, void* stream);
 
+/* Several independent file-layout Linears in ONE launch (no counterpart in
+ * the reference, whose callers launch one Triton kernel per matrix; each
+ * member computes what pp_quad_linear_fused computes for it).  Member j gets
+ * a share of the SMs in proportion to its codes and runs there as a launch
+ * of its own would, so the members' fixed per-launch costs (launch, table
+ * copy, first code copies, tail of the partition) overlap instead of adding
+ * up.  The members must be independent: no member reads what another writes.
+ * One launch when every member has batch 1 (M == 1), unit plugs, prepared
+ * tables, 16-byte aligned codes with K % 4 == 0, contiguous 8-byte aligned
+ * activations, at most 8 members, and fits its SM share
+ * (pp_quad_linear_group_single_launch says whether it does); otherwise the
+ * members run one after another through pp_quad_linear_fused.  Workspace as
+ * for the other entry points (pp_quad_linear_group_workspace_bytes).
+ */
+typedef struct pp_quad_linear_desc {
+  const void* x;                    /* (M, K) FP16, strides (ldx_m, ldx_k) */
+  int64_t ldx_m, ldx_k;
+  const uint32_t* codes;            /* row n at codes + n * ldw */
+  int64_t ldw;
+  const uint32_t* plug_idx;         /* as for pp_quad_linear_fused */
+  const void* plug_vals;
+  const uint32_t* plug_window_base;
+  uint32_t base_lo32;
+  const void* unit_plugs;
+  const uint32_t* unit_plug_off;
+  const void* tables;               /* prepared tables */
+  float scales[4];
+  void* out[4];                     /* (M, N) FP16, strides (ldo_m, ldo_n) */
+  int64_t ldo_m, ldo_n;
+  int64_t M, N, K;
+} pp_quad_linear_desc;
+
+PP_API int pp_quad_linear_group_workspace_bytes(int count, const pp_quad_linear_desc* descs, size_t* bytes);
+
+/* 1 if the group runs as one launch on the current device, else 0. */
+PP_API int pp_quad_linear_group_single_launch(int count, const pp_quad_linear_desc* descs);
+
+PP_API int pp_quad_linear_group(int count, const pp_quad_linear_desc* descs, void* workspace,
+                                size_t workspace_bytes, void* stream);
+
 /* FP16 decode of a (R, C) code matrix into four (R, C) FP16 matrices,
  * bit-exact with the reference kernel's chain (quad_kernels.py:103-121).
  * scales == NULL keeps the normalised weights; otherwise each is multiplied
@@ -337,6 +377,20 @@ PP_API int pp_quad_linear_gather(const void* x, int64_t ldx_k, const uint32_t* c
                                  uint32_t* const gather_flag[], uint32_t* gather_epoch,
                                  int64_t N, int64_t K, void* workspace, size_t workspace_bytes,
                                  void* stream);
+
+/* pp_quad_linear_group whose members' outputs are gathered as in
+ * pp_quad_linear_gather: member j's model-k row n goes to element
+ * k * gather_ld + gather_row0[j] + n of every rank's buffer, and the launch
+ * publishes ONE epoch for the whole group (one pp_gather_wait per group
+ * instead of one per Linear).  The members' out[] are not written.  Needs the
+ * one-launch conditions of pp_quad_linear_group (PP_ERR_INVALID otherwise):
+ * every rank must make the same number of launches into a buffer, so there
+ * is no member-by-member fallback.
+ */
+PP_API int pp_quad_linear_group_gather(int count, const pp_quad_linear_desc* descs, int world,
+                                       void* const gather_out[], int64_t gather_ld, const int64_t* gather_row0,
+                                       uint32_t* const gather_flag[], uint32_t* gather_epoch, void* workspace,
+                                       size_t workspace_bytes, void* stream);
 
 /* Makes `stream` wait until flags[q] (rank q's flag word in this rank's
  * flag array, q < world) has reached *epoch.  The wait is bounded (about a

@@ -28,6 +28,20 @@ _PTR7 = _c_void_p * 7
 _PTR4 = _c_void_p * 4
 _F4 = ctypes.c_float * 4
 
+class QuadLinearDesc(ctypes.Structure):
+    """``pp_quad_linear_desc``: one member of a grouped launch."""
+    _fields_ = [("x", ctypes.c_void_p), ("ldx_m", ctypes.c_int64), ("ldx_k", ctypes.c_int64),
+                ("codes", ctypes.c_void_p), ("ldw", ctypes.c_int64),
+                ("plug_idx", ctypes.c_void_p), ("plug_vals", ctypes.c_void_p),
+                ("plug_window_base", ctypes.c_void_p), ("base_lo32", ctypes.c_uint32),
+                ("unit_plugs", ctypes.c_void_p), ("unit_plug_off", ctypes.c_void_p),
+                ("tables", ctypes.c_void_p), ("scales", ctypes.c_float * 4),
+                ("out", ctypes.c_void_p * 4), ("ldo_m", ctypes.c_int64), ("ldo_n", ctypes.c_int64),
+                ("M", ctypes.c_int64), ("N", ctypes.c_int64), ("K", ctypes.c_int64)]
+
+
+_DESC_P = ctypes.POINTER(QuadLinearDesc)
+
 _SIGNATURES = {
     "pp_last_error": ([], ctypes.c_char_p),
     "pp_version": ([], _int),
@@ -57,6 +71,11 @@ _SIGNATURES = {
     "pp_quad_linear_fused": ([_c_void_p, _i64, _i64, _c_void_p, _i64, _c_void_p, _c_void_p, _c_void_p, _u32,
                               _c_void_p, _c_void_p, _c_void_p, _F4, _PTR4, _i64, _i64, _i64, _i64, _i64,
                               _c_void_p, _size_t, _c_void_p], _int),
+    "pp_quad_linear_group_workspace_bytes": ([_int, _DESC_P, ctypes.POINTER(_size_t)], _int),
+    "pp_quad_linear_group_single_launch": ([_int, _DESC_P], _int),
+    "pp_quad_linear_group": ([_int, _DESC_P, _c_void_p, _size_t, _c_void_p], _int),
+    "pp_quad_linear_group_gather": ([_int, _DESC_P, _int, _c_void_p, _i64, ctypes.POINTER(_i64), _c_void_p,
+                                     _c_void_p, _c_void_p, _size_t, _c_void_p], _int),
     "pp_ipc_handle": ([_c_void_p, _c_void_p, ctypes.POINTER(_size_t)], _int),
     "pp_ipc_open": ([_c_void_p, ctypes.POINTER(_c_void_p)], _int),
     "pp_ipc_close": ([_c_void_p], _int),

@@ -218,6 +218,8 @@ __global__ void __launch_bounds__(kDualTWarps * 32, 1) dual_tma_kernel(const __g
   if (cu0 >= cu1) return;  // uniform over the CTA
   Partition pt = p.part;
   pt.cta_start = p.cta_start;
+  pt.cta = blockIdx.x;
+  pt.ncta = gridDim.x;
   int* ti = reinterpret_cast<int*>(pp_smem + kDualTTables);
   const CtaTables tb{ti, ti + (NW + 1), ti + 2 * (NW + 1)};
   cta_tables_init<NW>(tb, cu0, cu1, p.part.upt);

@@ -44,6 +44,10 @@ struct Partition {
   // TMA engine only: unit start of every CTA (cta_start[G] = units), a
   // table the host fills; NULL for the register engine (equal split)
   const int* cta_start;
+  // TMA engine only: this CTA's index among the CTAs that share the
+  // partition, and their number (blockIdx.x and gridDim.x of a launch that
+  // runs one problem; a grouped launch gives each problem a range of CTAs)
+  int cta, ncta;
 };
 
 // CTA ranges of the TMA engine come from a host-filled table of at most
@@ -427,7 +431,7 @@ __device__ __forceinline__ void close_split(Op& op, const Partition& pt, const C
   __syncwarp();
   __threadfence_block();
   const bool inside = T * upt >= cu0 && T * upt + upt <= cu1;
-  float* gslot = pt.slots + ((int64_t)blockIdx.x * 2 + (T == tb.wtile[0] ? 0 : 1)) * (int64_t)nval;
+  float* gslot = pt.slots + ((int64_t)pt.cta * 2 + (T == tb.wtile[0] ? 0 : 1)) * (int64_t)nval;
   // one element per lane (batch 1): plain stores; larger tiles take eight
   // elements per lane at a time, whose plug corrections are loaded before
   // any of them is stored (store_outputs)
@@ -474,7 +478,7 @@ __device__ __forceinline__ void close_split(Op& op, const Partition& pt, const C
   }
   if (inside) return;
   // tile cut by a CTA boundary
-  const int G = gridDim.x;
+  const int G = pt.ncta;
   const int c_first = cta_of_unit(pt.cta_start, G, T * upt);
   const int c_last = cta_of_unit(pt.cta_start, G, T * upt + upt - 1);
   // the warp's slot stores are ordered before lane 0 (__syncwarp) and its

@@ -552,7 +552,7 @@ __host__ __device__ inline uint32_t quad_scratch_bytes(bool nk, int nb, int M) {
 // its first S units, whose copies overlap the table build or copy.  Then
 // every warp streams and reduces on its own; there is no closing barrier.
 template <bool NK, int NB, bool PLUG>
-__device__ __forceinline__ int* quad_gemv_run(const QuadParams& p) {
+__device__ __forceinline__ int* quad_gemv_run(const QuadParams& p, int cta, int ncta) {
   constexpr int NW = quad_warps(NK, NB);
   // the first code copies need the tensor map: fetch it while the
   // parameters and per-CTA tables are read
@@ -571,7 +571,7 @@ __device__ __forceinline__ int* quad_gemv_run(const QuadParams& p) {
     if (threadIdx.x == 0) atomicExch(status, 2);
     return nullptr;
   }
-  const int cu0 = p.cta_start[blockIdx.x], cu1 = p.cta_start[blockIdx.x + 1];
+  const int cu0 = p.cta_start[cta], cu1 = p.cta_start[cta + 1];
   if (cu0 >= cu1) return nullptr;  // uniform over the CTA
   const uint32_t tbar = L.flag;  // mbarrier of the prepared-table copies
   if (prepared && threadIdx.x == 0) {
@@ -582,6 +582,8 @@ __device__ __forceinline__ int* quad_gemv_run(const QuadParams& p) {
   }
   Partition pt = p.part;
   pt.cta_start = p.cta_start;
+  pt.cta = cta;
+  pt.ncta = ncta;
   int* ti = reinterpret_cast<int*>(pp_smem + (L.tables - base));
   const CtaTables tb{ti, ti + (NW + 1), ti + 2 * (NW + 1)};
   cta_tables_init<NW>(tb, cu0, cu1, p.part.upt);
@@ -659,7 +661,32 @@ __device__ __forceinline__ int* quad_gemv_run(const QuadParams& p) {
 // part in the gather's completion signal.
 template <bool NK, int NB, bool PLUG>
 __global__ void __launch_bounds__(quad_warps(NK, NB) * 32, 1) quad_gemv_kernel(const __grid_constant__ QuadParams p) {
-  int* const cta_arrivals = quad_gemv_run<NK, NB, PLUG>(p);
+  int* const cta_arrivals = quad_gemv_run<NK, NB, PLUG>(p, blockIdx.x, gridDim.x);
+  if (p.gather.world) gather_signal(p.gather, cta_arrivals, quad_warps(NK, NB));
+}
+
+// Several independent Linears in one launch: member j runs on CTAs
+// [first_cta[j], first_cta[j + 1]) with its own parameters, partition and
+// workspace, exactly as a launch of its own would, so the members' fixed
+// costs (launch, table copy, first code copies, tail) overlap instead of
+// adding up.  With a gather, every member stores into the same buffers and
+// the launch publishes once (the completion count spans the whole grid).
+constexpr int kMaxGroup = 8;
+
+struct QuadGroupParams {
+  int count;
+  int first_cta[kMaxGroup + 1];
+  QuadParams m[kMaxGroup];
+};
+
+template <bool NK, int NB, bool PLUG>
+__global__ void __launch_bounds__(quad_warps(NK, NB) * 32, 1)
+    quad_group_kernel(const __grid_constant__ QuadGroupParams g) {
+  int j = 0;
+  while (j + 1 < g.count && (int)blockIdx.x >= g.first_cta[j + 1]) ++j;
+  const QuadParams& p = g.m[j];
+  int* const cta_arrivals =
+      quad_gemv_run<NK, NB, PLUG>(p, (int)blockIdx.x - g.first_cta[j], g.first_cta[j + 1] - g.first_cta[j]);
   if (p.gather.world) gather_signal(p.gather, cta_arrivals, quad_warps(NK, NB));
 }
 
@@ -1086,6 +1113,189 @@ static int quad_run(const void* a, int64_t lda_m, int64_t lda_k, const uint32_t*
   return PP_OK;
 }
 
+// ------------------------------------------------------------ grouped --
+namespace {
+
+bool g_group_attr_done[64];
+int g_group_attr_limit[64];
+
+struct GroupPlan {
+  int count = 0, grid = 0;
+  bool one_launch = false;
+  int first_cta[kMaxGroup + 1];
+  size_t ws_off[kMaxGroup + 1];  // workspace region of member j: [ws_off[j], ws_off[j + 1])
+  PartitionPlan pl[kMaxGroup];
+  int starts[kMaxGroup][kMaxCtaTable + 1];
+};
+
+// Member j takes CTAs in proportion to its units (at least one), planned as
+// a launch of its own on that many SMs.  One launch needs every member to be
+// a batch-1 fused-plug Linear on the vector path whose warps' unit ranges
+// fit their offset tables; otherwise the members run one after another.
+int plan_group(int count, const pp_quad_linear_desc* d, int sms, GroupPlan* g) {
+  g->count = count;
+  g->one_launch = count >= 1 && count <= kMaxGroup;
+  int64_t units[kMaxGroup] = {0}, total = 0;
+  for (int j = 0; j < count && g->one_launch; ++j) {
+    const pp_quad_linear_desc& m = d[j];
+    const bool xok = m.x && m.ldx_k == 1 && aligned(m.x, 8);
+    if (m.M != 1 || m.N <= 0 || m.K <= 0 || !m.tables || !m.unit_plugs || !m.unit_plug_off || !m.plug_vals ||
+        !m.plug_idx || !m.plug_window_base || !xok || !quad_vector_ok(true, m.codes, 1, m.ldw, m.N, m.K) ||
+        m.N > INT32_MAX || m.K > INT32_MAX) {
+      g->one_launch = false;
+      break;
+    }
+    units[j] = cdiv(m.N, 8) * cdiv(m.K, 64);
+    total += units[j];
+  }
+  if (g->one_launch && total > 0) {
+    int cap[kMaxGroup], used = 0;
+    for (int j = 0; j < count; ++j) {
+      cap[j] = (int)((int64_t)sms * units[j] / total);
+      if (cap[j] < 1) cap[j] = 1;
+      used += cap[j];
+    }
+    while (used > sms) {  // take back from the largest share
+      int big = 0;
+      for (int j = 1; j < count; ++j)
+        if (cap[j] > cap[big]) big = j;
+      if (cap[big] <= 1) break;
+      --cap[big];
+      --used;
+    }
+    while (used < sms) {  // hand out what rounding left, to the members with the most units per CTA
+      int best = 0;
+      for (int j = 1; j < count; ++j)
+        if (units[j] * cap[best] > units[best] * cap[j]) best = j;
+      ++cap[best];
+      ++used;
+    }
+    g->first_cta[0] = 0;
+    g->ws_off[0] = 0;
+    for (int j = 0; j < count; ++j) {
+      const pp_quad_linear_desc& m = d[j];
+      g->pl[j] = quad_plan(true, 1, m.N, m.K, cap[j] < kMaxCtaTable ? cap[j] : kMaxCtaTable, g->starts[j]);
+      if (!fused_plugs_ok(g->pl[j], g->starts[j], 1)) {
+        g->one_launch = false;
+        break;
+      }
+      g->first_cta[j + 1] = g->first_cta[j] + g->pl[j].grid;
+      g->ws_off[j + 1] = g->ws_off[j] + align_up(g->pl[j].total(), 256);
+    }
+    if (g->one_launch) g->grid = g->first_cta[count];
+    if (g->one_launch && used > sms) g->one_launch = false;
+  } else {
+    g->one_launch = false;
+  }
+  return PP_OK;
+}
+
+int group_run(int count, const pp_quad_linear_desc* d, const PeerGather* gather, const int64_t* gather_row0,
+              void* ws, size_t ws_bytes, cudaStream_t s) {
+  if (count < 0 || (count > 0 && !d)) {
+    set_error("group: count must be >= 0 and descriptors non-NULL");
+    return PP_ERR_INVALID;
+  }
+  if (count == 0) return PP_OK;
+  const int sms = device_sm_count(current_device());
+  if (sms <= 0) {
+    set_error("cannot query the SM count of the current device");
+    return PP_ERR_CUDA;
+  }
+  GroupPlan g;
+  plan_group(count, d, sms, &g);
+  if (!g.one_launch) {
+    if (gather) {
+      set_error("a gathered group needs every member on the one-launch path (batch 1, unit plugs, vector path, "
+                "at most %d members)", kMaxGroup);
+      return PP_ERR_INVALID;
+    }
+    for (int j = 0; j < count; ++j) {  // one after another, sharing the workspace
+      const pp_quad_linear_desc& m = d[j];
+      int rc = pp_quad_linear_fused(m.x, m.ldx_m, m.ldx_k, m.codes, m.ldw, m.plug_idx, m.plug_vals,
+                                    m.plug_window_base, m.base_lo32, m.unit_plugs, m.unit_plug_off, m.tables,
+                                    m.scales, m.out, m.ldo_m, m.ldo_n, m.M, m.N, m.K, ws, ws_bytes, s);
+      if (rc) return rc;
+    }
+    return PP_OK;
+  }
+  if (ws_bytes < g.ws_off[count] || !ws || !aligned(ws, 256)) {
+    set_error("workspace of %zu bytes (256-byte aligned, zero-filled) required, got %zu", g.ws_off[count], ws_bytes);
+    return PP_ERR_WORKSPACE;
+  }
+  auto kern = quad_group_kernel<true, 1, true>;
+  int max_smem = 0;
+  int rc = ensure_smem_attr(kern, g_group_attr_done, g_group_attr_limit, &max_smem);
+  if (rc) return rc;
+  constexpr int NW = quad_warps(true, 1);
+  const uint32_t redb = quad_scratch_bytes(true, 1, 1);
+  const int stages = quad_stages(NW, redb, (uint32_t)reserved_smem(current_device()), (uint32_t)max_smem, kPlugCap);
+  if (stages == 0) {
+    set_error("no shared memory layout fits the per-CTA limit %d", max_smem);
+    return PP_ERR_INVALID;
+  }
+  static thread_local QuadGroupParams gp;  // ~12 KB: kept off the stack
+  gp = QuadGroupParams{};
+  gp.count = count;
+  for (int j = 0; j <= count; ++j) gp.first_cta[j] = g.first_cta[j];
+  uint8_t* wsb = reinterpret_cast<uint8_t*>(ws);
+  for (int j = 0; j < count; ++j) {
+    const pp_quad_linear_desc& m = d[j];
+    void* const unused_out[4] = {m.codes ? const_cast<uint32_t*>(m.codes) : nullptr, nullptr, nullptr, nullptr};
+    void* const probe[4] = {unused_out[0], unused_out[0], unused_out[0], unused_out[0]};
+    // a gathered member writes the gather buffers, not out[]
+    if ((rc = check_common(nullptr, m.tables, m.scales, gather ? probe : m.out, m.M, m.N, m.K))) return rc;
+    if (!aligned(m.plug_vals, 8) || !aligned(m.unit_plugs, 16) || !aligned(m.unit_plug_off, 4)) {
+      set_error("group member %d: plug_vals must be 8-byte, unit plugs 16-byte aligned", j);
+      return PP_ERR_INVALID;
+    }
+    QuadParams& prm = gp.m[j];
+    if ((rc = encode_tmap_u32_2d(&prm.tmap, m.codes, (uint64_t)m.K, (uint64_t)m.N, (uint64_t)m.ldw * 4, 32, 8)))
+      return rc;
+    prm.x = reinterpret_cast<const __half*>(m.x);
+    prm.ldx_m = m.ldx_m;
+    prm.ldx_k = m.ldx_k;
+    prm.codes = m.codes;
+    prm.ldc = m.ldw;
+    prm.tables = reinterpret_cast<const uint8_t*>(m.tables);
+    for (int i = 0; i < 4; ++i) {
+      prm.scale[i] = m.scales[i];
+      prm.out[i] = reinterpret_cast<__half*>(m.out[i]);
+    }
+    prm.ldo_m = m.ldo_m;
+    prm.ldo_n = m.ldo_n;
+    prm.M = 1;
+    prm.N = (int)m.N;
+    prm.K = (int)m.K;
+    prm.corr = nullptr;
+    prm.uplugs = reinterpret_cast<const uint8_t*>(m.unit_plugs);
+    prm.uplug_off = m.unit_plug_off;
+    prm.pcap = kPlugCap;
+    prm.part.units = (int)g.pl[j].units;
+    prm.part.upt = (int)g.pl[j].upt;
+    prm.part.counters = reinterpret_cast<int*>(wsb + g.ws_off[j]);
+    prm.part.slots = reinterpret_cast<float*>(wsb + g.ws_off[j] + g.pl[j].counters_bytes);
+    for (int c = 0; c <= g.pl[j].grid; ++c) prm.cta_start[c] = g.starts[j][c];
+    prm.stages = stages;
+    prm.smem_bytes = (uint32_t)max_smem;
+    prm.layout_base = (uint32_t)reserved_smem(current_device());
+    prm.layout = quad_layout(prm.layout_base, prm.smem_bytes, NW, stages, redb, true, kPlugCap);
+    if (gather) {
+      prm.gather = *gather;
+      prm.gather.row0 = gather_row0[j];
+      prm.gather.ctas = g.grid;  // one completion count over the whole launch
+      prm.gather.vec = (prm.gather.ld % 8 == 0 && prm.gather.row0 % 8 == 0) ? 1 : 0;
+      for (int q = 0; q < prm.gather.world; ++q)
+        if (!aligned(prm.gather.out[q], 16)) prm.gather.vec = 0;
+      prm.gather.done = reinterpret_cast<uint32_t*>(reinterpret_cast<int*>(wsb) + (kMaxGrid - 2));
+    }
+  }
+  return launch_kernel("quad_group_kernel", launch_overlap(), kern, dim3(g.grid), dim3(NW * 32), (size_t)max_smem,
+                       s, gp);
+}
+
+}  // namespace
+
 }  // namespace pp
 
 extern "C" {
@@ -1171,6 +1381,71 @@ int pp_quad_linear_fused(const void* x, int64_t ldx_m, int64_t ldx_k, const uint
                       reinterpret_cast<const uint8_t*>(unit_plugs), unit_plug_off, nullptr, tables, scales, out,
                       ldo_m, ldo_n, M, N, K, workspace, workspace_bytes, reinterpret_cast<cudaStream_t>(stream),
                       true);
+}
+
+int pp_quad_linear_group_workspace_bytes(int count, const pp_quad_linear_desc* descs, size_t* bytes) {
+  if (!bytes || count < 0 || (count > 0 && !descs)) {
+    pp::set_error("invalid arguments");
+    return PP_ERR_INVALID;
+  }
+  *bytes = 0;
+  if (count == 0) return PP_OK;
+  const int sms = pp::device_sm_count(pp::current_device());
+  pp::GroupPlan g;
+  pp::plan_group(count, descs, sms > 0 ? sms : 148, &g);
+  if (g.one_launch) {
+    *bytes = g.ws_off[count];
+    return PP_OK;
+  }
+  for (int j = 0; j < count; ++j) {  // members one after another
+    const size_t b = pp::quad_ws_bytes(true, descs[j].M, descs[j].N, descs[j].K, true);
+    if (b > *bytes) *bytes = b;
+  }
+  return PP_OK;
+}
+
+int pp_quad_linear_group_single_launch(int count, const pp_quad_linear_desc* descs) {
+  if (count < 1 || count > pp::kMaxGroup || !descs) return 0;
+  const int sms = pp::device_sm_count(pp::current_device());
+  pp::GroupPlan g;
+  pp::plan_group(count, descs, sms > 0 ? sms : 148, &g);
+  return g.one_launch ? 1 : 0;
+}
+
+int pp_quad_linear_group(int count, const pp_quad_linear_desc* descs, void* workspace, size_t workspace_bytes,
+                         void* stream) {
+  return pp::group_run(count, descs, nullptr, nullptr, workspace, workspace_bytes,
+                       reinterpret_cast<cudaStream_t>(stream));
+}
+
+int pp_quad_linear_group_gather(int count, const pp_quad_linear_desc* descs, int world, void* const gather_out[],
+                                int64_t gather_ld, const int64_t* gather_row0, uint32_t* const gather_flag[],
+                                uint32_t* gather_epoch, void* workspace, size_t workspace_bytes, void* stream) {
+  if (world < 1 || world > pp::kMaxPeers || !gather_out || !gather_flag || !gather_epoch || !gather_row0 ||
+      count < 1 || !descs) {
+    pp::set_error("group gather: world must be 1..%d, buffers, flags, rows and epoch non-NULL, count >= 1",
+                  pp::kMaxPeers);
+    return PP_ERR_INVALID;
+  }
+  pp::PeerGather g{};
+  for (int q = 0; q < world; ++q) {
+    if (!gather_out[q] || !gather_flag[q] || !pp::aligned(gather_out[q], 2) || !pp::aligned(gather_flag[q], 4)) {
+      pp::set_error("gather buffer or flag of rank %d is NULL or misaligned", q);
+      return PP_ERR_INVALID;
+    }
+    g.out[q] = reinterpret_cast<__half*>(gather_out[q]);
+    g.flag[q] = gather_flag[q];
+  }
+  for (int j = 0; j < count; ++j)
+    if (gather_ld < descs[j].N || gather_row0[j] < 0) {
+      pp::set_error("group gather: member %d needs ld >= N and row0 >= 0", j);
+      return PP_ERR_INVALID;
+    }
+  g.ld = gather_ld;
+  g.epoch = gather_epoch;
+  g.world = world;
+  return pp::group_run(count, descs, &g, gather_row0, workspace, workspace_bytes,
+                       reinterpret_cast<cudaStream_t>(stream));
 }
 
 int pp_quad_linear_gather(const void* x, int64_t ldx_k, const uint32_t* codes, int64_t ldw,

@@ -261,9 +261,13 @@ class PeerShardedGroup:
     unit plugs) of a Linear with ``Ns[j]`` rows; ``row0s[j]`` is the shard's
     first row.  A call launches every Linear with ``pp_quad_linear_gather``
     into buffer ``b`` (model-major: model k, Linear j, row n at
-    ``k * sum(Ns) + offset_j + n``), then waits for every rank.  The result
-    is ``peers.view(b)`` viewed as ``(4, sum(Ns))``, which the next call into
-    the same buffer overwrites: alternate the buffers.
+    ``k * sum(Ns) + offset_j + n``), then waits for every rank.  When every
+    rank's shards allow it (``single_launch``, agreed over the process group)
+    the Linears run as one grouped launch that publishes one epoch per call
+    (``pp_quad_linear_group_gather``); else one launch (and epoch) per
+    Linear.  The result is ``peers.view(b)`` viewed as ``(4, sum(Ns))``,
+    which the next call into the same buffer overwrites: alternate the
+    buffers.
     """
 
     def __init__(self, layers, Ns, row0s, peers: PeerBuffers):
@@ -282,6 +286,24 @@ class PeerShardedGroup:
         self.ws = torch.zeros(max(nb, 256), dtype=torch.uint8, device=dev)
         self._lib = _lib.load()
         self._args = {}
+        self._descs = {}
+        # One grouped launch per call (pp_quad_linear_group_gather: one epoch
+        # per call) when every rank's shards allow it; the ranks must agree,
+        # since each waits for the others' epoch counts.
+        from .quadpack import linear_desc
+        probe = [torch.empty((1, l.K), dtype=torch.float16, device=dev) for l in self.layers]
+        d = (_lib.QuadLinearDesc * len(self.layers))(*[linear_desc(x, l, None) for x, l in zip(probe, self.layers)])
+        ok = bool(self._lib.pp_quad_linear_group_single_launch(len(self.layers), d))
+        if peers.world > 1:
+            t = torch.tensor([1 if ok else 0], dtype=torch.int32, device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MIN, group=peers.group)
+            ok = bool(t.item())
+        self.single_launch = ok
+        if ok:
+            nb_g = _lib._size_t()
+            _lib.check(self._lib.pp_quad_linear_group_workspace_bytes(len(self.layers), d, ctypes.byref(nb_g)))
+            if nb_g.value > self.ws.numel():
+                self.ws = torch.zeros(nb_g.value, dtype=torch.uint8, device=dev)
         for b in range(peers.nbuf):
             outs = (ctypes.c_void_p * 8)(*peers.out_ptrs(b))
             flags = (ctypes.c_void_p * 8)(*peers.flag_ptrs(b))
@@ -294,9 +316,37 @@ class PeerShardedGroup:
                             peers.epoch_ptr(b), l.N, l.K))
             self._args[b] = (row, outs, flags)
 
+    def _group_args(self, xs, b):
+        """Descriptors and gather arguments of one grouped launch into buffer b."""
+        import ctypes
+
+        from . import _lib
+        from .quadpack import linear_desc
+        key = (b,) + tuple(x.data_ptr() for x in xs)
+        hit = self._descs.get(key)
+        if hit is None:
+            for x in xs:
+                if x.stride(-1) != 1 or x.data_ptr() % 8:
+                    raise ValueError("grouped gather needs contiguous, 8-byte aligned activations")
+            n = len(self.layers)
+            d = (_lib.QuadLinearDesc * n)(*[linear_desc(x.view(1, -1), l, None) for x, l in zip(xs, self.layers)])
+            rows = (ctypes.c_int64 * n)(*[c + r0 for c, r0 in zip(self.cols, self.row0s)])
+            _, outs, flags = self._args[b]
+            hit = self._descs[key] = (d, rows, outs, flags, list(xs))
+        return hit
+
     def __call__(self, xs, b: int, stream=None) -> torch.Tensor:
         from . import _lib
         s = stream if stream is not None else torch.cuda.current_stream(self.peers.device).cuda_stream
+        if self.single_launch:
+            d, rows, outs, flags, _ = self._group_args(xs, b)
+            rc = self._lib.pp_quad_linear_group_gather(len(self.layers), d, self.peers.world, outs, self.total, rows,
+                                                       flags, self.peers.epoch_ptr(b), self.ws.data_ptr(),
+                                                       self.ws.numel(), s)
+            if rc:
+                _lib.check(rc)
+            self.peers.wait(b, s)
+            return self.peers.view(b)[:4 * self.total].view(4, self.total)
         for x, a in zip(xs, self._args[b][0]):
             rc = self._lib.pp_quad_linear_gather(x.data_ptr(), x.stride(-1), *a, self.ws.data_ptr(),
                                                  self.ws.numel(), s)

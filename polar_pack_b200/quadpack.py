@@ -418,6 +418,59 @@ def quad_linear(x: torch.Tensor, layer: QuadLinearSlice, out=None) -> list[torch
     return out
 
 
+def linear_desc(x: torch.Tensor, layer: QuadLinearSlice, out) -> "_lib.QuadLinearDesc":
+    """The C descriptor of one ``quad_linear(x, layer, out)`` (pointers of the
+    given tensors: keep them alive while the descriptor is used)."""
+    d = _lib.QuadLinearDesc()
+    d.x, d.ldx_m, d.ldx_k = x.data_ptr(), x.stride(0), x.stride(1)
+    d.codes, d.ldw = layer.codes.data_ptr(), layer.codes.stride(0)
+    d.plug_idx, d.plug_vals = _lib.ptr(layer.plug_idx), _lib.ptr(layer.plug_vals)
+    d.plug_window_base, d.base_lo32 = _lib.ptr(layer.plug_window_base), layer.offset & 0xFFFFFFFF
+    d.unit_plugs, d.unit_plug_off = _lib.ptr(layer.unit_plugs), _lib.ptr(layer.unit_plug_off)
+    d.tables = layer.pack.tables.data_ptr()
+    for k in range(4):
+        d.scales[k] = float(layer.pack.scales[k])
+        d.out[k] = out[k].data_ptr() if out is not None else None
+    d.ldo_m, d.ldo_n = (out[0].stride(0), out[0].stride(1)) if out is not None else (0, 0)
+    d.M, d.N, d.K = x.shape[0], layer.N, layer.K
+    return d
+
+
+class QuadLinearGroup:
+    """Independent packed Linears launched together (``pp_quad_linear_group``).
+
+    ``layers[j]`` reads ``xs[j]`` and writes ``outs[j]`` (four ``(M, N_j)``
+    tensors); the tensors are fixed at construction, so a call is one library
+    call (and one kernel launch when every member is a batch-1 Linear with
+    unit plugs -- ``single_launch``), and it can be captured in a CUDA graph.
+    The members must not read each other's outputs.
+    """
+
+    def __init__(self, layers, xs, outs):
+        if not (len(layers) == len(xs) == len(outs)) or not layers:
+            raise ValueError("one input and one output set per Linear")
+        for x, l in zip(xs, layers):
+            if x.dim() != 2 or x.shape[1] != l.K or x.dtype != torch.float16:
+                raise ValueError("each x must be fp16 (M, K) of its Linear")
+        self.layers, self.xs, self.outs = list(layers), list(xs), [list(o) for o in outs]
+        self.device = _lib.require_cuda(*self.xs)
+        n = len(layers)
+        self.descs = (_lib.QuadLinearDesc * n)(*[linear_desc(x, l, o) for x, l, o in zip(xs, layers, outs)])
+        lib = _lib.load()
+        nb = _lib._size_t()
+        _lib.check(lib.pp_quad_linear_group_workspace_bytes(n, self.descs, ctypes.byref(nb)))
+        self.ws = torch.zeros(max(nb.value, 256), dtype=torch.uint8, device=self.device)
+        self.single_launch = bool(lib.pp_quad_linear_group_single_launch(n, self.descs))
+        self._lib = lib
+
+    def __call__(self, stream=None):
+        s = stream if stream is not None else _lib.stream_handle(self.device)
+        rc = self._lib.pp_quad_linear_group(len(self.layers), self.descs, self.ws.data_ptr(), self.ws.numel(), s)
+        if rc:
+            _lib.check(rc)
+        return self.outs
+
+
 def layer_offsets(layer_map: list[dict]) -> list[tuple[str, int, tuple[int, int]]]:
     """``(name, flat offset, (out, in))`` per entry of a ``collect_weights`` layer map.
 

@@ -67,17 +67,27 @@ def test_gather_single_rank_matches_fused(cuda, SHAPES):
     g.manual_seed(3)
     xs = [torch.randn(1, K, generator=g, device=cuda).half() for _, K in SHAPES]
     ref = [quad_linear(x, l) for x, l in zip(xs, layers)]
+    first = None
     for call in range(3):
         b = call % 2
-        y = grp(xs, b)
+        y = grp(xs, b).clone()
         torch.cuda.synchronize(cuda)
         col = 0
         for (N, _), r in zip(SHAPES, ref):
             for k in range(4):
-                assert torch.equal(y[k, col:col + N].view(torch.int16), r[k][0].view(torch.int16)), (N, k)
+                if grp.single_launch:   # one grouped launch: each Linear on its SM share (own split-K order)
+                    assert oq.rel_err(y[k, col:col + N].float().cpu().numpy(),
+                                      r[k][0].float().cpu().numpy()) <= TOL, (N, k)
+                else:                   # one launch per Linear: the same kernel and partition as the plain call
+                    assert torch.equal(y[k, col:col + N].view(torch.int16), r[k][0].view(torch.int16)), (N, k)
             col += N
+        if first is None:
+            first = y
+        else:
+            assert torch.equal(y.view(torch.int16), first.view(torch.int16))   # deterministic
     ep = peers.mem[peers.epoch_off:peers.epoch_off + 8].view(torch.int32).cpu().tolist()
-    assert ep == [2 * len(SHAPES), len(SHAPES)]  # launches made into buffers 0 and 1
+    per_call = 1 if grp.single_launch else len(SHAPES)   # epochs: launches made into buffers 0 and 1
+    assert ep == [2 * per_call, per_call]
     assert int(peers.status.item()) == 0
     peers.close()
 
