@@ -880,11 +880,19 @@ def run_e2e(torch, dist, sets, xs, dev, args, world, M, full_sets, pgroups=None)
         def step(i):
             graphs[i % len(graphs)][i % 2]()
     elif world == 1:
-        # the independent Linears as one row-sharded group writing into its
-        # send buffer, replayed with the copies from one graph per replica
-        groups = [RowShardedGroup([lambda x, out, l=l: quad_linear(x, l, out=out) for l in st], full_n,
-                                  writes_out=True) for st in sets]
-        graphs = [GraphedStep(lambda g=g: (g(dx), g.raw())[1], hx, dxf, cap) for g in groups]
+        # the independent Linears as one grouped launch (QuadLinearGroup)
+        # writing into one output buffer, replayed with the copies from one
+        # graph per replica
+        from polar_pack_b200.quadpack import QuadLinearGroup
+        graphs = []
+        for st in sets:
+            ob = torch.empty((4, M, sum(full_n)), dtype=torch.float16, device=dev)
+            outs, col = [], 0
+            for l in st:
+                outs.append([ob[k, :, col:col + l.N] for k in range(4)])
+                col += l.N
+            grp = QuadLinearGroup(st, dx, outs)
+            graphs.append(GraphedStep(lambda grp=grp, ob=ob: (grp(), ob)[1], hx, dxf, cap))
         host_out = graphs[0].host_out
 
         def step(i):
@@ -926,8 +934,8 @@ def run_e2e(torch, dist, sets, xs, dev, args, world, M, full_sets, pgroups=None)
             total += layer_bytes(l.N, l.K, l.p_hi - l.p_lo, M)
     return {"value": round(total / (ms * 1e-3) / 1e9, 1), "unit": UNIT, "h2d_bytes_per_step": int(h2d),
             "d2h_bytes_per_step": int(d2h),
-            "api": "polar_pack_b200.parallel.GraphedStep of a PeerShardedGroup (pp_quad_linear_gather)" if pgroups
-                   else "polar_pack_b200.parallel.GraphedStep of a RowShardedGroup of quadpack.quad_linear"
+            "api": "polar_pack_b200.parallel.GraphedStep of a PeerShardedGroup (grouped gathered launch)" if pgroups
+                   else "polar_pack_b200.parallel.GraphedStep of a quadpack.QuadLinearGroup (one grouped launch)"
                    if world == 1 else "polar_pack_b200.parallel.RowShardedGroup of quadpack.quad_linear",
             "timing": "each step: pinned host inputs -> device, the Linears, result -> pinned host, "
                       "one CUDA graph launch per step" if (pgroups or world == 1) else "eager calls"}

@@ -242,10 +242,12 @@ PP_API int pp_quad_linear_fused(const void* x, int64_t ldx_m, int64_t ldx_k,
  * up.  The members must be independent: no member reads what another writes.
  * One launch when every member has batch 1 (M == 1), unit plugs, prepared
  * tables, 16-byte aligned codes with K % 4 == 0, contiguous 8-byte aligned
- * activations, at most 8 members, and fits its SM share
- * (pp_quad_linear_group_single_launch says whether it does); otherwise the
- * members run one after another through pp_quad_linear_fused.  Workspace as
- * for the other entry points (pp_quad_linear_group_workspace_bytes).
+ * activation rows, the same flags, at most 8 members, and fits its SM share
+ * (at most 63 work units of 8 rows x 64 codes per warp;
+ * pp_quad_linear_group_single_launch says whether it does); otherwise the
+ * members run one after another through pp_quad_linear_fused, which neither
+ * flags nor an epilogue allow (PP_ERR_INVALID).  Workspace as for the other
+ * entry points (pp_quad_linear_group_workspace_bytes).
  */
 typedef struct pp_quad_linear_desc {
   const void* x;                    /* (M, K) FP16, strides (ldx_m, ldx_k) */
@@ -263,7 +265,18 @@ typedef struct pp_quad_linear_desc {
   void* out[4];                     /* (M, N) FP16, strides (ldo_m, ldo_n) */
   int64_t ldo_m, ldo_n;
   int64_t M, N, K;
+  /* PP_QUAD_PER_MODEL_X: x holds one activation row per model (4 rows, row
+   * stride ldx_m); model k multiplies row k and writes row 0 of out[k]
+   * (M == 1).  The four models of a decode step each carry their own
+   * hidden state, which this serves in the same single pass over the codes. */
+  uint32_t flags;
+  /* optional epilogue, per model (NULL: none): y = fp16(s_k * acc + bias[k][n]),
+   * then y = fp16(y + resid[k][m * ldo_m + n * ldo_n]); resid may equal out */
+  const void* bias[4];
+  const void* resid[4];
 } pp_quad_linear_desc;
+
+#define PP_QUAD_PER_MODEL_X 1u
 
 PP_API int pp_quad_linear_group_workspace_bytes(int count, const pp_quad_linear_desc* descs, size_t* bytes);
 
@@ -309,6 +322,49 @@ PP_API int pp_quad_unpack(const uint32_t* codes, int64_t n, const uint32_t* plug
 PP_API int pp_f16_linear(const void* x, int64_t ldx_m, int64_t ldx_model, int64_t M, int64_t K,
                          const void* const w[4], int64_t ldw, int64_t R, void* const out[4], int64_t ldo_m,
                          int64_t ldo_n, void* stream);
+
+/* ------------------------------------------------------- decoder step --
+ * The operations of a decoder step between the packed Linears, for the four
+ * models of a `.quadpack` decoding one token each (row m of every buffer
+ * belongs to model m).  No counterpart in the reference's code: its models
+ * run these steps inside Hugging Face Qwen2 modules during generate
+ * (polar_inference.py:224-229); the arithmetic follows those modules' FP16
+ * steps (see decode_ops.cu).  Positions are read from device memory so that a
+ * captured step can be replayed for every token.  A status word (device
+ * int, may be NULL) receives 4 for a token id outside the vocabulary (its
+ * row is zeroed) and 5 for a position outside the cache (nothing written).
+ */
+/* h[m][:] = tables[m][tokens[m]][:] (FP16 rows of H). */
+PP_API int pp_embed_rows(const int* tokens, const void* const tables[4], int64_t vocab, int64_t H, void* h,
+                         int64_t ldh, int* status, void* stream);
+
+/* y[m] = fp16(w[m] * fp16(x[m] * rsqrt(mean(x[m]^2) + eps))), FP32 statistics. */
+PP_API int pp_rmsnorm_rows(const void* x, int64_t ldx, const void* const w[4], int64_t H, float eps, void* y,
+                           int64_t ldy, void* stream);
+
+/* Rotary embedding of the token at *pos and its KV-cache append: row m of qkv
+ * holds nq query heads, nkv key heads and nkv value heads of hd FP16 values.
+ * Query heads are rotated in place, key heads rotated into k_cache[m] and
+ * value heads copied into v_cache[m] at position *pos (caches [max_pos][nkv][hd]).
+ * cos_t / sin_t: FP16 [max_pos][hd] tables of the rotation (both halves). */
+PP_API int pp_rope_kv_rows(void* qkv, int64_t ldq, int64_t nq, int64_t nkv, int64_t hd, const void* cos_t,
+                           const void* sin_t, int64_t max_pos, const int* pos, void* const k_cache[4],
+                           void* const v_cache[4], int* status, void* stream);
+
+/* Grouped-query decode attention of one token per model over cache positions
+ * 0..*pos: out[m][h] = softmax(q[m][h] k^T * scale) v with the kv head
+ * h / (nq / nkv); hd must be 128.  Split over `splits` position ranges, whose
+ * partial results the last arriving block combines in order (deterministic).
+ * Workspace: pp_decode_attention_workspace_bytes, zero-filled once. */
+PP_API int pp_decode_attention_workspace_bytes(int64_t nq, int64_t nkv, int64_t splits, size_t* bytes);
+
+PP_API int pp_decode_attention(const void* q, int64_t ldq, int64_t nq, int64_t nkv, int64_t hd,
+                               const void* const k_cache[4], const void* const v_cache[4], int64_t max_pos,
+                               const int* pos, float scale, void* out, int64_t ldo, int64_t splits,
+                               void* workspace, size_t workspace_bytes, void* stream);
+
+/* y[m][i] = fp16(fp16(silu(gate_up[m][i])) * gate_up[m][I + i]). */
+PP_API int pp_swiglu_rows(const void* gate_up, int64_t ldg, int64_t I, void* y, int64_t ldy, void* stream);
 
 /* ------------------------------------------------------------------ dual --
  * Kernel-layout fused dequant GEMM, the drop-in for `polar_dual_bitpacked`

@@ -37,7 +37,10 @@ class QuadLinearDesc(ctypes.Structure):
                 ("unit_plugs", ctypes.c_void_p), ("unit_plug_off", ctypes.c_void_p),
                 ("tables", ctypes.c_void_p), ("scales", ctypes.c_float * 4),
                 ("out", ctypes.c_void_p * 4), ("ldo_m", ctypes.c_int64), ("ldo_n", ctypes.c_int64),
-                ("M", ctypes.c_int64), ("N", ctypes.c_int64), ("K", ctypes.c_int64)]
+                ("M", ctypes.c_int64), ("N", ctypes.c_int64), ("K", ctypes.c_int64),
+                ("flags", ctypes.c_uint32), ("bias", ctypes.c_void_p * 4), ("resid", ctypes.c_void_p * 4)]
+
+PER_MODEL_X = 1
 
 
 _DESC_P = ctypes.POINTER(QuadLinearDesc)
@@ -88,6 +91,14 @@ _SIGNATURES = {
     "pp_quad_unpack": ([_c_void_p, _i64, _c_void_p, _c_void_p, _i64, _i64, _u32, _PTR7, _c_void_p,
                         _PTR4, _c_void_p], _int),
     "pp_f16_linear": ([_c_void_p, _i64, _i64, _i64, _i64, _PTR4, _i64, _i64, _PTR4, _i64, _i64, _c_void_p], _int),
+    "pp_embed_rows": ([_c_void_p, _PTR4, _i64, _i64, _c_void_p, _i64, _c_void_p, _c_void_p], _int),
+    "pp_rmsnorm_rows": ([_c_void_p, _i64, _PTR4, _i64, ctypes.c_float, _c_void_p, _i64, _c_void_p], _int),
+    "pp_rope_kv_rows": ([_c_void_p, _i64, _i64, _i64, _i64, _c_void_p, _c_void_p, _i64, _c_void_p, _PTR4, _PTR4,
+                         _c_void_p, _c_void_p], _int),
+    "pp_decode_attention_workspace_bytes": ([_i64, _i64, _i64, ctypes.POINTER(_size_t)], _int),
+    "pp_decode_attention": ([_c_void_p, _i64, _i64, _i64, _i64, _PTR4, _PTR4, _i64, _c_void_p, ctypes.c_float,
+                             _c_void_p, _i64, _i64, _c_void_p, _size_t, _c_void_p], _int),
+    "pp_swiglu_rows": ([_c_void_p, _i64, _i64, _c_void_p, _i64, _c_void_p], _int),
     "pp_dual_gemm_workspace_bytes": ([_i64, _i64, _i64, _i64, _i64, ctypes.POINTER(_size_t)], _int),
     "pp_dual_gemm": ([_c_void_p, _i64, _i64, _c_void_p, _i64, _i64, _c_void_p, _i64, _c_void_p,
                       _c_void_p, _c_void_p, _c_void_p, _c_void_p, _i64, _i64, _i64, _i64, _i64,

@@ -1,0 +1,385 @@
+// The operations of a decoder step that sit between the packed Linears, for
+// the four models of a `.quadpack` decoding one token each: embedding row
+// gather, RMSNorm, rotary embedding with the KV-cache append, grouped-query
+// decode attention over the cache, SwiGLU.  Every launch handles the four
+// models' rows (row m belongs to model m).  The reference serves these models
+// through Hugging Face Qwen2 modules (polar_inference.py:224-229 calls
+// model.generate); the arithmetic follows those modules' FP16 steps:
+//   RMSNorm   y = fp16(w * fp16(x * rsqrt(mean(x^2) + eps)))   (FP32 statistics)
+//   RoPE      q' = fp16(fp16(q * cos) + fp16(rotate_half(q) * sin)), cos/sin FP16
+//   attention softmax(q k^T * scale) v with FP32 scores, sums and weights
+//   SwiGLU    y = fp16(fp16(silu(g)) * u)                       (silu in FP32)
+// The position of the token is read from device memory, so a captured CUDA
+// graph of the step can be replayed for every position.
+#include <cuda_fp16.h>
+#include <math.h>
+
+#include "pp_common.cuh"
+#include "pp_host.h"
+
+namespace pp {
+namespace {
+
+constexpr int kModels = 4;
+
+struct EmbedParams {
+  const int* tokens;          // [4] token id per model (device)
+  const __half* table[kModels];  // [vocab][H] per model
+  __half* h;                  // [4][ldh]
+  int64_t ldh;
+  int H, vocab;
+  int* status;                // token out of range: 4 and a zero row
+};
+
+__global__ void embed_kernel(const EmbedParams p) {
+  const int m = blockIdx.x;
+  const int tok = p.tokens[m];
+  const bool ok = tok >= 0 && tok < p.vocab;
+  if (!ok && threadIdx.x == 0 && p.status) atomicExch(p.status, 4);
+  const __half* src = p.table[m] + (int64_t)(ok ? tok : 0) * p.H;
+  for (int i = threadIdx.x; i < p.H; i += blockDim.x) p.h[m * p.ldh + i] = ok ? src[i] : __float2half(0.f);
+}
+
+struct NormParams {
+  const __half* x;
+  int64_t ldx;
+  const __half* w[kModels];
+  __half* y;
+  int64_t ldy;
+  int H;
+  float eps;
+};
+
+__device__ __forceinline__ float block_sum(float v, float* red) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+  if (lane == 0) red[warp] = v;
+  __syncthreads();
+  float s = 0.f;
+  for (int i = 0; i < nw; ++i) s += red[i];  // same order in every thread
+  __syncthreads();
+  return s;
+}
+
+__global__ void rmsnorm_kernel(const NormParams p) {
+  __shared__ float red[32];
+  const int m = blockIdx.x;
+  const __half* x = p.x + m * p.ldx;
+  float ss = 0.f;
+  for (int i = threadIdx.x; i < p.H; i += blockDim.x) {
+    const float v = __half2float(x[i]);
+    ss = fmaf(v, v, ss);
+  }
+  const float r = rsqrtf(block_sum(ss, red) / (float)p.H + p.eps);
+  for (int i = threadIdx.x; i < p.H; i += blockDim.x) {
+    const __half n = __float2half_rn(__half2float(x[i]) * r);
+    p.y[m * p.ldy + i] = __float2half_rn(__half2float(p.w[m][i]) * __half2float(n));
+  }
+}
+
+struct RopeParams {
+  __half* qkv;            // [4][ldq]: q heads, k heads, v heads of the token
+  int64_t ldq;
+  const __half* cos_t;    // [max_pos][hd]: FP16 cos / sin of position p (both halves)
+  const __half* sin_t;
+  const int* pos;         // device: position of the token
+  __half* kc[kModels];    // [max_pos][nkv][hd] per model
+  __half* vc[kModels];
+  int nq, nkv, hd, max_pos;
+  int* status;            // position out of range: 5
+};
+
+// q and k heads rotated (q in place, k into the cache at pos), v copied.
+__global__ void rope_kv_kernel(const RopeParams p) {
+  const int m = blockIdx.x;
+  const int pos = *p.pos;
+  if (pos < 0 || pos >= p.max_pos) {
+    if (threadIdx.x == 0 && p.status) atomicExch(p.status, 5);
+    return;
+  }
+  const int half = p.hd / 2;
+  __half* row = p.qkv + m * p.ldq;
+  const __half* cs = p.cos_t + (int64_t)pos * p.hd;
+  const __half* sn = p.sin_t + (int64_t)pos * p.hd;
+  const int pairs = (p.nq + p.nkv) * half;
+  for (int t = threadIdx.x; t < pairs; t += blockDim.x) {
+    const int head = t / half, i = t - head * half;
+    __half* hp = row + head * p.hd;
+    const float a = __half2float(hp[i]), b = __half2float(hp[i + half]);
+    const float c1 = __half2float(cs[i]), s1 = __half2float(sn[i]);
+    const float c2 = __half2float(cs[i + half]), s2 = __half2float(sn[i + half]);
+    const float ac = __half2float(__float2half_rn(a * c1)), bs = __half2float(__float2half_rn(-b * s1));
+    const float bc = __half2float(__float2half_rn(b * c2)), as = __half2float(__float2half_rn(a * s2));
+    const __half o1 = __float2half_rn(ac + bs), o2 = __float2half_rn(bc + as);
+    if (head < p.nq) {
+      hp[i] = o1;
+      hp[i + half] = o2;
+    } else {
+      __half* kp = p.kc[m] + ((int64_t)pos * p.nkv + (head - p.nq)) * p.hd;
+      kp[i] = o1;
+      kp[i + half] = o2;
+    }
+  }
+  const __half* v = row + (p.nq + p.nkv) * p.hd;
+  __half* vp = p.vc[m] + (int64_t)pos * p.nkv * p.hd;
+  for (int i = threadIdx.x; i < p.nkv * p.hd; i += blockDim.x) vp[i] = v[i];
+}
+
+struct AttnParams {
+  const __half* q;        // [4][ldq], q heads first
+  int64_t ldq;
+  const __half* kc[kModels];
+  const __half* vc[kModels];
+  const int* pos;         // the token's position: keys 0..pos are attended
+  __half* out;            // [4][ldo]: nq heads x hd
+  int64_t ldo;
+  float* part;            // [4][nq][splits][kPartStride] partial (acc, max, sum)
+  int* cnt;               // [4][nkv] split arrivals (zero between launches)
+  int nq, nkv, splits, max_pos;
+  float scale;
+};
+
+constexpr int kHeadDim = 128;  // 4 dimensions per lane
+constexpr int kPartStride = kHeadDim + 4;  // floats per partial: acc, max, sum, 2 unused (16-byte rows)
+
+// Split-K decode attention: CTA (split, kv head, model); warp w is query head
+// kvh * group + w and walks keys [s0, s1) with an online softmax; lane l
+// holds dimensions 4l..4l+3.  The CTA whose arrival completes its
+// (model, kv head) combines the splits in split order (deterministic).
+__global__ void decode_attention_kernel(const AttnParams p) {
+  __shared__ int last;
+  const int split = blockIdx.x, kvh = blockIdx.y, m = blockIdx.z;
+  const int group = p.nq / p.nkv;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int qh = kvh * group + warp;
+  int len = *p.pos + 1;
+  if (len > p.max_pos) len = p.max_pos;
+  const int chunk = (len + p.splits - 1) / p.splits;
+  const int s0 = split * chunk, s1 = min(len, s0 + chunk);
+  const uint2 qv = *reinterpret_cast<const uint2*>(p.q + m * p.ldq + qh * kHeadDim + 4 * lane);
+  const float2 q01 = __half22float2(u2h(qv.x)), q23 = __half22float2(u2h(qv.y));
+  const __half* kb = p.kc[m] + (int64_t)kvh * kHeadDim + 4 * lane;
+  const __half* vb = p.vc[m] + (int64_t)kvh * kHeadDim + 4 * lane;
+  const int64_t stride = (int64_t)p.nkv * kHeadDim;
+  float mx = -INFINITY, sum = 0.f, a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
+  for (int t = s0; t < s1; ++t) {
+    const uint2 kv = *reinterpret_cast<const uint2*>(kb + t * stride);
+    const uint2 vv = *reinterpret_cast<const uint2*>(vb + t * stride);
+    const float2 k01 = __half22float2(u2h(kv.x)), k23 = __half22float2(u2h(kv.y));
+    float s = q01.x * k01.x + q01.y * k01.y + q23.x * k23.x + q23.y * k23.y;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+    s *= p.scale;
+    const float mn = fmaxf(mx, s);
+    const float corr = expf(mx - mn), e = expf(s - mn);
+    const float2 v01 = __half22float2(u2h(vv.x)), v23 = __half22float2(u2h(vv.y));
+    sum = sum * corr + e;
+    a0 = a0 * corr + e * v01.x;
+    a1 = a1 * corr + e * v01.y;
+    a2 = a2 * corr + e * v23.x;
+    a3 = a3 * corr + e * v23.y;
+    mx = mn;
+  }
+  float* pp = p.part + (((int64_t)m * p.nq + qh) * p.splits + split) * kPartStride;
+  *reinterpret_cast<float4*>(pp + 4 * lane) = make_float4(a0, a1, a2, a3);
+  if (lane == 0) {
+    pp[kHeadDim] = mx;
+    pp[kHeadDim + 1] = sum;
+  }
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) last = atomicAdd(p.cnt + m * p.nkv + kvh, 1) == p.splits - 1;
+  __syncthreads();
+  if (!last) return;
+  __threadfence();
+  const float* base = p.part + ((int64_t)m * p.nq + qh) * p.splits * kPartStride;
+  float M = -INFINITY;
+  for (int sp = 0; sp < p.splits; ++sp) M = fmaxf(M, __ldcg(base + sp * kPartStride + kHeadDim));
+  float L = 0.f, o0 = 0.f, o1 = 0.f, o2 = 0.f, o3 = 0.f;
+  for (int sp = 0; sp < p.splits; ++sp) {
+    const float* b = base + sp * kPartStride;
+    const float ms = __ldcg(b + kHeadDim);
+    if (ms == -INFINITY) continue;  // an empty split
+    const float w = expf(ms - M);
+    L += w * __ldcg(b + kHeadDim + 1);
+    o0 += w * __ldcg(b + 4 * lane);
+    o1 += w * __ldcg(b + 4 * lane + 1);
+    o2 += w * __ldcg(b + 4 * lane + 2);
+    o3 += w * __ldcg(b + 4 * lane + 3);
+  }
+  const float inv = 1.f / L;
+  __half2* o = reinterpret_cast<__half2*>(p.out + m * p.ldo + qh * kHeadDim + 4 * lane);
+  o[0] = __floats2half2_rn(o0 * inv, o1 * inv);
+  o[1] = __floats2half2_rn(o2 * inv, o3 * inv);
+  __syncthreads();
+  if (threadIdx.x == 0) p.cnt[m * p.nkv + kvh] = 0;
+}
+
+struct SwigluParams {
+  const __half* gu;  // [4][ldg]: gate (I values) then up (I values)
+  int64_t ldg;
+  __half* y;         // [4][ldy]
+  int64_t ldy;
+  int I;
+};
+
+__global__ void swiglu_kernel(const SwigluParams p) {
+  const int m = blockIdx.y;
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < p.I; i += gridDim.x * blockDim.x) {
+    const float g = __half2float(p.gu[m * p.ldg + i]);
+    const __half sg = __float2half_rn(g / (1.f + expf(-g)));
+    p.y[m * p.ldy + i] = __float2half_rn(__half2float(sg) * __half2float(p.gu[m * p.ldg + p.I + i]));
+  }
+}
+
+}  // namespace
+}  // namespace pp
+
+extern "C" {
+
+int pp_embed_rows(const int* tokens, const void* const tables[4], int64_t vocab, int64_t H, void* h, int64_t ldh,
+                  int* status, void* stream) {
+  if (!tokens || !tables || !h || H <= 0 || vocab <= 0 || ldh < H || H > INT32_MAX || vocab > INT32_MAX) {
+    pp::set_error("pp_embed_rows: invalid arguments");
+    return PP_ERR_INVALID;
+  }
+  pp::EmbedParams p{};
+  p.tokens = tokens;
+  for (int k = 0; k < 4; ++k) {
+    if (!tables[k]) {
+      pp::set_error("pp_embed_rows: table %d is NULL", k);
+      return PP_ERR_INVALID;
+    }
+    p.table[k] = reinterpret_cast<const __half*>(tables[k]);
+  }
+  p.h = reinterpret_cast<__half*>(h);
+  p.ldh = ldh;
+  p.H = (int)H;
+  p.vocab = (int)vocab;
+  p.status = status;
+  pp::embed_kernel<<<4, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(p);
+  return pp::check_launch("embed_kernel");
+}
+
+int pp_rmsnorm_rows(const void* x, int64_t ldx, const void* const w[4], int64_t H, float eps, void* y, int64_t ldy,
+                    void* stream) {
+  if (!x || !w || !y || H <= 0 || H > INT32_MAX || ldx < H || ldy < H) {
+    pp::set_error("pp_rmsnorm_rows: invalid arguments");
+    return PP_ERR_INVALID;
+  }
+  pp::NormParams p{};
+  p.x = reinterpret_cast<const __half*>(x);
+  p.ldx = ldx;
+  for (int k = 0; k < 4; ++k) {
+    if (!w[k]) {
+      pp::set_error("pp_rmsnorm_rows: weight %d is NULL", k);
+      return PP_ERR_INVALID;
+    }
+    p.w[k] = reinterpret_cast<const __half*>(w[k]);
+  }
+  p.y = reinterpret_cast<__half*>(y);
+  p.ldy = ldy;
+  p.H = (int)H;
+  p.eps = eps;
+  pp::rmsnorm_kernel<<<4, 512, 0, reinterpret_cast<cudaStream_t>(stream)>>>(p);
+  return pp::check_launch("rmsnorm_kernel");
+}
+
+int pp_rope_kv_rows(void* qkv, int64_t ldq, int64_t nq, int64_t nkv, int64_t hd, const void* cos_t,
+                    const void* sin_t, int64_t max_pos, const int* pos, void* const k_cache[4],
+                    void* const v_cache[4], int* status, void* stream) {
+  if (!qkv || !cos_t || !sin_t || !pos || !k_cache || !v_cache || nq <= 0 || nkv <= 0 || hd <= 0 || hd % 2 ||
+      max_pos <= 0 || ldq < (nq + 2 * nkv) * hd || nq > 4096 || nkv > 4096 || hd > 4096 || max_pos > INT32_MAX) {
+    pp::set_error("pp_rope_kv_rows: invalid arguments");
+    return PP_ERR_INVALID;
+  }
+  pp::RopeParams p{};
+  p.qkv = reinterpret_cast<__half*>(qkv);
+  p.ldq = ldq;
+  p.cos_t = reinterpret_cast<const __half*>(cos_t);
+  p.sin_t = reinterpret_cast<const __half*>(sin_t);
+  p.pos = pos;
+  for (int k = 0; k < 4; ++k) {
+    if (!k_cache[k] || !v_cache[k]) {
+      pp::set_error("pp_rope_kv_rows: cache of model %d is NULL", k);
+      return PP_ERR_INVALID;
+    }
+    p.kc[k] = reinterpret_cast<__half*>(k_cache[k]);
+    p.vc[k] = reinterpret_cast<__half*>(v_cache[k]);
+  }
+  p.nq = (int)nq;
+  p.nkv = (int)nkv;
+  p.hd = (int)hd;
+  p.max_pos = (int)max_pos;
+  p.status = status;
+  pp::rope_kv_kernel<<<4, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(p);
+  return pp::check_launch("rope_kv_kernel");
+}
+
+int pp_decode_attention_workspace_bytes(int64_t nq, int64_t nkv, int64_t splits, size_t* bytes) {
+  if (!bytes || nq <= 0 || nkv <= 0 || splits <= 0) {
+    pp::set_error("invalid arguments");
+    return PP_ERR_INVALID;
+  }
+  *bytes = pp::align_up((size_t)4 * nkv * sizeof(int), 256) +
+           (size_t)4 * nq * splits * pp::kPartStride * sizeof(float);
+  return PP_OK;
+}
+
+int pp_decode_attention(const void* q, int64_t ldq, int64_t nq, int64_t nkv, int64_t hd,
+                        const void* const k_cache[4], const void* const v_cache[4], int64_t max_pos,
+                        const int* pos, float scale, void* out, int64_t ldo, int64_t splits, void* workspace,
+                        size_t workspace_bytes, void* stream) {
+  if (!q || !k_cache || !v_cache || !pos || !out || hd != pp::kHeadDim || nq <= 0 || nkv <= 0 || nq % nkv ||
+      nq / nkv > 32 || splits <= 0 || splits > 65535 || max_pos <= 0 || max_pos > INT32_MAX ||
+      !pp::aligned(q, 8) || ldq % 4 || !pp::aligned(out, 4) || ldo % 2) {
+    pp::set_error("pp_decode_attention: head_dim must be %d, nq a multiple of nkv (at most 32 q heads per kv "
+                  "head), 8-byte aligned q rows, 4-byte aligned output rows", pp::kHeadDim);
+    return PP_ERR_INVALID;
+  }
+  size_t need = 0;
+  pp_decode_attention_workspace_bytes(nq, nkv, splits, &need);
+  if (!workspace || workspace_bytes < need || !pp::aligned(workspace, 256)) {
+    pp::set_error("pp_decode_attention: workspace of %zu bytes (256-byte aligned, zero-filled) required", need);
+    return PP_ERR_WORKSPACE;
+  }
+  pp::AttnParams p{};
+  p.q = reinterpret_cast<const __half*>(q);
+  p.ldq = ldq;
+  for (int k = 0; k < 4; ++k) {
+    if (!k_cache[k] || !v_cache[k] || !pp::aligned(k_cache[k], 8) || !pp::aligned(v_cache[k], 8)) {
+      pp::set_error("pp_decode_attention: cache of model %d is NULL or not 8-byte aligned", k);
+      return PP_ERR_INVALID;
+    }
+    p.kc[k] = reinterpret_cast<const __half*>(k_cache[k]);
+    p.vc[k] = reinterpret_cast<const __half*>(v_cache[k]);
+  }
+  p.pos = pos;
+  p.out = reinterpret_cast<__half*>(out);
+  p.ldo = ldo;
+  p.cnt = reinterpret_cast<int*>(workspace);
+  p.part = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(workspace) +
+                                    pp::align_up((size_t)4 * nkv * sizeof(int), 256));
+  p.nq = (int)nq;
+  p.nkv = (int)nkv;
+  p.splits = (int)splits;
+  p.max_pos = (int)max_pos;
+  p.scale = scale;
+  pp::decode_attention_kernel<<<dim3((unsigned)splits, (unsigned)nkv, 4), (unsigned)(32 * (nq / nkv)), 0,
+                                reinterpret_cast<cudaStream_t>(stream)>>>(p);
+  return pp::check_launch("decode_attention_kernel");
+}
+
+int pp_swiglu_rows(const void* gate_up, int64_t ldg, int64_t I, void* y, int64_t ldy, void* stream) {
+  if (!gate_up || !y || I <= 0 || I > INT32_MAX || ldg < 2 * I || ldy < I) {
+    pp::set_error("pp_swiglu_rows: invalid arguments");
+    return PP_ERR_INVALID;
+  }
+  pp::SwigluParams p{reinterpret_cast<const __half*>(gate_up), ldg, reinterpret_cast<__half*>(y), ldy, (int)I};
+  const unsigned gx = (unsigned)((I + 255) / 256 < 64 ? (I + 255) / 256 : 64);
+  pp::swiglu_kernel<<<dim3(gx, 4), 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(p);
+  return pp::check_launch("swiglu_kernel");
+}
+
+}  // extern "C"

@@ -101,6 +101,10 @@ struct QuadParams {
   uint32_t pcap;
   // outputs gathered into every rank's buffer (batch 1; world 0: none)
   PeerGather gather;
+  // epilogue (NULL: none): y = fp16(s_k * acc + bias_k[n]), then
+  // y = fp16(y + resid_k[m][n]) (resid with the output strides, may be out)
+  const __half* bias[4];
+  const __half* resid[4];
   int cta_start[kMaxCtaTable + 1];  // unit start of every CTA (plan_cta_starts)
 };
 
@@ -115,9 +119,15 @@ constexpr uint32_t kPlugCap = 512u;
 
 // NK: file layout.  DIRECT: tables at a 64 KiB-aligned shared address (see
 // decode_quad).  PLUG: fused plug correction (NK, NB == 1, batch 1).
-template <bool NK, int NB, bool DIRECT, bool PLUG = false>
+// DIAG: one activation row per model (NK, NB == 1, M == 1): x has four rows,
+// model q multiplies row q and writes row 0 of out[q].  The four rows feed
+// mma batch columns 0-3; model q's result is column q of its fragment rows
+// (the other columns hold products nobody stores), and the plug terms, which
+// need x_q, collect in four separate per-lane sums.
+template <bool NK, int NB, bool DIRECT, bool PLUG = false, bool DIAG = false>
 struct QuadOp {
   static_assert(!PLUG || (NK && NB == 1), "fused plugs: file layout, one batch tile");
+  static_assert(!DIAG || (NK && NB == 1), "per-model activations: file layout, one batch tile");
   static constexpr int kWarps = quad_warps(NK, NB);
   static constexpr int kTileW = NK ? 8 : 32;  // output features per tile
   static constexpr int kT = NK ? 1 : 4;       // mma pairs per 16-k step
@@ -144,6 +154,10 @@ struct QuadOp {
   uint32_t pring = 0u;
   uint2 pv0, pv1;
   uint32_t px;
+  // DIAG + PLUG: per-model plug sums of this lane's entries and the two
+  // entries' activations of every model (x_q[col0] | x_q[col1] << 16)
+  float pacc[4];
+  uint32_t pxq[4];
 
   __device__ __forceinline__ QuadOp(const QuadParams& p_, uint32_t lut_saddr)
       : p(p_), g((threadIdx.x & 31) >> 2), c(threadIdx.x & 3),
@@ -155,7 +169,8 @@ struct QuadOp {
 #pragma unroll
     for (int nb = 0; nb < NB; ++nb) {
       const int bat = nb * 8 + g;
-      xrow[nb] = x + (int64_t)(bat < Mv ? bat : 0) * ldx_m + (NK ? 4 * c : 0);
+      const int rows = DIAG ? 4 : Mv;  // DIAG: activation row q = model q
+      xrow[nb] = x + (int64_t)(bat < rows ? bat : 0) * ldx_m + (NK ? 4 * c : 0);
     }
 #pragma unroll
     for (int s = 0; s < 4; ++s) {
@@ -181,6 +196,10 @@ struct QuadOp {
         for (int h = 0; h < 2; ++h)
 #pragma unroll
           for (int j = 0; j < 4; ++j) acc[t][nb][h][j] = 0.f;
+    if constexpr (DIAG && PLUG) {
+#pragma unroll
+      for (int q = 0; q < 4; ++q) pacc[q] = 0.f;
+    }
   }
 
   __device__ __forceinline__ void begin(int, int) {}
@@ -265,31 +284,77 @@ struct QuadOp {
       const __half* xk = x + kc * 64;
       const uint32_t e0 = lo + (uint32_t)c, e1 = e0 + 4u;
       pv0 = pv1 = make_uint2(0u, 0u);
-      px = 0u;
+      px = 0u;  // the two entries' columns; plug_x() loads their activations
       if (32u + 9u * n <= kPlugCap) {
         const uint32_t vb = ps + 32u, kb = ps + 32u + 8u * n;
         if (e0 < hi) {
           pv0 = lds_u2(vb + 8u * e0);
-          px = ld_u16(xk + lds_u8(kb + e0));
+          px = lds_u8(kb + e0);
         }
         if (e1 < hi) {
           pv1 = lds_u2(vb + 8u * e1);
-          px |= (uint32_t)ld_u16(xk + lds_u8(kb + e1)) << 16;
+          px |= lds_u8(kb + e1) << 16;
         }
-        for (uint32_t e = e1 + 4u; e < hi; e += 4u) plug_fma(lds_u2(vb + 8u * e), ld_u16(xk + lds_u8(kb + e)));
+        for (uint32_t e = e1 + 4u; e < hi; e += 4u) plug_term(lds_u2(vb + 8u * e), xk, lds_u8(kb + e));
       } else {
         const uint8_t* gs = p.uplugs + __ldg(p.uplug_off + u);
         for (uint32_t e = e0; e < hi; e += 4u)
-          plug_fma(__ldg(reinterpret_cast<const uint2*>(gs + 32u + 8u * e)), ld_u16(xk + __ldg(gs + 32u + 8u * n + e)));
+          plug_term(__ldg(reinterpret_cast<const uint2*>(gs + 32u + 8u * e)), xk, __ldg(gs + 32u + 8u * n + e));
+      }
+    }
+  }
+
+  // PLUG: the activations of the unit's first two plug entries of this lane
+  // (columns from side(); an empty entry has value zero and reads column 0),
+  // loaded at the start of the unit's compute so the decode hides them
+  __device__ __forceinline__ void plug_x(int kc) {
+    if constexpr (PLUG) {
+      const __half* xk = x + kc * 64;
+      if constexpr (DIAG) {
+#pragma unroll
+        for (int q = 0; q < 4; ++q)
+          pxq[q] = (uint32_t)ld_u16(xk + q * ldx_m + (px & 0xFFu)) |
+                   ((uint32_t)ld_u16(xk + q * ldx_m + (px >> 16)) << 16);
+      } else {
+        px = (uint32_t)ld_u16(xk + (px & 0xFFu)) | ((uint32_t)ld_u16(xk + (px >> 16)) << 16);
       }
     }
   }
 
   __device__ __forceinline__ void plug_finish() {
     if constexpr (PLUG) {
-      plug_fma(pv0, px & 0xFFFFu);
-      plug_fma(pv1, px >> 16);
+      if constexpr (DIAG) {
+        plug_fma4(pv0, pxq, 0);
+        plug_fma4(pv1, pxq, 16);
+      } else {
+        plug_fma(pv0, px & 0xFFFFu);
+        plug_fma(pv1, px >> 16);
+      }
     }
+  }
+
+  // one plug entry (values v, column col of the unit at xk) applied now
+  __device__ __forceinline__ void plug_term(uint2 v, const __half* xk, uint32_t col) {
+    if constexpr (DIAG) {
+      uint32_t xq[4];
+#pragma unroll
+      for (int q = 0; q < 4; ++q) xq[q] = ld_u16(xk + q * ldx_m + col);
+      plug_fma4(v, xq, 0);
+    } else {
+      plug_fma(v, ld_u16(xk + col));
+    }
+  }
+
+  // DIAG: pacc[q] += value q * x_q (the FP16 activation in bits sh..sh+15
+  // of xq[q]), FP16 operands and one FP32 rounding, as in plug_fma
+  __device__ __forceinline__ void plug_fma4(uint2 v, const uint32_t (&xq)[4], int sh) {
+    asm("{\n .reg .f16 v0, v1, v2, v3, x0, x1, x2, x3;\n .reg .b16 t;\n"
+        " mov.b32 {v0, v1}, %4;\n mov.b32 {v2, v3}, %5;\n"
+        " mov.b32 {x0, t}, %6;\n mov.b32 {x1, t}, %7;\n mov.b32 {x2, t}, %8;\n mov.b32 {x3, t}, %9;\n"
+        " fma.rn.f32.f16 %0, v0, x0, %0;\n fma.rn.f32.f16 %1, v1, x1, %1;\n"
+        " fma.rn.f32.f16 %2, v2, x2, %2;\n fma.rn.f32.f16 %3, v3, x3, %3;\n}"
+        : "+f"(pacc[0]), "+f"(pacc[1]), "+f"(pacc[2]), "+f"(pacc[3])
+        : "r"(v.x), "r"(v.y), "r"(xq[0] >> sh), "r"(xq[1] >> sh), "r"(xq[2] >> sh), "r"(xq[3] >> sh));
   }
 
   // acc(model q, batch column 2c) += value q * x with the FP16 operands
@@ -309,7 +374,18 @@ struct QuadOp {
   // the row in batch column 0 (fragment register 2 (q & 1) of half q >> 1
   // for model q).
   __device__ __forceinline__ void end_chunk() {
-    if constexpr (PLUG) {
+    if constexpr (PLUG && DIAG) {
+      // the row's four lanes sum each model's plug terms; lane c = q >> 1
+      // holds model q's result (column q) in register (q & 1) * 3 of half q >> 1
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        float v = pacc[q];
+        v += __shfl_xor_sync(0xffffffffu, v, 1);
+        v += __shfl_xor_sync(0xffffffffu, v, 2);
+        if (c == (q >> 1)) acc[0][0][q >> 1][(q & 1) * 3] += v;
+        pacc[q] = 0.f;
+      }
+    } else if constexpr (PLUG) {
 #pragma unroll
       for (int h = 0; h < 2; ++h)
 #pragma unroll
@@ -323,6 +399,7 @@ struct QuadOp {
   }
 
   __device__ __forceinline__ void compute(const Buf& b, int tile, int kc) {
+    plug_x(kc);
     if (kc * (NK ? 64 : 16) + (NK ? 64 : 16) <= Kv) compute_unit<true>(b, kc);
     else compute_unit<false>(b, kc);
     plug_finish();
@@ -339,7 +416,7 @@ struct QuadOp {
         for (int nb = 0; nb < NB; ++nb)
           // PLUG (batch 1): only lanes g = 0 feed activations; the other
           // batch columns stay zero for side()'s plug terms
-          xb[s][nb] = (PLUG && g != 0) ? make_uint2(0u, 0u) : xquad<FULL>(nb, kbase, s);
+          xb[s][nb] = (PLUG && !DIAG && g != 0) ? make_uint2(0u, 0u) : xquad<FULL>(nb, kbase, s);
 #pragma unroll
       for (int s = 0; s < 4; ++s) {
         const int kp = kbase + 16 * s + 4 * c;
@@ -408,7 +485,11 @@ struct QuadOp {
 #pragma unroll
           for (int j = 0; j < 4; ++j) {
             const int bat = nb * 8 + 2 * c + (j & 1);
-            if (bat < M) slot[((2 * h + (j >> 1)) * M + bat) * kTileW + fi] = acc[t][nb][h][j];
+            if constexpr (DIAG) {  // model q's result is batch column q: stored as batch row 0
+              if (bat == 2 * h + (j >> 1)) slot[(2 * h + (j >> 1)) * kTileW + fi] = acc[t][nb][h][j];
+            } else if (bat < M) {
+              slot[((2 * h + (j >> 1)) * M + bat) * kTileW + fi] = acc[t][nb][h][j];
+            }
           }
     }
   }
@@ -418,7 +499,7 @@ struct QuadOp {
   // replaces eight 2-byte stores (each a separate NVLink write to a peer).
   static constexpr bool kGather16 = NK && NB == 1;
   __device__ __forceinline__ bool gather16(int tile) const {
-    return p.gather.world && p.gather.vec && tile * 8 + 8 <= Nv;
+    return !DIAG && p.gather.world && p.gather.vec && tile * 8 + 8 <= Nv && !p.bias[0] && !p.resid[0];
   }
   // lane = element (model lane >> 3, row lane & 7) of tile `tile`; v is the
   // sum before the plug correction and the scale
@@ -458,6 +539,20 @@ struct QuadOp {
         return;
       }
     }
+    if constexpr (DIAG) {
+      const int f = tile * kTileW + pr;
+      if (f >= Nv) return;
+#pragma unroll
+      for (int h = 0; h < 2; ++h)
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+          if (2 * c + (j & 1) == 2 * h + (j >> 1)) store(2 * h + (j >> 1), 0, f, acc[0][0][h][j]);
+    } else {
+      store_tile_rows(tile);
+    }
+  }
+
+  __device__ __forceinline__ void store_tile_rows(int tile) {
 #pragma unroll
     for (int t = 0; t < kT; ++t) {
       const int f = tile * kTileW + (NK ? pr : 4 * g + t);
@@ -493,7 +588,10 @@ struct QuadOp {
 
   // v already includes the plug correction
   __device__ __forceinline__ void store_raw(int model, int bat, int f, float v) const {
-    const __half h = __float2half_rn(v * p.scale[model]);
+    const __half* bias = p.bias[model];
+    const __half* resid = p.resid[model];
+    __half h = __float2half_rn(v * p.scale[model] + (bias ? __half2float(bias[f]) : 0.f));
+    if (resid) h = __float2half_rn(__half2float(h) + __half2float(resid[(int64_t)bat * p.ldo_m + (int64_t)f * p.ldo_n]));
     if (p.gather.world) {  // batch 1: element (model, row0 + f) of every rank's buffer
       const int64_t o = (int64_t)model * p.gather.ld + p.gather.row0 + f;
 #pragma unroll
@@ -514,10 +612,10 @@ __device__ __forceinline__ uint32_t plug_bytes(const QuadParams& p, uint32_t pta
   return len < kPlugCap ? len : kPlugCap;
 }
 
-template <bool NK, int NB, bool DIRECT, bool PLUG>
+template <bool NK, int NB, bool DIRECT, bool PLUG, bool DIAG>
 __device__ __forceinline__ void quad_body(const QuadParams& p, const Partition& pt, const QuadLayout& L, TmaRing& rg,
                                           const CtaTables& tb, int cu0, int cu1, int wu0, int wu1, int* status) {
-  using Op = QuadOp<NK, NB, DIRECT, PLUG>;
+  using Op = QuadOp<NK, NB, DIRECT, PLUG, DIAG>;
   const uint32_t base = (uint32_t)__cvta_generic_to_shared(pp_smem);
   float* red = reinterpret_cast<float*>(pp_smem + (L.scratch - base));
   const int warp = threadIdx.x >> 5;
@@ -551,7 +649,7 @@ __host__ __device__ inline uint32_t quad_scratch_bytes(bool nk, int nb, int M) {
 // are filled; after it lane 0 of every warp initialises its ring and issues
 // its first S units, whose copies overlap the table build or copy.  Then
 // every warp streams and reduces on its own; there is no closing barrier.
-template <bool NK, int NB, bool PLUG>
+template <bool NK, int NB, bool PLUG, bool DIAG>
 __device__ __forceinline__ int* quad_gemv_run(const QuadParams& p, int cta, int ncta) {
   constexpr int NW = quad_warps(NK, NB);
   // the first code copies need the tensor map: fetch it while the
@@ -652,16 +750,16 @@ __device__ __forceinline__ int* quad_gemv_run(const QuadParams& p, int cta, int 
   // outputs may belong to the previous kernel of the stream
   pdl_wait();
   if (wu0 >= wu1) return tb.cnt + 2 * NW;
-  if (L.direct) quad_body<NK, NB, true, PLUG>(p, pt, L, rg, tb, cu0, cu1, wu0, wu1, status);
-  else quad_body<NK, NB, false, PLUG>(p, pt, L, rg, tb, cu0, cu1, wu0, wu1, status);
+  if (L.direct) quad_body<NK, NB, true, PLUG, DIAG>(p, pt, L, rg, tb, cu0, cu1, wu0, wu1, status);
+  else quad_body<NK, NB, false, PLUG, DIAG>(p, pt, L, rg, tb, cu0, cu1, wu0, wu1, status);
   return tb.cnt + 2 * NW;
 }
 
 // Every warp leaves quad_gemv_run, whatever path it took, and then takes
 // part in the gather's completion signal.
-template <bool NK, int NB, bool PLUG>
+template <bool NK, int NB, bool PLUG, bool DIAG = false>
 __global__ void __launch_bounds__(quad_warps(NK, NB) * 32, 1) quad_gemv_kernel(const __grid_constant__ QuadParams p) {
-  int* const cta_arrivals = quad_gemv_run<NK, NB, PLUG>(p, blockIdx.x, gridDim.x);
+  int* const cta_arrivals = quad_gemv_run<NK, NB, PLUG, DIAG>(p, blockIdx.x, gridDim.x);
   if (p.gather.world) gather_signal(p.gather, cta_arrivals, quad_warps(NK, NB));
 }
 
@@ -679,14 +777,14 @@ struct QuadGroupParams {
   QuadParams m[kMaxGroup];
 };
 
-template <bool NK, int NB, bool PLUG>
+template <bool NK, int NB, bool PLUG, bool DIAG>
 __global__ void __launch_bounds__(quad_warps(NK, NB) * 32, 1)
     quad_group_kernel(const __grid_constant__ QuadGroupParams g) {
   int j = 0;
   while (j + 1 < g.count && (int)blockIdx.x >= g.first_cta[j + 1]) ++j;
   const QuadParams& p = g.m[j];
   int* const cta_arrivals =
-      quad_gemv_run<NK, NB, PLUG>(p, (int)blockIdx.x - g.first_cta[j], g.first_cta[j + 1] - g.first_cta[j]);
+      quad_gemv_run<NK, NB, PLUG, DIAG>(p, (int)blockIdx.x - g.first_cta[j], g.first_cta[j + 1] - g.first_cta[j]);
   if (p.gather.world) gather_signal(p.gather, cta_arrivals, quad_warps(NK, NB));
 }
 
@@ -1116,8 +1214,8 @@ static int quad_run(const void* a, int64_t lda_m, int64_t lda_k, const uint32_t*
 // ------------------------------------------------------------ grouped --
 namespace {
 
-bool g_group_attr_done[64];
-int g_group_attr_limit[64];
+bool g_group_attr_done[128];  // [0, 64): shared activations, [64, 128): per-model rows, by device
+int g_group_attr_limit[128];
 
 struct GroupPlan {
   int count = 0, grid = 0;
@@ -1138,7 +1236,8 @@ int plan_group(int count, const pp_quad_linear_desc* d, int sms, GroupPlan* g) {
   int64_t units[kMaxGroup] = {0}, total = 0;
   for (int j = 0; j < count && g->one_launch; ++j) {
     const pp_quad_linear_desc& m = d[j];
-    const bool xok = m.x && m.ldx_k == 1 && aligned(m.x, 8);
+    const bool xok = m.x && m.ldx_k == 1 && aligned(m.x, 8) && (m.ldx_m * 2) % 8 == 0 && m.flags == d[0].flags &&
+                     (m.flags & ~PP_QUAD_PER_MODEL_X) == 0;
     if (m.M != 1 || m.N <= 0 || m.K <= 0 || !m.tables || !m.unit_plugs || !m.unit_plug_off || !m.plug_vals ||
         !m.plug_idx || !m.plug_window_base || !xok || !quad_vector_ok(true, m.codes, 1, m.ldw, m.N, m.K) ||
         m.N > INT32_MAX || m.K > INT32_MAX) {
@@ -1204,10 +1303,15 @@ int group_run(int count, const pp_quad_linear_desc* d, const PeerGather* gather,
   }
   GroupPlan g;
   plan_group(count, d, sms, &g);
+  bool extra = false;  // flags or an epilogue: the one-launch path only
+  for (int j = 0; j < count; ++j) {
+    extra |= d[j].flags != 0;
+    for (int k = 0; k < 4; ++k) extra |= d[j].bias[k] != nullptr || d[j].resid[k] != nullptr;
+  }
   if (!g.one_launch) {
-    if (gather) {
-      set_error("a gathered group needs every member on the one-launch path (batch 1, unit plugs, vector path, "
-                "at most %d members)", kMaxGroup);
+    if (gather || extra) {
+      set_error("a gathered group, per-model activations and epilogues need every member on the one-launch path "
+                "(batch 1, unit plugs, vector path, same flags, at most %d members, fits its SM share)", kMaxGroup);
       return PP_ERR_INVALID;
     }
     for (int j = 0; j < count; ++j) {  // one after another, sharing the workspace
@@ -1223,9 +1327,11 @@ int group_run(int count, const pp_quad_linear_desc* d, const PeerGather* gather,
     set_error("workspace of %zu bytes (256-byte aligned, zero-filled) required, got %zu", g.ws_off[count], ws_bytes);
     return PP_ERR_WORKSPACE;
   }
-  auto kern = quad_group_kernel<true, 1, true>;
+  const bool diag = (d[0].flags & PP_QUAD_PER_MODEL_X) != 0;
+  auto kern = diag ? quad_group_kernel<true, 1, true, true> : quad_group_kernel<true, 1, true, false>;
   int max_smem = 0;
-  int rc = ensure_smem_attr(kern, g_group_attr_done, g_group_attr_limit, &max_smem);
+  int rc = diag ? ensure_smem_attr(kern, g_group_attr_done + 64, g_group_attr_limit + 64, &max_smem)
+                : ensure_smem_attr(kern, g_group_attr_done, g_group_attr_limit, &max_smem);
   if (rc) return rc;
   constexpr int NW = quad_warps(true, 1);
   const uint32_t redb = quad_scratch_bytes(true, 1, 1);
@@ -1264,6 +1370,10 @@ int group_run(int count, const pp_quad_linear_desc* d, const PeerGather* gather,
     }
     prm.ldo_m = m.ldo_m;
     prm.ldo_n = m.ldo_n;
+    for (int i = 0; i < 4; ++i) {
+      prm.bias[i] = reinterpret_cast<const __half*>(m.bias[i]);
+      prm.resid[i] = reinterpret_cast<const __half*>(m.resid[i]);
+    }
     prm.M = 1;
     prm.N = (int)m.N;
     prm.K = (int)m.K;

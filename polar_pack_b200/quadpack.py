@@ -418,10 +418,20 @@ def quad_linear(x: torch.Tensor, layer: QuadLinearSlice, out=None) -> list[torch
     return out
 
 
-def linear_desc(x: torch.Tensor, layer: QuadLinearSlice, out) -> "_lib.QuadLinearDesc":
+def linear_desc(x: torch.Tensor, layer: QuadLinearSlice, out, per_model_x: bool = False, bias=None,
+                resid=None) -> "_lib.QuadLinearDesc":
     """The C descriptor of one ``quad_linear(x, layer, out)`` (pointers of the
-    given tensors: keep them alive while the descriptor is used)."""
+    given tensors: keep them alive while the descriptor is used).
+
+    ``per_model_x``: ``x`` has four rows, model k multiplies row k and writes
+    row 0 of ``out[k]``.  ``bias`` / ``resid``: four FP16 vectors (or None) of
+    the epilogue ``fp16(s_k acc + bias_k)``, then ``+ resid_k`` (``resid``
+    indexed like ``out``; it may be ``out`` itself)."""
     d = _lib.QuadLinearDesc()
+    d.flags = _lib.PER_MODEL_X if per_model_x else 0
+    for k in range(4):
+        d.bias[k] = bias[k].data_ptr() if bias is not None and bias[k] is not None else None
+        d.resid[k] = resid[k].data_ptr() if resid is not None and resid[k] is not None else None
     d.x, d.ldx_m, d.ldx_k = x.data_ptr(), x.stride(0), x.stride(1)
     d.codes, d.ldw = layer.codes.data_ptr(), layer.codes.stride(0)
     d.plug_idx, d.plug_vals = _lib.ptr(layer.plug_idx), _lib.ptr(layer.plug_vals)
@@ -432,7 +442,7 @@ def linear_desc(x: torch.Tensor, layer: QuadLinearSlice, out) -> "_lib.QuadLinea
         d.scales[k] = float(layer.pack.scales[k])
         d.out[k] = out[k].data_ptr() if out is not None else None
     d.ldo_m, d.ldo_n = (out[0].stride(0), out[0].stride(1)) if out is not None else (0, 0)
-    d.M, d.N, d.K = x.shape[0], layer.N, layer.K
+    d.M, d.N, d.K = (1 if per_model_x else x.shape[0]), layer.N, layer.K
     return d
 
 
@@ -446,16 +456,22 @@ class QuadLinearGroup:
     The members must not read each other's outputs.
     """
 
-    def __init__(self, layers, xs, outs):
+    def __init__(self, layers, xs, outs, per_model_x: bool = False, biases=None, resids=None):
         if not (len(layers) == len(xs) == len(outs)) or not layers:
             raise ValueError("one input and one output set per Linear")
         for x, l in zip(xs, layers):
             if x.dim() != 2 or x.shape[1] != l.K or x.dtype != torch.float16:
                 raise ValueError("each x must be fp16 (M, K) of its Linear")
+            if per_model_x and x.shape[0] != 4:
+                raise ValueError("per-model activations: x must have one row per model (4)")
         self.layers, self.xs, self.outs = list(layers), list(xs), [list(o) for o in outs]
         self.device = _lib.require_cuda(*self.xs)
         n = len(layers)
-        self.descs = (_lib.QuadLinearDesc * n)(*[linear_desc(x, l, o) for x, l, o in zip(xs, layers, outs)])
+        biases = biases or [None] * n
+        resids = resids or [None] * n
+        self._keep = (biases, resids)
+        self.descs = (_lib.QuadLinearDesc * n)(*[linear_desc(x, l, o, per_model_x, b, r)
+                                                 for x, l, o, b, r in zip(xs, layers, outs, biases, resids)])
         lib = _lib.load()
         nb = _lib._size_t()
         _lib.check(lib.pp_quad_linear_group_workspace_bytes(n, self.descs, ctypes.byref(nb)))
