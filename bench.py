@@ -144,6 +144,12 @@ DECODE_3B = {"layers": 36, "hidden": 2048, "inter": 11008, "q_heads": 16, "kv_he
              "vocab": 151936}
 
 
+# 7B-class dense decoder of BASELINE configs[4] (hidden 3584, intermediate
+# 18944, 28 q / 4 kv heads of 128, vocab 152064, 28 layers)
+DECODE_7B = {"layers": 28, "hidden": 3584, "inter": 18944, "q_heads": 28, "kv_heads": 4, "head_dim": 128,
+             "vocab": 152064}
+
+
 def decode_groups(cfg):
     """Launch groups of one decoder layer as (name, out N, in K), in stream
     order.  q/k/v and gate/up are consecutive Linears with one input, so in
@@ -417,9 +423,14 @@ def run_ours(args):
     e2e = run_e2e(torch, dist, sets, xs, dev, args, world, M, full_sets, pgroups)
 
     # the second half of the metric: 4-model decode tokens/s of a 3B-class step
-    decode = None
+    decode = decode7 = None
     if not args.no_decode and not args.shapes and M == 1:
-        decode = run_decode_step(torch, dist, dev, args, world, rank, lib, stream)
+        if world == 1:
+            decode = run_real_decode(torch, dev, args, stream, DECODE_3B, ctx=1024, seed=3000)
+            if not args.no_7b:
+                decode7 = run_real_decode(torch, dev, args, stream, DECODE_7B, ctx=1024, seed=7000)
+        else:
+            decode = run_decode_step(torch, dist, dev, args, world, rank, lib, stream)
     # batched rows on the same shapes (one GPU's kernel time)
     batched = None
     if not args.no_batched and M == 1:
@@ -461,6 +472,7 @@ def run_ours(args):
                    "per_shape_gemv_kernel": per_shape,
                    "parity": parity,
                    "decode_step_3b": decode,
+                   "decode_step_7b": decode7,
                    "dual_gemv_b1": dual,
                    "batched_rows": batched},
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
@@ -668,6 +680,78 @@ def run_dual_leg(torch, dev, args, lib, stream):
             "kernel": "dual_tma_kernel (batch 1, TMA engine)", "batch": M,
             "what": "polar_dual_bitpacked on the sweep shapes (in x out), graph of back-to-back launches over "
                     "replicas larger than L2, launch overlap on"}
+
+
+def run_real_decode(torch, dev, args, stream, arch, ctx, seed):
+    """One real decoder step of the four packed models on one GPU (BASELINE
+    configs[2] / configs[4] at batch 1): every layer distinct, each model with
+    its own token and hidden state, layers feeding each other, attention over
+    a KV cache of about ``ctx`` positions.  The step (embedding, RMSNorm,
+    packed qkv + bias, RoPE + KV append, decode attention, packed o +
+    residual, RMSNorm, packed gate_up, SwiGLU, packed down + residual, final
+    norm, packed lm_head) is one CUDA graph replayed per token."""
+    from polar_pack_b200.decoder import DecoderConfig, DecoderExtras, QuadDecoder, qwen2_layer_map
+    from polar_pack_b200.quadpack import DevicePackedStream, SyntheticModels, layer_offsets, pack_quad_generated
+    cfg = DecoderConfig(layers=arch["layers"], hidden=arch["hidden"], inter=arch["inter"], q_heads=arch["q_heads"],
+                        kv_heads=arch["kv_heads"], vocab=arch["vocab"], head_dim=arch["head_dim"],
+                        max_pos=ctx + 64)
+    lmap = qwen2_layer_map(cfg)
+    n = sum(e["numel"] for e in lmap)
+    t_pack = time.time()
+    p = pack_quad_generated(SyntheticModels(seed, dev), n, plug_cap=0.05, seed=42, windows=16, device=dev)
+    st = DevicePackedStream(p)
+    del p
+    torch.cuda.empty_cache()
+    t_pack = time.time() - t_pack
+    ex = DecoderExtras.random(cfg, dev, seed=seed + 1)
+    dec = QuadDecoder(st, cfg, ex, attn_splits=64)
+    st.check_plug_index()
+    g = torch.Generator(device=dev)
+    g.manual_seed(seed + 2)
+    for t in dec.kc + dec.vc:   # a cache of earlier tokens: the timed steps attend about ctx positions
+        t.copy_(torch.randn(t.shape, generator=g, device=dev) * 0.5)
+    steps = max(3, min(args.steps, 20))
+    start = ctx - steps - args.warmup - 1
+    dec.pos.fill_(start)
+    dec.capture(stream)
+    toks = torch.randint(0, cfg.vocab, (4,), generator=g, device=dev, dtype=torch.int32)
+    for _ in range(args.warmup):
+        dec.step(toks)
+    torch.cuda.synchronize(dev)
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0.record()
+    for _ in range(steps):
+        dec.step(toks)
+    t1.record()
+    torch.cuda.synchronize(dev)
+    ms = t0.elapsed_time(t1) / steps
+    finite = bool(torch.isfinite(dec.logits.float()).all())
+    status = int(dec.status.item())
+    if not finite or status:
+        raise RuntimeError(f"decode step produced non-finite logits or status {status}")
+    # algorithmic bytes of a step: the packed Linears (codes + plug entries +
+    # activations + outputs) and the KV cache read by attention
+    lin_bytes = 0
+    for name, off, (N, K) in layer_offsets(lmap):
+        lo, hi = st._plug_range(off, off + N * K)
+        lin_bytes += 4 * N * K + 12 * (hi - lo) + 2 * 4 * K + 2 * 4 * N
+    kv_bytes = cfg.layers * 4 * 2 * (ctx - 1) * cfg.kv_dim * 2
+    step_bytes = lin_bytes + kv_bytes
+    peak, peak_kind = measured_peak()
+    gbs = step_bytes / (ms * 1e-3) / 1e9
+    res = {"tok_s": round(4 / (ms * 1e-3), 1), "ms_per_step": round(ms, 3), "GB/s": round(gbs, 1),
+           "frac_of_measured_hbm": round(gbs / peak, 4), "bytes_per_step": int(step_bytes),
+           "launches_per_step": dec.launches_per_step(), "context": ctx, "batch_per_model": 1,
+           "pack_seconds": round(t_pack, 1),
+           "what": f"real 4-model decode step of a {cfg.layers}-layer dense decoder (hidden {cfg.hidden}, "
+                   f"intermediate {cfg.inter}, {cfg.q_heads} q / {cfg.kv_heads} kv heads, vocab {cfg.vocab}): "
+                   "one token per model, each with its own hidden state; every layer distinct; embedding, RMSNorm, "
+                   "packed qkv + bias, RoPE + KV append, decode attention, packed o + residual, RMSNorm, packed "
+                   "gate_up, SwiGLU, packed down + residual, final norm, packed lm_head",
+           "timing": "CUDA graph of one whole step, replayed per token; CUDA events"}
+    del dec, st, ex
+    torch.cuda.empty_cache()
+    return res
 
 
 def run_decode_step(torch, dist, dev, args, world, rank, lib, stream):
@@ -1106,7 +1190,8 @@ def main():
     ap.add_argument("--ref-fraction", type=float, default=1 / 32)
     ap.add_argument("--eager", action="store_true", help="time eager launches instead of CUDA graphs")
     ap.add_argument("--no-overlap", action="store_true", help="launch kernels without programmatic overlap")
-    ap.add_argument("--no-decode", action="store_true", help="skip the 3B decode-step leg")
+    ap.add_argument("--no-decode", action="store_true", help="skip the decode-step legs")
+    ap.add_argument("--no-7b", action="store_true", help="skip the 7B decode-step leg")
     ap.add_argument("--no-dual", action="store_true", help="skip the dual-pack kernel leg")
     ap.add_argument("--no-batched", action="store_true", help="skip the batched-rows leg")
     ap.add_argument("--nccl-gather", action="store_true",

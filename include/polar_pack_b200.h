@@ -342,26 +342,22 @@ PP_API int pp_embed_rows(const int* tokens, const void* const tables[4], int64_t
 PP_API int pp_rmsnorm_rows(const void* x, int64_t ldx, const void* const w[4], int64_t H, float eps, void* y,
                            int64_t ldy, void* stream);
 
-/* Rotary embedding of the token at *pos and its KV-cache append: row m of qkv
- * holds nq query heads, nkv key heads and nkv value heads of hd FP16 values.
- * Query heads are rotated in place, key heads rotated into k_cache[m] and
- * value heads copied into v_cache[m] at position *pos (caches [max_pos][nkv][hd]).
- * cos_t / sin_t: FP16 [max_pos][hd] tables of the rotation (both halves). */
-PP_API int pp_rope_kv_rows(void* qkv, int64_t ldq, int64_t nq, int64_t nkv, int64_t hd, const void* cos_t,
-                           const void* sin_t, int64_t max_pos, const int* pos, void* const k_cache[4],
-                           void* const v_cache[4], int* status, void* stream);
-
-/* Grouped-query decode attention of one token per model over cache positions
- * 0..*pos: out[m][h] = softmax(q[m][h] k^T * scale) v with the kv head
- * h / (nq / nkv); hd must be 128.  Split over `splits` position ranges, whose
+/* Grouped-query decode attention of one token per model, with the token's
+ * rotary embedding and KV-cache append fused in.  Row m of qkv holds the
+ * token's nq query, nkv key and nkv value heads of hd = 128 FP16 values, not
+ * rotated; cos_t / sin_t are FP16 [max_pos][hd] rotation tables (both
+ * halves).  The token's key is rotated and stored with its value into
+ * k_cache[m] / v_cache[m] ([max_pos][nkv][hd]) at *pos, then
+ *   out[m][h] = softmax(rope(q[m][h]) k^T * scale) v   over positions 0..*pos
+ * with kv head h / (nq / nkv).  Split over `splits` position ranges whose
  * partial results the last arriving block combines in order (deterministic).
  * Workspace: pp_decode_attention_workspace_bytes, zero-filled once. */
 PP_API int pp_decode_attention_workspace_bytes(int64_t nq, int64_t nkv, int64_t splits, size_t* bytes);
 
-PP_API int pp_decode_attention(const void* q, int64_t ldq, int64_t nq, int64_t nkv, int64_t hd,
-                               const void* const k_cache[4], const void* const v_cache[4], int64_t max_pos,
+PP_API int pp_decode_attention(void* qkv, int64_t ldq, int64_t nq, int64_t nkv, int64_t hd, const void* cos_t,
+                               const void* sin_t, void* const k_cache[4], void* const v_cache[4], int64_t max_pos,
                                const int* pos, float scale, void* out, int64_t ldo, int64_t splits,
-                               void* workspace, size_t workspace_bytes, void* stream);
+                               void* workspace, size_t workspace_bytes, int* status, void* stream);
 
 /* y[m][i] = fp16(fp16(silu(gate_up[m][i])) * gate_up[m][I + i]). */
 PP_API int pp_swiglu_rows(const void* gate_up, int64_t ldg, int64_t I, void* y, int64_t ldy, void* stream);

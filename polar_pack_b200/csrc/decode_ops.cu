@@ -1,7 +1,7 @@
 // The operations of a decoder step that sit between the packed Linears, for
 // the four models of a `.quadpack` decoding one token each: embedding row
-// gather, RMSNorm, rotary embedding with the KV-cache append, grouped-query
-// decode attention over the cache, SwiGLU.  Every launch handles the four
+// gather, RMSNorm, grouped-query decode attention over the KV cache with the
+// rotary embedding and the cache append of the token fused in, SwiGLU.  Every launch handles the four
 // models' rows (row m belongs to model m).  The reference serves these models
 // through Hugging Face Qwen2 modules (polar_inference.py:224-229 calls
 // model.generate); the arithmetic follows those modules' FP16 steps:
@@ -78,108 +78,124 @@ __global__ void rmsnorm_kernel(const NormParams p) {
   }
 }
 
-struct RopeParams {
-  __half* qkv;            // [4][ldq]: q heads, k heads, v heads of the token
-  int64_t ldq;
-  const __half* cos_t;    // [max_pos][hd]: FP16 cos / sin of position p (both halves)
-  const __half* sin_t;
-  const int* pos;         // device: position of the token
-  __half* kc[kModels];    // [max_pos][nkv][hd] per model
-  __half* vc[kModels];
-  int nq, nkv, hd, max_pos;
-  int* status;            // position out of range: 5
-};
-
-// q and k heads rotated (q in place, k into the cache at pos), v copied.
-__global__ void rope_kv_kernel(const RopeParams p) {
-  const int m = blockIdx.x;
-  const int pos = *p.pos;
-  if (pos < 0 || pos >= p.max_pos) {
-    if (threadIdx.x == 0 && p.status) atomicExch(p.status, 5);
-    return;
-  }
-  const int half = p.hd / 2;
-  __half* row = p.qkv + m * p.ldq;
-  const __half* cs = p.cos_t + (int64_t)pos * p.hd;
-  const __half* sn = p.sin_t + (int64_t)pos * p.hd;
-  const int pairs = (p.nq + p.nkv) * half;
-  for (int t = threadIdx.x; t < pairs; t += blockDim.x) {
-    const int head = t / half, i = t - head * half;
-    __half* hp = row + head * p.hd;
-    const float a = __half2float(hp[i]), b = __half2float(hp[i + half]);
-    const float c1 = __half2float(cs[i]), s1 = __half2float(sn[i]);
-    const float c2 = __half2float(cs[i + half]), s2 = __half2float(sn[i + half]);
-    const float ac = __half2float(__float2half_rn(a * c1)), bs = __half2float(__float2half_rn(-b * s1));
-    const float bc = __half2float(__float2half_rn(b * c2)), as = __half2float(__float2half_rn(a * s2));
-    const __half o1 = __float2half_rn(ac + bs), o2 = __float2half_rn(bc + as);
-    if (head < p.nq) {
-      hp[i] = o1;
-      hp[i + half] = o2;
-    } else {
-      __half* kp = p.kc[m] + ((int64_t)pos * p.nkv + (head - p.nq)) * p.hd;
-      kp[i] = o1;
-      kp[i + half] = o2;
-    }
-  }
-  const __half* v = row + (p.nq + p.nkv) * p.hd;
-  __half* vp = p.vc[m] + (int64_t)pos * p.nkv * p.hd;
-  for (int i = threadIdx.x; i < p.nkv * p.hd; i += blockDim.x) vp[i] = v[i];
-}
+constexpr int kHeadDim = 128;  // 4 dimensions per lane
+constexpr int kPartStride = kHeadDim + 4;  // floats per partial: acc, max, sum, 2 unused (16-byte rows)
+constexpr int kUnroll = 4;                 // cache positions whose loads are in flight together
 
 struct AttnParams {
-  const __half* q;        // [4][ldq], q heads first
+  const __half* qkv;      // [4][ldq]: the token's nq query, nkv key and nkv value heads (not rotated)
   int64_t ldq;
-  const __half* kc[kModels];
-  const __half* vc[kModels];
+  const __half* cos_t;    // [max_pos][hd] FP16 rotation tables (both halves)
+  const __half* sin_t;
+  __half* kc[kModels];    // [max_pos][nkv][hd] per model: rotated keys
+  __half* vc[kModels];
   const int* pos;         // the token's position: keys 0..pos are attended
   __half* out;            // [4][ldo]: nq heads x hd
   int64_t ldo;
-  float* part;            // [4][nq][splits][kPartStride] partial (acc, max, sum)
+  float* part;            // [4][nq][splits][kPartStride] partials (acc, max, sum)
   int* cnt;               // [4][nkv] split arrivals (zero between launches)
+  int* status;            // position outside the cache: 5
   int nq, nkv, splits, max_pos;
   float scale;
 };
 
-constexpr int kHeadDim = 128;  // 4 dimensions per lane
-constexpr int kPartStride = kHeadDim + 4;  // floats per partial: acc, max, sum, 2 unused (16-byte rows)
+// Rotary embedding of the four dimensions 4l..4l+3 a lane holds of a head
+// (v: those dimensions, FP32 of FP16): the pair of dimension d < hd/2 is
+// d + hd/2, held by lane l ^ 16.  q' = fp16(fp16(q cos) + fp16(rotate_half(q) sin)).
+__device__ __forceinline__ void rope4(float (&v)[4], const __half* cs, const __half* sn, int lane) {
+  float o[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) o[j] = __shfl_xor_sync(0xffffffffu, v[j], 16);
+  const bool lo = lane < 16;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const int d = 4 * lane + j;
+    const float c = __half2float(cs[d]), sn_ = __half2float(sn[d]);
+    const float rot = lo ? -o[j] : o[j];  // rotate_half: (-x2, x1)
+    v[j] = __half2float(__float2half_rn(__half2float(__float2half_rn(v[j] * c)) +
+                                        __half2float(__float2half_rn(rot * sn_))));
+  }
+}
 
-// Split-K decode attention: CTA (split, kv head, model); warp w is query head
-// kvh * group + w and walks keys [s0, s1) with an online softmax; lane l
-// holds dimensions 4l..4l+3.  The CTA whose arrival completes its
-// (model, kv head) combines the splits in split order (deterministic).
+// Split-K decode attention with the rotary embedding and the KV-cache append
+// of the token fused in.  CTA (split, kv head, model); warp w is query head
+// kvh * group + w, rotates its query and walks keys [s0, s1) with an online
+// softmax, kUnroll positions' loads at a time; lane l holds dimensions
+// 4l..4l+3.  The CTA whose range holds the token's position first writes
+// the token's rotated key and its value into the caches.  The CTA whose
+// arrival completes its (model, kv head) combines the splits in order
+// (deterministic).
 __global__ void decode_attention_kernel(const AttnParams p) {
   __shared__ int last;
   const int split = blockIdx.x, kvh = blockIdx.y, m = blockIdx.z;
   const int group = p.nq / p.nkv;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int qh = kvh * group + warp;
-  int len = *p.pos + 1;
-  if (len > p.max_pos) len = p.max_pos;
+  const int pos = *p.pos;
+  if (pos < 0 || pos >= p.max_pos) {
+    if (threadIdx.x == 0 && split == 0 && kvh == 0 && m == 0 && p.status) atomicExch(p.status, 5);
+    return;
+  }
+  const int len = pos + 1;
   const int chunk = (len + p.splits - 1) / p.splits;
   const int s0 = split * chunk, s1 = min(len, s0 + chunk);
-  const uint2 qv = *reinterpret_cast<const uint2*>(p.q + m * p.ldq + qh * kHeadDim + 4 * lane);
-  const float2 q01 = __half22float2(u2h(qv.x)), q23 = __half22float2(u2h(qv.y));
+  const __half* row = p.qkv + m * p.ldq;
+  const __half* cs = p.cos_t + (int64_t)pos * kHeadDim;
+  const __half* sn = p.sin_t + (int64_t)pos * kHeadDim;
+  const int64_t stride = (int64_t)p.nkv * kHeadDim;
+  if (s0 <= pos && pos < s1) {  // this CTA holds the token: append its key (rotated) and value first
+    if (warp == 0) {
+      const uint2 kr = *reinterpret_cast<const uint2*>(row + (p.nq + kvh) * kHeadDim + 4 * lane);
+      const uint2 vr = *reinterpret_cast<const uint2*>(row + (p.nq + p.nkv + kvh) * kHeadDim + 4 * lane);
+      const float2 k01 = __half22float2(u2h(kr.x)), k23 = __half22float2(u2h(kr.y));
+      float kv[4] = {k01.x, k01.y, k23.x, k23.y};
+      rope4(kv, cs, sn, lane);
+      __half2* kd = reinterpret_cast<__half2*>(p.kc[m] + (int64_t)pos * stride + kvh * kHeadDim + 4 * lane);
+      kd[0] = __floats2half2_rn(kv[0], kv[1]);
+      kd[1] = __floats2half2_rn(kv[2], kv[3]);
+      *reinterpret_cast<uint2*>(p.vc[m] + (int64_t)pos * stride + kvh * kHeadDim + 4 * lane) = vr;
+    }
+    __syncthreads();
+  }
+  const uint2 qr = *reinterpret_cast<const uint2*>(row + qh * kHeadDim + 4 * lane);
+  const float2 q01 = __half22float2(u2h(qr.x)), q23 = __half22float2(u2h(qr.y));
+  float q[4] = {q01.x, q01.y, q23.x, q23.y};
+  rope4(q, cs, sn, lane);
   const __half* kb = p.kc[m] + (int64_t)kvh * kHeadDim + 4 * lane;
   const __half* vb = p.vc[m] + (int64_t)kvh * kHeadDim + 4 * lane;
-  const int64_t stride = (int64_t)p.nkv * kHeadDim;
   float mx = -INFINITY, sum = 0.f, a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
-  for (int t = s0; t < s1; ++t) {
-    const uint2 kv = *reinterpret_cast<const uint2*>(kb + t * stride);
-    const uint2 vv = *reinterpret_cast<const uint2*>(vb + t * stride);
-    const float2 k01 = __half22float2(u2h(kv.x)), k23 = __half22float2(u2h(kv.y));
-    float s = q01.x * k01.x + q01.y * k01.y + q23.x * k23.x + q23.y * k23.y;
+  for (int t0 = s0; t0 < s1; t0 += kUnroll) {
+    uint2 kv[kUnroll], vv[kUnroll];
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
-    s *= p.scale;
-    const float mn = fmaxf(mx, s);
-    const float corr = expf(mx - mn), e = expf(s - mn);
-    const float2 v01 = __half22float2(u2h(vv.x)), v23 = __half22float2(u2h(vv.y));
-    sum = sum * corr + e;
-    a0 = a0 * corr + e * v01.x;
-    a1 = a1 * corr + e * v01.y;
-    a2 = a2 * corr + e * v23.x;
-    a3 = a3 * corr + e * v23.y;
-    mx = mn;
+    for (int u = 0; u < kUnroll; ++u) {
+      const int t = t0 + u < s1 ? t0 + u : s1 - 1;  // in range; duplicates are masked below
+      kv[u] = *reinterpret_cast<const uint2*>(kb + t * stride);
+      vv[u] = *reinterpret_cast<const uint2*>(vb + t * stride);
+    }
+    float sc[kUnroll];
+#pragma unroll
+    for (int u = 0; u < kUnroll; ++u) {
+      const float2 k01 = __half22float2(u2h(kv[u].x)), k23 = __half22float2(u2h(kv[u].y));
+      sc[u] = q[0] * k01.x + q[1] * k01.y + q[2] * k23.x + q[3] * k23.y;
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+      for (int u = 0; u < kUnroll; ++u) sc[u] += __shfl_xor_sync(0xffffffffu, sc[u], o);
+#pragma unroll
+    for (int u = 0; u < kUnroll; ++u) {
+      if (t0 + u >= s1) break;  // uniform over the warp
+      const float s = sc[u] * p.scale;
+      const float mn = fmaxf(mx, s);
+      const float corr = expf(mx - mn), e = expf(s - mn);
+      const float2 v01 = __half22float2(u2h(vv[u].x)), v23 = __half22float2(u2h(vv[u].y));
+      sum = sum * corr + e;
+      a0 = a0 * corr + e * v01.x;
+      a1 = a1 * corr + e * v01.y;
+      a2 = a2 * corr + e * v23.x;
+      a3 = a3 * corr + e * v23.y;
+      mx = mn;
+    }
   }
   float* pp = p.part + (((int64_t)m * p.nq + qh) * p.splits + split) * kPartStride;
   *reinterpret_cast<float4*>(pp + 4 * lane) = make_float4(a0, a1, a2, a3);
@@ -202,11 +218,12 @@ __global__ void decode_attention_kernel(const AttnParams p) {
     const float ms = __ldcg(b + kHeadDim);
     if (ms == -INFINITY) continue;  // an empty split
     const float w = expf(ms - M);
+    const float4 a = __ldcg(reinterpret_cast<const float4*>(b + 4 * lane));
     L += w * __ldcg(b + kHeadDim + 1);
-    o0 += w * __ldcg(b + 4 * lane);
-    o1 += w * __ldcg(b + 4 * lane + 1);
-    o2 += w * __ldcg(b + 4 * lane + 2);
-    o3 += w * __ldcg(b + 4 * lane + 3);
+    o0 += w * a.x;
+    o1 += w * a.y;
+    o2 += w * a.z;
+    o3 += w * a.w;
   }
   const float inv = 1.f / L;
   __half2* o = reinterpret_cast<__half2*>(p.out + m * p.ldo + qh * kHeadDim + 4 * lane);
@@ -286,37 +303,6 @@ int pp_rmsnorm_rows(const void* x, int64_t ldx, const void* const w[4], int64_t 
   return pp::check_launch("rmsnorm_kernel");
 }
 
-int pp_rope_kv_rows(void* qkv, int64_t ldq, int64_t nq, int64_t nkv, int64_t hd, const void* cos_t,
-                    const void* sin_t, int64_t max_pos, const int* pos, void* const k_cache[4],
-                    void* const v_cache[4], int* status, void* stream) {
-  if (!qkv || !cos_t || !sin_t || !pos || !k_cache || !v_cache || nq <= 0 || nkv <= 0 || hd <= 0 || hd % 2 ||
-      max_pos <= 0 || ldq < (nq + 2 * nkv) * hd || nq > 4096 || nkv > 4096 || hd > 4096 || max_pos > INT32_MAX) {
-    pp::set_error("pp_rope_kv_rows: invalid arguments");
-    return PP_ERR_INVALID;
-  }
-  pp::RopeParams p{};
-  p.qkv = reinterpret_cast<__half*>(qkv);
-  p.ldq = ldq;
-  p.cos_t = reinterpret_cast<const __half*>(cos_t);
-  p.sin_t = reinterpret_cast<const __half*>(sin_t);
-  p.pos = pos;
-  for (int k = 0; k < 4; ++k) {
-    if (!k_cache[k] || !v_cache[k]) {
-      pp::set_error("pp_rope_kv_rows: cache of model %d is NULL", k);
-      return PP_ERR_INVALID;
-    }
-    p.kc[k] = reinterpret_cast<__half*>(k_cache[k]);
-    p.vc[k] = reinterpret_cast<__half*>(v_cache[k]);
-  }
-  p.nq = (int)nq;
-  p.nkv = (int)nkv;
-  p.hd = (int)hd;
-  p.max_pos = (int)max_pos;
-  p.status = status;
-  pp::rope_kv_kernel<<<4, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(p);
-  return pp::check_launch("rope_kv_kernel");
-}
-
 int pp_decode_attention_workspace_bytes(int64_t nq, int64_t nkv, int64_t splits, size_t* bytes) {
   if (!bytes || nq <= 0 || nkv <= 0 || splits <= 0) {
     pp::set_error("invalid arguments");
@@ -327,15 +313,17 @@ int pp_decode_attention_workspace_bytes(int64_t nq, int64_t nkv, int64_t splits,
   return PP_OK;
 }
 
-int pp_decode_attention(const void* q, int64_t ldq, int64_t nq, int64_t nkv, int64_t hd,
-                        const void* const k_cache[4], const void* const v_cache[4], int64_t max_pos,
+int pp_decode_attention(void* qkv, int64_t ldq, int64_t nq, int64_t nkv, int64_t hd, const void* cos_t,
+                        const void* sin_t, void* const k_cache[4], void* const v_cache[4], int64_t max_pos,
                         const int* pos, float scale, void* out, int64_t ldo, int64_t splits, void* workspace,
-                        size_t workspace_bytes, void* stream) {
-  if (!q || !k_cache || !v_cache || !pos || !out || hd != pp::kHeadDim || nq <= 0 || nkv <= 0 || nq % nkv ||
-      nq / nkv > 32 || splits <= 0 || splits > 65535 || max_pos <= 0 || max_pos > INT32_MAX ||
-      !pp::aligned(q, 8) || ldq % 4 || !pp::aligned(out, 4) || ldo % 2) {
+                        size_t workspace_bytes, int* status, void* stream) {
+  if (!qkv || !cos_t || !sin_t || !k_cache || !v_cache || !pos || !out || hd != pp::kHeadDim || nq <= 0 ||
+      nkv <= 0 || nq % nkv || nq / nkv > 32 || splits <= 0 || splits > 65535 || max_pos <= 0 ||
+      max_pos > INT32_MAX || !pp::aligned(qkv, 8) || ldq % 4 || ldq < (nq + 2 * nkv) * hd || !pp::aligned(out, 4) ||
+      ldo % 2) {
     pp::set_error("pp_decode_attention: head_dim must be %d, nq a multiple of nkv (at most 32 q heads per kv "
-                  "head), 8-byte aligned q rows, 4-byte aligned output rows", pp::kHeadDim);
+                  "head), 8-byte aligned qkv rows holding nq + 2 nkv heads, 4-byte aligned output rows",
+                  pp::kHeadDim);
     return PP_ERR_INVALID;
   }
   size_t need = 0;
@@ -345,15 +333,17 @@ int pp_decode_attention(const void* q, int64_t ldq, int64_t nq, int64_t nkv, int
     return PP_ERR_WORKSPACE;
   }
   pp::AttnParams p{};
-  p.q = reinterpret_cast<const __half*>(q);
+  p.qkv = reinterpret_cast<const __half*>(qkv);
   p.ldq = ldq;
+  p.cos_t = reinterpret_cast<const __half*>(cos_t);
+  p.sin_t = reinterpret_cast<const __half*>(sin_t);
   for (int k = 0; k < 4; ++k) {
     if (!k_cache[k] || !v_cache[k] || !pp::aligned(k_cache[k], 8) || !pp::aligned(v_cache[k], 8)) {
       pp::set_error("pp_decode_attention: cache of model %d is NULL or not 8-byte aligned", k);
       return PP_ERR_INVALID;
     }
-    p.kc[k] = reinterpret_cast<const __half*>(k_cache[k]);
-    p.vc[k] = reinterpret_cast<const __half*>(v_cache[k]);
+    p.kc[k] = reinterpret_cast<__half*>(k_cache[k]);
+    p.vc[k] = reinterpret_cast<__half*>(v_cache[k]);
   }
   p.pos = pos;
   p.out = reinterpret_cast<__half*>(out);
@@ -361,6 +351,7 @@ int pp_decode_attention(const void* q, int64_t ldq, int64_t nq, int64_t nkv, int
   p.cnt = reinterpret_cast<int*>(workspace);
   p.part = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(workspace) +
                                     pp::align_up((size_t)4 * nkv * sizeof(int), 256));
+  p.status = status;
   p.nq = (int)nq;
   p.nkv = (int)nkv;
   p.splits = (int)splits;

@@ -15,8 +15,9 @@ Two ways to serve the Linears of a ``.quadpack`` from HBM without unpacking:
   generates through Hugging Face Qwen2 modules).  Every packed Linear is one
   launch over its codes that multiplies model k's weights with model k's row
   (``PP_QUAD_PER_MODEL_X``), with the q/k/v bias and the residual add in its
-  epilogue; RMSNorm, rotary embedding + KV-cache append, decode attention and
-  SwiGLU are this library's kernels (``decode_ops.cu``).  The step has fixed
+  epilogue; RMSNorm, decode attention (with the rotary embedding and the
+  KV-cache append fused in) and SwiGLU are this library's kernels
+  (``decode_ops.cu``).  The step has fixed
   buffers and a device-side position, so it can be captured once as a CUDA
   graph and replayed for every token.
 """
@@ -197,7 +198,7 @@ class QuadDecoder:
     ``logits`` ``[4][vocab]`` (FP16); the position advances by one per step.
     """
 
-    def __init__(self, pack, cfg: DecoderConfig, extras: DecoderExtras, attn_splits: int = 16):
+    def __init__(self, pack, cfg: DecoderConfig, extras: DecoderExtras, attn_splits: int = 64):
         self.pack, self.cfg, self.ex = pack, cfg, extras
         dev = self.device = pack.device
         self.lib = _lib.load()
@@ -250,7 +251,7 @@ class QuadDecoder:
         self.graph = None
 
     def launches_per_step(self) -> int:
-        return 2 + self.cfg.layers * 5 + sum(len(c) for g in self.groups for c in g) + len(self.head)
+        return 2 + self.cfg.layers * 4 + sum(len(c) for g in self.groups for c in g) + len(self.head)
 
     def _run(self, s) -> None:
         """Enqueue one step on stream handle s (tokens and pos already set)."""
@@ -262,13 +263,11 @@ class QuadDecoder:
         for l, (g_qkv, g_o, g_gu, g_d) in enumerate(self.groups):
             c(L.pp_rmsnorm_rows(self.h.data_ptr(), H, self._in_norm[l], H, cfg.rms_eps, self.xn.data_ptr(), H, s))
             run(g_qkv)
-            c(L.pp_rope_kv_rows(self.qkv.data_ptr(), self.qkv.stride(0), cfg.q_heads, cfg.kv_heads, cfg.head_dim,
-                                self.cos.data_ptr(), self.sin.data_ptr(), cfg.max_pos, self.pos.data_ptr(),
-                                self._kc[l], self._vc[l], self.status.data_ptr(), s))
             c(L.pp_decode_attention(self.qkv.data_ptr(), self.qkv.stride(0), cfg.q_heads, cfg.kv_heads,
-                                    cfg.head_dim, self._kc[l], self._vc[l], cfg.max_pos, self.pos.data_ptr(),
-                                    self.scale, self.attn.data_ptr(), self.attn.stride(0), self.splits,
-                                    self.attn_ws.data_ptr(), self.attn_ws.numel(), s))
+                                    cfg.head_dim, self.cos.data_ptr(), self.sin.data_ptr(), self._kc[l],
+                                    self._vc[l], cfg.max_pos, self.pos.data_ptr(), self.scale, self.attn.data_ptr(),
+                                    self.attn.stride(0), self.splits, self.attn_ws.data_ptr(),
+                                    self.attn_ws.numel(), self.status.data_ptr(), s))
             run(g_o)
             c(L.pp_rmsnorm_rows(self.h.data_ptr(), H, self._post_norm[l], H, cfg.rms_eps, self.xn.data_ptr(), H,
                                 s))

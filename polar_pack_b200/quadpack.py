@@ -579,6 +579,88 @@ def pack_quad_device(models, plug_cap: float = 0.05, seed: int = 42, windows: in
                 plug_vals=plug_vals, tail_vals=tail_t, threshold=thr)
 
 
+def pack_quad_generated(gen, n: int, plug_cap: float = 0.05, seed: int = 42, windows: int = 100,
+                        window: int = 1_000_000, chunk: int = 1 << 24, device=None) -> dict:
+    """:func:`pack_quad_device` for models too large to hold at once.
+
+    ``gen(start, stop)`` returns the four models' weights at flat positions
+    ``[start, stop)`` (four 1-D tensors on ``device``), the same values for a
+    position whatever range asks for it.  The passes are those of pack_quad
+    (quaternion_packer.py:52-138): float64 RMS, r_max and the plug threshold
+    over seeded windows, then codes and plug entries chunk by chunk, so only
+    the codes and one chunk live on the device.  Models of equal length (no
+    tails).
+    """
+    dev = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
+    acc = torch.zeros(4, dtype=torch.float64, device=dev)
+    r_max = torch.zeros((), dtype=torch.float32, device=dev)
+    for i in range(0, n, chunk):
+        ws = gen(i, min(i + chunk, n))
+        for k, w in enumerate(ws):
+            acc[k] += (w.double() ** 2).sum()
+    s = [float(torch.sqrt(acc[k] / n)) for k in range(4)]
+    for i in range(0, n, chunk):
+        wc = [w.float() / sk for w, sk in zip(gen(i, min(i + chunk, n)), s)]
+        r_max = torch.maximum(r_max, torch.sqrt(sum(x * x for x in wc)).max())
+    r_max = float(r_max) * 1.001
+    window = min(window, max(1, n - 1))
+    rng = np.random.default_rng(seed)
+    starts = rng.integers(0, max(1, n - window), windows)
+    errs = []
+    for st in starts:
+        wc = [w.float() / sk for w, sk in zip(gen(int(st), int(st) + window), s)]
+        errs.append(_quantize_chunk_torch(wc, r_max, True)[1].cpu().numpy())
+    thr = float(np.percentile(np.concatenate(errs), (1 - plug_cap) * 100))
+    codes = torch.empty(n, dtype=torch.uint32, device=dev)
+    pidx, pval = [], []
+    for i in range(0, n, chunk):
+        wc = [w.float() / sk for w, sk in zip(gen(i, min(i + chunk, n)), s)]
+        c, err = _quantize_chunk_torch(wc, r_max, True)
+        codes[i:i + c.numel()] = c
+        idx = torch.nonzero(err > thr).flatten()
+        if idx.numel():
+            pidx.append(idx + i)
+            pval.append(torch.stack([w[idx] for w in wc], dim=1).half())
+    plug_idx = torch.cat(pidx) if pidx else torch.zeros(0, dtype=torch.int64, device=dev)
+    plug_vals = torch.cat(pval) if pval else torch.zeros((0, 4), dtype=torch.float16, device=dev)
+    empty = torch.zeros(0, dtype=torch.float16, device=dev)
+    return dict(n=n, scales=s, r_max=r_max, tails=[0, 0, 0, 0], codes=codes, plug_pos=plug_idx,
+                plug_vals=plug_vals, tail_vals=[empty] * 4, threshold=thr)
+
+
+class SyntheticModels:
+    """Four correlated FP16 weight streams of any length, generated on demand:
+    base N(0, 0.02) + per-model delta N(0, 0.002), 0.1% of entries x 20 (the
+    benchmark distribution).  Blocks of ``block`` positions have their own
+    seeds, so ``self(start, stop)`` gives the same values for a position
+    whatever range is asked for (what :func:`pack_quad_generated` needs)."""
+
+    def __init__(self, seed: int, device, block: int = 1 << 20):
+        self.seed, self.device, self.block = seed, torch.device(device), block
+
+    def _block(self, b: int) -> list[torch.Tensor]:
+        g = torch.Generator(device=self.device)
+        g.manual_seed(self.seed * 1_000_003 + b)
+        B = self.block
+        base = torch.randn(B, generator=g, device=self.device) * 0.02
+        out = []
+        for _ in range(4):
+            w = base + torch.randn(B, generator=g, device=self.device) * 0.002
+            w = torch.where(torch.rand(B, generator=g, device=self.device) < 0.001, w * 20, w)
+            out.append(w.half())
+        return out
+
+    def __call__(self, start: int, stop: int) -> list[torch.Tensor]:
+        B = self.block
+        b0, b1 = start // B, (stop + B - 1) // B
+        parts = [self._block(b) for b in range(b0, b1)]
+        res = []
+        for k in range(4):
+            cat = torch.cat([p[k] for p in parts]) if len(parts) > 1 else parts[0][k]
+            res.append(cat[start - b0 * B:stop - b0 * B])
+        return res
+
+
 def to_bytes(p: dict) -> bytes:
     """Serialise :func:`pack_quad_device` output as a ``.quadpack`` v2 stream."""
     hdr = struct.pack(HEADER_FMT, MAGIC, VERSION, N_MODELS, p["n"], 8, 8, 8, 8, MU,
