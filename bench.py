@@ -7,37 +7,34 @@ Workload: the quad-pack single-layer sweep -- four correlated synthetic models
 (base N(0,0.02) + delta N(0,0.002), 0.1% entries x20, FP16), packed into
 ``.quadpack`` v2 streams (plug cap 5%), Linear shapes in x out = 2048x2048,
 2048x11008, 11008x2048, 2048x256, batch 1.  One step = the four Linears
-(4 outputs per pass over the codes).
-R = 4 replica streams rotate step to step, so each step reads ~200 MB of
-codes that were last touched 3 steps (~600 MB) earlier: inputs exceed the
-126 MB L2 and no flush is needed.  A Linear is one kernel launch: the
-fused GEMV with the plug-table correction inside (batch 1; larger batches
-add the CSR correction kernel).  Kernels run with launch overlap
-(programmatic dependent launch: each may start its weight-only prologue
-while the previous one finishes), unless ``--no-overlap``.
+(4 outputs per pass over the codes), run as ONE grouped launch
+(``QuadLinearGroup``: each Linear on its share of the SMs, plug correction
+fused).  R = 4 replica streams rotate step to step, so each step reads
+~230 MB of codes last touched ~690 MB earlier: inputs exceed the 126 MB L2
+and no flush is needed.  Kernels run with launch overlap (programmatic
+dependent launch) unless ``--no-overlap``.
 
-A second leg times the packed Linears of a 3B-class decode step (BASELINE
-36 layers of qkv / o / gate_up / down launches plus the lm_head,
-batch 1) and reports 4-model decode tokens/s under
-``config.decode_step_3b`` (``--no-decode`` skips it).  A third times the
-dual-pack kernel (2 models of 16-bit polar codes) on the sweep shapes at
-batch 1 under ``config.dual_gemv_b1`` (``--no-dual`` skips it), and a fourth
-the quad path at 16 and 64 batch rows (the tcgen05
-tile kernel where it applies) under ``config.batched_rows``
-(``--no-batched`` skips it).
+Further legs (in ``config``): real 4-model decode steps of the 3B-class
+(configs[2]) and 7B-class decoders at batch 1 per model
+(``decode_step_3b`` / ``decode_step_7b``; ``--no-decode``, ``--no-7b``), the
+dual-pack kernel on the sweep shapes (``dual_gemv_b1``; ``--no-dual``) and the
+quad path at 16 and 64 batch rows (configs[3]; ``batched_rows``;
+``--no-batched``).
 
 Metric: packed-stream GB/s = algorithmic bytes / device time, where the
 bytes of one Linear are 4*N*K (codes) + 12*P (plug index + values) +
-2*M*K (activations) + 8*M*N (four FP16 outputs).  The roofline entry times
-the dominant kernel, the GEMV with the plug correction fused in, one shape at
-a time over the same bytes.
+2*M*K (activations) + 8*M*N (four FP16 outputs).  The roofline entry is the
+step's grouped launch (the only kernel of the step).
 
 With N > 1 GPUs (launched by torch.distributed.run) each Linear is
 row-sharded (column-parallel): rank r owns output rows [r*N/P, (r+1)*N/P),
-which are a contiguous slice of the file-layout stream; the sweep's four
-Linears are independent, so one NCCL all-gather per step collects their
-outputs (the decode leg gathers after every launch, as a layer needs).  Total work is fixed
-(strong scaling); time is the max over ranks of CUDA-event time.
+a contiguous slice of the file-layout stream.  The GEMVs store their rows
+straight into every rank's buffer over NVLink (peer memory), the sweep's
+four Linears as one grouped launch that publishes once, then one bounded
+wait per step (``--nccl-gather``: one NCCL all-gather per step instead).
+Each rank's gathered outputs are checked against the unsharded Linears
+before timing.  Total work is fixed (strong scaling); time is the max over
+ranks of CUDA-event time.
 
 ``--impl reference`` times the reference's own CPU path (the oracle's
 restatement of ``unpack_quad`` -- float64 decode, plug merge, scale -- then a
@@ -148,16 +145,6 @@ DECODE_3B = {"layers": 36, "hidden": 2048, "inter": 11008, "q_heads": 16, "kv_he
 # 18944, 28 q / 4 kv heads of 128, vocab 152064, 28 layers)
 DECODE_7B = {"layers": 28, "hidden": 3584, "inter": 18944, "q_heads": 28, "kv_heads": 4, "head_dim": 128,
              "vocab": 152064}
-
-
-def decode_groups(cfg):
-    """Launch groups of one decoder layer as (name, out N, in K), in stream
-    order.  q/k/v and gate/up are consecutive Linears with one input, so in
-    the `.quadpack` stream (each Linear (out, in) row-major, layer-map order)
-    each group is one contiguous (sum of outs, in) matrix: one launch."""
-    h, i = cfg["hidden"], cfg["inter"]
-    q, kv = cfg["q_heads"] * cfg["head_dim"], cfg["kv_heads"] * cfg["head_dim"]
-    return [("qkv", q + 2 * kv, h), ("o", h, q), ("gate_up", 2 * i, h), ("down", h, i)]
 
 
 # ------------------------------------------------------------ workload ----
@@ -425,12 +412,11 @@ def run_ours(args):
     # the second half of the metric: 4-model decode tokens/s of a 3B-class step
     decode = decode7 = None
     if not args.no_decode and not args.shapes and M == 1:
-        if world == 1:
-            decode = run_real_decode(torch, dev, args, stream, DECODE_3B, ctx=1024, seed=3000)
-            if not args.no_7b:
-                decode7 = run_real_decode(torch, dev, args, stream, DECODE_7B, ctx=1024, seed=7000)
-        else:
-            decode = run_decode_step(torch, dist, dev, args, world, rank, lib, stream)
+        decode = run_real_decode(torch, dist, dev, args, stream, DECODE_3B, ctx=1024, seed=3000, world=world,
+                                 rank=rank)
+        if not args.no_7b:
+            decode7 = run_real_decode(torch, dist, dev, args, stream, DECODE_7B, ctx=1024, seed=7000, world=world,
+                                      rank=rank)
     # batched rows on the same shapes (one GPU's kernel time)
     batched = None
     if not args.no_batched and M == 1:
@@ -682,14 +668,17 @@ def run_dual_leg(torch, dev, args, lib, stream):
                     "replicas larger than L2, launch overlap on"}
 
 
-def run_real_decode(torch, dev, args, stream, arch, ctx, seed):
-    """One real decoder step of the four packed models on one GPU (BASELINE
-    configs[2] / configs[4] at batch 1): every layer distinct, each model with
-    its own token and hidden state, layers feeding each other, attention over
-    a KV cache of about ``ctx`` positions.  The step (embedding, RMSNorm,
-    packed qkv + bias, RoPE + KV append, decode attention, packed o +
-    residual, RMSNorm, packed gate_up, SwiGLU, packed down + residual, final
-    norm, packed lm_head) is one CUDA graph replayed per token."""
+def run_real_decode(torch, dist, dev, args, stream, arch, ctx, seed, world=1, rank=0):
+    """One real decoder step of the four packed models (BASELINE configs[2] /
+    configs[4] at batch 1): every layer distinct, each model with its own
+    token and hidden state, layers feeding each other, attention over a KV
+    cache of about ``ctx`` positions.  The step (embedding, RMSNorm, packed
+    qkv + bias, decode attention with RoPE + KV append, packed o + residual,
+    RMSNorm, packed gate_up, SwiGLU, packed down + residual, final norm,
+    packed lm_head) is one CUDA graph replayed per token.  With N > 1 GPUs
+    every packed Linear is row-sharded and gathered by its GEMV into every
+    rank's buffers over NVLink (one bounded wait per Linear); the rest runs
+    on every rank.  Time: max over ranks of CUDA-event time."""
     from polar_pack_b200.decoder import DecoderConfig, DecoderExtras, QuadDecoder, qwen2_layer_map
     from polar_pack_b200.quadpack import DevicePackedStream, SyntheticModels, layer_offsets, pack_quad_generated
     cfg = DecoderConfig(layers=arch["layers"], hidden=arch["hidden"], inter=arch["inter"], q_heads=arch["q_heads"],
@@ -704,7 +693,7 @@ def run_real_decode(torch, dev, args, stream, arch, ctx, seed):
     torch.cuda.empty_cache()
     t_pack = time.time() - t_pack
     ex = DecoderExtras.random(cfg, dev, seed=seed + 1)
-    dec = QuadDecoder(st, cfg, ex, attn_splits=64)
+    dec = QuadDecoder(st, cfg, ex, world=world, rank=rank)
     st.check_plug_index()
     g = torch.Generator(device=dev)
     g.manual_seed(seed + 2)
@@ -713,11 +702,15 @@ def run_real_decode(torch, dev, args, stream, arch, ctx, seed):
     steps = max(3, min(args.steps, 20))
     start = ctx - steps - args.warmup - 1
     dec.pos.fill_(start)
+    if world > 1:
+        dist.barrier()
     dec.capture(stream)
     toks = torch.randint(0, cfg.vocab, (4,), generator=g, device=dev, dtype=torch.int32)
     for _ in range(args.warmup):
         dec.step(toks)
     torch.cuda.synchronize(dev)
+    if world > 1:
+        dist.barrier()
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     t0.record()
     for _ in range(steps):
@@ -726,7 +719,11 @@ def run_real_decode(torch, dev, args, stream, arch, ctx, seed):
     torch.cuda.synchronize(dev)
     ms = t0.elapsed_time(t1) / steps
     finite = bool(torch.isfinite(dec.logits.float()).all())
-    status = int(dec.status.item())
+    status = int(dec.status.item()) + (int(dec.peers.status.item()) if dec.peers is not None else 0)
+    if world > 1:
+        t = torch.tensor([ms, 0.0 if finite else 1.0, float(status)], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms, finite, status = float(t[0]), float(t[1]) == 0.0, int(t[2])
     if not finite or status:
         raise RuntimeError(f"decode step produced non-finite logits or status {status}")
     # algorithmic bytes of a step: the packed Linears (codes + plug entries +
@@ -749,186 +746,13 @@ def run_real_decode(torch, dev, args, stream, arch, ctx, seed):
                    "packed qkv + bias, RoPE + KV append, decode attention, packed o + residual, RMSNorm, packed "
                    "gate_up, SwiGLU, packed down + residual, final norm, packed lm_head",
            "timing": "CUDA graph of one whole step, replayed per token; CUDA events"}
+    if world > 1:
+        res["parallelism"] = (f"row-sharded x{world}: each GEMV stores its rows into every rank's buffer over "
+                              "NVLink, one bounded wait per Linear; norms and attention on every rank")
+    dec.graph = None
+    torch.cuda.synchronize(dev)
+    dec.close()
     del dec, st, ex
-    torch.cuda.empty_cache()
-    return res
-
-
-def run_decode_step(torch, dist, dev, args, world, rank, lib, stream):
-    """The packed Linears of one 3B-class decode step at batch 1: 36 layers of
-    four launches (qkv, o, gate_up, down) plus the lm_head, each launch one
-    fused GEMV with its plug correction.  Two distinct layer weight sets
-    (616 MB of codes, more than L2) alternate over the 36 layers, so every
-    launch streams codes L2 does not hold; the lm_head (1.24 GB) is its own.
-    Inputs are fixed random vectors: the attention, norms and activation
-    functions between the Linears are outside this path and not run.  With
-    N > 1 GPUs each launch computes the rank's row shard and one all-gather
-    per launch collects the outputs, as the layer's next step needs them.
-    Returns the leg's summary for the JSON line."""
-    import ctypes as C
-    from polar_pack_b200 import _lib
-    from polar_pack_b200.parallel import row_shard, shard_width
-    from polar_pack_b200.quadpack import DevicePackedStream, pack_quad_device, quad_linear_workspace_bytes
-    cfg, M = DECODE_3B, 1
-    groups = decode_groups(cfg)
-    per_layer = sum(N * K for _, N, K in groups)
-    distinct = 2
-    head_nk = (cfg["vocab"], cfg["hidden"])
-    n = distinct * per_layer + head_nk[0] * head_nk[1]
-    models = synth_models(torch, n, 3000, dev)
-    p = pack_quad_device(models, plug_cap=0.05, seed=42, windows=16, window=1_000_000)
-    del models
-    torch.cuda.empty_cache()
-    st = DevicePackedStream(p)
-    del p
-    st.check_plug_index()
-    g = torch.Generator(device=dev)
-    g.manual_seed(11)
-    xin = {K: torch.randn(M, K, generator=g, device=dev).half() for K in {K for _, _, K in groups}}
-
-    def shard(off, N, K):
-        n0, n1 = row_shard(N, world, rank)
-        return st.linear(off + n0 * K, n1 - n0, K)
-
-    units, off = [], 0   # per distinct layer: its groups; then the head
-    for _ in range(distinct):
-        row = []
-        for name, N, K in groups:
-            row.append((N, K, shard(off, N, K)))
-            off += N * K
-        units.append(row)
-    head = (head_nk[0], head_nk[1], shard(off, *head_nk))
-    lins = [u for row in units for u in row] + [head]
-    ws_bytes = max(quad_linear_workspace_bytes(M, l.N, l.K) for _, _, l in lins)
-    ws = torch.zeros(max(ws_bytes, 256), dtype=torch.uint8, device=dev)
-    sh = stream.cuda_stream
-
-    def prep(N, K, l):
-        w = shard_width(N, world)
-        send = torch.zeros((4, M, w), dtype=torch.float16, device=dev)
-        recv = torch.empty((world * 4, M, w), dtype=torch.float16, device=dev) if world > 1 else None
-        outs = [send[k, :, :l.N] for k in range(4)]
-        x = xin[K]
-        a = (x.data_ptr(), x.stride(0), x.stride(1), l.codes.data_ptr(), l.K, _lib.ptr(l.plug_idx),
-             _lib.ptr(l.plug_vals), _lib.ptr(l.plug_window_base), C.c_uint32(l.offset & 0xFFFFFFFF),
-             _lib.ptr(l.unit_plugs), _lib.ptr(l.unit_plug_off), l.pack.tables.data_ptr(), _lib.floats4(l.pack.scales),
-             _lib.ptrs(outs, 4), outs[0].stride(0), outs[0].stride(1), M, l.N, l.K, ws.data_ptr(), ws.numel(), sh)
-        return a, send, recv, outs
-
-    # N > 1 GPUs: each launch stores its rows into every rank's gather
-    # buffer (peer memory) and a bounded wait follows it; the layers' launches
-    # alternate buffers 0 and 1, the lm_head uses buffer 2, so no buffer is
-    # written twice in a row, across steps either
-    use_peer = world > 1 and not args.nccl_gather
-    peers = None
-    if use_peer:
-        from polar_pack_b200.parallel import PeerBuffers
-        peers = PeerBuffers(4 * max(N for N, _, _ in lins), nbuf=3, device=dev)
-
-    def prep_peer(N, K, l, b):
-        n0, _ = row_shard(N, world, rank)
-        outs = (C.c_void_p * 8)(*peers.out_ptrs(b))
-        flags = (C.c_void_p * 8)(*peers.flag_ptrs(b))
-        x = xin[K]
-        a = (x.data_ptr(), x.stride(1), l.codes.data_ptr(), l.K, _lib.ptr(l.plug_idx), _lib.ptr(l.plug_vals),
-             _lib.ptr(l.plug_window_base), C.c_uint32(l.offset & 0xFFFFFFFF), _lib.ptr(l.unit_plugs),
-             _lib.ptr(l.unit_plug_off), l.pack.tables.data_ptr(), _lib.floats4(l.pack.scales), world, outs, N, n0,
-             flags, peers.epoch_ptr(b), l.N, l.K, ws.data_ptr(), ws.numel(), sh)
-        return ("peer", a, b, outs, flags)
-
-    if use_peer:
-        k = 0
-        calls = []
-        for row in units:
-            r_ = []
-            for N, K, l in row:
-                r_.append(prep_peer(N, K, l, k % 2))
-                k += 1
-            calls.append(r_)
-        head_call = prep_peer(*head, 2)
-    else:
-        calls = [[prep(N, K, l) for N, K, l in row] for row in units]
-        head_call = prep(*head)
-
-    def launch(c):
-        if c[0] == "peer":
-            rc = lib.pp_quad_linear_gather(*c[1])
-            if rc:
-                _lib.check(rc)
-            peers.wait(c[2], sh)
-            return
-        rc = lib.pp_quad_linear_fused(*c[0])
-        if rc:
-            _lib.check(rc)
-        if world > 1:
-            dist.all_gather_into_tensor(c[2], c[1])
-
-    def step():
-        for layer in range(cfg["layers"]):
-            for c in calls[layer % distinct]:
-                launch(c)
-        launch(head_call)
-
-    for _ in range(2):
-        step()
-    torch.cuda.synchronize(dev)
-    graph = None
-    if not args.eager:
-        try:
-            graph = torch.cuda.CUDAGraph()
-            with torch.cuda.graph(graph, stream=stream):
-                step()
-            graph.replay()
-            torch.cuda.synchronize(dev)
-        except Exception as e:  # capture unsupported: time eager launches
-            print(f"decode graph capture failed, timing eager launches: {e}", file=sys.stderr)
-            graph = None
-    run = graph.replay if graph is not None else step
-    for _ in range(args.warmup):
-        run()
-    torch.cuda.synchronize(dev)
-    if world > 1:
-        dist.barrier()
-    steps = max(3, min(args.steps, 10))
-    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    t0.record(stream)
-    for _ in range(steps):
-        run()
-    t1.record(stream)
-    torch.cuda.synchronize(dev)
-    ms = t0.elapsed_time(t1) / steps
-    if world > 1:
-        t = torch.tensor([ms], dtype=torch.float64, device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
-    del graph
-    # whole-job algorithmic bytes of one step: the full Linears (all ranks' shards)
-    full_p = []
-    off = 0
-    for _ in range(distinct):
-        row = []
-        for name, N, K in groups:
-            lo, hi = st._plug_range(off, off + N * K)
-            row.append(layer_bytes(N, K, hi - lo, M))
-            off += N * K
-        full_p.append(row)
-    lo, hi = st._plug_range(off, off + head_nk[0] * head_nk[1])
-    step_bytes = sum(sum(full_p[l % distinct]) for l in range(cfg["layers"])) + \
-        layer_bytes(head_nk[0], head_nk[1], hi - lo, M)
-    launches = cfg["layers"] * len(groups) + 1
-    res = {"tok_s": round(4 * M / (ms * 1e-3), 1), "ms_per_step": round(ms, 3),
-           "GB/s": round(step_bytes / (ms * 1e-3) / 1e9, 1), "bytes_per_step": int(step_bytes),
-           "launches_per_step": launches * (2 if use_peer else 1),
-           "gather": ("peer stores + one wait kernel per GEMV" if use_peer else
-                      "NCCL all-gather per GEMV") if world > 1 else "none",
-           "what": "4-model tokens/s of the packed Linears of a 3B-class decode step at batch 1 "
-                   "(36 layers x [qkv 2560x2048, o 2048x2048, gate_up 22016x2048, down 2048x11008] + lm_head "
-                   "151936x2048; 2 distinct layer weight sets alternate); attention, norms and activations "
-                   "between them are outside the path and not run",
-           "timing": "CUDA graph of one whole step" if run is not step else "eager launches"}
-    del calls, head_call, units, head, lins, st
-    if peers is not None:
-        peers.close()
     torch.cuda.empty_cache()
     return res
 

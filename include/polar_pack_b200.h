@@ -383,6 +383,41 @@ PP_API int pp_dual_gemm(const void* a, int64_t lda_m, int64_t lda_k,
                  int64_t M, int64_t N, int64_t K,
                  void* workspace, size_t workspace_bytes, void* stream);
 
+/* `.dualpack` file streams (reference polar_bitpack.py:26-29, 79-91,
+ * 160-172): 2-byte big-endian codes amp << phase_bits | phase per pair of
+ * weights, FP16 group maxima (groups of group_size pairs restarting at every
+ * chunk of chunk_size pairs), ascending uint32 plug positions with exact FP16
+ * amplitudes.
+ *
+ * Restore of pairs [start, start + n), the counterpart of unpack_dual_models
+ * (polar_bitpack.py:194-260), bit-exact: amp = float32(amp_norm[aq] * scale[g])
+ * (or float32(plug value) at plugged positions), w1 = float32(amp * cos_t[ph]),
+ * w2 = float32(amp * sin_t[ph]), all products in float64.  amp_norm / cos_t /
+ * sin_t: the float64 tables of the restore ([2^amp_bits], [2^phase_bits]).
+ * plug_idx / plug_vals: the plug entries of the range (positions relative to
+ * base_lo32, the low 32 bits of `start`, modulo 2^32).  Outputs: float32 w1/w2
+ * and/or their FP16 roundings h1/h2 (any may be NULL). */
+PP_API int pp_dual_unpack(const uint8_t* codes, const void* scales, int64_t chunk_size, int64_t group_size,
+                          int phase_bits, const double* amp_norm, const double* cos_t, const double* sin_t,
+                          const uint32_t* plug_idx, const void* plug_vals, int64_t n_plugs, uint32_t base_lo32,
+                          int64_t start, int64_t n, float* w1, float* w2, void* h1, void* h2, void* stream);
+
+/* One nn.Linear (out N, in K) of the two models straight from the file layout:
+ * pairs [offset + n K, offset + n K + K) are row n;
+ *   y_j[m][n] = fp16( sum_k x[m][k] * fp16(w_j[n][k]) )   (FP32 accumulation)
+ * with w_j decoded in FP32 from amp_norm (FP32 [2^amp_bits]) and cos_sin
+ * (FP32 (cos, sin) pairs [2^phase_bits]).  Plugged pairs must have their
+ * amplitude field cleared in `codes` (they decode to zero) and come as a
+ * per-row list: entries [row_ptr[n], row_ptr[n + 1]) of plug_col (int) and
+ * plug_w (FP16 (W1, W2) pairs).  codes 16-byte aligned and readable up to
+ * the next 16-byte boundary; chunk and group sizes multiples of 8;
+ * M <= 4; x (M, K) FP16 with row stride ldx; y1 / y2 (M, N) with row stride ldy. */
+PP_API int pp_dual_file_linear(const uint8_t* codes, const void* scales, int64_t chunk_size, int64_t group_size,
+                               int phase_bits, const float* amp_norm, const void* cos_sin, int64_t offset,
+                               const int* row_ptr, const int* plug_col, const void* plug_w, const void* x,
+                               int64_t ldx, int64_t M, int64_t N, int64_t K, void* y1, void* y2, int64_t ldy,
+                               void* stream);
+
 /* FP16 decode of a (K, N) int16 matrix into two FP16 matrices, bit-exact with
  * the reference kernel (polar_kernels.py:64-79). */
 PP_API int pp_dual_decode(const int16_t* packed, int64_t ldp_k, int64_t ldp_n, int64_t K, int64_t N,

@@ -102,6 +102,12 @@ _SIGNATURES = {
     "pp_dual_gemm": ([_c_void_p, _i64, _i64, _c_void_p, _i64, _i64, _c_void_p, _i64, _c_void_p,
                       _c_void_p, _c_void_p, _c_void_p, _c_void_p, _i64, _i64, _i64, _i64, _i64,
                       _c_void_p, _size_t, _c_void_p], _int),
+    "pp_dual_unpack": ([_c_void_p, _c_void_p, _i64, _i64, _int, _c_void_p, _c_void_p, _c_void_p, _c_void_p,
+                        _c_void_p, _i64, _u32, _i64, _i64, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p],
+                       _int),
+    "pp_dual_file_linear": ([_c_void_p, _c_void_p, _i64, _i64, _int, _c_void_p, _c_void_p, _i64, _c_void_p,
+                             _c_void_p, _c_void_p, _c_void_p, _i64, _i64, _i64, _i64, _c_void_p, _c_void_p, _i64,
+                             _c_void_p], _int),
     "pp_dual_decode": ([_c_void_p, _i64, _i64, _i64, _i64, _c_void_p, _i64, _c_void_p, _c_void_p,
                         _c_void_p, _c_void_p, _c_void_p, _i64, _i64, _c_void_p], _int),
 }

@@ -188,6 +188,56 @@ def linear_chunks(pack, offset: int, N: int, K: int, sms: int, x, out, bias=None
     return res
 
 
+class GatheredLinear:
+    """This rank's row shard of a packed Linear with per-model activations,
+    its outputs gathered into every rank's buffer (``peers`` buffer ``b``,
+    viewed ``[4][N]``) by the GEMV itself, then one bounded wait.
+
+    The shard runs in as many row chunks as the largest shard of any rank
+    needs (one fused launch each), so that every rank makes the same number
+    of launches into the buffer -- the wait compares launch counts.
+    ``bias`` / ``resid``: four ``[N]`` vectors (the shard's rows are used)."""
+
+    def __init__(self, pack, offset, N, K, sms, x, peers, b, world, rank, bias=None, resid=None):
+        import ctypes as C
+
+        from .parallel import row_shard
+        from .quadpack import linear_desc
+        n0, n1 = row_shard(N, world, rank)
+        nch = len(fused_rows(-(-N // world), K, sms))
+        step = -(-(-(-(n1 - n0) // nch)) // 8) * 8
+        self.peers, self.b, self.lib = peers, b, _lib.load()
+        self.outs = (C.c_void_p * 8)(*peers.out_ptrs(b))
+        self.flags = (C.c_void_p * 8)(*peers.flag_ptrs(b))
+        self.calls, self._keep = [], []
+        for c in range(nch):
+            r0 = n0 + c * step
+            r1 = min(n1, r0 + step)
+            if r1 <= r0:
+                raise ValueError("a rank's shard is too small for the common number of row chunks")
+            lin = pack.linear(offset + r0 * K, r1 - r0, K)
+            bb = [bias[k][r0:r1] for k in range(4)] if bias is not None else None
+            rr = [resid[k:k + 1, r0:r1] for k in range(4)] if resid is not None else None
+            d = (_lib.QuadLinearDesc * 1)(linear_desc(x, lin, None, True, bb, rr))
+            if not self.lib.pp_quad_linear_group_single_launch(1, d):
+                raise ValueError("a shard chunk does not fit one fused launch")
+            nb = _lib._size_t()
+            _lib.check(self.lib.pp_quad_linear_group_workspace_bytes(1, d, C.byref(nb)))
+            ws = torch.zeros(max(nb.value, 256), dtype=torch.uint8, device=x.device)
+            self.calls.append((d, (C.c_int64 * 1)(r0), ws))
+            self._keep.append((lin, bb, rr))
+        self.N = N
+
+    def __call__(self, s) -> None:
+        p = self.peers
+        for d, row0, ws in self.calls:
+            rc = self.lib.pp_quad_linear_group_gather(1, d, p.world, self.outs, self.N, row0, self.flags,
+                                                      p.epoch_ptr(self.b), ws.data_ptr(), ws.numel(), s)
+            if rc:
+                _lib.check(rc)
+        p.wait(self.b, s)
+
+
 class QuadDecoder:
     """One decoder step of the four models of a ``.quadpack`` on one GPU.
 
@@ -196,9 +246,17 @@ class QuadDecoder:
     and gate, up are consecutive with one input, so each pair or triple is
     one launch).  ``step(tokens)`` takes one token id per model and returns
     ``logits`` ``[4][vocab]`` (FP16); the position advances by one per step.
+
+    With ``world > 1`` (one process per GPU, ``torch.distributed`` set up) the
+    packed Linears are row-sharded: each rank streams its rows of every
+    Linear and stores its outputs into every rank's buffers over NVLink
+    (:class:`GatheredLinear`); norms, attention and SwiGLU run on every rank
+    over the gathered activations, so every rank holds the whole step's
+    state and the logits.
     """
 
-    def __init__(self, pack, cfg: DecoderConfig, extras: DecoderExtras, attn_splits: int = 64):
+    def __init__(self, pack, cfg: DecoderConfig, extras: DecoderExtras, attn_splits: int = 64, world: int = 1,
+                 rank: int = 0):
         self.pack, self.cfg, self.ex = pack, cfg, extras
         dev = self.device = pack.device
         self.lib = _lib.load()
@@ -208,19 +266,29 @@ class QuadDecoder:
         self.tokens = torch.zeros(4, dtype=torch.int32, device=dev)
         self.pos = torch.zeros(1, dtype=torch.int32, device=dev)
         self.status = torch.zeros(1, dtype=torch.int32, device=dev)
-        self.h = torch.zeros(4, H, **f16)
+        self.world, self.rank = world, rank
+        self.peers = None
+        if world > 1:
+            # the outputs of the packed Linears live in buffers every rank writes:
+            # 0 qkv, 1 the residual stream h, 2 gate_up, 3 logits
+            from .parallel import PeerBuffers
+            self.peers = PeerBuffers(4 * max(qkv_n, H, 2 * I, V), nbuf=4, device=dev)
+            view = lambda b, n: self.peers.view(b)[:4 * n].view(4, n)
+            self.qkv, self.h, self.gu, self.logits = view(0, qkv_n), view(1, H), view(2, 2 * I), view(3, V)
+        else:
+            self.h = torch.zeros(4, H, **f16)
+            self.qkv = torch.zeros(4, qkv_n, **f16)
+            self.gu = torch.zeros(4, 2 * I, **f16)
+            self.logits = torch.zeros(4, V, **f16)
         self.xn = torch.zeros(4, H, **f16)
-        self.qkv = torch.zeros(4, qkv_n, **f16)
         self.attn = torch.zeros(4, cfg.q_dim, **f16)
-        self.gu = torch.zeros(4, 2 * I, **f16)
         self.act = torch.zeros(4, I, **f16)
-        self.logits = torch.zeros(4, V, **f16)
         self.kc = [torch.zeros(4, cfg.max_pos, cfg.kv_heads, cfg.head_dim, **f16) for _ in range(cfg.layers)]
         self.vc = [torch.zeros(4, cfg.max_pos, cfg.kv_heads, cfg.head_dim, **f16) for _ in range(cfg.layers)]
         self.cos, self.sin = rope_tables(cfg, dev)
-        self.splits = attn_splits
+        self.splits = attn_splits   # attention: position ranges per (model, kv head)
         nb = _lib._size_t()
-        _lib.check(self.lib.pp_decode_attention_workspace_bytes(cfg.q_heads, cfg.kv_heads, attn_splits,
+        _lib.check(self.lib.pp_decode_attention_workspace_bytes(cfg.q_heads, cfg.kv_heads, self.splits,
                                                                 ctypes.byref(nb)))
         self.attn_ws = torch.zeros(nb.value, dtype=torch.uint8, device=dev)
         offs = {n: (o, s) for n, o, s in layer_offsets(qwen2_layer_map(cfg))}
@@ -233,13 +301,24 @@ class QuadDecoder:
             og, _ = offs[p + "mlp.gate_proj"]
             od, _ = offs[p + "mlp.down_proj"]
             bias = [extras.qkv_bias[l, k] for k in range(4)] if extras.qkv_bias is not None else None
-            self.groups.append((
-                linear_chunks(pack, oq, qkv_n, H, sms, self.xn, self.qkv, bias=bias),
-                linear_chunks(pack, oo, H, cfg.q_dim, sms, self.attn, self.h, resid=self.h),
-                linear_chunks(pack, og, 2 * I, H, sms, self.xn, self.gu),
-                linear_chunks(pack, od, H, I, sms, self.act, self.h, resid=self.h)))
+            if world > 1:
+                pr = self.peers
+                self.groups.append((
+                    [GatheredLinear(pack, oq, qkv_n, H, sms, self.xn, pr, 0, world, rank, bias=bias)],
+                    [GatheredLinear(pack, oo, H, cfg.q_dim, sms, self.attn, pr, 1, world, rank, resid=self.h)],
+                    [GatheredLinear(pack, og, 2 * I, H, sms, self.xn, pr, 2, world, rank)],
+                    [GatheredLinear(pack, od, H, I, sms, self.act, pr, 1, world, rank, resid=self.h)]))
+            else:
+                self.groups.append((
+                    linear_chunks(pack, oq, qkv_n, H, sms, self.xn, self.qkv, bias=bias),
+                    linear_chunks(pack, oo, H, cfg.q_dim, sms, self.attn, self.h, resid=self.h),
+                    linear_chunks(pack, og, 2 * I, H, sms, self.xn, self.gu),
+                    linear_chunks(pack, od, H, I, sms, self.act, self.h, resid=self.h)))
         ol, _ = offs["lm_head"]
-        self.head = linear_chunks(pack, ol, V, H, sms, self.xn, self.logits)
+        if world > 1:
+            self.head = [GatheredLinear(pack, ol, V, H, sms, self.xn, self.peers, 3, world, rank)]
+        else:
+            self.head = linear_chunks(pack, ol, V, H, sms, self.xn, self.logits)
         P4 = _lib._PTR4
         self._emb = P4(*[extras.embed[k].data_ptr() for k in range(4)])
         self._in_norm = [P4(*[extras.in_norm[l, k].data_ptr() for k in range(4)]) for l in range(cfg.layers)]
@@ -251,7 +330,15 @@ class QuadDecoder:
         self.graph = None
 
     def launches_per_step(self) -> int:
-        return 2 + self.cfg.layers * 4 + sum(len(c) for g in self.groups for c in g) + len(self.head)
+        n = lambda g: len(g.calls) + 1 if isinstance(g, GatheredLinear) else 1   # + the gather wait
+        return 2 + self.cfg.layers * 4 + sum(n(g) for grp in self.groups for c in grp for g in c) + \
+            sum(n(g) for g in self.head)
+
+    def close(self) -> None:
+        """Unmap the peers' buffers (collective over the process group)."""
+        if self.peers is not None:
+            self.peers.close()
+            self.peers = None
 
     def _run(self, s) -> None:
         """Enqueue one step on stream handle s (tokens and pos already set)."""

@@ -441,7 +441,9 @@ def linear_desc(x: torch.Tensor, layer: QuadLinearSlice, out, per_model_x: bool 
     for k in range(4):
         d.scales[k] = float(layer.pack.scales[k])
         d.out[k] = out[k].data_ptr() if out is not None else None
-    d.ldo_m, d.ldo_n = (out[0].stride(0), out[0].stride(1)) if out is not None else (0, 0)
+    # output strides (gathered members write no out[], but a residual is read with these strides)
+    src = out if out is not None else resid
+    d.ldo_m, d.ldo_n = (src[0].stride(0), src[0].stride(1)) if src is not None else (0, 1)
     d.M, d.N, d.K = (1 if per_model_x else x.shape[0]), layer.N, layer.K
     return d
 

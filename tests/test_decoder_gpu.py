@@ -149,7 +149,7 @@ def test_decoder_step_matches_float32_reference(cuda, packed):
     cfg, buf, restored = packed
     pk = QuadPackDevice(QuadPackFile(buf), cuda)
     ex = DecoderExtras.random(cfg, cuda, seed=1)
-    dec = QuadDecoder(pk, cfg, ex, attn_splits=4)
+    dec = QuadDecoder(pk, cfg, ex)
     Ws = [{n: t.to(cuda) for n, t in _linear_weights(cfg, restored, k).items()} for k in range(4)]
     exs = [dict(embed=ex.embed[k].float(), in_norm=ex.in_norm[:, k].float(), post_norm=ex.post_norm[:, k].float(),
                 final=ex.final_norm[k].float(), bias=ex.qkv_bias[:, k].float()) for k in range(4)]
@@ -173,3 +173,61 @@ def test_decoder_step_matches_float32_reference(cuda, packed):
         again = dec.step(toks).float()
         torch.cuda.synchronize()
         assert torch.equal(again, got)
+
+
+def _dec_worker(rank, world, port, buf, q):
+    try:
+        import os
+        import sys
+        from datetime import timedelta
+
+        import torch.distributed as dist
+        sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+        os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+        dev = torch.device("cuda", rank)
+        torch.cuda.set_device(dev)
+        dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev, timeout=timedelta(seconds=60))
+        from polar_pack_b200.decoder import DecoderExtras, QuadDecoder
+        from polar_pack_b200.quadpack import QuadPackDevice, QuadPackFile
+        cfg = _cfg()
+        pk = QuadPackDevice(QuadPackFile(buf), dev)
+        ex = DecoderExtras.random(cfg, dev, seed=1)
+        dist_dec = QuadDecoder(pk, cfg, ex, world=world, rank=rank)
+        one = QuadDecoder(pk, cfg, ex)
+        rng = np.random.default_rng(3)
+        worst = 0.0
+        for _ in range(4):
+            toks = rng.integers(0, cfg.vocab, 4)
+            a = dist_dec.step(toks).float().clone()
+            b = one.step(toks).float()
+            torch.cuda.synchronize(dev)
+            worst = max(worst, float((a - b).abs().max() / b.abs().max()))
+        ok = worst <= 1e-2 and int(dist_dec.peers.status.item()) == 0
+        torch.cuda.synchronize(dev)
+        dist_dec.close()
+        dist.destroy_process_group()
+        q.put((rank, bool(ok), f"{worst:.3g}"))
+    except Exception as e:
+        q.put((rank, False, repr(e)))
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_decoder_two_ranks_matches_one_gpu(packed):
+    """Row-sharded decoder on two GPUs (GEMVs gather their rows into both
+    ranks' buffers over NVLink) against the one-GPU decoder on the same pack."""
+    import socket
+
+    import torch.multiprocessing as mp
+    cfg, buf, _ = packed
+    with socket.socket() as s_:
+        s_.bind(("127.0.0.1", 0))
+        port = s_.getsockname()[1]
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_dec_worker, args=(r, 2, port, buf, q)) for r in range(2)]
+    for p_ in procs:
+        p_.start()
+    res = [q.get(timeout=300) for _ in procs]
+    for p_ in procs:
+        p_.join(timeout=60)
+    assert all(ok for _, ok, _ in res), res

@@ -126,3 +126,24 @@ def test_tail_split_rows():
     assert (s.coded, s.straddle, s.first_tail, s.tail_start) == (0, False, 0, 8)
     s = tail_split(0, 10, 8, n, tails)              # wholly coded
     assert (s.coded, s.straddle) == (10, False) and all(s.present)
+
+
+def test_dualpack_reader(dualpack_golden):
+    """Product reader of .dualpack v2 against the oracle's section parser
+    (polar_bitpack.py:26-29, 194-215)."""
+    from polar_pack_b200.dualpack import DualPackFile, dual_tables
+    buf = dualpack_golden["stream"].tobytes()
+    f = DualPackFile(buf)
+    hdr, codes, scales, pidx, pval = of.dual_sections(buf)
+    h = f.header
+    assert (h.n_pairs, h.n1, h.n2, h.amp_bits, h.phase_bits, h.group_size, h.chunk_size, h.plug_n) == \
+        (hdr["n_pairs"], hdr["n1"], hdr["n2"], hdr["amp_bits"], hdr["phase_bits"], hdr["group_size"],
+         hdr["chunk_size"], hdr["plug_n"])
+    be = (f.codes[0::2].astype(np.uint32) << 8) | f.codes[1::2]
+    np.testing.assert_array_equal(be, codes)
+    np.testing.assert_array_equal(f.scales.view(np.uint16), scales.view(np.uint16))
+    np.testing.assert_array_equal(f.plug_idx, pidx)
+    amp, c, s = dual_tables(h)
+    assert amp[0] == 0.0 and amp.size == 2 ** h.amp_bits and c.size == 2 ** h.phase_bits
+    with pytest.raises(ValueError):
+        DualPackFile(buf[:70])
