@@ -333,6 +333,11 @@ PP_API int pp_f16_linear(const void* x, int64_t ldx_m, int64_t ldx_model, int64_
  * captured step can be replayed for every token.  A status word (device
  * int, may be NULL) receives 4 for a token id outside the vocabulary (its
  * row is zeroed) and 5 for a position outside the cache (nothing written).
+ * RMSNorm, attention and SwiGLU can first wait for a gathered input buffer
+ * (wait_flags != NULL: this rank's flag array of the buffer, wait_world
+ * ranks, wait_epoch this rank's launches into it; the same bounded wait as
+ * pp_gather_wait, run by every block before it reads), which saves the
+ * separate pp_gather_wait launch after a gathered Linear.
  */
 /* h[m][:] = tables[m][tokens[m]][:] (FP16 rows of H). */
 PP_API int pp_embed_rows(const int* tokens, const void* const tables[4], int64_t vocab, int64_t H, void* h,
@@ -340,7 +345,8 @@ PP_API int pp_embed_rows(const int* tokens, const void* const tables[4], int64_t
 
 /* y[m] = fp16(w[m] * fp16(x[m] * rsqrt(mean(x[m]^2) + eps))), FP32 statistics. */
 PP_API int pp_rmsnorm_rows(const void* x, int64_t ldx, const void* const w[4], int64_t H, float eps, void* y,
-                           int64_t ldy, void* stream);
+                           int64_t ldy, const uint32_t* wait_flags, int wait_world, const uint32_t* wait_epoch,
+                           int* wait_status, void* stream);
 
 /* Grouped-query decode attention of one token per model, with the token's
  * rotary embedding and KV-cache append fused in.  Row m of qkv holds the
@@ -357,10 +363,13 @@ PP_API int pp_decode_attention_workspace_bytes(int64_t nq, int64_t nkv, int64_t 
 PP_API int pp_decode_attention(void* qkv, int64_t ldq, int64_t nq, int64_t nkv, int64_t hd, const void* cos_t,
                                const void* sin_t, void* const k_cache[4], void* const v_cache[4], int64_t max_pos,
                                const int* pos, float scale, void* out, int64_t ldo, int64_t splits,
-                               void* workspace, size_t workspace_bytes, int* status, void* stream);
+                               void* workspace, size_t workspace_bytes, int* status, const uint32_t* wait_flags,
+                               int wait_world, const uint32_t* wait_epoch, int* wait_status, void* stream);
 
 /* y[m][i] = fp16(fp16(silu(gate_up[m][i])) * gate_up[m][I + i]). */
-PP_API int pp_swiglu_rows(const void* gate_up, int64_t ldg, int64_t I, void* y, int64_t ldy, void* stream);
+PP_API int pp_swiglu_rows(const void* gate_up, int64_t ldg, int64_t I, void* y, int64_t ldy,
+                          const uint32_t* wait_flags, int wait_world, const uint32_t* wait_epoch, int* wait_status,
+                          void* stream);
 
 /* ------------------------------------------------------------------ dual --
  * Kernel-layout fused dequant GEMM, the drop-in for `polar_dual_bitpacked`

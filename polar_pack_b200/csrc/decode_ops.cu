@@ -10,7 +10,10 @@
 //   attention softmax(q k^T * scale) v with FP32 scores, sums and weights
 //   SwiGLU    y = fp16(fp16(silu(g)) * u)                       (silu in FP32)
 // The position of the token is read from device memory, so a captured CUDA
-// graph of the step can be replayed for every position.
+// graph of the step can be replayed for every position.  Each kernel lets
+// the next launch of its stream start at once (griddepcontrol): a packed
+// Linear launched with launch overlap then streams its tables and first
+// codes while this kernel runs, and waits for it before reading activations.
 #include <cuda_fp16.h>
 #include <math.h>
 
@@ -22,6 +25,41 @@ namespace {
 
 constexpr int kModels = 4;
 
+// An optional wait for a gathered buffer (the row-sharded Linears of several
+// GPUs store their outputs into every rank's buffer and publish an epoch per
+// launch, pp_peer.h): before reading the buffer, thread 0 of every block
+// polls until each rank's flag word has reached this rank's epoch count, at
+// most about a second; a rank that never publishes sets *status to 3 and the
+// block goes on.  flags == NULL: no wait.
+struct GatherWait {
+  const uint32_t* flags;  // this rank's flag array of the buffer, one word per rank
+  const uint32_t* epoch;  // this rank's launches into the buffer
+  int* status;
+  int world;
+};
+
+__device__ __forceinline__ void gather_wait_block(const GatherWait& w) {
+  if (w.flags == nullptr) return;
+  if (threadIdx.x == 0) {
+    const uint32_t e = *w.epoch;
+    for (int q = 0; q < w.world; ++q) {
+      int i = 0;
+      for (; i < (1 << 24); ++i) {
+        uint32_t v;
+        asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(w.flags + q) : "memory");
+        if ((int32_t)(v - e) >= 0) break;
+        __nanosleep(64);
+      }
+      if (i == (1 << 24) && w.status) atomicExch(w.status, 3);
+    }
+  }
+  __syncthreads();
+}
+
+inline GatherWait make_wait(const uint32_t* flags, int world, const uint32_t* epoch, int* status) {
+  return GatherWait{flags, epoch, status, world};
+}
+
 struct EmbedParams {
   const int* tokens;          // [4] token id per model (device)
   const __half* table[kModels];  // [vocab][H] per model
@@ -32,6 +70,7 @@ struct EmbedParams {
 };
 
 __global__ void embed_kernel(const EmbedParams p) {
+  pdl_launch_dependents();  // the next packed Linear may start its weight-only prologue
   const int m = blockIdx.x;
   const int tok = p.tokens[m];
   const bool ok = tok >= 0 && tok < p.vocab;
@@ -41,6 +80,7 @@ __global__ void embed_kernel(const EmbedParams p) {
 }
 
 struct NormParams {
+  GatherWait wait;
   const __half* x;
   int64_t ldx;
   const __half* w[kModels];
@@ -64,6 +104,8 @@ __device__ __forceinline__ float block_sum(float v, float* red) {
 
 __global__ void rmsnorm_kernel(const NormParams p) {
   __shared__ float red[32];
+  pdl_launch_dependents();  // the next packed Linear may start its weight-only prologue
+  gather_wait_block(p.wait);
   const int m = blockIdx.x;
   const __half* x = p.x + m * p.ldx;
   float ss = 0.f;
@@ -81,8 +123,10 @@ __global__ void rmsnorm_kernel(const NormParams p) {
 constexpr int kHeadDim = 128;  // 4 dimensions per lane
 constexpr int kPartStride = kHeadDim + 4;  // floats per partial: acc, max, sum, 2 unused (16-byte rows)
 constexpr int kUnroll = 4;                 // cache positions whose loads are in flight together
+constexpr int kCombineBatch = 16;          // splits whose partials the combine loads together
 
 struct AttnParams {
+  GatherWait wait;
   const __half* qkv;      // [4][ldq]: the token's nq query, nkv key and nkv value heads (not rotated)
   int64_t ldq;
   const __half* cos_t;    // [max_pos][hd] FP16 rotation tables (both halves)
@@ -127,6 +171,8 @@ __device__ __forceinline__ void rope4(float (&v)[4], const __half* cs, const __h
 // (deterministic).
 __global__ void decode_attention_kernel(const AttnParams p) {
   __shared__ int last;
+  pdl_launch_dependents();  // the next packed Linear may start its weight-only prologue
+  gather_wait_block(p.wait);
   const int split = blockIdx.x, kvh = blockIdx.y, m = blockIdx.z;
   const int group = p.nq / p.nkv;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -209,21 +255,40 @@ __global__ void decode_attention_kernel(const AttnParams p) {
   __syncthreads();
   if (!last) return;
   __threadfence();
+  // combine: the maxima and sums with the lanes over the splits, then each
+  // lane's four dimensions over the splits, kCombineBatch splits' loads at a
+  // time (fixed order: deterministic)
   const float* base = p.part + ((int64_t)m * p.nq + qh) * p.splits * kPartStride;
   float M = -INFINITY;
-  for (int sp = 0; sp < p.splits; ++sp) M = fmaxf(M, __ldcg(base + sp * kPartStride + kHeadDim));
-  float L = 0.f, o0 = 0.f, o1 = 0.f, o2 = 0.f, o3 = 0.f;
-  for (int sp = 0; sp < p.splits; ++sp) {
-    const float* b = base + sp * kPartStride;
-    const float ms = __ldcg(b + kHeadDim);
-    if (ms == -INFINITY) continue;  // an empty split
-    const float w = expf(ms - M);
-    const float4 a = __ldcg(reinterpret_cast<const float4*>(b + 4 * lane));
-    L += w * __ldcg(b + kHeadDim + 1);
-    o0 += w * a.x;
-    o1 += w * a.y;
-    o2 += w * a.z;
-    o3 += w * a.w;
+  for (int sp = lane; sp < p.splits; sp += 32) M = fmaxf(M, __ldcg(base + sp * kPartStride + kHeadDim));
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+  float L = 0.f;
+  for (int sp = lane; sp < p.splits; sp += 32) {
+    const float ms = __ldcg(base + sp * kPartStride + kHeadDim);
+    if (ms != -INFINITY) L += expf(ms - M) * __ldcg(base + sp * kPartStride + kHeadDim + 1);
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) L += __shfl_xor_sync(0xffffffffu, L, o);
+  float o0 = 0.f, o1 = 0.f, o2 = 0.f, o3 = 0.f;
+  for (int sp0 = 0; sp0 < p.splits; sp0 += kCombineBatch) {
+    float w[kCombineBatch];
+    float4 a[kCombineBatch];
+#pragma unroll
+    for (int u = 0; u < kCombineBatch; ++u) {
+      const int sp = sp0 + u < p.splits ? sp0 + u : p.splits - 1;
+      const float* b = base + sp * kPartStride;
+      const float ms = __ldcg(b + kHeadDim);
+      w[u] = (sp0 + u < p.splits && ms != -INFINITY) ? expf(ms - M) : 0.f;  // empty splits weigh nothing
+      a[u] = __ldcg(reinterpret_cast<const float4*>(b + 4 * lane));
+    }
+#pragma unroll
+    for (int u = 0; u < kCombineBatch; ++u) {
+      o0 += w[u] * a[u].x;
+      o1 += w[u] * a[u].y;
+      o2 += w[u] * a[u].z;
+      o3 += w[u] * a[u].w;
+    }
   }
   const float inv = 1.f / L;
   __half2* o = reinterpret_cast<__half2*>(p.out + m * p.ldo + qh * kHeadDim + 4 * lane);
@@ -234,6 +299,7 @@ __global__ void decode_attention_kernel(const AttnParams p) {
 }
 
 struct SwigluParams {
+  GatherWait wait;
   const __half* gu;  // [4][ldg]: gate (I values) then up (I values)
   int64_t ldg;
   __half* y;         // [4][ldy]
@@ -242,6 +308,8 @@ struct SwigluParams {
 };
 
 __global__ void swiglu_kernel(const SwigluParams p) {
+  pdl_launch_dependents();  // the next packed Linear may start its weight-only prologue
+  gather_wait_block(p.wait);
   const int m = blockIdx.y;
   for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < p.I; i += gridDim.x * blockDim.x) {
     const float g = __half2float(p.gu[m * p.ldg + i]);
@@ -280,7 +348,12 @@ int pp_embed_rows(const int* tokens, const void* const tables[4], int64_t vocab,
 }
 
 int pp_rmsnorm_rows(const void* x, int64_t ldx, const void* const w[4], int64_t H, float eps, void* y, int64_t ldy,
+                    const uint32_t* wait_flags, int wait_world, const uint32_t* wait_epoch, int* wait_status,
                     void* stream) {
+  if (wait_flags && (!wait_epoch || wait_world < 1 || wait_world > 8)) {
+    pp::set_error("pp_rmsnorm_rows: a wait needs its epoch and 1..8 ranks");
+    return PP_ERR_INVALID;
+  }
   if (!x || !w || !y || H <= 0 || H > INT32_MAX || ldx < H || ldy < H) {
     pp::set_error("pp_rmsnorm_rows: invalid arguments");
     return PP_ERR_INVALID;
@@ -299,6 +372,7 @@ int pp_rmsnorm_rows(const void* x, int64_t ldx, const void* const w[4], int64_t 
   p.ldy = ldy;
   p.H = (int)H;
   p.eps = eps;
+  p.wait = pp::make_wait(wait_flags, wait_world, wait_epoch, wait_status);
   pp::rmsnorm_kernel<<<4, 512, 0, reinterpret_cast<cudaStream_t>(stream)>>>(p);
   return pp::check_launch("rmsnorm_kernel");
 }
@@ -316,7 +390,12 @@ int pp_decode_attention_workspace_bytes(int64_t nq, int64_t nkv, int64_t splits,
 int pp_decode_attention(void* qkv, int64_t ldq, int64_t nq, int64_t nkv, int64_t hd, const void* cos_t,
                         const void* sin_t, void* const k_cache[4], void* const v_cache[4], int64_t max_pos,
                         const int* pos, float scale, void* out, int64_t ldo, int64_t splits, void* workspace,
-                        size_t workspace_bytes, int* status, void* stream) {
+                        size_t workspace_bytes, int* status, const uint32_t* wait_flags, int wait_world,
+                        const uint32_t* wait_epoch, int* wait_status, void* stream) {
+  if (wait_flags && (!wait_epoch || wait_world < 1 || wait_world > 8)) {
+    pp::set_error("pp_decode_attention: a wait needs its epoch and 1..8 ranks");
+    return PP_ERR_INVALID;
+  }
   if (!qkv || !cos_t || !sin_t || !k_cache || !v_cache || !pos || !out || hd != pp::kHeadDim || nq <= 0 ||
       nkv <= 0 || nq % nkv || nq / nkv > 32 || splits <= 0 || splits > 65535 || max_pos <= 0 ||
       max_pos > INT32_MAX || !pp::aligned(qkv, 8) || ldq % 4 || ldq < (nq + 2 * nkv) * hd || !pp::aligned(out, 4) ||
@@ -357,17 +436,24 @@ int pp_decode_attention(void* qkv, int64_t ldq, int64_t nq, int64_t nkv, int64_t
   p.splits = (int)splits;
   p.max_pos = (int)max_pos;
   p.scale = scale;
+  p.wait = pp::make_wait(wait_flags, wait_world, wait_epoch, wait_status);
   pp::decode_attention_kernel<<<dim3((unsigned)splits, (unsigned)nkv, 4), (unsigned)(32 * (nq / nkv)), 0,
                                 reinterpret_cast<cudaStream_t>(stream)>>>(p);
   return pp::check_launch("decode_attention_kernel");
 }
 
-int pp_swiglu_rows(const void* gate_up, int64_t ldg, int64_t I, void* y, int64_t ldy, void* stream) {
+int pp_swiglu_rows(const void* gate_up, int64_t ldg, int64_t I, void* y, int64_t ldy, const uint32_t* wait_flags,
+                   int wait_world, const uint32_t* wait_epoch, int* wait_status, void* stream) {
+  if (wait_flags && (!wait_epoch || wait_world < 1 || wait_world > 8)) {
+    pp::set_error("pp_swiglu_rows: a wait needs its epoch and 1..8 ranks");
+    return PP_ERR_INVALID;
+  }
   if (!gate_up || !y || I <= 0 || I > INT32_MAX || ldg < 2 * I || ldy < I) {
     pp::set_error("pp_swiglu_rows: invalid arguments");
     return PP_ERR_INVALID;
   }
-  pp::SwigluParams p{reinterpret_cast<const __half*>(gate_up), ldg, reinterpret_cast<__half*>(y), ldy, (int)I};
+  pp::SwigluParams p{pp::make_wait(wait_flags, wait_world, wait_epoch, wait_status),
+                     reinterpret_cast<const __half*>(gate_up), ldg, reinterpret_cast<__half*>(y), ldy, (int)I};
   const unsigned gx = (unsigned)((I + 255) / 256 < 64 ? (I + 255) / 256 : 64);
   pp::swiglu_kernel<<<dim3(gx, 4), 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(p);
   return pp::check_launch("swiglu_kernel");

@@ -229,13 +229,14 @@ class GatheredLinear:
         self.N = N
 
     def __call__(self, s) -> None:
+        """The shard's launches; the reader of the buffer waits for every rank
+        (``wait_args``), either inside its own kernel or with ``peers.wait``."""
         p = self.peers
         for d, row0, ws in self.calls:
             rc = self.lib.pp_quad_linear_group_gather(1, d, p.world, self.outs, self.N, row0, self.flags,
                                                       p.epoch_ptr(self.b), ws.data_ptr(), ws.numel(), s)
             if rc:
                 _lib.check(rc)
-        p.wait(self.b, s)
 
 
 class QuadDecoder:
@@ -255,7 +256,7 @@ class QuadDecoder:
     state and the logits.
     """
 
-    def __init__(self, pack, cfg: DecoderConfig, extras: DecoderExtras, attn_splits: int = 64, world: int = 1,
+    def __init__(self, pack, cfg: DecoderConfig, extras: DecoderExtras, attn_splits: int = 32, world: int = 1,
                  rank: int = 0):
         self.pack, self.cfg, self.ex = pack, cfg, extras
         dev = self.device = pack.device
@@ -330,9 +331,9 @@ class QuadDecoder:
         self.graph = None
 
     def launches_per_step(self) -> int:
-        n = lambda g: len(g.calls) + 1 if isinstance(g, GatheredLinear) else 1   # + the gather wait
+        n = lambda g: len(g.calls) if isinstance(g, GatheredLinear) else 1
         return 2 + self.cfg.layers * 4 + sum(n(g) for grp in self.groups for c in grp for g in c) + \
-            sum(n(g) for g in self.head)
+            sum(n(g) for g in self.head) + (1 if self.peers is not None else 0)   # + the logits wait
 
     def close(self) -> None:
         """Unmap the peers' buffers (collective over the process group)."""
@@ -340,29 +341,44 @@ class QuadDecoder:
             self.peers.close()
             self.peers = None
 
+    def _wait(self, b: int):
+        """Arguments of the in-kernel wait for gathered buffer b (none on one GPU)."""
+        if self.peers is None:
+            return (None, 0, None, None)
+        p = self.peers
+        return (p.local_flags(b), p.world, p.epoch_ptr(b), p.status.data_ptr())
+
     def _run(self, s) -> None:
-        """Enqueue one step on stream handle s (tokens and pos already set)."""
+        """Enqueue one step on stream handle s (tokens and pos already set).
+        With several GPUs, the kernel that reads a gathered buffer (qkv: 0,
+        h: 1, gate_up: 2) first waits for every rank's launches into it; the
+        logits (3) get a wait launch of their own at the end of the step."""
         L, cfg, c = self.lib, self.cfg, _lib.check
         H, I = cfg.hidden, cfg.inter
         c(L.pp_embed_rows(self.tokens.data_ptr(), self._emb, cfg.vocab, H, self.h.data_ptr(), H,
                           self.status.data_ptr(), s))
         run = lambda chunks: [g(s) for g in chunks]
+        none = (None, 0, None, None)
         for l, (g_qkv, g_o, g_gu, g_d) in enumerate(self.groups):
-            c(L.pp_rmsnorm_rows(self.h.data_ptr(), H, self._in_norm[l], H, cfg.rms_eps, self.xn.data_ptr(), H, s))
+            c(L.pp_rmsnorm_rows(self.h.data_ptr(), H, self._in_norm[l], H, cfg.rms_eps, self.xn.data_ptr(), H,
+                                *(self._wait(1) if l > 0 else none), s))
             run(g_qkv)
             c(L.pp_decode_attention(self.qkv.data_ptr(), self.qkv.stride(0), cfg.q_heads, cfg.kv_heads,
                                     cfg.head_dim, self.cos.data_ptr(), self.sin.data_ptr(), self._kc[l],
                                     self._vc[l], cfg.max_pos, self.pos.data_ptr(), self.scale, self.attn.data_ptr(),
                                     self.attn.stride(0), self.splits, self.attn_ws.data_ptr(),
-                                    self.attn_ws.numel(), self.status.data_ptr(), s))
+                                    self.attn_ws.numel(), self.status.data_ptr(), *self._wait(0), s))
             run(g_o)
             c(L.pp_rmsnorm_rows(self.h.data_ptr(), H, self._post_norm[l], H, cfg.rms_eps, self.xn.data_ptr(), H,
-                                s))
+                                *self._wait(1), s))
             run(g_gu)
-            c(L.pp_swiglu_rows(self.gu.data_ptr(), self.gu.stride(0), I, self.act.data_ptr(), I, s))
+            c(L.pp_swiglu_rows(self.gu.data_ptr(), self.gu.stride(0), I, self.act.data_ptr(), I, *self._wait(2), s))
             run(g_d)
-        c(L.pp_rmsnorm_rows(self.h.data_ptr(), H, self._final, H, cfg.rms_eps, self.xn.data_ptr(), H, s))
+        c(L.pp_rmsnorm_rows(self.h.data_ptr(), H, self._final, H, cfg.rms_eps, self.xn.data_ptr(), H,
+                            *self._wait(1), s))
         run(self.head)
+        if self.peers is not None:
+            self.peers.wait(3, s)
 
     def _advance(self) -> None:
         self.pos.add_(1)
