@@ -355,8 +355,14 @@ PP_API int pp_rmsnorm_rows(const void* x, int64_t ldx, const void* const w[4], i
  * halves).  The token's key is rotated and stored with its value into
  * k_cache[m] / v_cache[m] ([max_pos][nkv][hd]) at *pos, then
  *   out[m][h] = softmax(rope(q[m][h]) k^T * scale) v   over positions 0..*pos
- * with kv head h / (nq / nkv).  Split over `splits` position ranges whose
- * partial results the last arriving block combines in order (deterministic).
+ * with kv head h / (nq / nkv), at most 16 query heads per kv head.  Scores
+ * and the softmax run in FP32 on the tensor cores (all query heads of a kv
+ * head share each 32-position tile of keys and values); the softmax weights
+ * are rounded to FP16 for the value product.  Split over `splits` (1..4096)
+ * position ranges of eight 32-position warp tiles each; the last arriving
+ * block combines the partial results in order (deterministic).  Caches
+ * 16-byte aligned (rows arrive by bulk copies); status must not be NULL
+ * here (a tile copy that never lands sets it to 1).
  * Workspace: pp_decode_attention_workspace_bytes, zero-filled once. */
 PP_API int pp_decode_attention_workspace_bytes(int64_t nq, int64_t nkv, int64_t splits, size_t* bytes);
 

@@ -256,7 +256,7 @@ class QuadDecoder:
     state and the logits.
     """
 
-    def __init__(self, pack, cfg: DecoderConfig, extras: DecoderExtras, attn_splits: int = 32, world: int = 1,
+    def __init__(self, pack, cfg: DecoderConfig, extras: DecoderExtras, attn_splits: int | None = None, world: int = 1,
                  rank: int = 0):
         self.pack, self.cfg, self.ex = pack, cfg, extras
         dev = self.device = pack.device
@@ -287,7 +287,9 @@ class QuadDecoder:
         self.kc = [torch.zeros(4, cfg.max_pos, cfg.kv_heads, cfg.head_dim, **f16) for _ in range(cfg.layers)]
         self.vc = [torch.zeros(4, cfg.max_pos, cfg.kv_heads, cfg.head_dim, **f16) for _ in range(cfg.layers)]
         self.cos, self.sin = rope_tables(cfg, dev)
-        self.splits = attn_splits   # attention: position ranges per (model, kv head)
+        # attention: position ranges per (model, kv head); by default one per
+        # 128 positions of the cache (four 32-position warp tiles at full length)
+        self.splits = attn_splits if attn_splits else max(1, min(64, -(-cfg.max_pos // 128)))
         nb = _lib._size_t()
         _lib.check(self.lib.pp_decode_attention_workspace_bytes(cfg.q_heads, cfg.kv_heads, self.splits,
                                                                 ctypes.byref(nb)))
