@@ -202,11 +202,15 @@ def require_cuda(*tensors) -> torch.device:
 
 
 def set_launch_overlap(enable: bool) -> bool:
-    """Programmatic dependent launch for the quad GEMV kernels (process-wide).
+    """Programmatic dependent launch for the quad GEMV kernels and the
+    decoder-step ops (process-wide).
 
     While on, the codes, tables and plug arrays of a call must not be
     written by the kernel launched immediately before it on the same
-    stream.  Returns the previous setting.
+    stream; nor the norm weights of pp_rmsnorm_rows, nor the position and
+    the cache rows before it of pp_decode_attention, by any kernel still
+    running before them (a step sets its position before its first launch).
+    Returns the previous setting.
     """
     return bool(load().pp_set_launch_overlap(1 if enable else 0))
 

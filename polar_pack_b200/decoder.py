@@ -201,10 +201,10 @@ class GatheredLinear:
     def __init__(self, pack, offset, N, K, sms, x, peers, b, world, rank, bias=None, resid=None):
         import ctypes as C
 
-        from .parallel import row_shard
+        from .parallel import row_shard, shard_width
         from .quadpack import linear_desc
         n0, n1 = row_shard(N, world, rank)
-        nch = len(fused_rows(-(-N // world), K, sms))
+        nch = len(fused_rows(shard_width(N, world), K, sms))
         step = -(-(-(-(n1 - n0) // nch)) // 8) * 8
         self.peers, self.b, self.lib = peers, b, _lib.load()
         self.outs = (C.c_void_p * 8)(*peers.out_ptrs(b))
@@ -288,8 +288,9 @@ class QuadDecoder:
         self.vc = [torch.zeros(4, cfg.max_pos, cfg.kv_heads, cfg.head_dim, **f16) for _ in range(cfg.layers)]
         self.cos, self.sin = rope_tables(cfg, dev)
         # attention: position ranges per (model, kv head); by default one per
-        # 128 positions of the cache (four 32-position warp tiles at full length)
-        self.splits = attn_splits if attn_splits else max(1, min(64, -(-cfg.max_pos // 128)))
+        # 256 positions of the cache (a CTA's eight 32-position warp tiles at
+        # full length), which keeps the CTAs of one launch within one wave
+        self.splits = attn_splits if attn_splits else max(1, min(64, -(-cfg.max_pos // 256)))
         nb = _lib._size_t()
         _lib.check(self.lib.pp_decode_attention_workspace_bytes(cfg.q_heads, cfg.kv_heads, self.splits,
                                                                 ctypes.byref(nb)))

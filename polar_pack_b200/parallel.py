@@ -18,16 +18,26 @@ import torch
 import torch.distributed as dist
 
 
+SHARD_ALIGN = 8   # rows: one GEMV output tile
+
+
+def _shard_bound(N: int, world: int, r: int) -> int:
+    return N if r >= world else (N * r // world) // SHARD_ALIGN * SHARD_ALIGN
+
+
 def row_shard(N: int, world: int, rank: int) -> tuple[int, int]:
-    """Rows ``[n0, n1)`` of rank ``rank``: contiguous, sizes differ by at most one."""
+    """Rows ``[n0, n1)`` of rank ``rank``: contiguous, the inner boundaries on
+    multiples of 8 rows (sizes differ by less than 8 + 1), so that a rank's
+    8-row output tiles are whole tiles of the unsharded Linear and reach the
+    gathered buffers as 16-byte stores."""
     if world <= 0 or not 0 <= rank < world:
         raise ValueError(f"bad rank {rank} of {world}")
-    return N * rank // world, N * (rank + 1) // world
+    return _shard_bound(N, world, rank), _shard_bound(N, world, rank + 1)
 
 
 def shard_width(N: int, world: int) -> int:
     """Padded per-rank width used for the all-gather (equal sizes on every rank)."""
-    return -(-N // world)
+    return max(_shard_bound(N, world, r + 1) - _shard_bound(N, world, r) for r in range(world))
 
 
 class RowShardedLinear:

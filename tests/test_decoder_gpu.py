@@ -143,7 +143,18 @@ def _ref_step(cfg, W, ex, cache, pos, tok):
     return W["lm_head"] @ _rms(h, ex["final"], cfg.rms_eps)
 
 
-def test_decoder_step_matches_float32_reference(cuda, packed):
+@pytest.fixture(params=[False, True], ids=["serial", "overlap"])
+def overlap(request):
+    """Launch overlap (programmatic dependent launch) off and on: with it on,
+    attention copies cache tiles and the norms read their weights before
+    waiting for the previous launch."""
+    from polar_pack_b200 import _lib
+    old = _lib.set_launch_overlap(request.param)
+    yield request.param
+    _lib.set_launch_overlap(old)
+
+
+def test_decoder_step_matches_float32_reference(cuda, packed, overlap):
     from polar_pack_b200.decoder import DecoderExtras, QuadDecoder
     from polar_pack_b200.quadpack import QuadPackDevice, QuadPackFile
     cfg, buf, restored = packed

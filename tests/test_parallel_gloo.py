@@ -139,6 +139,8 @@ def test_row_shard_bounds():
             assert b[0][0] == 0 and b[-1][1] == N
             assert all(b[i][1] == b[i + 1][0] for i in range(world - 1))
             assert max(n1 - n0 for n0, n1 in b) <= shard_width(N, world)
+            assert all(n0 % 8 == 0 for n0, _ in b)            # whole 8-row output tiles
+            assert max(n1 - n0 for n0, n1 in b) - min(n1 - n0 for n0, n1 in b) < 9
     with pytest.raises(ValueError):
         row_shard(8, 2, 2)
 
