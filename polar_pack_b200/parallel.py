@@ -22,14 +22,21 @@ SHARD_ALIGN = 8   # rows: one GEMV output tile
 
 
 def _shard_bound(N: int, world: int, r: int) -> int:
-    return N if r >= world else (N * r // world) // SHARD_ALIGN * SHARD_ALIGN
+    if r >= world:
+        return N
+    if N < SHARD_ALIGN * world:          # no empty shard for a tiny Linear: split row by row
+        return N * r // world
+    tiles = -(-N // SHARD_ALIGN)
+    return tiles * r // world * SHARD_ALIGN
 
 
 def row_shard(N: int, world: int, rank: int) -> tuple[int, int]:
-    """Rows ``[n0, n1)`` of rank ``rank``: contiguous, the inner boundaries on
-    multiples of 8 rows (sizes differ by less than 8 + 1), so that a rank's
-    8-row output tiles are whole tiles of the unsharded Linear and reach the
-    gathered buffers as 16-byte stores."""
+    """Rows ``[n0, n1)`` of rank ``rank``: contiguous.  When every rank can
+    hold 8 rows, the ranks take equal shares (within one) of the 8-row output
+    tiles, so the inner boundaries lie on multiples of 8 rows: a rank's tiles
+    are whole tiles of the unsharded Linear and reach the gathered buffers as
+    16-byte stores (sizes differ by at most 8 rows).  A Linear of fewer than
+    8 rows per rank is split row by row (sizes differ by at most one)."""
     if world <= 0 or not 0 <= rank < world:
         raise ValueError(f"bad rank {rank} of {world}")
     return _shard_bound(N, world, rank), _shard_bound(N, world, rank + 1)

@@ -133,14 +133,18 @@ def test_grouped_gather_matches_full(writes_out):
 
 def test_row_shard_bounds():
     from polar_pack_b200.parallel import row_shard, shard_width
-    for N in (1, 7, 256, 2048, 11008):
+    for N in (1, 7, 8, 16, 63, 64, 256, 2048, 11008, 151936):
         for world in (1, 2, 4, 8):
             b = [row_shard(N, world, r) for r in range(world)]
             assert b[0][0] == 0 and b[-1][1] == N
             assert all(b[i][1] == b[i + 1][0] for i in range(world - 1))
             assert max(n1 - n0 for n0, n1 in b) <= shard_width(N, world)
-            assert all(n0 % 8 == 0 for n0, _ in b)            # whole 8-row output tiles
-            assert max(n1 - n0 for n0, n1 in b) - min(n1 - n0 for n0, n1 in b) < 9
+            if N >= 8 * world:
+                assert all(n0 % 8 == 0 for n0, _ in b)        # whole 8-row output tiles
+                assert min(n1 - n0 for n0, n1 in b) >= 8
+                assert max(n1 - n0 for n0, n1 in b) - min(n1 - n0 for n0, n1 in b) <= 8
+            else:
+                assert max(n1 - n0 for n0, n1 in b) - min(n1 - n0 for n0, n1 in b) <= 1
     with pytest.raises(ValueError):
         row_shard(8, 2, 2)
 
