@@ -274,6 +274,11 @@ typedef struct pp_quad_linear_desc {
    * then y = fp16(y + resid[k][m * ldo_m + n * ldo_n]); resid may equal out */
   const void* bias[4];
   const void* resid[4];
+  /* PP_QUAD_PER_MODEL_X, optional (NULL: none): the same four activation
+   * rows interleaved, x_il[4 * k + q] = x[q][k] (FP16, 8-byte aligned).  The
+   * fused plug correction then reads the four models' activations of a
+   * plugged column with one load instead of four. */
+  const void* x_il;
 } pp_quad_linear_desc;
 
 #define PP_QUAD_PER_MODEL_X 1u
@@ -343,10 +348,12 @@ PP_API int pp_f16_linear(const void* x, int64_t ldx_m, int64_t ldx_model, int64_
 PP_API int pp_embed_rows(const int* tokens, const void* const tables[4], int64_t vocab, int64_t H, void* h,
                          int64_t ldh, int* status, void* stream);
 
-/* y[m] = fp16(w[m] * fp16(x[m] * rsqrt(mean(x[m]^2) + eps))), FP32 statistics. */
+/* y[m] = fp16(w[m] * fp16(x[m] * rsqrt(mean(x[m]^2) + eps))), FP32 statistics.
+ * y_il (optional, NULL: none; 8-byte aligned): the same values interleaved,
+ * y_il[4 * i + m] = y[m][i], as pp_quad_linear_desc.x_il takes them. */
 PP_API int pp_rmsnorm_rows(const void* x, int64_t ldx, const void* const w[4], int64_t H, float eps, void* y,
-                           int64_t ldy, const uint32_t* wait_flags, int wait_world, const uint32_t* wait_epoch,
-                           int* wait_status, void* stream);
+                           int64_t ldy, void* y_il, const uint32_t* wait_flags, int wait_world,
+                           const uint32_t* wait_epoch, int* wait_status, void* stream);
 
 /* Grouped-query decode attention of one token per model, with the token's
  * rotary embedding and KV-cache append fused in.  Row m of qkv holds the
@@ -362,18 +369,20 @@ PP_API int pp_rmsnorm_rows(const void* x, int64_t ldx, const void* const w[4], i
  * position ranges of eight 32-position warp tiles each; the last arriving
  * block combines the partial results in order (deterministic).  Caches
  * 16-byte aligned (rows arrive by bulk copies); status must not be NULL
- * here (a tile copy that never lands sets it to 1).
+ * here (a tile copy that never lands sets it to 1).  out_il (optional,
+ * 8-byte aligned): the output also interleaved, out_il[4 * i + m] = out[m][i].
  * Workspace: pp_decode_attention_workspace_bytes, zero-filled once. */
 PP_API int pp_decode_attention_workspace_bytes(int64_t nq, int64_t nkv, int64_t splits, size_t* bytes);
 
 PP_API int pp_decode_attention(void* qkv, int64_t ldq, int64_t nq, int64_t nkv, int64_t hd, const void* cos_t,
                                const void* sin_t, void* const k_cache[4], void* const v_cache[4], int64_t max_pos,
-                               const int* pos, float scale, void* out, int64_t ldo, int64_t splits,
+                               const int* pos, float scale, void* out, int64_t ldo, void* out_il, int64_t splits,
                                void* workspace, size_t workspace_bytes, int* status, const uint32_t* wait_flags,
                                int wait_world, const uint32_t* wait_epoch, int* wait_status, void* stream);
 
-/* y[m][i] = fp16(fp16(silu(gate_up[m][i])) * gate_up[m][I + i]). */
-PP_API int pp_swiglu_rows(const void* gate_up, int64_t ldg, int64_t I, void* y, int64_t ldy,
+/* y[m][i] = fp16(fp16(silu(gate_up[m][i])) * gate_up[m][I + i]); y_il as for
+ * pp_rmsnorm_rows. */
+PP_API int pp_swiglu_rows(const void* gate_up, int64_t ldg, int64_t I, void* y, int64_t ldy, void* y_il,
                           const uint32_t* wait_flags, int wait_world, const uint32_t* wait_epoch, int* wait_status,
                           void* stream);
 

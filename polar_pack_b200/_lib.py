@@ -38,7 +38,8 @@ class QuadLinearDesc(ctypes.Structure):
                 ("tables", ctypes.c_void_p), ("scales", ctypes.c_float * 4),
                 ("out", ctypes.c_void_p * 4), ("ldo_m", ctypes.c_int64), ("ldo_n", ctypes.c_int64),
                 ("M", ctypes.c_int64), ("N", ctypes.c_int64), ("K", ctypes.c_int64),
-                ("flags", ctypes.c_uint32), ("bias", ctypes.c_void_p * 4), ("resid", ctypes.c_void_p * 4)]
+                ("flags", ctypes.c_uint32), ("bias", ctypes.c_void_p * 4), ("resid", ctypes.c_void_p * 4),
+                ("x_il", ctypes.c_void_p)]
 
 PER_MODEL_X = 1
 
@@ -92,14 +93,14 @@ _SIGNATURES = {
                         _PTR4, _c_void_p], _int),
     "pp_f16_linear": ([_c_void_p, _i64, _i64, _i64, _i64, _PTR4, _i64, _i64, _PTR4, _i64, _i64, _c_void_p], _int),
     "pp_embed_rows": ([_c_void_p, _PTR4, _i64, _i64, _c_void_p, _i64, _c_void_p, _c_void_p], _int),
-    "pp_rmsnorm_rows": ([_c_void_p, _i64, _PTR4, _i64, ctypes.c_float, _c_void_p, _i64, _c_void_p, _int, _c_void_p,
-                         _c_void_p, _c_void_p], _int),
+    "pp_rmsnorm_rows": ([_c_void_p, _i64, _PTR4, _i64, ctypes.c_float, _c_void_p, _i64, _c_void_p, _c_void_p, _int,
+                         _c_void_p, _c_void_p, _c_void_p], _int),
     "pp_decode_attention_workspace_bytes": ([_i64, _i64, _i64, ctypes.POINTER(_size_t)], _int),
     "pp_decode_attention": ([_c_void_p, _i64, _i64, _i64, _i64, _c_void_p, _c_void_p, _PTR4, _PTR4, _i64,
-                             _c_void_p, ctypes.c_float, _c_void_p, _i64, _i64, _c_void_p, _size_t, _c_void_p,
-                             _c_void_p, _int, _c_void_p, _c_void_p, _c_void_p], _int),
-    "pp_swiglu_rows": ([_c_void_p, _i64, _i64, _c_void_p, _i64, _c_void_p, _int, _c_void_p, _c_void_p, _c_void_p],
-                       _int),
+                             _c_void_p, ctypes.c_float, _c_void_p, _i64, _c_void_p, _i64, _c_void_p, _size_t,
+                             _c_void_p, _c_void_p, _int, _c_void_p, _c_void_p, _c_void_p], _int),
+    "pp_swiglu_rows": ([_c_void_p, _i64, _i64, _c_void_p, _i64, _c_void_p, _c_void_p, _int, _c_void_p, _c_void_p,
+                        _c_void_p], _int),
     "pp_dual_gemm_workspace_bytes": ([_i64, _i64, _i64, _i64, _i64, ctypes.POINTER(_size_t)], _int),
     "pp_dual_gemm": ([_c_void_p, _i64, _i64, _c_void_p, _i64, _i64, _c_void_p, _i64, _c_void_p,
                       _c_void_p, _c_void_p, _c_void_p, _c_void_p, _i64, _i64, _i64, _i64, _i64,

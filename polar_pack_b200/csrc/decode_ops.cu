@@ -90,6 +90,7 @@ struct NormParams {
   const __half* w[kModels];
   __half* y;
   int64_t ldy;
+  __half* y_il;  // optional interleaved copy: y_il[4 * i + m] = y[m][i]
   int H;
   float eps;
 };
@@ -102,13 +103,19 @@ __device__ __forceinline__ float block_sum(float v, float* red) {
   __syncthreads();
   float s = 0.f;
   for (int i = 0; i < nw; ++i) s += red[i];  // same order in every thread
-  __syncthreads();
   return s;
+}
+
+__device__ __forceinline__ uint2 pack4(const __half (&v)[kModels]) {
+  return make_uint2((uint32_t)__half_as_ushort(v[0]) | ((uint32_t)__half_as_ushort(v[1]) << 16),
+                    (uint32_t)__half_as_ushort(v[2]) | ((uint32_t)__half_as_ushort(v[3]) << 16));
 }
 
 constexpr int kNormThreads = 512;
 constexpr int kNormPer = 8;  // elements a thread keeps in registers (rows up to 4096)
 
+// CTA m normalises model m's row (one CTA per model keeps the four
+// reductions in parallel; the interleaved copy is written element by element).
 __global__ void rmsnorm_kernel(const NormParams p) {
   __shared__ float red[32];
   pdl_launch_dependents();  // the next packed Linear may start its weight-only prologue
@@ -137,14 +144,21 @@ __global__ void rmsnorm_kernel(const NormParams p) {
   }
   const float r = rsqrtf(block_sum(ss, red) / (float)p.H + p.eps);
   __half* y = p.y + m * p.ldy;
+  __half* yil = p.y_il;
 #pragma unroll
   for (int j = 0; j < kNormPer; ++j) {
     const int i = threadIdx.x + j * kNormThreads;
-    if (i < p.H) y[i] = __float2half_rn(wv[j] * __half2float(__float2half_rn(xv[j] * r)));
+    if (i < p.H) {
+      const __half v = __float2half_rn(wv[j] * __half2float(__float2half_rn(xv[j] * r)));
+      y[i] = v;
+      if (yil) yil[4 * i + m] = v;
+    }
   }
   for (int i = threadIdx.x + kNormPer * kNormThreads; i < p.H; i += kNormThreads) {
     const __half n = __float2half_rn(__half2float(x[i]) * r);
-    y[i] = __float2half_rn(__half2float(w[i]) * __half2float(n));
+    const __half v = __float2half_rn(__half2float(w[i]) * __half2float(n));
+    y[i] = v;
+    if (yil) yil[4 * i + m] = v;
   }
 }
 
@@ -182,6 +196,7 @@ struct AttnParams {
   const int* pos;         // the token's position: keys 0..pos are attended
   __half* out;            // [4][ldo]: nq heads x hd
   int64_t ldo;
+  __half* out_il;         // optional interleaved copy: out_il[4 * i + m] = out[m][i]
   float* part;            // [4][nq][splits * kAttnWarps][kPartStride] partials (acc, max, sum)
   int* cnt;               // [4][nkv] split arrivals (zero between launches)
   int* status;            // position outside the cache: 5; a tile that never arrived: 1
@@ -544,9 +559,17 @@ __global__ void __launch_bounds__(kAttnWarps * 32) decode_attention_kernel(const
       }
     }
     const float inv = 1.f / L;
+    const __half2 r01 = __floats2half2_rn(o0 * inv, o1 * inv), r23 = __floats2half2_rn(o2 * inv, o3 * inv);
     __half2* op = reinterpret_cast<__half2*>(p.out + m * p.ldo + qh * kHeadDim + 4 * lane);
-    op[0] = __floats2half2_rn(o0 * inv, o1 * inv);
-    op[1] = __floats2half2_rn(o2 * inv, o3 * inv);
+    op[0] = r01;
+    op[1] = r23;
+    if (p.out_il) {
+      __half* il = p.out_il + 4 * (qh * kHeadDim + 4 * lane) + m;
+      il[0] = __low2half(r01);
+      il[4] = __high2half(r01);
+      il[8] = __low2half(r23);
+      il[12] = __high2half(r23);
+    }
   }
   __syncthreads();
   if (threadIdx.x == 0) p.cnt[m * p.nkv + kvh] = 0;
@@ -558,18 +581,26 @@ struct SwigluParams {
   int64_t ldg;
   __half* y;         // [4][ldy]
   int64_t ldy;
+  __half* y_il;      // optional interleaved copy: y_il[4 * i + m] = y[m][i]
   int I;
 };
 
+// A thread produces element i of the four models (interleaved copy: one
+// 8-byte store).
 __global__ void swiglu_kernel(const SwigluParams p) {
   pdl_launch_dependents();  // the next packed Linear may start its weight-only prologue
   pdl_wait();
   gather_wait_block(p.wait);
-  const int m = blockIdx.y;
   for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < p.I; i += gridDim.x * blockDim.x) {
-    const float g = __half2float(p.gu[m * p.ldg + i]);
-    const __half sg = __float2half_rn(g / (1.f + expf(-g)));
-    p.y[m * p.ldy + i] = __float2half_rn(__half2float(sg) * __half2float(p.gu[m * p.ldg + p.I + i]));
+    __half v[kModels];
+#pragma unroll
+    for (int m = 0; m < kModels; ++m) {
+      const float g = __half2float(p.gu[m * p.ldg + i]);
+      const __half sg = __float2half_rn(g / (1.f + expf(-g)));
+      v[m] = __float2half_rn(__half2float(sg) * __half2float(p.gu[m * p.ldg + p.I + i]));
+      p.y[m * p.ldy + i] = v[m];
+    }
+    if (p.y_il) *reinterpret_cast<uint2*>(p.y_il + 4 * i) = pack4(v);
   }
 }
 
@@ -606,13 +637,13 @@ int pp_embed_rows(const int* tokens, const void* const tables[4], int64_t vocab,
 }
 
 int pp_rmsnorm_rows(const void* x, int64_t ldx, const void* const w[4], int64_t H, float eps, void* y, int64_t ldy,
-                    const uint32_t* wait_flags, int wait_world, const uint32_t* wait_epoch, int* wait_status,
-                    void* stream) {
+                    void* y_il, const uint32_t* wait_flags, int wait_world, const uint32_t* wait_epoch,
+                    int* wait_status, void* stream) {
   if (wait_flags && (!wait_epoch || wait_world < 1 || wait_world > 8)) {
     pp::set_error("pp_rmsnorm_rows: a wait needs its epoch and 1..8 ranks");
     return PP_ERR_INVALID;
   }
-  if (!x || !w || !y || H <= 0 || H > INT32_MAX || ldx < H || ldy < H) {
+  if (!x || !w || !y || H <= 0 || H > INT32_MAX / 4 || ldx < H || ldy < H || (y_il && !pp::aligned(y_il, 8))) {
     pp::set_error("pp_rmsnorm_rows: invalid arguments");
     return PP_ERR_INVALID;
   }
@@ -628,6 +659,7 @@ int pp_rmsnorm_rows(const void* x, int64_t ldx, const void* const w[4], int64_t 
   }
   p.y = reinterpret_cast<__half*>(y);
   p.ldy = ldy;
+  p.y_il = reinterpret_cast<__half*>(y_il);
   p.H = (int)H;
   p.eps = eps;
   p.wait = pp::make_wait(wait_flags, wait_world, wait_epoch, wait_status);
@@ -647,7 +679,8 @@ int pp_decode_attention_workspace_bytes(int64_t nq, int64_t nkv, int64_t splits,
 
 int pp_decode_attention(void* qkv, int64_t ldq, int64_t nq, int64_t nkv, int64_t hd, const void* cos_t,
                         const void* sin_t, void* const k_cache[4], void* const v_cache[4], int64_t max_pos,
-                        const int* pos, float scale, void* out, int64_t ldo, int64_t splits, void* workspace,
+                        const int* pos, float scale, void* out, int64_t ldo, void* out_il, int64_t splits,
+                        void* workspace,
                         size_t workspace_bytes, int* status, const uint32_t* wait_flags, int wait_world,
                         const uint32_t* wait_epoch, int* wait_status, void* stream) {
   if (wait_flags && (!wait_epoch || wait_world < 1 || wait_world > 8)) {
@@ -657,7 +690,7 @@ int pp_decode_attention(void* qkv, int64_t ldq, int64_t nq, int64_t nkv, int64_t
   if (!qkv || !cos_t || !sin_t || !k_cache || !v_cache || !pos || !out || !status || hd != pp::kHeadDim ||
       nq <= 0 || nkv <= 0 || nq % nkv || nq / nkv > 16 || splits <= 0 || splits > 4096 || max_pos <= 0 ||
       max_pos > INT32_MAX || !pp::aligned(qkv, 8) || ldq % 4 || ldq < (nq + 2 * nkv) * hd || !pp::aligned(out, 4) ||
-      ldo % 2 || nkv * 4 > 65535) {
+      ldo % 2 || nkv * 4 > 65535 || (out_il && !pp::aligned(out_il, 8))) {
     pp::set_error("pp_decode_attention: head_dim must be %d, nq a multiple of nkv (at most 16 q heads per kv "
                   "head), 1..4096 splits, 8-byte aligned qkv rows holding nq + 2 nkv heads, 4-byte aligned output "
                   "rows, a status word",
@@ -687,6 +720,7 @@ int pp_decode_attention(void* qkv, int64_t ldq, int64_t nq, int64_t nkv, int64_t
   p.pos = pos;
   p.out = reinterpret_cast<__half*>(out);
   p.ldo = ldo;
+  p.out_il = reinterpret_cast<__half*>(out_il);
   p.cnt = reinterpret_cast<int*>(workspace);
   p.part = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(workspace) +
                                     pp::align_up((size_t)4 * nkv * sizeof(int), 256));
@@ -713,20 +747,22 @@ int pp_decode_attention(void* qkv, int64_t ldq, int64_t nq, int64_t nkv, int64_t
                            reinterpret_cast<cudaStream_t>(stream), p);
 }
 
-int pp_swiglu_rows(const void* gate_up, int64_t ldg, int64_t I, void* y, int64_t ldy, const uint32_t* wait_flags,
-                   int wait_world, const uint32_t* wait_epoch, int* wait_status, void* stream) {
+int pp_swiglu_rows(const void* gate_up, int64_t ldg, int64_t I, void* y, int64_t ldy, void* y_il,
+                   const uint32_t* wait_flags, int wait_world, const uint32_t* wait_epoch, int* wait_status,
+                   void* stream) {
   if (wait_flags && (!wait_epoch || wait_world < 1 || wait_world > 8)) {
     pp::set_error("pp_swiglu_rows: a wait needs its epoch and 1..8 ranks");
     return PP_ERR_INVALID;
   }
-  if (!gate_up || !y || I <= 0 || I > INT32_MAX || ldg < 2 * I || ldy < I) {
+  if (!gate_up || !y || I <= 0 || I > INT32_MAX / 4 || ldg < 2 * I || ldy < I || (y_il && !pp::aligned(y_il, 8))) {
     pp::set_error("pp_swiglu_rows: invalid arguments");
     return PP_ERR_INVALID;
   }
   pp::SwigluParams p{pp::make_wait(wait_flags, wait_world, wait_epoch, wait_status),
-                     reinterpret_cast<const __half*>(gate_up), ldg, reinterpret_cast<__half*>(y), ldy, (int)I};
-  const unsigned gx = (unsigned)((I + 255) / 256 < 64 ? (I + 255) / 256 : 64);
-  return pp::launch_kernel("swiglu_kernel", pp::launch_overlap(), pp::swiglu_kernel, dim3(gx, 4), dim3(256), 0,
+                     reinterpret_cast<const __half*>(gate_up), ldg, reinterpret_cast<__half*>(y), ldy,
+                     reinterpret_cast<__half*>(y_il), (int)I};
+  const unsigned gx = (unsigned)((I + 255) / 256 < 128 ? (I + 255) / 256 : 128);
+  return pp::launch_kernel("swiglu_kernel", pp::launch_overlap(), pp::swiglu_kernel, dim3(gx), dim3(256), 0,
                            reinterpret_cast<cudaStream_t>(stream), p);
 }
 

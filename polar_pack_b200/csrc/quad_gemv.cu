@@ -105,6 +105,9 @@ struct QuadParams {
   // y = fp16(y + resid_k[m][n]) (resid with the output strides, may be out)
   const __half* bias[4];
   const __half* resid[4];
+  // DIAG, optional (NULL: none): the four activation rows interleaved,
+  // xil[4 * k + q] = x_q[k]; a plug entry's four activations are one load
+  const __half* xil;
   int cta_start[kMaxCtaTable + 1];  // unit start of every CTA (plan_cta_starts)
 };
 
@@ -311,10 +314,19 @@ struct QuadOp {
     if constexpr (PLUG) {
       const __half* xk = x + kc * 64;
       if constexpr (DIAG) {
+        if (p.xil) {  // uniform: the two entries' four activations, one 8-byte load each
+          const __half* xi = p.xil + (int64_t)kc * 64 * 4;
+          const uint2 a = ld_u2(xi + 4u * (px & 0xFFu)), b = ld_u2(xi + 4u * (px >> 16));
+          pxq[0] = lo_pair(a.x, b.x);
+          pxq[1] = hi_pair(a.x, b.x);
+          pxq[2] = lo_pair(a.y, b.y);
+          pxq[3] = hi_pair(a.y, b.y);
+        } else {
 #pragma unroll
-        for (int q = 0; q < 4; ++q)
-          pxq[q] = (uint32_t)ld_u16(xk + q * ldx_m + (px & 0xFFu)) |
-                   ((uint32_t)ld_u16(xk + q * ldx_m + (px >> 16)) << 16);
+          for (int q = 0; q < 4; ++q)
+            pxq[q] = (uint32_t)ld_u16(xk + q * ldx_m + (px & 0xFFu)) |
+                     ((uint32_t)ld_u16(xk + q * ldx_m + (px >> 16)) << 16);
+        }
       } else {
         px = (uint32_t)ld_u16(xk + (px & 0xFFu)) | ((uint32_t)ld_u16(xk + (px >> 16)) << 16);
       }
@@ -415,8 +427,10 @@ struct QuadOp {
 #pragma unroll
         for (int nb = 0; nb < NB; ++nb)
           // PLUG (batch 1): only lanes g = 0 feed activations; the other
-          // batch columns stay zero for side()'s plug terms
-          xb[s][nb] = (PLUG && !DIAG && g != 0) ? make_uint2(0u, 0u) : xquad<FULL>(nb, kbase, s);
+          // batch columns stay zero for side()'s plug terms.  DIAG: batch
+          // columns 4-7 are never stored, lanes g >= 4 load nothing
+          xb[s][nb] = ((PLUG && !DIAG && g != 0) || (DIAG && g >= 4)) ? make_uint2(0u, 0u)
+                                                                       : xquad<FULL>(nb, kbase, s);
 #pragma unroll
       for (int s = 0; s < 4; ++s) {
         const int kp = kbase + 16 * s + 4 * c;
@@ -1351,8 +1365,9 @@ int group_run(int count, const pp_quad_linear_desc* d, const PeerGather* gather,
     void* const probe[4] = {unused_out[0], unused_out[0], unused_out[0], unused_out[0]};
     // a gathered member writes the gather buffers, not out[]
     if ((rc = check_common(nullptr, m.tables, m.scales, gather ? probe : m.out, m.M, m.N, m.K))) return rc;
-    if (!aligned(m.plug_vals, 8) || !aligned(m.unit_plugs, 16) || !aligned(m.unit_plug_off, 4)) {
-      set_error("group member %d: plug_vals must be 8-byte, unit plugs 16-byte aligned", j);
+    if (!aligned(m.plug_vals, 8) || !aligned(m.unit_plugs, 16) || !aligned(m.unit_plug_off, 4) ||
+        !aligned(m.x_il, 8)) {
+      set_error("group member %d: plug_vals and x_il must be 8-byte, unit plugs 16-byte aligned", j);
       return PP_ERR_INVALID;
     }
     QuadParams& prm = gp.m[j];
@@ -1374,6 +1389,7 @@ int group_run(int count, const pp_quad_linear_desc* d, const PeerGather* gather,
       prm.bias[i] = reinterpret_cast<const __half*>(m.bias[i]);
       prm.resid[i] = reinterpret_cast<const __half*>(m.resid[i]);
     }
+    prm.xil = diag ? reinterpret_cast<const __half*>(m.x_il) : nullptr;
     prm.M = 1;
     prm.N = (int)m.N;
     prm.K = (int)m.K;

@@ -173,15 +173,16 @@ def fused_rows(N: int, K: int, sms: int) -> list[tuple[int, int]]:
     return [(r0, min(N, r0 + step)) for r0 in range(0, N, step)]
 
 
-def linear_chunks(pack, offset: int, N: int, K: int, sms: int, x, out, bias=None, resid=None):
+def linear_chunks(pack, offset: int, N: int, K: int, sms: int, x, out, bias=None, resid=None, x_il=None):
     """One per-model-activation group launch per row chunk of the Linear at
-    ``offset`` (``out`` / ``bias`` / ``resid``: [4][N] tensors, or None)."""
+    ``offset`` (``out`` / ``bias`` / ``resid``: [4][N] tensors, or None;
+    ``x_il``: the activations interleaved, see ``linear_desc``)."""
     res = []
     for r0, r1 in fused_rows(N, K, sms):
         cut = lambda t: [t[k:k + 1, r0:r1] for k in range(4)] if t is not None else None
         cutb = [bias[k][r0:r1] for k in range(4)] if bias is not None else None
         g = QuadLinearGroup([pack.linear(offset + r0 * K, r1 - r0, K)], [x], [cut(out)], per_model_x=True,
-                            biases=[cutb], resids=[cut(resid)])
+                            biases=[cutb], resids=[cut(resid)], x_ils=[x_il])
         if not g.single_launch:
             raise ValueError(f"rows [{r0}, {r1}) of the Linear at {offset} do not fit one fused launch")
         res.append(g)
@@ -198,7 +199,7 @@ class GatheredLinear:
     of launches into the buffer -- the wait compares launch counts.
     ``bias`` / ``resid``: four ``[N]`` vectors (the shard's rows are used)."""
 
-    def __init__(self, pack, offset, N, K, sms, x, peers, b, world, rank, bias=None, resid=None):
+    def __init__(self, pack, offset, N, K, sms, x, peers, b, world, rank, bias=None, resid=None, x_il=None):
         import ctypes as C
 
         from .parallel import row_shard, shard_width
@@ -218,7 +219,7 @@ class GatheredLinear:
             lin = pack.linear(offset + r0 * K, r1 - r0, K)
             bb = [bias[k][r0:r1] for k in range(4)] if bias is not None else None
             rr = [resid[k:k + 1, r0:r1] for k in range(4)] if resid is not None else None
-            d = (_lib.QuadLinearDesc * 1)(linear_desc(x, lin, None, True, bb, rr))
+            d = (_lib.QuadLinearDesc * 1)(linear_desc(x, lin, None, True, bb, rr, x_il))
             if not self.lib.pp_quad_linear_group_single_launch(1, d):
                 raise ValueError("a shard chunk does not fit one fused launch")
             nb = _lib._size_t()
@@ -284,6 +285,12 @@ class QuadDecoder:
         self.xn = torch.zeros(4, H, **f16)
         self.attn = torch.zeros(4, cfg.q_dim, **f16)
         self.act = torch.zeros(4, I, **f16)
+        # the inputs of the large Linears (gate_up, down, lm_head) also
+        # interleaved ([i][model]): their fused plug correction reads a
+        # column's four activations with one load (x_il); the small q/k/v and
+        # o Linears gain less than the extra stores cost
+        self.xn_il = torch.zeros(4 * H, **f16)
+        self.act_il = torch.zeros(4 * I, **f16)
         self.kc = [torch.zeros(4, cfg.max_pos, cfg.kv_heads, cfg.head_dim, **f16) for _ in range(cfg.layers)]
         self.vc = [torch.zeros(4, cfg.max_pos, cfg.kv_heads, cfg.head_dim, **f16) for _ in range(cfg.layers)]
         self.cos, self.sin = rope_tables(cfg, dev)
@@ -310,19 +317,21 @@ class QuadDecoder:
                 self.groups.append((
                     [GatheredLinear(pack, oq, qkv_n, H, sms, self.xn, pr, 0, world, rank, bias=bias)],
                     [GatheredLinear(pack, oo, H, cfg.q_dim, sms, self.attn, pr, 1, world, rank, resid=self.h)],
-                    [GatheredLinear(pack, og, 2 * I, H, sms, self.xn, pr, 2, world, rank)],
-                    [GatheredLinear(pack, od, H, I, sms, self.act, pr, 1, world, rank, resid=self.h)]))
+                    [GatheredLinear(pack, og, 2 * I, H, sms, self.xn, pr, 2, world, rank, x_il=self.xn_il)],
+                    [GatheredLinear(pack, od, H, I, sms, self.act, pr, 1, world, rank, resid=self.h,
+                                    x_il=self.act_il)]))
             else:
                 self.groups.append((
                     linear_chunks(pack, oq, qkv_n, H, sms, self.xn, self.qkv, bias=bias),
                     linear_chunks(pack, oo, H, cfg.q_dim, sms, self.attn, self.h, resid=self.h),
-                    linear_chunks(pack, og, 2 * I, H, sms, self.xn, self.gu),
-                    linear_chunks(pack, od, H, I, sms, self.act, self.h, resid=self.h)))
+                    linear_chunks(pack, og, 2 * I, H, sms, self.xn, self.gu, x_il=self.xn_il),
+                    linear_chunks(pack, od, H, I, sms, self.act, self.h, resid=self.h, x_il=self.act_il)))
         ol, _ = offs["lm_head"]
         if world > 1:
-            self.head = [GatheredLinear(pack, ol, V, H, sms, self.xn, self.peers, 3, world, rank)]
+            self.head = [GatheredLinear(pack, ol, V, H, sms, self.xn, self.peers, 3, world, rank,
+                                        x_il=self.xn_il)]
         else:
-            self.head = linear_chunks(pack, ol, V, H, sms, self.xn, self.logits)
+            self.head = linear_chunks(pack, ol, V, H, sms, self.xn, self.logits, x_il=self.xn_il)
         P4 = _lib._PTR4
         self._emb = P4(*[extras.embed[k].data_ptr() for k in range(4)])
         self._in_norm = [P4(*[extras.in_norm[l, k].data_ptr() for k in range(4)]) for l in range(cfg.layers)]
@@ -364,21 +373,23 @@ class QuadDecoder:
         none = (None, 0, None, None)
         for l, (g_qkv, g_o, g_gu, g_d) in enumerate(self.groups):
             c(L.pp_rmsnorm_rows(self.h.data_ptr(), H, self._in_norm[l], H, cfg.rms_eps, self.xn.data_ptr(), H,
-                                *(self._wait(1) if l > 0 else none), s))
+                                None, *(self._wait(1) if l > 0 else none), s))
             run(g_qkv)
             c(L.pp_decode_attention(self.qkv.data_ptr(), self.qkv.stride(0), cfg.q_heads, cfg.kv_heads,
                                     cfg.head_dim, self.cos.data_ptr(), self.sin.data_ptr(), self._kc[l],
                                     self._vc[l], cfg.max_pos, self.pos.data_ptr(), self.scale, self.attn.data_ptr(),
-                                    self.attn.stride(0), self.splits, self.attn_ws.data_ptr(),
+                                    self.attn.stride(0), None, self.splits,
+                                    self.attn_ws.data_ptr(),
                                     self.attn_ws.numel(), self.status.data_ptr(), *self._wait(0), s))
             run(g_o)
             c(L.pp_rmsnorm_rows(self.h.data_ptr(), H, self._post_norm[l], H, cfg.rms_eps, self.xn.data_ptr(), H,
-                                *self._wait(1), s))
+                                self.xn_il.data_ptr(), *self._wait(1), s))
             run(g_gu)
-            c(L.pp_swiglu_rows(self.gu.data_ptr(), self.gu.stride(0), I, self.act.data_ptr(), I, *self._wait(2), s))
+            c(L.pp_swiglu_rows(self.gu.data_ptr(), self.gu.stride(0), I, self.act.data_ptr(), I,
+                               self.act_il.data_ptr(), *self._wait(2), s))
             run(g_d)
         c(L.pp_rmsnorm_rows(self.h.data_ptr(), H, self._final, H, cfg.rms_eps, self.xn.data_ptr(), H,
-                            *self._wait(1), s))
+                            self.xn_il.data_ptr(), *self._wait(1), s))
         run(self.head)
         if self.peers is not None:
             self.peers.wait(3, s)

@@ -419,16 +419,22 @@ def quad_linear(x: torch.Tensor, layer: QuadLinearSlice, out=None) -> list[torch
 
 
 def linear_desc(x: torch.Tensor, layer: QuadLinearSlice, out, per_model_x: bool = False, bias=None,
-                resid=None) -> "_lib.QuadLinearDesc":
+                resid=None, x_il: torch.Tensor | None = None) -> "_lib.QuadLinearDesc":
     """The C descriptor of one ``quad_linear(x, layer, out)`` (pointers of the
     given tensors: keep them alive while the descriptor is used).
 
     ``per_model_x``: ``x`` has four rows, model k multiplies row k and writes
-    row 0 of ``out[k]``.  ``bias`` / ``resid``: four FP16 vectors (or None) of
-    the epilogue ``fp16(s_k acc + bias_k)``, then ``+ resid_k`` (``resid``
-    indexed like ``out``; it may be ``out`` itself)."""
+    row 0 of ``out[k]``; ``x_il`` (optional) holds the same rows interleaved,
+    ``x_il[4 i + k] = x[k][i]``, which the fused plug correction reads with
+    one load per plugged column.  ``bias`` / ``resid``: four FP16 vectors (or
+    None) of the epilogue ``fp16(s_k acc + bias_k)``, then ``+ resid_k``
+    (``resid`` indexed like ``out``; it may be ``out`` itself)."""
     d = _lib.QuadLinearDesc()
     d.flags = _lib.PER_MODEL_X if per_model_x else 0
+    if x_il is not None:
+        if not per_model_x or x_il.numel() < 4 * layer.K or x_il.dtype != torch.float16:
+            raise ValueError("x_il: per-model activations only, FP16, 4 * K values")
+        d.x_il = x_il.data_ptr()
     for k in range(4):
         d.bias[k] = bias[k].data_ptr() if bias is not None and bias[k] is not None else None
         d.resid[k] = resid[k].data_ptr() if resid is not None and resid[k] is not None else None
@@ -458,7 +464,7 @@ class QuadLinearGroup:
     The members must not read each other's outputs.
     """
 
-    def __init__(self, layers, xs, outs, per_model_x: bool = False, biases=None, resids=None):
+    def __init__(self, layers, xs, outs, per_model_x: bool = False, biases=None, resids=None, x_ils=None):
         if not (len(layers) == len(xs) == len(outs)) or not layers:
             raise ValueError("one input and one output set per Linear")
         for x, l in zip(xs, layers):
@@ -471,9 +477,11 @@ class QuadLinearGroup:
         n = len(layers)
         biases = biases or [None] * n
         resids = resids or [None] * n
-        self._keep = (biases, resids)
-        self.descs = (_lib.QuadLinearDesc * n)(*[linear_desc(x, l, o, per_model_x, b, r)
-                                                 for x, l, o, b, r in zip(xs, layers, outs, biases, resids)])
+        x_ils = x_ils or [None] * n
+        self._keep = (biases, resids, x_ils)
+        self.descs = (_lib.QuadLinearDesc * n)(*[linear_desc(x, l, o, per_model_x, b, r, xi)
+                                                 for x, l, o, b, r, xi in zip(xs, layers, outs, biases, resids,
+                                                                              x_ils)])
         lib = _lib.load()
         nb = _lib._size_t()
         _lib.check(lib.pp_quad_linear_group_workspace_bytes(n, self.descs, ctypes.byref(nb)))

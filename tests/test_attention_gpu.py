@@ -56,6 +56,7 @@ class _Attn:
         self.status = torch.zeros(1, dtype=torch.int32, device=device)
         self.pos = torch.zeros(1, dtype=torch.int32, device=device)
         self.out = torch.zeros(4, nq * HD, dtype=torch.float16, device=device)
+        self.out_il = torch.zeros(4 * nq * HD, dtype=torch.float16, device=device)
         P4 = _lib._PTR4
         self._kc = P4(*[self.kc[k].data_ptr() for k in range(4)])
         self._vc = P4(*[self.vc[k].data_ptr() for k in range(4)])
@@ -72,7 +73,8 @@ class _Attn:
         self._lib.check(self.lib.pp_decode_attention(
             qkv.data_ptr(), qkv.stride(0), self.nq, self.nkv, HD, self.cos.data_ptr(), self.sin.data_ptr(),
             self._kc, self._vc, self.max_pos, self.pos.data_ptr(), 1.0 / math.sqrt(HD), self.out.data_ptr(),
-            self.out.stride(0), self.splits, self.ws.data_ptr(), self.ws.numel(), self.status.data_ptr(),
+            self.out.stride(0), self.out_il.data_ptr(), self.splits, self.ws.data_ptr(), self.ws.numel(),
+            self.status.data_ptr(),
             None, 0, None, None, self._lib.stream_handle(self.dev)))
         torch.cuda.synchronize(self.dev)
         return qkv
@@ -93,6 +95,7 @@ class _Attn:
         got = self.out.view(4, nq, HD).float()
         err = float((got - ref).abs().max() / V.abs().max())
         assert err <= TOL, (pos, err)
+        assert torch.equal(self.out_il.view(-1, 4).t(), self.out)      # interleaved copy
         assert int(self.status.item()) == 0
 
 
@@ -124,5 +127,5 @@ def test_attention_rejects_unsupported_groups(cuda):
     with pytest.raises(ValueError):
         _lib.check(a.lib.pp_decode_attention(
             a.out.data_ptr(), 0, 34, 2, HD, a.cos.data_ptr(), a.sin.data_ptr(), a._kc, a._vc, 64,
-            a.pos.data_ptr(), 1.0, a.out.data_ptr(), a.out.stride(0), 2, a.ws.data_ptr(), a.ws.numel(),
+            a.pos.data_ptr(), 1.0, a.out.data_ptr(), a.out.stride(0), None, 2, a.ws.data_ptr(), a.ws.numel(),
             a.status.data_ptr(), None, 0, None, None, _lib.stream_handle(a.dev)))

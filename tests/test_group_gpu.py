@@ -92,3 +92,30 @@ def test_group_members_one_after_another(cuda, stream):
         ref = quad_linear(xs[j], l)
         for k in range(4):
             assert torch.equal(outs[j][k].view(torch.int16), ref[k].view(torch.int16))
+
+
+def test_per_model_rows_with_interleaved_copy(cuda, stream):
+    """Per-model activation rows (model k multiplies row k, as in a 4-model
+    decode step) against the oracle; with the interleaved copy x_il the plug
+    correction reads its activations differently but sums the same terms in
+    the same order: bit-identical."""
+    from polar_pack_b200.quadpack import QuadLinearGroup
+    buf, pk, layers = stream
+    g = torch.Generator(device=cuda).manual_seed(3)
+    xs = [torch.randn(4, K, generator=g, device=cuda).half() for K, _ in SHAPES]
+    ils = [x.t().contiguous().view(-1) for x in xs]
+    res = []
+    for x_ils in (None, ils):
+        outs = [[torch.full((1, N), float("nan"), dtype=torch.half, device=cuda) for _ in range(4)]
+                for _, N in SHAPES]
+        grp = QuadLinearGroup(layers, xs, outs, per_model_x=True, x_ils=x_ils)
+        assert grp.single_launch
+        grp()
+        torch.cuda.synchronize()
+        res.append(outs)
+    for j, l in enumerate(layers):
+        for k in range(4):
+            ref = oracle_out(buf, l, xs[j][k:k + 1].cpu().numpy())
+            got = res[0][j][k].cpu().numpy()
+            assert oq.rel_err(got, ref[k]) <= TOL, (SHAPES[j], k)
+            assert torch.equal(res[1][j][k].view(torch.int16), res[0][j][k].view(torch.int16)), (SHAPES[j], k)
