@@ -205,6 +205,9 @@ def run_ours(args):
 
     M = args.batch
     _lib.set_launch_overlap(not args.no_overlap)
+    if args.decode_only:
+        run_decode_only(torch, dist, dev, args, world, rank)
+        return
     streams = build_streams(torch, args.replicas, dev)
     sets = [layer_slices(s, SHAPES, rank, world) for s in streams]
     for s in streams:
@@ -670,6 +673,23 @@ def run_dual_leg(torch, dev, args, lib, stream):
                     "replicas larger than L2, launch overlap on"}
 
 
+def run_decode_only(torch, dist, dev, args, world, rank):
+    """``--decode-only``: the decode-step legs alone (for profiling them); one
+    JSON line with tokens/s of the 3B-class step as ``value``."""
+    stream = torch.cuda.Stream(dev)
+    torch.cuda.set_stream(stream)
+    d3 = run_real_decode(torch, dist, dev, args, stream, DECODE_3B, ctx=1024, seed=3000, world=world, rank=rank)
+    d7 = None if args.no_7b else run_real_decode(torch, dist, dev, args, stream, DECODE_7B, ctx=1024, seed=7000,
+                                                 world=world, rank=rank)
+    if rank == 0:
+        print(json.dumps({"metric": "4-model decode tokens/s (3B-class step)", "value": d3["tok_s"], "unit": "tok/s",
+                          "n_gpus": world, "higher_is_better": True, "data": "synthetic",
+                          "config": {"decode_step_3b": d3, "decode_step_7b": d7}}), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
 def run_real_decode(torch, dist, dev, args, stream, arch, ctx, seed, world=1, rank=0):
     """One real decoder step of the four packed models (BASELINE configs[2] /
     configs[4] at batch 1): every layer distinct, each model with its own
@@ -1018,6 +1038,7 @@ def main():
     ap.add_argument("--no-overlap", action="store_true", help="launch kernels without programmatic overlap")
     ap.add_argument("--no-decode", action="store_true", help="skip the decode-step legs")
     ap.add_argument("--no-7b", action="store_true", help="skip the 7B decode-step leg")
+    ap.add_argument("--decode-only", action="store_true", help="run only the decode-step legs (profiling)")
     ap.add_argument("--no-dual", action="store_true", help="skip the dual-pack kernel leg")
     ap.add_argument("--no-batched", action="store_true", help="skip the batched-rows leg")
     ap.add_argument("--nccl-gather", action="store_true",
