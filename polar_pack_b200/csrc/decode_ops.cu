@@ -585,22 +585,46 @@ struct SwigluParams {
   int I;
 };
 
-// A thread produces element i of the four models (interleaved copy: one
-// 8-byte store).
+__device__ __forceinline__ __half swiglu1(__half g_, __half u) {
+  const float g = __half2float(g_);
+  const __half sg = __float2half_rn(g / (1.f + expf(-g)));
+  return __float2half_rn(__half2float(sg) * __half2float(u));
+}
+
+// A thread produces elements 2j, 2j + 1 of the four models: 4-byte loads and
+// stores, and the interleaved copy of the pair as one 16-byte store (PAIRS:
+// even I, ldg and ldy, 4-byte aligned rows, 16-byte aligned y_il); else one
+// element of the four models per thread.
+template <bool PAIRS>
 __global__ void swiglu_kernel(const SwigluParams p) {
   pdl_launch_dependents();  // the next packed Linear may start its weight-only prologue
   pdl_wait();
   gather_wait_block(p.wait);
-  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < p.I; i += gridDim.x * blockDim.x) {
-    __half v[kModels];
+  const int n = PAIRS ? p.I / 2 : p.I;
+  for (int j = blockIdx.x * blockDim.x + threadIdx.x; j < n; j += gridDim.x * blockDim.x) {
+    if constexpr (PAIRS) {
+      __half a[kModels], b[kModels];
 #pragma unroll
-    for (int m = 0; m < kModels; ++m) {
-      const float g = __half2float(p.gu[m * p.ldg + i]);
-      const __half sg = __float2half_rn(g / (1.f + expf(-g)));
-      v[m] = __float2half_rn(__half2float(sg) * __half2float(p.gu[m * p.ldg + p.I + i]));
-      p.y[m * p.ldy + i] = v[m];
+      for (int m = 0; m < kModels; ++m) {
+        const __half2 g = *reinterpret_cast<const __half2*>(p.gu + m * p.ldg + 2 * j);
+        const __half2 u = *reinterpret_cast<const __half2*>(p.gu + m * p.ldg + p.I + 2 * j);
+        a[m] = swiglu1(__low2half(g), __low2half(u));
+        b[m] = swiglu1(__high2half(g), __high2half(u));
+        *reinterpret_cast<__half2*>(p.y + m * p.ldy + 2 * j) = __halves2half2(a[m], b[m]);
+      }
+      if (p.y_il) {
+        const uint2 lo = pack4(a), hi = pack4(b);
+        *reinterpret_cast<uint4*>(p.y_il + 8 * j) = make_uint4(lo.x, lo.y, hi.x, hi.y);
+      }
+    } else {
+      __half v[kModels];
+#pragma unroll
+      for (int m = 0; m < kModels; ++m) {
+        v[m] = swiglu1(p.gu[m * p.ldg + j], p.gu[m * p.ldg + p.I + j]);
+        p.y[m * p.ldy + j] = v[m];
+      }
+      if (p.y_il) *reinterpret_cast<uint2*>(p.y_il + 4 * j) = pack4(v);
     }
-    if (p.y_il) *reinterpret_cast<uint2*>(p.y_il + 4 * i) = pack4(v);
   }
 }
 
@@ -761,8 +785,12 @@ int pp_swiglu_rows(const void* gate_up, int64_t ldg, int64_t I, void* y, int64_t
   pp::SwigluParams p{pp::make_wait(wait_flags, wait_world, wait_epoch, wait_status),
                      reinterpret_cast<const __half*>(gate_up), ldg, reinterpret_cast<__half*>(y), ldy,
                      reinterpret_cast<__half*>(y_il), (int)I};
-  const unsigned gx = (unsigned)((I + 255) / 256 < 128 ? (I + 255) / 256 : 128);
-  return pp::launch_kernel("swiglu_kernel", pp::launch_overlap(), pp::swiglu_kernel, dim3(gx), dim3(256), 0,
+  const bool pairs = I % 2 == 0 && ldg % 2 == 0 && ldy % 2 == 0 && pp::aligned(gate_up, 4) && pp::aligned(y, 4) &&
+                     (!y_il || pp::aligned(y_il, 16));
+  const int64_t n = pairs ? I / 2 : I;
+  const unsigned gx = (unsigned)((n + 255) / 256 < 128 ? (n + 255) / 256 : 128);
+  return pp::launch_kernel("swiglu_kernel", pp::launch_overlap(),
+                           pairs ? pp::swiglu_kernel<true> : pp::swiglu_kernel<false>, dim3(gx), dim3(256), 0,
                            reinterpret_cast<cudaStream_t>(stream), p);
 }
 
