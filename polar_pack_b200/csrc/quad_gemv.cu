@@ -62,7 +62,7 @@ size_t quad_tc_slots_bytes(int64_t M, int64_t N, int64_t K, int sms);
 int launch_quad_tc(const void* x, int64_t ldx_m, const uint32_t* codes, int64_t ldw, const void* tables,
                    const float scales[4], void* const out[4], int64_t ldo_m, int64_t ldo_n, const float* corr,
                    int64_t corr_q, int64_t Mc, int64_t N, int64_t K, int* counters, float* slots,
-                   cudaStream_t s);
+                   const void* uplugs, const uint32_t* uplug_off, cudaStream_t s);
 constexpr int64_t kTcLaunchRows = 128;
 
 // Warps per CTA.  Shared memory holds the 128 KiB tables, each warp's TMA
@@ -1129,31 +1129,41 @@ static int quad_run(const void* a, int64_t lda_m, int64_t lda_k, const uint32_t*
     return PP_ERR_CUDA;
   }
   if (tables && nk && quad_tc_ok(M, N, K, codes, ldc_n, a, lda_m, lda_k)) {
-    // batched tensor-core path: every code decoded once for up to 128 batch rows
-    const size_t csz = plug ? tc_corr_bytes(M, N) : 0;
+    // batched tensor-core path: every code decoded once for up to 128 batch
+    // rows.  With the unit plug stream and more than 32 rows the plug values
+    // are substituted into the decoded tiles; otherwise a separate kernel
+    // computes an FP32 correction, whose cost grows with the rows while the
+    // substitution's is fixed (2048 x 11008: 132 vs 140 us at 32 rows,
+    // 182 vs 154 us at 64).
+    auto in_tile = [&](int64_t Mc) { return plug && uplugs != nullptr && Mc > 32; };
+    const int64_t last = M % kTcLaunchRows ? M % kTcLaunchRows : kTcLaunchRows;  // rows of the last launch
+    const bool sep = plug && (!in_tile(M < kTcLaunchRows ? M : kTcLaunchRows) || !in_tile(last));
+    const size_t csz = sep ? tc_corr_bytes(M, N) : 0;
     const size_t ssz = quad_tc_slots_bytes(M, N, K, sms);
-    const size_t need = kCounterBytes + csz + ssz + (plug ? xt_bytes(K) : 0);
+    const size_t need = kCounterBytes + csz + ssz + (sep ? xt_bytes(K) : 0);
     if (ws_bytes < need || !ws || !aligned(ws, 256)) {
       set_error("workspace of %zu bytes (256-byte aligned, zero-filled) required, got %zu", need, ws_bytes);
       return PP_ERR_WORKSPACE;
     }
     int* counters = reinterpret_cast<int*>(ws);
-    float* corr = plug ? reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(ws) + kCounterBytes) : nullptr;
+    float* corr = sep ? reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(ws) + kCounterBytes) : nullptr;
     float* slots = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(ws) + kCounterBytes + csz);
-    __half* xt = plug ? reinterpret_cast<__half*>(reinterpret_cast<uint8_t*>(ws) + kCounterBytes + csz + ssz)
-                      : nullptr;
+    __half* xt = sep ? reinterpret_cast<__half*>(reinterpret_cast<uint8_t*>(ws) + kCounterBytes + csz + ssz)
+                     : nullptr;
     for (int64_t m0 = 0; m0 < M; m0 += kTcLaunchRows) {
       const int64_t Mc = (M - m0) < kTcLaunchRows ? (M - m0) : kTcLaunchRows;
       const __half* xc = reinterpret_cast<const __half*>(a) + m0 * lda_m;
       void* oc[4];
       for (int i = 0; i < 4; ++i) oc[i] = reinterpret_cast<__half*>(out[i]) + m0 * ldo_m;
-      if (plug) {  // all rows of the launch in one correction
+      const bool tile_plugs = in_tile(Mc);
+      if (plug && !tile_plugs) {  // all rows of the launch in one correction
         PlugCorrParams cp{xc, lda_m, plug_idx, reinterpret_cast<const uint2*>(plug_vals), wbase, base_lo32,
                           (int)Mc, (int)N, (int)K, (int)cdiv(K, 64), corr, Mc * N, xt};
         if ((rc = launch_plug_corr(cp, s))) return rc;
       }
-      if ((rc = launch_quad_tc(xc, lda_m, codes, ldc_n, tables, scales, oc, ldo_m, ldo_n, corr, Mc * N, Mc, N, K,
-                               counters, slots, s)))
+      if ((rc = launch_quad_tc(xc, lda_m, codes, ldc_n, tables, scales, oc, ldo_m, ldo_n,
+                               plug && !tile_plugs ? corr : nullptr, Mc * N, Mc, N, K, counters, slots,
+                               tile_plugs ? uplugs : nullptr, tile_plugs ? uplug_off : nullptr, s)))
         return rc;
     }
     return PP_OK;

@@ -16,9 +16,15 @@
 //                     N = nmma, K = 16) per model into four FP32 accumulators
 //                     in tensor memory, and tcgen05.commit releases the
 //                     stage when the tensor core is done with it.
+// Plug entries (the `.quadpack` plug table) are substituted into the A tiles:
+// per 64-column window the producer bulk-copies the window's segments of the
+// Linear's unit-major plug stream (one per 8-row tile), and each decoder
+// thread writes the plug values of its row and 8 columns over its decoded
+// weights -- the reference's own substitution, before the matmul.  (Without
+// the stream, a separate kernel computes an FP32 correction instead.)
 // Decoder warps 0-3 then read the accumulators (tcgen05.ld), add the plug
-// correction, scale and store FP16 -- or, with split-K, write FP32 partials
-// that the last CTA of the tile sums in split order (deterministic).
+// correction if any, scale and store FP16 -- or, with split-K, write FP32
+// partials that the last CTA of the tile sums in split order (deterministic).
 // Every mbarrier wait is bounded; tensor memory is released on every path.
 #include "pp_common.cuh"
 #include "pp_engine.cuh"
@@ -38,8 +44,11 @@ constexpr uint32_t kTcATileBytes = kTcRows * kTcK * 2;      // 4 KiB per model
 constexpr uint32_t kTcCSlotBytes = kTcCodeBytes + kTcXBytes;  // 12 KiB: one stage's TMA data
 constexpr uint32_t kTcASlotBytes = 4 * kTcATileBytes;       // 16 KiB: one stage's four A tiles
 constexpr int kTcMaxStages = 8;                             // code slots
-constexpr int kTcASlots = 3;                                // A-tile slots
+constexpr int kTcASlots = 2;                                // A-tile slots: one per decoder group
 constexpr int kTcMaxRows = 128;                             // batch rows per launch
+constexpr uint32_t kTcPlugSeg = 512;                        // staged bytes of one unit's plug segment
+constexpr uint32_t kTcPlugSlot = (kTcRows / 8) * kTcPlugSeg;  // one 64-column window: 16 segments
+constexpr int kTcPlugMaxStages = 4;                         // code slots with plugs (slot reuse, see below)
 
 struct QuadTcParams {
   CUtensorMap tmap_codes;  // (K, N) uint32, box 16 x 128, 64-byte swizzle
@@ -58,15 +67,26 @@ struct QuadTcParams {
   uint32_t smem_bytes;
   float* slots;            // split-K partials [tiles * splits][4][nmma][128]
   int* counters;           // [tiles] arrival counters (zero between launches); [kMaxGrid - 1] status
+  // in-tile plug substitution (uplugs NULL: none): the Linear's unit-major
+  // plug stream (units of 8 rows x 64 columns, tile-major, upt per 8-row
+  // tile; segment: 8 header words start | end << 10 | n << 20, n FP16x4
+  // values, n column bytes) and its unit byte offsets; nrt 8-row tiles
+  const uint8_t* uplugs;
+  const uint32_t* uplug_off;
+  int upt, nrt;
 };
 
 // Shared memory: tables at the first 64 KiB boundary when they fit (direct
 // gathers), else at the base; then, first-fit below and above the tables
 // (1 KiB aligned), S code slots (a stage's codes and activations, filled by
-// TMA) and two A-tile slots (a stage's decoded weights), then the
-// mbarriers and the tensor-memory address slot.  The code ring runs ahead
-// of the decode by up to S stages, so more code slots hide more HBM
-// latency; the A tiles only need to cover the MMA of the previous stage.
+// TMA), two A-tile slots (a stage's decoded weights, one per decoder
+// group), with plugs two plug window slots, then the mbarriers and the
+// tensor-memory address slot.  The code ring runs ahead of the decode by up
+// to S stages, so more code slots hide more HBM latency; the A tiles only
+// need to cover the MMA of the group's previous stage.  (A third A-tile slot
+// measured no faster and, with plugs, costs a code slot: 2048 x 11008 at 64
+// rows took 207 us with three A slots and two code slots, 153 us with two
+// and three.)
 // A ring of equal slots: slots [0, n0) from b0 (below the tables), the rest
 // from b1 (above them), so a slot address is plain arithmetic (no indexed
 // array, which would live in local memory).
@@ -80,13 +100,14 @@ struct TcRing {
 struct TcLayout {
   uint32_t lut, bars, tslot;
   TcRing cr, ar;  // code slots (kTcCSlotBytes), A-tile slots (kTcASlotBytes)
+  uint32_t plug;  // two plug window slots (plugs only)
   int direct, ok;
 };
 
-__host__ __device__ inline TcLayout tc_layout(uint32_t base, uint32_t size, int S) {
+__host__ __device__ inline TcLayout tc_layout(uint32_t base, uint32_t size, int S, bool plugs) {
   TcLayout L{};
   const uint64_t end = (uint64_t)base + size;
-  const uint32_t small = 256;  // (2 S + 2 kTcASlots + 2) mbarriers + tmem slot
+  const uint32_t small = 256;  // (2 S + 2 kTcASlots + 4) mbarriers + tmem slot
   for (int direct = 1; direct >= 0; --direct) {
     L = TcLayout{};
     const uint32_t lut = direct ? ((base + 0xFFFFu) & ~0xFFFFu) : base;
@@ -105,6 +126,11 @@ __host__ __device__ inline TcLayout tc_layout(uint32_t base, uint32_t size, int 
       return fb <= end;
     };
     if (!ring(kTcASlots, kTcASlotBytes, &L.ar) || !ring(S, kTcCSlotBytes, &L.cr)) continue;
+    if (plugs) {
+      TcRing pr{};
+      if (!ring(1, 2 * kTcPlugSlot, &pr)) continue;
+      L.plug = pr.at(0, 2 * kTcPlugSlot);
+    }
     if (fa + small <= lut) L.bars = (uint32_t)fa;
     else if (fb + small <= end) L.bars = (uint32_t)fb;
     else continue;
@@ -210,12 +236,70 @@ __device__ __forceinline__ void tc_decode_stage(uint32_t codes, uint32_t a_tiles
                "r"(m3.y), "r"(m3.z), "r"(m3.w) : "memory");
 }
 
+// Plug values of this decoder thread's row and 8 columns written over its
+// decoded weights (after its own stores of the stage, so they win).  The
+// row's entries of the window's unit are sorted by column: the scan stops
+// at the first column past the thread's range.  A segment larger than its
+// staged bytes is read from global memory.
+__device__ __forceinline__ void tc_patch_plugs(const QuadTcParams& p, uint32_t pslot, uint32_t a_tiles, int tile,
+                                               int kc, int kq) {
+  const int i = threadIdx.x & 255;
+  const int row = i & 127, h = i >> 7;
+  const int rt = tile * (kTcRows / 8) + (row >> 3);  // 8-row tile of the Linear
+  if (rt >= p.nrt) return;
+  const uint32_t seg = pslot + (uint32_t)(row >> 3) * kTcPlugSeg;
+  const uint32_t hdr = lds_u32(seg + 4u * (uint32_t)(row & 7));
+  const uint32_t lo = hdr & 1023u, hi = (hdr >> 10) & 1023u, n = hdr >> 20;
+  if (lo >= hi) return;
+  const uint32_t c0 = (uint32_t)(kq * kTcK + 8 * h);  // first column of the thread in the unit
+  const uint32_t aoff = (uint32_t)((row >> 3) * 256 + (row & 7) * 32 + ((h ^ ((row >> 2) & 1)) << 4));
+  const bool staged = 32u + 9u * n <= kTcPlugSeg;
+  const uint8_t* gs = staged ? nullptr : p.uplugs + __ldg(p.uplug_off + (int64_t)rt * p.upt + kc);
+  for (uint32_t e = lo; e < hi; ++e) {
+    const uint32_t col = staged ? lds_u8(seg + 32u + 8u * n + e) : (uint32_t)__ldg(gs + 32u + 8u * n + e);
+    if (col >= c0 + 8u) break;  // sorted: the rest lie past this thread's columns
+    if (col < c0) continue;
+    const uint2 v = staged ? lds_u2(seg + 32u + 8u * e) : __ldg(reinterpret_cast<const uint2*>(gs + 32u + 8u * e));
+    const uint32_t a = a_tiles + aoff + 2u * (col - c0);
+    asm volatile("st.shared.b16 [%0], %1;" ::"r"(a), "h"((uint16_t)(v.x & 0xFFFFu)) : "memory");
+    asm volatile("st.shared.b16 [%0], %1;" ::"r"(a + kTcATileBytes), "h"((uint16_t)(v.x >> 16)) : "memory");
+    asm volatile("st.shared.b16 [%0], %1;" ::"r"(a + 2 * kTcATileBytes), "h"((uint16_t)(v.y & 0xFFFFu)) : "memory");
+    asm volatile("st.shared.b16 [%0], %1;" ::"r"(a + 3 * kTcATileBytes), "h"((uint16_t)(v.y >> 16)) : "memory");
+  }
+}
+
+// Producer (one lane): the plug segments of 64-column window kc of the
+// tile's 16 row tiles into a window slot, up to kTcPlugSeg bytes each, on
+// the slot's barrier.
+__device__ __forceinline__ void tc_issue_plugs(const QuadTcParams& p, uint32_t pslot, uint32_t bar, int tile,
+                                               int kc) {
+  uint32_t off[kTcRows / 8], len[kTcRows / 8];
+  uint32_t total = 0;
+#pragma unroll
+  for (int t = 0; t < kTcRows / 8; ++t) {
+    const int rt = tile * (kTcRows / 8) + t;
+    off[t] = len[t] = 0u;
+    if (rt < p.nrt) {
+      const int64_t u = (int64_t)rt * p.upt + kc;
+      off[t] = __ldg(p.uplug_off + u);
+      const uint32_t l = __ldg(p.uplug_off + u + 1) - off[t];
+      len[t] = l < kTcPlugSeg ? l : kTcPlugSeg;
+    }
+    total += len[t];
+  }
+  mbar_expect_tx(bar, total);
+#pragma unroll
+  for (int t = 0; t < kTcRows / 8; ++t)
+    if (len[t]) bulk_load(pslot + (uint32_t)t * kTcPlugSeg, p.uplugs + off[t], len[t], bar);
+}
+
 __global__ void __launch_bounds__(kTcThreads, 1) quad_tc_kernel(const __grid_constant__ QuadTcParams p) {
   pdl_launch_dependents();
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   int* status = p.counters + (kMaxGrid - 1);
   const uint32_t base = (uint32_t)__cvta_generic_to_shared(pp_smem);
-  const TcLayout L = tc_layout(base, p.smem_bytes, p.stages);
+  const bool plugs = p.uplugs != nullptr;
+  const TcLayout L = tc_layout(base, p.smem_bytes, p.stages, plugs);
   if (!L.ok) {  // the host plans for this never to happen
     if (tid == 0) atomicExch(status, 2);
     return;
@@ -231,6 +315,14 @@ __global__ void __launch_bounds__(kTcThreads, 1) quad_tc_kernel(const __grid_con
   const uint32_t full = L.bars, empty = L.bars + 8u * S;
   const uint32_t afull = L.bars + 16u * S, aempty = afull + 8u * kTcASlots;
   const uint32_t done = aempty + 8u * kTcASlots, tbar = done + 8u;
+  // plug window slots: window w (64 columns, four stages) goes to slot
+  // (w - w0) & 1 on barrier pfull + 8 * slot.  A slot is refilled two
+  // windows later, when the producer issues the first stage of that window:
+  // it has then waited for stage r - S (S <= 4) to be multiplied, and every
+  // stage before it, including the last stage of the slot's previous
+  // window (r - 5 or earlier), was decoded and patched before that.
+  const uint32_t pfull = tbar + 8u;
+  const int w0 = (c0 * kTcK) / 64;
   if (tid == 0) {
     for (int s = 0; s < S; ++s) {
       mbar_init(full + 8u * s, 1);
@@ -242,6 +334,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) quad_tc_kernel(const __grid_con
     }
     mbar_init(done, 1);
     mbar_init(tbar, 1);
+    mbar_init(pfull, 1);
+    mbar_init(pfull + 8u, 1);
     fence_mbar_init();
     mbar_expect_tx(tbar, kQuadLutBytes);
     for (uint32_t off = 0; off < kQuadLutBytes; off += 16384u) bulk_load(L.lut + off, p.tables + off, 16384u, tbar);
@@ -261,11 +355,16 @@ __global__ void __launch_bounds__(kTcThreads, 1) quad_tc_kernel(const __grid_con
       prefetch_tmap(&p.tmap_codes);
       prefetch_tmap(&p.tmap_x);
       const uint32_t xbytes = (uint32_t)p.nmma * kTcK * 2u;
-      // codes of the first stages are weights: issue them before the wait
+      // codes (and plug segments) of the first stages are weights: issue them before the wait
       const int pre = nst < S ? nst : S;
       for (int r = 0; r < pre; ++r) {
         mbar_expect_tx(full + 8u * r, kTcCodeBytes + xbytes);
         tma_load_2d(L.cr.at(r, kTcCSlotBytes), &p.tmap_codes, (c0 + r) * kTcK, n0, full + 8u * r);
+        const int kc = ((c0 + r) * kTcK) / 64;
+        if (plugs && (r == 0 || ((c0 + r) * kTcK) % 64 == 0)) {
+          const uint32_t ps = (uint32_t)((kc - w0) & 1);
+          tc_issue_plugs(p, L.plug + ps * kTcPlugSlot, pfull + 8u * ps, tile, kc);
+        }
       }
       pdl_wait();  // activations may come from the previous kernel
       for (int r = 0; r < pre; ++r) tma_load_2d(L.cr.at(r, kTcCSlotBytes) + kTcCodeBytes, &p.tmap_x, (c0 + r) * kTcK, 0, full + 8u * r);
@@ -276,6 +375,11 @@ __global__ void __launch_bounds__(kTcThreads, 1) quad_tc_kernel(const __grid_con
         mbar_expect_tx(full + 8u * s, kTcCodeBytes + xbytes);
         tma_load_2d(L.cr.at(s, kTcCSlotBytes), &p.tmap_codes, (c0 + r) * kTcK, n0, full + 8u * s);
         tma_load_2d(L.cr.at(s, kTcCSlotBytes) + kTcCodeBytes, &p.tmap_x, (c0 + r) * kTcK, 0, full + 8u * s);
+        if (plugs && ((c0 + r) * kTcK) % 64 == 0) {
+          const int kc = ((c0 + r) * kTcK) / 64;
+          const uint32_t ps = (uint32_t)((kc - w0) & 1);
+          tc_issue_plugs(p, L.plug + ps * kTcPlugSlot, pfull + 8u * ps, tile, kc);
+        }
       }
     }
   } else if (warp == kTcDecodeWarps + 1) {
@@ -315,6 +419,13 @@ __global__ void __launch_bounds__(kTcThreads, 1) quad_tc_kernel(const __grid_con
           break;
         if (L.direct) tc_decode_stage<true>(L.cr.at(s, kTcCSlotBytes), L.ar.at(a, kTcASlotBytes), lb0, lb1, 0u, 0u);
         else tc_decode_stage<false>(L.cr.at(s, kTcCSlotBytes), L.ar.at(a, kTcASlotBytes), lb0, lb1, add0, add1);
+        if (plugs) {
+          const int kc = ((c0 + r) * kTcK) / 64;
+          const uint32_t ps = (uint32_t)((kc - w0) & 1);
+          if (!mbar_wait_bounded(pfull + 8u * ps, (uint32_t)((kc - w0) >> 1) & 1u, status)) break;
+          tc_patch_plugs(p, L.plug + ps * kTcPlugSlot, L.ar.at(a, kTcASlotBytes), tile, kc,
+                         (((c0 + r) * kTcK) % 64) / kTcK);
+        }
         fence_proxy_async();  // the A tiles are read by the tensor core (async proxy)
         __syncwarp();
         if (lane == 0) mbar_arrive(afull + 8u * a);
@@ -469,7 +580,7 @@ size_t quad_tc_slots_bytes(int64_t M, int64_t N, int64_t K, int sms) {
 int launch_quad_tc(const void* x, int64_t ldx_m, const uint32_t* codes, int64_t ldw, const void* tables,
                    const float scales[4], void* const out[4], int64_t ldo_m, int64_t ldo_n, const float* corr,
                    int64_t corr_q, int64_t Mc, int64_t N, int64_t K, int* counters, float* slots,
-                   cudaStream_t s) {
+                   const void* uplugs, const uint32_t* uplug_off, cudaStream_t s) {
   const int dev = current_device();
   const int sms = device_sm_count(dev);
   int max_smem = 0;
@@ -503,10 +614,15 @@ int launch_quad_tc(const void* x, int64_t ldx_m, const uint32_t* codes, int64_t 
   prm.tmem_cols = cols;
   prm.counters = counters;
   prm.slots = slots;
+  const bool plugs = uplugs != nullptr;
+  prm.uplugs = reinterpret_cast<const uint8_t*>(uplugs);
+  prm.uplug_off = uplug_off;
+  prm.upt = (int)cdiv(K, 64);
+  prm.nrt = (int)cdiv(N, 8);
   const uint32_t reserved = (uint32_t)reserved_smem(dev);
-  int S = kTcMaxStages;
-  while (S > 1 && !tc_layout(reserved, (uint32_t)max_smem, S).ok) --S;
-  if (!tc_layout(reserved, (uint32_t)max_smem, S).ok) {
+  int S = plugs ? kTcPlugMaxStages : kTcMaxStages;
+  while (S > 1 && !tc_layout(reserved, (uint32_t)max_smem, S, plugs).ok) --S;
+  if (!tc_layout(reserved, (uint32_t)max_smem, S, plugs).ok) {
     set_error("no shared memory layout for the tensor-core kernel within %d bytes", max_smem);
     return PP_ERR_INVALID;
   }

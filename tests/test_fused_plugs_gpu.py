@@ -188,11 +188,13 @@ def test_long_partition_runs_in_row_chunks(cuda):
     torch.cuda.empty_cache()
 
 
-@pytest.mark.parametrize("M", [3, 17, 64, 130])
+@pytest.mark.parametrize("M", [3, 17, 33, 64, 130])
 def test_batched_plugs_tensor_core_path(cuda, M):
-    """N >= 4096 above 16 rows takes the tcgen05 kernel, with the plug
-    correction for all of a launch's rows (up to 128) in one kernel over
-    the transposed activations; 130 rows are launches of 128 and 2."""
+    """N >= 4096 above 16 rows takes the tcgen05 kernel.  A launch of more
+    than 32 rows substitutes the plug values into its decoded tiles; up to
+    32 rows a separate kernel computes the correction for all of the
+    launch's rows over the transposed activations.  130 rows are launches of
+    128 (substituted) and 2 (corrected)."""
     lin = Linear(cuda, 4096, 320, 0.05, True, seed=100 + M)
     x = np.random.default_rng(M).normal(0, 1, size=(M, 320)).astype(np.float16)
     y = lin.run(torch.from_numpy(x).to(cuda))
