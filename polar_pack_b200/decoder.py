@@ -296,14 +296,16 @@ class QuadDecoder:
         self.cos, self.sin = rope_tables(cfg, dev)
         # attention: position ranges per (model, kv head); by default one per
         # 256 positions of the cache (a CTA's eight 32-position warp tiles at
-        # full length), which keeps the CTAs of one launch within one wave
-        self.splits = attn_splits if attn_splits else max(1, min(64, -(-cfg.max_pos // 256)))
+        # full length), at most as many as keep the launch's splits x kv heads
+        # x 4 CTAs (one per SM: each holds ~147 KB of shared memory) in one wave
+        sms = self.lib.pp_device_sm_count(dev.index if dev.index is not None else 0)
+        wave = max(1, sms // (4 * cfg.kv_heads))
+        self.splits = attn_splits if attn_splits else max(1, min(64, wave, -(-cfg.max_pos // 256)))
         nb = _lib._size_t()
         _lib.check(self.lib.pp_decode_attention_workspace_bytes(cfg.q_heads, cfg.kv_heads, self.splits,
                                                                 ctypes.byref(nb)))
         self.attn_ws = torch.zeros(nb.value, dtype=torch.uint8, device=dev)
         offs = {n: (o, s) for n, o, s in layer_offsets(qwen2_layer_map(cfg))}
-        sms = self.lib.pp_device_sm_count(dev.index if dev.index is not None else 0)
         self.groups = []   # per layer: launches (row chunks) of qkv, o, gate_up, down
         for l in range(cfg.layers):
             p = f"model.layers.{l}."
